@@ -1,0 +1,225 @@
+/*
+ * qwenscriber_cuda.h -- C ABI of libqwenscriber_cuda, the sm_100a (B200)
+ * backend for Qwenscriber's decoder token loop.
+ *
+ * The library is a drop-in `cuda` backend beside the reference's `wasm` and
+ * `webgpu` backends. Its model and decode families mirror the reference's
+ * `qw_model_*` / `qw_decode_*` exports (src/wasm/exports.zig) and their state
+ * machine (src/wasm/model.zig:9-26): idle -> ready -> loaded -> decoding.
+ * Status codes are the reference's own numbers (src/wasm/abi.zig:50-84).
+ *
+ * Conventions (src/wasm/abi.zig:1-17, docs/src/reference/c-abi.md):
+ *   - fixed-width integers, pointer plus explicit length, no library types;
+ *   - every call returns a status (0 ok, negative failure) unless noted;
+ *   - caller-owned buffers; the library never frees caller memory;
+ *   - a handle is bound to one CUDA device and is not thread-safe; use one
+ *     handle per GPU, each driven by its own host thread or process.
+ *
+ * Unlike the WASM build, which borrows the caller's shard bytes for the life
+ * of the model (src/wasm/model.zig:28-42), this library copies each tensor
+ * payload into device memory (HBM) when it is added, after which the caller
+ * may release its buffer.
+ */
+#ifndef QWENSCRIBER_CUDA_H
+#define QWENSCRIBER_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ABI version: major << 16 | minor (src/wasm/abi.zig:15-28). */
+#define QWC_ABI_MAJOR 1u
+#define QWC_ABI_MINOR 0u
+
+/* Status codes: identical numbers to src/wasm/abi.zig:50-84. */
+enum {
+  QWC_OK = 0,
+  QWC_INVALID_ARGUMENT = -1,
+  QWC_OUT_OF_MEMORY = -2,
+  QWC_UNSUPPORTED = -3,
+  QWC_BAD_MAGIC = -4,
+  QWC_BAD_VERSION = -5,
+  QWC_CHECKSUM_MISMATCH = -6,
+  QWC_SHAPE_MISMATCH = -7,
+  QWC_INVALID_STATE = -8,
+  QWC_LIMIT_EXCEEDED = -9,
+  QWC_NOT_FOUND = -10,
+  QWC_TRUNCATED = -11,
+  QWC_INVALID_ENCODING = -12,
+  QWC_UNSUPPORTED_MODEL = -13,
+  QWC_AUDIO_TOO_LONG = -14
+};
+
+/* Tensor formats: src/core/dtype.zig:17-24. */
+enum { QWC_FORMAT_F32 = 0, QWC_FORMAT_F16 = 1, QWC_FORMAT_BF16 = 2, QWC_FORMAT_Q4 = 16, QWC_FORMAT_Q5 = 17, QWC_FORMAT_Q8 = 18 };
+
+/* Key/value cache formats: src/wasm/abi.zig:36-46. */
+enum { QWC_CACHE_F32 = 0, QWC_CACHE_Q8 = 1 };
+
+/* Decoder tensor kinds: the reference's container.TensorKind values
+ * (src/core/container.zig:333-376). Decoder layers are numbered 1..=layers
+ * and tensors outside a layer use layer 0 (src/core/qwen3_asr/layout.zig:14-28). */
+enum {
+  QWC_KIND_DECODER_EMBED_TOKENS = 30,
+  QWC_KIND_DECODER_FINAL_NORM = 31,
+  QWC_KIND_DECODER_OUTPUT = 32,
+  QWC_KIND_DECODER_Q = 33,
+  QWC_KIND_DECODER_K = 34,
+  QWC_KIND_DECODER_V = 35,
+  QWC_KIND_DECODER_O = 36,
+  QWC_KIND_DECODER_Q_NORM = 37,
+  QWC_KIND_DECODER_K_NORM = 38,
+  QWC_KIND_DECODER_ATTENTION_NORM = 39,
+  QWC_KIND_DECODER_FFN_NORM = 40,
+  QWC_KIND_DECODER_GATE = 41,
+  QWC_KIND_DECODER_UP = 42,
+  QWC_KIND_DECODER_DOWN = 43
+};
+
+/* Feature bits (src/wasm/abi.zig:179-207): model and decode families, plus
+ * the batched multi-stream family this backend adds. */
+#define QWC_FEATURE_MODEL (1u << 3)
+#define QWC_FEATURE_DECODE (1u << 4)
+#define QWC_FEATURE_STREAMS (1u << 8)
+
+/* qw_model_requirements layout, 48 bytes (src/wasm/abi.zig:281-290). */
+typedef struct qwc_requirements {
+  uint64_t weight_bytes;  /* device bytes holding the weight payloads */
+  uint64_t cache_bytes;   /* key/value cache, all layers, all stream slots */
+  uint64_t scratch_bytes; /* activations, rope tables, logits, partials */
+  uint64_t total_bytes;   /* weight_bytes + cache_bytes + scratch_bytes */
+  uint32_t max_positions;
+  uint32_t max_audio_frames;
+  uint32_t max_decode_tokens;
+  uint32_t reserved;
+} qwc_requirements;
+
+/* Handle options (qwc_set_option). */
+enum {
+  /* Nonzero: decode does not stop at end-of-sequence tokens (fixed-length
+   * benchmarking, as src/cli/transcribe.zig:200-208 runs Decoder.step). */
+  QWC_OPTION_IGNORE_EOS = 1,
+  /* Nonzero: keep the last computed logits of each stream on the device so
+   * qwc_debug_logits can return them (parity testing). */
+  QWC_OPTION_KEEP_LOGITS = 2,
+  /* Decode steps computed ahead per device launch (1..256, default 16). */
+  QWC_OPTION_STEP_CHUNK = 3
+};
+
+/* ---- version and lifecycle (src/wasm/exports.zig:49-120) ---- */
+
+/* qw_abi_version (exports.zig:49). */
+uint32_t qwc_abi_version(void);
+/* qw_features (exports.zig:300-309; abi.zig:202-207). */
+uint32_t qwc_features(void);
+/* qw_create: returns a nonzero handle bound to CUDA device `device`, or 0. */
+uint32_t qwc_create(int32_t device);
+/* qw_destroy: releases every device allocation of the handle. */
+int32_t qwc_destroy(uint32_t handle);
+/* Text of a status code (abi.zig:153-171); never NULL. */
+const char* qwc_status_message(int32_t status);
+int32_t qwc_set_option(uint32_t handle, uint32_t option, uint32_t value);
+
+/* ---- model family (src/wasm/exports.zig:320-425; src/wasm/model.zig:136-263) ---- */
+
+/* qw_model_begin: starts a model attempt; legal in every state and also the unload path. */
+int32_t qwc_model_begin(uint32_t handle);
+/* Replaces qw_model_add_shard for one tensor: `payload` holds that tensor's
+ * container payload -- for q4/q5/q8 the f16 scale plane, padding to 16 bytes,
+ * then the code plane (src/core/quant.zig:144-176); for f32 vectors the
+ * values. Copied to device memory before returning. */
+int32_t qwc_model_add_tensor(uint32_t handle, uint32_t kind, uint32_t layer, uint32_t format, uint32_t rows,
+                             uint32_t cols, const void* payload, uint64_t len);
+/* qw_model_set_cache_format (exports.zig:352-363): ready state only. */
+int32_t qwc_model_set_cache_format(uint32_t handle, uint32_t format);
+/* Number of independent decode streams the next finish allocates (default 1). */
+int32_t qwc_model_set_streams(uint32_t handle, uint32_t streams);
+/* qw_model_finish: validates the 160-byte Config (src/core/model_config.zig:110-177,
+ * 260-328), resolves every tensor, allocates caches and scratch. */
+int32_t qwc_model_finish(uint32_t handle, const void* config, uint32_t config_len);
+/* qw_model_requirements (exports.zig:371-378). */
+int32_t qwc_model_requirements(uint32_t handle, qwc_requirements* out);
+/* qw_model_tensor_count (exports.zig:384-389): tensors held by the loaded model. */
+int32_t qwc_model_tensor_count(uint32_t handle, uint32_t* out);
+
+/* ---- decode family, stream slot 0 (src/wasm/exports.zig:440-497; model.zig:370-474) ---- */
+
+/* qw_decode_begin after the audio tower: resets stream 0's cache, prefills
+ * `prompt` (token == Config.token_audio_pad consumes the next of `audio_steps`
+ * rows of `audio`, text_hidden_size f32 each; decoder.zig:308-333) and holds
+ * the first predicted token. */
+int32_t qwc_decode_begin(uint32_t handle, const uint32_t* prompt, uint32_t prompt_len, const float* audio,
+                         uint32_t audio_steps, uint32_t max_tokens);
+/* qw_decode_step: 1 and *token_out written, 0 when finished, <0 status. */
+int32_t qwc_decode_step(uint32_t handle, uint32_t* token_out);
+/* qw_decode_tokens: copies the ids produced so far, returns their count. */
+int32_t qwc_decode_tokens(uint32_t handle, uint32_t* out, uint32_t capacity);
+/* qw_decode_end: back to loaded; the cache is cleared. */
+int32_t qwc_decode_end(uint32_t handle);
+
+/* ---- multi-stream family: independent streams batched per device step ---- */
+
+int32_t qwc_stream_begin(uint32_t handle, uint32_t slot, const uint32_t* prompt, uint32_t prompt_len,
+                         const float* audio, uint32_t audio_steps, uint32_t max_tokens);
+/* Advances every decoding slot by one token. results[slot]: 1 token written
+ * to tokens_out[slot], 0 finished or idle, <0 status. Returns the number of
+ * tokens produced, or <0 status. Both arrays hold `streams` entries. */
+int32_t qwc_streams_step(uint32_t handle, uint32_t* tokens_out, int32_t* results);
+int32_t qwc_stream_tokens(uint32_t handle, uint32_t slot, uint32_t* out, uint32_t capacity);
+int32_t qwc_stream_end(uint32_t handle, uint32_t slot);
+
+/* ---- measurement and parity (not part of the reference ABI) ---- */
+
+/* Runs `steps` greedy decode steps of stream 0 on the device (held token
+ * first), without end-of-sequence handling, and reports their device time in
+ * milliseconds measured with CUDA events on the handle's stream. */
+int32_t qwc_decode_run_timed(uint32_t handle, uint32_t steps, float* device_ms);
+/* Last logits computed for `slot` (QWC_OPTION_KEEP_LOGITS must be set). */
+int32_t qwc_debug_logits(uint32_t handle, uint32_t slot, float* out, uint32_t count);
+/* Raw key (which = 0) or value (which = 1) cache bytes of `slot`, in the
+ * reference's layer-major two-plane layout (src/core/qwen3_asr/decoder.zig:45-65). */
+int32_t qwc_debug_cache(uint32_t handle, uint32_t slot, uint32_t which, void* out, uint64_t len);
+/* Device kernels launched by this handle since creation. */
+uint64_t qwc_kernel_launches(uint32_t handle);
+/* Rotary tables as the model builds them (src/core/qwen3_asr/kernels.zig:534-564):
+ * max_positions rows of head_dim / 2 values each. Host-only. */
+int32_t qwc_rope_tables(float theta, uint32_t head_dim, uint32_t max_positions, float* cos_out, float* sin_out);
+
+/* ---- device-pointer operators (caller's CUDA stream; NULL = default stream) ----
+ * The per-token kernels' building blocks, exposed so a host can run one step
+ * of the token loop on its own buffers and so parity tests can check each
+ * against the reference arithmetic. All pointers are device pointers. */
+
+/* quant.dequantizeRow (src/core/quant.zig:348-364) over `rows` rows: bit exact. */
+int32_t qwc_op_dequantize(uint32_t format, const void* scales, const void* codes, uint32_t rows, uint32_t cols,
+                          float* out, void* stream);
+/* quant.quantizeRow(.q8) (src/core/quant.zig:197-288) over `rows` rows: bit exact. */
+int32_t qwc_op_quantize_q8(const float* values, uint32_t rows, uint32_t cols, void* scales, void* codes,
+                           void* stream);
+/* kernels.linearQuantized with one token (src/core/qwen3_asr/kernels.zig:118-158): out[rows]. */
+int32_t qwc_op_gemv(uint32_t format, const void* scales, const void* codes, uint32_t rows, uint32_t cols,
+                    const float* x, float* out, void* stream);
+/* kernels.decodeAttentionStepQ8 (src/core/qwen3_asr/kernels.zig:697-767) over
+ * `cached` rows of a cache laid out as planes of `max_positions` rows. */
+int32_t qwc_op_attention_q8(const float* query, const void* keys_scales, const void* keys_codes,
+                            const void* values_scales, const void* values_codes, uint32_t cached, uint32_t heads,
+                            uint32_t kv_heads, uint32_t head_dim, float* out, void* stream);
+/* Decoder.argmaxLogits (src/core/qwen3_asr/decoder.zig:290-301): first index
+ * of the maximum. Uses a device workspace the library allocates per call. */
+int32_t qwc_op_argmax(const float* values, uint32_t count, uint32_t* out_index, void* stream);
+/* math.rmsNormInPlace per row (src/core/math.zig:120-130), out of place. */
+int32_t qwc_op_rmsnorm(const float* x, const float* weight, uint32_t width, uint32_t rows, float eps, float* out,
+                       void* stream);
+/* kernels.ropeInPlace at one position (src/core/qwen3_asr/kernels.zig:495-527). */
+int32_t qwc_op_rope(float* x, uint32_t heads, uint32_t head_dim, const float* cos_table, const float* sin_table,
+                    uint32_t position, void* stream);
+/* kernels.siluMul (src/core/qwen3_asr/kernels.zig:233-239). */
+int32_t qwc_op_silu_mul(const float* gate, const float* up, uint32_t n, float* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QWENSCRIBER_CUDA_H */

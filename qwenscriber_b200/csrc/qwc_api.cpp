@@ -1,0 +1,930 @@
+// qwc_api.cpp -- host runtime of libqwenscriber_cuda: the C ABI declared in
+// include/qwenscriber_cuda.h.
+//
+// Mirrors the reference's model/decode state machine (src/wasm/model.zig),
+// argument validation and status mapping (src/wasm/exports.zig,
+// src/wasm/abi.zig), Config validation (src/core/model_config.zig:260-328) and
+// the decoder's capacity rules (src/core/qwen3_asr/model.zig:62, decoder.zig:142).
+// Device work is launched on one CUDA stream per handle.
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <deque>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <vector>
+
+#include "../../include/qwenscriber_cuda.h"
+#include "qwc_internal.h"
+
+namespace qwc {
+namespace {
+
+// ---- Config (src/core/model_config.zig:110-177), byte for byte ----
+struct Config {
+  uint8_t magic[8];
+  uint32_t format_version, architecture;
+  uint32_t audio_d_model, audio_layers, audio_attention_heads, audio_ffn_dim, audio_downsample_hidden_size,
+      audio_n_window, audio_n_window_infer, audio_max_position_steps, audio_output_dim, mel_bins;
+  float audio_layer_norm_eps;
+  uint32_t text_hidden_size, text_layers, text_attention_heads, text_key_value_heads, text_head_dim, text_ffn_dim,
+      vocab_size;
+  float text_rms_norm_eps, rope_theta;
+  uint32_t max_positions, max_decode_tokens;
+  uint32_t token_audio_start, token_audio_end, token_audio_pad, token_im_start, token_im_end, token_endoftext,
+      token_asr_text, token_eos_primary, token_eos_secondary, token_pad;
+  uint32_t flags, reserved1, reserved2, reserved3;
+};
+static_assert(sizeof(Config) == 160, "model_config.zig:364");
+static_assert(offsetof(Config, audio_d_model) == 16, "model_config.zig:371");
+static_assert(offsetof(Config, text_hidden_size) == 60, "model_config.zig:372");
+static_assert(offsetof(Config, token_audio_start) == 104, "model_config.zig:373");
+static_assert(offsetof(Config, flags) == 144, "model_config.zig:374");
+static_assert(sizeof(qwc_requirements) == 48, "abi.zig:389");
+
+constexpr uint32_t kMelBins = 128;          // src/core/mel.zig:50
+constexpr uint32_t kCapacityFrames = 3000;  // src/core/mel.zig:55-58
+constexpr uint32_t kFieldMax = 1u << 24;    // model_config.zig:26
+constexpr uint32_t kLayerMax = 512;
+constexpr uint32_t kVocabMax = 1u << 21;
+constexpr uint32_t kDecodeTokensMax = 8192;
+
+uint32_t conv_steps(uint32_t n) {
+  for (int i = 0; i < 3; ++i) n = (n - 1) / 2 + 1;
+  return n;
+}
+
+// model_config.zig:260-328. Every failure other than magic, version and
+// capacity maps to invalid_argument, as abi.zig:91-147 reports them.
+int32_t validate_config(const Config& c) {
+  if (std::memcmp(c.magic, "QWCFG001", 8) != 0) return QWC_BAD_MAGIC;
+  if (c.format_version != 1) return QWC_BAD_VERSION;
+  if ((c.flags & ~1u) != 0 || c.reserved1 || c.reserved2 || c.reserved3) return QWC_INVALID_ARGUMENT;
+  if (c.architecture != 1) return QWC_INVALID_ARGUMENT;
+  auto range = [](uint32_t v) { return v != 0 && v <= kFieldMax; };
+  auto layers = [](uint32_t v) { return v != 0 && v <= kLayerMax; };
+  if (!range(c.audio_d_model) || !range(c.audio_ffn_dim) || !range(c.audio_downsample_hidden_size) ||
+      !range(c.audio_output_dim) || !range(c.text_hidden_size) || !range(c.text_ffn_dim) || !range(c.text_head_dim) ||
+      !layers(c.audio_layers) || !layers(c.text_layers)) {
+    return QWC_INVALID_ARGUMENT;
+  }
+  if (c.mel_bins != kMelBins) return QWC_INVALID_ARGUMENT;
+  if (c.audio_attention_heads == 0 || c.audio_d_model % c.audio_attention_heads != 0) return QWC_INVALID_ARGUMENT;
+  const uint32_t audio_head = c.audio_d_model / c.audio_attention_heads;
+  if (audio_head < 2 || audio_head % 2 != 0) return QWC_INVALID_ARGUMENT;
+  if (c.text_attention_heads == 0 || c.text_key_value_heads == 0) return QWC_INVALID_ARGUMENT;
+  if (c.text_attention_heads % c.text_key_value_heads != 0) return QWC_INVALID_ARGUMENT;
+  if (c.text_head_dim < 2 || c.text_head_dim % 2 != 0) return QWC_INVALID_ARGUMENT;
+  if (c.text_hidden_size != c.audio_output_dim) return QWC_INVALID_ARGUMENT;
+  if (c.audio_n_window == 0) return QWC_INVALID_ARGUMENT;
+  const uint32_t chunk = c.audio_n_window * 2;
+  if (chunk > kCapacityFrames || c.audio_n_window_infer % chunk != 0) return QWC_INVALID_ARGUMENT;
+  if (c.audio_max_position_steps < conv_steps(chunk)) return QWC_INVALID_ARGUMENT;
+  if (c.vocab_size == 0 || c.vocab_size > kVocabMax) return QWC_INVALID_ARGUMENT;
+  if (!range(c.max_positions)) return QWC_INVALID_ARGUMENT;
+  if (c.max_decode_tokens == 0 || c.max_decode_tokens > kDecodeTokensMax) return QWC_INVALID_ARGUMENT;
+  if (!std::isfinite(c.audio_layer_norm_eps) || !(c.audio_layer_norm_eps > 0.0f)) return QWC_INVALID_ARGUMENT;
+  if (!std::isfinite(c.text_rms_norm_eps) || !(c.text_rms_norm_eps > 0.0f)) return QWC_INVALID_ARGUMENT;
+  if (!std::isfinite(c.rope_theta) || !(c.rope_theta > 1.0f)) return QWC_INVALID_ARGUMENT;
+  const uint32_t tokens[] = {c.token_audio_start, c.token_audio_end, c.token_audio_pad, c.token_im_start,
+                             c.token_im_end, c.token_endoftext, c.token_asr_text, c.token_eos_primary,
+                             c.token_eos_secondary, c.token_pad};
+  for (uint32_t t : tokens) {
+    if (t >= c.vocab_size) return QWC_INVALID_ARGUMENT;
+  }
+  // model.zig:1006-1009 (validateCapacity): CapacityExceeded -> limit_exceeded.
+  if (c.max_positions == 0 || c.max_positions > kPositionLimit) return QWC_LIMIT_EXCEEDED;
+  return QWC_OK;
+}
+
+// ---- rotary tables: kernels.zig:534-564 with Zig's std.math.pow(f32) ----
+// (the published Go math.Pow algorithm: exp(yf * log x) times x^yi by
+// repeated squaring, in f32), restricted to x > 0 finite.
+float pow_f32(float x, float y) {
+  if (y == 0.0f || x == 1.0f) return 1.0f;
+  if (std::isnan(x) || std::isnan(y)) return std::nanf("");
+  if (y == 1.0f) return x;
+  if (y == 0.5f) return std::sqrt(x);
+  if (y == -0.5f) return 1.0f / std::sqrt(x);
+  float yi;
+  float yf = std::modf(std::fabs(y), &yi);
+  float a1 = 1.0f;
+  int32_t ae = 0;
+  if (yf != 0.0f) {
+    if (yf > 0.5f) {
+      yf -= 1.0f;
+      yi += 1.0f;
+    }
+    a1 = std::exp(yf * std::log(x));
+  }
+  int xe = 0;
+  float x1 = std::frexp(x, &xe);
+  for (int32_t i = static_cast<int32_t>(yi); i != 0; i >>= 1) {
+    if (xe < -(1 << 9) || (1 << 9) < xe) {
+      ae += xe;
+      break;
+    }
+    if (i & 1) {
+      a1 *= x1;
+      ae += xe;
+    }
+    x1 *= x1;
+    xe <<= 1;
+    if (x1 < 0.5f) {
+      x1 += x1;
+      xe -= 1;
+    }
+  }
+  if (y < 0.0f) {
+    a1 = 1.0f / a1;
+    ae = -ae;
+  }
+  return std::ldexp(a1, ae);
+}
+
+void build_rope(float theta, uint32_t head_dim, uint32_t max_positions, float* cos_out, float* sin_out) {
+  const uint32_t half = head_dim / 2;
+  std::vector<float> inv(half);
+  for (uint32_t i = 0; i < half; ++i) {
+    const float exponent = -2.0f * static_cast<float>(i) / static_cast<float>(head_dim);
+    inv[i] = pow_f32(theta, exponent);
+  }
+  for (uint32_t p = 0; p < max_positions; ++p) {
+    for (uint32_t i = 0; i < half; ++i) {
+      const float angle = static_cast<float>(p) * inv[i];
+      cos_out[size_t(p) * half + i] = std::cos(angle);
+      sin_out[size_t(p) * half + i] = std::sin(angle);
+    }
+  }
+}
+
+// ---- handles ----
+
+enum class State { kIdle, kReady, kLoaded };
+
+struct DevBuf {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  DevBuf() = default;
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  ~DevBuf() {
+    if (ptr) cudaFree(ptr);
+  }
+  int32_t alloc(size_t n) {
+    if (ptr) cudaFree(ptr);
+    ptr = nullptr;
+    bytes = 0;
+    if (n == 0) return QWC_OK;
+    if (cudaMalloc(&ptr, n) != cudaSuccess) {
+      cudaGetLastError();
+      ptr = nullptr;
+      return QWC_OUT_OF_MEMORY;
+    }
+    bytes = n;
+    return QWC_OK;
+  }
+  template <typename T>
+  T* as() const {
+    return static_cast<T*>(ptr);
+  }
+};
+
+struct Tensor {
+  uint32_t kind, layer, format, rows, cols;
+  std::unique_ptr<DevBuf> buf;
+  uint64_t scales_offset = 0, codes_offset = 0;
+};
+
+struct StreamSlot {
+  bool decoding = false;
+  bool finished = false;
+  uint32_t position = 0;         // positions the device has filled
+  uint32_t next_token = 0;       // predicted, not yet produced
+  uint32_t max_tokens = 0;
+  std::vector<uint32_t> generated;
+  std::deque<uint32_t> ahead;    // predictions computed beyond next_token
+};
+
+struct Handle {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  State state = State::kIdle;
+  uint32_t cache_format = QWC_CACHE_F32;  // the reference's default (model.zig:119)
+  uint32_t streams = 1;
+  bool ignore_eos = false;
+  bool keep_logits = false;
+  uint32_t step_chunk = 16;
+  uint64_t launches = 0;
+  std::map<std::pair<uint32_t, uint32_t>, Tensor> tensors;
+  Config config{};
+  int grid = 0;
+  DevModel host_model{};
+  DevBuf model_buf, rope_cos, rope_sin, k_cache, v_cache;
+  DevBuf qkv, attn_out, hidden_g, act, attn_part, attn_count, amax_val, amax_idx, barrier, error, tokens_out, logits;
+  DevBuf prompt_ids, prompt_rows, audio_rows;
+  uint32_t max_chunks = 0;
+  uint64_t weight_bytes = 0;
+  std::vector<StreamSlot> slots;
+
+  ~Handle() {
+    if (stream) cudaStreamDestroy(stream);
+  }
+};
+
+std::mutex g_mutex;
+std::map<uint32_t, std::unique_ptr<Handle>> g_handles;
+uint32_t g_next_handle = 1;
+
+Handle* lookup(uint32_t h) {
+  std::lock_guard<std::mutex> lock(g_mutex);
+  auto it = g_handles.find(h);
+  return it == g_handles.end() ? nullptr : it->second.get();
+}
+
+int32_t status_of(cudaError_t e) {
+  if (e == cudaSuccess) return QWC_OK;
+  cudaGetLastError();
+  if (e == cudaErrorMemoryAllocation) return QWC_OUT_OF_MEMORY;
+  return QWC_INVALID_STATE;
+}
+
+#define QWC_TRY(expr)                        \
+  do {                                       \
+    const int32_t _st = (expr);              \
+    if (_st != QWC_OK) return _st;           \
+  } while (0)
+
+#define QWC_CUDA(expr) QWC_TRY(status_of(expr))
+
+void release_model(Handle* h) {
+  h->tensors.clear();
+  for (DevBuf* b : {&h->model_buf, &h->rope_cos, &h->rope_sin, &h->k_cache, &h->v_cache, &h->qkv, &h->attn_out,
+                    &h->hidden_g, &h->act, &h->attn_part, &h->attn_count, &h->amax_val, &h->amax_idx, &h->barrier,
+                    &h->error, &h->tokens_out, &h->logits, &h->prompt_ids, &h->prompt_rows, &h->audio_rows}) {
+    b->alloc(0);
+  }
+  h->slots.clear();
+  h->weight_bytes = 0;
+}
+
+bool is_vector_kind(uint32_t kind) {
+  return kind == QWC_KIND_DECODER_FINAL_NORM || kind == QWC_KIND_DECODER_Q_NORM || kind == QWC_KIND_DECODER_K_NORM ||
+         kind == QWC_KIND_DECODER_ATTENTION_NORM || kind == QWC_KIND_DECODER_FFN_NORM;
+}
+
+DevMat make_mat(const Tensor& t) {
+  DevMat m{};
+  m.scales = static_cast<const uint8_t*>(t.buf->ptr) + t.scales_offset;
+  m.codes = static_cast<const uint8_t*>(t.buf->ptr) + t.codes_offset;
+  m.rows = t.rows;
+  m.cols = t.cols;
+  m.format = t.format;
+  m.groups = t.cols / kGroup;
+  m.scale_row = m.groups * 2;
+  m.code_row = m.groups * data_bytes_per_group(t.format);
+  return m;
+}
+
+// The decode kernel's layout rules for one matrix: q4/q8, whole 512-byte
+// code spans per row, at most two K segments of 96 activations per lane.
+int32_t kernel_fits(const DevMat& m) {
+  if (m.format != kFormatQ4 && m.format != kFormatQ8) return QWC_UNSUPPORTED_MODEL;
+  if (m.code_row % 512 != 0 || m.scale_row % 16 != 0) return QWC_UNSUPPORTED_MODEL;
+  const uint32_t ch = m.code_row / 512;
+  const uint32_t vals = m.format == kFormatQ4 ? 32 : 16;
+  const bool ks1 = ch * vals <= 96;
+  const bool ks2 = ch % 2 == 0 && (ch / 2) * vals <= 96;
+  if (!ks1 && !ks2) return QWC_UNSUPPORTED_MODEL;
+  if (m.scale_row + m.code_row > 28 * 1024) return QWC_UNSUPPORTED_MODEL;
+  return QWC_OK;
+}
+
+int32_t finish_model(Handle* h, const Config& c) {
+  QWC_TRY(validate_config(c));
+  const uint32_t hidden = c.text_hidden_size, qw = c.text_attention_heads * c.text_head_dim,
+                 kvw = c.text_key_value_heads * c.text_head_dim, ffn = c.text_ffn_dim, L = c.text_layers;
+  if (h->cache_format != QWC_CACHE_Q8) return QWC_UNSUPPORTED;  // this backend keeps the q8 cache
+  if (L > kMaxLayers || c.text_head_dim != kHeadDim || c.text_attention_heads != 2 * c.text_key_value_heads) {
+    return QWC_UNSUPPORTED_MODEL;
+  }
+  if (hidden % 4 != 0 || hidden > 8192 || qw > 8192 || ffn > 8192) return QWC_UNSUPPORTED_MODEL;
+  const bool tied = (c.flags & 1u) != 0;
+
+  auto find = [&](uint32_t kind, uint32_t layer) -> const Tensor* {
+    auto it = h->tensors.find({kind, layer});
+    return it == h->tensors.end() ? nullptr : &it->second;
+  };
+  // Shapes of src/core/qwen3_asr/layout.zig:264-320 (decoder layers) and the fixed tensors.
+  auto need_mat = [&](uint32_t kind, uint32_t layer, uint32_t rows, uint32_t cols, DevMat* out) -> int32_t {
+    const Tensor* t = find(kind, layer);
+    if (!t) return QWC_NOT_FOUND;
+    if (is_vector_kind(kind) || t->rows != rows || t->cols != cols) return QWC_SHAPE_MISMATCH;
+    *out = make_mat(*t);
+    return kernel_fits(*out);
+  };
+  auto need_vec = [&](uint32_t kind, uint32_t layer, uint32_t width, const float** out) -> int32_t {
+    const Tensor* t = find(kind, layer);
+    if (!t) return QWC_NOT_FOUND;
+    if (t->format != QWC_FORMAT_F32 || uint64_t(t->rows) * t->cols != width) return QWC_SHAPE_MISMATCH;
+    *out = static_cast<const float*>(t->buf->ptr);
+    return QWC_OK;
+  };
+
+  DevModel& m = h->host_model;
+  m = DevModel{};
+  QWC_TRY(need_mat(QWC_KIND_DECODER_EMBED_TOKENS, 0, c.vocab_size, hidden, &m.embed));
+  QWC_TRY(need_vec(QWC_KIND_DECODER_FINAL_NORM, 0, hidden, &m.final_norm));
+  if (tied) {
+    m.lm_head = m.embed;  // model.zig:391-394
+  } else {
+    QWC_TRY(need_mat(QWC_KIND_DECODER_OUTPUT, 0, c.vocab_size, hidden, &m.lm_head));
+  }
+  // The lm_head's argmax runs per warp, so one warp must hold a whole row.
+  if ((m.lm_head.code_row / 512) * (m.lm_head.format == kFormatQ4 ? 32u : 16u) > 96) return QWC_UNSUPPORTED_MODEL;
+  for (uint32_t l = 0; l < L; ++l) {
+    DevLayer& D = m.layers[l];
+    const uint32_t layer = l + 1;  // decoder_layer_base (layout.zig:26)
+    QWC_TRY(need_mat(QWC_KIND_DECODER_Q, layer, qw, hidden, &D.q));
+    QWC_TRY(need_mat(QWC_KIND_DECODER_K, layer, kvw, hidden, &D.k));
+    QWC_TRY(need_mat(QWC_KIND_DECODER_V, layer, kvw, hidden, &D.v));
+    QWC_TRY(need_mat(QWC_KIND_DECODER_O, layer, hidden, qw, &D.o));
+    QWC_TRY(need_vec(QWC_KIND_DECODER_Q_NORM, layer, c.text_head_dim, &D.q_norm));
+    QWC_TRY(need_vec(QWC_KIND_DECODER_K_NORM, layer, c.text_head_dim, &D.k_norm));
+    QWC_TRY(need_vec(QWC_KIND_DECODER_ATTENTION_NORM, layer, hidden, &D.attn_norm));
+    QWC_TRY(need_vec(QWC_KIND_DECODER_FFN_NORM, layer, hidden, &D.ffn_norm));
+    QWC_TRY(need_mat(QWC_KIND_DECODER_GATE, layer, ffn, hidden, &D.gate));
+    QWC_TRY(need_mat(QWC_KIND_DECODER_UP, layer, ffn, hidden, &D.up));
+    QWC_TRY(need_mat(QWC_KIND_DECODER_DOWN, layer, hidden, ffn, &D.down));
+    if (D.q.format != D.k.format || D.q.format != D.v.format || D.gate.format != D.up.format) {
+      return QWC_UNSUPPORTED_MODEL;
+    }
+  }
+
+  cudaSetDevice(h->device);
+  h->grid = decode_grid_size(h->device);
+  if (h->grid <= 0) return QWC_INVALID_STATE;
+  // Rows of a non-LM stage held by one CTA must fit the kernel's row buffers.
+  const uint32_t widest = std::max({qw + 2 * kvw, ffn, hidden});
+  if ((widest + h->grid - 1) / h->grid > 256) return QWC_UNSUPPORTED_MODEL;
+
+  m.n_layers = L;
+  m.hidden = hidden;
+  m.q_heads = c.text_attention_heads;
+  m.kv_heads = c.text_key_value_heads;
+  m.head_dim = c.text_head_dim;
+  m.ffn = ffn;
+  m.vocab = c.vocab_size;
+  m.max_positions = c.max_positions;
+  m.eps = c.text_rms_norm_eps;
+  m.attn_scaling = 1.0f / std::sqrt(static_cast<float>(c.text_head_dim));
+  const uint64_t kv_groups = kvw / kGroup;
+  m.cache_scales_bytes = uint64_t(c.max_positions) * kv_groups * 2;
+  m.cache_layer_stride = m.cache_scales_bytes + uint64_t(c.max_positions) * kvw;
+  m.cache_stream_stride = m.cache_layer_stride * L;
+
+  // Rotary tables, built on the host (kernels.zig:534-558) and uploaded.
+  const size_t half = c.text_head_dim / 2;
+  std::vector<float> cos_t(size_t(c.max_positions) * half), sin_t(cos_t.size());
+  build_rope(c.rope_theta, c.text_head_dim, c.max_positions, cos_t.data(), sin_t.data());
+  QWC_TRY(h->rope_cos.alloc(cos_t.size() * 4));
+  QWC_TRY(h->rope_sin.alloc(sin_t.size() * 4));
+  QWC_CUDA(cudaMemcpy(h->rope_cos.ptr, cos_t.data(), cos_t.size() * 4, cudaMemcpyHostToDevice));
+  QWC_CUDA(cudaMemcpy(h->rope_sin.ptr, sin_t.data(), sin_t.size() * 4, cudaMemcpyHostToDevice));
+  m.rope_cos = h->rope_cos.as<float>();
+  m.rope_sin = h->rope_sin.as<float>();
+
+  // q8 key/value cache per stream (decoder.zig:58-65, model.zig:253-260).
+  QWC_TRY(h->k_cache.alloc(m.cache_stream_stride * h->streams));
+  QWC_TRY(h->v_cache.alloc(m.cache_stream_stride * h->streams));
+  QWC_CUDA(cudaMemset(h->k_cache.ptr, 0, h->k_cache.bytes));
+  QWC_CUDA(cudaMemset(h->v_cache.ptr, 0, h->v_cache.bytes));
+
+  h->max_chunks = (c.max_positions + kAttnChunk - 1) / kAttnChunk;
+  QWC_TRY(h->qkv.alloc(size_t(qw + 2 * kvw) * 4));
+  QWC_TRY(h->attn_out.alloc(size_t(qw) * 4));
+  QWC_TRY(h->hidden_g.alloc(size_t(hidden) * 4));
+  QWC_TRY(h->act.alloc(size_t(ffn) * 4));
+  QWC_TRY(h->attn_part.alloc(size_t(c.text_attention_heads) * h->max_chunks * (kHeadDim + 2) * 4));
+  QWC_TRY(h->attn_count.alloc(size_t(c.text_key_value_heads) * 4));
+  QWC_CUDA(cudaMemset(h->attn_count.ptr, 0, h->attn_count.bytes));
+  QWC_TRY(h->amax_val.alloc(size_t(h->grid) * 4));
+  QWC_TRY(h->amax_idx.alloc(size_t(h->grid) * 4));
+  QWC_TRY(h->barrier.alloc(256));
+  QWC_TRY(h->error.alloc(256));
+  QWC_CUDA(cudaMemset(h->error.ptr, 0, h->error.bytes));
+  QWC_TRY(h->tokens_out.alloc(size_t(std::max<uint32_t>(c.max_positions, 256)) * 4));
+  QWC_TRY(h->logits.alloc(size_t(c.vocab_size) * 4));
+  QWC_TRY(h->prompt_ids.alloc(size_t(c.max_positions) * 4));
+  QWC_TRY(h->prompt_rows.alloc(size_t(c.max_positions) * 4));
+  QWC_TRY(h->audio_rows.alloc(size_t(c.max_positions) * hidden * 4));
+
+  QWC_TRY(h->model_buf.alloc(sizeof(DevModel)));
+  QWC_CUDA(cudaMemcpy(h->model_buf.ptr, &m, sizeof(DevModel), cudaMemcpyHostToDevice));
+  h->slots.assign(h->streams, StreamSlot{});
+  h->config = c;
+  return QWC_OK;
+}
+
+// One launch of the persistent decode kernel for stream 0; waits for it and
+// reads back the produced tokens.
+int32_t run_decode(Handle* h, uint32_t n_tokens, uint32_t first_position, uint32_t n_forced, uint32_t first_input,
+                   uint32_t logits_from, std::vector<uint32_t>* tokens) {
+  const DevModel& m = h->host_model;
+  DecodeLaunch L{};
+  L.model = h->model_buf.as<DevModel>();
+  L.k_cache = h->k_cache.as<uint8_t>();
+  L.v_cache = h->v_cache.as<uint8_t>();
+  L.n_tokens = n_tokens;
+  L.first_position = first_position;
+  L.n_forced = n_forced;
+  L.forced_token = h->prompt_ids.as<uint32_t>();
+  L.forced_row = h->prompt_rows.as<int32_t>();
+  L.audio = h->audio_rows.as<float>();
+  L.first_input = first_input;
+  L.logits_from = logits_from;
+  L.tokens_out = h->tokens_out.as<uint32_t>();
+  L.logits_out = h->keep_logits ? h->logits.as<float>() : nullptr;
+  L.qkv = h->qkv.as<float>();
+  L.attn_out = h->attn_out.as<float>();
+  L.hidden_g = h->hidden_g.as<float>();
+  L.act = h->act.as<float>();
+  L.attn_part = h->attn_part.as<float>();
+  L.attn_count = h->attn_count.as<uint32_t>();
+  L.amax_val = h->amax_val.as<float>();
+  L.amax_idx = h->amax_idx.as<uint32_t>();
+  L.barrier = h->barrier.as<uint32_t>();
+  L.error = h->error.as<int32_t>();
+  L.timeout_ns = 4000000000ull;
+  L.max_chunks = h->max_chunks;
+  (void)m;
+  QWC_CUDA(cudaMemsetAsync(h->barrier.ptr, 0, 4, h->stream));
+  const int e = launch_decode(L, h->grid, h->stream);
+  if (e != 0) return status_of(static_cast<cudaError_t>(e));
+  h->launches += 1;
+  int32_t device_error = 0;
+  QWC_CUDA(cudaMemcpyAsync(&device_error, h->error.ptr, 4, cudaMemcpyDeviceToHost, h->stream));
+  if (tokens && n_tokens > logits_from) {
+    tokens->resize(n_tokens);
+    QWC_CUDA(cudaMemcpyAsync(tokens->data(), h->tokens_out.ptr, size_t(n_tokens) * 4, cudaMemcpyDeviceToHost,
+                             h->stream));
+  }
+  QWC_CUDA(cudaStreamSynchronize(h->stream));
+  if (device_error != 0) {
+    cudaMemsetAsync(h->error.ptr, 0, 4, h->stream);
+    cudaStreamSynchronize(h->stream);
+    return QWC_INVALID_STATE;
+  }
+  return QWC_OK;
+}
+
+// src/wasm/model.zig:495-499
+bool ends_sequence(const Config& c, uint32_t token) {
+  return token == c.token_eos_primary || token == c.token_eos_secondary || token == c.token_endoftext;
+}
+
+int32_t stream_begin(Handle* h, uint32_t slot, const uint32_t* prompt, uint32_t prompt_len, const float* audio,
+                     uint32_t audio_steps, uint32_t max_tokens) {
+  if (h->state != State::kLoaded) return QWC_INVALID_STATE;
+  if (slot >= h->slots.size()) return QWC_INVALID_ARGUMENT;
+  StreamSlot& s = h->slots[slot];
+  if (s.decoding) return QWC_INVALID_STATE;
+  const Config& c = h->config;
+  if (max_tokens == 0 || max_tokens > c.max_decode_tokens) return QWC_LIMIT_EXCEEDED;  // model.zig:380-381
+  if (!prompt || prompt_len == 0) return QWC_SHAPE_MISMATCH;                            // decoder.zig:317
+  if (audio_steps > 0 && !audio) return QWC_INVALID_ARGUMENT;
+  if (prompt_len > c.max_positions) return QWC_LIMIT_EXCEEDED;                          // decoder.zig:142
+  std::vector<int32_t> rows(prompt_len);
+  uint32_t audio_index = 0;
+  for (uint32_t i = 0; i < prompt_len; ++i) {
+    if (prompt[i] >= c.vocab_size) return QWC_SHAPE_MISMATCH;  // embeddingRow bounds (decoder.zig:365-367)
+    if (prompt[i] == c.token_audio_pad) {
+      if (audio_index >= audio_steps) return QWC_SHAPE_MISMATCH;  // PromptMismatch (decoder.zig:323)
+      rows[i] = static_cast<int32_t>(audio_index++);
+    } else {
+      rows[i] = -1;
+    }
+  }
+  if (audio_index != audio_steps) return QWC_SHAPE_MISMATCH;  // decoder.zig:331
+  if (slot != 0) return QWC_UNSUPPORTED;
+  cudaSetDevice(h->device);
+  // Decoder.reset (decoder.zig:109-121): the whole cache goes back to zero.
+  const uint64_t stride = h->host_model.cache_stream_stride;
+  QWC_CUDA(cudaMemsetAsync(h->k_cache.as<uint8_t>() + stride * slot, 0, stride, h->stream));
+  QWC_CUDA(cudaMemsetAsync(h->v_cache.as<uint8_t>() + stride * slot, 0, stride, h->stream));
+  QWC_CUDA(cudaMemcpyAsync(h->prompt_ids.ptr, prompt, size_t(prompt_len) * 4, cudaMemcpyHostToDevice, h->stream));
+  QWC_CUDA(cudaMemcpyAsync(h->prompt_rows.ptr, rows.data(), size_t(prompt_len) * 4, cudaMemcpyHostToDevice, h->stream));
+  if (audio_steps) {
+    QWC_CUDA(cudaMemcpyAsync(h->audio_rows.ptr, audio, size_t(audio_steps) * c.text_hidden_size * 4,
+                             cudaMemcpyHostToDevice, h->stream));
+  }
+  std::vector<uint32_t> tokens;
+  QWC_TRY(run_decode(h, prompt_len, 0, prompt_len, 0, prompt_len - 1, &tokens));
+  s = StreamSlot{};
+  s.decoding = true;
+  s.position = prompt_len;
+  s.next_token = tokens[prompt_len - 1];
+  s.max_tokens = max_tokens;
+  s.generated.reserve(max_tokens);
+  return QWC_OK;
+}
+
+// Computes the prediction that follows `token` (which sits at s.position),
+// launching a chunk of steps ahead when none is buffered.
+int32_t advance(Handle* h, StreamSlot& s, uint32_t token, uint32_t budget) {
+  if (s.ahead.empty()) {
+    const Config& c = h->config;
+    if (s.position >= c.max_positions) return QWC_LIMIT_EXCEEDED;  // PositionExceeded (decoder.zig:142)
+    uint32_t n = std::min<uint32_t>(h->step_chunk, budget);
+    n = std::min<uint32_t>(n, c.max_positions - s.position);
+    n = std::max<uint32_t>(n, 1);
+    std::vector<uint32_t> tokens;
+    QWC_TRY(run_decode(h, n, s.position, 0, token, 0, &tokens));
+    for (uint32_t i = 0; i < n; ++i) s.ahead.push_back(tokens[i]);
+    s.position += n;
+  }
+  s.next_token = s.ahead.front();
+  s.ahead.pop_front();
+  return QWC_OK;
+}
+
+// src/wasm/model.zig:423-451
+int32_t stream_step(Handle* h, uint32_t slot, uint32_t* token_out) {
+  if (h->state != State::kLoaded || slot >= h->slots.size()) return QWC_INVALID_STATE;
+  StreamSlot& s = h->slots[slot];
+  if (!s.decoding) return QWC_INVALID_STATE;
+  if (s.finished) return 0;
+  if (!h->ignore_eos && ends_sequence(h->config, s.next_token)) {
+    s.finished = true;
+    return 0;
+  }
+  if (s.generated.size() >= s.max_tokens) {
+    s.finished = true;
+    return 0;
+  }
+  *token_out = s.next_token;
+  s.generated.push_back(s.next_token);
+  if (s.generated.size() >= s.max_tokens) {
+    s.finished = true;
+    return 1;
+  }
+  const uint32_t budget = s.max_tokens - static_cast<uint32_t>(s.generated.size());
+  QWC_TRY(advance(h, s, s.next_token, budget));
+  return 1;
+}
+
+}  // namespace
+}  // namespace qwc
+
+using namespace qwc;
+
+extern "C" {
+
+uint32_t qwc_abi_version(void) { return (QWC_ABI_MAJOR << 16) | QWC_ABI_MINOR; }
+
+uint32_t qwc_features(void) { return QWC_FEATURE_MODEL | QWC_FEATURE_DECODE; }
+
+const char* qwc_status_message(int32_t status) {
+  switch (status) {
+    case QWC_OK: return "ok";
+    case QWC_INVALID_ARGUMENT: return "invalid argument";
+    case QWC_OUT_OF_MEMORY: return "out of memory";
+    case QWC_UNSUPPORTED: return "unsupported";
+    case QWC_BAD_MAGIC: return "bad magic";
+    case QWC_BAD_VERSION: return "bad version";
+    case QWC_CHECKSUM_MISMATCH: return "checksum mismatch";
+    case QWC_SHAPE_MISMATCH: return "shape mismatch";
+    case QWC_INVALID_STATE: return "invalid state";
+    case QWC_LIMIT_EXCEEDED: return "limit exceeded";
+    case QWC_NOT_FOUND: return "not found";
+    case QWC_TRUNCATED: return "truncated input";
+    case QWC_INVALID_ENCODING: return "invalid encoding";
+    case QWC_UNSUPPORTED_MODEL: return "unsupported model";
+    case QWC_AUDIO_TOO_LONG: return "audio too long";
+    default: return "unknown status";
+  }
+}
+
+uint32_t qwc_create(int32_t device) {
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  if (device < 0 || device >= count) return 0;
+  if (cudaSetDevice(device) != cudaSuccess) return 0;
+  auto h = std::make_unique<Handle>();
+  h->device = device;
+  if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess) return 0;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  const uint32_t id = g_next_handle++;
+  g_handles[id] = std::move(h);
+  return id;
+}
+
+int32_t qwc_destroy(uint32_t handle) {
+  std::unique_ptr<Handle> h;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    auto it = g_handles.find(handle);
+    if (it == g_handles.end()) return QWC_INVALID_ARGUMENT;
+    h = std::move(it->second);
+    g_handles.erase(it);
+  }
+  cudaSetDevice(h->device);
+  cudaStreamSynchronize(h->stream);
+  release_model(h.get());
+  return QWC_OK;
+}
+
+int32_t qwc_set_option(uint32_t handle, uint32_t option, uint32_t value) {
+  Handle* h = lookup(handle);
+  if (!h) return QWC_INVALID_ARGUMENT;
+  switch (option) {
+    case QWC_OPTION_IGNORE_EOS: h->ignore_eos = value != 0; return QWC_OK;
+    case QWC_OPTION_KEEP_LOGITS: h->keep_logits = value != 0; return QWC_OK;
+    case QWC_OPTION_STEP_CHUNK:
+      if (value == 0 || value > 256) return QWC_INVALID_ARGUMENT;
+      h->step_chunk = value;
+      return QWC_OK;
+    default: return QWC_INVALID_ARGUMENT;
+  }
+}
+
+// src/wasm/model.zig:136-141: releases whatever the handle holds.
+int32_t qwc_model_begin(uint32_t handle) {
+  Handle* h = lookup(handle);
+  if (!h) return QWC_INVALID_ARGUMENT;
+  cudaSetDevice(h->device);
+  cudaStreamSynchronize(h->stream);
+  release_model(h);
+  h->cache_format = QWC_CACHE_F32;
+  h->streams = 1;
+  h->state = State::kReady;
+  return QWC_OK;
+}
+
+int32_t qwc_model_add_tensor(uint32_t handle, uint32_t kind, uint32_t layer, uint32_t format, uint32_t rows,
+                             uint32_t cols, const void* payload, uint64_t len) {
+  Handle* h = lookup(handle);
+  if (!h) return QWC_INVALID_ARGUMENT;
+  if (h->state != State::kReady) return QWC_INVALID_STATE;
+  if (!payload || rows == 0 || cols == 0) return QWC_INVALID_ARGUMENT;
+  if (kind < QWC_KIND_DECODER_EMBED_TOKENS || kind > QWC_KIND_DECODER_DOWN) return QWC_UNSUPPORTED_MODEL;
+  if (h->tensors.count({kind, layer})) return QWC_INVALID_ARGUMENT;  // DuplicateTensor
+  Tensor t;
+  t.kind = kind;
+  t.layer = layer;
+  t.format = format;
+  t.rows = rows;
+  t.cols = cols;
+  uint64_t need = 0;
+  if (format == QWC_FORMAT_F32) {
+    need = uint64_t(rows) * cols * 4;
+  } else if (format == QWC_FORMAT_Q4 || format == QWC_FORMAT_Q8) {
+    if (cols % kGroup != 0) return QWC_SHAPE_MISMATCH;  // RowNotGroupAligned (quant.zig:77-81)
+    // quant.zig:144-176 with a 16-byte-aligned base.
+    const uint64_t groups = uint64_t(rows) * (cols / kGroup);
+    const uint64_t scales_len = groups * 2;
+    t.scales_offset = 0;
+    t.codes_offset = (scales_len + 15) / 16 * 16;
+    need = t.codes_offset + groups * data_bytes_per_group(format);
+  } else {
+    return QWC_UNSUPPORTED_MODEL;
+  }
+  if (len < need) return QWC_TRUNCATED;
+  cudaSetDevice(h->device);
+  t.buf = std::make_unique<DevBuf>();
+  QWC_TRY(t.buf->alloc(need));
+  QWC_CUDA(cudaMemcpy(t.buf->ptr, payload, need, cudaMemcpyHostToDevice));
+  h->weight_bytes += need;
+  h->tensors.emplace(std::make_pair(kind, layer), std::move(t));
+  return QWC_OK;
+}
+
+int32_t qwc_model_set_cache_format(uint32_t handle, uint32_t format) {
+  Handle* h = lookup(handle);
+  if (!h) return QWC_INVALID_ARGUMENT;
+  if (format != QWC_CACHE_F32 && format != QWC_CACHE_Q8) return QWC_INVALID_ARGUMENT;
+  if (h->state != State::kReady || h->tensors.empty()) return QWC_INVALID_STATE;  // model.zig:184-188
+  h->cache_format = format;
+  return QWC_OK;
+}
+
+int32_t qwc_model_set_streams(uint32_t handle, uint32_t streams) {
+  Handle* h = lookup(handle);
+  if (!h) return QWC_INVALID_ARGUMENT;
+  if (h->state != State::kReady) return QWC_INVALID_STATE;
+  if (streams == 0) return QWC_INVALID_ARGUMENT;
+  if (streams != 1) return QWC_UNSUPPORTED;
+  h->streams = streams;
+  return QWC_OK;
+}
+
+int32_t qwc_model_finish(uint32_t handle, const void* config, uint32_t config_len) {
+  Handle* h = lookup(handle);
+  if (!h) return QWC_INVALID_ARGUMENT;
+  if (h->state != State::kReady) return QWC_INVALID_STATE;
+  if (!config) return QWC_INVALID_ARGUMENT;
+  if (config_len != sizeof(Config)) return QWC_TRUNCATED;  // model_config.zig:353-354
+  Config c;
+  std::memcpy(&c, config, sizeof(Config));
+  QWC_TRY(validate_config(c));
+  if (h->tensors.empty()) return QWC_INVALID_STATE;  // model.zig:208
+  const int32_t st = finish_model(h, c);
+  if (st != QWC_OK) {
+    // model.zig:197-204: a failed load releases what it allocated; shards stay.
+    for (DevBuf* b : {&h->model_buf, &h->rope_cos, &h->rope_sin, &h->k_cache, &h->v_cache, &h->qkv, &h->attn_out,
+                      &h->hidden_g, &h->act, &h->attn_part, &h->attn_count, &h->amax_val, &h->amax_idx, &h->barrier,
+                      &h->error, &h->tokens_out, &h->logits, &h->prompt_ids, &h->prompt_rows, &h->audio_rows}) {
+      b->alloc(0);
+    }
+    return st;
+  }
+  h->state = State::kLoaded;
+  return QWC_OK;
+}
+
+int32_t qwc_model_requirements(uint32_t handle, qwc_requirements* out) {
+  Handle* h = lookup(handle);
+  if (!h || !out) return QWC_INVALID_ARGUMENT;
+  if (h->state != State::kLoaded) return QWC_INVALID_STATE;
+  qwc_requirements r{};
+  r.weight_bytes = h->weight_bytes;
+  r.cache_bytes = h->k_cache.bytes + h->v_cache.bytes;
+  uint64_t scratch = 0;
+  for (const DevBuf* b : {&h->model_buf, &h->rope_cos, &h->rope_sin, &h->qkv, &h->attn_out, &h->hidden_g, &h->act,
+                          &h->attn_part, &h->attn_count, &h->amax_val, &h->amax_idx, &h->barrier, &h->error,
+                          &h->tokens_out, &h->logits, &h->prompt_ids, &h->prompt_rows, &h->audio_rows}) {
+    scratch += b->bytes;
+  }
+  r.scratch_bytes = scratch;
+  r.total_bytes = r.weight_bytes + r.cache_bytes + r.scratch_bytes;
+  r.max_positions = h->config.max_positions;
+  r.max_audio_frames = kCapacityFrames;
+  r.max_decode_tokens = h->config.max_decode_tokens;
+  r.reserved = 0;
+  *out = r;
+  return QWC_OK;
+}
+
+int32_t qwc_model_tensor_count(uint32_t handle, uint32_t* out) {
+  Handle* h = lookup(handle);
+  if (!h || !out) return QWC_INVALID_ARGUMENT;
+  if (h->state != State::kLoaded) return QWC_INVALID_STATE;
+  *out = static_cast<uint32_t>(h->tensors.size());
+  return QWC_OK;
+}
+
+int32_t qwc_decode_begin(uint32_t handle, const uint32_t* prompt, uint32_t prompt_len, const float* audio,
+                         uint32_t audio_steps, uint32_t max_tokens) {
+  Handle* h = lookup(handle);
+  if (!h) return QWC_INVALID_ARGUMENT;
+  return stream_begin(h, 0, prompt, prompt_len, audio, audio_steps, max_tokens);
+}
+
+int32_t qwc_decode_step(uint32_t handle, uint32_t* token_out) {
+  Handle* h = lookup(handle);
+  if (!h || !token_out) return QWC_INVALID_ARGUMENT;
+  cudaSetDevice(h->device);
+  return stream_step(h, 0, token_out);
+}
+
+int32_t qwc_stream_tokens(uint32_t handle, uint32_t slot, uint32_t* out, uint32_t capacity) {
+  Handle* h = lookup(handle);
+  if (!h) return QWC_INVALID_ARGUMENT;
+  if (h->state != State::kLoaded || slot >= h->slots.size() || !h->slots[slot].decoding) return QWC_INVALID_STATE;
+  const StreamSlot& s = h->slots[slot];
+  if (capacity < s.generated.size()) return QWC_LIMIT_EXCEEDED;  // model.zig:455-461
+  if (!s.generated.empty() && !out) return QWC_INVALID_ARGUMENT;
+  std::copy(s.generated.begin(), s.generated.end(), out);
+  return static_cast<int32_t>(s.generated.size());
+}
+
+int32_t qwc_decode_tokens(uint32_t handle, uint32_t* out, uint32_t capacity) {
+  return qwc_stream_tokens(handle, 0, out, capacity);
+}
+
+int32_t qwc_stream_end(uint32_t handle, uint32_t slot) {
+  Handle* h = lookup(handle);
+  if (!h) return QWC_INVALID_ARGUMENT;
+  if (h->state != State::kLoaded || slot >= h->slots.size() || !h->slots[slot].decoding) return QWC_INVALID_STATE;
+  cudaSetDevice(h->device);
+  const uint64_t stride = h->host_model.cache_stream_stride;
+  QWC_CUDA(cudaMemsetAsync(h->k_cache.as<uint8_t>() + stride * slot, 0, stride, h->stream));
+  QWC_CUDA(cudaMemsetAsync(h->v_cache.as<uint8_t>() + stride * slot, 0, stride, h->stream));
+  QWC_CUDA(cudaStreamSynchronize(h->stream));
+  h->slots[slot] = StreamSlot{};
+  return QWC_OK;
+}
+
+int32_t qwc_decode_end(uint32_t handle) { return qwc_stream_end(handle, 0); }
+
+int32_t qwc_stream_begin(uint32_t handle, uint32_t slot, const uint32_t* prompt, uint32_t prompt_len,
+                         const float* audio, uint32_t audio_steps, uint32_t max_tokens) {
+  Handle* h = lookup(handle);
+  if (!h) return QWC_INVALID_ARGUMENT;
+  return stream_begin(h, slot, prompt, prompt_len, audio, audio_steps, max_tokens);
+}
+
+int32_t qwc_streams_step(uint32_t handle, uint32_t* tokens_out, int32_t* results) {
+  Handle* h = lookup(handle);
+  if (!h || !tokens_out || !results) return QWC_INVALID_ARGUMENT;
+  if (h->state != State::kLoaded) return QWC_INVALID_STATE;
+  cudaSetDevice(h->device);
+  int32_t produced = 0;
+  for (uint32_t slot = 0; slot < h->slots.size(); ++slot) {
+    if (!h->slots[slot].decoding) {
+      results[slot] = 0;
+      continue;
+    }
+    const int32_t r = stream_step(h, slot, &tokens_out[slot]);
+    results[slot] = r;
+    if (r == 1) ++produced;
+    if (r < 0) return r;
+  }
+  return produced;
+}
+
+int32_t qwc_decode_run_timed(uint32_t handle, uint32_t steps, float* device_ms) {
+  Handle* h = lookup(handle);
+  if (!h || !device_ms) return QWC_INVALID_ARGUMENT;
+  if (h->state != State::kLoaded || h->slots.empty() || !h->slots[0].decoding) return QWC_INVALID_STATE;
+  StreamSlot& s = h->slots[0];
+  if (s.generated.size() + steps > s.max_tokens) return QWC_LIMIT_EXCEEDED;
+  if (s.position + steps > h->config.max_positions) return QWC_LIMIT_EXCEEDED;
+  cudaSetDevice(h->device);
+  s.ahead.clear();
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  float total = 0.0f;
+  uint32_t token = s.next_token;
+  uint32_t done = 0;
+  std::vector<uint32_t> tokens;
+  int32_t st = QWC_OK;
+  while (done < steps && st == QWC_OK) {
+    const uint32_t n = std::min<uint32_t>(h->step_chunk, steps - done);
+    cudaEventRecord(e0, h->stream);
+    st = run_decode(h, n, s.position, 0, token, 0, &tokens);
+    if (st != QWC_OK) break;
+    cudaEventRecord(e1, h->stream);
+    cudaEventSynchronize(e1);
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, e0, e1);
+    total += ms;
+    for (uint32_t i = 0; i < n; ++i) {
+      s.generated.push_back(token);
+      token = tokens[i];
+    }
+    s.position += n;
+    done += n;
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  s.next_token = token;
+  *device_ms = total;
+  return st;
+}
+
+int32_t qwc_debug_logits(uint32_t handle, uint32_t slot, float* out, uint32_t count) {
+  Handle* h = lookup(handle);
+  if (!h || !out) return QWC_INVALID_ARGUMENT;
+  if (h->state != State::kLoaded || slot >= h->slots.size()) return QWC_INVALID_STATE;
+  if (!h->keep_logits) return QWC_INVALID_STATE;
+  if (count < h->config.vocab_size) return QWC_LIMIT_EXCEEDED;
+  cudaSetDevice(h->device);
+  QWC_CUDA(cudaMemcpyAsync(out, h->logits.ptr, size_t(h->config.vocab_size) * 4, cudaMemcpyDeviceToHost, h->stream));
+  QWC_CUDA(cudaStreamSynchronize(h->stream));
+  return QWC_OK;
+}
+
+int32_t qwc_debug_cache(uint32_t handle, uint32_t slot, uint32_t which, void* out, uint64_t len) {
+  Handle* h = lookup(handle);
+  if (!h || !out || which > 1) return QWC_INVALID_ARGUMENT;
+  if (h->state != State::kLoaded || slot >= h->slots.size()) return QWC_INVALID_STATE;
+  const uint64_t stride = h->host_model.cache_stream_stride;
+  if (len < stride) return QWC_LIMIT_EXCEEDED;
+  cudaSetDevice(h->device);
+  const uint8_t* src = (which == 0 ? h->k_cache.as<uint8_t>() : h->v_cache.as<uint8_t>()) + stride * slot;
+  QWC_CUDA(cudaMemcpyAsync(out, src, stride, cudaMemcpyDeviceToHost, h->stream));
+  QWC_CUDA(cudaStreamSynchronize(h->stream));
+  return QWC_OK;
+}
+
+uint64_t qwc_kernel_launches(uint32_t handle) {
+  Handle* h = lookup(handle);
+  return h ? h->launches : 0;
+}
+
+int32_t qwc_rope_tables(float theta, uint32_t head_dim, uint32_t max_positions, float* cos_out, float* sin_out) {
+  if (!cos_out || !sin_out || head_dim == 0 || head_dim % 2 != 0) return QWC_INVALID_ARGUMENT;
+  build_rope(theta, head_dim, max_positions, cos_out, sin_out);
+  return QWC_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,225 @@
+// qwc_device.cuh -- device helpers for the sm_100a decoder kernels.
+//
+// Dequantization strategy (exact): a 4-bit code u sits at bit offset 4*i of a
+// 32-bit word. OR-ing the masked nibble into the mantissa of 2^23 gives the
+// float 2^23 + u*16^i exactly (i <= 4; nibbles 5..7 are shifted down by 12
+// first). Subtracting 2^23 + 8*16^i leaves (u - 8)*16^i exactly, and the
+// matching activation is pre-scaled by 16^-i, so every product equals the
+// reference's (u - 8) * x (src/core/quant.zig:315-345) before rounding. q8
+// bytes go through one byte-permute into 2^23 + b the same way. The
+// arithmetic runs on the packed fma.rn.f32x2 / add.rn.f32x2 of sm_100.
+#pragma once
+
+#include <cstdint>
+#include <cuda_fp16.h>
+
+namespace qwc {
+
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+
+__device__ __forceinline__ float2 unpack2(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
+__device__ __forceinline__ float bits_f32(uint32_t b) { return __uint_as_float(b); }
+
+constexpr uint32_t kMagic = 0x4B000000u;  // 2^23
+// -(2^23 + 8 * 16^i): the q4 bias of nibble position i after the magic OR.
+constexpr float kNegM0 = -8388616.0f;
+constexpr float kNegM1 = -8388736.0f;
+constexpr float kNegM2 = -8390656.0f;
+constexpr float kNegM3 = -8421376.0f;
+constexpr float kNegM4 = -8912896.0f;
+constexpr float kNegQ8 = -8388736.0f;  // -(2^23 + 128)
+
+// Pre-scale of the activation paired with nibble position i of a word:
+// 16^-i for i <= 4, 16^-(i-3) for the shifted nibbles 5..7.
+__host__ __device__ constexpr float q4_xscale(int i) {
+  return i == 0 ? 1.0f
+       : i == 1 ? 0.0625f
+       : i == 2 ? 0.00390625f
+       : i == 3 ? 0.000244140625f
+       : i == 4 ? 0.0000152587890625f
+       : i == 5 ? 0.00390625f
+       : i == 6 ? 0.000244140625f
+                : 0.0000152587890625f;
+}
+
+// Accumulates 8 nibbles of `w` against 4 packed pre-scaled activation pairs.
+__device__ __forceinline__ void q4_word(uint32_t w, const uint64_t* x2, uint64_t& acc) {
+  const uint32_t h = w >> 12;
+  const uint64_t v01 = pack2(bits_f32((w & 0x0000000Fu) | kMagic), bits_f32((w & 0x000000F0u) | kMagic));
+  const uint64_t v23 = pack2(bits_f32((w & 0x00000F00u) | kMagic), bits_f32((w & 0x0000F000u) | kMagic));
+  const uint64_t v45 = pack2(bits_f32((w & 0x000F0000u) | kMagic), bits_f32((h & 0x00000F00u) | kMagic));
+  const uint64_t v67 = pack2(bits_f32((h & 0x0000F000u) | kMagic), bits_f32((h & 0x000F0000u) | kMagic));
+  acc = fma2(add2(v01, pack2(kNegM0, kNegM1)), x2[0], acc);
+  acc = fma2(add2(v23, pack2(kNegM2, kNegM3)), x2[1], acc);
+  acc = fma2(add2(v45, pack2(kNegM4, kNegM2)), x2[2], acc);
+  acc = fma2(add2(v67, pack2(kNegM3, kNegM4)), x2[3], acc);
+}
+
+// 32 q4 weights (one 16-byte chunk) against 16 packed activation pairs.
+__device__ __forceinline__ float q4_chunk_dot(uint4 w, const uint64_t* x2) {
+  uint64_t a = 0, b = 0;
+  q4_word(w.x, x2 + 0, a);
+  q4_word(w.y, x2 + 4, b);
+  q4_word(w.z, x2 + 8, a);
+  q4_word(w.w, x2 + 12, b);
+  const float2 fa = unpack2(a), fb = unpack2(b);
+  return (fa.x + fa.y) + (fb.x + fb.y);
+}
+
+__device__ __forceinline__ void q8_word(uint32_t w, const uint64_t* x2, uint64_t& acc) {
+  const uint64_t v01 = pack2(bits_f32(__byte_perm(w, kMagic, 0x7440)), bits_f32(__byte_perm(w, kMagic, 0x7441)));
+  const uint64_t v23 = pack2(bits_f32(__byte_perm(w, kMagic, 0x7442)), bits_f32(__byte_perm(w, kMagic, 0x7443)));
+  const uint64_t bias = pack2(kNegQ8, kNegQ8);
+  acc = fma2(add2(v01, bias), x2[0], acc);
+  acc = fma2(add2(v23, bias), x2[1], acc);
+}
+
+// 16 q8 weights (one 16-byte chunk) against 8 packed activation pairs.
+__device__ __forceinline__ float q8_chunk_dot(uint4 w, const uint64_t* x2) {
+  uint64_t a = 0, b = 0;
+  q8_word(w.x, x2 + 0, a);
+  q8_word(w.y, x2 + 2, b);
+  q8_word(w.z, x2 + 4, a);
+  q8_word(w.w, x2 + 6, b);
+  const float2 fa = unpack2(a), fb = unpack2(b);
+  return (fa.x + fa.y) + (fb.x + fb.y);
+}
+
+__device__ __forceinline__ float f16_bits_to_f32(uint16_t bits) { return __half2float(__ushort_as_half(bits)); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// L2-coherent loads for data other CTAs wrote during this launch.
+__device__ __forceinline__ float ld_cg(const float* p) { return __ldcg(p); }
+__device__ __forceinline__ float4 ld_cg4(const float4* p) { return __ldcg(p); }
+
+__device__ __forceinline__ uint4 ld_nc4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---- mbarrier and bulk async copy (sm_90+ PTX; no multicast) ----
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bulk copy global -> shared, completing on `bar` (cp.async.bulk, non-multicast).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Waits on an mbarrier phase with a wall-clock bound. Returns false (and sets
+// *error) if the bound is hit or another CTA already reported an error.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int32_t* error, uint64_t deadline,
+                                                  int32_t code) {
+  uint32_t spins = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if ((++spins & 255u) == 0) {
+      if (*reinterpret_cast<volatile int32_t*>(error) != 0) return false;
+      if (global_timer_ns() > deadline) {
+        atomicCAS(error, 0, code);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void red_release_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Named barrier over the consumer warps only (the producer warp never joins).
+__device__ __forceinline__ void consumer_sync(uint32_t threads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(threads) : "memory");
+}
+
+// quant.zig:280-288 for q8 (bias 128): round half away from zero against the
+// stored f16 scale, then clamp into [-128, 127].
+__device__ __forceinline__ uint8_t q8_code(float value, float stored_scale) {
+  if (stored_scale == 0.0f) return 128;
+  const float scaled = __fdiv_rn(value, stored_scale);
+  const float rounded = scaled >= 0.0f ? floorf(__fadd_rn(scaled, 0.5f)) : ceilf(__fsub_rn(scaled, 0.5f));
+  int code;
+  if (rounded <= -128.0f) code = -128;
+  else if (rounded >= 127.0f) code = 127;
+  else code = static_cast<int>(rounded);
+  return static_cast<uint8_t>(code + 128);
+}
+
+}  // namespace qwc

@@ -1,0 +1,230 @@
+"""Python host binding of libqwenscriber_cuda (the CUDA decoder backend).
+
+`CudaModel` mirrors the reference runtime's model and decode families
+(src/wasm/exports.zig `qw_model_*` / `qw_decode_*`, src/wasm/model.zig) with
+the same argument meaning, state machine and error codes: a negative status
+raises `QwcError` carrying the reference's status number (src/wasm/abi.zig:50-84).
+
+The library must have been built for sm_100a (`qwenscriber_b200.build`); there
+is no CPU fallback: without the shared library or a CUDA device every call
+fails loudly.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, c_char_p, c_float, c_int32, c_uint32, c_uint64, c_void_p
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libqwenscriber_cuda.so")
+
+STATUS = {
+    0: "ok", -1: "invalid_argument", -2: "out_of_memory", -3: "unsupported", -4: "bad_magic", -5: "bad_version",
+    -6: "checksum_mismatch", -7: "shape_mismatch", -8: "invalid_state", -9: "limit_exceeded", -10: "not_found",
+    -11: "truncated", -12: "invalid_encoding", -13: "unsupported_model", -14: "audio_too_long",
+}
+
+CACHE_F32, CACHE_Q8 = 0, 1
+OPTION_IGNORE_EOS, OPTION_KEEP_LOGITS, OPTION_STEP_CHUNK = 1, 2, 3
+FEATURE_MODEL, FEATURE_DECODE, FEATURE_STREAMS = 1 << 3, 1 << 4, 1 << 8
+
+# Every symbol include/qwenscriber_cuda.h declares: (restype, argtypes).
+SIGNATURES = {
+    "qwc_abi_version": (c_uint32, []),
+    "qwc_features": (c_uint32, []),
+    "qwc_create": (c_uint32, [c_int32]),
+    "qwc_destroy": (c_int32, [c_uint32]),
+    "qwc_status_message": (c_char_p, [c_int32]),
+    "qwc_set_option": (c_int32, [c_uint32, c_uint32, c_uint32]),
+    "qwc_model_begin": (c_int32, [c_uint32]),
+    "qwc_model_add_tensor": (c_int32, [c_uint32, c_uint32, c_uint32, c_uint32, c_uint32, c_uint32, c_void_p, c_uint64]),
+    "qwc_model_set_cache_format": (c_int32, [c_uint32, c_uint32]),
+    "qwc_model_set_streams": (c_int32, [c_uint32, c_uint32]),
+    "qwc_model_finish": (c_int32, [c_uint32, c_void_p, c_uint32]),
+    "qwc_model_requirements": (c_int32, [c_uint32, c_void_p]),
+    "qwc_model_tensor_count": (c_int32, [c_uint32, POINTER(c_uint32)]),
+    "qwc_decode_begin": (c_int32, [c_uint32, c_void_p, c_uint32, c_void_p, c_uint32, c_uint32]),
+    "qwc_decode_step": (c_int32, [c_uint32, POINTER(c_uint32)]),
+    "qwc_decode_tokens": (c_int32, [c_uint32, c_void_p, c_uint32]),
+    "qwc_decode_end": (c_int32, [c_uint32]),
+    "qwc_stream_begin": (c_int32, [c_uint32, c_uint32, c_void_p, c_uint32, c_void_p, c_uint32, c_uint32]),
+    "qwc_streams_step": (c_int32, [c_uint32, c_void_p, c_void_p]),
+    "qwc_stream_tokens": (c_int32, [c_uint32, c_uint32, c_void_p, c_uint32]),
+    "qwc_stream_end": (c_int32, [c_uint32, c_uint32]),
+    "qwc_decode_run_timed": (c_int32, [c_uint32, c_uint32, POINTER(c_float)]),
+    "qwc_debug_logits": (c_int32, [c_uint32, c_uint32, c_void_p, c_uint32]),
+    "qwc_debug_cache": (c_int32, [c_uint32, c_uint32, c_uint32, c_void_p, c_uint64]),
+    "qwc_kernel_launches": (c_uint64, [c_uint32]),
+    "qwc_rope_tables": (c_int32, [c_float, c_uint32, c_uint32, c_void_p, c_void_p]),
+    "qwc_op_dequantize": (c_int32, [c_uint32, c_void_p, c_void_p, c_uint32, c_uint32, c_void_p, c_void_p]),
+    "qwc_op_quantize_q8": (c_int32, [c_void_p, c_uint32, c_uint32, c_void_p, c_void_p, c_void_p]),
+    "qwc_op_gemv": (c_int32, [c_uint32, c_void_p, c_void_p, c_uint32, c_uint32, c_void_p, c_void_p, c_void_p]),
+    "qwc_op_attention_q8": (
+        c_int32,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_uint32, c_uint32, c_uint32, c_uint32, c_void_p, c_void_p],
+    ),
+    "qwc_op_argmax": (c_int32, [c_void_p, c_uint32, c_void_p, c_void_p]),
+    "qwc_op_rmsnorm": (c_int32, [c_void_p, c_void_p, c_uint32, c_uint32, c_float, c_void_p, c_void_p]),
+    "qwc_op_rope": (c_int32, [c_void_p, c_uint32, c_uint32, c_void_p, c_void_p, c_uint32, c_void_p]),
+    "qwc_op_silu_mul": (c_int32, [c_void_p, c_void_p, c_uint32, c_void_p, c_void_p]),
+}
+
+
+class QwcError(RuntimeError):
+    def __init__(self, status: int, call: str):
+        self.status = status
+        self.name = STATUS.get(status, "unknown")
+        super().__init__(f"{call} failed: {self.name} ({status})")
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Loads the in-tree shared library; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise FileNotFoundError(f"{LIB_PATH} is missing: run qwenscriber_b200.build.build() first")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(status: int, call: str) -> int:
+    if status < 0:
+        raise QwcError(status, call)
+    return status
+
+
+def _ptr(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data
+
+
+class Requirements(ctypes.Structure):
+    _fields_ = [
+        ("weight_bytes", c_uint64), ("cache_bytes", c_uint64), ("scratch_bytes", c_uint64), ("total_bytes", c_uint64),
+        ("max_positions", c_uint32), ("max_audio_frames", c_uint32), ("max_decode_tokens", c_uint32),
+        ("reserved", c_uint32),
+    ]
+
+
+assert ctypes.sizeof(Requirements) == 48
+
+
+class CudaModel:
+    """One handle bound to one CUDA device: a loaded decoder and its streams."""
+
+    def __init__(self, device: int = 0):
+        self._L = lib()
+        self.handle = self._L.qwc_create(device)
+        if self.handle == 0:
+            raise QwcError(-1, f"qwc_create({device})")
+        self.vocab = 0
+
+    def close(self) -> None:
+        if self.handle:
+            self._L.qwc_destroy(self.handle)
+            self.handle = 0
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---- model family ----
+    def begin(self) -> None:
+        check(self._L.qwc_model_begin(self.handle), "qwc_model_begin")
+
+    def add_tensor(self, kind: int, layer: int, fmt: int, rows: int, cols: int, payload: np.ndarray) -> None:
+        p = np.ascontiguousarray(payload)
+        check(self._L.qwc_model_add_tensor(self.handle, kind, layer, fmt, rows, cols, p.ctypes.data, p.nbytes),
+              f"qwc_model_add_tensor(kind={kind}, layer={layer})")
+
+    def set_cache_format(self, fmt: int) -> None:
+        check(self._L.qwc_model_set_cache_format(self.handle, fmt), "qwc_model_set_cache_format")
+
+    def set_streams(self, n: int) -> None:
+        check(self._L.qwc_model_set_streams(self.handle, n), "qwc_model_set_streams")
+
+    def finish(self, config_bytes: bytes) -> None:
+        buf = ctypes.create_string_buffer(bytes(config_bytes), len(config_bytes))
+        check(self._L.qwc_model_finish(self.handle, buf, len(config_bytes)), "qwc_model_finish")
+        from .config import Config
+        self.vocab = Config.unpack(bytes(config_bytes)).vocab_size
+
+    def requirements(self) -> dict:
+        r = Requirements()
+        check(self._L.qwc_model_requirements(self.handle, ctypes.byref(r)), "qwc_model_requirements")
+        return {name: getattr(r, name) for name, _ in Requirements._fields_}
+
+    def tensor_count(self) -> int:
+        n = c_uint32(0)
+        check(self._L.qwc_model_tensor_count(self.handle, ctypes.byref(n)), "qwc_model_tensor_count")
+        return n.value
+
+    def set_option(self, option: int, value: int) -> None:
+        check(self._L.qwc_set_option(self.handle, option, value), "qwc_set_option")
+
+    # ---- decode family (stream 0) ----
+    def decode_begin(self, prompt, audio: np.ndarray | None, max_tokens: int) -> None:
+        ids = np.ascontiguousarray(np.asarray(prompt, dtype=np.uint32))
+        rows = None if audio is None else np.ascontiguousarray(audio, dtype=np.float32)
+        steps = 0 if rows is None else rows.shape[0]
+        check(self._L.qwc_decode_begin(self.handle, ids.ctypes.data, ids.size, _ptr(rows), steps, max_tokens),
+              "qwc_decode_begin")
+
+    def decode_step(self) -> int | None:
+        """The next token, or None once the sequence has finished (qw_decode_step's 1 / 0)."""
+        out = c_uint32(0)
+        r = check(self._L.qwc_decode_step(self.handle, ctypes.byref(out)), "qwc_decode_step")
+        return out.value if r == 1 else None
+
+    def decode_tokens(self, capacity: int = 8192) -> list[int]:
+        out = np.zeros(capacity, np.uint32)
+        n = check(self._L.qwc_decode_tokens(self.handle, out.ctypes.data, capacity), "qwc_decode_tokens")
+        return out[:n].tolist()
+
+    def decode_end(self) -> None:
+        check(self._L.qwc_decode_end(self.handle), "qwc_decode_end")
+
+    def run_timed(self, steps: int) -> float:
+        ms = c_float(0.0)
+        check(self._L.qwc_decode_run_timed(self.handle, steps, ctypes.byref(ms)), "qwc_decode_run_timed")
+        return ms.value
+
+    # ---- parity hooks ----
+    def debug_logits(self, slot: int = 0) -> np.ndarray:
+        out = np.zeros(self.vocab, np.float32)
+        check(self._L.qwc_debug_logits(self.handle, slot, out.ctypes.data, out.size), "qwc_debug_logits")
+        return out
+
+    def debug_cache(self, which: int, nbytes: int, slot: int = 0) -> np.ndarray:
+        out = np.zeros(nbytes, np.uint8)
+        check(self._L.qwc_debug_cache(self.handle, slot, which, out.ctypes.data, nbytes), "qwc_debug_cache")
+        return out
+
+    def launches(self) -> int:
+        return int(self._L.qwc_kernel_launches(self.handle))
+
+
+def rope_tables(theta: float, head_dim: int, max_positions: int) -> tuple[np.ndarray, np.ndarray]:
+    half = head_dim // 2
+    c = np.zeros(max_positions * half, np.float32)
+    s = np.zeros(max_positions * half, np.float32)
+    check(lib().qwc_rope_tables(theta, head_dim, max_positions, c.ctypes.data, s.ctypes.data), "qwc_rope_tables")
+    return c, s

@@ -1,0 +1,143 @@
+"""Seeded synthetic decoders and prompts for the benchmark configurations.
+
+No checkpoint or dataset is available, so every input is drawn with numpy's
+PCG64 (`default_rng`), in the shapes and value distributions the benchmark
+configurations state:
+
+  * q8 models: f32 weights N(0, 0.02), quantized with the reference's q8
+    blocks (quant.zig:197-288 via `quant.quantize`);
+  * q4 "direct" models: int4 codes uniform in [-8, 7] (bytes uniform in
+    [0, 255], i.e. two uniform nibbles) and f16 group scales |N(0, 0.003)|;
+  * RMSNorm weights 1.0 f32; the lm_head tied to the embedding;
+  * prompts: `audio_rows` N(0, 1) prefix embeddings, then `text_ids` token ids
+    uniform in [0, vocab) (an id equal to Config.token_audio_pad is redrawn,
+    since it would consume an audio row).
+
+Tensors are generated in the reference's layout order (layout.zig: layer 0
+tensors by kind, then decoder layers 1..L by kind) from one generator seeded
+with `seed`; prompts come from `default_rng([seed, 1, stream])`.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+
+import numpy as np
+
+from . import quant
+from .config import Config, qwen3_asr_0p6b, qwen3_asr_1p7b
+
+# container.zig:333-376 (decoder kinds)
+EMBED, FINAL_NORM, OUTPUT = 30, 31, 32
+Q, K, V, O, Q_NORM, K_NORM, ATTN_NORM, FFN_NORM, GATE, UP, DOWN = range(33, 44)
+
+
+@dataclasses.dataclass
+class Tensor:
+    kind: int
+    layer: int
+    fmt: int
+    rows: int
+    cols: int
+    payload: np.ndarray
+
+
+@dataclasses.dataclass
+class Model:
+    config: Config
+    fmt: int
+    tensors: list[Tensor]
+
+    @property
+    def weight_bytes(self) -> int:
+        return sum(t.payload.nbytes for t in self.tensors if t.fmt != quant.F32)
+
+
+def _matrix(rng: np.random.Generator, fmt: int, rows: int, cols: int, std: float, q4_scale_std: float) -> np.ndarray:
+    if fmt == quant.Q8:
+        w = rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(std)
+        scales, codes = quant.quantize(quant.Q8, w)
+    else:
+        codes = rng.integers(0, 256, size=(rows, cols // 2), dtype=np.uint8)
+        s = np.abs(rng.standard_normal((rows, cols // quant.GROUP), dtype=np.float32) * np.float32(q4_scale_std))
+        scales = s.astype(np.float16).view(np.uint16)
+    return quant.payload(fmt, scales, codes)
+
+
+def make_model(config: Config, fmt: int, seed: int, std: float = 0.02, q4_scale_std: float = 0.003) -> Model:
+    rng = np.random.default_rng(seed)
+    c = config
+    h, qw, kvw, ffn = c.text_hidden_size, c.q_width, c.kv_width, c.text_ffn_dim
+    ones = lambda n: np.ones(n, np.float32)  # noqa: E731
+    tensors = [Tensor(EMBED, 0, fmt, c.vocab_size, h, _matrix(rng, fmt, c.vocab_size, h, std, q4_scale_std)),
+               Tensor(FINAL_NORM, 0, quant.F32, 1, h, ones(h))]
+    if not c.tied:
+        tensors.append(Tensor(OUTPUT, 0, fmt, c.vocab_size, h, _matrix(rng, fmt, c.vocab_size, h, std, q4_scale_std)))
+    for layer in range(1, c.text_layers + 1):
+        for kind, rows, cols in ((Q, qw, h), (K, kvw, h), (V, kvw, h), (O, h, qw)):
+            tensors.append(Tensor(kind, layer, fmt, rows, cols, _matrix(rng, fmt, rows, cols, std, q4_scale_std)))
+        tensors.append(Tensor(Q_NORM, layer, quant.F32, 1, c.text_head_dim, ones(c.text_head_dim)))
+        tensors.append(Tensor(K_NORM, layer, quant.F32, 1, c.text_head_dim, ones(c.text_head_dim)))
+        tensors.append(Tensor(ATTN_NORM, layer, quant.F32, 1, h, ones(h)))
+        tensors.append(Tensor(FFN_NORM, layer, quant.F32, 1, h, ones(h)))
+        for kind, rows, cols in ((GATE, ffn, h), (UP, ffn, h), (DOWN, h, ffn)):
+            tensors.append(Tensor(kind, layer, fmt, rows, cols, _matrix(rng, fmt, rows, cols, std, q4_scale_std)))
+    return Model(c, fmt, tensors)
+
+
+@dataclasses.dataclass
+class Prompt:
+    tokens: np.ndarray  # uint32 [n]
+    audio: np.ndarray   # float32 [audio_steps, hidden]
+
+
+def make_prompt(config: Config, audio_rows: int, text_ids: int, seed: int, stream: int = 0) -> Prompt:
+    rng = np.random.default_rng([seed, 1, stream])
+    audio = rng.standard_normal((audio_rows, config.text_hidden_size), dtype=np.float32)
+    ids = rng.integers(0, config.vocab_size, size=text_ids, dtype=np.int64)
+    while np.any(ids == config.token_audio_pad):
+        bad = ids == config.token_audio_pad
+        ids[bad] = rng.integers(0, config.vocab_size, size=int(bad.sum()))
+    tokens = np.concatenate([np.full(audio_rows, config.token_audio_pad, np.int64), ids]).astype(np.uint32)
+    return Prompt(tokens, audio)
+
+
+# BASELINE.json configs[0..4]
+@dataclasses.dataclass
+class Workload:
+    name: str
+    config: Config
+    fmt: int
+    seed: int
+    audio_rows: int | tuple[int, int]
+    text_ids: int
+    decode: int
+    streams: int
+
+
+def workloads() -> dict[str, Workload]:
+    return {
+        "cfg0_0p6b_q8_b1": Workload("cfg0_0p6b_q8_b1", qwen3_asr_0p6b(max_positions=512, max_decode_tokens=512),
+                                    quant.Q8, 0, 188, 8, 64, 1),
+        "cfg1_0p6b_q4_b1": Workload("cfg1_0p6b_q4_b1", qwen3_asr_0p6b(max_positions=1024, max_decode_tokens=1024),
+                                    quant.Q4, 0, 500, 12, 256, 1),
+        "cfg2_1p7b_q4_b1": Workload("cfg2_1p7b_q4_b1", qwen3_asr_1p7b(max_positions=1024, max_decode_tokens=1024),
+                                    quant.Q4, 1, 375, 16, 448, 1),
+        "cfg3_1p7b_q4_s64": Workload("cfg3_1p7b_q4_s64", qwen3_asr_1p7b(max_positions=2048, max_decode_tokens=1024),
+                                     quant.Q4, 1, (100, 1500), 16, 256, 64),
+        "cfg4_1p7b_q4_s64_long": Workload("cfg4_1p7b_q4_s64_long",
+                                          qwen3_asr_1p7b(max_positions=4096, max_decode_tokens=1024),
+                                          quant.Q4, 1, (2048, 3584), 16, 512, 64),
+    }
+
+
+def load_into(model: Model, target, cache_format: int = 1, streams: int | None = None) -> None:
+    """Loads a synthetic model through the reference-shaped model family of `target`
+    (a `runtime.CudaModel`, or anything with the same methods)."""
+    target.begin()
+    for t in model.tensors:
+        target.add_tensor(t.kind, t.layer, t.fmt, t.rows, t.cols, t.payload)
+    target.set_cache_format(cache_format)
+    if streams is not None:
+        target.set_streams(streams)
+    target.finish(model.config.pack())

@@ -1,0 +1,172 @@
+"""End-to-end parity of the persistent decode kernel against the CPU oracle,
+through the reference-shaped model and decode families of the C ABI.
+
+Bars (north star): greedy token ids identical; logits within 2e-2 max-abs and
+cosine >= 0.9999 at every step; q8 cache codes within one code of the
+oracle's (the K/V rows come out of a GEMV with a different summation order, so
+a value sitting on a rounding tie may round the other way) with scales within
+one f16 ulp, and nearly all codes exact.
+"""
+
+import numpy as np
+import pytest
+
+from qwenscriber_b200 import quant, synthetic
+from qwenscriber_b200 import runtime as rt
+
+from .parity import cosine, kv_compare, oracle_model, small_config
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_ATOL = 2e-2
+COSINE_MIN = 0.9999
+
+
+def _gpu_model(model, chunk=1, keep_logits=True):
+    m = rt.CudaModel(0)
+    synthetic.load_into(model, m, cache_format=rt.CACHE_Q8)
+    m.set_option(rt.OPTION_KEEP_LOGITS, 1 if keep_logits else 0)
+    m.set_option(rt.OPTION_STEP_CHUNK, chunk)
+    m.set_option(rt.OPTION_IGNORE_EOS, 1)
+    return m
+
+
+def _run_parity(model, prompt, steps, check_kv=True):
+    c = model.config
+    om = oracle_model(model)
+    gm = _gpu_model(model)
+    try:
+        nxt = om.prefill(prompt.tokens, prompt.audio, prompt.audio.shape[0])
+        gm.decode_begin(prompt.tokens, prompt.audio, steps + 1)
+        worst_abs, worst_cos = 0.0, 1.0
+        lo, lg = om.logits(c.vocab_size), gm.debug_logits()
+        worst_abs, worst_cos = max(worst_abs, float(np.max(np.abs(lo - lg)))), min(worst_cos, cosine(lo, lg))
+        tokens_o, tokens_g = [], []
+        for _ in range(steps):
+            tg = gm.decode_step()
+            tokens_o.append(nxt)
+            tokens_g.append(tg)
+            assert tg == nxt, f"token {len(tokens_g)}: gpu {tg} oracle {nxt}"
+            nxt = om.step(nxt)
+            lo, lg = om.logits(c.vocab_size), gm.debug_logits()
+            worst_abs = max(worst_abs, float(np.max(np.abs(lo - lg))))
+            worst_cos = min(worst_cos, cosine(lo, lg))
+        assert worst_abs <= LOGIT_ATOL, worst_abs
+        assert worst_cos >= COSINE_MIN, worst_cos
+        assert gm.decode_tokens() == tokens_g
+        if check_kv:
+            positions = om.position
+            ok, ov = om.cache_q8()
+            gk = gm.debug_cache(0, ok.size)
+            gv = gm.debug_cache(1, ov.size)
+            for gpu_b, ora_b in ((gk, ok), (gv, ov)):
+                r = kv_compare(gpu_b, ora_b, c, positions)
+                assert r["codes_max"] <= 1 and r["scale_ulps_max"] <= 1, r
+                assert r["codes_exact"] >= 0.99 and r["scales_exact"] >= 0.99, r
+        gm.decode_end()
+        return worst_abs, worst_cos
+    finally:
+        gm.close()
+        om.close()
+
+
+@pytest.mark.parametrize("fmt", [quant.Q8, quant.Q4])
+def test_small_decoder_matches_oracle(gpu, cuda_lib, oracle_lib, fmt):
+    c = small_config(fmt, layers=2)
+    model = synthetic.make_model(c, fmt, seed=7)
+    prompt = synthetic.make_prompt(c, 40, 6, seed=7)
+    _run_parity(model, prompt, steps=24)
+
+
+def test_small_decoder_1p7b_geometry(gpu, cuda_lib, oracle_lib):
+    # hidden 2048, ffn 6144: the down projection takes two K segments per row.
+    c = small_config(quant.Q4, layers=3, big=True)
+    model = synthetic.make_model(c, quant.Q4, seed=3)
+    prompt = synthetic.make_prompt(c, 150, 9, seed=3)
+    _run_parity(model, prompt, steps=16)
+
+
+def test_long_prompt_spans_many_attention_chunks(gpu, cuda_lib, oracle_lib):
+    # 600 positions: five 128-position split-K chunks per head and the last-arriver combine.
+    c = small_config(quant.Q8, layers=1, max_positions=1024)
+    model = synthetic.make_model(c, quant.Q8, seed=5)
+    prompt = synthetic.make_prompt(c, 590, 10, seed=5)
+    _run_parity(model, prompt, steps=8)
+
+
+def test_chunked_steps_match_single_steps(gpu, cuda_lib, oracle_lib):
+    # Several steps per device launch produce the same greedy chain as one per launch.
+    c = small_config(quant.Q4, layers=2)
+    model = synthetic.make_model(c, quant.Q4, seed=9)
+    prompt = synthetic.make_prompt(c, 20, 4, seed=9)
+    outs = []
+    for chunk in (1, 7, 32):
+        m = _gpu_model(model, chunk=chunk, keep_logits=False)
+        m.decode_begin(prompt.tokens, prompt.audio, 40)
+        outs.append([m.decode_step() for _ in range(40)])
+        assert m.decode_step() is None  # budget reached (model.zig:435-438)
+        m.close()
+    assert outs[0] == outs[1] == outs[2]
+
+
+def test_state_machine_and_limits(gpu, cuda_lib):
+    c = small_config(quant.Q8, layers=1, max_positions=64)
+    model = synthetic.make_model(c, quant.Q8, seed=1)
+    m = rt.CudaModel(0)
+    with pytest.raises(rt.QwcError) as e:
+        m.decode_begin([1, 2], None, 4)
+    assert e.value.name == "invalid_state"  # decode before load (model.zig:376)
+    m.begin()
+    with pytest.raises(rt.QwcError) as e:
+        m.finish(c.pack())
+    assert e.value.name == "invalid_state"  # no tensors (model.zig:208)
+    for t in model.tensors:
+        m.add_tensor(t.kind, t.layer, t.fmt, t.rows, t.cols, t.payload)
+    with pytest.raises(rt.QwcError) as e:
+        t = model.tensors[0]
+        m.add_tensor(t.kind, t.layer, t.fmt, t.rows, t.cols, t.payload)
+    assert e.value.name == "invalid_argument"  # DuplicateTensor
+    m.set_cache_format(rt.CACHE_Q8)
+    bad = c.pack()
+    with pytest.raises(rt.QwcError) as e:
+        m.finish(b"X" + bad[1:])
+    assert e.value.name == "bad_magic"
+    m.finish(bad)
+    with pytest.raises(rt.QwcError) as e:
+        m.set_cache_format(rt.CACHE_Q8)
+    assert e.value.name == "invalid_state"  # refused after load (model.zig:184-188)
+    req = m.requirements()
+    assert req["total_bytes"] == req["weight_bytes"] + req["cache_bytes"] + req["scratch_bytes"]
+    assert req["max_positions"] == 64 and req["max_audio_frames"] == 3000
+    assert m.tensor_count() == len(model.tensors)
+    with pytest.raises(rt.QwcError) as e:
+        m.decode_begin([1, 2], None, 0)
+    assert e.value.name == "limit_exceeded"  # max_tokens == 0 (model.zig:380)
+    with pytest.raises(rt.QwcError) as e:
+        m.decode_begin([c.token_audio_pad], None, 4)
+    assert e.value.name == "shape_mismatch"  # PromptMismatch (decoder.zig:323)
+    with pytest.raises(rt.QwcError) as e:
+        m.decode_begin(list(range(65)), None, 4)
+    assert e.value.name == "limit_exceeded"  # beyond max_positions
+    # A prompt that fills the cache: decoding stops with limit_exceeded (decoder.zig:142).
+    m.set_option(rt.OPTION_IGNORE_EOS, 1)
+    m.decode_begin(list(range(1, 61)), None, 32)
+    got = [m.decode_step() for _ in range(4)]
+    assert all(isinstance(t, int) for t in got)
+    with pytest.raises(rt.QwcError) as e:
+        m.decode_step()
+    assert e.value.name == "limit_exceeded"
+    m.decode_end()
+    with pytest.raises(rt.QwcError) as e:
+        m.decode_step()
+    assert e.value.name == "invalid_state"
+    m.close()
+
+
+def test_cfg0_greedy_tokens_identical(gpu, cuda_lib, oracle_lib):
+    """0.6B, q8 weights N(0, 0.02) seed 0, 188 audio rows + 8 ids, q8 cache, 64 greedy tokens."""
+    w = synthetic.workloads()["cfg0_0p6b_q8_b1"]
+    model = synthetic.make_model(w.config, w.fmt, w.seed)
+    prompt = synthetic.make_prompt(w.config, w.audio_rows, w.text_ids, w.seed)
+    worst_abs, worst_cos = _run_parity(model, prompt, steps=w.decode, check_kv=True)
+    print(f"cfg0 parity: max |dlogit| {worst_abs:.3e}, min cosine {worst_cos:.8f}")
