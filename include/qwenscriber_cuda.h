@@ -179,6 +179,15 @@ int32_t qwc_stream_end(uint32_t handle, uint32_t slot);
 int32_t qwc_decode_run_timed(uint32_t handle, uint32_t steps, float* device_ms);
 /* Last logits computed for `slot` (QWC_OPTION_KEEP_LOGITS must be set). */
 int32_t qwc_debug_logits(uint32_t handle, uint32_t slot, float* out, uint32_t count);
+/* Reads the token `slot` holds for its next qwc_decode_step into *held_out;
+ * when `force` >= 0, replaces it with `force` first (teacher forcing for
+ * parity runs). Requires one decode step per launch (QWC_OPTION_STEP_CHUNK 1)
+ * or no steps computed ahead. */
+int32_t qwc_debug_hold(uint32_t handle, uint32_t slot, int64_t force, uint32_t* held_out);
+/* Device scratch of the last launch's last forward pass, last layer:
+ * which 0 = hidden (after the final residual add), 1 = q|k|v projections
+ * (before QK-norm and RoPE), 2 = attention output, 3 = silu(gate) * up. */
+int32_t qwc_debug_scratch(uint32_t handle, uint32_t which, float* out, uint32_t count);
 /* Raw key (which = 0) or value (which = 1) cache bytes of `slot`, in the
  * reference's layer-major two-plane layout (src/core/qwen3_asr/decoder.zig:45-65). */
 int32_t qwc_debug_cache(uint32_t handle, uint32_t slot, uint32_t which, void* out, uint64_t len);

@@ -87,6 +87,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "orc_step": (c_int32, [c_void_p, c_uint32, u32p]),
         "orc_logits": (fp, [c_void_p]),
         "orc_hidden": (fp, [c_void_p]),
+        "orc_scratch": (fp, [c_void_p, c_int, POINTER(c_uint32)]),
         "orc_cache_keys_q8": (u8p, [c_void_p, POINTER(c_uint64)]),
         "orc_cache_values_q8": (u8p, [c_void_p, POINTER(c_uint64)]),
         "orc_rope_cos": (fp, [c_void_p]),
@@ -299,6 +300,11 @@ class OracleModel:
     def hidden(self, width: int) -> np.ndarray:
         p = self._L.orc_hidden(self._h)
         return np.ctypeslib.as_array(p, shape=(width,)).copy()
+
+    def scratch(self, which: int) -> np.ndarray:
+        n = c_uint32(0)
+        p = self._L.orc_scratch(self._h, which, ctypes.byref(n))
+        return np.ctypeslib.as_array(p, shape=(n.value,)).copy()
 
     def cache_q8(self) -> tuple[np.ndarray, np.ndarray]:
         n = c_uint64(0)

@@ -928,6 +928,21 @@ int32_t orc_step(OrcModel* m, uint32_t token, uint32_t* next_out) {
 const float* orc_logits(const OrcModel* m) { return m->logits.data(); }
 const float* orc_hidden(const OrcModel* m) { return m->hidden.data(); }
 
+const float* orc_scratch(const OrcModel* m, int which, uint32_t* count_out) {
+  const std::vector<float>* v = nullptr;
+  switch (which) {
+    case 0: v = &m->hidden; break;
+    case 1: v = &m->query; break;
+    case 2: v = &m->key; break;
+    case 3: v = &m->value; break;
+    case 4: v = &m->attention_out; break;
+    case 5: v = &m->gate; break;
+    default: *count_out = 0; return nullptr;
+  }
+  *count_out = static_cast<uint32_t>(v->size());
+  return v->data();
+}
+
 const uint8_t* orc_cache_keys_q8(const OrcModel* m, uint64_t* len_out) {
   *len_out = m->cache_keys_q8.size();
   return m->cache_keys_q8.data();

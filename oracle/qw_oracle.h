@@ -87,6 +87,9 @@ int32_t orc_prefill(OrcModel* model, const uint32_t* tokens, uint32_t n_tokens, 
 int32_t orc_step(OrcModel* model, uint32_t token, uint32_t* next_out);
 const float* orc_logits(const OrcModel* model);
 const float* orc_hidden(const OrcModel* model);
+/* Scratch of the last forward pass's last layer: 0 hidden, 1 query (normed,
+ * rotated), 2 key (normed, rotated), 3 value, 4 attention_out, 5 silu(gate)*up. */
+const float* orc_scratch(const OrcModel* model, int which, uint32_t* count_out);
 const uint8_t* orc_cache_keys_q8(const OrcModel* model, uint64_t* len_out);
 const uint8_t* orc_cache_values_q8(const OrcModel* model, uint64_t* len_out);
 const float* orc_rope_cos(const OrcModel* model);

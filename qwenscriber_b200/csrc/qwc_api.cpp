@@ -903,6 +903,32 @@ int32_t qwc_debug_logits(uint32_t handle, uint32_t slot, float* out, uint32_t co
   return QWC_OK;
 }
 
+int32_t qwc_debug_hold(uint32_t handle, uint32_t slot, int64_t force, uint32_t* held_out) {
+  Handle* h = lookup(handle);
+  if (!h || !held_out) return QWC_INVALID_ARGUMENT;
+  if (h->state != State::kLoaded || slot >= h->slots.size() || !h->slots[slot].decoding) return QWC_INVALID_STATE;
+  StreamSlot& s = h->slots[slot];
+  if (force >= 0) {
+    if (!s.ahead.empty()) return QWC_INVALID_STATE;
+    if (static_cast<uint64_t>(force) >= h->config.vocab_size) return QWC_INVALID_ARGUMENT;
+    s.next_token = static_cast<uint32_t>(force);
+  }
+  *held_out = s.next_token;
+  return QWC_OK;
+}
+
+int32_t qwc_debug_scratch(uint32_t handle, uint32_t which, float* out, uint32_t count) {
+  Handle* h = lookup(handle);
+  if (!h || !out || which > 3) return QWC_INVALID_ARGUMENT;
+  if (h->state != State::kLoaded) return QWC_INVALID_STATE;
+  const DevBuf* b = which == 0 ? &h->hidden_g : which == 1 ? &h->qkv : which == 2 ? &h->attn_out : &h->act;
+  if (uint64_t(count) * 4 < b->bytes) return QWC_LIMIT_EXCEEDED;
+  cudaSetDevice(h->device);
+  QWC_CUDA(cudaMemcpyAsync(out, b->ptr, b->bytes, cudaMemcpyDeviceToHost, h->stream));
+  QWC_CUDA(cudaStreamSynchronize(h->stream));
+  return static_cast<int32_t>(b->bytes / 4);
+}
+
 int32_t qwc_debug_cache(uint32_t handle, uint32_t slot, uint32_t which, void* out, uint64_t len) {
   Handle* h = lookup(handle);
   if (!h || !out || which > 1) return QWC_INVALID_ARGUMENT;

@@ -14,7 +14,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from ctypes import POINTER, c_char_p, c_float, c_int32, c_uint32, c_uint64, c_void_p
+from ctypes import POINTER, c_char_p, c_float, c_int32, c_int64, c_uint32, c_uint64, c_void_p
 
 import numpy as np
 
@@ -56,6 +56,8 @@ SIGNATURES = {
     "qwc_stream_end": (c_int32, [c_uint32, c_uint32]),
     "qwc_decode_run_timed": (c_int32, [c_uint32, c_uint32, POINTER(c_float)]),
     "qwc_debug_logits": (c_int32, [c_uint32, c_uint32, c_void_p, c_uint32]),
+    "qwc_debug_hold": (c_int32, [c_uint32, c_uint32, c_int64, POINTER(c_uint32)]),
+    "qwc_debug_scratch": (c_int32, [c_uint32, c_uint32, c_void_p, c_uint32]),
     "qwc_debug_cache": (c_int32, [c_uint32, c_uint32, c_uint32, c_void_p, c_uint64]),
     "qwc_kernel_launches": (c_uint64, [c_uint32]),
     "qwc_rope_tables": (c_int32, [c_float, c_uint32, c_uint32, c_void_p, c_void_p]),
@@ -212,6 +214,17 @@ class CudaModel:
         out = np.zeros(self.vocab, np.float32)
         check(self._L.qwc_debug_logits(self.handle, slot, out.ctypes.data, out.size), "qwc_debug_logits")
         return out
+
+    def debug_hold(self, force: int = -1, slot: int = 0) -> int:
+        """The token held for the next decode step; `force` >= 0 replaces it first."""
+        out = c_uint32(0)
+        check(self._L.qwc_debug_hold(self.handle, slot, force, ctypes.byref(out)), "qwc_debug_hold")
+        return out.value
+
+    def debug_scratch(self, which: int, count: int = 16384) -> np.ndarray:
+        out = np.zeros(count, np.float32)
+        n = check(self._L.qwc_debug_scratch(self.handle, which, out.ctypes.data, count), "qwc_debug_scratch")
+        return out[:n]
 
     def debug_cache(self, which: int, nbytes: int, slot: int = 0) -> np.ndarray:
         out = np.zeros(nbytes, np.uint8)

@@ -139,7 +139,7 @@ def test_rmsnorm_rope_silu(gpu, cuda_lib, oracle_lib):
     dx, dw = _dev(torch, x), _dev(torch, w)
     _call("qwc_op_rmsnorm", dx.data_ptr(), dw.data_ptr(), 2048, 3, 1e-6, out.data_ptr(), None)
     torch.cuda.synchronize()
-    np.testing.assert_allclose(out.cpu().numpy(), O.rmsnorm(x, w, 2048, 1e-6), atol=1e-4, rtol=1e-4)
+    np.testing.assert_allclose(out.cpu().numpy(), O.rmsnorm(x, w, 2048, 1e-6).reshape(-1), atol=1e-4, rtol=1e-4)
 
     cos, sin = rt.rope_tables(1000000.0, 128, 512)
     q = rng.standard_normal(16 * 128).astype(np.float32)
