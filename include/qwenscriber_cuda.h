@@ -106,7 +106,10 @@ enum {
    * qwc_debug_logits can return them (parity testing). */
   QWC_OPTION_KEEP_LOGITS = 2,
   /* Decode steps computed ahead per device launch (1..256, default 16). */
-  QWC_OPTION_STEP_CHUNK = 3
+  QWC_OPTION_STEP_CHUNK = 3,
+  /* Nonzero: every launch records a phase timeline of its first step
+   * (%globaltimer per CTA at each phase boundary); see qwc_debug_trace. */
+  QWC_OPTION_TRACE = 4
 };
 
 /* ---- version and lifecycle (src/wasm/exports.zig:49-120) ---- */
@@ -188,6 +191,11 @@ int32_t qwc_debug_hold(uint32_t handle, uint32_t slot, int64_t force, uint32_t* 
  * which 0 = hidden (after the final residual add), 1 = q|k|v projections
  * (before QK-norm and RoPE), 2 = attention output, 3 = silu(gate) * up. */
 int32_t qwc_debug_scratch(uint32_t handle, uint32_t which, float* out, uint32_t count);
+/* Phase timeline of the last launch (QWC_OPTION_TRACE): grid x 512 nanosecond
+ * stamps, 11 per layer (layer start, QKV input ready, QKV done, barrier,
+ * attention done, barrier, O done, barrier, gate/up done, barrier, down done
+ * + barrier) then lm_head start, done, barrier. Returns the count. */
+int32_t qwc_debug_trace(uint32_t handle, uint64_t* out, uint32_t count);
 /* Raw key (which = 0) or value (which = 1) cache bytes of `slot`, in the
  * reference's layer-major two-plane layout (src/core/qwen3_asr/decoder.zig:45-65). */
 int32_t qwc_debug_cache(uint32_t handle, uint32_t slot, uint32_t which, void* out, uint64_t len);

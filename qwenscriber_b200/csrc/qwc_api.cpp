@@ -7,10 +7,13 @@
 // the decoder's capacity rules (src/core/qwen3_asr/model.zig:62, decoder.zig:142).
 // Device work is launched on one CUDA stream per handle.
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <deque>
 #include <map>
@@ -218,6 +221,7 @@ struct Handle {
   uint32_t streams = 1;
   bool ignore_eos = false;
   bool keep_logits = false;
+  bool trace = false;
   uint32_t step_chunk = 16;
   uint64_t launches = 0;
   std::map<std::pair<uint32_t, uint32_t>, Tensor> tensors;
@@ -226,9 +230,10 @@ struct Handle {
   DevModel host_model{};
   DevBuf model_buf, rope_cos, rope_sin, k_cache, v_cache;
   DevBuf qkv, attn_out, hidden_g, act, attn_part, attn_count, amax_val, amax_idx, barrier, error, tokens_out, logits;
-  DevBuf prompt_ids, prompt_rows, audio_rows;
+  DevBuf prompt_ids, prompt_rows, audio_rows, trace_buf;
   uint32_t max_chunks = 0;
   uint64_t weight_bytes = 0;
+  KvMaps kv_maps{};
   std::vector<StreamSlot> slots;
 
   ~Handle() {
@@ -248,6 +253,7 @@ Handle* lookup(uint32_t h) {
 
 int32_t status_of(cudaError_t e) {
   if (e == cudaSuccess) return QWC_OK;
+  if (std::getenv("QWC_VERBOSE")) std::fprintf(stderr, "qwc: CUDA error: %s\n", cudaGetErrorString(e));
   cudaGetLastError();
   if (e == cudaErrorMemoryAllocation) return QWC_OUT_OF_MEMORY;
   return QWC_INVALID_STATE;
@@ -265,7 +271,7 @@ void release_model(Handle* h) {
   h->tensors.clear();
   for (DevBuf* b : {&h->model_buf, &h->rope_cos, &h->rope_sin, &h->k_cache, &h->v_cache, &h->qkv, &h->attn_out,
                     &h->hidden_g, &h->act, &h->attn_part, &h->attn_count, &h->amax_val, &h->amax_idx, &h->barrier,
-                    &h->error, &h->tokens_out, &h->logits, &h->prompt_ids, &h->prompt_rows, &h->audio_rows}) {
+                    &h->error, &h->tokens_out, &h->logits, &h->prompt_ids, &h->prompt_rows, &h->audio_rows, &h->trace_buf}) {
     b->alloc(0);
   }
   h->slots.clear();
@@ -291,17 +297,50 @@ DevMat make_mat(const Tensor& t) {
 }
 
 // The decode kernel's layout rules for one matrix: q4/q8, whole 512-byte
-// code spans per row, at most two K segments of 96 activations per lane.
+// code spans per row (a warp reads 32 x 16 bytes per step), K within the
+// activation buffer, and one row per ring slot at least.
 int32_t kernel_fits(const DevMat& m) {
   if (m.format != kFormatQ4 && m.format != kFormatQ8) return QWC_UNSUPPORTED_MODEL;
   if (m.code_row % 512 != 0 || m.scale_row % 16 != 0) return QWC_UNSUPPORTED_MODEL;
-  const uint32_t ch = m.code_row / 512;
-  const uint32_t vals = m.format == kFormatQ4 ? 32 : 16;
-  const bool ks1 = ch * vals <= 96;
-  const bool ks2 = ch % 2 == 0 && (ch / 2) * vals <= 96;
-  if (!ks1 && !ks2) return QWC_UNSUPPORTED_MODEL;
+  if (m.cols > 8192) return QWC_UNSUPPORTED_MODEL;
   if (m.scale_row + m.code_row > 28 * 1024) return QWC_UNSUPPORTED_MODEL;
   return QWC_OK;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against libcuda).
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = []() -> EncodeTiledFn {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// One q8 cache plane of stream 0 as a 3-D u8 tensor [layer][position][row
+// bytes], boxes of `box_x` bytes x kAttnChunk positions x 1 layer.
+int32_t encode_plane(uint8_t* out, uint8_t* base, uint64_t row_bytes, uint64_t positions, uint64_t layers,
+                     uint64_t layer_stride, uint32_t box_x) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn) return QWC_INVALID_STATE;
+  const cuuint64_t dims[3] = {row_bytes, positions, layers};
+  const cuuint64_t strides[2] = {row_bytes, layer_stride};
+  const cuuint32_t box[3] = {box_x, kAttnChunk, 1};
+  const cuuint32_t elem[3] = {1, 1, 1};
+  const CUresult r = fn(reinterpret_cast<CUtensorMap*>(out), CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base, dims, strides, box,
+                        elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? QWC_OK : QWC_INVALID_STATE;
 }
 
 int32_t finish_model(Handle* h, const Config& c) {
@@ -312,7 +351,10 @@ int32_t finish_model(Handle* h, const Config& c) {
   if (L > kMaxLayers || c.text_head_dim != kHeadDim || c.text_attention_heads != 2 * c.text_key_value_heads) {
     return QWC_UNSUPPORTED_MODEL;
   }
-  if (hidden % 4 != 0 || hidden > 8192 || qw > 8192 || ffn > 8192) return QWC_UNSUPPORTED_MODEL;
+  // A norm weight vector travels as one ring slot; the cache's TMA boxes need
+  // 16-byte rows of scales (four kv heads).
+  if (hidden % 4 != 0 || hidden > kHiddenMax || qw > 8192 || ffn > 8192) return QWC_UNSUPPORTED_MODEL;
+  if (c.text_key_value_heads % 4 != 0) return QWC_UNSUPPORTED_MODEL;
   const bool tied = (c.flags & 1u) != 0;
 
   auto find = [&](uint32_t kind, uint32_t layer) -> const Tensor* {
@@ -344,8 +386,6 @@ int32_t finish_model(Handle* h, const Config& c) {
   } else {
     QWC_TRY(need_mat(QWC_KIND_DECODER_OUTPUT, 0, c.vocab_size, hidden, &m.lm_head));
   }
-  // The lm_head's argmax runs per warp, so one warp must hold a whole row.
-  if ((m.lm_head.code_row / 512) * (m.lm_head.format == kFormatQ4 ? 32u : 16u) > 96) return QWC_UNSUPPORTED_MODEL;
   for (uint32_t l = 0; l < L; ++l) {
     DevLayer& D = m.layers[l];
     const uint32_t layer = l + 1;  // decoder_layer_base (layout.zig:26)
@@ -371,6 +411,10 @@ int32_t finish_model(Handle* h, const Config& c) {
   // Rows of a non-LM stage held by one CTA must fit the kernel's row buffers.
   const uint32_t widest = std::max({qw + 2 * kvw, ffn, hidden});
   if ((widest + h->grid - 1) / h->grid > 256) return QWC_UNSUPPORTED_MODEL;
+  // Every CTA streams at least one tile of each stage, which keeps a layer's
+  // attention tiles (TMA reads of cache rows earlier tokens wrote) more than
+  // a ring's depth of tiles behind those writes.
+  if (std::min(hidden, ffn) < static_cast<uint32_t>(h->grid)) return QWC_UNSUPPORTED_MODEL;
 
   m.n_layers = L;
   m.hidden = hidden;
@@ -403,6 +447,19 @@ int32_t finish_model(Handle* h, const Config& c) {
   QWC_TRY(h->v_cache.alloc(m.cache_stream_stride * h->streams));
   QWC_CUDA(cudaMemset(h->k_cache.ptr, 0, h->k_cache.bytes));
   QWC_CUDA(cudaMemset(h->v_cache.ptr, 0, h->v_cache.bytes));
+  {
+    static_assert(sizeof(CUtensorMap) == 128, "KvMaps holds 128-byte tensor maps");
+    const uint64_t kv_row = kvw, scale_row = uint64_t(kvw / kGroup) * 2;
+    uint8_t* kc = h->k_cache.as<uint8_t>();
+    uint8_t* vc = h->v_cache.as<uint8_t>();
+    KvMaps& km = h->kv_maps;
+    QWC_TRY(encode_plane(km.k_codes, kc + m.cache_scales_bytes, kv_row, c.max_positions, L, m.cache_layer_stride,
+                         kHeadDim));
+    QWC_TRY(encode_plane(km.v_codes, vc + m.cache_scales_bytes, kv_row, c.max_positions, L, m.cache_layer_stride,
+                         kHeadDim));
+    QWC_TRY(encode_plane(km.k_scales, kc, scale_row, c.max_positions, L, m.cache_layer_stride, 16));
+    QWC_TRY(encode_plane(km.v_scales, vc, scale_row, c.max_positions, L, m.cache_layer_stride, 16));
+  }
 
   h->max_chunks = (c.max_positions + kAttnChunk - 1) / kAttnChunk;
   QWC_TRY(h->qkv.alloc(size_t(qw + 2 * kvw) * 4));
@@ -460,11 +517,20 @@ int32_t run_decode(Handle* h, uint32_t n_tokens, uint32_t first_position, uint32
   L.barrier = h->barrier.as<uint32_t>();
   L.error = h->error.as<int32_t>();
   L.timeout_ns = 4000000000ull;
+  if (h->trace) {
+    if (h->trace_buf.bytes == 0) QWC_TRY(h->trace_buf.alloc(size_t(h->grid) * kTraceEvents * 8));
+    QWC_CUDA(cudaMemsetAsync(h->trace_buf.ptr, 0, h->trace_buf.bytes, h->stream));
+    L.trace = h->trace_buf.as<uint64_t>();
+    L.trace_token = 0;
+  }
   L.max_chunks = h->max_chunks;
   (void)m;
   QWC_CUDA(cudaMemsetAsync(h->barrier.ptr, 0, 4, h->stream));
-  const int e = launch_decode(L, h->grid, h->stream);
-  if (e != 0) return status_of(static_cast<cudaError_t>(e));
+  const int e = launch_decode(L, h->kv_maps, h->grid, h->stream);
+  if (e != 0) {
+    if (std::getenv("QWC_VERBOSE")) std::fprintf(stderr, "qwc: decode launch failed: %s\n", cudaGetErrorString(static_cast<cudaError_t>(e)));
+    return status_of(static_cast<cudaError_t>(e));
+  }
   h->launches += 1;
   int32_t device_error = 0;
   QWC_CUDA(cudaMemcpyAsync(&device_error, h->error.ptr, 4, cudaMemcpyDeviceToHost, h->stream));
@@ -475,6 +541,7 @@ int32_t run_decode(Handle* h, uint32_t n_tokens, uint32_t first_position, uint32
   }
   QWC_CUDA(cudaStreamSynchronize(h->stream));
   if (device_error != 0) {
+    if (std::getenv("QWC_VERBOSE")) std::fprintf(stderr, "qwc: decode kernel gave up waiting (code %d)\n", device_error);
     cudaMemsetAsync(h->error.ptr, 0, 4, h->stream);
     cudaStreamSynchronize(h->stream);
     return QWC_INVALID_STATE;
@@ -647,6 +714,7 @@ int32_t qwc_set_option(uint32_t handle, uint32_t option, uint32_t value) {
   switch (option) {
     case QWC_OPTION_IGNORE_EOS: h->ignore_eos = value != 0; return QWC_OK;
     case QWC_OPTION_KEEP_LOGITS: h->keep_logits = value != 0; return QWC_OK;
+    case QWC_OPTION_TRACE: h->trace = value != 0; return QWC_OK;
     case QWC_OPTION_STEP_CHUNK:
       if (value == 0 || value > 256) return QWC_INVALID_ARGUMENT;
       h->step_chunk = value;
@@ -927,6 +995,18 @@ int32_t qwc_debug_scratch(uint32_t handle, uint32_t which, float* out, uint32_t 
   QWC_CUDA(cudaMemcpyAsync(out, b->ptr, b->bytes, cudaMemcpyDeviceToHost, h->stream));
   QWC_CUDA(cudaStreamSynchronize(h->stream));
   return static_cast<int32_t>(b->bytes / 4);
+}
+
+int32_t qwc_debug_trace(uint32_t handle, uint64_t* out, uint32_t count) {
+  Handle* h = lookup(handle);
+  if (!h || !out) return QWC_INVALID_ARGUMENT;
+  if (h->trace_buf.bytes == 0) return QWC_INVALID_STATE;
+  const uint64_t n = h->trace_buf.bytes / 8;
+  if (count < n) return QWC_LIMIT_EXCEEDED;
+  cudaSetDevice(h->device);
+  QWC_CUDA(cudaMemcpyAsync(out, h->trace_buf.ptr, h->trace_buf.bytes, cudaMemcpyDeviceToHost, h->stream));
+  QWC_CUDA(cudaStreamSynchronize(h->stream));
+  return static_cast<int32_t>(n);
 }
 
 int32_t qwc_debug_cache(uint32_t handle, uint32_t slot, uint32_t which, void* out, uint64_t len) {

@@ -5,16 +5,17 @@
 // by the argmax (decoder.zig:290-301). One CTA per SM, co-resident
 // (cooperative launch):
 //
-//   * warp 8 (producer) streams this CTA's fixed share of every weight matrix
+//   * the producer warp streams this CTA's fixed share of every weight matrix
 //     -- whole rows, in the reference's two-plane q4/q8 layout -- from HBM into
 //     a ring of shared-memory slots with cp.async.bulk, tracked by mbarriers.
 //     Weights never depend on activations, so it runs ahead across phase
-//     boundaries, layers and tokens and keeps HBM busy while the consumers
-//     wait at barriers.
-//   * warps 0-7 (consumers) dequantize in registers and reduce with warp
-//     shuffles (the dot products of kernels.zig:118-158), then run the fused
-//     epilogues: QK-RMSNorm + RoPE + q8 KV append inside the attention phase,
-//     residual adds, SwiGLU, and the argmax.
+//     boundaries, layers and tokens while the consumers wait at barriers.
+//   * eight consumer warps dequantize in registers and reduce with warp
+//     shuffles (the dot products of kernels.zig:118-158); the activation
+//     vector sits in shared memory, read once per 16-byte code chunk and
+//     shared by the four rows a warp works on at a time. Fused epilogues:
+//     QK-RMSNorm + RoPE + q8 KV append inside the attention phase, residual
+//     adds, SwiGLU, and the argmax.
 //
 // Phases per layer, separated by grid barriers: QKV -> attention (split-K
 // flash decode over the q8 cache, last-arriver combine) -> O + residual ->
@@ -25,6 +26,8 @@
 
 #include <cuda_runtime.h>
 
+#include <cstddef>
+
 #include "qwc_device.cuh"
 #include "qwc_internal.h"
 
@@ -34,11 +37,28 @@ namespace {
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kThreads = kConsumerThreads + 32;
+constexpr int kRowsPerPass = 4;                // rows one warp works on at a time
 constexpr int kSlots = 6;
 constexpr uint32_t kSlotBytes = 28 * 1024;
-constexpr uint32_t kXMax = 8192;        // floats in the activation buffer (max K)
-constexpr uint32_t kRowsMax = 256;      // rows of one stage per CTA (non-LM stages)
-constexpr uint32_t kResidMax = 256;     // hidden rows owned by one CTA
+constexpr uint32_t kXMax = 8192;               // floats in the activation buffer (max K)
+constexpr uint32_t kRowsMax = 256;             // rows of one stage per CTA (non-LM stages)
+constexpr uint32_t kResidMax = 256;            // hidden rows owned by one CTA
+static_assert(kConsumerThreads == 2 * kHeadDim, "attention maps (query head, dimension) onto the consumer threads");
+static_assert(kConsumerWarps == 8, "attention splits a chunk into eight warps of positions");
+
+// Attention tile: one ring slot per (kv head, position chunk) unit.
+constexpr uint32_t kTileKCodes = 0;                                     // [kAttnChunk][kHeadDim] key codes
+constexpr uint32_t kTileVCodes = kTileKCodes + kAttnChunk * kHeadDim;   // [kAttnChunk][kHeadDim] value codes
+constexpr uint32_t kTileKScales = kTileVCodes + kAttnChunk * kHeadDim;  // [kAttnChunk][16 B]: scales of 4 kv heads
+constexpr uint32_t kTileVScales = kTileKScales + kAttnChunk * 16;
+constexpr uint32_t kTileQNorm = kTileVScales + kAttnChunk * 16;         // [kHeadDim] f32
+constexpr uint32_t kTileKNorm = kTileQNorm + kHeadDim * 4;
+constexpr uint32_t kTileCos = kTileKNorm + kHeadDim * 4;                // [kHeadDim / 2] f32 for this position
+constexpr uint32_t kTileSin = kTileCos + kHeadDim * 2;
+constexpr uint32_t kAttnTileBytes = kTileSin + kHeadDim * 2;
+static_assert(kTileVCodes % 128 == 0 && kTileKScales % 128 == 0 && kTileVScales % 128 == 0 && kTileQNorm % 16 == 0 &&
+                  kTileCos % 16 == 0 && kTileSin % 16 == 0,
+              "TMA boxes land on 128-byte boundaries, bulk copies on 16-byte boundaries");
 
 enum Stage : int { kStQKV = 0, kStO = 1, kStGate = 2, kStUp = 3, kStDown = 4, kStLM = 5 };
 
@@ -48,8 +68,8 @@ struct Smem {
   uint8_t ring[kSlots][kSlotBytes];
   uint64_t full[kSlots];
   uint64_t empty[kSlots];
-  float x[kXMax];                 // activation vector, swizzled (x_index)
-  float part[2][kRowsMax];        // per-row partial dot products (K segments)
+  float x[kXMax];                 // activation vector, swizzled (x_index), q4-prescaled when asked
+  float part[kRowsMax];           // per-row dot products of the current stage
   float gate[kRowsMax];           // gate outputs waiting for the up rows
   float resid[kResidMax];         // this CTA's rows of the residual stream
   float red[kConsumerWarps * 2];  // block reductions
@@ -59,14 +79,26 @@ struct Smem {
 };
 
 // Attention scratch overlays the activation buffer (never live together).
+// Members read or written with 128-bit accesses are 16-byte aligned.
 struct AttnSmem {
-  float q[2][kHeadDim];
-  float tmp[2][kHeadDim];
-  float prob[2][kAttnChunk];
-  float vpart[kConsumerWarps][2][kHeadDim];
-  float kv_new[2][kHeadDim];
+  alignas(16) float q[2][4][36];  // rotated query heads, 32-dimension quarters padded against bank conflicts
+  alignas(16) float tmp[2][kHeadDim];
+  alignas(16) float ktmp[kHeadDim];
+  alignas(16) float prob[2][kAttnChunk];
+  alignas(16) float lsum[2][8];
+  alignas(16) float mx[2];
+  alignas(16) float vpart[8][2][kHeadDim];
+  alignas(16) uint32_t new_codes[2][kHeadDim / 4];  // the appended key (0) / value (1) row, packed q8 codes
+  alignas(16) uint32_t new_scales[2][2];            // f16 scale bits of its two groups
 };
+static_assert(offsetof(AttnSmem, q) % 16 == 0 && offsetof(AttnSmem, vpart) % 16 == 0 &&
+                  offsetof(AttnSmem, new_codes) % 16 == 0 && (sizeof(float) * 36) % 16 == 0,
+              "vector accesses in the attention scratch need 16-byte alignment");
+static_assert(offsetof(Smem, x) % 16 == 0 && offsetof(Smem, ring) % 128 == 0 && kSlotBytes % 128 == 0,
+              "activation buffer and TMA destinations alignment");
 static_assert(sizeof(AttnSmem) <= sizeof(float) * kXMax, "attention scratch must fit the activation buffer");
+static_assert(kAttnTileBytes <= kSlotBytes, "an attention tile fills one ring slot");
+static_assert(kHiddenMax * 4 <= kSlotBytes, "a norm weight vector fills one ring slot");
 
 // Float4-granular XOR swizzle so a lane's 32 (or 16) consecutive activations
 // load conflict-free with 128-bit shared loads.
@@ -83,12 +115,17 @@ __device__ __forceinline__ Span split_rows(uint32_t rows, uint32_t c, uint32_t n
   return {static_cast<uint32_t>((uint64_t(rows) * c) / n), static_cast<uint32_t>((uint64_t(rows) * (c + 1)) / n)};
 }
 
+// One matrix's rows within a CTA's share of a stage. The plane pointers and
+// row pitches are copied out of the model description so the streaming loops
+// keep them in registers.
 struct Piece {
-  const DevMat* mat;
-  uint32_t row0;     // first matrix row
-  uint32_t rows;     // rows in this piece
-  uint32_t local0;   // index of row0 within the CTA's share of the stage
-  uint32_t out0;     // index of row0 in the stage's output vector
+  const uint8_t* scales;  // first row's scales
+  const uint8_t* codes;   // first row's codes
+  uint32_t scale_row;     // bytes of scales per row
+  uint32_t code_row;      // bytes of codes per row
+  uint32_t rows;          // rows in this piece
+  uint32_t local0;        // index of the first row within the CTA's share of the stage
+  uint32_t out0;          // index of the first row in the stage's output vector
 };
 
 // The CTA's share of a stage: identical for the producer and the consumers.
@@ -96,7 +133,10 @@ __device__ int stage_pieces(const DevModel& m, uint32_t layer, int stage, uint32
   const DevLayer& L = m.layers[layer];
   int count = 0;
   auto add = [&](const DevMat* mat, uint32_t r0, uint32_t r1, uint32_t local0, uint32_t out0) {
-    if (r1 > r0) out[count++] = Piece{mat, r0, r1 - r0, local0, out0};
+    if (r1 > r0) {
+      const uint32_t sr = mat->scale_row, cr = mat->code_row;
+      out[count++] = Piece{mat->scales + size_t(r0) * sr, mat->codes + size_t(r0) * cr, sr, cr, r1 - r0, local0, out0};
+    }
   };
   switch (stage) {
     case kStQKV: {
@@ -139,7 +179,17 @@ __device__ int stage_pieces(const DevModel& m, uint32_t layer, int stage, uint32
   return count;
 }
 
-__device__ __forceinline__ uint32_t rows_per_tile(const DevMat& mat) { return kSlotBytes / (mat.scale_row + mat.code_row); }
+__device__ __forceinline__ uint32_t rows_per_tile(const Piece& p) { return kSlotBytes / (p.scale_row + p.code_row); }
+
+__device__ __forceinline__ uint32_t stage_format(const DevModel& m, uint32_t layer, int stage) {
+  const DevLayer& L = m.layers[layer];
+  return stage == kStLM ? m.lm_head.format
+       : stage == kStQKV ? L.q.format
+       : stage == kStO ? L.o.format
+       : stage == kStGate ? L.gate.format
+       : stage == kStUp ? L.up.format
+                        : L.down.format;
+}
 
 // ---------------------------------------------------------------------------
 // Producer
@@ -152,28 +202,77 @@ struct Producer {
   uint64_t timeout_ns;
   bool ok = true;
 
-  __device__ void issue(const DevMat& mat, uint32_t r0, uint32_t nr) {
+  // Waits for the next free slot, arms its full barrier for `bytes` and
+  // returns it (nullptr after an error).
+  __device__ uint8_t* begin_tile(uint32_t bytes, uint64_t** bar) {
     const uint32_t slot = it % kSlots;
     const uint32_t parity = ((it / kSlots) & 1u) ^ 1u;
     if (!mbar_wait_bounded(&s->empty[slot], parity, error, global_timer_ns() + timeout_ns, kErrEmpty)) {
       ok = false;
-      return;
+      return nullptr;
     }
-    const uint32_t bytes_s = nr * mat.scale_row;
-    const uint32_t bytes_c = nr * mat.code_row;
-    mbar_arrive_expect_tx(&s->full[slot], bytes_s + bytes_c);
-    bulk_g2s(s->ring[slot], mat.scales + size_t(r0) * mat.scale_row, bytes_s, &s->full[slot]);
-    bulk_g2s(s->ring[slot] + bytes_s, mat.codes + size_t(r0) * mat.code_row, bytes_c, &s->full[slot]);
+    mbar_arrive_expect_tx(&s->full[slot], bytes);
+    *bar = &s->full[slot];
     ++it;
+    return s->ring[slot];
+  }
+
+  // `nr` whole rows of one matrix: their scales, then their codes.
+  __device__ void issue(const Piece& pc, uint32_t r0, uint32_t nr) {
+    const uint32_t bytes_s = nr * pc.scale_row;
+    const uint32_t bytes_c = nr * pc.code_row;
+    uint64_t* bar;
+    uint8_t* dst = begin_tile(bytes_s + bytes_c, &bar);
+    if (!dst) return;
+    bulk_g2s(dst, pc.scales + size_t(r0) * pc.scale_row, bytes_s, bar);
+    bulk_g2s(dst + bytes_s, pc.codes + size_t(r0) * pc.code_row, bytes_c, bar);
+  }
+
+  // A norm weight vector of n floats.
+  __device__ void vector_tile(const float* v, uint32_t n) {
+    uint64_t* bar;
+    uint8_t* dst = begin_tile(n * 4, &bar);
+    if (!dst) return;
+    bulk_g2s(dst, v, n * 4, bar);
+  }
+
+  // This CTA's attention units at `position` (the same walk as attention_stage).
+  __device__ void attention_tiles(const DevModel& m, const KvMaps& maps, uint32_t layer, uint32_t position) {
+    const uint32_t chunks = position / kAttnChunk + 1;
+    const uint32_t units = m.kv_heads * chunks;
+    const DevLayer& L = m.layers[layer];
+    const float* cos_row = m.rope_cos + size_t(position) * (kHeadDim / 2);
+    const float* sin_row = m.rope_sin + size_t(position) * (kHeadDim / 2);
+    for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      const uint32_t h = u / chunks;
+      const uint32_t ch = u % chunks;
+      uint64_t* bar;
+      uint8_t* dst = begin_tile(kAttnTileBytes, &bar);
+      if (!dst) return;
+      // The cache rows were written with ordinary stores by earlier tokens;
+      // order them before this async-proxy read.
+      fence_proxy_async_global();
+      const int32_t y = static_cast<int32_t>(ch * kAttnChunk);
+      const int32_t z = static_cast<int32_t>(layer);
+      const int32_t xs = static_cast<int32_t>((h * 4u) & ~15u);  // 16-byte box holding kv head h's two f16 scales
+      tma_load_3d(dst + kTileKCodes, maps.k_codes, static_cast<int32_t>(h * kHeadDim), y, z, bar);
+      tma_load_3d(dst + kTileVCodes, maps.v_codes, static_cast<int32_t>(h * kHeadDim), y, z, bar);
+      tma_load_3d(dst + kTileKScales, maps.k_scales, xs, y, z, bar);
+      tma_load_3d(dst + kTileVScales, maps.v_scales, xs, y, z, bar);
+      bulk_g2s(dst + kTileQNorm, L.q_norm, kHeadDim * 4, bar);
+      bulk_g2s(dst + kTileKNorm, L.k_norm, kHeadDim * 4, bar);
+      bulk_g2s(dst + kTileCos, cos_row, kHeadDim * 2, bar);
+      bulk_g2s(dst + kTileSin, sin_row, kHeadDim * 2, bar);
+    }
   }
 
   __device__ void stage(const DevModel& m, uint32_t layer, int st) {
     Piece pieces[3];
     const int np = stage_pieces(m, layer, st, blockIdx.x, gridDim.x, pieces);
     for (int p = 0; p < np && ok; ++p) {
-      const uint32_t per = rows_per_tile(*pieces[p].mat);
+      const uint32_t per = rows_per_tile(pieces[p]);
       for (uint32_t r = 0; r < pieces[p].rows && ok; r += per) {
-        issue(*pieces[p].mat, pieces[p].row0 + r, min(per, pieces[p].rows - r));
+        issue(pieces[p], r, min(per, pieces[p].rows - r));
       }
     }
   }
@@ -193,15 +292,28 @@ struct Producer {
   }
 };
 
-__device__ void run_producer(const DecodeLaunch& P, Smem* s) {
+// The producer's stream, in the consumers' order: per layer the attention
+// norm, QKV rows, attention tiles, O rows, the FFN norm, gate, up and down
+// rows; then, for tokens with logits, the final norm and the lm_head rows.
+__device__ void run_producer(const DecodeLaunch& P, const KvMaps& maps, Smem* s) {
   if ((threadIdx.x & 31) != 0) return;
   const DevModel& m = *P.model;
   Producer pr{s, 0, P.error, P.timeout_ns, true};
   for (uint32_t t = 0; t < P.n_tokens && pr.ok; ++t) {
+    const uint32_t position = P.first_position + t;
     for (uint32_t l = 0; l < m.n_layers && pr.ok; ++l) {
-      for (int st = kStQKV; st <= kStDown && pr.ok; ++st) pr.stage(m, l, st);
+      const DevLayer& L = m.layers[l];
+      pr.vector_tile(L.attn_norm, m.hidden);
+      if (pr.ok) pr.stage(m, l, kStQKV);
+      if (pr.ok) pr.attention_tiles(m, maps, l, position);
+      if (pr.ok) pr.stage(m, l, kStO);
+      if (pr.ok) pr.vector_tile(L.ffn_norm, m.hidden);
+      for (int st = kStGate; st <= kStDown && pr.ok; ++st) pr.stage(m, l, st);
     }
-    if (t >= P.logits_from && pr.ok) pr.stage(m, 0, kStLM);
+    if (t >= P.logits_from && pr.ok) {
+      pr.vector_tile(m.final_norm, m.hidden);
+      if (pr.ok) pr.stage(m, 0, kStLM);
+    }
   }
   if (!pr.ok) pr.drain();
 }
@@ -216,12 +328,39 @@ struct Ctx {
   Smem* s;
   uint32_t it;        // tile counter, in step with the producer
   uint32_t barriers;  // grid barriers passed
-  uint64_t deadline;
   bool ok;
   int warp, lane, tid;
+  bool tracing;           // this token's phase timeline is being recorded
+  uint64_t full_wait_ns;  // thread 0: time spent waiting for streamed tiles
+  uint64_t bar_wait_ns;   // thread 0: time between barrier arrival and release
 };
 
 __device__ bool error_set(const int32_t* e) { return *reinterpret_cast<const volatile int32_t*>(e) != 0; }
+
+// Phase timeline (DecodeLaunch::trace): event e of the traced token.
+__device__ __forceinline__ void trace_mark(const Ctx& c, uint32_t e) {
+  if (c.tracing && c.tid == 0 && e < kTraceEvents) c.P->trace[blockIdx.x * kTraceEvents + e] = global_timer_ns();
+}
+
+// Waits (bounded) for the next streamed tile and returns its slot. Every
+// consumer warp acquires and releases every tile, in stream order.
+__device__ const uint8_t* acquire_tile(Ctx& c) {
+  const uint32_t slot = c.it % kSlots;
+  const uint32_t parity = (c.it / kSlots) & 1u;
+  const uint64_t w0 = (c.tracing && c.tid == 0) ? global_timer_ns() : 0;
+  if (c.ok && !mbar_wait_bounded(&c.s->full[slot], parity, c.P->error, global_timer_ns() + c.P->timeout_ns, kErrFull)) {
+    c.ok = false;
+  }
+  if (c.tracing && c.tid == 0) c.full_wait_ns += global_timer_ns() - w0;
+  return c.s->ring[slot];
+}
+
+// Hands the current slot back to the producer once this warp is done with it.
+__device__ void release_tile(Ctx& c) {
+  __syncwarp();
+  if (c.lane == 0) mbar_arrive(&c.s->empty[c.it % kSlots]);
+  ++c.it;
+}
 
 // Grid-wide barrier among the consumer warps of every CTA. The counter is
 // monotonic within a launch (zeroed by the host before it).
@@ -230,7 +369,9 @@ __device__ void grid_barrier(Ctx& c) {
   if (c.tid == 0) {
     c.barriers += 1;
     const uint32_t target = c.barriers * gridDim.x;
-    __threadfence();
+    const uint64_t arrive = c.tracing ? global_timer_ns() : 0;
+    // The release is cumulative: it publishes every write the CTA's threads
+    // made before the bar.sync above.
     red_release_add(c.P->barrier, 1);
     const uint64_t deadline = global_timer_ns() + c.P->timeout_ns;
     uint32_t spins = 0;
@@ -244,6 +385,7 @@ __device__ void grid_barrier(Ctx& c) {
       }
     }
     c.s->flag = error_set(c.P->error) ? 1u : 0u;
+    if (c.tracing) c.bar_wait_ns += global_timer_ns() - arrive;
   }
   consumer_sync(kConsumerThreads);
   if (c.s->flag) c.ok = false;
@@ -261,58 +403,92 @@ __device__ float block_sum(Ctx& c, float v) {
   return total;
 }
 
-// x <- rmsnorm(raw) * weight over `width` values already stored raw in x
-// (math.zig:120-130: value * inverse_rms * weight).
-__device__ void normalize_x(Ctx& c, uint32_t width, const float* weight) {
+// Multiplies x[k] by 16^-(nibble position) for q4 stages (see qwc_device.cuh).
+__device__ __forceinline__ float prescale(float v, uint32_t k, bool q4) { return q4 ? v * q4_xscale(k & 7u) : v; }
+
+constexpr int kMaxPerThread = (kHiddenMax + kConsumerThreads - 1) / kConsumerThreads;
+
+// x <- rmsnorm(raw) * weight (math.zig:120-130: value * inverse_rms * weight),
+// stored prescaled for q4 stages. `raw` holds this thread's values
+// (k = tid + i * kConsumerThreads); the weight vector is the next streamed tile.
+__device__ void normalize_into_x(Ctx& c, const float (&raw)[kMaxPerThread], uint32_t width, bool q4) {
   float ss = 0.0f;
-  for (uint32_t k = c.tid; k < width; k += kConsumerThreads) {
-    const float v = c.s->x[x_index(k)];
-    ss = fmaf(v, v, ss);
+#pragma unroll
+  for (int i = 0; i < kMaxPerThread; ++i) {
+    const uint32_t k = c.tid + i * kConsumerThreads;
+    if (k < width) ss = fmaf(raw[i], raw[i], ss);
   }
   const float total = block_sum(c, ss);
   const float inv = 1.0f / sqrtf(total / static_cast<float>(width) + c.m->eps);
-  for (uint32_t k = c.tid; k < width; k += kConsumerThreads) {
-    const uint32_t i = x_index(k);
-    c.s->x[i] = c.s->x[i] * inv * __ldg(weight + k);
+  const float* weight = reinterpret_cast<const float*>(acquire_tile(c));
+#pragma unroll
+  for (int i = 0; i < kMaxPerThread; ++i) {
+    const uint32_t k = c.tid + i * kConsumerThreads;
+    if (k < width) c.s->x[x_index(k)] = prescale(raw[i] * inv * weight[k], k, q4);
   }
+  release_tile(c);
   consumer_sync(kConsumerThreads);
 }
 
-// Copies a global vector other CTAs wrote into x (L2-coherent loads).
-__device__ void load_x_global(Ctx& c, const float* src, uint32_t width) {
+// x <- rmsnorm(hidden) * weight for a hidden vector other CTAs wrote (L2 loads).
+__device__ void norm_global_into_x(Ctx& c, const float* src, uint32_t width, bool q4) {
+  float raw[kMaxPerThread];
+#pragma unroll
+  for (int i = 0; i < kMaxPerThread; ++i) {
+    const uint32_t k = c.tid + i * kConsumerThreads;
+    raw[i] = k < width ? ld_cg(src + k) : 0.0f;
+  }
+  normalize_into_x(c, raw, width, q4);
+}
+
+// Copies a vector other CTAs wrote into x (L2-coherent loads), prescaled for q4.
+__device__ void load_x_global(Ctx& c, const float* src, uint32_t width, bool q4) {
   for (uint32_t k4 = c.tid; k4 < width / 4; k4 += kConsumerThreads) {
-    const float4 v = ld_cg4(reinterpret_cast<const float4*>(src) + k4);
-    *reinterpret_cast<float4*>(&c.s->x[x_index(k4 * 4)]) = v;
+    float4 v = ld_cg4(reinterpret_cast<const float4*>(src) + k4);
+    const uint32_t k = k4 * 4;
+    v.x = prescale(v.x, k, q4);
+    v.y = prescale(v.y, k + 1, q4);
+    v.z = prescale(v.z, k + 2, q4);
+    v.w = prescale(v.w, k + 3, q4);
+    *reinterpret_cast<float4*>(&c.s->x[x_index(k)]) = v;
   }
   consumer_sync(kConsumerThreads);
 }
 
 // Layer-0 input: the token's embedding row (decoder.zig:346-376, quant.zig:348-364)
-// or an audio row, written raw into x.
-__device__ void load_x_input(Ctx& c, uint32_t token, int32_t audio_row) {
+// or an audio row; this CTA's residual rows keep the raw values, x the normed.
+__device__ void input_into_x(Ctx& c, uint32_t token, int32_t audio_row, Span own, bool q4) {
   const DevModel& m = *c.m;
   const uint32_t hidden = m.hidden;
-  if (audio_row >= 0) {
-    const float* src = c.P->audio + size_t(audio_row) * hidden;
-    for (uint32_t k = c.tid; k < hidden; k += kConsumerThreads) c.s->x[x_index(k)] = __ldg(src + k);
-  } else {
-    const DevMat& e = m.embed;
-    const uint8_t* srow = e.scales + size_t(token) * e.scale_row;
-    const uint8_t* crow = e.codes + size_t(token) * e.code_row;
-    for (uint32_t k = c.tid; k < hidden; k += kConsumerThreads) {
-      const uint32_t g = k / kGroup;
-      const float scale = f16_bits_to_f32(__ldg(reinterpret_cast<const uint16_t*>(srow) + g));
-      int code;
-      if (e.format == kFormatQ4) {
-        const uint8_t b = __ldg(crow + k / 2);
-        code = static_cast<int>((k & 1u) ? (b >> 4) : (b & 0x0F)) - 8;
+  float raw[kMaxPerThread];
+  const DevMat& e = m.embed;
+  const uint32_t e_format = e.format;
+  const uint8_t* srow = e.scales + size_t(token) * e.scale_row;
+  const uint8_t* crow = e.codes + size_t(token) * e.code_row;
+  const float* arow = c.P->audio + size_t(audio_row < 0 ? 0 : audio_row) * hidden;
+#pragma unroll
+  for (int i = 0; i < kMaxPerThread; ++i) {
+    const uint32_t k = c.tid + i * kConsumerThreads;
+    float v = 0.0f;
+    if (k < hidden) {
+      if (audio_row >= 0) {
+        v = __ldg(arow + k);
       } else {
-        code = static_cast<int>(__ldg(crow + k)) - 128;
+        const float scale = f16_bits_to_f32_fast(__ldg(reinterpret_cast<const uint16_t*>(srow) + k / kGroup));
+        int code;
+        if (e_format == kFormatQ4) {
+          const uint8_t b = __ldg(crow + k / 2);
+          code = static_cast<int>((k & 1u) ? (b >> 4) : (b & 0x0F)) - 8;
+        } else {
+          code = static_cast<int>(__ldg(crow + k)) - 128;
+        }
+        v = static_cast<float>(code) * scale;
       }
-      c.s->x[x_index(k)] = static_cast<float>(code) * scale;
+      if (k >= own.begin && k < own.end) c.s->resid[k - own.begin] = v;
     }
+    raw[i] = v;
   }
-  consumer_sync(kConsumerThreads);
+  normalize_into_x(c, raw, hidden, q4);
 }
 
 // ---- GEMV over the streamed tiles ----
@@ -321,352 +497,327 @@ template <uint32_t FMT>
 struct Fmt;
 template <>
 struct Fmt<kFormatQ4> {
-  static constexpr int kVals = 32;     // weights per 16-byte chunk
-  static constexpr int kPairs = 16;
+  static constexpr int kPairs = 16;    // packed activation pairs per 16-byte chunk
   static constexpr uint32_t kDB = 32;  // code bytes per group
   static constexpr uint32_t kKPerByte = 2;
 };
 template <>
 struct Fmt<kFormatQ8> {
-  static constexpr int kVals = 16;
   static constexpr int kPairs = 8;
   static constexpr uint32_t kDB = 64;
   static constexpr uint32_t kKPerByte = 1;
 };
-
-// Loads this lane's activations for chunks [seg * CHS, seg * CHS + CHS) as
-// packed pairs (q4: pre-scaled per nibble position).
-template <uint32_t FMT, int CHS>
-__device__ __forceinline__ void load_x_regs(const Smem* s, int lane, int seg, uint64_t (&x2)[CHS * Fmt<FMT>::kPairs]) {
-#pragma unroll
-  for (int jj = 0; jj < CHS; ++jj) {
-    const uint32_t j = static_cast<uint32_t>(seg * CHS + jj);
-    const uint32_t kbase = (16u * lane + 512u * j) * Fmt<FMT>::kKPerByte;
-#pragma unroll
-    for (int q = 0; q < Fmt<FMT>::kVals / 4; ++q) {
-      const float4 v = *reinterpret_cast<const float4*>(&s->x[x_index(kbase + 4 * q)]);
-      if constexpr (FMT == kFormatQ4) {
-        const int i0 = (4 * q) % 8;
-        x2[jj * 16 + 2 * q + 0] = pack2(v.x * q4_xscale(i0 + 0), v.y * q4_xscale(i0 + 1));
-        x2[jj * 16 + 2 * q + 1] = pack2(v.z * q4_xscale(i0 + 2), v.w * q4_xscale(i0 + 3));
-      } else {
-        x2[jj * 8 + 2 * q + 0] = pack2(v.x, v.y);
-        x2[jj * 8 + 2 * q + 1] = pack2(v.z, v.w);
-      }
-    }
-  }
-}
-
-// Dot product of one row of a tile (this lane's chunks) before the warp sum.
-template <uint32_t FMT, int CHS>
-__device__ __forceinline__ float row_partial(const uint8_t* srow, const uint8_t* crow, int lane, int seg,
-                                             const uint64_t (&x2)[CHS * Fmt<FMT>::kPairs]) {
-  float acc = 0.0f;
-#pragma unroll
-  for (int jj = 0; jj < CHS; ++jj) {
-    const uint32_t off = 16u * lane + 512u * static_cast<uint32_t>(seg * CHS + jj);
-    const uint4 w = *reinterpret_cast<const uint4*>(crow + off);
-    const float scale = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(srow + (off / Fmt<FMT>::kDB) * 2));
-    float d;
-    if constexpr (FMT == kFormatQ4) {
-      d = q4_chunk_dot(w, x2 + jj * 16);
-    } else {
-      d = q8_chunk_dot(w, x2 + jj * 8);
-    }
-    acc = fmaf(d, scale, acc);
-  }
-  return acc;
-}
 
 struct Best {
   float v;
   uint32_t i;
 };
 
-// Consumes the stage's tiles. Non-LM stages leave per-row partial sums in
-// s->part[seg][local]; the LM stage keeps a running argmax per warp and
-// optionally stores the logits.
-template <uint32_t FMT, int CHS>
-__device__ void gemv_tiles(Ctx& c, const Piece* pieces, int np, int ks, bool lm, Best& best, float* logits_out) {
-  const int seg = c.warp % ks;
-  const int rstart = c.warp / ks;
-  const int rstride = kConsumerWarps / ks;
-  uint64_t x2[CHS * Fmt<FMT>::kPairs];
-  load_x_regs<FMT, CHS>(c.s, c.lane, seg, x2);
-  for (int p = 0; p < np; ++p) {
-    const DevMat& mat = *pieces[p].mat;
-    const uint32_t per = rows_per_tile(mat);
-    for (uint32_t r = 0; r < pieces[p].rows; r += per) {
-      const uint32_t nr = min(per, pieces[p].rows - r);
-      const uint32_t slot = c.it % kSlots;
-      const uint32_t parity = (c.it / kSlots) & 1u;
-      if (c.ok && !mbar_wait_bounded(&c.s->full[slot], parity, c.P->error, global_timer_ns() + c.P->timeout_ns,
-                                     kErrFull)) {
-        c.ok = false;
-      }
+// Consumes the stage's tiles. Non-LM stages leave per-row dot products in
+// s->part[local]; the LM stage keeps a running argmax per lane and optionally
+// stores the logits. Lane l of a warp always takes the 16-byte code chunks at
+// l * 16 + 512 * j of a row, and the matching activations from x.
+template <uint32_t FMT>
+__device__ void gemv_tiles(Ctx& c, const Piece* pieces, int np, bool lm, Best& best, float* logits_out) {
+#pragma unroll
+  for (int p = 0; p < 3; ++p) {
+    if (p >= np) break;
+    const Piece pc = pieces[p];
+    const uint32_t per = rows_per_tile(pc);
+    const uint32_t chunks = pc.code_row / 512u;
+    for (uint32_t r = 0; r < pc.rows; r += per) {
+      const uint32_t nr = min(per, pc.rows - r);
+      const uint8_t* base = acquire_tile(c);
       if (c.ok) {
-        const uint8_t* base = c.s->ring[slot];
-        const uint8_t* codes = base + nr * mat.scale_row;
-        for (uint32_t i = rstart; i < nr; i += rstride) {
-          float v = row_partial<FMT, CHS>(base + i * mat.scale_row, codes + i * mat.code_row, c.lane, seg, x2);
-          v = warp_sum(v);
-          if (c.lane == 0) {
-            const uint32_t local = pieces[p].local0 + r + i;
+        const uint8_t* codes = base + nr * pc.scale_row;
+        const uint32_t magic = magic_reg();
+        // Up to four rows per pass (rows i0, i0 + 8, ...): independent
+        // dot-product chains that share each activation load, reduced
+        // together (warp_sum4). Rows past the tile are skipped (warp-uniform).
+        for (uint32_t i0 = c.warp; i0 < nr; i0 += kRowsPerPass * kConsumerWarps) {
+          float acc[kRowsPerPass] = {0.0f, 0.0f, 0.0f, 0.0f};
+          for (uint32_t j = 0; j < chunks; ++j) {
+            const uint32_t off = 16u * c.lane + 512u * j;
+            const uint32_t kbase = off * Fmt<FMT>::kKPerByte;
+            uint64_t x2[Fmt<FMT>::kPairs];
+#pragma unroll
+            for (int q = 0; q < Fmt<FMT>::kPairs / 2; ++q) {
+              const float4 v = *reinterpret_cast<const float4*>(&c.s->x[x_index(kbase + 4 * q)]);
+              x2[2 * q] = pack2(v.x, v.y);
+              x2[2 * q + 1] = pack2(v.z, v.w);
+            }
+#pragma unroll
+            for (int q = 0; q < kRowsPerPass; ++q) {
+              const uint32_t row = i0 + q * kConsumerWarps;
+              if (row < nr) {
+                const uint4 w = *reinterpret_cast<const uint4*>(codes + row * pc.code_row + off);
+                const float scale = f16_bits_to_f32_fast(
+                    *reinterpret_cast<const uint16_t*>(base + row * pc.scale_row + (off / Fmt<FMT>::kDB) * 2));
+                float d;
+                if constexpr (FMT == kFormatQ4) {
+                  d = q4_chunk_dot(w, x2, magic);
+                } else {
+                  d = q8_chunk_dot(w, x2);
+                }
+                acc[q] = fmaf(d, scale, acc[q]);
+              }
+            }
+          }
+          const float total = warp_sum4(acc[0], acc[1], acc[2], acc[3]);
+          const uint32_t q = static_cast<uint32_t>(c.lane) >> 3;
+          const uint32_t i = i0 + q * kConsumerWarps;
+          if ((c.lane & 7) == 0 && i < nr) {
+            const uint32_t local = pc.local0 + r + i;
             if (!lm) {
-              c.s->part[seg][local] = v;
+              c.s->part[local] = total;
             } else {
-              const uint32_t row = pieces[p].out0 + r + i;
-              if (logits_out) logits_out[row] = v;
-              if (v > best.v || (v == best.v && row < best.i)) best = Best{v, row};
+              const uint32_t row = pc.out0 + r + i;
+              if (logits_out) logits_out[row] = total;
+              if (total > best.v || (total == best.v && row < best.i)) best = Best{total, row};
             }
           }
         }
       }
-      __syncwarp();
-      if (c.lane == 0) mbar_arrive(&c.s->empty[slot]);
-      ++c.it;
+      release_tile(c);
     }
   }
 }
 
-__device__ __forceinline__ int choose_ks(const DevMat& mat, int vals_per_chunk, int& chs) {
-  const int ch = static_cast<int>(mat.code_row / 512u);
-  for (int ks = 1; ks <= kConsumerWarps; ks *= 2) {
-    if (ch % ks == 0 && (ch / ks) * vals_per_chunk <= 96) {
-      chs = ch / ks;
-      return ks;
-    }
-  }
-  chs = 0;
-  return 0;
-}
-
-// Runs one GEMV stage over the CTA's pieces; returns the K-segment count.
-__device__ int gemv_stage(Ctx& c, int stage, uint32_t layer, Best& best, float* logits_out) {
+// Runs one GEMV stage over the CTA's pieces.
+__device__ void gemv_stage(Ctx& c, int stage, uint32_t layer, Best& best, float* logits_out) {
   Piece pieces[3];
   const int np = stage_pieces(*c.m, layer, stage, blockIdx.x, gridDim.x, pieces);
-  const DevMat& ref = stage == kStLM ? c.m->lm_head
-                    : stage == kStQKV ? c.m->layers[layer].q
-                    : stage == kStO ? c.m->layers[layer].o
-                    : stage == kStGate ? c.m->layers[layer].gate
-                    : stage == kStUp ? c.m->layers[layer].up
-                                     : c.m->layers[layer].down;
-  const bool lm = stage == kStLM;
-  int chs = 0;
-  int ks;
-  if (ref.format == kFormatQ4) {
-    ks = choose_ks(ref, 32, chs);
-    switch (chs) {
-      case 1: gemv_tiles<kFormatQ4, 1>(c, pieces, np, ks, lm, best, logits_out); break;
-      case 2: gemv_tiles<kFormatQ4, 2>(c, pieces, np, ks, lm, best, logits_out); break;
-      case 3: gemv_tiles<kFormatQ4, 3>(c, pieces, np, ks, lm, best, logits_out); break;
-      default: if (c.tid == 0) atomicCAS(c.P->error, 0, kErrShape); c.ok = false; break;
-    }
+  if (stage_format(*c.m, layer, stage) == kFormatQ4) {
+    gemv_tiles<kFormatQ4>(c, pieces, np, stage == kStLM, best, logits_out);
   } else {
-    ks = choose_ks(ref, 16, chs);
-    switch (chs) {
-      case 1: gemv_tiles<kFormatQ8, 1>(c, pieces, np, ks, lm, best, logits_out); break;
-      case 2: gemv_tiles<kFormatQ8, 2>(c, pieces, np, ks, lm, best, logits_out); break;
-      case 3: gemv_tiles<kFormatQ8, 3>(c, pieces, np, ks, lm, best, logits_out); break;
-      case 4: gemv_tiles<kFormatQ8, 4>(c, pieces, np, ks, lm, best, logits_out); break;
-      case 5: gemv_tiles<kFormatQ8, 5>(c, pieces, np, ks, lm, best, logits_out); break;
-      case 6: gemv_tiles<kFormatQ8, 6>(c, pieces, np, ks, lm, best, logits_out); break;
-      default: if (c.tid == 0) atomicCAS(c.P->error, 0, kErrShape); c.ok = false; break;
-    }
+    gemv_tiles<kFormatQ8>(c, pieces, np, stage == kStLM, best, logits_out);
   }
   consumer_sync(kConsumerThreads);
-  return ks;
-}
-
-__device__ __forceinline__ float stage_row_value(const Smem* s, uint32_t local, int ks) {
-  return ks == 2 ? s->part[0][local] + s->part[1][local] : s->part[0][local];
 }
 
 // ---- attention (decodeAttentionStepQ8, kernels.zig:697-767, split-K) ----
+//
+// Unit u = (kv head h, chunk ch of kAttnChunk positions); CTA b takes units
+// b, b + grid, ... The producer streams each unit's tile: the chunk's cached
+// key/value rows (codes and scales, TMA boxes of the q8 cache), the layer's
+// q/k RMSNorm weights and this position's RoPE row. The newest position's
+// key/value row is computed here by the unit that holds it and never read
+// back from the cache.
 
 __device__ void attention_stage(Ctx& c, uint32_t layer, uint32_t position) {
   const DevModel& m = *c.m;
   AttnSmem* a = reinterpret_cast<AttnSmem*>(c.s->x);
-  const uint32_t n_pos = position + 1;
-  const uint32_t chunks = (n_pos + kAttnChunk - 1) / kAttnChunk;
+  const uint32_t chunks = position / kAttnChunk + 1;
   const uint32_t units = m.kv_heads * chunks;
   const uint32_t kvw = m.kv_heads * kHeadDim;
   const uint32_t qw = m.q_heads * kHeadDim;
   const uint32_t kv_groups = kvw / kGroup;
-  const uint8_t* kl = c.P->k_cache + size_t(layer) * m.cache_layer_stride;
-  const uint8_t* vl = c.P->v_cache + size_t(layer) * m.cache_layer_stride;
-  const DevLayer& L = m.layers[layer];
-  const float* cos_row = m.rope_cos + size_t(position) * (kHeadDim / 2);
-  const float* sin_row = m.rope_sin + size_t(position) * (kHeadDim / 2);
+  uint8_t* kl = c.P->k_cache + size_t(layer) * m.cache_layer_stride;
+  uint8_t* vl = c.P->v_cache + size_t(layer) * m.cache_layer_stride;
   const int tid = c.tid;
+  const int j = tid / kHeadDim;  // query head 2h + j; for the appended row, key (0) / value (1)
+  const int d = tid % kHeadDim;
+  const uint32_t newest = position;
 
-  for (uint32_t u = blockIdx.x; u < units && c.ok; u += gridDim.x) {
+  for (uint32_t u = blockIdx.x; u < units; u += gridDim.x) {
     const uint32_t h = u / chunks;
     const uint32_t ch = u % chunks;
-    const int j = tid / kHeadDim;        // which query head of the pair, or k (0) / v (1)
-    const int d = tid % kHeadDim;
-    // Query heads 2h, 2h+1: per-head RMSNorm (decoder.zig:180-186), then RoPE.
+    const bool last = ch == chunks - 1;
+    // 1. Query rows 2h, 2h+1 (and in the last chunk the new key/value rows)
+    // from L2, issued before waiting for the tile.
+    const float qraw = ld_cg(c.P->qkv + (2 * h + j) * kHeadDim + d);
+    const float kvraw = last ? ld_cg(c.P->qkv + qw + size_t(j) * kvw + h * kHeadDim + d) : 0.0f;
+    const uint8_t* tile = acquire_tile(c);
+    const float* q_norm = reinterpret_cast<const float*>(tile + kTileQNorm);
+    const float* k_norm = reinterpret_cast<const float*>(tile + kTileKNorm);
+    const float* cos_row = reinterpret_cast<const float*>(tile + kTileCos);
+    const float* sin_row = reinterpret_cast<const float*>(tile + kTileSin);
+    // 2. Per-head RMSNorm of the queries and the new key (decoder.zig:180-195).
     {
-      const float raw = ld_cg(c.P->qkv + (2 * h + j) * kHeadDim + d);
-      const float ss = warp_sum(raw * raw);
-      if (c.lane == 0) c.s->red[c.warp] = ss;
+      const float ss = warp_sum(qraw * qraw);
+      const float kss = warp_sum(kvraw * kvraw);
+      if (c.lane == 0) {
+        c.s->red[c.warp] = ss;
+        c.s->red[kConsumerWarps + c.warp] = kss;
+      }
       consumer_sync(kConsumerThreads);
       const int w0 = j * 4;
       const float total = ((c.s->red[w0] + c.s->red[w0 + 1]) + c.s->red[w0 + 2]) + c.s->red[w0 + 3];
       const float inv = 1.0f / sqrtf(total / static_cast<float>(kHeadDim) + m.eps);
-      a->tmp[j][d] = raw * inv * __ldg(L.q_norm + d);
-      consumer_sync(kConsumerThreads);
-      if (d < kHeadDim / 2) {
-        const float lo = a->tmp[j][d], hi = a->tmp[j][d + kHeadDim / 2];
-        const float cs = __ldg(cos_row + d), sn = __ldg(sin_row + d);
-        a->q[j][d] = lo * cs - hi * sn;
-        a->q[j][d + kHeadDim / 2] = hi * cs + lo * sn;
+      a->tmp[j][d] = qraw * inv * q_norm[d];
+      if (last && j == 0) {
+        const float kt = ((c.s->red[kConsumerWarps] + c.s->red[kConsumerWarps + 1]) + c.s->red[kConsumerWarps + 2]) +
+                         c.s->red[kConsumerWarps + 3];
+        const float kinv = 1.0f / sqrtf(kt / static_cast<float>(kHeadDim) + m.eps);
+        a->ktmp[d] = kvraw * kinv * k_norm[d];
       }
       consumer_sync(kConsumerThreads);
     }
-    // The unit holding the newest position appends its key and value row
-    // (decoder.zig:187-216): key -> K-RMSNorm -> RoPE -> q8; value -> q8.
-    if (ch == chunks - 1) {
-      const float raw = ld_cg(c.P->qkv + qw + size_t(j) * kvw + h * kHeadDim + d);
-      float val = raw;
+    // 3. RoPE (rotate_half, kernels.zig rope) of the queries and the new key.
+    const int pair = d % (kHeadDim / 2);
+    const float cs = cos_row[pair], sn = sin_row[pair];
+    {
+      const float lo = a->tmp[j][pair], hi = a->tmp[j][pair + kHeadDim / 2];
+      const float rot = d < kHeadDim / 2 ? lo * cs - hi * sn : hi * cs + lo * sn;
+      a->q[j][d / 32][d % 32] = rot;
+    }
+    // 4. The last chunk appends the new key (normed, rotated) and value rows
+    // as q8 (decoder.zig:187-216, quant.zig:197-227): one 64-value group per
+    // two warps. The codes also stay in shared memory for this unit.
+    if (last) {
+      float val = kvraw;
       if (j == 0) {
-        const float ss = warp_sum(raw * raw);
-        if (c.lane == 0) c.s->red[c.warp] = ss;
-      }
-      consumer_sync(kConsumerThreads);
-      if (j == 0) {
-        const float total = ((c.s->red[0] + c.s->red[1]) + c.s->red[2]) + c.s->red[3];
-        const float inv = 1.0f / sqrtf(total / static_cast<float>(kHeadDim) + m.eps);
-        a->tmp[0][d] = raw * inv * __ldg(L.k_norm + d);
-      }
-      consumer_sync(kConsumerThreads);
-      if (j == 0) {
-        const int pair = d < kHeadDim / 2 ? d : d - kHeadDim / 2;
-        const float lo = a->tmp[0][pair], hi = a->tmp[0][pair + kHeadDim / 2];
-        const float cs = __ldg(cos_row + pair), sn = __ldg(sin_row + pair);
+        const float lo = a->ktmp[pair], hi = a->ktmp[pair + kHeadDim / 2];
         val = d < kHeadDim / 2 ? lo * cs - hi * sn : hi * cs + lo * sn;
       }
-      // q8 quantization of each 64-value group (quant.zig:197-227): two warps per group.
       const float amax = warp_max(fabsf(val));
+      consumer_sync(kConsumerThreads);
       if (c.lane == 0) c.s->red[c.warp] = amax;
       consumer_sync(kConsumerThreads);
       const int gw = (c.warp / 2) * 2;
       const float gmax = fmaxf(c.s->red[gw], c.s->red[gw + 1]);
       const __half sh = __float2half_rn(gmax / 128.0f);
-      const float stored = __half2float(sh);
-      const uint8_t code = q8_code(val, stored);
-      uint8_t* plane = const_cast<uint8_t*>(j == 0 ? kl : vl);
+      const uint8_t code = q8_code(val, __half2float(sh));
+      uint8_t* plane = j == 0 ? kl : vl;
       plane[m.cache_scales_bytes + size_t(position) * kvw + h * kHeadDim + d] = code;
+      reinterpret_cast<uint8_t*>(a->new_codes[j])[d] = code;
       if ((d % kGroup) == 0) {
-        reinterpret_cast<uint16_t*>(plane + size_t(position) * kv_groups * 2)[h * 2 + d / kGroup] =
-            __half_as_ushort(sh);
+        reinterpret_cast<uint16_t*>(plane + size_t(position) * kv_groups * 2)[h * 2 + d / kGroup] = __half_as_ushort(sh);
+        a->new_scales[j][d / kGroup] = __half_as_ushort(sh);
       }
-      __threadfence_block();
-      consumer_sync(kConsumerThreads);
+      // Later tokens read this row through TMA (the async proxy).
+      fence_proxy_async_global();
     }
-    // Scores: 16 positions per warp, a lane pair per position, one 64-value
-    // group per lane (q8GroupDot, kernels.zig:636-661).
-    const float scaling = m.attn_scaling;
-    float m_run[2];
+    consumer_sync(kConsumerThreads);
+    // 5. Scores (q8GroupDot, kernels.zig:636-661): four lanes per position,
+    // 32 dimensions each; the two lanes of a 64-value group add their sums
+    // before the group scale.
+    const uint32_t r = static_cast<uint32_t>(tid) / 4;
+    const uint32_t qd = static_cast<uint32_t>(tid) % 4;
+    float p0, p1;
     {
-      const uint32_t pl = c.warp * 16 + c.lane / 2;
-      const uint32_t p = ch * kAttnChunk + pl;
-      const int g = c.lane & 1;
-      float s0 = 0.0f, s1 = 0.0f;
-      if (p < n_pos) {
-        const uint8_t* codes = kl + m.cache_scales_bytes + size_t(p) * kvw + h * kHeadDim + g * kGroup;
-        const float scale = f16_bits_to_f32(
-            __ldcg(reinterpret_cast<const unsigned short*>(kl + size_t(p) * kv_groups * 2) + h * 2 + g));
-        uint64_t acc0 = 0, acc1 = 0;
-        const uint64_t bias = pack2(kNegQ8, kNegQ8);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint4 w = __ldcg(reinterpret_cast<const uint4*>(codes) + q);
-          const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const int base = g * kGroup + q * 16 + t * 4;
-            const uint64_t c01 = add2(pack2(bits_f32(__byte_perm(words[t], kMagic, 0x7440)),
-                                            bits_f32(__byte_perm(words[t], kMagic, 0x7441))), bias);
-            const uint64_t c23 = add2(pack2(bits_f32(__byte_perm(words[t], kMagic, 0x7442)),
-                                            bits_f32(__byte_perm(words[t], kMagic, 0x7443))), bias);
-            acc0 = fma2(c01, pack2(a->q[0][base], a->q[0][base + 1]), acc0);
-            acc0 = fma2(c23, pack2(a->q[0][base + 2], a->q[0][base + 3]), acc0);
-            acc1 = fma2(c01, pack2(a->q[1][base], a->q[1][base + 1]), acc1);
-            acc1 = fma2(c23, pack2(a->q[1][base + 2], a->q[1][base + 3]), acc1);
-          }
-        }
-        const float2 f0 = unpack2(acc0), f1 = unpack2(acc1);
-        s0 = (f0.x + f0.y) * scale;
-        s1 = (f1.x + f1.y) * scale;
+      const uint32_t pos = ch * kAttnChunk + r;
+      const bool valid = pos <= newest;
+      uint4 kw0, kw1;
+      uint32_t kbits;
+      if (pos == newest) {
+        const uint4* src = reinterpret_cast<const uint4*>(a->new_codes[0]) + qd * 2;
+        kw0 = src[0];
+        kw1 = src[1];
+        kbits = a->new_scales[0][qd / 2];
+      } else {
+        const uint4* src = reinterpret_cast<const uint4*>(tile + kTileKCodes + r * kHeadDim + qd * 32);
+        kw0 = src[0];
+        kw1 = src[1];
+        kbits = *reinterpret_cast<const uint16_t*>(tile + kTileKScales + r * 16 + (h % 4) * 4 + (qd / 2) * 2);
       }
-      s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
-      s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
-      const bool valid = p < n_pos;
-      const float sc0 = valid ? scaling * s0 : -INFINITY;
-      const float sc1 = valid ? scaling * s1 : -INFINITY;
+      const uint32_t words[8] = {kw0.x, kw0.y, kw0.z, kw0.w, kw1.x, kw1.y, kw1.z, kw1.w};
+      const uint64_t bias = pack2(kNegQ8, kNegQ8);
+      uint64_t acc0 = 0, acc1 = 0;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        const float4 q0 = *reinterpret_cast<const float4*>(&a->q[0][qd][4 * w]);
+        const float4 q1 = *reinterpret_cast<const float4*>(&a->q[1][qd][4 * w]);
+        const uint64_t c01 = add2(pack2(bits_f32(__byte_perm(words[w], kMagic, 0x7440)),
+                                        bits_f32(__byte_perm(words[w], kMagic, 0x7441))), bias);
+        const uint64_t c23 = add2(pack2(bits_f32(__byte_perm(words[w], kMagic, 0x7442)),
+                                        bits_f32(__byte_perm(words[w], kMagic, 0x7443))), bias);
+        acc0 = fma2(c01, pack2(q0.x, q0.y), acc0);
+        acc0 = fma2(c23, pack2(q0.z, q0.w), acc0);
+        acc1 = fma2(c01, pack2(q1.x, q1.y), acc1);
+        acc1 = fma2(c23, pack2(q1.z, q1.w), acc1);
+      }
+      const float2 f0 = unpack2(acc0), f1 = unpack2(acc1);
+      float g0 = f0.x + f0.y, g1 = f1.x + f1.y;
+      g0 += __shfl_xor_sync(0xffffffffu, g0, 1);
+      g1 += __shfl_xor_sync(0xffffffffu, g1, 1);
+      const float scale = f16_bits_to_f32_fast(kbits);
+      g0 *= scale;
+      g1 *= scale;
+      g0 += __shfl_xor_sync(0xffffffffu, g0, 2);
+      g1 += __shfl_xor_sync(0xffffffffu, g1, 2);
+      const float sc0 = valid ? m.attn_scaling * g0 : -INFINITY;
+      const float sc1 = valid ? m.attn_scaling * g1 : -INFINITY;
       // Chunk maxima (math.zig:77-93 subtracts the row max before exp).
       const float w0 = warp_max(sc0), w1 = warp_max(sc1);
-      consumer_sync(kConsumerThreads);
       if (c.lane == 0) {
         c.s->red[c.warp] = w0;
         c.s->red[kConsumerWarps + c.warp] = w1;
       }
       consumer_sync(kConsumerThreads);
-      m_run[0] = -INFINITY;
-      m_run[1] = -INFINITY;
+      float m0 = -INFINITY, m1 = -INFINITY;
 #pragma unroll
       for (int w = 0; w < kConsumerWarps; ++w) {
-        m_run[0] = fmaxf(m_run[0], c.s->red[w]);
-        m_run[1] = fmaxf(m_run[1], c.s->red[kConsumerWarps + w]);
+        m0 = fmaxf(m0, c.s->red[w]);
+        m1 = fmaxf(m1, c.s->red[kConsumerWarps + w]);
       }
-      if ((c.lane & 1) == 0) {
-        a->prob[0][pl] = valid ? expf(sc0 - m_run[0]) : 0.0f;
-        a->prob[1][pl] = valid ? expf(sc1 - m_run[1]) : 0.0f;
+      p0 = valid ? expf(sc0 - m0) : 0.0f;
+      p1 = valid ? expf(sc1 - m1) : 0.0f;
+      if (qd == 0) {
+        a->prob[0][r] = p0;
+        a->prob[1][r] = p1;
       }
+      const float l0 = warp_sum(qd == 0 ? p0 : 0.0f), l1 = warp_sum(qd == 0 ? p1 : 0.0f);
+      if (c.lane == 0) {
+        a->lsum[0][c.warp] = l0;
+        a->lsum[1][c.warp] = l1;
+      }
+      a->mx[j] = j == 0 ? m0 : m1;
       consumer_sync(kConsumerThreads);
     }
-    // Values (q8GroupAccumulate, kernels.zig:665-688): lane = 4 dims, warp = 16 positions.
+    // 6. Values (q8GroupAccumulate, kernels.zig:665-688): lane = 4
+    // dimensions, warp = 8 positions.
     {
       float acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
-      const int g = (4 * c.lane) / kGroup;
-      for (int q = 0; q < 16; ++q) {
-        const uint32_t pl = c.warp * 16 + q;
-        const uint32_t p = ch * kAttnChunk + pl;
-        if (p >= n_pos) break;
-        const uint32_t word =
-            __ldcg(reinterpret_cast<const unsigned int*>(vl + m.cache_scales_bytes + size_t(p) * kvw + h * kHeadDim) +
-                   c.lane);
-        const float scale = f16_bits_to_f32(
-            __ldcg(reinterpret_cast<const unsigned short*>(vl + size_t(p) * kv_groups * 2) + h * 2 + g));
-        const float sw0 = scale * a->prob[0][pl];
-        const float sw1 = scale * a->prob[1][pl];
+      const uint32_t grp = static_cast<uint32_t>(c.lane) / 16;
+#pragma unroll
+      for (int i = 0; i < kAttnChunk / kConsumerWarps; ++i) {
+        const uint32_t rr = c.warp * (kAttnChunk / kConsumerWarps) + i;
+        const uint32_t pos = ch * kAttnChunk + rr;
+        uint32_t word, bits;
+        if (pos == newest) {
+          word = a->new_codes[1][c.lane];
+          bits = a->new_scales[1][grp];
+        } else {
+          word = *reinterpret_cast<const uint32_t*>(tile + kTileVCodes + rr * kHeadDim + 4 * c.lane);
+          bits = *reinterpret_cast<const uint16_t*>(tile + kTileVScales + rr * 16 + (h % 4) * 4 + grp * 2);
+        }
+        const float scale = f16_bits_to_f32_fast(bits);
+        const bool valid = pos <= newest;
+        const float sw0 = valid ? scale * a->prob[0][rr] : 0.0f;
+        const float sw1 = valid ? scale * a->prob[1][rr] : 0.0f;
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
-          const float cv = static_cast<float>((word >> (8 * t)) & 0xFFu) - 128.0f;
+          const float cv = bits_f32(__byte_perm(word, kMagic, 0x7440 + t)) + kNegQ8;  // code - 128, exact
           acc[0][t] = fmaf(cv, sw0, acc[0][t]);
           acc[1][t] = fmaf(cv, sw1, acc[1][t]);
         }
       }
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        a->vpart[c.warp][0][4 * c.lane + t] = acc[0][t];
-        a->vpart[c.warp][1][4 * c.lane + t] = acc[1][t];
-      }
+      release_tile(c);
+      *reinterpret_cast<float4*>(&a->vpart[c.warp][0][4 * c.lane]) = make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
+      *reinterpret_cast<float4*>(&a->vpart[c.warp][1][4 * c.lane]) = make_float4(acc[1][0], acc[1][1], acc[1][2], acc[1][3]);
     }
     consumer_sync(kConsumerThreads);
-    // Chunk partial: o[d], max, sum -> global, then the last unit of this kv
-    // head combines every chunk (flash-decode rescale).
-    {
-      float o = 0.0f;
+    // 7. One chunk: the output directly. Several: a chunk partial (o[d], max,
+    // sum) to global, then the last unit of this kv head to finish combines
+    // them (flash-decode rescale).
+    float o = 0.0f, l = 0.0f;
 #pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) o += a->vpart[w][j][d];
+    for (int w = 0; w < kConsumerWarps; ++w) {
+      o += a->vpart[w][j][d];
+      l += a->lsum[j][w];
+    }
+    const float mj = a->mx[j];
+    if (chunks == 1) {
+      c.P->attn_out[(2 * h + j) * kHeadDim + d] = o / l;
+      consumer_sync(kConsumerThreads);
+      continue;
+    }
+    {
       float* dst = c.P->attn_part + (size_t(2 * h + j) * c.P->max_chunks + ch) * (kHeadDim + 2);
       dst[d] = o;
       if (d == 0) {
-        float l = 0.0f;
-        for (uint32_t q = 0; q < kAttnChunk; ++q) l += a->prob[j][q];
-        dst[kHeadDim] = m_run[j];
+        dst[kHeadDim] = mj;
         dst[kHeadDim + 1] = l;
       }
     }
@@ -679,16 +830,39 @@ __device__ void attention_stage(Ctx& c, uint32_t layer, uint32_t position) {
     consumer_sync(kConsumerThreads);
     if (c.s->flag) {
       __threadfence();
+      // Chunks are combined eight at a time with all loads of a batch issued
+      // together (online rescale).
       float mx = -INFINITY;
-      for (uint32_t q = 0; q < chunks; ++q) {
-        mx = fmaxf(mx, ld_cg(c.P->attn_part + (size_t(2 * h + j) * c.P->max_chunks + q) * (kHeadDim + 2) + kHeadDim));
-      }
-      float o = 0.0f, l = 0.0f;
-      for (uint32_t q = 0; q < chunks; ++q) {
-        const float* src = c.P->attn_part + (size_t(2 * h + j) * c.P->max_chunks + q) * (kHeadDim + 2);
-        const float f = expf(ld_cg(src + kHeadDim) - mx);
-        o = fmaf(ld_cg(src + d), f, o);
-        l = fmaf(ld_cg(src + kHeadDim + 1), f, l);
+      o = 0.0f;
+      l = 0.0f;
+      const float* base = c.P->attn_part + size_t(2 * h + j) * c.P->max_chunks * (kHeadDim + 2);
+      for (uint32_t q0 = 0; q0 < chunks; q0 += 8) {
+        float pm[8], po[8], pl[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          pm[q] = -INFINITY;
+          po[q] = 0.0f;
+          pl[q] = 0.0f;
+          if (q0 + q < chunks) {
+            const float* src = base + size_t(q0 + q) * (kHeadDim + 2);
+            pm[q] = ld_cg(src + kHeadDim);
+            po[q] = ld_cg(src + d);
+            pl[q] = ld_cg(src + kHeadDim + 1);
+          }
+        }
+        float bm = mx;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) bm = fmaxf(bm, pm[q]);
+        const float rescale = (mx == -INFINITY) ? 0.0f : expf(mx - bm);
+        o *= rescale;
+        l *= rescale;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float f = (pm[q] == -INFINITY) ? 0.0f : expf(pm[q] - bm);
+          o = fmaf(po[q], f, o);
+          l = fmaf(pl[q], f, l);
+        }
+        mx = bm;
       }
       c.P->attn_out[(2 * h + j) * kHeadDim + d] = o / l;
       if (tid == 0) c.P->attn_count[h] = 0;
@@ -701,8 +875,8 @@ __device__ void attention_stage(Ctx& c, uint32_t layer, uint32_t position) {
 
 __device__ void run_consumers(const DecodeLaunch& P, Smem* s) {
   const DevModel& m = *P.model;
-  Ctx c{&P, &m, s, 0, 0, 0, true, static_cast<int>(threadIdx.x / 32), static_cast<int>(threadIdx.x % 32),
-        static_cast<int>(threadIdx.x)};
+  Ctx c{&P, &m, s, 0, 0, true, static_cast<int>(threadIdx.x / 32), static_cast<int>(threadIdx.x % 32),
+        static_cast<int>(threadIdx.x), false, 0, 0};
   const Span own = split_rows(m.hidden, blockIdx.x, gridDim.x);  // hidden rows of O and down
   const uint32_t qw = m.q_heads * kHeadDim;
   uint32_t input = P.first_input;
@@ -714,87 +888,95 @@ __device__ void run_consumers(const DecodeLaunch& P, Smem* s) {
       input = P.forced_token[t];
       row = P.forced_row ? P.forced_row[t] : -1;
     }
+    c.tracing = P.trace != nullptr && t == P.trace_token;
     for (uint32_t l = 0; l < m.n_layers && c.ok; ++l) {
-      const DevLayer& L = m.layers[l];
       Best best{-INFINITY, 0};
+      const uint32_t e0 = l * kTraceEventsPerLayer;
+      trace_mark(c, e0 + 0);
       // -- QKV: x = rmsnorm(hidden) (decoder.zig:165-176)
+      const bool qkv_q4 = stage_format(m, l, kStQKV) == kFormatQ4;
       if (l == 0) {
-        load_x_input(c, input, row);
-        for (uint32_t r = own.begin + c.tid; r < own.end; r += kConsumerThreads) {
-          s->resid[r - own.begin] = s->x[x_index(r)];
-        }
+        input_into_x(c, input, row, own, qkv_q4);
       } else {
-        load_x_global(c, P.hidden_g, m.hidden);
+        norm_global_into_x(c, P.hidden_g, m.hidden, qkv_q4);
       }
-      normalize_x(c, m.hidden, L.attn_norm);
+      trace_mark(c, e0 + 1);
+      gemv_stage(c, kStQKV, l, best, nullptr);
       {
-        const int ks = gemv_stage(c, kStQKV, l, best, nullptr);
         Piece pieces[3];
         const int np = stage_pieces(m, l, kStQKV, blockIdx.x, gridDim.x, pieces);
         for (int p = 0; p < np; ++p) {
           for (uint32_t i = c.tid; i < pieces[p].rows; i += kConsumerThreads) {
-            P.qkv[pieces[p].out0 + i] = stage_row_value(s, pieces[p].local0 + i, ks);
+            P.qkv[pieces[p].out0 + i] = s->part[pieces[p].local0 + i];
           }
         }
       }
+      trace_mark(c, e0 + 2);
       grid_barrier(c);
       if (!c.ok) break;
+      trace_mark(c, e0 + 3);
       // -- attention over position + 1 cached rows (decoder.zig:216-253)
       attention_stage(c, l, position);
+      trace_mark(c, e0 + 4);
       grid_barrier(c);
       if (!c.ok) break;
+      trace_mark(c, e0 + 5);
       // -- O projection + residual (decoder.zig:256-257)
-      load_x_global(c, P.attn_out, qw);
-      {
-        const int ks = gemv_stage(c, kStO, l, best, nullptr);
-        for (uint32_t r = own.begin + c.tid; r < own.end; r += kConsumerThreads) {
-          const float h = s->resid[r - own.begin] + stage_row_value(s, r - own.begin, ks);
-          s->resid[r - own.begin] = h;
-          P.hidden_g[r] = h;
-        }
+      load_x_global(c, P.attn_out, qw, stage_format(m, l, kStO) == kFormatQ4);
+      gemv_stage(c, kStO, l, best, nullptr);
+      for (uint32_t r = own.begin + c.tid; r < own.end; r += kConsumerThreads) {
+        const float h = s->resid[r - own.begin] + s->part[r - own.begin];
+        s->resid[r - own.begin] = h;
+        P.hidden_g[r] = h;
       }
+      trace_mark(c, e0 + 6);
       grid_barrier(c);
       if (!c.ok) break;
+      trace_mark(c, e0 + 7);
       // -- RMSNorm -> gate/up -> SwiGLU (decoder.zig:259-269)
-      load_x_global(c, P.hidden_g, m.hidden);
-      normalize_x(c, m.hidden, L.ffn_norm);
+      norm_global_into_x(c, P.hidden_g, m.hidden, stage_format(m, l, kStGate) == kFormatQ4);
       const Span fr = split_rows(m.ffn, blockIdx.x, gridDim.x);
-      {
-        const int ks = gemv_stage(c, kStGate, l, best, nullptr);
-        for (uint32_t i = c.tid; i < fr.end - fr.begin; i += kConsumerThreads) s->gate[i] = stage_row_value(s, i, ks);
-        consumer_sync(kConsumerThreads);
+      gemv_stage(c, kStGate, l, best, nullptr);
+      for (uint32_t i = c.tid; i < fr.end - fr.begin; i += kConsumerThreads) s->gate[i] = s->part[i];
+      consumer_sync(kConsumerThreads);
+      gemv_stage(c, kStUp, l, best, nullptr);
+      for (uint32_t i = c.tid; i < fr.end - fr.begin; i += kConsumerThreads) {
+        const float g = s->gate[i];
+        const float silu = g / (1.0f + expf(-g));
+        P.act[fr.begin + i] = silu * s->part[i];
       }
-      {
-        const int ks = gemv_stage(c, kStUp, l, best, nullptr);
-        for (uint32_t i = c.tid; i < fr.end - fr.begin; i += kConsumerThreads) {
-          const float g = s->gate[i];
-          const float silu = g / (1.0f + expf(-g));
-          P.act[fr.begin + i] = silu * stage_row_value(s, i, ks);
-        }
-      }
+      trace_mark(c, e0 + 8);
       grid_barrier(c);
       if (!c.ok) break;
       // -- down + residual (decoder.zig:270-271)
-      load_x_global(c, P.act, m.ffn);
-      {
-        const int ks = gemv_stage(c, kStDown, l, best, nullptr);
-        for (uint32_t r = own.begin + c.tid; r < own.end; r += kConsumerThreads) {
-          const float h = s->resid[r - own.begin] + stage_row_value(s, r - own.begin, ks);
-          s->resid[r - own.begin] = h;
-          P.hidden_g[r] = h;
-        }
+      load_x_global(c, P.act, m.ffn, stage_format(m, l, kStDown) == kFormatQ4);
+      gemv_stage(c, kStDown, l, best, nullptr);
+      for (uint32_t r = own.begin + c.tid; r < own.end; r += kConsumerThreads) {
+        const float h = s->resid[r - own.begin] + s->part[r - own.begin];
+        s->resid[r - own.begin] = h;
+        P.hidden_g[r] = h;
       }
+      trace_mark(c, e0 + 9);
       grid_barrier(c);
       if (!c.ok) break;
+      trace_mark(c, e0 + 10);
     }
     if (!c.ok) break;
     if (t >= P.logits_from) {
       // -- final RMSNorm -> lm_head -> argmax (decoder.zig:277-301)
-      load_x_global(c, P.hidden_g, m.hidden);
-      normalize_x(c, m.hidden, m.final_norm);
+      norm_global_into_x(c, P.hidden_g, m.hidden, m.lm_head.format == kFormatQ4);
       Best best{-INFINITY, 0xFFFFFFFFu};
       float* logits = (P.logits_out && t + 1 == P.n_tokens) ? P.logits_out : nullptr;
+      const uint32_t el = m.n_layers * kTraceEventsPerLayer;
+      trace_mark(c, el + 0);
       gemv_stage(c, kStLM, 0, best, logits);
+      trace_mark(c, el + 1);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best.v, o);
+        const uint32_t oi = __shfl_xor_sync(0xffffffffu, best.i, o);
+        if (ov > best.v || (ov == best.v && oi < best.i)) best = Best{ov, oi};
+      }
       if (c.lane == 0) {
         s->amax_v[c.warp] = best.v;
         s->amax_i[c.warp] = best.i;
@@ -811,16 +993,38 @@ __device__ void run_consumers(const DecodeLaunch& P, Smem* s) {
       }
       grid_barrier(c);
       if (!c.ok) break;
+      trace_mark(c, el + 2);
+      if (c.tracing && c.tid == 0) {
+        P.trace[blockIdx.x * kTraceEvents + kTraceEvents - 2] = c.full_wait_ns;
+        P.trace[blockIdx.x * kTraceEvents + kTraceEvents - 1] = c.bar_wait_ns;
+      }
+      // Every CTA combines the per-CTA maxima (one L2 round trip, then a
+      // block reduction). CTA row ranges ascend, so lowest-index-on-tie over
+      // (value, index) pairs is the reference's first-maximum rule.
+      Best b{-INFINITY, 0xFFFFFFFFu};
+      for (uint32_t q = c.tid; q < gridDim.x; q += kConsumerThreads) {
+        const Best o{ld_cg(P.amax_val + q), __ldcg(P.amax_idx + q)};
+        if (o.v > b.v || (o.v == b.v && o.i < b.i)) b = o;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, b.v, o);
+        const uint32_t oi = __shfl_xor_sync(0xffffffffu, b.i, o);
+        if (ov > b.v || (ov == b.v && oi < b.i)) b = Best{ov, oi};
+      }
+      if (c.lane == 0) {
+        s->amax_v[c.warp] = b.v;
+        s->amax_i[c.warp] = b.i;
+      }
+      consumer_sync(kConsumerThreads);
       if (c.tid == 0) {
-        // Combine in CTA order: CTA row ranges ascend, so strict `>` keeps
-        // the lowest index among equal maxima.
-        Best b{ld_cg(P.amax_val), __ldcg(P.amax_idx)};
-        for (uint32_t q = 1; q < gridDim.x; ++q) {
-          const float v = ld_cg(P.amax_val + q);
-          if (v > b.v) b = Best{v, __ldcg(P.amax_idx + q)};
+        Best f{s->amax_v[0], s->amax_i[0]};
+        for (int w = 1; w < kConsumerWarps; ++w) {
+          const Best o{s->amax_v[w], s->amax_i[w]};
+          if (o.v > f.v || (o.v == f.v && o.i < f.i)) f = o;
         }
-        s->flag = b.i;
-        if (blockIdx.x == 0) P.tokens_out[t] = b.i;
+        s->flag = f.i;
+        if (blockIdx.x == 0) P.tokens_out[t] = f.i;
       }
       consumer_sync(kConsumerThreads);
       input = s->flag;
@@ -829,7 +1033,8 @@ __device__ void run_consumers(const DecodeLaunch& P, Smem* s) {
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeLaunch P) {
+__global__ void __launch_bounds__(kThreads, 1)
+    decode_kernel(const __grid_constant__ DecodeLaunch P, const __grid_constant__ KvMaps maps) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem* s = reinterpret_cast<Smem*>(smem_raw);
   if (threadIdx.x == 0) {
@@ -841,7 +1046,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeLaunch 
   }
   __syncthreads();
   if (threadIdx.x >= kConsumerThreads) {
-    run_producer(P, s);
+    run_producer(P, maps, s);
   } else {
     run_consumers(P, s);
   }
@@ -857,16 +1062,13 @@ int decode_grid_size(int device) {
   return sms;
 }
 
-int launch_decode(const DecodeLaunch& launch, int grid, void* stream) {
-  static bool configured = false;
+int launch_decode(const DecodeLaunch& launch, const KvMaps& maps, int grid, void* stream) {
   const int smem = decode_kernel_smem_bytes();
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    configured = true;
-  }
+  cudaError_t e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return static_cast<int>(e);
   DecodeLaunch copy = launch;
-  void* args[] = {&copy};
+  KvMaps maps_copy = maps;
+  void* args[] = {&copy, &maps_copy};
   return static_cast<int>(cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(decode_kernel), dim3(grid),
                                                       dim3(kThreads), args, static_cast<size_t>(smem),
                                                       static_cast<cudaStream_t>(stream)));

@@ -63,13 +63,29 @@ __host__ __device__ constexpr float q4_xscale(int i) {
                 : 0.0000152587890625f;
 }
 
+// (w & MASK) | magic in one lop3 (LUT 0xEA = (a & b) | c).
+template <uint32_t MASK>
+__device__ __forceinline__ uint32_t and_or(uint32_t w, uint32_t magic) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(w), "n"(MASK), "r"(magic));
+  return r;
+}
+
+// The magic constant in a register the compiler will not fold back into an
+// immediate (so each nibble costs one lop3).
+__device__ __forceinline__ uint32_t magic_reg() {
+  uint32_t m = kMagic;
+  asm volatile("" : "+r"(m));
+  return m;
+}
+
 // Accumulates 8 nibbles of `w` against 4 packed pre-scaled activation pairs.
-__device__ __forceinline__ void q4_word(uint32_t w, const uint64_t* x2, uint64_t& acc) {
+__device__ __forceinline__ void q4_word(uint32_t w, uint32_t magic, const uint64_t* x2, uint64_t& acc) {
   const uint32_t h = w >> 12;
-  const uint64_t v01 = pack2(bits_f32((w & 0x0000000Fu) | kMagic), bits_f32((w & 0x000000F0u) | kMagic));
-  const uint64_t v23 = pack2(bits_f32((w & 0x00000F00u) | kMagic), bits_f32((w & 0x0000F000u) | kMagic));
-  const uint64_t v45 = pack2(bits_f32((w & 0x000F0000u) | kMagic), bits_f32((h & 0x00000F00u) | kMagic));
-  const uint64_t v67 = pack2(bits_f32((h & 0x0000F000u) | kMagic), bits_f32((h & 0x000F0000u) | kMagic));
+  const uint64_t v01 = pack2(bits_f32(and_or<0x0000000Fu>(w, magic)), bits_f32(and_or<0x000000F0u>(w, magic)));
+  const uint64_t v23 = pack2(bits_f32(and_or<0x00000F00u>(w, magic)), bits_f32(and_or<0x0000F000u>(w, magic)));
+  const uint64_t v45 = pack2(bits_f32(and_or<0x000F0000u>(w, magic)), bits_f32(and_or<0x00000F00u>(h, magic)));
+  const uint64_t v67 = pack2(bits_f32(and_or<0x0000F000u>(h, magic)), bits_f32(and_or<0x000F0000u>(h, magic)));
   acc = fma2(add2(v01, pack2(kNegM0, kNegM1)), x2[0], acc);
   acc = fma2(add2(v23, pack2(kNegM2, kNegM3)), x2[1], acc);
   acc = fma2(add2(v45, pack2(kNegM4, kNegM2)), x2[2], acc);
@@ -77,15 +93,17 @@ __device__ __forceinline__ void q4_word(uint32_t w, const uint64_t* x2, uint64_t
 }
 
 // 32 q4 weights (one 16-byte chunk) against 16 packed activation pairs.
-__device__ __forceinline__ float q4_chunk_dot(uint4 w, const uint64_t* x2) {
+__device__ __forceinline__ float q4_chunk_dot(uint4 w, const uint64_t* x2, uint32_t magic) {
   uint64_t a = 0, b = 0;
-  q4_word(w.x, x2 + 0, a);
-  q4_word(w.y, x2 + 4, b);
-  q4_word(w.z, x2 + 8, a);
-  q4_word(w.w, x2 + 12, b);
+  q4_word(w.x, magic, x2 + 0, a);
+  q4_word(w.y, magic, x2 + 4, b);
+  q4_word(w.z, magic, x2 + 8, a);
+  q4_word(w.w, magic, x2 + 12, b);
   const float2 fa = unpack2(a), fb = unpack2(b);
   return (fa.x + fa.y) + (fb.x + fb.y);
 }
+
+__device__ __forceinline__ float q4_chunk_dot(uint4 w, const uint64_t* x2) { return q4_chunk_dot(w, x2, magic_reg()); }
 
 __device__ __forceinline__ void q8_word(uint32_t w, const uint64_t* x2, uint64_t& acc) {
   const uint64_t v01 = pack2(bits_f32(__byte_perm(w, kMagic, 0x7440)), bits_f32(__byte_perm(w, kMagic, 0x7441)));
@@ -108,10 +126,50 @@ __device__ __forceinline__ float q8_chunk_dot(uint4 w, const uint64_t* x2) {
 
 __device__ __forceinline__ float f16_bits_to_f32(uint16_t bits) { return __half2float(__ushort_as_half(bits)); }
 
+// f16 -> f32 on the integer and FMA pipes: the exponent/mantissa bits moved
+// into f32 position read as 2^-112 times the value (an f32 subnormal for an
+// f16 subnormal), and the exact multiply by 2^112 restores it. Exact for
+// every finite f16, zero and subnormals included (FTZ must be off).
+__device__ __forceinline__ float f16_bits_to_f32_fast(uint32_t bits) {
+  const float magnitude = __uint_as_float((bits & 0x7FFFu) << 13) * 0x1p112f;
+  return __uint_as_float(__float_as_uint(magnitude) | ((bits & 0x8000u) << 16));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
+}
+
+// Sums four per-lane values across the warp with 6 shuffles (a transposing
+// butterfly): afterwards lanes 8q..8q+7 hold the total of value q.
+__device__ __forceinline__ float warp_sum4(float v0, float v1, float v2, float v3) {
+  const unsigned lane = threadIdx.x & 31u;
+  const bool hi16 = (lane & 16u) != 0;
+  float a = hi16 ? v2 : v0, b = hi16 ? v3 : v1;
+  const float sa = hi16 ? v0 : v2, sb = hi16 ? v1 : v3;
+  a += __shfl_xor_sync(0xffffffffu, sa, 16);
+  b += __shfl_xor_sync(0xffffffffu, sb, 16);
+  const bool hi8 = (lane & 8u) != 0;
+  float r = hi8 ? b : a;
+  r += __shfl_xor_sync(0xffffffffu, hi8 ? a : b, 8);
+  r += __shfl_xor_sync(0xffffffffu, r, 4);
+  r += __shfl_xor_sync(0xffffffffu, r, 2);
+  r += __shfl_xor_sync(0xffffffffu, r, 1);
+  return r;
+}
+
+// Sums two per-lane values across the warp with 5 shuffles: afterwards lanes
+// 0..15 hold the total of v0 and lanes 16..31 the total of v1.
+__device__ __forceinline__ float warp_sum2(float v0, float v1) {
+  const bool hi16 = (threadIdx.x & 16u) != 0;
+  float r = hi16 ? v1 : v0;
+  r += __shfl_xor_sync(0xffffffffu, hi16 ? v0 : v1, 16);
+  r += __shfl_xor_sync(0xffffffffu, r, 8);
+  r += __shfl_xor_sync(0xffffffffu, r, 4);
+  r += __shfl_xor_sync(0xffffffffu, r, 2);
+  r += __shfl_xor_sync(0xffffffffu, r, 1);
+  return r;
 }
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -176,6 +234,21 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       "l"(src), "r"(bytes), "r"(smem_addr(bar))
       : "memory");
 }
+
+// One box of a 3-D tensor map (no multicast) into shared memory, completing
+// on `bar`. x is the innermost coordinate in elements; x * element size must
+// be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* map, int32_t x, int32_t y, int32_t z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
+          "r"(smem_addr(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Orders this thread's generic-proxy global accesses before later async-proxy
+// (bulk copy / TMA) accesses.
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
 // Waits on an mbarrier phase with a wall-clock bound. Returns false (and sets
 // *error) if the bound is hit or another CTA already reported an error.

@@ -14,7 +14,8 @@ constexpr uint32_t kFormatQ4 = 16;
 constexpr uint32_t kFormatQ8 = 18;
 constexpr uint32_t kMaxLayers = 64;
 constexpr uint32_t kPositionLimit = 8192;  // src/core/qwen3_asr/model.zig:62
-constexpr uint32_t kAttnChunk = 128;       // positions per split-K attention unit
+constexpr uint32_t kAttnChunk = 64;        // positions per split-K attention unit
+constexpr uint32_t kHiddenMax = 4096;      // widest hidden vector of the decode kernel
 constexpr uint32_t kHeadDim = 128;         // the kernels are written for head_dim 128
 
 inline uint32_t data_bytes_per_group(uint32_t format) {
@@ -100,7 +101,26 @@ struct DecodeLaunch {
   int32_t* error;            // nonzero after a bounded wait gave up
   uint64_t timeout_ns;
   uint32_t max_chunks;
+  // Optional phase timeline: when non-null, thread 0 of every CTA stores
+  // %globaltimer at each phase boundary of token `trace_token` into
+  // trace[cta * kTraceEvents + event].
+  uint64_t* trace;
+  uint32_t trace_token;
 };
+
+// TMA descriptors (CUtensorMap, 128 opaque bytes each) of stream 0's q8
+// key/value cache, viewed as 3-D u8 tensors [layer][position][bytes]: the
+// codes planes (row = kv_width bytes) and the scales planes (row = kv_groups
+// * 2 bytes). Built by the host with cuTensorMapEncodeTiled.
+struct alignas(64) KvMaps {
+  uint8_t k_codes[128];
+  uint8_t k_scales[128];
+  uint8_t v_codes[128];
+  uint8_t v_scales[128];
+};
+
+constexpr uint32_t kTraceEvents = 512;
+constexpr uint32_t kTraceEventsPerLayer = 11;
 
 }  // namespace qwc
 
@@ -108,6 +128,6 @@ struct DecodeLaunch {
 namespace qwc {
 int decode_kernel_smem_bytes();
 // Returns cudaError_t as int.
-int launch_decode(const DecodeLaunch& launch, int grid, void* stream);
+int launch_decode(const DecodeLaunch& launch, const KvMaps& maps, int grid, void* stream);
 int decode_grid_size(int device);
 }  // namespace qwc

@@ -28,7 +28,7 @@ STATUS = {
 }
 
 CACHE_F32, CACHE_Q8 = 0, 1
-OPTION_IGNORE_EOS, OPTION_KEEP_LOGITS, OPTION_STEP_CHUNK = 1, 2, 3
+OPTION_IGNORE_EOS, OPTION_KEEP_LOGITS, OPTION_STEP_CHUNK, OPTION_TRACE = 1, 2, 3, 4
 FEATURE_MODEL, FEATURE_DECODE, FEATURE_STREAMS = 1 << 3, 1 << 4, 1 << 8
 
 # Every symbol include/qwenscriber_cuda.h declares: (restype, argtypes).
@@ -58,6 +58,7 @@ SIGNATURES = {
     "qwc_debug_logits": (c_int32, [c_uint32, c_uint32, c_void_p, c_uint32]),
     "qwc_debug_hold": (c_int32, [c_uint32, c_uint32, c_int64, POINTER(c_uint32)]),
     "qwc_debug_scratch": (c_int32, [c_uint32, c_uint32, c_void_p, c_uint32]),
+    "qwc_debug_trace": (c_int32, [c_uint32, c_void_p, c_uint32]),
     "qwc_debug_cache": (c_int32, [c_uint32, c_uint32, c_uint32, c_void_p, c_uint64]),
     "qwc_kernel_launches": (c_uint64, [c_uint32]),
     "qwc_rope_tables": (c_int32, [c_float, c_uint32, c_uint32, c_void_p, c_void_p]),
@@ -224,6 +225,11 @@ class CudaModel:
     def debug_scratch(self, which: int, count: int = 16384) -> np.ndarray:
         out = np.zeros(count, np.float32)
         n = check(self._L.qwc_debug_scratch(self.handle, which, out.ctypes.data, count), "qwc_debug_scratch")
+        return out[:n]
+
+    def debug_trace(self, count: int = 148 * 512 * 2) -> np.ndarray:
+        out = np.zeros(count, np.uint64)
+        n = check(self._L.qwc_debug_trace(self.handle, out.ctypes.data, count), "qwc_debug_trace")
         return out[:n]
 
     def debug_cache(self, which: int, nbytes: int, slot: int = 0) -> np.ndarray:
