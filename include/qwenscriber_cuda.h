@@ -227,6 +227,18 @@ int32_t qwc_op_attention_q8(const float* query, const void* keys_scales, const v
 /* Decoder.argmaxLogits (src/core/qwen3_asr/decoder.zig:290-301): first index
  * of the maximum. Uses a device workspace the library allocates per call. */
 int32_t qwc_op_argmax(const float* values, uint32_t count, uint32_t* out_index, void* stream);
+/* The same argmax with no device allocation: its scratch is a fixed 4 KiB
+ * array compiled into the library. No counterpart in the reference; for
+ * callers that must not enter the CUDA allocator while decoding, such as a
+ * serving process that has handed all free HBM to its weight and KV-cache
+ * pools, where an allocation can fail or wait on other work. At most
+ * QWC_ARGMAX_NOALLOC_MAX_COUNT values (else QWC_LIMIT_EXCEEDED). The first
+ * call on each device looks up the scratch address (cudaGetSymbolAddress),
+ * so make it before any stream capture. One scratch per device: calls that
+ * overlap on a device (other streams or host threads) race; calls on one
+ * stream are ordered. */
+#define QWC_ARGMAX_NOALLOC_MAX_COUNT 4194304u
+int32_t qwc_op_argmax_noalloc(const float* values, uint32_t count, uint32_t* out_index, void* stream);
 /* math.rmsNormInPlace per row (src/core/math.zig:120-130), out of place. */
 int32_t qwc_op_rmsnorm(const float* x, const float* weight, uint32_t width, uint32_t rows, float eps, float* out,
                        void* stream);

@@ -8,6 +8,8 @@
 
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "../../include/qwenscriber_cuda.h"
 #include "qwc_device.cuh"
 #include "qwc_internal.h"
@@ -275,6 +277,42 @@ int32_t status_of(cudaError_t e) {
 
 bool quant_format_ok(uint32_t format) { return format == kFormatQ4 || format == kFormatQ8; }
 
+// ---- argmax over a fixed, statically allocated device scratch ----
+//
+// qwc_op_argmax_noalloc runs the same two passes as qwc_op_argmax, but its
+// block partials live in this file-scope array instead of a per-call
+// workspace. Pass 1 writes every partial that pass 2 reads, so nothing in
+// it has to start at zero. There is one array per device: two calls in
+// flight on one device at the same time (different streams or host
+// threads) share it and race.
+constexpr uint32_t kNoallocPartials = 512;   // capacity: 512 partials, 4 KiB
+constexpr uint32_t kNoallocPerBlock = 8192;  // most values one pass-1 block reduces
+static_assert(uint64_t(kNoallocPartials) * kNoallocPerBlock == QWC_ARGMAX_NOALLOC_MAX_COUNT,
+              "the header's count limit is the scratch capacity times the values per block");
+static __device__ __align__(256) ArgmaxPartial g_argmax_scratch[kNoallocPartials];
+
+constexpr int kNoallocDevices = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_scratch[kNoallocDevices] = {};
+
+// The device address of g_argmax_scratch on the current device, looked up
+// once per device (the first call on that device does the lookup).
+int32_t noalloc_scratch(ArgmaxPartial** out) {
+  int device = -1;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return status_of(e);
+  if (device < 0 || device >= kNoallocDevices) return QWC_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_scratch[device]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_argmax_scratch);
+    if (e != cudaSuccess) return status_of(e);
+    g_noalloc_scratch[device] = p;
+  }
+  *out = static_cast<ArgmaxPartial*>(g_noalloc_scratch[device]);
+  return QWC_OK;
+}
+
 }  // namespace
 }  // namespace qwc
 
@@ -365,6 +403,20 @@ int32_t qwc_op_silu_mul(const float* gate, const float* up, uint32_t n, float* o
   if (n == 0) return QWC_OK;
   silu_mul_kernel<<<(n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       gate, up, n, out);
+  return status_of(cudaGetLastError());
+}
+
+int32_t qwc_op_argmax_noalloc(const float* values, uint32_t count, uint32_t* out_index, void* stream) {
+  if (!values || !out_index || count == 0) return QWC_INVALID_ARGUMENT;
+  if (count > QWC_ARGMAX_NOALLOC_MAX_COUNT) return QWC_LIMIT_EXCEEDED;
+  ArgmaxPartial* scratch = nullptr;
+  const int32_t st = noalloc_scratch(&scratch);
+  if (st != QWC_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint32_t blocks = (count + 255u) / 256u;
+  if (blocks > kNoallocPartials) blocks = kNoallocPartials;
+  argmax_partial_kernel<<<blocks, 256, 0, s>>>(values, count, scratch);
+  argmax_final_kernel<<<1, 32, 0, s>>>(scratch, blocks, out_index);
   return status_of(cudaGetLastError());
 }
 

@@ -30,6 +30,8 @@ STATUS = {
 CACHE_F32, CACHE_Q8 = 0, 1
 OPTION_IGNORE_EOS, OPTION_KEEP_LOGITS, OPTION_STEP_CHUNK, OPTION_TRACE = 1, 2, 3, 4
 FEATURE_MODEL, FEATURE_DECODE, FEATURE_STREAMS = 1 << 3, 1 << 4, 1 << 8
+LIMIT_EXCEEDED = -9
+ARGMAX_NOALLOC_MAX_COUNT = 4194304  # QWC_ARGMAX_NOALLOC_MAX_COUNT
 
 # Every symbol include/qwenscriber_cuda.h declares: (restype, argtypes).
 SIGNATURES = {
@@ -70,6 +72,7 @@ SIGNATURES = {
         [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_uint32, c_uint32, c_uint32, c_uint32, c_void_p, c_void_p],
     ),
     "qwc_op_argmax": (c_int32, [c_void_p, c_uint32, c_void_p, c_void_p]),
+    "qwc_op_argmax_noalloc": (c_int32, [c_void_p, c_uint32, c_void_p, c_void_p]),
     "qwc_op_rmsnorm": (c_int32, [c_void_p, c_void_p, c_uint32, c_uint32, c_float, c_void_p, c_void_p]),
     "qwc_op_rope": (c_int32, [c_void_p, c_uint32, c_uint32, c_void_p, c_void_p, c_uint32, c_void_p]),
     "qwc_op_silu_mul": (c_int32, [c_void_p, c_void_p, c_uint32, c_void_p, c_void_p]),
