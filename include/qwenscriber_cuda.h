@@ -239,6 +239,14 @@ int32_t qwc_op_argmax(const float* values, uint32_t count, uint32_t* out_index, 
  * stream are ordered. */
 #define QWC_ARGMAX_NOALLOC_MAX_COUNT 4194304u
 int32_t qwc_op_argmax_noalloc(const float* values, uint32_t count, uint32_t* out_index, void* stream);
+/* kernels.linearQuantized (src/core/qwen3_asr/kernels.zig:118-158) for up to
+ * 64 independent streams at once on the tensor cores: out[s][r] = sum_k
+ * W[r][k] * x[s][k], x as [streams][cols] f32, out as [streams][rows] f32.
+ * Weights are dequantized to f16 and activations rounded to f16 (one
+ * rounding each), products accumulate in f32. cols must be a multiple of
+ * 512. Uses a device workspace the library allocates per call. */
+int32_t qwc_op_gemm_streams(uint32_t format, const void* scales, const void* codes, uint32_t rows, uint32_t cols,
+                            const float* x, uint32_t streams, float* out, void* stream);
 /* math.rmsNormInPlace per row (src/core/math.zig:120-130), out of place. */
 int32_t qwc_op_rmsnorm(const float* x, const float* weight, uint32_t width, uint32_t rows, float eps, float* out,
                        void* stream);

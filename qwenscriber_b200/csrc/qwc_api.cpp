@@ -327,20 +327,38 @@ EncodeTiledFn encode_tiled() {
   return fn;
 }
 
+}  // namespace
+
+int32_t encode_tensor_map(uint8_t* out128, int type, uint32_t rank, void* base, const uint64_t* dims,
+                               const uint64_t* strides, const uint32_t* box, bool swizzle128) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn || rank < 1 || rank > 5) return QWC_INVALID_STATE;
+  cuuint64_t d[5], st[4];
+  cuuint32_t b[5], el[5];
+  for (uint32_t i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    el[i] = 1;
+    if (i + 1 < rank) st[i] = strides[i];
+  }
+  const CUresult r =
+      fn(reinterpret_cast<CUtensorMap*>(out128), type == kMapF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8,
+         rank, base, d, st, b, el, CU_TENSOR_MAP_INTERLEAVE_NONE,
+         swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? QWC_OK : QWC_INVALID_STATE;
+}
+
+namespace {
+
 // One q8 cache plane of stream 0 as a 3-D u8 tensor [layer][position][row
 // bytes], boxes of `box_x` bytes x kAttnChunk positions x 1 layer.
 int32_t encode_plane(uint8_t* out, uint8_t* base, uint64_t row_bytes, uint64_t positions, uint64_t layers,
                      uint64_t layer_stride, uint32_t box_x) {
-  EncodeTiledFn fn = encode_tiled();
-  if (!fn) return QWC_INVALID_STATE;
-  const cuuint64_t dims[3] = {row_bytes, positions, layers};
-  const cuuint64_t strides[2] = {row_bytes, layer_stride};
-  const cuuint32_t box[3] = {box_x, kAttnChunk, 1};
-  const cuuint32_t elem[3] = {1, 1, 1};
-  const CUresult r = fn(reinterpret_cast<CUtensorMap*>(out), CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base, dims, strides, box,
-                        elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? QWC_OK : QWC_INVALID_STATE;
+  const uint64_t dims[3] = {row_bytes, positions, layers};
+  const uint64_t strides[2] = {row_bytes, layer_stride};
+  const uint32_t box[3] = {box_x, kAttnChunk, 1};
+  return encode_tensor_map(out, kMapU8, 3, base, dims, strides, box, false);
 }
 
 int32_t finish_model(Handle* h, const Config& c) {

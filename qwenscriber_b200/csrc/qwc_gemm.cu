@@ -1,0 +1,491 @@
+// qwc_gemm.cu -- quantized-weight GEMM for independent decode streams on the
+// 5th-generation tensor cores (tcgen05, sm_100a).
+//
+// out[s][r] = sum_k W[r][k] * x[s][k] for up to 64 streams s at once: the
+// projections of kernels.linearQuantized (src/core/qwen3_asr/kernels.zig:118-158)
+// for a batch of streams. W stays in the reference's two-plane q4/q8 layout
+// (src/core/quant.zig:144-176). Per CTA: one tile of 128 weight rows and a
+// range of K, in blocks of 128:
+//
+//   warp 0   TMA producer: raw code and scale boxes of the tile, and the
+//            activation box, into a 4-stage ring (mbarrier complete_tx);
+//   warp 1   TMEM owner and MMA issuer: tcgen05.mma kind::f16, M=128, N=64,
+//            K=16, accumulating in TMEM; tcgen05.commit frees ring stages;
+//   warps 2-5 dequantize each raw block into f16 (code - bias) * scale, one
+//            row per thread, into a 2-stage operand buffer in the canonical
+//            K-major no-swizzle layout; then read the accumulator back
+//            (tcgen05.ld) and store f32 results.
+//
+// The f16 operands round each dequantized weight and each activation once
+// (11-bit significands); products accumulate in f32.
+//
+// Activations arrive by TMA in 128-byte-swizzled rows (two boxes of 64 K per
+// block); the dequantized weights are written by the threads in the
+// no-swizzle core-matrix layout.
+//
+// K order inside every 8-value chunk is permuted the same way for weights
+// and activations, [0 4 1 5 2 6 3 7], so one lop3 extracts two values of a
+// 32-bit q4 code word at once. The sum over K does not depend on the order.
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+
+#include "../../include/qwenscriber_cuda.h"
+#include "qwc_device.cuh"
+#include "qwc_internal.h"
+
+namespace qwc {
+namespace {
+
+constexpr int kGemmThreads = 192;
+constexpr int kRawStages = 4;
+constexpr int kAStages = 2;
+constexpr uint32_t kTileM = 128;
+constexpr uint32_t kTileN = 64;
+constexpr uint32_t kKBlock = 128;
+constexpr uint32_t kAStageBytes = kTileM * kKBlock * 2;  // 32 KB of f16
+constexpr uint32_t kBStageBytes = kTileN * kKBlock * 2;  // 16 KB of f16
+constexpr uint32_t kCodeStageBytes = kTileM * kKBlock;   // q8: 128 B per row; q4 uses half
+constexpr uint32_t kScaleStageBytes = kTileM * 16;       // one 16-byte box column of scales
+constexpr uint32_t kTmemCols = 64;
+
+struct __align__(1024) GemmSmem {
+  uint8_t a16[kAStages][kAStageBytes];
+  uint8_t b[kRawStages][kBStageBytes];
+  uint8_t codes[kRawStages][kCodeStageBytes];
+  uint8_t scales[kRawStages][kScaleStageBytes];
+  uint64_t raw_full[kRawStages];
+  uint64_t raw_empty[kRawStages];
+  uint64_t a_full[kAStages];
+  uint64_t a_empty[kAStages];
+  uint64_t acc_full;
+  uint32_t tmem_base;
+};
+static_assert(offsetof(GemmSmem, b) % 1024 == 0 && offsetof(GemmSmem, codes) % 128 == 0 &&
+                  offsetof(GemmSmem, scales) % 128 == 0,
+              "TMA destinations need 128-byte alignment");
+
+// ---- tcgen05 wrappers ----
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst_smem)),
+               "r"(cols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor, K-major. No swizzle: core matrices of
+// 8 rows x 16 bytes stored contiguously, `lbo` = byte distance between the
+// two 8-element K halves of an MMA, `sbo` = byte distance between 8-row
+// groups. 128-byte swizzle: rows of 128 bytes, `sbo` = 1024 (8 rows), the
+// atom 1024-byte aligned; K steps inside the atom advance the start address.
+constexpr uint32_t kLayoutNone = 0, kLayoutSw128 = 2;
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+  uint64_t d = static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;  // descriptor version for sm_100
+  d |= static_cast<uint64_t>(layout & 7u) << 61;
+  return d;  // base offset 0, absolute leading-offset mode
+}
+
+// Instruction descriptor: f16 x f16 -> f32, both K-major, M = 128, N = 64.
+constexpr uint32_t kIdesc = (1u << 4) | ((kTileN >> 3) << 17) | ((kTileM >> 4) << 24);
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* map, int32_t x, int32_t y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_addr(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// 32 lanes x 64 columns of f32 from TMEM (lane quarter of this warp).
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
+  uint32_t r[64];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+      "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]),
+        "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]),
+        "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]),
+        "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]),
+        "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// ---- dequantization to f16 pairs ----
+
+__device__ __forceinline__ uint32_t hsub2_bits(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t lop_and_or(uint32_t w, uint32_t mask, uint32_t magic) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(w), "r"(mask), "r"(magic));
+  return r;
+}
+
+// Eight q4 codes (one 32-bit word, K order 0..7) -> 16 bytes of f16 in the
+// chunk order [0 4 1 5 2 6 3 7]: (code - 8) * scale, rounded once.
+__device__ __forceinline__ uint4 dequant_q4_word(uint32_t w, uint32_t scale2) {
+  const uint32_t magic = 0x64006400u;  // f16 1024 in both halves
+  const uint32_t bias = 0x64086408u;   // f16 1032 = 1024 + 8
+  const uint32_t mask = 0x000F000Fu;
+  uint4 o;
+  o.x = hmul2_bits(hsub2_bits(lop_and_or(w, mask, magic), bias), scale2);
+  o.y = hmul2_bits(hsub2_bits(lop_and_or(w >> 4, mask, magic), bias), scale2);
+  o.z = hmul2_bits(hsub2_bits(lop_and_or(w >> 8, mask, magic), bias), scale2);
+  o.w = hmul2_bits(hsub2_bits(lop_and_or(w >> 12, mask, magic), bias), scale2);
+  return o;
+}
+
+// Eight q8 codes (two words, K order 0..7) -> the same chunk order.
+__device__ __forceinline__ uint4 dequant_q8_words(uint32_t w0, uint32_t w1, uint32_t scale2) {
+  const uint32_t magic = 0x64006400u;
+  const uint32_t bias = 0x64806480u;  // f16 1152 = 1024 + 128
+  const uint32_t mask = 0x00FF00FFu;
+  uint4 o;
+  o.x = hmul2_bits(hsub2_bits(lop_and_or(__byte_perm(w0, w1, 0x0400), mask, magic), bias), scale2);
+  o.y = hmul2_bits(hsub2_bits(lop_and_or(__byte_perm(w0, w1, 0x0501), mask, magic), bias), scale2);
+  o.z = hmul2_bits(hsub2_bits(lop_and_or(__byte_perm(w0, w1, 0x0602), mask, magic), bias), scale2);
+  o.w = hmul2_bits(hsub2_bits(lop_and_or(__byte_perm(w0, w1, 0x0703), mask, magic), bias), scale2);
+  return o;
+}
+
+struct GemmParams {
+  uint32_t rows;        // M
+  uint32_t cols;        // K (multiple of kKBlock)
+  uint32_t streams;     // N actually used (<= kTileN)
+  uint32_t format;      // q4 / q8
+  uint32_t kb_per_split;
+  float* out;           // [split][streams][rows]
+  int32_t* error;
+  uint64_t timeout_ns;
+};
+
+enum GemmError : int32_t { kGemmErrWait = 1 };
+
+__device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity, const GemmParams& p) {
+  return mbar_wait_bounded(bar, parity, p.error, global_timer_ns() + p.timeout_ns, kGemmErrWait);
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_streams_kernel(const __grid_constant__ CUtensorMap map_codes, const __grid_constant__ CUtensorMap map_scales,
+                        const __grid_constant__ CUtensorMap map_b, const GemmParams p) {
+  extern __shared__ __align__(1024) uint8_t gemm_smem_raw[];
+  // The swizzle atoms need 1024-byte alignment in the shared window.
+  const uint32_t pad = (1024u - (smem_addr(gemm_smem_raw) & 1023u)) & 1023u;
+  GemmSmem* s = reinterpret_cast<GemmSmem*>(gemm_smem_raw + pad);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t m0 = blockIdx.x * kTileM;
+  const uint32_t kblocks = p.cols / kKBlock;
+  const uint32_t kb0 = blockIdx.y * p.kb_per_split;
+  const uint32_t kb1 = min(kblocks, kb0 + p.kb_per_split);
+  const uint32_t nkb = kb1 > kb0 ? kb1 - kb0 : 0;
+  const bool q4 = p.format == kFormatQ4;
+  const uint32_t code_box = q4 ? kKBlock / 2 : kKBlock;  // bytes of codes per row per block
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kRawStages; ++i) {
+      mbar_init(&s->raw_full[i], 1);
+      mbar_init(&s->raw_empty[i], 1);
+    }
+    for (int i = 0; i < kAStages; ++i) {
+      mbar_init(&s->a_full[i], 4);
+      mbar_init(&s->a_empty[i], 1);
+    }
+    mbar_init(&s->acc_full, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(&s->tmem_base, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s->tmem_base;
+  bool ok = true;
+
+  if (warp == 0) {
+    // ---- producer ----
+    if (lane == 0) {
+      for (uint32_t i = 0; i < nkb && ok; ++i) {
+        const uint32_t st = i % kRawStages;
+        if (i >= kRawStages && !wait_bounded(&s->raw_empty[st], ((i / kRawStages) - 1) & 1u, p)) {
+          ok = false;
+          break;
+        }
+        const uint32_t kb = kb0 + i;
+        mbar_arrive_expect_tx(&s->raw_full[st], kTileM * code_box + kScaleStageBytes + kBStageBytes);
+        tma_load_2d(s->codes[st], &map_codes, static_cast<int32_t>(kb * code_box), static_cast<int32_t>(m0),
+                    &s->raw_full[st]);
+        // The 16-byte scale box holding this block's two groups.
+        tma_load_2d(s->scales[st], &map_scales, static_cast<int32_t>((kb * 4u) & ~15u), static_cast<int32_t>(m0),
+                    &s->raw_full[st]);
+        tma_load_2d(s->b[st], &map_b, static_cast<int32_t>(kb * kKBlock), 0, &s->raw_full[st]);
+        tma_load_2d(s->b[st] + kBStageBytes / 2, &map_b, static_cast<int32_t>(kb * kKBlock + 64), 0,
+                    &s->raw_full[st]);
+      }
+      // Drain: every armed stage must have landed before the CTA exits.
+      for (uint32_t i = (nkb > kRawStages ? nkb - kRawStages : 0); i < nkb; ++i) {
+        const uint32_t st = i % kRawStages;
+        wait_bounded(&s->raw_full[st], (i / kRawStages) & 1u, p);
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      for (uint32_t i = 0; i < nkb && ok; ++i) {
+        const uint32_t st = i % kRawStages;
+        const uint32_t at = i % kAStages;
+        if (!wait_bounded(&s->raw_full[st], (i / kRawStages) & 1u, p) ||
+            !wait_bounded(&s->a_full[at], (i / kAStages) & 1u, p)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_base = smem_addr(s->a16[at]);
+        const uint32_t b_base = smem_addr(s->b[st]);
+#pragma unroll
+        for (uint32_t k = 0; k < kKBlock / 16; ++k) {
+          // A: two 8-element K chunks per MMA, 2048 B apart (128 rows x 16 B).
+          // B: 64-element swizzle atoms of 64 rows x 128 B; 32 B per K step.
+          const uint64_t ad = umma_desc(a_base + k * 2 * 2048, 2048, 128, kLayoutNone);
+          const uint64_t bd = umma_desc(b_base + (k / 4) * (kBStageBytes / 2) + (k % 4) * 32, 16, 1024, kLayoutSw128);
+          umma_f16(tmem, ad, bd, (i > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(&s->a_empty[at]);
+        umma_commit(&s->raw_empty[st]);
+      }
+      umma_commit(&s->acc_full);
+      // MMAs still in flight must finish before TMEM is released.
+      if (!ok) wait_bounded(&s->acc_full, 0, p);
+    }
+  } else {
+    // ---- dequantize, then epilogue ----
+    const uint32_t r = (warp - 2) * 32 + lane;  // row of the tile this thread dequantizes
+    for (uint32_t i = 0; i < nkb && ok; ++i) {
+      const uint32_t st = i % kRawStages;
+      const uint32_t at = i % kAStages;
+      if (!wait_bounded(&s->raw_full[st], (i / kRawStages) & 1u, p)) {
+        ok = false;
+        break;
+      }
+      if (i >= kAStages && !wait_bounded(&s->a_empty[at], ((i / kAStages) - 1) & 1u, p)) {
+        ok = false;
+        break;
+      }
+      const uint32_t kb = kb0 + i;
+      const uint8_t* srow = s->scales[st] + r * 16 + ((kb * 4u) & 15u);
+      const uint16_t sb0 = *reinterpret_cast<const uint16_t*>(srow);
+      const uint16_t sb1 = *reinterpret_cast<const uint16_t*>(srow + 2);
+      const uint32_t sc0 = static_cast<uint32_t>(sb0) * 0x10001u;
+      const uint32_t sc1 = static_cast<uint32_t>(sb1) * 0x10001u;
+      uint8_t* a = s->a16[at] + r * 16;
+      if (q4) {
+        const uint4* src = reinterpret_cast<const uint4*>(s->codes[st] + r * (kKBlock / 2));
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 w = src[q];
+          const uint32_t sc = q < 2 ? sc0 : sc1;  // chunks 0-7: group 0, 8-15: group 1
+          *reinterpret_cast<uint4*>(a + (4 * q + 0) * 2048) = dequant_q4_word(w.x, sc);
+          *reinterpret_cast<uint4*>(a + (4 * q + 1) * 2048) = dequant_q4_word(w.y, sc);
+          *reinterpret_cast<uint4*>(a + (4 * q + 2) * 2048) = dequant_q4_word(w.z, sc);
+          *reinterpret_cast<uint4*>(a + (4 * q + 3) * 2048) = dequant_q4_word(w.w, sc);
+        }
+      } else {
+        const uint4* src = reinterpret_cast<const uint4*>(s->codes[st] + r * kKBlock);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const uint4 w = src[q];
+          const uint32_t sc = q < 4 ? sc0 : sc1;
+          *reinterpret_cast<uint4*>(a + (2 * q + 0) * 2048) = dequant_q8_words(w.x, w.y, sc);
+          *reinterpret_cast<uint4*>(a + (2 * q + 1) * 2048) = dequant_q8_words(w.z, w.w, sc);
+        }
+      }
+      // Generic-proxy stores, read next by the tensor core (async proxy).
+      fence_proxy_async_shared();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s->a_full[at]);
+    }
+    // Epilogue: TMEM lane = tile row; this warp may read lanes 32 * (warp % 4) + [0, 32).
+    bool go = ok && nkb > 0 && wait_bounded(&s->acc_full, 0, p);
+    go = __all_sync(0xffffffffu, go);  // tcgen05.ld is warp-collective
+    if (go) {
+      tc_fence_after();
+      const uint32_t quarter = static_cast<uint32_t>(warp % 4);
+      float v[64];
+      tmem_ld64(tmem + ((quarter * 32u) << 16), v);
+      const uint32_t row = m0 + quarter * 32 + lane;
+      if (row < p.rows) {
+        float* out = p.out + size_t(blockIdx.y) * p.streams * p.rows + row;
+#pragma unroll
+        for (int n = 0; n < 64; ++n) {
+          if (n < static_cast<int>(p.streams)) out[size_t(n) * p.rows] = v[n];
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// x[s][k] f32 -> f16 activations in the permuted chunk order, rows padded to
+// `ld` (elements).
+__global__ void pack_activations_kernel(const float* x, uint32_t streams, uint32_t cols, __half* out) {
+  const uint32_t chunks = cols / 8;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < streams * chunks; i += gridDim.x * blockDim.x) {
+    const uint32_t sidx = i / chunks, c = i % chunks;
+    const float* src = x + size_t(sidx) * cols + c * 8;
+    const int perm[8] = {0, 4, 1, 5, 2, 6, 3, 7};
+    __align__(16) __half h[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) h[j] = __float2half_rn(src[perm[j]]);
+    *reinterpret_cast<uint4*>(out + size_t(sidx) * cols + c * 8) = *reinterpret_cast<const uint4*>(h);
+  }
+}
+
+__global__ void sum_splits_kernel(const float* parts, uint32_t splits, uint32_t n, float* out) {
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    float acc = parts[i];
+    for (uint32_t sp = 1; sp < splits; ++sp) acc += parts[size_t(sp) * n + i];
+    out[i] = acc;
+  }
+}
+
+}  // namespace
+
+int gemm_smem_bytes() { return static_cast<int>(sizeof(GemmSmem)) + 1024; }
+
+}  // namespace qwc
+
+using namespace qwc;
+
+namespace {
+
+int32_t gemm_status(cudaError_t e) {
+  if (e == cudaSuccess) return QWC_OK;
+  cudaGetLastError();
+  return e == cudaErrorMemoryAllocation ? QWC_OUT_OF_MEMORY : QWC_INVALID_STATE;
+}
+
+}  // namespace
+
+extern "C" int32_t qwc_op_gemm_streams(uint32_t format, const void* scales, const void* codes, uint32_t rows,
+                                       uint32_t cols, const float* x, uint32_t streams, float* out, void* stream) {
+  if (!scales || !codes || !x || !out || rows == 0) return QWC_INVALID_ARGUMENT;
+  if (format != kFormatQ4 && format != kFormatQ8) return QWC_UNSUPPORTED;
+  if (cols == 0 || cols % kKBlock != 0 || streams == 0 || streams > kTileN) return QWC_INVALID_ARGUMENT;
+  if (reinterpret_cast<uintptr_t>(scales) % 16 != 0 || reinterpret_cast<uintptr_t>(codes) % 16 != 0) {
+    return QWC_INVALID_ARGUMENT;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const uint32_t groups = cols / kGroup;
+  const uint32_t scale_row = groups * 2;
+  const uint32_t code_row = groups * data_bytes_per_group(format);
+  if (scale_row % 16 != 0) return QWC_UNSUPPORTED;
+  const uint32_t kblocks = cols / kKBlock;
+  const uint32_t mtiles = (rows + kTileM - 1) / kTileM;
+  int sms = 148;
+  int device = 0;
+  cudaGetDevice(&device);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  uint32_t splits = 1;
+  while (mtiles * (splits + 1) <= static_cast<uint32_t>(sms) && splits < kblocks) ++splits;
+  const uint32_t kps = (kblocks + splits - 1) / splits;
+  splits = (kblocks + kps - 1) / kps;
+
+  // Workspace: error word, packed activations, split partials.
+  const size_t xb_bytes = (size_t(streams) * cols * 2 + 255) / 256 * 256;
+  const size_t part_bytes = size_t(splits) * streams * rows * 4;
+  void* ws = nullptr;
+  cudaError_t e = cudaMallocAsync(&ws, 256 + xb_bytes + part_bytes, st);
+  if (e != cudaSuccess) return gemm_status(e);
+  int32_t* err = static_cast<int32_t*>(ws);
+  __half* xb = reinterpret_cast<__half*>(static_cast<uint8_t*>(ws) + 256);
+  float* parts = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + 256 + xb_bytes);
+  cudaMemsetAsync(err, 0, 4, st);
+  pack_activations_kernel<<<256, 256, 0, st>>>(x, streams, cols, xb);
+
+  alignas(64) uint8_t maps[3][128];
+  int32_t rc = QWC_OK;
+  {
+    const uint64_t dims_c[2] = {code_row, rows};
+    const uint64_t str_c[1] = {code_row};
+    const uint32_t box_c[2] = {format == kFormatQ4 ? kKBlock / 2 : kKBlock, kTileM};
+    const uint64_t dims_s[2] = {scale_row, rows};
+    const uint64_t str_s[1] = {scale_row};
+    const uint32_t box_s[2] = {16, kTileM};
+    const uint64_t dims_b[2] = {cols, streams};
+    const uint64_t str_b[1] = {uint64_t(cols) * 2};
+    const uint32_t box_b[2] = {64, kTileN};
+    rc = encode_tensor_map(maps[0], kMapU8, 2, const_cast<void*>(codes), dims_c, str_c, box_c, false);
+    if (rc == QWC_OK) rc = encode_tensor_map(maps[1], kMapU8, 2, const_cast<void*>(scales), dims_s, str_s, box_s, false);
+    if (rc == QWC_OK) rc = encode_tensor_map(maps[2], kMapF16, 2, xb, dims_b, str_b, box_b, true);
+  }
+  if (rc != QWC_OK) {
+    cudaFreeAsync(ws, st);
+    return rc;
+  }
+  GemmParams gp{rows, cols, streams, format, kps, parts, err, 2000000000ull};
+  const int smem = gemm_smem_bytes();
+  cudaFuncSetAttribute(gemm_streams_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  gemm_streams_kernel<<<dim3(mtiles, splits), kGemmThreads, smem, st>>>(
+      *reinterpret_cast<const CUtensorMap*>(maps[0]), *reinterpret_cast<const CUtensorMap*>(maps[1]),
+      *reinterpret_cast<const CUtensorMap*>(maps[2]), gp);
+  e = cudaGetLastError();
+  if (e == cudaSuccess) {
+    sum_splits_kernel<<<256, 256, 0, st>>>(parts, splits, streams * rows, out);
+    e = cudaGetLastError();
+  }
+  int32_t herr = 0;
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&herr, err, 4, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  cudaFreeAsync(ws, st);
+  if (e != cudaSuccess) return gemm_status(e);
+  return herr != 0 ? QWC_INVALID_STATE : QWC_OK;
+}

@@ -130,4 +130,12 @@ int decode_kernel_smem_bytes();
 // Returns cudaError_t as int.
 int launch_decode(const DecodeLaunch& launch, const KvMaps& maps, int grid, void* stream);
 int decode_grid_size(int device);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point. `strides`
+// holds rank - 1 byte strides (dimension 1 up); `swizzle128` selects the
+// 128-byte swizzle. Returns a QWC_* status.
+enum MapType : int { kMapU8 = 0, kMapF16 = 1 };
+int32_t encode_tensor_map(uint8_t* out128, int type, uint32_t rank, void* base, const uint64_t* dims,
+                          const uint64_t* strides, const uint32_t* box, bool swizzle128);
+int gemm_smem_bytes();
 }  // namespace qwc

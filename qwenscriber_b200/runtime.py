@@ -73,6 +73,8 @@ SIGNATURES = {
     ),
     "qwc_op_argmax": (c_int32, [c_void_p, c_uint32, c_void_p, c_void_p]),
     "qwc_op_argmax_noalloc": (c_int32, [c_void_p, c_uint32, c_void_p, c_void_p]),
+    "qwc_op_gemm_streams": (c_int32, [c_uint32, c_void_p, c_void_p, c_uint32, c_uint32, c_void_p, c_uint32,
+                                      c_void_p, c_void_p]),
     "qwc_op_rmsnorm": (c_int32, [c_void_p, c_void_p, c_uint32, c_uint32, c_float, c_void_p, c_void_p]),
     "qwc_op_rope": (c_int32, [c_void_p, c_uint32, c_uint32, c_void_p, c_void_p, c_uint32, c_void_p]),
     "qwc_op_silu_mul": (c_int32, [c_void_p, c_void_p, c_uint32, c_void_p, c_void_p]),

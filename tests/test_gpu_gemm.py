@@ -1,0 +1,72 @@
+"""The tensor-core stream GEMM (qwc_op_gemm_streams) against exact references.
+
+Weights are dequantized to f16 and activations rounded to f16 inside the
+kernel (one rounding each, as documented in the header), so the first check
+is against the f64 product of exactly those f16 operands, where only the f32
+accumulation order differs (relative 1e-5 of sum |w x|). The second check
+bounds the distance to the reference's f32 linearQuantized
+(kernels.zig:118-158, the oracle) by the two roundings.
+"""
+
+import numpy as np
+import pytest
+
+import oracle as O
+from qwenscriber_b200 import quant
+from qwenscriber_b200 import runtime as rt
+
+pytestmark = pytest.mark.gpu
+
+
+def _planes(rng, fmt, rows, cols):
+    groups = cols // 64
+    scales = (np.abs(rng.standard_normal((rows, groups))) * 0.003 + 1e-4).astype(np.float16)
+    scales[0, 0] = np.float16(0.0)
+    codes = rng.integers(0, 256, size=(rows, groups * quant.DATA_BYTES[fmt]), dtype=np.uint8)
+    return scales, codes
+
+
+def _f16_weights(fmt, scales, codes):
+    rows = codes.shape[0]
+    if fmt == quant.Q4:
+        lo = (codes & 0x0F).astype(np.int32)
+        hi = (codes >> 4).astype(np.int32)
+        q = np.empty((rows, codes.shape[1] * 2), np.int32)
+        q[:, 0::2], q[:, 1::2] = lo, hi
+        q -= 8
+    else:
+        q = codes.astype(np.int32) - 128
+    s = np.repeat(scales.astype(np.float32), 64, axis=1)
+    return (q.astype(np.float32) * s).astype(np.float16)
+
+
+@pytest.mark.parametrize("fmt,rows,cols,streams", [
+    (quant.Q4, 256, 1024, 64), (quant.Q4, 300, 2048, 7), (quant.Q8, 384, 2048, 64),
+    (quant.Q4, 128, 6144, 64), (quant.Q8, 200, 1024, 33)])
+def test_gemm_streams(gpu, cuda_lib, oracle_lib, fmt, rows, cols, streams):
+    import torch
+
+    rng = np.random.default_rng(rows * 7 + cols + streams)
+    scales, codes = _planes(rng, fmt, rows, cols)
+    x = rng.standard_normal((streams, cols)).astype(np.float32)
+    ds = torch.from_numpy(scales.view(np.uint16).copy()).cuda()
+    dc = torch.from_numpy(codes).cuda()
+    dx = torch.from_numpy(x).cuda()
+    out = torch.zeros((streams, rows), dtype=torch.float32, device=gpu)
+    st = cuda_lib.qwc_op_gemm_streams(fmt, ds.data_ptr(), dc.data_ptr(), rows, cols, dx.data_ptr(), streams,
+                                      out.data_ptr(), None)
+    torch.cuda.synchronize()
+    assert st == 0, rt.STATUS.get(st, st)
+    got = out.cpu().numpy()
+
+    w16 = _f16_weights(fmt, scales, codes).astype(np.float64)
+    x16 = x.astype(np.float16).astype(np.float64)
+    exact16 = x16 @ w16.T
+    mag16 = np.abs(x16) @ np.abs(w16).T
+    err = np.abs(got - exact16)
+    assert np.all(err <= 1e-5 * mag16 + 1e-30), float(np.max(err / (mag16 + 1e-30)))
+
+    # Against the reference's f32 path: within the two f16 roundings.
+    ref = O.linear_quantized(fmt, scales.view(np.uint8), codes, x)
+    mag = np.abs(x) @ np.abs(_f16_weights(fmt, scales, codes).astype(np.float32)).T
+    assert np.all(np.abs(got - ref) <= 1.2e-3 * mag + 1e-6)
