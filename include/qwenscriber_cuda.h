@@ -163,7 +163,14 @@ int32_t qwc_decode_tokens(uint32_t handle, uint32_t* out, uint32_t capacity);
 /* qw_decode_end: back to loaded; the cache is cleared. */
 int32_t qwc_decode_end(uint32_t handle);
 
-/* ---- multi-stream family: independent streams batched per device step ---- */
+/* ---- multi-stream family: independent streams batched per device step ----
+ * With qwc_model_set_streams(n), 2 <= n <= 64, every step runs all slots
+ * together (projections on the tensor cores with the slots as GEMM columns,
+ * as in qwc_op_gemm_streams). A slot
+ * begun with qwc_stream_begin consumes its prompt one position per
+ * qwc_streams_step; results[slot] is then 2 until the prompt's last position,
+ * which yields the slot's first token (1). The stop rule is the reference's.
+ * The qwc_decode_* family is for single-stream handles. */
 
 int32_t qwc_stream_begin(uint32_t handle, uint32_t slot, const uint32_t* prompt, uint32_t prompt_len,
                          const float* audio, uint32_t audio_steps, uint32_t max_tokens);
@@ -173,6 +180,10 @@ int32_t qwc_stream_begin(uint32_t handle, uint32_t slot, const uint32_t* prompt,
 int32_t qwc_streams_step(uint32_t handle, uint32_t* tokens_out, int32_t* results);
 int32_t qwc_stream_tokens(uint32_t handle, uint32_t slot, uint32_t* out, uint32_t capacity);
 int32_t qwc_stream_end(uint32_t handle, uint32_t slot);
+/* Measurement: `steps` greedy steps of every decoding slot of a batched
+ * handle (all past their prompts), chained on the device without host
+ * round trips or end-of-sequence handling; device time in milliseconds. */
+int32_t qwc_streams_run_timed(uint32_t handle, uint32_t steps, float* device_ms);
 
 /* ---- measurement and parity (not part of the reference ABI) ---- */
 
@@ -242,9 +253,10 @@ int32_t qwc_op_argmax_noalloc(const float* values, uint32_t count, uint32_t* out
 /* kernels.linearQuantized (src/core/qwen3_asr/kernels.zig:118-158) for up to
  * 64 independent streams at once on the tensor cores: out[s][r] = sum_k
  * W[r][k] * x[s][k], x as [streams][cols] f32, out as [streams][rows] f32.
- * Weights are dequantized to f16 and activations rounded to f16 (one
- * rounding each), products accumulate in f32. cols must be a multiple of
- * 512. Uses a device workspace the library allocates per call. */
+ * Each dequantized weight enters as an exact pair of f16 values (hi + lo)
+ * and each activation as f16 hi + lo (22 significant bits); products
+ * accumulate in f32. cols must be a multiple of 512. Uses a device workspace
+ * the library allocates per call. */
 int32_t qwc_op_gemm_streams(uint32_t format, const void* scales, const void* codes, uint32_t rows, uint32_t cols,
                             const float* x, uint32_t streams, float* out, void* stream);
 /* math.rmsNormInPlace per row (src/core/math.zig:120-130), out of place. */

@@ -211,6 +211,47 @@ struct StreamSlot {
   uint32_t max_tokens = 0;
   std::vector<uint32_t> generated;
   std::deque<uint32_t> ahead;    // predictions computed beyond next_token
+  // Batched mode: the prompt is consumed one position per step.
+  std::vector<uint32_t> prompt;
+  std::vector<int32_t> rows;     // audio row per prompt position, or -1
+  uint32_t prompt_pos = 0;
+  uint32_t last_token = 0;       // next input once the prompt is consumed
+  std::unique_ptr<DevBuf> audio;
+};
+
+// TMA descriptors of one weight matrix for the stream GEMM.
+struct MatMaps {
+  alignas(64) uint8_t codes[128];
+  alignas(64) uint8_t scales[128];
+};
+
+// Device state of the batched multi-stream step (streams > 1).
+struct Batched {
+  DevBuf hidden, xb_h, xb_q, xb_f, part0, qrot, attn_part, attn_count, logits, tokens, desc, audio_ptrs, err;
+  DevBuf history, counter;
+  std::vector<MatMaps> mq, mk, mv, mo, mg, mu, md;
+  MatMaps mlm;
+  alignas(64) uint8_t b_h[128];
+  alignas(64) uint8_t b_q[128];
+  alignas(64) uint8_t b_f[128];
+  KvMaps4 kv;
+  uint32_t splits_qkv = 1, splits_o = 1, splits_gu = 1, splits_down = 1;
+  uint32_t kernels_per_step = 0;
+  uint32_t history_rows = 0;
+  int attn_grid = 0;
+  StreamsStep P{};
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  SlotStep* host_desc = nullptr;    // pinned
+  uint32_t* host_tokens = nullptr;  // pinned
+  int32_t* host_err = nullptr;      // pinned
+  ~Batched() {
+    if (exec) cudaGraphExecDestroy(exec);
+    if (graph) cudaGraphDestroy(graph);
+    if (host_desc) cudaFreeHost(host_desc);
+    if (host_tokens) cudaFreeHost(host_tokens);
+    if (host_err) cudaFreeHost(host_err);
+  }
 };
 
 struct Handle {
@@ -234,6 +275,7 @@ struct Handle {
   uint32_t max_chunks = 0;
   uint64_t weight_bytes = 0;
   KvMaps kv_maps{};
+  std::unique_ptr<Batched> batched;  // streams > 1
   std::vector<StreamSlot> slots;
 
   ~Handle() {
@@ -275,6 +317,7 @@ void release_model(Handle* h) {
     b->alloc(0);
   }
   h->slots.clear();
+  h->batched.reset();
   h->weight_bytes = 0;
 }
 
@@ -360,6 +403,8 @@ int32_t encode_plane(uint8_t* out, uint8_t* base, uint64_t row_bytes, uint64_t p
   const uint32_t box[3] = {box_x, kAttnChunk, 1};
   return encode_tensor_map(out, kMapU8, 3, base, dims, strides, box, false);
 }
+
+int32_t build_batched(Handle* h);
 
 int32_t finish_model(Handle* h, const Config& c) {
   QWC_TRY(validate_config(c));
@@ -500,8 +545,10 @@ int32_t finish_model(Handle* h, const Config& c) {
 
   QWC_TRY(h->model_buf.alloc(sizeof(DevModel)));
   QWC_CUDA(cudaMemcpy(h->model_buf.ptr, &m, sizeof(DevModel), cudaMemcpyHostToDevice));
-  h->slots.assign(h->streams, StreamSlot{});
+  h->slots.clear();
+  h->slots.resize(h->streams);
   h->config = c;
+  if (h->streams > 1) QWC_TRY(build_batched(h));
   return QWC_OK;
 }
 
@@ -572,6 +619,316 @@ bool ends_sequence(const Config& c, uint32_t token) {
   return token == c.token_eos_primary || token == c.token_eos_secondary || token == c.token_endoftext;
 }
 
+// ---- batched multi-stream step ----
+
+int32_t mat_maps(const DevMat& m, MatMaps* out) {
+  return gemm_weight_maps(m.format, m.codes, m.scales, m.rows, m.cols, out->codes, out->scales);
+}
+
+int32_t act_map(uint8_t* out, void* base, uint32_t cols) { return gemm_act_map(base, cols, out); }
+
+int32_t kv_map4(uint8_t* out, uint8_t* base, uint64_t row, const DevModel& m, uint32_t streams, uint32_t box_x) {
+  const uint64_t dims[4] = {row, m.max_positions, m.n_layers, streams};
+  const uint64_t str[3] = {row, m.cache_layer_stride, m.cache_stream_stride};
+  const uint32_t box[4] = {box_x, kAttnChunk, 1, 1};
+  return encode_tensor_map(out, kMapU8, 4, base, dims, str, box, false);
+}
+
+// Enqueues one whole step on the handle's stream (recorded into the graph).
+int32_t record_step(Handle* h) {
+  Batched& b = *h->batched;
+  const DevModel& m = h->host_model;
+  const StreamsStep& P = b.P;
+  void* st = h->stream;
+  const uint32_t qw = m.q_heads * kHeadDim, kvw = m.kv_heads * kHeadDim;
+  uint32_t kernels = 0;
+  auto ok = [&](int e) -> int32_t {
+    ++kernels;
+    return e == 0 ? QWC_OK : status_of(static_cast<cudaError_t>(e));
+  };
+  auto gemm = [&](std::initializer_list<const MatMaps*> mats, std::initializer_list<const DevMat*> dms,
+                  const uint8_t* bmap, uint32_t cols, uint32_t splits, float* out, uint32_t ld) -> int32_t {
+    alignas(64) uint8_t cm[3][128];
+    alignas(64) uint8_t sm[3][128];
+    uint32_t rows[3], fmts[3], offs[3];
+    uint32_t n = 0, off = 0;
+    auto mi = mats.begin();
+    for (const DevMat* d : dms) {
+      std::memcpy(cm[n], (*mi)->codes, 128);
+      std::memcpy(sm[n], (*mi)->scales, 128);
+      rows[n] = d->rows;
+      fmts[n] = d->format;
+      offs[n] = off;
+      off += d->rows;
+      ++n;
+      ++mi;
+    }
+    return ok(launch_gemm_jobs(cm, sm, rows, fmts, offs, n, bmap, cols, kMaxStreams, splits, out, ld, P.error, st));
+  };
+  float* part = b.part0.as<float>();
+  QWC_TRY(ok(launch_streams_norm(P, 1, m.layers[0].attn_norm, nullptr, 0, st)));
+  for (uint32_t l = 0; l < m.n_layers; ++l) {
+    const DevLayer& L = m.layers[l];
+    if (l > 0) QWC_TRY(ok(launch_streams_norm(P, 0, L.attn_norm, part, b.splits_down, st)));
+    QWC_TRY(gemm({&b.mq[l], &b.mk[l], &b.mv[l]}, {&L.q, &L.k, &L.v}, b.b_h, m.hidden, b.splits_qkv, part,
+                 qw + 2 * kvw));
+    QWC_TRY(ok(launch_streams_qkv(P, l, b.splits_qkv, m.kv_heads, st)));
+    QWC_TRY(ok(launch_streams_attention(P, b.kv, l, b.attn_grid, st)));
+    QWC_TRY(gemm({&b.mo[l]}, {&L.o}, b.b_q, qw, b.splits_o, part, m.hidden));
+    QWC_TRY(ok(launch_streams_norm(P, 0, L.ffn_norm, part, b.splits_o, st)));
+    QWC_TRY(gemm({&b.mg[l], &b.mu[l]}, {&L.gate, &L.up}, b.b_h, m.hidden, b.splits_gu, part, 2 * m.ffn));
+    QWC_TRY(ok(launch_streams_swiglu(P, b.splits_gu, st)));
+    QWC_TRY(gemm({&b.md[l]}, {&L.down}, b.b_f, m.ffn, b.splits_down, part, m.hidden));
+  }
+  QWC_TRY(ok(launch_streams_norm(P, 0, m.final_norm, part, b.splits_down, st)));
+  QWC_TRY(gemm({&b.mlm}, {&m.lm_head}, b.b_h, m.hidden, 1, b.logits.as<float>(), m.vocab));
+  QWC_TRY(ok(launch_streams_argmax(P, st)));
+  QWC_TRY(ok(launch_streams_advance(P, b.history.as<uint32_t>(), b.counter.as<uint32_t>(), b.history_rows, st)));
+  b.kernels_per_step = kernels;
+  return QWC_OK;
+}
+
+int32_t build_batched(Handle* h) {
+  const DevModel& m = h->host_model;
+  const Config& c = h->config;
+  auto bp = std::make_unique<Batched>();
+  Batched& b = *bp;
+  const uint32_t qw = m.q_heads * kHeadDim, kvw = m.kv_heads * kHeadDim;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, h->device);
+  b.splits_qkv = gemm_splits(qw + 2 * kvw, m.hidden, sms);
+  b.splits_o = gemm_splits(m.hidden, qw, sms);
+  b.splits_gu = gemm_splits(2 * m.ffn, m.hidden, sms);
+  b.splits_down = gemm_splits(m.hidden, m.ffn, sms);
+  b.attn_grid = 2 * sms;
+  const size_t part_cols = std::max({size_t(b.splits_qkv) * (qw + 2 * kvw), size_t(b.splits_o) * m.hidden,
+                                     size_t(b.splits_gu) * 2 * m.ffn, size_t(b.splits_down) * m.hidden});
+  const size_t S = kMaxStreams;
+  QWC_TRY(b.hidden.alloc(S * m.hidden * 4));
+  QWC_TRY(b.xb_h.alloc(2 * S * m.hidden * 2));
+  QWC_TRY(b.xb_q.alloc(2 * S * qw * 2));
+  QWC_TRY(b.xb_f.alloc(2 * S * m.ffn * 2));
+  QWC_TRY(b.part0.alloc(S * part_cols * 4));
+  QWC_TRY(b.qrot.alloc(S * qw * 4));
+  QWC_TRY(b.attn_part.alloc(S * m.q_heads * h->max_chunks * (kHeadDim + 2) * 4));
+  QWC_TRY(b.attn_count.alloc(S * m.kv_heads * 4));
+  QWC_TRY(b.logits.alloc(S * m.vocab * 4));
+  QWC_TRY(b.tokens.alloc(S * 4));
+  QWC_TRY(b.desc.alloc(S * sizeof(SlotStep)));
+  QWC_TRY(b.audio_ptrs.alloc(S * sizeof(float*)));
+  QWC_TRY(b.err.alloc(256));
+  b.history_rows = std::max<uint32_t>(c.max_positions, 1);
+  QWC_TRY(b.history.alloc(size_t(b.history_rows) * S * 4));
+  QWC_TRY(b.counter.alloc(256));
+  for (DevBuf* z : {&b.hidden, &b.xb_h, &b.xb_q, &b.xb_f, &b.attn_count, &b.tokens, &b.desc, &b.audio_ptrs, &b.err,
+                    &b.counter}) {
+    QWC_CUDA(cudaMemset(z->ptr, 0, z->bytes));
+  }
+  if (cudaMallocHost(&b.host_desc, S * sizeof(SlotStep)) != cudaSuccess ||
+      cudaMallocHost(&b.host_tokens, S * 4) != cudaSuccess || cudaMallocHost(&b.host_err, 64) != cudaSuccess) {
+    cudaGetLastError();
+    return QWC_OUT_OF_MEMORY;
+  }
+  const uint32_t L = m.n_layers;
+  for (auto* v : {&b.mq, &b.mk, &b.mv, &b.mo, &b.mg, &b.mu, &b.md}) v->resize(L);
+  for (uint32_t l = 0; l < L; ++l) {
+    const DevLayer& D = m.layers[l];
+    QWC_TRY(mat_maps(D.q, &b.mq[l]));
+    QWC_TRY(mat_maps(D.k, &b.mk[l]));
+    QWC_TRY(mat_maps(D.v, &b.mv[l]));
+    QWC_TRY(mat_maps(D.o, &b.mo[l]));
+    QWC_TRY(mat_maps(D.gate, &b.mg[l]));
+    QWC_TRY(mat_maps(D.up, &b.mu[l]));
+    QWC_TRY(mat_maps(D.down, &b.md[l]));
+  }
+  QWC_TRY(mat_maps(m.lm_head, &b.mlm));
+  QWC_TRY(act_map(b.b_h, b.xb_h.ptr, m.hidden));
+  QWC_TRY(act_map(b.b_q, b.xb_q.ptr, qw));
+  QWC_TRY(act_map(b.b_f, b.xb_f.ptr, m.ffn));
+  const uint64_t scale_row = uint64_t(kvw / kGroup) * 2;
+  QWC_TRY(kv_map4(b.kv.k_codes, h->k_cache.as<uint8_t>() + m.cache_scales_bytes, kvw, m, h->streams, kHeadDim));
+  QWC_TRY(kv_map4(b.kv.v_codes, h->v_cache.as<uint8_t>() + m.cache_scales_bytes, kvw, m, h->streams, kHeadDim));
+  QWC_TRY(kv_map4(b.kv.k_scales, h->k_cache.as<uint8_t>(), scale_row, m, h->streams, 16));
+  QWC_TRY(kv_map4(b.kv.v_scales, h->v_cache.as<uint8_t>(), scale_row, m, h->streams, 16));
+
+  StreamsStep& P = b.P;
+  P.model = h->model_buf.as<DevModel>();
+  P.desc = b.desc.as<SlotStep>();
+  P.audio = b.audio_ptrs.as<const float*>();
+  P.hidden = b.hidden.as<float>();
+  P.xb_h = b.xb_h.ptr;
+  P.xb_q = b.xb_q.ptr;
+  P.xb_f = b.xb_f.ptr;
+  P.part0 = b.part0.as<float>();
+  P.qrot = b.qrot.as<float>();
+  P.attn_part = b.attn_part.as<float>();
+  P.attn_count = b.attn_count.as<uint32_t>();
+  P.k_cache = h->k_cache.as<uint8_t>();
+  P.v_cache = h->v_cache.as<uint8_t>();
+  P.logits = b.logits.as<float>();
+  P.tokens = b.tokens.as<uint32_t>();
+  P.error = b.err.as<int32_t>();
+  P.max_chunks = h->max_chunks;
+  P.timeout_ns = 2000000000ull;
+
+  int e = prepare_gemm_kernel();
+  if (e == 0) e = prepare_stream_kernels();
+  if (e != 0) return status_of(static_cast<cudaError_t>(e));
+  h->batched = std::move(bp);
+  // The step is recorded once as a CUDA graph and replayed every step.
+  QWC_CUDA(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+  const int32_t rec = record_step(h);
+  cudaGraph_t graph = nullptr;
+  const cudaError_t ce = cudaStreamEndCapture(h->stream, &graph);
+  if (rec != QWC_OK || ce != cudaSuccess) {
+    if (graph) cudaGraphDestroy(graph);
+    cudaGetLastError();
+    h->batched.reset();
+    return rec != QWC_OK ? rec : status_of(ce);
+  }
+  h->batched->graph = graph;
+  const cudaError_t ie = cudaGraphInstantiate(&h->batched->exec, graph, 0);
+  if (ie != cudaSuccess) {
+    h->batched.reset();
+    return status_of(ie);
+  }
+  return QWC_OK;
+}
+
+// One batched step: every decoding slot consumes its next prompt position or
+// its last token. results[slot]: 1 token emitted, 2 prompt position consumed
+// (no token yet), 0 idle or finished.
+int32_t batched_step(Handle* h, uint32_t* tokens_out, int32_t* results) {
+  Batched& b = *h->batched;
+  const Config& c = h->config;
+  const uint32_t n = static_cast<uint32_t>(h->slots.size());
+  bool any = false;
+  for (uint32_t slot = 0; slot < kMaxStreams; ++slot) {
+    SlotStep d{0, 0, 0, -1};
+    if (slot < n) {
+      StreamSlot& s = h->slots[slot];
+      results[slot] = 0;
+      if (s.decoding && !s.finished) {
+        if (s.position >= c.max_positions) {
+          s.finished = true;  // PositionExceeded (decoder.zig:142)
+          results[slot] = QWC_LIMIT_EXCEEDED;
+        } else if (s.prompt_pos < s.prompt.size()) {
+          d = SlotStep{1, s.position, static_cast<int32_t>(s.prompt[s.prompt_pos]), s.rows[s.prompt_pos]};
+        } else {
+          d = SlotStep{1, s.position, static_cast<int32_t>(s.last_token), -1};
+        }
+      }
+    }
+    b.host_desc[slot] = d;
+    any = any || d.active;
+  }
+  if (!any) return 0;
+  cudaStream_t st = h->stream;
+  QWC_CUDA(cudaMemcpyAsync(b.desc.ptr, b.host_desc, kMaxStreams * sizeof(SlotStep), cudaMemcpyHostToDevice, st));
+  QWC_CUDA(cudaGraphLaunch(b.exec, st));
+  QWC_CUDA(cudaMemcpyAsync(b.host_tokens, b.tokens.ptr, kMaxStreams * 4, cudaMemcpyDeviceToHost, st));
+  QWC_CUDA(cudaMemcpyAsync(b.host_err, b.err.ptr, 16, cudaMemcpyDeviceToHost, st));
+  QWC_CUDA(cudaStreamSynchronize(st));
+  h->launches += b.kernels_per_step;
+  if (*b.host_err != 0) {
+    if (std::getenv("QWC_VERBOSE")) {
+      std::fprintf(stderr, "qwc: batched step gave up waiting (code %d, detail %d %d %d)\n", b.host_err[0],
+                   b.host_err[1], b.host_err[2], b.host_err[3]);
+    }
+    cudaMemsetAsync(b.err.ptr, 0, 16, st);
+    cudaStreamSynchronize(st);
+    return QWC_INVALID_STATE;
+  }
+  int32_t produced = 0;
+  for (uint32_t slot = 0; slot < n; ++slot) {
+    if (!b.host_desc[slot].active) continue;
+    StreamSlot& s = h->slots[slot];
+    s.position += 1;
+    if (s.prompt_pos < s.prompt.size()) {
+      s.prompt_pos += 1;
+      if (s.prompt_pos < s.prompt.size()) {
+        results[slot] = 2;
+        continue;
+      }
+    }
+    const uint32_t token = b.host_tokens[slot];
+    if (!h->ignore_eos && ends_sequence(c, token)) {  // model.zig:423-451: EOS ends the stream, not emitted
+      s.finished = true;
+      continue;
+    }
+    tokens_out[slot] = token;
+    s.generated.push_back(token);
+    s.last_token = token;
+    results[slot] = 1;
+    ++produced;
+    if (s.generated.size() >= s.max_tokens) s.finished = true;
+  }
+  return produced;
+}
+
+// `steps` device-chained steps of every active slot (all past their
+// prompts), timed with CUDA events; the tokens are appended afterwards.
+int32_t batched_run_timed(Handle* h, uint32_t steps, float* device_ms) {
+  Batched& b = *h->batched;
+  const uint32_t n = static_cast<uint32_t>(h->slots.size());
+  bool any = false;
+  for (uint32_t slot = 0; slot < kMaxStreams; ++slot) {
+    SlotStep d{0, 0, 0, -1};
+    if (slot < n) {
+      StreamSlot& s = h->slots[slot];
+      if (s.decoding && !s.finished) {
+        if (s.prompt_pos < s.prompt.size()) return QWC_INVALID_STATE;  // prompts must be consumed first
+        if (s.position + steps > h->config.max_positions) return QWC_LIMIT_EXCEEDED;
+        if (s.generated.size() + steps > s.max_tokens) return QWC_LIMIT_EXCEEDED;
+        d = SlotStep{1, s.position, static_cast<int32_t>(s.last_token), -1};
+      }
+    }
+    b.host_desc[slot] = d;
+    any = any || d.active;
+  }
+  if (!any || steps == 0 || steps > b.history_rows) return QWC_INVALID_ARGUMENT;
+  cudaStream_t st = h->stream;
+  QWC_CUDA(cudaMemcpyAsync(b.desc.ptr, b.host_desc, kMaxStreams * sizeof(SlotStep), cudaMemcpyHostToDevice, st));
+  QWC_CUDA(cudaMemsetAsync(b.counter.ptr, 0, 4, st));
+  cudaEvent_t e0, e1;
+  QWC_CUDA(cudaEventCreate(&e0));
+  QWC_CUDA(cudaEventCreate(&e1));
+  cudaEventRecord(e0, st);
+  cudaError_t le = cudaSuccess;
+  for (uint32_t i = 0; i < steps && le == cudaSuccess; ++i) le = cudaGraphLaunch(b.exec, st);
+  cudaEventRecord(e1, st);
+  std::vector<uint32_t> hist(size_t(steps) * kMaxStreams);
+  if (le == cudaSuccess) {
+    le = cudaMemcpyAsync(hist.data(), b.history.ptr, hist.size() * 4, cudaMemcpyDeviceToHost, st);
+  }
+  if (le == cudaSuccess) le = cudaMemcpyAsync(b.host_err, b.err.ptr, 4, cudaMemcpyDeviceToHost, st);
+  if (le == cudaSuccess) le = cudaStreamSynchronize(st);
+  float ms = 0.0f;
+  if (le == cudaSuccess) cudaEventElapsedTime(&ms, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (le != cudaSuccess) return status_of(le);
+  h->launches += uint64_t(b.kernels_per_step) * steps;
+  if (*b.host_err != 0) {
+    cudaMemsetAsync(b.err.ptr, 0, 4, st);
+    cudaStreamSynchronize(st);
+    return QWC_INVALID_STATE;
+  }
+  for (uint32_t slot = 0; slot < n; ++slot) {
+    if (!b.host_desc[slot].active) continue;
+    StreamSlot& s = h->slots[slot];
+    for (uint32_t i = 0; i < steps; ++i) {
+      const uint32_t t = hist[size_t(i) * kMaxStreams + slot];
+      s.generated.push_back(t);
+      s.last_token = t;
+    }
+    s.position += steps;
+    if (s.generated.size() >= s.max_tokens) s.finished = true;
+  }
+  *device_ms = ms;
+  return QWC_OK;
+}
+
 int32_t stream_begin(Handle* h, uint32_t slot, const uint32_t* prompt, uint32_t prompt_len, const float* audio,
                      uint32_t audio_steps, uint32_t max_tokens) {
   if (h->state != State::kLoaded) return QWC_INVALID_STATE;
@@ -595,8 +952,32 @@ int32_t stream_begin(Handle* h, uint32_t slot, const uint32_t* prompt, uint32_t 
     }
   }
   if (audio_index != audio_steps) return QWC_SHAPE_MISMATCH;  // decoder.zig:331
-  if (slot != 0) return QWC_UNSUPPORTED;
   cudaSetDevice(h->device);
+  if (h->batched) {
+    // Batched mode: the prompt is consumed by later qwc_streams_step calls,
+    // one position per step, alongside the other slots.
+    const uint64_t stride = h->host_model.cache_stream_stride;
+    QWC_CUDA(cudaMemsetAsync(h->k_cache.as<uint8_t>() + stride * slot, 0, stride, h->stream));
+    QWC_CUDA(cudaMemsetAsync(h->v_cache.as<uint8_t>() + stride * slot, 0, stride, h->stream));
+    s = StreamSlot{};
+    const float* dev_audio = nullptr;
+    if (audio_steps) {
+      s.audio = std::make_unique<DevBuf>();
+      QWC_TRY(s.audio->alloc(size_t(audio_steps) * c.text_hidden_size * 4));
+      QWC_CUDA(cudaMemcpyAsync(s.audio->ptr, audio, s.audio->bytes, cudaMemcpyHostToDevice, h->stream));
+      dev_audio = s.audio->as<float>();
+    }
+    QWC_CUDA(cudaMemcpyAsync(h->batched->audio_ptrs.as<const float*>() + slot, &dev_audio, sizeof(dev_audio),
+                             cudaMemcpyHostToDevice, h->stream));
+    QWC_CUDA(cudaStreamSynchronize(h->stream));
+    s.prompt.assign(prompt, prompt + prompt_len);
+    s.rows = std::move(rows);
+    s.decoding = true;
+    s.max_tokens = max_tokens;
+    s.generated.reserve(max_tokens);
+    return QWC_OK;
+  }
+  if (slot != 0) return QWC_UNSUPPORTED;
   // Decoder.reset (decoder.zig:109-121): the whole cache goes back to zero.
   const uint64_t stride = h->host_model.cache_stream_stride;
   QWC_CUDA(cudaMemsetAsync(h->k_cache.as<uint8_t>() + stride * slot, 0, stride, h->stream));
@@ -640,6 +1021,7 @@ int32_t advance(Handle* h, StreamSlot& s, uint32_t token, uint32_t budget) {
 // src/wasm/model.zig:423-451
 int32_t stream_step(Handle* h, uint32_t slot, uint32_t* token_out) {
   if (h->state != State::kLoaded || slot >= h->slots.size()) return QWC_INVALID_STATE;
+  if (h->batched) return QWC_UNSUPPORTED;  // batched handles advance with qwc_streams_step
   StreamSlot& s = h->slots[slot];
   if (!s.decoding) return QWC_INVALID_STATE;
   if (s.finished) return 0;
@@ -671,7 +1053,7 @@ extern "C" {
 
 uint32_t qwc_abi_version(void) { return (QWC_ABI_MAJOR << 16) | QWC_ABI_MINOR; }
 
-uint32_t qwc_features(void) { return QWC_FEATURE_MODEL | QWC_FEATURE_DECODE; }
+uint32_t qwc_features(void) { return QWC_FEATURE_MODEL | QWC_FEATURE_DECODE | QWC_FEATURE_STREAMS; }
 
 const char* qwc_status_message(int32_t status) {
   switch (status) {
@@ -806,7 +1188,7 @@ int32_t qwc_model_set_streams(uint32_t handle, uint32_t streams) {
   if (!h) return QWC_INVALID_ARGUMENT;
   if (h->state != State::kReady) return QWC_INVALID_STATE;
   if (streams == 0) return QWC_INVALID_ARGUMENT;
-  if (streams != 1) return QWC_UNSUPPORTED;
+  if (streams > kMaxStreams) return QWC_LIMIT_EXCEEDED;
   h->streams = streams;
   return QWC_OK;
 }
@@ -870,6 +1252,7 @@ int32_t qwc_decode_begin(uint32_t handle, const uint32_t* prompt, uint32_t promp
                          uint32_t audio_steps, uint32_t max_tokens) {
   Handle* h = lookup(handle);
   if (!h) return QWC_INVALID_ARGUMENT;
+  if (h->batched) return QWC_UNSUPPORTED;  // the stream family drives batched handles
   return stream_begin(h, 0, prompt, prompt_len, audio, audio_steps, max_tokens);
 }
 
@@ -903,6 +1286,11 @@ int32_t qwc_stream_end(uint32_t handle, uint32_t slot) {
   const uint64_t stride = h->host_model.cache_stream_stride;
   QWC_CUDA(cudaMemsetAsync(h->k_cache.as<uint8_t>() + stride * slot, 0, stride, h->stream));
   QWC_CUDA(cudaMemsetAsync(h->v_cache.as<uint8_t>() + stride * slot, 0, stride, h->stream));
+  if (h->batched) {
+    const float* none = nullptr;
+    QWC_CUDA(cudaMemcpyAsync(h->batched->audio_ptrs.as<const float*>() + slot, &none, sizeof(none),
+                             cudaMemcpyHostToDevice, h->stream));
+  }
   QWC_CUDA(cudaStreamSynchronize(h->stream));
   h->slots[slot] = StreamSlot{};
   return QWC_OK;
@@ -922,6 +1310,7 @@ int32_t qwc_streams_step(uint32_t handle, uint32_t* tokens_out, int32_t* results
   if (!h || !tokens_out || !results) return QWC_INVALID_ARGUMENT;
   if (h->state != State::kLoaded) return QWC_INVALID_STATE;
   cudaSetDevice(h->device);
+  if (h->batched) return batched_step(h, tokens_out, results);
   int32_t produced = 0;
   for (uint32_t slot = 0; slot < h->slots.size(); ++slot) {
     if (!h->slots[slot].decoding) {
@@ -934,6 +1323,14 @@ int32_t qwc_streams_step(uint32_t handle, uint32_t* tokens_out, int32_t* results
     if (r < 0) return r;
   }
   return produced;
+}
+
+int32_t qwc_streams_run_timed(uint32_t handle, uint32_t steps, float* device_ms) {
+  Handle* h = lookup(handle);
+  if (!h || !device_ms) return QWC_INVALID_ARGUMENT;
+  if (h->state != State::kLoaded || !h->batched) return QWC_INVALID_STATE;
+  cudaSetDevice(h->device);
+  return batched_run_timed(h, steps, device_ms);
 }
 
 int32_t qwc_decode_run_timed(uint32_t handle, uint32_t steps, float* device_ms) {
@@ -981,9 +1378,15 @@ int32_t qwc_debug_logits(uint32_t handle, uint32_t slot, float* out, uint32_t co
   Handle* h = lookup(handle);
   if (!h || !out) return QWC_INVALID_ARGUMENT;
   if (h->state != State::kLoaded || slot >= h->slots.size()) return QWC_INVALID_STATE;
-  if (!h->keep_logits) return QWC_INVALID_STATE;
   if (count < h->config.vocab_size) return QWC_LIMIT_EXCEEDED;
   cudaSetDevice(h->device);
+  if (h->batched) {
+    const float* row = h->batched->logits.as<float>() + size_t(slot) * h->config.vocab_size;
+    QWC_CUDA(cudaMemcpyAsync(out, row, size_t(h->config.vocab_size) * 4, cudaMemcpyDeviceToHost, h->stream));
+    QWC_CUDA(cudaStreamSynchronize(h->stream));
+    return QWC_OK;
+  }
+  if (!h->keep_logits) return QWC_INVALID_STATE;
   QWC_CUDA(cudaMemcpyAsync(out, h->logits.ptr, size_t(h->config.vocab_size) * 4, cudaMemcpyDeviceToHost, h->stream));
   QWC_CUDA(cudaStreamSynchronize(h->stream));
   return QWC_OK;
@@ -994,6 +1397,17 @@ int32_t qwc_debug_hold(uint32_t handle, uint32_t slot, int64_t force, uint32_t* 
   if (!h || !held_out) return QWC_INVALID_ARGUMENT;
   if (h->state != State::kLoaded || slot >= h->slots.size() || !h->slots[slot].decoding) return QWC_INVALID_STATE;
   StreamSlot& s = h->slots[slot];
+  if (h->batched) {
+    // The next input of a slot past its prompt: its last emitted token.
+    if (s.prompt_pos < s.prompt.size() || s.generated.empty()) return QWC_INVALID_STATE;
+    if (force >= 0) {
+      if (static_cast<uint64_t>(force) >= h->config.vocab_size) return QWC_INVALID_ARGUMENT;
+      s.last_token = static_cast<uint32_t>(force);
+      s.generated.back() = s.last_token;
+    }
+    *held_out = s.last_token;
+    return QWC_OK;
+  }
   if (force >= 0) {
     if (!s.ahead.empty()) return QWC_INVALID_STATE;
     if (static_cast<uint64_t>(force) >= h->config.vocab_size) return QWC_INVALID_ARGUMENT;

@@ -5,23 +5,26 @@
 // projections of kernels.linearQuantized (src/core/qwen3_asr/kernels.zig:118-158)
 // for a batch of streams. W stays in the reference's two-plane q4/q8 layout
 // (src/core/quant.zig:144-176). Per CTA: one tile of 128 weight rows and a
-// range of K, in blocks of 128:
+// range of K, in blocks of 64 (one quantization group):
 //
 //   warp 0   TMA producer: raw code and scale boxes of the tile, and the
 //            activation box, into a 4-stage ring (mbarrier complete_tx);
-//   warp 1   TMEM owner and MMA issuer: tcgen05.mma kind::f16, M=128, N=64,
+//   warp 1   TMEM owner and MMA issuer: tcgen05.mma kind::f16, M=128, N=128,
 //            K=16, accumulating in TMEM; tcgen05.commit frees ring stages;
-//   warps 2-5 dequantize each raw block into f16 (code - bias) * scale, one
-//            row per thread, into a 2-stage operand buffer in the canonical
-//            K-major no-swizzle layout; then read the accumulator back
-//            (tcgen05.ld) and store f32 results.
+//   warps 2-5 dequantize each raw block, one row per thread, into a 2-stage
+//            operand buffer in the canonical K-major no-swizzle layout; then
+//            read the accumulator back (tcgen05.ld) and store f32 results.
 //
-// The f16 operands round each dequantized weight and each activation once
-// (11-bit significands); products accumulate in f32.
+// Exactness: a dequantized weight (code - bias) * scale is split into
+// hi = f16(w) and lo = w - hi, which is exact in f16 (at most 8 significant
+// bits remain); each activation into hi = f16(x) and lo = f16(x - hi). The
+// activation box holds the 64 hi rows, then the 64 lo rows, as the MMA's 128
+// columns; two MMAs per K step (weights hi, then lo) accumulate w * (x_hi +
+// x_lo) in f32, and the epilogue adds the two column halves. Products are thus
+// those of the exact weights with 22-bit activations.
 //
-// Activations arrive by TMA in 128-byte-swizzled rows (two boxes of 64 K per
-// block); the dequantized weights are written by the threads in the
-// no-swizzle core-matrix layout.
+// Activations arrive by TMA in 128-byte-swizzled rows; the dequantized weights
+// are written by the threads in the no-swizzle core-matrix layout.
 //
 // K order inside every 8-value chunk is permuted the same way for weights
 // and activations, [0 4 1 5 2 6 3 7], so one lop3 extracts two values of a
@@ -32,6 +35,7 @@
 #include <cuda_runtime.h>
 
 #include <cstddef>
+#include <cstring>
 
 #include "../../include/qwenscriber_cuda.h"
 #include "qwc_device.cuh"
@@ -44,16 +48,17 @@ constexpr int kGemmThreads = 192;
 constexpr int kRawStages = 4;
 constexpr int kAStages = 2;
 constexpr uint32_t kTileM = 128;
-constexpr uint32_t kTileN = 64;
-constexpr uint32_t kKBlock = 128;
-constexpr uint32_t kAStageBytes = kTileM * kKBlock * 2;  // 32 KB of f16
-constexpr uint32_t kBStageBytes = kTileN * kKBlock * 2;  // 16 KB of f16
-constexpr uint32_t kCodeStageBytes = kTileM * kKBlock;   // q8: 128 B per row; q4 uses half
-constexpr uint32_t kScaleStageBytes = kTileM * 16;       // one 16-byte box column of scales
-constexpr uint32_t kTmemCols = 64;
+constexpr uint32_t kStreamCols = 64;                      // streams per launch
+constexpr uint32_t kTileN = 2 * kStreamCols;              // hi rows then lo rows
+constexpr uint32_t kKBlock = 64;
+constexpr uint32_t kAHalfBytes = kTileM * kKBlock * 2;    // 16 KB of f16 (hi or lo)
+constexpr uint32_t kBStageBytes = kTileN * kKBlock * 2;   // 16 KB of f16, one 128-byte swizzle atom column
+constexpr uint32_t kCodeStageBytes = kTileM * kKBlock;    // q8: 64 B per row; q4 uses half
+constexpr uint32_t kScaleStageBytes = kTileM * 16;        // one 16-byte box column of scales
+constexpr uint32_t kTmemCols = 128;
 
 struct __align__(1024) GemmSmem {
-  uint8_t a16[kAStages][kAStageBytes];
+  uint8_t a16[kAStages][2][kAHalfBytes];
   uint8_t b[kRawStages][kBStageBytes];
   uint8_t codes[kRawStages][kCodeStageBytes];
   uint8_t scales[kRawStages][kScaleStageBytes];
@@ -66,7 +71,7 @@ struct __align__(1024) GemmSmem {
 };
 static_assert(offsetof(GemmSmem, b) % 1024 == 0 && offsetof(GemmSmem, codes) % 128 == 0 &&
                   offsetof(GemmSmem, scales) % 128 == 0,
-              "TMA destinations need 128-byte alignment");
+              "TMA destinations need 128-byte alignment (swizzled boxes 1024)");
 
 // ---- tcgen05 wrappers ----
 
@@ -99,7 +104,7 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint
   return d;  // base offset 0, absolute leading-offset mode
 }
 
-// Instruction descriptor: f16 x f16 -> f32, both K-major, M = 128, N = 64.
+// Instruction descriptor: f16 x f16 -> f32, both K-major, M = 128, N = 128.
 constexpr uint32_t kIdesc = (1u << 4) | ((kTileN >> 3) << 17) | ((kTileM >> 4) << 24);
 
 __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
@@ -167,64 +172,103 @@ __device__ __forceinline__ uint32_t lop_and_or(uint32_t w, uint32_t mask, uint32
   return r;
 }
 
-// Eight q4 codes (one 32-bit word, K order 0..7) -> 16 bytes of f16 in the
-// chunk order [0 4 1 5 2 6 3 7]: (code - 8) * scale, rounded once.
-__device__ __forceinline__ uint4 dequant_q4_word(uint32_t w, uint32_t scale2) {
+__device__ __forceinline__ uint32_t hfma2_bits(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+
+// Two centred codes (exact f16) times the scale: hi = f16(c * s), lo = the
+// exact remainder c * s - hi (one fused multiply-add).
+__device__ __forceinline__ void split_pair(uint32_t c2, uint32_t scale2, uint32_t& hi, uint32_t& lo) {
+  hi = hmul2_bits(c2, scale2);
+  lo = hfma2_bits(c2, scale2, hi ^ 0x80008000u);
+}
+
+// Eight q4 codes (one 32-bit word, K order 0..7) -> 16 bytes of f16 hi and
+// lo in the chunk order [0 4 1 5 2 6 3 7].
+__device__ __forceinline__ void dequant_q4_word(uint32_t w, uint32_t scale2, uint4& hi, uint4& lo) {
   const uint32_t magic = 0x64006400u;  // f16 1024 in both halves
   const uint32_t bias = 0x64086408u;   // f16 1032 = 1024 + 8
   const uint32_t mask = 0x000F000Fu;
-  uint4 o;
-  o.x = hmul2_bits(hsub2_bits(lop_and_or(w, mask, magic), bias), scale2);
-  o.y = hmul2_bits(hsub2_bits(lop_and_or(w >> 4, mask, magic), bias), scale2);
-  o.z = hmul2_bits(hsub2_bits(lop_and_or(w >> 8, mask, magic), bias), scale2);
-  o.w = hmul2_bits(hsub2_bits(lop_and_or(w >> 12, mask, magic), bias), scale2);
-  return o;
+  split_pair(hsub2_bits(lop_and_or(w, mask, magic), bias), scale2, hi.x, lo.x);
+  split_pair(hsub2_bits(lop_and_or(w >> 4, mask, magic), bias), scale2, hi.y, lo.y);
+  split_pair(hsub2_bits(lop_and_or(w >> 8, mask, magic), bias), scale2, hi.z, lo.z);
+  split_pair(hsub2_bits(lop_and_or(w >> 12, mask, magic), bias), scale2, hi.w, lo.w);
 }
 
 // Eight q8 codes (two words, K order 0..7) -> the same chunk order.
-__device__ __forceinline__ uint4 dequant_q8_words(uint32_t w0, uint32_t w1, uint32_t scale2) {
+__device__ __forceinline__ void dequant_q8_words(uint32_t w0, uint32_t w1, uint32_t scale2, uint4& hi, uint4& lo) {
   const uint32_t magic = 0x64006400u;
   const uint32_t bias = 0x64806480u;  // f16 1152 = 1024 + 128
   const uint32_t mask = 0x00FF00FFu;
-  uint4 o;
-  o.x = hmul2_bits(hsub2_bits(lop_and_or(__byte_perm(w0, w1, 0x0400), mask, magic), bias), scale2);
-  o.y = hmul2_bits(hsub2_bits(lop_and_or(__byte_perm(w0, w1, 0x0501), mask, magic), bias), scale2);
-  o.z = hmul2_bits(hsub2_bits(lop_and_or(__byte_perm(w0, w1, 0x0602), mask, magic), bias), scale2);
-  o.w = hmul2_bits(hsub2_bits(lop_and_or(__byte_perm(w0, w1, 0x0703), mask, magic), bias), scale2);
-  return o;
+  split_pair(hsub2_bits(lop_and_or(__byte_perm(w0, w1, 0x0400), mask, magic), bias), scale2, hi.x, lo.x);
+  split_pair(hsub2_bits(lop_and_or(__byte_perm(w0, w1, 0x0501), mask, magic), bias), scale2, hi.y, lo.y);
+  split_pair(hsub2_bits(lop_and_or(__byte_perm(w0, w1, 0x0602), mask, magic), bias), scale2, hi.z, lo.z);
+  split_pair(hsub2_bits(lop_and_or(__byte_perm(w0, w1, 0x0703), mask, magic), bias), scale2, hi.w, lo.w);
 }
 
-struct GemmParams {
+// One weight matrix of a launch. A launch multiplies up to three matrices
+// that share K and the activations (Q, K and V; gate and up).
+struct GemmJob {
   uint32_t rows;        // M
-  uint32_t cols;        // K (multiple of kKBlock)
-  uint32_t streams;     // N actually used (<= kTileN)
+  uint32_t mtiles;      // ceil(rows / 128)
   uint32_t format;      // q4 / q8
+  uint32_t out_offset;  // first output column of this matrix in each output row
+};
+
+struct GemmParams {
+  GemmJob job[3];
+  uint32_t njobs;
+  uint32_t cols;        // K (multiple of kKBlock)
+  uint32_t streams;     // stream columns written (<= kStreamCols); output rows per split
   uint32_t kb_per_split;
-  float* out;           // [split][streams][rows]
+  float* out;           // [split][streams][out_ld]
+  uint32_t out_ld;
   int32_t* error;
   uint64_t timeout_ns;
 };
 
+struct alignas(64) GemmMaps {
+  CUtensorMap codes[3];
+  CUtensorMap scales[3];
+  CUtensorMap b;
+};
+
 enum GemmError : int32_t { kGemmErrWait = 1 };
 
-__device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity, const GemmParams& p) {
-  return mbar_wait_bounded(bar, parity, p.error, global_timer_ns() + p.timeout_ns, kGemmErrWait);
+// Bounded wait; on expiry the first failing thread also records where
+// (error[1..3] = code site, block x, block y).
+__device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity, const GemmParams& p, int32_t site = 0) {
+  if (mbar_wait_bounded(bar, parity, p.error, global_timer_ns() + p.timeout_ns, kGemmErrWait + site)) return true;
+  if (*reinterpret_cast<volatile int32_t*>(p.error) == kGemmErrWait + site) {
+    p.error[1] = site;
+    p.error[2] = static_cast<int32_t>(blockIdx.x);
+    p.error[3] = static_cast<int32_t>(blockIdx.y);
+  }
+  return false;
 }
 
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_streams_kernel(const __grid_constant__ CUtensorMap map_codes, const __grid_constant__ CUtensorMap map_scales,
-                        const __grid_constant__ CUtensorMap map_b, const GemmParams p) {
+    gemm_streams_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
   extern __shared__ __align__(1024) uint8_t gemm_smem_raw[];
   // The swizzle atoms need 1024-byte alignment in the shared window.
   const uint32_t pad = (1024u - (smem_addr(gemm_smem_raw) & 1023u)) & 1023u;
   GemmSmem* s = reinterpret_cast<GemmSmem*>(gemm_smem_raw + pad);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const uint32_t m0 = blockIdx.x * kTileM;
+  // Which matrix and which 128-row tile of it this CTA takes.
+  uint32_t tile = blockIdx.x, jb = 0;
+  while (jb + 1 < p.njobs && tile >= p.job[jb].mtiles) tile -= p.job[jb++].mtiles;
+  const GemmJob job = p.job[jb];
+  const CUtensorMap* map_codes = &maps.codes[jb];
+  const CUtensorMap* map_scales = &maps.scales[jb];
+  const CUtensorMap* map_b = &maps.b;
+  const uint32_t m0 = tile * kTileM;
   const uint32_t kblocks = p.cols / kKBlock;
   const uint32_t kb0 = blockIdx.y * p.kb_per_split;
   const uint32_t kb1 = min(kblocks, kb0 + p.kb_per_split);
   const uint32_t nkb = kb1 > kb0 ? kb1 - kb0 : 0;
-  const bool q4 = p.format == kFormatQ4;
+  const bool q4 = job.format == kFormatQ4;
   const uint32_t code_box = q4 ? kKBlock / 2 : kKBlock;  // bytes of codes per row per block
 
   if (threadIdx.x == 0) {
@@ -251,20 +295,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       for (uint32_t i = 0; i < nkb && ok; ++i) {
         const uint32_t st = i % kRawStages;
-        if (i >= kRawStages && !wait_bounded(&s->raw_empty[st], ((i / kRawStages) - 1) & 1u, p)) {
+        if (i >= kRawStages && !wait_bounded(&s->raw_empty[st], ((i / kRawStages) - 1) & 1u, p, 10)) {
           ok = false;
           break;
         }
         const uint32_t kb = kb0 + i;
         mbar_arrive_expect_tx(&s->raw_full[st], kTileM * code_box + kScaleStageBytes + kBStageBytes);
-        tma_load_2d(s->codes[st], &map_codes, static_cast<int32_t>(kb * code_box), static_cast<int32_t>(m0),
+        tma_load_2d(s->codes[st], map_codes, static_cast<int32_t>(kb * code_box), static_cast<int32_t>(m0),
                     &s->raw_full[st]);
-        // The 16-byte scale box holding this block's two groups.
-        tma_load_2d(s->scales[st], &map_scales, static_cast<int32_t>((kb * 4u) & ~15u), static_cast<int32_t>(m0),
+        // The 16-byte scale box holding this block's group.
+        tma_load_2d(s->scales[st], map_scales, static_cast<int32_t>((kb * 2u) & ~15u), static_cast<int32_t>(m0),
                     &s->raw_full[st]);
-        tma_load_2d(s->b[st], &map_b, static_cast<int32_t>(kb * kKBlock), 0, &s->raw_full[st]);
-        tma_load_2d(s->b[st] + kBStageBytes / 2, &map_b, static_cast<int32_t>(kb * kKBlock + 64), 0,
-                    &s->raw_full[st]);
+        tma_load_2d(s->b[st], map_b, static_cast<int32_t>(kb * kKBlock), 0, &s->raw_full[st]);
       }
       // Drain: every armed stage must have landed before the CTA exits.
       for (uint32_t i = (nkb > kRawStages ? nkb - kRawStages : 0); i < nkb; ++i) {
@@ -278,21 +320,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (uint32_t i = 0; i < nkb && ok; ++i) {
         const uint32_t st = i % kRawStages;
         const uint32_t at = i % kAStages;
-        if (!wait_bounded(&s->raw_full[st], (i / kRawStages) & 1u, p) ||
-            !wait_bounded(&s->a_full[at], (i / kAStages) & 1u, p)) {
+        if (!wait_bounded(&s->raw_full[st], (i / kRawStages) & 1u, p, 20) ||
+            !wait_bounded(&s->a_full[at], (i / kAStages) & 1u, p, 30)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t a_base = smem_addr(s->a16[at]);
+        const uint32_t a_hi = smem_addr(s->a16[at][0]);
+        const uint32_t a_lo = smem_addr(s->a16[at][1]);
         const uint32_t b_base = smem_addr(s->b[st]);
 #pragma unroll
         for (uint32_t k = 0; k < kKBlock / 16; ++k) {
           // A: two 8-element K chunks per MMA, 2048 B apart (128 rows x 16 B).
-          // B: 64-element swizzle atoms of 64 rows x 128 B; 32 B per K step.
-          const uint64_t ad = umma_desc(a_base + k * 2 * 2048, 2048, 128, kLayoutNone);
-          const uint64_t bd = umma_desc(b_base + (k / 4) * (kBStageBytes / 2) + (k % 4) * 32, 16, 1024, kLayoutSw128);
-          umma_f16(tmem, ad, bd, (i > 0 || k > 0) ? 1u : 0u);
+          // B: one swizzle atom of 128 rows x 128 B; 32 B per K step.
+          const uint64_t bd = umma_desc(b_base + k * 32, 16, 1024, kLayoutSw128);
+          umma_f16(tmem, umma_desc(a_hi + k * 2 * 2048, 2048, 128, kLayoutNone), bd, (i > 0 || k > 0) ? 1u : 0u);
+          umma_f16(tmem, umma_desc(a_lo + k * 2 * 2048, 2048, 128, kLayoutNone), bd, 1u);
         }
         umma_commit(&s->a_empty[at]);
         umma_commit(&s->raw_empty[st]);
@@ -307,40 +350,44 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (uint32_t i = 0; i < nkb && ok; ++i) {
       const uint32_t st = i % kRawStages;
       const uint32_t at = i % kAStages;
-      if (!wait_bounded(&s->raw_full[st], (i / kRawStages) & 1u, p)) {
+      if (!wait_bounded(&s->raw_full[st], (i / kRawStages) & 1u, p, 40)) {
         ok = false;
         break;
       }
-      if (i >= kAStages && !wait_bounded(&s->a_empty[at], ((i / kAStages) - 1) & 1u, p)) {
+      if (i >= kAStages && !wait_bounded(&s->a_empty[at], ((i / kAStages) - 1) & 1u, p, 50)) {
         ok = false;
         break;
       }
       const uint32_t kb = kb0 + i;
-      const uint8_t* srow = s->scales[st] + r * 16 + ((kb * 4u) & 15u);
-      const uint16_t sb0 = *reinterpret_cast<const uint16_t*>(srow);
-      const uint16_t sb1 = *reinterpret_cast<const uint16_t*>(srow + 2);
-      const uint32_t sc0 = static_cast<uint32_t>(sb0) * 0x10001u;
-      const uint32_t sc1 = static_cast<uint32_t>(sb1) * 0x10001u;
-      uint8_t* a = s->a16[at] + r * 16;
+      const uint16_t sb = *reinterpret_cast<const uint16_t*>(s->scales[st] + r * 16 + ((kb * 2u) & 15u));
+      const uint32_t sc = static_cast<uint32_t>(sb) * 0x10001u;
+      uint8_t* ahi = s->a16[at][0] + r * 16;
+      uint8_t* alo = s->a16[at][1] + r * 16;
+      uint4 hi, lo;
       if (q4) {
         const uint4* src = reinterpret_cast<const uint4*>(s->codes[st] + r * (kKBlock / 2));
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < 2; ++q) {
           const uint4 w = src[q];
-          const uint32_t sc = q < 2 ? sc0 : sc1;  // chunks 0-7: group 0, 8-15: group 1
-          *reinterpret_cast<uint4*>(a + (4 * q + 0) * 2048) = dequant_q4_word(w.x, sc);
-          *reinterpret_cast<uint4*>(a + (4 * q + 1) * 2048) = dequant_q4_word(w.y, sc);
-          *reinterpret_cast<uint4*>(a + (4 * q + 2) * 2048) = dequant_q4_word(w.z, sc);
-          *reinterpret_cast<uint4*>(a + (4 * q + 3) * 2048) = dequant_q4_word(w.w, sc);
+          const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            dequant_q4_word(words[t], sc, hi, lo);
+            *reinterpret_cast<uint4*>(ahi + (4 * q + t) * 2048) = hi;
+            *reinterpret_cast<uint4*>(alo + (4 * q + t) * 2048) = lo;
+          }
         }
       } else {
         const uint4* src = reinterpret_cast<const uint4*>(s->codes[st] + r * kKBlock);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
+        for (int q = 0; q < 4; ++q) {
           const uint4 w = src[q];
-          const uint32_t sc = q < 4 ? sc0 : sc1;
-          *reinterpret_cast<uint4*>(a + (2 * q + 0) * 2048) = dequant_q8_words(w.x, w.y, sc);
-          *reinterpret_cast<uint4*>(a + (2 * q + 1) * 2048) = dequant_q8_words(w.z, w.w, sc);
+          dequant_q8_words(w.x, w.y, sc, hi, lo);
+          *reinterpret_cast<uint4*>(ahi + (2 * q + 0) * 2048) = hi;
+          *reinterpret_cast<uint4*>(alo + (2 * q + 0) * 2048) = lo;
+          dequant_q8_words(w.z, w.w, sc, hi, lo);
+          *reinterpret_cast<uint4*>(ahi + (2 * q + 1) * 2048) = hi;
+          *reinterpret_cast<uint4*>(alo + (2 * q + 1) * 2048) = lo;
         }
       }
       // Generic-proxy stores, read next by the tensor core (async proxy).
@@ -349,19 +396,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (lane == 0) mbar_arrive(&s->a_full[at]);
     }
     // Epilogue: TMEM lane = tile row; this warp may read lanes 32 * (warp % 4) + [0, 32).
-    bool go = ok && nkb > 0 && wait_bounded(&s->acc_full, 0, p);
+    bool go = ok && nkb > 0 && wait_bounded(&s->acc_full, 0, p, 60);
     go = __all_sync(0xffffffffu, go);  // tcgen05.ld is warp-collective
     if (go) {
       tc_fence_after();
       const uint32_t quarter = static_cast<uint32_t>(warp % 4);
-      float v[64];
+      float v[64], vlo[64];
       tmem_ld64(tmem + ((quarter * 32u) << 16), v);
+      tmem_ld64(tmem + ((quarter * 32u) << 16) + kStreamCols, vlo);
+#pragma unroll
+      for (int n = 0; n < 64; ++n) v[n] += vlo[n];  // x_hi and x_lo columns
       const uint32_t row = m0 + quarter * 32 + lane;
-      if (row < p.rows) {
-        float* out = p.out + size_t(blockIdx.y) * p.streams * p.rows + row;
+      if (row < job.rows) {
+        float* out = p.out + size_t(blockIdx.y) * p.streams * p.out_ld + job.out_offset + row;
 #pragma unroll
         for (int n = 0; n < 64; ++n) {
-          if (n < static_cast<int>(p.streams)) out[size_t(n) * p.rows] = v[n];
+          if (n < static_cast<int>(p.streams)) out[size_t(n) * p.out_ld] = v[n];
         }
       }
     }
@@ -374,18 +424,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
-// x[s][k] f32 -> f16 activations in the permuted chunk order, rows padded to
-// `ld` (elements).
+// x[s][k] f32 -> the activation box rows: f16 hi values in rows [0, 64),
+// lo remainders in rows [64, 128), chunks in the permuted order.
 __global__ void pack_activations_kernel(const float* x, uint32_t streams, uint32_t cols, __half* out) {
   const uint32_t chunks = cols / 8;
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < streams * chunks; i += gridDim.x * blockDim.x) {
     const uint32_t sidx = i / chunks, c = i % chunks;
     const float* src = x + size_t(sidx) * cols + c * 8;
     const int perm[8] = {0, 4, 1, 5, 2, 6, 3, 7};
-    __align__(16) __half h[8];
+    __align__(16) __half hi[8];
+    __align__(16) __half lo[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) h[j] = __float2half_rn(src[perm[j]]);
-    *reinterpret_cast<uint4*>(out + size_t(sidx) * cols + c * 8) = *reinterpret_cast<const uint4*>(h);
+    for (int j = 0; j < 8; ++j) {
+      const float v = src[perm[j]];
+      hi[j] = __float2half_rn(v);
+      lo[j] = __float2half_rn(v - __half2float(hi[j]));
+    }
+    *reinterpret_cast<uint4*>(out + size_t(sidx) * cols + c * 8) = *reinterpret_cast<const uint4*>(hi);
+    *reinterpret_cast<uint4*>(out + size_t(kStreamCols + sidx) * cols + c * 8) = *reinterpret_cast<const uint4*>(lo);
   }
 }
 
@@ -400,6 +456,98 @@ __global__ void sum_splits_kernel(const float* parts, uint32_t splits, uint32_t 
 }  // namespace
 
 int gemm_smem_bytes() { return static_cast<int>(sizeof(GemmSmem)) + 1024; }
+
+int prepare_gemm_kernel() {
+  return static_cast<int>(
+      cudaFuncSetAttribute(gemm_streams_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_smem_bytes()));
+}
+
+// TMA descriptors of one weight matrix and of an activation buffer, with the
+// box sizes the kernel's transaction counts assume.
+int32_t gemm_weight_maps(uint32_t format, const void* codes, const void* scales, uint32_t rows, uint32_t cols,
+                         uint8_t* codes_map, uint8_t* scales_map) {
+  const uint32_t groups = cols / kGroup;
+  const uint64_t code_row = uint64_t(groups) * data_bytes_per_group(format), scale_row = uint64_t(groups) * 2;
+  const uint64_t dims_c[2] = {code_row, rows};
+  const uint64_t str_c[1] = {code_row};
+  const uint32_t box_c[2] = {format == kFormatQ4 ? kKBlock / 2 : kKBlock, kTileM};
+  const uint64_t dims_s[2] = {scale_row, rows};
+  const uint64_t str_s[1] = {scale_row};
+  const uint32_t box_s[2] = {16, kTileM};
+  const int32_t rc = encode_tensor_map(codes_map, kMapU8, 2, const_cast<void*>(codes), dims_c, str_c, box_c, false);
+  if (rc != QWC_OK) return rc;
+  return encode_tensor_map(scales_map, kMapU8, 2, const_cast<void*>(scales), dims_s, str_s, box_s, false);
+}
+
+int32_t gemm_act_map(void* base, uint32_t cols, uint8_t* out) {
+  const uint64_t dims[2] = {cols, kTileN};
+  const uint64_t str[1] = {uint64_t(cols) * 2};
+  const uint32_t box[2] = {kKBlock, kTileN};
+  return encode_tensor_map(out, kMapF16, 2, base, dims, str, box, true);
+}
+
+// Splits of K so that the launch fills whole waves of CTAs (one per SM).
+uint32_t gemm_splits(uint32_t rows, uint32_t cols, int sms) {
+  const uint32_t mtiles = (rows + kTileM - 1) / kTileM;
+  const uint32_t kblocks = cols / kKBlock;
+  uint32_t best = 1;
+  double best_eff = 0.0;
+  for (uint32_t want = 1; want <= kblocks && want <= 48; ++want) {
+    const uint32_t kps = (kblocks + want - 1) / want;
+    const uint32_t splits = (kblocks + kps - 1) / kps;
+    const uint32_t ctas = mtiles * splits;
+    const uint32_t waves = (ctas + sms - 1) / sms;
+    const double eff = double(ctas) / (double(waves) * sms);
+    if (eff > best_eff + 0.02) {
+      best_eff = eff;
+      best = splits;
+    }
+  }
+  return best;
+}
+
+// A launch over up to three matrices (maps: codes/scales per matrix, then
+// the activations); `splits` divides K.
+int launch_gemm_jobs(const uint8_t (*codes_maps)[128], const uint8_t (*scale_maps)[128], const uint32_t* rows,
+                     const uint32_t* formats, const uint32_t* out_offsets, uint32_t njobs, const uint8_t* map_b,
+                     uint32_t cols, uint32_t streams, uint32_t splits, float* out, uint32_t out_ld, int32_t* error,
+                     void* stream) {
+  GemmMaps maps;
+  GemmParams p{};
+  uint32_t tiles = 0;
+  for (uint32_t j = 0; j < njobs; ++j) {
+    std::memcpy(&maps.codes[j], codes_maps[j], 128);
+    std::memcpy(&maps.scales[j], scale_maps[j], 128);
+    p.job[j] = GemmJob{rows[j], (rows[j] + kTileM - 1) / kTileM, formats[j], out_offsets[j]};
+    tiles += p.job[j].mtiles;
+  }
+  for (uint32_t j = njobs; j < 3; ++j) {
+    std::memcpy(&maps.codes[j], codes_maps[0], 128);
+    std::memcpy(&maps.scales[j], scale_maps[0], 128);
+  }
+  std::memcpy(&maps.b, map_b, 128);
+  const uint32_t kblocks = cols / kKBlock;
+  p.njobs = njobs;
+  p.cols = cols;
+  p.streams = streams;
+  p.kb_per_split = (kblocks + splits - 1) / splits;
+  p.out = out;
+  p.out_ld = out_ld;
+  p.error = error;
+  p.timeout_ns = 2000000000ull;
+  const uint32_t real_splits = (kblocks + p.kb_per_split - 1) / p.kb_per_split;
+  const int smem = gemm_smem_bytes();
+  gemm_streams_kernel<<<dim3(tiles, real_splits), kGemmThreads, smem, static_cast<cudaStream_t>(stream)>>>(maps, p);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int launch_gemm_streams(const uint8_t* map_codes, const uint8_t* map_scales, const uint8_t* map_b, uint32_t rows,
+                        uint32_t cols, uint32_t format, uint32_t splits, float* out, int32_t* error, void* stream) {
+  const uint8_t(*cm)[128] = reinterpret_cast<const uint8_t(*)[128]>(map_codes);
+  const uint8_t(*sm)[128] = reinterpret_cast<const uint8_t(*)[128]>(map_scales);
+  const uint32_t off = 0;
+  return launch_gemm_jobs(cm, sm, &rows, &format, &off, 1, map_b, cols, kStreamCols, splits, out, rows, error, stream);
+}
 
 }  // namespace qwc
 
@@ -419,7 +567,7 @@ extern "C" int32_t qwc_op_gemm_streams(uint32_t format, const void* scales, cons
                                        uint32_t cols, const float* x, uint32_t streams, float* out, void* stream) {
   if (!scales || !codes || !x || !out || rows == 0) return QWC_INVALID_ARGUMENT;
   if (format != kFormatQ4 && format != kFormatQ8) return QWC_UNSUPPORTED;
-  if (cols == 0 || cols % kKBlock != 0 || streams == 0 || streams > kTileN) return QWC_INVALID_ARGUMENT;
+  if (cols == 0 || cols % 512 != 0 || streams == 0 || streams > kStreamCols) return QWC_INVALID_ARGUMENT;
   if (reinterpret_cast<uintptr_t>(scales) % 16 != 0 || reinterpret_cast<uintptr_t>(codes) % 16 != 0) {
     return QWC_INVALID_ARGUMENT;
   }
@@ -427,20 +575,17 @@ extern "C" int32_t qwc_op_gemm_streams(uint32_t format, const void* scales, cons
   const uint32_t groups = cols / kGroup;
   const uint32_t scale_row = groups * 2;
   const uint32_t code_row = groups * data_bytes_per_group(format);
-  if (scale_row % 16 != 0) return QWC_UNSUPPORTED;
-  const uint32_t kblocks = cols / kKBlock;
-  const uint32_t mtiles = (rows + kTileM - 1) / kTileM;
   int sms = 148;
   int device = 0;
   cudaGetDevice(&device);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-  uint32_t splits = 1;
-  while (mtiles * (splits + 1) <= static_cast<uint32_t>(sms) && splits < kblocks) ++splits;
-  const uint32_t kps = (kblocks + splits - 1) / splits;
-  splits = (kblocks + kps - 1) / kps;
+  const uint32_t kblocks = cols / kKBlock;
+  const uint32_t want = gemm_splits(rows, cols, sms);
+  const uint32_t kps = (kblocks + want - 1) / want;
+  const uint32_t splits = (kblocks + kps - 1) / kps;
 
   // Workspace: error word, packed activations, split partials.
-  const size_t xb_bytes = (size_t(streams) * cols * 2 + 255) / 256 * 256;
+  const size_t xb_bytes = (size_t(kTileN) * cols * 2 + 255) / 256 * 256;
   const size_t part_bytes = size_t(splits) * streams * rows * 4;
   void* ws = nullptr;
   cudaError_t e = cudaMallocAsync(&ws, 256 + xb_bytes + part_bytes, st);
@@ -448,36 +593,22 @@ extern "C" int32_t qwc_op_gemm_streams(uint32_t format, const void* scales, cons
   int32_t* err = static_cast<int32_t*>(ws);
   __half* xb = reinterpret_cast<__half*>(static_cast<uint8_t*>(ws) + 256);
   float* parts = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + 256 + xb_bytes);
-  cudaMemsetAsync(err, 0, 4, st);
+  cudaMemsetAsync(ws, 0, 256 + xb_bytes, st);
   pack_activations_kernel<<<256, 256, 0, st>>>(x, streams, cols, xb);
 
   alignas(64) uint8_t maps[3][128];
-  int32_t rc = QWC_OK;
-  {
-    const uint64_t dims_c[2] = {code_row, rows};
-    const uint64_t str_c[1] = {code_row};
-    const uint32_t box_c[2] = {format == kFormatQ4 ? kKBlock / 2 : kKBlock, kTileM};
-    const uint64_t dims_s[2] = {scale_row, rows};
-    const uint64_t str_s[1] = {scale_row};
-    const uint32_t box_s[2] = {16, kTileM};
-    const uint64_t dims_b[2] = {cols, streams};
-    const uint64_t str_b[1] = {uint64_t(cols) * 2};
-    const uint32_t box_b[2] = {64, kTileN};
-    rc = encode_tensor_map(maps[0], kMapU8, 2, const_cast<void*>(codes), dims_c, str_c, box_c, false);
-    if (rc == QWC_OK) rc = encode_tensor_map(maps[1], kMapU8, 2, const_cast<void*>(scales), dims_s, str_s, box_s, false);
-    if (rc == QWC_OK) rc = encode_tensor_map(maps[2], kMapF16, 2, xb, dims_b, str_b, box_b, true);
-  }
+  int32_t rc = gemm_weight_maps(format, codes, scales, rows, cols, maps[0], maps[1]);
+  if (rc == QWC_OK) rc = gemm_act_map(xb, cols, maps[2]);
   if (rc != QWC_OK) {
     cudaFreeAsync(ws, st);
     return rc;
   }
-  GemmParams gp{rows, cols, streams, format, kps, parts, err, 2000000000ull};
-  const int smem = gemm_smem_bytes();
-  cudaFuncSetAttribute(gemm_streams_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  gemm_streams_kernel<<<dim3(mtiles, splits), kGemmThreads, smem, st>>>(
-      *reinterpret_cast<const CUtensorMap*>(maps[0]), *reinterpret_cast<const CUtensorMap*>(maps[1]),
-      *reinterpret_cast<const CUtensorMap*>(maps[2]), gp);
-  e = cudaGetLastError();
+  const uint32_t off = 0;
+  int le = prepare_gemm_kernel();
+  if (le == 0) le = launch_gemm_jobs(reinterpret_cast<const uint8_t(*)[128]>(maps[0]),
+                            reinterpret_cast<const uint8_t(*)[128]>(maps[1]), &rows, &format, &off, 1, maps[2], cols,
+                            streams, splits, parts, rows, err, st);
+  e = static_cast<cudaError_t>(le);
   if (e == cudaSuccess) {
     sum_splits_kernel<<<256, 256, 0, st>>>(parts, splits, streams * rows, out);
     e = cudaGetLastError();

@@ -131,6 +131,78 @@ int decode_kernel_smem_bytes();
 int launch_decode(const DecodeLaunch& launch, const KvMaps& maps, int grid, void* stream);
 int decode_grid_size(int device);
 
+// ---- batched multi-stream step (qwc_streams.cu) ----
+
+constexpr uint32_t kMaxStreams = 64;  // stream columns of the tensor-core GEMM
+
+// What one slot does in the next batched step: consume `token` (embedding
+// row) or, when `audio_row` >= 0, that row of the slot's audio, at `position`.
+struct SlotStep {
+  int32_t active;
+  uint32_t position;
+  int32_t token;
+  int32_t audio_row;
+};
+
+// Device buffers and shapes shared by the step's kernels. All [slot] arrays
+// have kMaxStreams rows; inactive slots are skipped (their rows hold zeros).
+struct StreamsStep {
+  const DevModel* model;
+  const SlotStep* desc;          // [kMaxStreams]
+  const float* const* audio;     // [kMaxStreams] per-slot audio rows (device pointers, may be null)
+  float* hidden;                 // [slot][hidden]
+  void* xb_h;                    // f16 [2 x slot][hidden]: hi rows, then lo rows (GEMM activation layout)
+  void* xb_q;                    // f16 [2 x slot][q width]
+  void* xb_f;                    // f16 [2 x slot][ffn]
+  float* part0;                  // [split][slot][rows] projection partials
+  float* qrot;                   // [slot][q width]: normed, rotated queries
+  float* attn_part;              // [slot][q head][chunk][head_dim + 2]
+  uint32_t* attn_count;          // [slot][kv head]
+  uint8_t* k_cache;
+  uint8_t* v_cache;
+  float* logits;                 // [slot][vocab]
+  uint32_t* tokens;              // [slot]
+  int32_t* error;
+  uint32_t max_chunks;
+  uint64_t timeout_ns;
+};
+
+// 4-D TMA descriptors over every slot's q8 cache: [slot][layer][position][row bytes].
+struct alignas(64) KvMaps4 {
+  uint8_t k_codes[128];
+  uint8_t k_scales[128];
+  uint8_t v_codes[128];
+  uint8_t v_scales[128];
+};
+
+// One tensor-core GEMM launch over up to three matrices sharing K and the
+// activations: out[split][streams][out_ld], matrix j's rows at column
+// out_offsets[j]. Maps are 128-byte CUtensorMaps.
+int launch_gemm_jobs(const uint8_t (*codes_maps)[128], const uint8_t (*scale_maps)[128], const uint32_t* rows,
+                     const uint32_t* formats, const uint32_t* out_offsets, uint32_t njobs, const uint8_t* map_b,
+                     uint32_t cols, uint32_t streams, uint32_t splits, float* out, uint32_t out_ld, int32_t* error,
+                     void* stream);
+int launch_gemm_streams(const uint8_t* map_codes, const uint8_t* map_scales, const uint8_t* map_b, uint32_t rows,
+                        uint32_t cols, uint32_t format, uint32_t splits, float* out, int32_t* error, void* stream);
+// TMA descriptors for the stream GEMM: a weight matrix (codes and scales
+// planes) and an activation buffer of 128 f16 rows (hi, then lo) x cols.
+int32_t gemm_weight_maps(uint32_t format, const void* codes, const void* scales, uint32_t rows, uint32_t cols,
+                         uint8_t* codes_map, uint8_t* scales_map);
+int32_t gemm_act_map(void* base, uint32_t cols, uint8_t* out);
+// Split count for a GEMM of `rows` x `cols` on `sms` SMs.
+uint32_t gemm_splits(uint32_t rows, uint32_t cols, int sms);
+// Step kernels; each returns cudaError_t as int.
+int launch_streams_norm(const StreamsStep& P, int input_mode, const float* weight, const float* parts,
+                        uint32_t splits, void* stream);
+int launch_streams_qkv(const StreamsStep& P, uint32_t layer, uint32_t splits, uint32_t kv_heads, void* stream);
+int launch_streams_attention(const StreamsStep& P, const KvMaps4& maps, uint32_t layer, int grid, void* stream);
+int launch_streams_swiglu(const StreamsStep& P, uint32_t splits, void* stream);
+int launch_streams_argmax(const StreamsStep& P, void* stream);
+int launch_streams_advance(const StreamsStep& P, uint32_t* history, uint32_t* counter, uint32_t rows, void* stream);
+// Kernel attributes (dynamic shared memory) set once, outside stream capture.
+int prepare_stream_kernels();
+int prepare_gemm_kernel();
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point. `strides`
 // holds rank - 1 byte strides (dimension 1 up); `swizzle128` selects the
 // 128-byte swizzle. Returns a QWC_* status.

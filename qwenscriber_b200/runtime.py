@@ -56,6 +56,7 @@ SIGNATURES = {
     "qwc_streams_step": (c_int32, [c_uint32, c_void_p, c_void_p]),
     "qwc_stream_tokens": (c_int32, [c_uint32, c_uint32, c_void_p, c_uint32]),
     "qwc_stream_end": (c_int32, [c_uint32, c_uint32]),
+    "qwc_streams_run_timed": (c_int32, [c_uint32, c_uint32, c_void_p]),
     "qwc_decode_run_timed": (c_int32, [c_uint32, c_uint32, POINTER(c_float)]),
     "qwc_debug_logits": (c_int32, [c_uint32, c_uint32, c_void_p, c_uint32]),
     "qwc_debug_hold": (c_int32, [c_uint32, c_uint32, c_int64, POINTER(c_uint32)]),
@@ -213,6 +214,34 @@ class CudaModel:
     def run_timed(self, steps: int) -> float:
         ms = c_float(0.0)
         check(self._L.qwc_decode_run_timed(self.handle, steps, ctypes.byref(ms)), "qwc_decode_run_timed")
+        return ms.value
+
+    # ---- multi-stream family (handles with set_streams(n), n >= 2) ----
+    def stream_begin(self, slot: int, prompt, audio: np.ndarray | None, max_tokens: int) -> None:
+        ids = np.ascontiguousarray(np.asarray(prompt, dtype=np.uint32))
+        rows = None if audio is None or len(audio) == 0 else np.ascontiguousarray(audio, dtype=np.float32)
+        steps = 0 if rows is None else rows.shape[0]
+        check(self._L.qwc_stream_begin(self.handle, slot, ids.ctypes.data, ids.size, _ptr(rows), steps, max_tokens),
+              "qwc_stream_begin")
+
+    def streams_step(self, slots: int) -> tuple[np.ndarray, np.ndarray, int]:
+        """One batched step: (tokens, results, produced); results 1 = token, 2 = prompt position, 0 = idle/done."""
+        tokens = np.zeros(max(slots, 64), np.uint32)
+        results = np.zeros(max(slots, 64), np.int32)
+        n = check(self._L.qwc_streams_step(self.handle, tokens.ctypes.data, results.ctypes.data), "qwc_streams_step")
+        return tokens[:slots], results[:slots], n
+
+    def stream_tokens(self, slot: int, capacity: int = 8192) -> list[int]:
+        out = np.zeros(capacity, np.uint32)
+        n = check(self._L.qwc_stream_tokens(self.handle, slot, out.ctypes.data, capacity), "qwc_stream_tokens")
+        return out[:n].tolist()
+
+    def stream_end(self, slot: int) -> None:
+        check(self._L.qwc_stream_end(self.handle, slot), "qwc_stream_end")
+
+    def streams_run_timed(self, steps: int) -> float:
+        ms = c_float(0.0)
+        check(self._L.qwc_streams_run_timed(self.handle, steps, ctypes.byref(ms)), "qwc_streams_run_timed")
         return ms.value
 
     # ---- parity hooks ----
