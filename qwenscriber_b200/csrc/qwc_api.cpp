@@ -724,6 +724,8 @@ int32_t build_batched(Handle* h) {
                     &b.counter}) {
     QWC_CUDA(cudaMemset(z->ptr, 0, z->bytes));
   }
+  // Attention partials: a NaN max marks "no segment starts at this chunk".
+  QWC_CUDA(cudaMemset(b.attn_part.ptr, 0xFF, b.attn_part.bytes));
   if (cudaMallocHost(&b.host_desc, S * sizeof(SlotStep)) != cudaSuccess ||
       cudaMallocHost(&b.host_tokens, S * 4) != cudaSuccess || cudaMallocHost(&b.host_err, 64) != cudaSuccess) {
     cudaGetLastError();

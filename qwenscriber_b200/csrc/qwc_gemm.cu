@@ -486,20 +486,22 @@ int32_t gemm_act_map(void* base, uint32_t cols, uint8_t* out) {
   return encode_tensor_map(out, kMapF16, 2, base, dims, str, box, true);
 }
 
-// Splits of K so that the launch fills whole waves of CTAs (one per SM).
+// Splits of K for a launch of `rows` x `cols`: the fewest waves of CTAs (one
+// per SM) weighed against per-CTA fixed cost (about four K blocks of
+// pipeline fill, TMEM set-up and epilogue) and the partial sums the next
+// kernel reads.
 uint32_t gemm_splits(uint32_t rows, uint32_t cols, int sms) {
   const uint32_t mtiles = (rows + kTileM - 1) / kTileM;
   const uint32_t kblocks = cols / kKBlock;
   uint32_t best = 1;
-  double best_eff = 0.0;
-  for (uint32_t want = 1; want <= kblocks && want <= 48; ++want) {
+  double best_cost = 1e30;
+  for (uint32_t want = 1; want <= kblocks && want <= 32; ++want) {
     const uint32_t kps = (kblocks + want - 1) / want;
     const uint32_t splits = (kblocks + kps - 1) / kps;
-    const uint32_t ctas = mtiles * splits;
-    const uint32_t waves = (ctas + sms - 1) / sms;
-    const double eff = double(ctas) / (double(waves) * sms);
-    if (eff > best_eff + 0.02) {
-      best_eff = eff;
+    const uint32_t waves = (mtiles * splits + sms - 1) / sms;
+    const double cost = double(waves) * (kps + 4.0) + 0.5 * splits;
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
       best = splits;
     }
   }
@@ -572,9 +574,6 @@ extern "C" int32_t qwc_op_gemm_streams(uint32_t format, const void* scales, cons
     return QWC_INVALID_ARGUMENT;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const uint32_t groups = cols / kGroup;
-  const uint32_t scale_row = groups * 2;
-  const uint32_t code_row = groups * data_bytes_per_group(format);
   int sms = 148;
   int device = 0;
   cudaGetDevice(&device);

@@ -213,27 +213,41 @@ __global__ void __launch_bounds__(256) streams_qkv_kernel(const StreamsStep P, u
 }
 
 // ---- split-K decode attention over every slot (kernels.zig:697-767) ----
+//
+// Units (slot, kv head, 64-position chunk) in that order are dealt to CTAs in
+// contiguous ranges, so a CTA walks consecutive chunks of the same (slot,
+// head) and carries an online softmax across them (running max, sum and
+// output). A producer warp keeps a ring of TMA boxes of upcoming chunks in
+// flight. Each (slot, head) segment a CTA finishes becomes one partial
+// (o[128], max, sum) per query head; the CTA whose segment completes the
+// head's chunk count combines the partials (flash-decode rescale).
 
 constexpr uint32_t kTK = 0;                                    // [64][128] key codes
 constexpr uint32_t kTV = kTK + kAttnChunk * kHeadDim;          // [64][128] value codes
 constexpr uint32_t kTKS = kTV + kAttnChunk * kHeadDim;         // [64][16 B] key scales (4 kv heads)
 constexpr uint32_t kTVS = kTKS + kAttnChunk * 16;              // [64][16 B] value scales
 constexpr uint32_t kTileBytes = kTVS + kAttnChunk * 16;
-static_assert(kTV % 128 == 0 && kTKS % 128 == 0 && kTVS % 128 == 0, "TMA boxes land on 128-byte boundaries");
+constexpr int kAttnSlots = 4;
+constexpr int kAttnConsumers = 256;
+static_assert(kTV % 128 == 0 && kTKS % 128 == 0 && kTVS % 128 == 0 && kTileBytes % 128 == 0,
+              "TMA boxes land on 128-byte boundaries");
 
-struct __align__(128) AttnTile {
-  uint8_t tile[kTileBytes];
-  alignas(16) float q[2][4][36];
+struct __align__(128) AttnSmem {
+  uint8_t ring[kAttnSlots][kTileBytes];
+  alignas(16) float q[2][4][36];   // rotated queries, 32-dim quarters padded against bank conflicts
   alignas(16) float prob[2][kAttnChunk];
-  alignas(16) float lsum[2][8];
-  alignas(16) float mx[2];
   alignas(16) float vpart[8][2][kHeadDim];
-  alignas(16) float red[16];
+  alignas(16) float red[2][8];
+  alignas(16) float lsum[2][8];
+  float mnew[2];
   uint32_t prefix[kMaxStreams + 1];
   uint32_t flag;
-  alignas(8) uint64_t bar;
+  alignas(8) uint64_t full[kAttnSlots];
+  alignas(8) uint64_t empty[kAttnSlots];
 };
-static_assert(offsetof(AttnTile, vpart) % 16 == 0 && offsetof(AttnTile, q) % 16 == 0, "vector access alignment");
+static_assert(offsetof(AttnSmem, vpart) % 16 == 0 && offsetof(AttnSmem, q) % 16 == 0 &&
+                  offsetof(AttnSmem, prob) % 16 == 0,
+              "vector access alignment");
 
 __device__ __forceinline__ void tma_load_4d(void* dst, const void* map, int32_t x, int32_t y, int32_t z, int32_t w,
                                             uint64_t* bar) {
@@ -244,83 +258,176 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* map, int32_t 
       : "memory");
 }
 
-__global__ void __launch_bounds__(256) streams_attention_kernel(const StreamsStep P, const __grid_constant__ KvMaps4 maps,
-                                                                uint32_t layer) {
+struct UnitPos {
+  uint32_t s, h, ch, chunks;
+};
+
+__device__ __forceinline__ UnitPos unit_pos(const AttnSmem* a, const StreamsStep& P, uint32_t kv_heads, uint32_t u) {
+  uint32_t lo = 0, hi = kMaxStreams;
+  while (hi - lo > 1) {
+    const uint32_t mid = (lo + hi) / 2;
+    if (a->prefix[mid] <= u) lo = mid; else hi = mid;
+  }
+  const uint32_t chunks = P.desc[lo].position / kAttnChunk + 1;
+  const uint32_t r = u - a->prefix[lo];
+  return UnitPos{lo, r / chunks, r % chunks, chunks};
+}
+
+__global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kernel(const StreamsStep P,
+                                                                               const __grid_constant__ KvMaps4 maps,
+                                                                               uint32_t layer) {
   extern __shared__ __align__(128) uint8_t attn_smem_raw[];
-  AttnTile* a = reinterpret_cast<AttnTile*>(attn_smem_raw);
+  AttnSmem* a = reinterpret_cast<AttnSmem*>(attn_smem_raw);
   const DevModel& m = *P.model;
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-  const int j = tid / kHeadDim, dd = tid % kHeadDim;
   const uint32_t qw = m.q_heads * kHeadDim;
+  const uint32_t kv_heads = m.kv_heads;
   if (tid == 0) {
-    mbar_init(&a->bar, 1);
+    for (int i = 0; i < kAttnSlots; ++i) {
+      mbar_init(&a->full[i], 1);
+      mbar_init(&a->empty[i], 8);
+    }
     fence_mbar_init();
     uint32_t acc = 0;
     for (uint32_t s = 0; s < kMaxStreams; ++s) {
       a->prefix[s] = acc;
       const SlotStep d = P.desc[s];
-      if (d.active) acc += m.kv_heads * (d.position / kAttnChunk + 1);
+      if (d.active) acc += kv_heads * (d.position / kAttnChunk + 1);
     }
     a->prefix[kMaxStreams] = acc;
   }
   __syncthreads();
   const uint32_t total = a->prefix[kMaxStreams];
-  uint32_t phase = 0;
-  bool ok = true;
-  for (uint32_t u = blockIdx.x; u < total; u += gridDim.x) {
-    // Slot of unit u: the last s with prefix[s] <= u.
-    uint32_t lo = 0, hi = kMaxStreams;
-    while (hi - lo > 1) {
-      const uint32_t mid = (lo + hi) / 2;
-      if (a->prefix[mid] <= u) lo = mid; else hi = mid;
-    }
-    const uint32_t s = lo;
-    const SlotStep d = P.desc[s];
-    const uint32_t chunks = d.position / kAttnChunk + 1;
-    const uint32_t r = u - a->prefix[s];
-    const uint32_t h = r / chunks, ch = r % chunks;
-    const uint32_t newest = d.position;
-    if (tid == 0) {
-      mbar_arrive_expect_tx(&a->bar, kTileBytes);
-      const int32_t y = static_cast<int32_t>(ch * kAttnChunk), z = static_cast<int32_t>(layer),
-                    w = static_cast<int32_t>(s);
-      const int32_t xs = static_cast<int32_t>((h * 4u) & ~15u);
-      tma_load_4d(a->tile + kTK, maps.k_codes, static_cast<int32_t>(h * kHeadDim), y, z, w, &a->bar);
-      tma_load_4d(a->tile + kTV, maps.v_codes, static_cast<int32_t>(h * kHeadDim), y, z, w, &a->bar);
-      tma_load_4d(a->tile + kTKS, maps.k_scales, xs, y, z, w, &a->bar);
-      tma_load_4d(a->tile + kTVS, maps.v_scales, xs, y, z, w, &a->bar);
-    }
-    // Rotated queries 2h, 2h+1 (L2) while the tile lands.
-    a->q[j][dd / 32][dd % 32] = P.qrot[size_t(s) * qw + (2 * h + j) * kHeadDim + dd];
-    if (ok && !mbar_wait_bounded(&a->bar, phase, P.error, global_timer_ns() + P.timeout_ns, 101)) {
-      ok = false;
-      if (*reinterpret_cast<volatile int32_t*>(P.error) == 101 && tid == 0) {
-        P.error[1] = static_cast<int32_t>(layer);
-        P.error[2] = static_cast<int32_t>(u);
-        P.error[3] = static_cast<int32_t>(s);
+  const uint32_t u0 = static_cast<uint32_t>((uint64_t(total) * blockIdx.x) / gridDim.x);
+  const uint32_t u1 = static_cast<uint32_t>((uint64_t(total) * (blockIdx.x + 1)) / gridDim.x);
+
+  if (warp == 8) {
+    // ---- producer: TMA boxes of units u0..u1 into the ring ----
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (uint32_t u = u0; u < u1; ++u, ++it) {
+        const uint32_t slot = it % kAttnSlots;
+        if (it >= kAttnSlots &&
+            !mbar_wait_bounded(&a->empty[slot], ((it / kAttnSlots) - 1) & 1u, P.error,
+                               global_timer_ns() + P.timeout_ns, 102)) {
+          break;
+        }
+        const UnitPos up = unit_pos(a, P, kv_heads, u);
+        uint8_t* dst = a->ring[slot];
+        mbar_arrive_expect_tx(&a->full[slot], kTileBytes);
+        const int32_t y = static_cast<int32_t>(up.ch * kAttnChunk), z = static_cast<int32_t>(layer),
+                      w = static_cast<int32_t>(up.s);
+        const int32_t xs = static_cast<int32_t>((up.h * 4u) & ~15u);
+        tma_load_4d(dst + kTK, maps.k_codes, static_cast<int32_t>(up.h * kHeadDim), y, z, w, &a->full[slot]);
+        tma_load_4d(dst + kTV, maps.v_codes, static_cast<int32_t>(up.h * kHeadDim), y, z, w, &a->full[slot]);
+        tma_load_4d(dst + kTKS, maps.k_scales, xs, y, z, w, &a->full[slot]);
+        tma_load_4d(dst + kTVS, maps.v_scales, xs, y, z, w, &a->full[slot]);
       }
-    }
-    if (__syncthreads_or(!ok)) {
-      // A box never landed: wait once more (bounded) so no copy is still in
-      // flight when the CTA exits, and stop.
-      if (tid == 0) {
+      // Every armed box must land before the CTA exits.
+      const uint32_t n = u1 > u0 ? u1 - u0 : 0;
+      for (uint32_t i = (n > kAttnSlots ? n - kAttnSlots : 0); i < n; ++i) {
         const uint64_t deadline = global_timer_ns() + 1000000000ull;
-        while (!mbar_try_wait(&a->bar, phase) && global_timer_ns() < deadline) {
+        while (!mbar_try_wait(&a->full[i % kAttnSlots], (i / kAttnSlots) & 1u) && global_timer_ns() < deadline) {
         }
       }
-      __syncthreads();
+    }
+    return;
+  }
+
+  // ---- consumers: 256 threads; thread (j, d) owns output dim d of query head 2h + j ----
+  const int j = tid / kHeadDim, dd = tid % kHeadDim;
+  const uint32_t rr = static_cast<uint32_t>(tid) / 4, qd = static_cast<uint32_t>(tid) % 4;
+  const uint32_t grp = static_cast<uint32_t>(lane) / 16;
+  bool ok = true;
+  float o_run = 0.0f, l_run = 0.0f, m_run = -INFINITY;
+  UnitPos cur{0xFFFFFFFFu, 0xFFFFFFFFu, 0, 0};
+  uint32_t seg_first = 0, seg_count = 0;
+
+  // Emits the running state of the current (slot, head) segment.
+  auto flush = [&]() {
+    __half* xq = static_cast<__half*>(P.xb_q) + size_t(cur.s) * qw;
+    const size_t xq_lo = size_t(kMaxStreams) * qw;
+    const uint32_t col = (2 * cur.h + j) * kHeadDim + dd;
+    const uint32_t out_index = (col & ~7u) | chunk_slot(col & 7u);
+    if (seg_count == cur.chunks) {
+      store_one(xq + out_index, xq_lo, o_run / l_run);
       return;
     }
-    phase ^= 1u;
-    // Scores: four lanes per position, the two lanes of a 64-value group add
+    float* part = P.attn_part + ((size_t(cur.s) * m.q_heads + 2 * cur.h + j) * P.max_chunks + seg_first) * (kHeadDim + 2);
+    part[dd] = o_run;
+    if (dd == 0) part[kHeadDim + 1] = l_run;
+    __threadfence();
+    consumer_sync(kAttnConsumers);
+    if (dd == 0) {
+      // The max goes last: a non-NaN max marks the partial as written.
+      reinterpret_cast<volatile float*>(part)[kHeadDim] = m_run;
+    }
+    __threadfence();
+    consumer_sync(kAttnConsumers);
+    uint32_t* counter = P.attn_count + size_t(cur.s) * kv_heads + cur.h;
+    if (tid == 0) {
+      const uint32_t prev = atomicAdd(counter, seg_count);
+      a->flag = (prev + seg_count == cur.chunks) ? 1u : 0u;
+    }
+    consumer_sync(kAttnConsumers);
+    if (a->flag) {
+      __threadfence();
+      float mx = -INFINITY, o = 0.0f, l = 0.0f;
+      float* base = P.attn_part + (size_t(cur.s) * m.q_heads + 2 * cur.h + j) * P.max_chunks * (kHeadDim + 2);
+      for (uint32_t c = 0; c < cur.chunks; ++c) {
+        float* src = base + size_t(c) * (kHeadDim + 2);
+        const float pm = ld_cg(src + kHeadDim);
+        if (pm != pm) continue;  // NaN: no segment starts at this chunk
+        const float po = ld_cg(src + dd), pl = ld_cg(src + kHeadDim + 1);
+        const float nm = fmaxf(mx, pm);
+        const float f_old = (mx == -INFINITY) ? 0.0f : expf(mx - nm);
+        const float f_new = expf(pm - nm);
+        o = o * f_old + po * f_new;
+        l = l * f_old + pl * f_new;
+        mx = nm;
+      }
+      store_one(xq + out_index, xq_lo, o / l);
+      consumer_sync(kAttnConsumers);
+      // Reset for the next step: partial maxima back to NaN, counter to 0.
+      for (uint32_t c = tid; c < cur.chunks * 2; c += kAttnConsumers) {
+        float* base2 = P.attn_part + (size_t(cur.s) * m.q_heads + 2 * cur.h + (c & 1u)) * P.max_chunks * (kHeadDim + 2);
+        base2[size_t(c >> 1) * (kHeadDim + 2) + kHeadDim] = __int_as_float(-1);
+      }
+      if (tid == 0) *counter = 0;
+    }
+    consumer_sync(kAttnConsumers);
+  };
+
+  uint32_t it = 0;
+  for (uint32_t u = u0; u < u1; ++u, ++it) {
+    const UnitPos up = unit_pos(a, P, kv_heads, u);
+    if (up.s != cur.s || up.h != cur.h) {
+      if (cur.s != 0xFFFFFFFFu) flush();
+      cur = up;
+      seg_first = up.ch;
+      seg_count = 0;
+      o_run = 0.0f;
+      l_run = 0.0f;
+      m_run = -INFINITY;
+      a->q[j][dd / 32][dd % 32] = P.qrot[size_t(up.s) * qw + (2 * up.h + j) * kHeadDim + dd];
+    }
+    const uint32_t slot = it % kAttnSlots;
+    if (ok && !mbar_wait_bounded(&a->full[slot], (it / kAttnSlots) & 1u, P.error, global_timer_ns() + P.timeout_ns,
+                                 101)) {
+      ok = false;
+    }
+    consumer_sync(kAttnConsumers);  // q written, tile landed
+    const uint8_t* tile = a->ring[slot];
+    const uint32_t newest = P.desc[up.s].position;
+    // Scores: four lanes per position; the two lanes of a 64-value group add
     // their sums before the group scale (q8GroupDot, kernels.zig:636-661).
-    const uint32_t rr = static_cast<uint32_t>(tid) / 4, qd = static_cast<uint32_t>(tid) % 4;
-    const uint32_t pos = ch * kAttnChunk + rr;
+    const uint32_t pos = up.ch * kAttnChunk + rr;
     const bool valid = ok && pos <= newest;
+    float sc0, sc1;
     {
-      const uint4* src = reinterpret_cast<const uint4*>(a->tile + kTK + rr * kHeadDim + qd * 32);
+      const uint4* src = reinterpret_cast<const uint4*>(tile + kTK + rr * kHeadDim + qd * 32);
       const uint4 kw0 = src[0], kw1 = src[1];
-      const uint32_t kbits = *reinterpret_cast<const uint16_t*>(a->tile + kTKS + rr * 16 + (h % 4) * 4 + (qd / 2) * 2);
+      const uint32_t kbits = *reinterpret_cast<const uint16_t*>(tile + kTKS + rr * 16 + (up.h % 4) * 4 + (qd / 2) * 2);
       const uint32_t words[8] = {kw0.x, kw0.y, kw0.z, kw0.w, kw1.x, kw1.y, kw1.z, kw1.w};
       const uint64_t bias = pack2(kNegQ8, kNegQ8);
       uint64_t acc0 = 0, acc1 = 0;
@@ -346,48 +453,50 @@ __global__ void __launch_bounds__(256) streams_attention_kernel(const StreamsSte
       g1 *= scale;
       g0 += __shfl_xor_sync(0xffffffffu, g0, 2);
       g1 += __shfl_xor_sync(0xffffffffu, g1, 2);
-      const float sc0 = valid ? m.attn_scaling * g0 : -INFINITY;
-      const float sc1 = valid ? m.attn_scaling * g1 : -INFINITY;
+      sc0 = valid ? m.attn_scaling * g0 : -INFINITY;
+      sc1 = valid ? m.attn_scaling * g1 : -INFINITY;
       const float w0 = warp_max(sc0), w1 = warp_max(sc1);
       if (lane == 0) {
-        a->red[warp] = w0;
-        a->red[8 + warp] = w1;
+        a->red[0][warp] = w0;
+        a->red[1][warp] = w1;
       }
-      __syncthreads();
-      float m0 = -INFINITY, m1 = -INFINITY;
-#pragma unroll
-      for (int w = 0; w < 8; ++w) {
-        m0 = fmaxf(m0, a->red[w]);
-        m1 = fmaxf(m1, a->red[8 + w]);
-      }
-      const float p0 = valid ? expf(sc0 - m0) : 0.0f;
-      const float p1 = valid ? expf(sc1 - m1) : 0.0f;
-      if (qd == 0) {
-        a->prob[0][rr] = p0;
-        a->prob[1][rr] = p1;
-      }
-      const float l0 = warp_sum(qd == 0 ? p0 : 0.0f), l1 = warp_sum(qd == 0 ? p1 : 0.0f);
-      if (lane == 0) {
-        a->lsum[0][warp] = l0;
-        a->lsum[1][warp] = l1;
-      }
-      if (tid == 0) {
-        a->mx[0] = m0;
-        a->mx[1] = m1;
-      }
-      __syncthreads();
     }
+    consumer_sync(kAttnConsumers);
+    float cm0 = -INFINITY, cm1 = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      cm0 = fmaxf(cm0, a->red[0][w]);
+      cm1 = fmaxf(cm1, a->red[1][w]);
+    }
+    // Online softmax (math.zig:77-93 subtracts the row max before exp). The
+    // threads of a head share its running max; the probabilities need both
+    // heads' new maxima, published through shared memory.
+    const float m_new = fmaxf(m_run, j == 0 ? cm0 : cm1);
+    if (dd == 0) a->mnew[j] = m_new;
+    consumer_sync(kAttnConsumers);
+    const float mh0 = a->mnew[0], mh1 = a->mnew[1];
+    const float p0 = valid ? expf(sc0 - mh0) : 0.0f;
+    const float p1 = valid ? expf(sc1 - mh1) : 0.0f;
+    if (qd == 0) {
+      a->prob[0][rr] = p0;
+      a->prob[1][rr] = p1;
+    }
+    const float l0 = warp_sum(qd == 0 ? p0 : 0.0f), l1 = warp_sum(qd == 0 ? p1 : 0.0f);
+    if (lane == 0) {
+      a->lsum[0][warp] = l0;
+      a->lsum[1][warp] = l1;
+    }
+    consumer_sync(kAttnConsumers);
     // Values (q8GroupAccumulate, kernels.zig:665-688): lane = 4 dims, warp = 8 positions.
     {
       float acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
-      const uint32_t grp = static_cast<uint32_t>(lane) / 16;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const uint32_t q = warp * 8 + i;
-        const uint32_t word = *reinterpret_cast<const uint32_t*>(a->tile + kTV + q * kHeadDim + 4 * lane);
-        const uint32_t bits = *reinterpret_cast<const uint16_t*>(a->tile + kTVS + q * 16 + (h % 4) * 4 + grp * 2);
+        const uint32_t word = *reinterpret_cast<const uint32_t*>(tile + kTV + q * kHeadDim + 4 * lane);
+        const uint32_t bits = *reinterpret_cast<const uint16_t*>(tile + kTVS + q * 16 + (up.h % 4) * 4 + grp * 2);
         const float scale = f16_bits_to_f32_fast(bits);
-        const bool vq = ok && ch * kAttnChunk + q <= newest;
+        const bool vq = ok && up.ch * kAttnChunk + q <= newest;
         const float sw0 = vq ? scale * a->prob[0][q] : 0.0f;
         const float sw1 = vq ? scale * a->prob[1][q] : 0.0f;
 #pragma unroll
@@ -397,81 +506,26 @@ __global__ void __launch_bounds__(256) streams_attention_kernel(const StreamsSte
           acc[1][t] = fmaf(cv, sw1, acc[1][t]);
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a->empty[slot]);  // this warp is done with the tile
       *reinterpret_cast<float4*>(&a->vpart[warp][0][4 * lane]) = make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
       *reinterpret_cast<float4*>(&a->vpart[warp][1][4 * lane]) = make_float4(acc[1][0], acc[1][1], acc[1][2], acc[1][3]);
     }
-    __syncthreads();
+    consumer_sync(kAttnConsumers);
     float o = 0.0f, l = 0.0f;
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
       o += a->vpart[w][j][dd];
       l += a->lsum[j][w];
     }
-    const float mj = a->mx[j];
-    __half* xq = static_cast<__half*>(P.xb_q) + size_t(s) * qw;
-    const uint32_t col = (2 * h + j) * kHeadDim + dd;
-    const uint32_t out_index = (col & ~7u) | chunk_slot(col & 7u);
-    const size_t xq_lo = size_t(kMaxStreams) * qw;
-    if (chunks == 1) {
-      store_one(xq + out_index, xq_lo, o / l);
-      __syncthreads();
-      continue;
-    }
-    {
-      float* dst = P.attn_part + ((size_t(s) * m.q_heads + 2 * h + j) * P.max_chunks + ch) * (kHeadDim + 2);
-      dst[dd] = o;
-      if (dd == 0) {
-        dst[kHeadDim] = mj;
-        dst[kHeadDim + 1] = l;
-      }
-    }
-    __threadfence();
-    __syncthreads();
-    uint32_t* counter = P.attn_count + size_t(s) * m.kv_heads + h;
-    if (tid == 0) {
-      const uint32_t prev = atomicAdd(counter, 1u);
-      a->flag = (prev == chunks - 1) ? 1u : 0u;
-    }
-    __syncthreads();
-    if (a->flag) {
-      __threadfence();
-      float mx = -INFINITY;
-      o = 0.0f;
-      l = 0.0f;
-      const float* base = P.attn_part + (size_t(s) * m.q_heads + 2 * h + j) * P.max_chunks * (kHeadDim + 2);
-      for (uint32_t q0 = 0; q0 < chunks; q0 += 8) {
-        float pm[8], po[8], pl[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          pm[q] = -INFINITY;
-          po[q] = 0.0f;
-          pl[q] = 0.0f;
-          if (q0 + q < chunks) {
-            const float* src = base + size_t(q0 + q) * (kHeadDim + 2);
-            pm[q] = ld_cg(src + kHeadDim);
-            po[q] = ld_cg(src + dd);
-            pl[q] = ld_cg(src + kHeadDim + 1);
-          }
-        }
-        float bm = mx;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) bm = fmaxf(bm, pm[q]);
-        const float rescale = (mx == -INFINITY) ? 0.0f : expf(mx - bm);
-        o *= rescale;
-        l *= rescale;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const float f = (pm[q] == -INFINITY) ? 0.0f : expf(pm[q] - bm);
-          o = fmaf(po[q], f, o);
-          l = fmaf(pl[q], f, l);
-        }
-        mx = bm;
-      }
-      store_one(xq + out_index, xq_lo, o / l);
-      if (tid == 0) *counter = 0;
-    }
-    __syncthreads();
+    const float rescale = (m_run == -INFINITY) ? 0.0f : expf(m_run - m_new);
+    o_run = o_run * rescale + o;
+    l_run = l_run * rescale + l;
+    m_run = m_new;
+    ++seg_count;
+    consumer_sync(kAttnConsumers);  // vpart / prob / red reused by the next unit
   }
+  if (cur.s != 0xFFFFFFFFu) flush();
 }
 
 // ---- SwiGLU (kernels.zig:233-239) into f16 activations ----
@@ -575,7 +629,7 @@ int launch_streams_advance(const StreamsStep& P, uint32_t* history, uint32_t* co
 
 int prepare_stream_kernels() {
   return static_cast<int>(cudaFuncSetAttribute(streams_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(sizeof(AttnTile))));
+                                               static_cast<int>(sizeof(AttnSmem))));
 }
 
 int launch_streams_norm(const StreamsStep& P, int input_mode, const float* weight, const float* parts, uint32_t splits,
@@ -595,8 +649,8 @@ int launch_streams_qkv(const StreamsStep& P, uint32_t layer, uint32_t splits, ui
 }
 
 int launch_streams_attention(const StreamsStep& P, const KvMaps4& maps, uint32_t layer, int grid, void* stream) {
-  const int smem = static_cast<int>(sizeof(AttnTile));
-  streams_attention_kernel<<<grid, 256, smem, static_cast<cudaStream_t>(stream)>>>(P, maps, layer);
+  const int smem = static_cast<int>(sizeof(AttnSmem));
+  streams_attention_kernel<<<grid, kAttnConsumers + 32, smem, static_cast<cudaStream_t>(stream)>>>(P, maps, layer);
   return static_cast<int>(cudaGetLastError());
 }
 

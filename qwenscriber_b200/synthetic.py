@@ -131,6 +131,15 @@ def workloads() -> dict[str, Workload]:
     }
 
 
+def prefix_lengths(w: Workload) -> list[int]:
+    """Audio-prefix rows of every stream of a multi-stream workload (uniform in
+    the stated range, per-workload seed)."""
+    if isinstance(w.audio_rows, int):
+        return [w.audio_rows] * w.streams
+    lo, hi = w.audio_rows
+    return [int(x) for x in np.random.default_rng([w.seed, 3]).integers(lo, hi + 1, size=w.streams)]
+
+
 def load_into(model: Model, target, cache_format: int = 1, streams: int | None = None) -> None:
     """Loads a synthetic model through the reference-shaped model family of `target`
     (a `runtime.CudaModel`, or anything with the same methods)."""
