@@ -11,9 +11,10 @@
 //            activation box, into a 4-stage ring (mbarrier complete_tx);
 //   warp 1   TMEM owner and MMA issuer: tcgen05.mma kind::f16, M=128, N=128,
 //            K=16, accumulating in TMEM; tcgen05.commit frees ring stages;
-//   warps 2-5 dequantize each raw block, one row per thread, into a 2-stage
-//            operand buffer in the canonical K-major no-swizzle layout; then
-//            read the accumulator back (tcgen05.ld) and store f32 results.
+//   warps 2-9 dequantize each raw block, half a row per thread, into a
+//            2-stage operand buffer in the canonical K-major no-swizzle
+//            layout; then read the accumulator back (tcgen05.ld) and store
+//            f32 results (two warps per TMEM lane quarter, 32 streams each).
 //
 // Exactness: a dequantized weight (code - bias) * scale is split into
 // hi = f16(w) and lo = w - hi, which is exact in f16 (at most 8 significant
@@ -44,7 +45,8 @@
 namespace qwc {
 namespace {
 
-constexpr int kGemmThreads = 192;
+constexpr int kGemmThreads = 320;
+constexpr int kDequantWarps = 8;
 constexpr int kRawStages = 4;
 constexpr int kAStages = 2;
 constexpr uint32_t kTileM = 128;
@@ -130,28 +132,22 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* map, int32_t 
       : "memory");
 }
 
-// 32 lanes x 64 columns of f32 from TMEM (lane quarter of this warp).
-__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
-  uint32_t r[64];
+// 32 lanes x 32 columns of f32 from TMEM (lane quarter of this warp).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
-      "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
-      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
         "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
         "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]),
-        "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]),
-        "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]),
-        "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]),
-        "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr)
       : "memory");
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // ---- dequantization to f16 pairs ----
@@ -277,7 +273,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&s->raw_empty[i], 1);
     }
     for (int i = 0; i < kAStages; ++i) {
-      mbar_init(&s->a_full[i], 4);
+      mbar_init(&s->a_full[i], kDequantWarps);
       mbar_init(&s->a_empty[i], 1);
     }
     mbar_init(&s->acc_full, 1);
@@ -346,7 +342,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     // ---- dequantize, then epilogue ----
-    const uint32_t r = (warp - 2) * 32 + lane;  // row of the tile this thread dequantizes
+    const uint32_t t = (warp - 2) * 32 + lane;
+    const uint32_t r = t % kTileM;   // row of the tile
+    const uint32_t half = t / kTileM;  // which four of the block's eight 8-value chunks
     for (uint32_t i = 0; i < nkb && ok; ++i) {
       const uint32_t st = i % kRawStages;
       const uint32_t at = i % kAStages;
@@ -361,26 +359,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t kb = kb0 + i;
       const uint16_t sb = *reinterpret_cast<const uint16_t*>(s->scales[st] + r * 16 + ((kb * 2u) & 15u));
       const uint32_t sc = static_cast<uint32_t>(sb) * 0x10001u;
-      uint8_t* ahi = s->a16[at][0] + r * 16;
-      uint8_t* alo = s->a16[at][1] + r * 16;
+      uint8_t* ahi = s->a16[at][0] + r * 16 + half * 4 * 2048;
+      uint8_t* alo = s->a16[at][1] + r * 16 + half * 4 * 2048;
       uint4 hi, lo;
       if (q4) {
-        const uint4* src = reinterpret_cast<const uint4*>(s->codes[st] + r * (kKBlock / 2));
+        const uint4 w = *reinterpret_cast<const uint4*>(s->codes[st] + r * (kKBlock / 2) + half * 16);
+        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const uint4 w = src[q];
-          const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            dequant_q4_word(words[t], sc, hi, lo);
-            *reinterpret_cast<uint4*>(ahi + (4 * q + t) * 2048) = hi;
-            *reinterpret_cast<uint4*>(alo + (4 * q + t) * 2048) = lo;
-          }
+        for (int c = 0; c < 4; ++c) {
+          dequant_q4_word(words[c], sc, hi, lo);
+          *reinterpret_cast<uint4*>(ahi + c * 2048) = hi;
+          *reinterpret_cast<uint4*>(alo + c * 2048) = lo;
         }
       } else {
-        const uint4* src = reinterpret_cast<const uint4*>(s->codes[st] + r * kKBlock);
+        const uint4* src = reinterpret_cast<const uint4*>(s->codes[st] + r * kKBlock + half * 32);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < 2; ++q) {
           const uint4 w = src[q];
           dequant_q8_words(w.x, w.y, sc, hi, lo);
           *reinterpret_cast<uint4*>(ahi + (2 * q + 0) * 2048) = hi;
@@ -395,23 +389,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&s->a_full[at]);
     }
-    // Epilogue: TMEM lane = tile row; this warp may read lanes 32 * (warp % 4) + [0, 32).
+    // Epilogue: TMEM lane = tile row; a warp may read lanes 32 * (warp % 4) +
+    // [0, 32). The two warps of a quarter take streams [0, 32) and [32, 64):
+    // columns n (x hi) and 64 + n (x lo).
     bool go = ok && nkb > 0 && wait_bounded(&s->acc_full, 0, p, 60);
     go = __all_sync(0xffffffffu, go);  // tcgen05.ld is warp-collective
     if (go) {
       tc_fence_after();
       const uint32_t quarter = static_cast<uint32_t>(warp % 4);
-      float v[64], vlo[64];
-      tmem_ld64(tmem + ((quarter * 32u) << 16), v);
-      tmem_ld64(tmem + ((quarter * 32u) << 16) + kStreamCols, vlo);
-#pragma unroll
-      for (int n = 0; n < 64; ++n) v[n] += vlo[n];  // x_hi and x_lo columns
+      const uint32_t n0 = ((warp - 2) / 4) * 32;
+      float v[32], vlo[32];
+      tmem_ld32(tmem + ((quarter * 32u) << 16) + n0, v);
+      tmem_ld32(tmem + ((quarter * 32u) << 16) + kStreamCols + n0, vlo);
       const uint32_t row = m0 + quarter * 32 + lane;
       if (row < job.rows) {
         float* out = p.out + size_t(blockIdx.y) * p.streams * p.out_ld + job.out_offset + row;
 #pragma unroll
-        for (int n = 0; n < 64; ++n) {
-          if (n < static_cast<int>(p.streams)) out[size_t(n) * p.out_ld] = v[n];
+        for (int n = 0; n < 32; ++n) {
+          if (n0 + n < p.streams) out[size_t(n0 + n) * p.out_ld] = v[n] + vlo[n];
         }
       }
     }

@@ -33,22 +33,11 @@
 namespace qwc {
 namespace {
 
-constexpr int kNormThreads = 256;
-constexpr int kNormPer = kHiddenMax / kNormThreads;
+constexpr int kNormThreads = 512;
+constexpr int kNormPer4 = kHiddenMax / 4 / kNormThreads;  // float4 groups per thread
 
 // Position of element e (0..7) of a chunk in the activation layout.
 __device__ __forceinline__ uint32_t chunk_slot(uint32_t e) { return ((e & 3u) << 1) | (e >> 2); }
-
-__device__ __forceinline__ float block_sum_256(float v, float* red) {
-  v = warp_sum(v);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = v;
-  __syncthreads();
-  float t = 0.0f;
-#pragma unroll
-  for (int w = 0; w < 8; ++w) t += red[w];
-  __syncthreads();
-  return t;
-}
 
 // Writes 8 f32 values (K order k0..k0+7) as one 16-byte chunk of the
 // activation layout: f16 hi values at `dst`, the f16 remainders x - hi at
@@ -73,15 +62,18 @@ __device__ __forceinline__ void store_one(__half* dst, size_t lo_offset, float v
 }
 
 // ---- residual + RMSNorm -> f16 activations (decoder.zig:165-176, 256-262, 277-283) ----
+//
+// One CTA per slot; a thread owns float4 groups of the hidden vector, so the
+// loads of every split's partial are independent 16-byte loads.
 
 template <int kInput>
 __global__ void __launch_bounds__(kNormThreads) streams_norm_kernel(const StreamsStep P, const float* weight,
                                                                     const float* parts, uint32_t splits) {
   __shared__ float xs[kHiddenMax];
-  __shared__ float red[8];
+  __shared__ float red[kNormThreads / 32];
   const DevModel& m = *P.model;
   const uint32_t s = blockIdx.x;
-  const uint32_t hidden = m.hidden;
+  const uint32_t hidden = m.hidden, h4 = hidden / 4;
   __half* xb = static_cast<__half*>(P.xb_h) + size_t(s) * hidden;
   const SlotStep d = P.desc[s];
   const size_t lo = size_t(kMaxStreams) * hidden;
@@ -92,50 +84,80 @@ __global__ void __launch_bounds__(kNormThreads) streams_norm_kernel(const Stream
     }
     return;
   }
-  float* h = P.hidden + size_t(s) * hidden;
-  float v[kNormPer];
+  float4* h = reinterpret_cast<float4*>(P.hidden + size_t(s) * hidden);
+  float4 v[kNormPer4];
   float ss = 0.0f;
 #pragma unroll
-  for (int i = 0; i < kNormPer; ++i) {
-    const uint32_t k = threadIdx.x + i * kNormThreads;
-    float x = 0.0f;
-    if (k < hidden) {
+  for (int i = 0; i < kNormPer4; ++i) {
+    const uint32_t k4 = threadIdx.x + i * kNormThreads;
+    float4 x = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (k4 < h4) {
       if (kInput) {
         if (d.audio_row >= 0) {
-          x = P.audio[s][size_t(d.audio_row) * hidden + k];
+          x = reinterpret_cast<const float4*>(P.audio[s] + size_t(d.audio_row) * hidden)[k4];
         } else {
           // embeddingRow, quantized branch (decoder.zig:346-376, quant.zig:348-364).
           const DevMat& e = m.embed;
+          const uint32_t k = k4 * 4;
           const float scale = f16_bits_to_f32(
               reinterpret_cast<const uint16_t*>(e.scales + size_t(d.token) * e.scale_row)[k / kGroup]);
           const uint8_t* crow = e.codes + size_t(d.token) * e.code_row;
-          int code;
+          float c[4];
           if (e.format == kFormatQ4) {
-            const uint8_t b = crow[k / 2];
-            code = static_cast<int>((k & 1u) ? (b >> 4) : (b & 0x0F)) - 8;
+            const uint16_t b = *reinterpret_cast<const uint16_t*>(crow + k / 2);
+            c[0] = static_cast<float>(static_cast<int>(b & 0xF) - 8);
+            c[1] = static_cast<float>(static_cast<int>((b >> 4) & 0xF) - 8);
+            c[2] = static_cast<float>(static_cast<int>((b >> 8) & 0xF) - 8);
+            c[3] = static_cast<float>(static_cast<int>((b >> 12) & 0xF) - 8);
           } else {
-            code = static_cast<int>(crow[k]) - 128;
+            const uint32_t b = *reinterpret_cast<const uint32_t*>(crow + k);
+#pragma unroll
+            for (int t = 0; t < 4; ++t) c[t] = static_cast<float>(static_cast<int>((b >> (8 * t)) & 0xFF) - 128);
           }
-          x = static_cast<float>(code) * scale;
+          x = make_float4(c[0] * scale, c[1] * scale, c[2] * scale, c[3] * scale);
         }
       } else {
         // The projection is the sum of its split-K partials, then the
         // residual add (kernels.zig:221-230).
-        float y = parts[size_t(s) * hidden + k];
-        for (uint32_t sp = 1; sp < splits; ++sp) y += parts[(size_t(sp) * kMaxStreams + s) * hidden + k];
-        x = h[k] + y;
+        const float4* pp = reinterpret_cast<const float4*>(parts) + size_t(s) * h4 + k4;
+        const size_t stride = size_t(kMaxStreams) * h4;
+        float4 y = pp[0];
+#pragma unroll 4
+        for (uint32_t sp = 1; sp < splits; ++sp) {
+          const float4 t = pp[sp * stride];
+          y.x += t.x;
+          y.y += t.y;
+          y.z += t.z;
+          y.w += t.w;
+        }
+        const float4 r = h[k4];
+        x = make_float4(r.x + y.x, r.y + y.y, r.z + y.z, r.w + y.w);
       }
-      h[k] = x;
-      ss = fmaf(x, x, ss);
+      h[k4] = x;
+      ss = fmaf(x.x, x.x, ss);
+      ss = fmaf(x.y, x.y, ss);
+      ss = fmaf(x.z, x.z, ss);
+      ss = fmaf(x.w, x.w, ss);
     }
     v[i] = x;
   }
-  const float total = block_sum_256(ss, red);
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = ss;
+  __syncthreads();
+  float total = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kNormThreads / 32; ++w) total += red[w];
   const float inv = 1.0f / sqrtf(total / static_cast<float>(hidden) + m.eps);
 #pragma unroll
-  for (int i = 0; i < kNormPer; ++i) {
-    const uint32_t k = threadIdx.x + i * kNormThreads;
-    if (k < hidden) xs[k] = v[i] * inv * weight[k];
+  for (int i = 0; i < kNormPer4; ++i) {
+    const uint32_t k4 = threadIdx.x + i * kNormThreads;
+    if (k4 < h4) {
+      const float4 w = reinterpret_cast<const float4*>(weight)[k4];
+      xs[k4 * 4 + 0] = v[i].x * inv * w.x;
+      xs[k4 * 4 + 1] = v[i].y * inv * w.y;
+      xs[k4 * 4 + 2] = v[i].z * inv * w.z;
+      xs[k4 * 4 + 3] = v[i].w * inv * w.w;
+    }
   }
   __syncthreads();
   for (uint32_t c = threadIdx.x; c < hidden / 8; c += kNormThreads) {
