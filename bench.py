@@ -9,8 +9,14 @@ configs[2] of the benchmark definition: Qwen3-ASR-1.7B decoder, q4 weights
 (W + K = 448 by default). Weights (0.91 GB) exceed the 126 MB L2, so no flush
 is needed between steps.
 
+The same line carries a `streams64` object: configs[3] of the benchmark
+definition, 64 independent streams per GPU of the same model (prefixes
+uniform in [100, 1500] audio rows + 16 text ids, staggered so every prompt
+ends on the same step), timed over greedy steps of all 64 slots with the
+batched tensor-core step, with its own roofline and end-to-end figures.
+
 Under torchrun (N > 1) every rank holds a full weight replica and decodes its
-own independent stream (streams shard across GPUs with no exchange): value =
+own independent streams (streams shard across GPUs with no exchange): value =
 tokens of all ranks / the slowest rank's device time.
 
 `--impl reference` times the CPU restatement of the reference's Zig decode
@@ -47,6 +53,9 @@ def parse_args():
     p.add_argument("--workload", default="cfg2_1p7b_q4_b1")
     p.add_argument("--chunk", type=int, default=64, help="decode steps per device launch")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--streams-workload", default="cfg3_1p7b_q4_s64",
+                   help="multi-stream workload measured beside the main one ('none' to skip)")
+    p.add_argument("--streams-steps", type=int, default=200)
     return p.parse_args()
 
 
@@ -184,6 +193,98 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
+def streams_bytes(model, positions: list[int], steps: int) -> float:
+    """Algorithmic bytes of `steps` batched steps: every weight payload once
+    per step (shared by all slots), the norm vectors, and per slot its
+    embedding row, its (position + 1) q8 KV rows read and the row written."""
+    c = model.config
+    weights = sum(t.payload.nbytes for t in model.tensors if t.fmt != 0)
+    norms = sum(t.payload.nbytes for t in model.tensors if t.fmt == 0)
+    embed_row = c.text_hidden_size // 64 * (2 + (32 if model.fmt == 16 else 64))
+    per_pos = c.text_layers * 2 * (c.kv_width + c.kv_width // 64 * 2)
+    total = 0.0
+    for i in range(steps):
+        total += weights + norms
+        for p0 in positions:
+            p = p0 + i
+            total += embed_row + (p + 1) * per_pos + per_pos
+    return total
+
+
+def measure_streams(args, model, w, rank, local_rank, barrier, world):
+    """The multi-stream workload on this rank's GPU: slots begin staggered so
+    that every prompt ends on the same step, then `streams_steps` greedy steps
+    of all slots are timed on the device (qwc_streams_run_timed), then 32 steps
+    through qwc_streams_step (host buffers each step) for the end-to-end figure."""
+    import dataclasses
+
+    import torch
+    import torch.distributed as dist
+
+    from qwenscriber_b200 import runtime as rt
+    from qwenscriber_b200 import synthetic
+
+    m = dataclasses.replace(model, config=w.config)
+    gm = rt.CudaModel(local_rank)
+    synthetic.load_into(m, gm, cache_format=rt.CACHE_Q8, streams=w.streams)
+    gm.set_option(rt.OPTION_IGNORE_EOS, 1)
+    lengths = synthetic.prefix_lengths(w)
+    prompts = [synthetic.make_prompt(w.config, lengths[s], w.text_ids, w.seed + 1000 * rank, stream=s)
+               for s in range(w.streams)]
+    plen = [len(p.tokens) for p in prompts]
+    pmax = max(plen)
+    warm, e2e_steps = 4, 32
+    steps = min(args.streams_steps, w.decode - 1 - warm - e2e_steps)
+    starts: dict[int, list[int]] = {}
+    for s in range(w.streams):
+        starts.setdefault(pmax - plen[s], []).append(s)
+    t0 = time.perf_counter()
+    for step in range(pmax):
+        for s in starts.get(step, []):
+            gm.stream_begin(s, prompts[s].tokens, prompts[s].audio, w.decode)
+        gm.streams_step(w.streams)
+    prefill_s = time.perf_counter() - t0
+    gm.streams_run_timed(warm)
+    positions = [pmax + warm] * w.streams  # every slot: prompt + first token + warm-up steps filled
+    barrier()
+    launches0 = gm.launches()
+    with ClockSampler(local_rank) as clocks:
+        ms = gm.streams_run_timed(steps)
+    launches = gm.launches() - launches0
+    barrier()
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        gm.streams_step(w.streams)
+    e2e_s = time.perf_counter() - t0
+    barrier()
+    if world > 1:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    gm.close()
+    tokens = steps * w.streams * world
+    bytes_total = streams_bytes(m, positions, steps)
+    peak, peak_kind = measured_peak()
+    achieved = bytes_total / (ms / 1000.0) / 1e9
+    return {
+        "workload": w.name, "streams_per_gpu": w.streams, "value": tokens / (ms / 1000.0), "unit": "tokens/s",
+        "ms_per_step": ms / steps, "steps": steps, "warmup": warm,
+        "prompt": f"{w.text_ids} text ids after U[{w.audio_rows[0]}, {w.audio_rows[1]}] audio rows per stream; "
+                  f"slots begin staggered so all prompts end together ({pmax} positions, {prefill_s:.1f} s)",
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_kind": peak_kind, "bytes_per_step": bytes_total / steps},
+        "e2e": {"value": e2e_steps * w.streams * world / e2e_s, "unit": "tokens/s",
+                "h2d_bytes_per_step": 64 * 16, "d2h_bytes_per_step": 64 * 4 + 16,
+                "includes": "qwc_streams_step: slot descriptors up, one graph replay, tokens down, per step"},
+        "gpu_launches": launches, "clocks": clocks.summary(),
+    }
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -241,6 +342,11 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
 
+    streams = None
+    if args.streams_workload != "none":
+        streams = measure_streams(args, model, synthetic.workloads()[args.streams_workload], rank, local_rank,
+                                  barrier, world)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
@@ -270,6 +376,7 @@ def run_ours(args, rank, world, local_rank):
             "gpu_launches": launches,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
+            "streams64": streams,
         }
         print(json.dumps(line), flush=True)
     gm.close()
