@@ -109,7 +109,11 @@ enum {
   QWC_OPTION_STEP_CHUNK = 3,
   /* Nonzero: every launch records a phase timeline of its first step
    * (%globaltimer per CTA at each phase boundary); see qwc_debug_trace. */
-  QWC_OPTION_TRACE = 4
+  QWC_OPTION_TRACE = 4,
+  /* Prompt prefill of single-stream handles: 0 (default) batched on the
+   * tensor cores, 64 positions per step; 1 token by token through the
+   * persistent decode kernel. */
+  QWC_OPTION_PREFILL_SERIAL = 5
 };
 
 /* ---- version and lifecycle (src/wasm/exports.zig:49-120) ---- */
@@ -166,17 +170,19 @@ int32_t qwc_decode_end(uint32_t handle);
 /* ---- multi-stream family: independent streams batched per device step ----
  * With qwc_model_set_streams(n), 2 <= n <= 64, every step runs all slots
  * together (projections on the tensor cores with the slots as GEMM columns,
- * as in qwc_op_gemm_streams). A slot
- * begun with qwc_stream_begin consumes its prompt one position per
- * qwc_streams_step; results[slot] is then 2 until the prompt's last position,
- * which yields the slot's first token (1). The stop rule is the reference's.
- * The qwc_decode_* family is for single-stream handles. */
+ * as in qwc_op_gemm_streams). qwc_stream_begin prefills the slot's prompt
+ * (64 positions per tensor-core step) and holds its first prediction, as
+ * qw_decode_begin does; each qwc_streams_step then emits every decoding
+ * slot's held token and computes the next (decodeStep, model.zig:423-451).
+ * The qwc_decode_* family is for single-stream handles, whose prompts are
+ * prefilled the same way. */
 
 int32_t qwc_stream_begin(uint32_t handle, uint32_t slot, const uint32_t* prompt, uint32_t prompt_len,
                          const float* audio, uint32_t audio_steps, uint32_t max_tokens);
 /* Advances every decoding slot by one token. results[slot]: 1 token written
- * to tokens_out[slot], 0 finished or idle, <0 status. Returns the number of
- * tokens produced, or <0 status. Both arrays hold `streams` entries. */
+ * to tokens_out[slot], 0 finished or idle, <0 status of that slot
+ * (QWC_LIMIT_EXCEEDED at max_positions). Returns the number of tokens
+ * produced, or <0 status. Both arrays hold `streams` entries. */
 int32_t qwc_streams_step(uint32_t handle, uint32_t* tokens_out, int32_t* results);
 int32_t qwc_stream_tokens(uint32_t handle, uint32_t slot, uint32_t* out, uint32_t capacity);
 int32_t qwc_stream_end(uint32_t handle, uint32_t slot);

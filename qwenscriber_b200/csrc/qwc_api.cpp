@@ -211,12 +211,9 @@ struct StreamSlot {
   uint32_t max_tokens = 0;
   std::vector<uint32_t> generated;
   std::deque<uint32_t> ahead;    // predictions computed beyond next_token
-  // Batched mode: the prompt is consumed one position per step.
-  std::vector<uint32_t> prompt;
-  std::vector<int32_t> rows;     // audio row per prompt position, or -1
-  uint32_t prompt_pos = 0;
-  uint32_t last_token = 0;       // next input once the prompt is consumed
-  std::unique_ptr<DevBuf> audio;
+  std::unique_ptr<DevBuf> audio;  // the prompt's audio rows (device)
+  bool logits_batched = false;     // the last logits of this slot come from the batched step
+  uint32_t logits_col = 0;         // ... in this column of its logits buffer
 };
 
 // TMA descriptors of one weight matrix for the stream GEMM.
@@ -263,6 +260,7 @@ struct Handle {
   bool ignore_eos = false;
   bool keep_logits = false;
   bool trace = false;
+  bool prefill_serial = false;  // QWC_OPTION_PREFILL_SERIAL
   uint32_t step_chunk = 16;
   uint64_t launches = 0;
   std::map<std::pair<uint32_t, uint32_t>, Tensor> tensors;
@@ -548,7 +546,9 @@ int32_t finish_model(Handle* h, const Config& c) {
   h->slots.clear();
   h->slots.resize(h->streams);
   h->config = c;
-  if (h->streams > 1) QWC_TRY(build_batched(h));
+  // Every handle gets the batched engine: it runs the prompt prefills (64
+  // positions per step) and, with streams > 1, the batched decode steps.
+  QWC_TRY(build_batched(h));
   return QWC_OK;
 }
 
@@ -797,34 +797,10 @@ int32_t build_batched(Handle* h) {
   return QWC_OK;
 }
 
-// One batched step: every decoding slot consumes its next prompt position or
-// its last token. results[slot]: 1 token emitted, 2 prompt position consumed
-// (no token yet), 0 idle or finished.
-int32_t batched_step(Handle* h, uint32_t* tokens_out, int32_t* results) {
+// Runs the captured step once for the columns in b.host_desc and reads the
+// argmax of every column back.
+int32_t run_batched(Handle* h) {
   Batched& b = *h->batched;
-  const Config& c = h->config;
-  const uint32_t n = static_cast<uint32_t>(h->slots.size());
-  bool any = false;
-  for (uint32_t slot = 0; slot < kMaxStreams; ++slot) {
-    SlotStep d{0, 0, 0, -1};
-    if (slot < n) {
-      StreamSlot& s = h->slots[slot];
-      results[slot] = 0;
-      if (s.decoding && !s.finished) {
-        if (s.position >= c.max_positions) {
-          s.finished = true;  // PositionExceeded (decoder.zig:142)
-          results[slot] = QWC_LIMIT_EXCEEDED;
-        } else if (s.prompt_pos < s.prompt.size()) {
-          d = SlotStep{1, s.position, static_cast<int32_t>(s.prompt[s.prompt_pos]), s.rows[s.prompt_pos]};
-        } else {
-          d = SlotStep{1, s.position, static_cast<int32_t>(s.last_token), -1};
-        }
-      }
-    }
-    b.host_desc[slot] = d;
-    any = any || d.active;
-  }
-  if (!any) return 0;
   cudaStream_t st = h->stream;
   QWC_CUDA(cudaMemcpyAsync(b.desc.ptr, b.host_desc, kMaxStreams * sizeof(SlotStep), cudaMemcpyHostToDevice, st));
   QWC_CUDA(cudaGraphLaunch(b.exec, st));
@@ -841,48 +817,97 @@ int32_t batched_step(Handle* h, uint32_t* tokens_out, int32_t* results) {
     cudaStreamSynchronize(st);
     return QWC_INVALID_STATE;
   }
+  return QWC_OK;
+}
+
+// Decoder.prefill (decoder.zig:308-333) of one stream in 64-position steps:
+// the columns of a step are consecutive positions of the stream, sharing its
+// cache. Returns the prediction after the prompt's last position.
+int32_t batched_prefill(Handle* h, uint32_t slot, const uint32_t* prompt, const std::vector<int32_t>& rows,
+                        uint32_t prompt_len, uint32_t* next_out, uint32_t* column_out) {
+  Batched& b = *h->batched;
+  uint32_t last_col = 0;
+  for (uint32_t c0 = 0; c0 < prompt_len; c0 += kMaxStreams) {
+    const uint32_t n = std::min<uint32_t>(kMaxStreams, prompt_len - c0);
+    for (uint32_t i = 0; i < kMaxStreams; ++i) {
+      b.host_desc[i] = i < n ? SlotStep{1, c0 + i, static_cast<int32_t>(prompt[c0 + i]), rows[c0 + i],
+                                        static_cast<int32_t>(slot), {0, 0, 0}}
+                             : SlotStep{0, 0, 0, -1, 0, {0, 0, 0}};
+    }
+    QWC_TRY(run_batched(h));
+    last_col = n - 1;
+  }
+  *next_out = b.host_tokens[last_col];
+  *column_out = last_col;
+  return QWC_OK;
+}
+
+// One batched decode step (streams > 1), the reference's decodeStep per slot
+// (src/wasm/model.zig:423-451): each decoding slot emits its held token
+// unless it ends the sequence, then the held token is fed through the step
+// to predict the next. results[slot]: 1 token emitted, 0 finished or idle.
+int32_t batched_step(Handle* h, uint32_t* tokens_out, int32_t* results) {
+  Batched& b = *h->batched;
+  const Config& c = h->config;
+  const uint32_t n = static_cast<uint32_t>(h->slots.size());
+  bool any = false;
   int32_t produced = 0;
+  for (uint32_t slot = 0; slot < kMaxStreams; ++slot) {
+    SlotStep d{0, 0, 0, -1, 0, {0, 0, 0}};
+    if (slot < n) {
+      StreamSlot& s = h->slots[slot];
+      results[slot] = 0;
+      if (s.decoding && !s.finished) {
+        const uint32_t t = s.next_token;
+        if (!h->ignore_eos && ends_sequence(c, t)) {
+          s.finished = true;  // EOS ends the stream and is not emitted
+        } else {
+          tokens_out[slot] = t;
+          s.generated.push_back(t);
+          results[slot] = 1;
+          ++produced;
+          if (s.generated.size() >= s.max_tokens) {
+            s.finished = true;
+          } else if (s.position >= c.max_positions) {
+            results[slot] = QWC_LIMIT_EXCEEDED;  // PositionExceeded (decoder.zig:142)
+            s.finished = true;
+          } else {
+            d = SlotStep{1, s.position, static_cast<int32_t>(t), -1, static_cast<int32_t>(slot), {0, 0, 0}};
+          }
+        }
+      }
+    }
+    b.host_desc[slot] = d;
+    any = any || d.active;
+  }
+  if (!any) return produced;
+  QWC_TRY(run_batched(h));
   for (uint32_t slot = 0; slot < n; ++slot) {
     if (!b.host_desc[slot].active) continue;
     StreamSlot& s = h->slots[slot];
     s.position += 1;
-    if (s.prompt_pos < s.prompt.size()) {
-      s.prompt_pos += 1;
-      if (s.prompt_pos < s.prompt.size()) {
-        results[slot] = 2;
-        continue;
-      }
-    }
-    const uint32_t token = b.host_tokens[slot];
-    if (!h->ignore_eos && ends_sequence(c, token)) {  // model.zig:423-451: EOS ends the stream, not emitted
-      s.finished = true;
-      continue;
-    }
-    tokens_out[slot] = token;
-    s.generated.push_back(token);
-    s.last_token = token;
-    results[slot] = 1;
-    ++produced;
-    if (s.generated.size() >= s.max_tokens) s.finished = true;
+    s.next_token = b.host_tokens[slot];
+    s.logits_batched = true;
+    s.logits_col = slot;
   }
   return produced;
 }
 
-// `steps` device-chained steps of every active slot (all past their
-// prompts), timed with CUDA events; the tokens are appended afterwards.
+// `steps` device-chained decode steps of every decoding slot (streams > 1),
+// timed with CUDA events: as `steps` qwc_streams_step calls without the stop
+// rule, with the emitted tokens appended afterwards.
 int32_t batched_run_timed(Handle* h, uint32_t steps, float* device_ms) {
   Batched& b = *h->batched;
   const uint32_t n = static_cast<uint32_t>(h->slots.size());
   bool any = false;
   for (uint32_t slot = 0; slot < kMaxStreams; ++slot) {
-    SlotStep d{0, 0, 0, -1};
+    SlotStep d{0, 0, 0, -1, 0, {0, 0, 0}};
     if (slot < n) {
       StreamSlot& s = h->slots[slot];
       if (s.decoding && !s.finished) {
-        if (s.prompt_pos < s.prompt.size()) return QWC_INVALID_STATE;  // prompts must be consumed first
         if (s.position + steps > h->config.max_positions) return QWC_LIMIT_EXCEEDED;
         if (s.generated.size() + steps > s.max_tokens) return QWC_LIMIT_EXCEEDED;
-        d = SlotStep{1, s.position, static_cast<int32_t>(s.last_token), -1};
+        d = SlotStep{1, s.position, static_cast<int32_t>(s.next_token), -1, static_cast<int32_t>(slot), {0, 0, 0}};
       }
     }
     b.host_desc[slot] = d;
@@ -903,7 +928,7 @@ int32_t batched_run_timed(Handle* h, uint32_t steps, float* device_ms) {
   if (le == cudaSuccess) {
     le = cudaMemcpyAsync(hist.data(), b.history.ptr, hist.size() * 4, cudaMemcpyDeviceToHost, st);
   }
-  if (le == cudaSuccess) le = cudaMemcpyAsync(b.host_err, b.err.ptr, 4, cudaMemcpyDeviceToHost, st);
+  if (le == cudaSuccess) le = cudaMemcpyAsync(b.host_err, b.err.ptr, 16, cudaMemcpyDeviceToHost, st);
   if (le == cudaSuccess) le = cudaStreamSynchronize(st);
   float ms = 0.0f;
   if (le == cudaSuccess) cudaEventElapsedTime(&ms, e0, e1);
@@ -912,7 +937,7 @@ int32_t batched_run_timed(Handle* h, uint32_t steps, float* device_ms) {
   if (le != cudaSuccess) return status_of(le);
   h->launches += uint64_t(b.kernels_per_step) * steps;
   if (*b.host_err != 0) {
-    cudaMemsetAsync(b.err.ptr, 0, 4, st);
+    cudaMemsetAsync(b.err.ptr, 0, 16, st);
     cudaStreamSynchronize(st);
     return QWC_INVALID_STATE;
   }
@@ -920,11 +945,12 @@ int32_t batched_run_timed(Handle* h, uint32_t steps, float* device_ms) {
     if (!b.host_desc[slot].active) continue;
     StreamSlot& s = h->slots[slot];
     for (uint32_t i = 0; i < steps; ++i) {
-      const uint32_t t = hist[size_t(i) * kMaxStreams + slot];
-      s.generated.push_back(t);
-      s.last_token = t;
+      s.generated.push_back(s.next_token);
+      s.next_token = hist[size_t(i) * kMaxStreams + slot];
     }
     s.position += steps;
+    s.logits_batched = true;
+    s.logits_col = slot;
     if (s.generated.size() >= s.max_tokens) s.finished = true;
   }
   *device_ms = ms;
@@ -955,49 +981,44 @@ int32_t stream_begin(Handle* h, uint32_t slot, const uint32_t* prompt, uint32_t 
   }
   if (audio_index != audio_steps) return QWC_SHAPE_MISMATCH;  // decoder.zig:331
   cudaSetDevice(h->device);
-  if (h->batched) {
-    // Batched mode: the prompt is consumed by later qwc_streams_step calls,
-    // one position per step, alongside the other slots.
-    const uint64_t stride = h->host_model.cache_stream_stride;
-    QWC_CUDA(cudaMemsetAsync(h->k_cache.as<uint8_t>() + stride * slot, 0, stride, h->stream));
-    QWC_CUDA(cudaMemsetAsync(h->v_cache.as<uint8_t>() + stride * slot, 0, stride, h->stream));
-    s = StreamSlot{};
-    const float* dev_audio = nullptr;
-    if (audio_steps) {
-      s.audio = std::make_unique<DevBuf>();
-      QWC_TRY(s.audio->alloc(size_t(audio_steps) * c.text_hidden_size * 4));
-      QWC_CUDA(cudaMemcpyAsync(s.audio->ptr, audio, s.audio->bytes, cudaMemcpyHostToDevice, h->stream));
-      dev_audio = s.audio->as<float>();
-    }
-    QWC_CUDA(cudaMemcpyAsync(h->batched->audio_ptrs.as<const float*>() + slot, &dev_audio, sizeof(dev_audio),
-                             cudaMemcpyHostToDevice, h->stream));
-    QWC_CUDA(cudaStreamSynchronize(h->stream));
-    s.prompt.assign(prompt, prompt + prompt_len);
-    s.rows = std::move(rows);
-    s.decoding = true;
-    s.max_tokens = max_tokens;
-    s.generated.reserve(max_tokens);
-    return QWC_OK;
-  }
-  if (slot != 0) return QWC_UNSUPPORTED;
-  // Decoder.reset (decoder.zig:109-121): the whole cache goes back to zero.
+  // Decoder.reset (decoder.zig:109-121): the slot's cache goes back to zero.
   const uint64_t stride = h->host_model.cache_stream_stride;
   QWC_CUDA(cudaMemsetAsync(h->k_cache.as<uint8_t>() + stride * slot, 0, stride, h->stream));
   QWC_CUDA(cudaMemsetAsync(h->v_cache.as<uint8_t>() + stride * slot, 0, stride, h->stream));
-  QWC_CUDA(cudaMemcpyAsync(h->prompt_ids.ptr, prompt, size_t(prompt_len) * 4, cudaMemcpyHostToDevice, h->stream));
-  QWC_CUDA(cudaMemcpyAsync(h->prompt_rows.ptr, rows.data(), size_t(prompt_len) * 4, cudaMemcpyHostToDevice, h->stream));
-  if (audio_steps) {
-    QWC_CUDA(cudaMemcpyAsync(h->audio_rows.ptr, audio, size_t(audio_steps) * c.text_hidden_size * 4,
-                             cudaMemcpyHostToDevice, h->stream));
-  }
-  std::vector<uint32_t> tokens;
-  QWC_TRY(run_decode(h, prompt_len, 0, prompt_len, 0, prompt_len - 1, &tokens));
   s = StreamSlot{};
+  const float* dev_audio = nullptr;
+  if (audio_steps) {
+    s.audio = std::make_unique<DevBuf>();
+    QWC_TRY(s.audio->alloc(size_t(audio_steps) * c.text_hidden_size * 4));
+    QWC_CUDA(cudaMemcpyAsync(s.audio->ptr, audio, s.audio->bytes, cudaMemcpyHostToDevice, h->stream));
+    dev_audio = s.audio->as<float>();
+  }
+  QWC_CUDA(cudaMemcpyAsync(h->batched->audio_ptrs.as<const float*>() + slot, &dev_audio, sizeof(dev_audio),
+                           cudaMemcpyHostToDevice, h->stream));
+  QWC_CUDA(cudaStreamSynchronize(h->stream));
+  uint32_t next = 0, col = 0;
+  if (h->prefill_serial && h->streams == 1) {
+    // Token by token through the persistent kernel (decoder.zig:308-333 as written).
+    QWC_CUDA(cudaMemcpyAsync(h->prompt_ids.ptr, prompt, size_t(prompt_len) * 4, cudaMemcpyHostToDevice, h->stream));
+    QWC_CUDA(cudaMemcpyAsync(h->prompt_rows.ptr, rows.data(), size_t(prompt_len) * 4, cudaMemcpyHostToDevice,
+                             h->stream));
+    if (audio_steps) {
+      QWC_CUDA(cudaMemcpyAsync(h->audio_rows.ptr, audio, size_t(audio_steps) * c.text_hidden_size * 4,
+                               cudaMemcpyHostToDevice, h->stream));
+    }
+    std::vector<uint32_t> tokens;
+    QWC_TRY(run_decode(h, prompt_len, 0, prompt_len, 0, prompt_len - 1, &tokens));
+    next = tokens[prompt_len - 1];
+  } else {
+    QWC_TRY(batched_prefill(h, slot, prompt, rows, prompt_len, &next, &col));
+  }
   s.decoding = true;
   s.position = prompt_len;
-  s.next_token = tokens[prompt_len - 1];
+  s.next_token = next;
   s.max_tokens = max_tokens;
   s.generated.reserve(max_tokens);
+  s.logits_batched = !(h->prefill_serial && h->streams == 1);
+  s.logits_col = col;
   return QWC_OK;
 }
 
@@ -1014,6 +1035,7 @@ int32_t advance(Handle* h, StreamSlot& s, uint32_t token, uint32_t budget) {
     QWC_TRY(run_decode(h, n, s.position, 0, token, 0, &tokens));
     for (uint32_t i = 0; i < n; ++i) s.ahead.push_back(tokens[i]);
     s.position += n;
+    s.logits_batched = false;
   }
   s.next_token = s.ahead.front();
   s.ahead.pop_front();
@@ -1023,7 +1045,7 @@ int32_t advance(Handle* h, StreamSlot& s, uint32_t token, uint32_t budget) {
 // src/wasm/model.zig:423-451
 int32_t stream_step(Handle* h, uint32_t slot, uint32_t* token_out) {
   if (h->state != State::kLoaded || slot >= h->slots.size()) return QWC_INVALID_STATE;
-  if (h->batched) return QWC_UNSUPPORTED;  // batched handles advance with qwc_streams_step
+  if (h->streams > 1) return QWC_UNSUPPORTED;  // multi-stream handles advance with qwc_streams_step
   StreamSlot& s = h->slots[slot];
   if (!s.decoding) return QWC_INVALID_STATE;
   if (s.finished) return 0;
@@ -1117,6 +1139,7 @@ int32_t qwc_set_option(uint32_t handle, uint32_t option, uint32_t value) {
     case QWC_OPTION_IGNORE_EOS: h->ignore_eos = value != 0; return QWC_OK;
     case QWC_OPTION_KEEP_LOGITS: h->keep_logits = value != 0; return QWC_OK;
     case QWC_OPTION_TRACE: h->trace = value != 0; return QWC_OK;
+    case QWC_OPTION_PREFILL_SERIAL: h->prefill_serial = value != 0; return QWC_OK;
     case QWC_OPTION_STEP_CHUNK:
       if (value == 0 || value > 256) return QWC_INVALID_ARGUMENT;
       h->step_chunk = value;
@@ -1254,7 +1277,7 @@ int32_t qwc_decode_begin(uint32_t handle, const uint32_t* prompt, uint32_t promp
                          uint32_t audio_steps, uint32_t max_tokens) {
   Handle* h = lookup(handle);
   if (!h) return QWC_INVALID_ARGUMENT;
-  if (h->batched) return QWC_UNSUPPORTED;  // the stream family drives batched handles
+  if (h->streams > 1) return QWC_UNSUPPORTED;  // the stream family drives multi-stream handles
   return stream_begin(h, 0, prompt, prompt_len, audio, audio_steps, max_tokens);
 }
 
@@ -1288,7 +1311,7 @@ int32_t qwc_stream_end(uint32_t handle, uint32_t slot) {
   const uint64_t stride = h->host_model.cache_stream_stride;
   QWC_CUDA(cudaMemsetAsync(h->k_cache.as<uint8_t>() + stride * slot, 0, stride, h->stream));
   QWC_CUDA(cudaMemsetAsync(h->v_cache.as<uint8_t>() + stride * slot, 0, stride, h->stream));
-  if (h->batched) {
+  {
     const float* none = nullptr;
     QWC_CUDA(cudaMemcpyAsync(h->batched->audio_ptrs.as<const float*>() + slot, &none, sizeof(none),
                              cudaMemcpyHostToDevice, h->stream));
@@ -1312,7 +1335,7 @@ int32_t qwc_streams_step(uint32_t handle, uint32_t* tokens_out, int32_t* results
   if (!h || !tokens_out || !results) return QWC_INVALID_ARGUMENT;
   if (h->state != State::kLoaded) return QWC_INVALID_STATE;
   cudaSetDevice(h->device);
-  if (h->batched) return batched_step(h, tokens_out, results);
+  if (h->streams > 1) return batched_step(h, tokens_out, results);
   int32_t produced = 0;
   for (uint32_t slot = 0; slot < h->slots.size(); ++slot) {
     if (!h->slots[slot].decoding) {
@@ -1330,7 +1353,7 @@ int32_t qwc_streams_step(uint32_t handle, uint32_t* tokens_out, int32_t* results
 int32_t qwc_streams_run_timed(uint32_t handle, uint32_t steps, float* device_ms) {
   Handle* h = lookup(handle);
   if (!h || !device_ms) return QWC_INVALID_ARGUMENT;
-  if (h->state != State::kLoaded || !h->batched) return QWC_INVALID_STATE;
+  if (h->state != State::kLoaded || h->streams < 2) return QWC_INVALID_STATE;
   cudaSetDevice(h->device);
   return batched_run_timed(h, steps, device_ms);
 }
@@ -1382,8 +1405,8 @@ int32_t qwc_debug_logits(uint32_t handle, uint32_t slot, float* out, uint32_t co
   if (h->state != State::kLoaded || slot >= h->slots.size()) return QWC_INVALID_STATE;
   if (count < h->config.vocab_size) return QWC_LIMIT_EXCEEDED;
   cudaSetDevice(h->device);
-  if (h->batched) {
-    const float* row = h->batched->logits.as<float>() + size_t(slot) * h->config.vocab_size;
+  if (h->slots[slot].logits_batched) {
+    const float* row = h->batched->logits.as<float>() + size_t(h->slots[slot].logits_col) * h->config.vocab_size;
     QWC_CUDA(cudaMemcpyAsync(out, row, size_t(h->config.vocab_size) * 4, cudaMemcpyDeviceToHost, h->stream));
     QWC_CUDA(cudaStreamSynchronize(h->stream));
     return QWC_OK;
@@ -1399,17 +1422,6 @@ int32_t qwc_debug_hold(uint32_t handle, uint32_t slot, int64_t force, uint32_t* 
   if (!h || !held_out) return QWC_INVALID_ARGUMENT;
   if (h->state != State::kLoaded || slot >= h->slots.size() || !h->slots[slot].decoding) return QWC_INVALID_STATE;
   StreamSlot& s = h->slots[slot];
-  if (h->batched) {
-    // The next input of a slot past its prompt: its last emitted token.
-    if (s.prompt_pos < s.prompt.size() || s.generated.empty()) return QWC_INVALID_STATE;
-    if (force >= 0) {
-      if (static_cast<uint64_t>(force) >= h->config.vocab_size) return QWC_INVALID_ARGUMENT;
-      s.last_token = static_cast<uint32_t>(force);
-      s.generated.back() = s.last_token;
-    }
-    *held_out = s.last_token;
-    return QWC_OK;
-  }
   if (force >= 0) {
     if (!s.ahead.empty()) return QWC_INVALID_STATE;
     if (static_cast<uint64_t>(force) >= h->config.vocab_size) return QWC_INVALID_ARGUMENT;

@@ -135,13 +135,18 @@ int decode_grid_size(int device);
 
 constexpr uint32_t kMaxStreams = 64;  // stream columns of the tensor-core GEMM
 
-// What one slot does in the next batched step: consume `token` (embedding
-// row) or, when `audio_row` >= 0, that row of the slot's audio, at `position`.
+// What one GEMM column does in the next batched step: consume `token`
+// (embedding row) or, when `audio_row` >= 0, that row of the stream's audio,
+// at `position` of the stream whose cache is slot `cache`. Decode steps use
+// one column per stream; a prefill uses up to 64 columns of one stream
+// (consecutive positions, causal through the shared cache).
 struct SlotStep {
   int32_t active;
   uint32_t position;
   int32_t token;
   int32_t audio_row;
+  int32_t cache;
+  int32_t pad[3];
 };
 
 // Device buffers and shapes shared by the step's kernels. All [slot] arrays

@@ -94,7 +94,7 @@ __global__ void __launch_bounds__(kNormThreads) streams_norm_kernel(const Stream
     if (k4 < h4) {
       if (kInput) {
         if (d.audio_row >= 0) {
-          x = reinterpret_cast<const float4*>(P.audio[s] + size_t(d.audio_row) * hidden)[k4];
+          x = reinterpret_cast<const float4*>(P.audio[d.cache] + size_t(d.audio_row) * hidden)[k4];
         } else {
           // embeddingRow, quantized branch (decoder.zig:346-376, quant.zig:348-364).
           const DevMat& e = m.embed;
@@ -226,7 +226,8 @@ __global__ void __launch_bounds__(256) streams_qkv_kernel(const StreamsStep P, u
   const float gmax = fmaxf(red[gw], red[gw + 1]);
   const __half sh = __float2half_rn(gmax / 128.0f);
   const uint8_t code = q8_code(val, __half2float(sh));
-  uint8_t* plane = (j == 0 ? P.k_cache : P.v_cache) + size_t(s) * m.cache_stream_stride + size_t(layer) * m.cache_layer_stride;
+  uint8_t* plane =
+      (j == 0 ? P.k_cache : P.v_cache) + size_t(d.cache) * m.cache_stream_stride + size_t(layer) * m.cache_layer_stride;
   plane[m.cache_scales_bytes + size_t(d.position) * kvw + h * kHeadDim + dd] = code;
   if ((dd % kGroup) == 0) {
     reinterpret_cast<uint16_t*>(plane + size_t(d.position) * (kvw / kGroup) * 2)[h * 2 + dd / kGroup] =
@@ -280,8 +281,9 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* map, int32_t 
       : "memory");
 }
 
+// Unit of column s (its stream's cache slot `cache`), kv head h, chunk ch.
 struct UnitPos {
-  uint32_t s, h, ch, chunks;
+  uint32_t s, h, ch, chunks, cache;
 };
 
 __device__ __forceinline__ UnitPos unit_pos(const AttnSmem* a, const StreamsStep& P, uint32_t kv_heads, uint32_t u) {
@@ -292,7 +294,7 @@ __device__ __forceinline__ UnitPos unit_pos(const AttnSmem* a, const StreamsStep
   }
   const uint32_t chunks = P.desc[lo].position / kAttnChunk + 1;
   const uint32_t r = u - a->prefix[lo];
-  return UnitPos{lo, r / chunks, r % chunks, chunks};
+  return UnitPos{lo, r / chunks, r % chunks, chunks, static_cast<uint32_t>(P.desc[lo].cache)};
 }
 
 __global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kernel(const StreamsStep P,
@@ -338,7 +340,7 @@ __global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kern
         uint8_t* dst = a->ring[slot];
         mbar_arrive_expect_tx(&a->full[slot], kTileBytes);
         const int32_t y = static_cast<int32_t>(up.ch * kAttnChunk), z = static_cast<int32_t>(layer),
-                      w = static_cast<int32_t>(up.s);
+                      w = static_cast<int32_t>(up.cache);
         const int32_t xs = static_cast<int32_t>((up.h * 4u) & ~15u);
         tma_load_4d(dst + kTK, maps.k_codes, static_cast<int32_t>(up.h * kHeadDim), y, z, w, &a->full[slot]);
         tma_load_4d(dst + kTV, maps.v_codes, static_cast<int32_t>(up.h * kHeadDim), y, z, w, &a->full[slot]);
@@ -362,7 +364,7 @@ __global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kern
   const uint32_t grp = static_cast<uint32_t>(lane) / 16;
   bool ok = true;
   float o_run = 0.0f, l_run = 0.0f, m_run = -INFINITY;
-  UnitPos cur{0xFFFFFFFFu, 0xFFFFFFFFu, 0, 0};
+  UnitPos cur{0xFFFFFFFFu, 0xFFFFFFFFu, 0, 0, 0};
   uint32_t seg_first = 0, seg_count = 0;
 
   // Emits the running state of the current (slot, head) segment.

@@ -107,6 +107,7 @@ def test_kernel_stages_on_identical_inputs(gpu, cuda_lib, oracle_lib):
         model = synthetic.make_model(c, fmt, seed=7)
         om = oracle_model(model)
         gm = _gpu_model(model)
+        gm.set_option(rt.OPTION_PREFILL_SERIAL, 1)  # the persistent kernel runs the prompt too
         # one position: attention returns v exactly; every stage within float rounding
         p1 = synthetic.make_prompt(c, 1, 0, seed=7)
         om.prefill(p1.tokens, p1.audio, 1)

@@ -2,12 +2,14 @@
 the CPU oracle, one oracle decoder per slot, through the stream family of the
 C ABI.
 
-Every slot has its own prompt (ragged lengths, some spanning several
-64-position attention chunks). After each qwc_streams_step, every slot that
-emitted a token is compared with its oracle: the logits within the north
-star's bounds (2e-2 max-abs, cosine >= 0.9999), the token identical or a
-near tie (oracle margin <= 2 x the measured logit error), in which case the
-oracle's token is forced so later steps compare on identical inputs.
+Every slot has its own prompt (ragged lengths, some spanning several 64-position
+attention chunks and several 64-position prefill steps). qwc_stream_begin
+prefills and holds the first prediction; each qwc_streams_step emits the held
+tokens and predicts the next ones. Before every step each slot's held token
+is compared with its oracle's: identical, or a near tie (oracle margin <= 2 x
+the measured logit error), in which case the oracle's token is forced so
+later steps compare on identical inputs. After every step the logits are
+held to the north star's bounds (2e-2 max-abs, cosine >= 0.9999).
 
 The batched projections feed exact weights and 22-bit activations to the
 tensor cores (documented in the header), so the q8 cache rows are held to the
@@ -36,7 +38,7 @@ def _prompts(config, slots, seed, lengths):
     return out
 
 
-def _run(model, slots, lengths, tokens_per_slot, max_near_ties, seed=5):
+def _run(model, slots, lengths, steps, max_near_ties, seed=5):
     c = model.config
     prompts = _prompts(c, slots, seed, lengths)
     gm = rt.CudaModel(0)
@@ -44,45 +46,42 @@ def _run(model, slots, lengths, tokens_per_slot, max_near_ties, seed=5):
     try:
         synthetic.load_into(model, gm, cache_format=rt.CACHE_Q8, streams=slots)
         gm.set_option(rt.OPTION_IGNORE_EOS, 1)
-        expect, logits = [], []
+        expect, worst_abs, worst_cos, ties = [], 0.0, 1.0, []
+
+        def compare(s):
+            nonlocal worst_abs, worst_cos
+            lo, lg = oms[s].logits(c.vocab_size), gm.debug_logits(s)
+            worst_abs = max(worst_abs, float(np.max(np.abs(lo - lg))))
+            worst_cos = min(worst_cos, cosine(lo, lg))
+            return lo, float(np.max(np.abs(lo - lg)))
+
+        errs = []
         for s, p in enumerate(prompts):
             om = oracle_model(model, threads=4)
             oms.append(om)
             expect.append(om.prefill(p.tokens, p.audio, p.audio.shape[0]))
-            logits.append(om.logits(c.vocab_size))
-            gm.stream_begin(s, p.tokens, p.audio, tokens_per_slot)
-        emitted = [0] * slots
-        worst_abs, worst_cos, ties = 0.0, 1.0, []
-        for _ in range(max(len(p.tokens) for p in prompts) + tokens_per_slot + 2):
-            toks, res, _ = gm.streams_step(slots)
+            gm.stream_begin(s, p.tokens, p.audio, steps + 1)
+            errs.append(compare(s))
+        for k in range(steps):
             for s in range(slots):
-                if res[s] != 1:
-                    assert res[s] in (0, 2), res[s]
-                    continue
-                lg = gm.debug_logits(s)
-                lo = logits[s]
-                err = float(np.max(np.abs(lo - lg)))
-                worst_abs = max(worst_abs, err)
-                worst_cos = min(worst_cos, cosine(lo, lg))
-                tok = int(toks[s])
-                if tok != expect[s]:
-                    ties.append({"slot": s, "step": emitted[s], "oracle": expect[s], "gpu": tok,
-                                 "margin": float(lo[expect[s]] - lo[tok]), "logit_err": err})
-                    assert lo[expect[s]] - lo[tok] <= 2 * err
+                held = gm.debug_hold(slot=s)
+                if held != expect[s]:
+                    lo, err = errs[s]
+                    ties.append({"slot": s, "step": k, "oracle": expect[s], "gpu": held,
+                                 "margin": float(lo[expect[s]] - lo[held]), "logit_err": err})
+                    assert lo[expect[s]] - lo[held] <= 2 * err
                     gm.debug_hold(force=expect[s], slot=s)
-                emitted[s] += 1
-                if emitted[s] < tokens_per_slot:
-                    expect[s] = oms[s].step(expect[s])
-                    logits[s] = oms[s].logits(c.vocab_size)
-            if all(e >= tokens_per_slot for e in emitted):
-                break
-        print(f"streams parity: {slots} slots, max |dlogit| {worst_abs:.3e}, min cosine {worst_cos:.9f}, "
-              f"near ties {len(ties)} {ties[:4]}")
-        assert all(e == tokens_per_slot for e in emitted), emitted
+            toks, res, n = gm.streams_step(slots)
+            assert n == slots and np.all(res == 1), res
+            for s in range(slots):
+                assert int(toks[s]) == expect[s]
+                expect[s] = oms[s].step(expect[s])
+                errs[s] = compare(s)
+        print(f"streams parity: {slots} slots, {steps} steps, max |dlogit| {worst_abs:.3e}, "
+              f"min cosine {worst_cos:.9f}, near ties {len(ties)} {ties[:4]}")
         assert worst_abs <= LOGIT_ATOL, worst_abs
         assert worst_cos >= COSINE_MIN, worst_cos
         assert len(ties) <= max_near_ties, ties
-        # The q8 cache rows of a few slots against their oracles.
         for s in range(min(slots, 3)):
             ok_, ov = oms[s].cache_q8()
             for which, ora in ((0, ok_), (1, ov)):
@@ -90,7 +89,6 @@ def _run(model, slots, lengths, tokens_per_slot, max_near_ties, seed=5):
                 print(f"slot {s} kv {'kv'[which]}: {r}")
                 assert r["codes_max"] <= 1 and r["scale_ulps_max"] <= 1, r
                 assert r["codes_exact"] >= 0.99 and r["scales_exact"] >= 0.95, r
-        return gm, prompts
     finally:
         gm.close()
         for om in oms:
@@ -101,14 +99,14 @@ def _run(model, slots, lengths, tokens_per_slot, max_near_ties, seed=5):
 def test_streams_match_oracle(gpu, cuda_lib, oracle_lib, fmt):
     config = small_config(fmt, layers=2, vocab=8192, max_positions=512)
     model = synthetic.make_model(config, fmt, seed=21)
-    _run(model, slots=6, lengths=[(10, 4), (60, 8), (3, 2), (120, 10), (0, 5), (70, 1)], tokens_per_slot=12,
+    _run(model, slots=6, lengths=[(10, 4), (60, 8), (3, 2), (150, 10), (0, 5), (70, 1)], steps=12,
          max_near_ties=3)
 
 
 def test_sixty_four_streams(gpu, cuda_lib, oracle_lib):
     config = small_config(quant.Q4, layers=2, vocab=8192, max_positions=256)
     model = synthetic.make_model(config, quant.Q4, seed=22)
-    _run(model, slots=64, lengths=[(5, 3), (20, 4), (1, 2), (66, 3)], tokens_per_slot=4, max_near_ties=6)
+    _run(model, slots=64, lengths=[(5, 3), (20, 4), (1, 2), (66, 3)], steps=4, max_near_ties=6)
 
 
 def test_device_chained_steps_match_host_steps(gpu, cuda_lib, oracle_lib):
@@ -124,20 +122,12 @@ def test_device_chained_steps_match_host_steps(gpu, cuda_lib, oracle_lib):
         gm.set_option(rt.OPTION_IGNORE_EOS, 1)
         for s, p in enumerate(prompts):
             gm.stream_begin(s, p.tokens, p.audio, 64)
-        while True:  # consume every prompt; each slot then holds its first token
-            _, res, _ = gm.streams_step(5)
-            if not np.any(res == 2):
-                break
-        # Align: every slot has emitted exactly one token once all prompts are done.
-        while min(len(gm.stream_tokens(s)) for s in range(5)) < 2:
-            gm.streams_step(5)
-        base = [len(gm.stream_tokens(s)) for s in range(5)]
+        gm.streams_step(5)
         if timed:
-            ms = gm.streams_run_timed(8)
-            assert ms > 0
+            assert gm.streams_run_timed(8) > 0
         else:
             for _ in range(8):
                 gm.streams_step(5)
-        runs.append([gm.stream_tokens(s)[base[s]:base[s] + 8] for s in range(5)])
+        runs.append([gm.stream_tokens(s) for s in range(5)])
         gm.close()
-    assert runs[0] == runs[1]
+    assert runs[0] == runs[1] and all(len(r) == 9 for r in runs[0])
