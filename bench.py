@@ -11,8 +11,8 @@ is needed between steps.
 
 The same line carries a `streams64` object: configs[3] of the benchmark
 definition, 64 independent streams per GPU of the same model (prefixes
-uniform in [100, 1500] audio rows + 16 text ids, staggered so every prompt
-ends on the same step), timed over greedy steps of all 64 slots with the
+uniform in [100, 1500] audio rows + 16 text ids, each prefilled on the tensor
+cores when its slot begins), timed over greedy steps of all 64 slots with the
 batched tensor-core step, with its own roofline and end-to-end figures.
 
 Under torchrun (N > 1) every rank holds a full weight replica and decodes its
@@ -212,9 +212,9 @@ def streams_bytes(model, positions: list[int], steps: int) -> float:
 
 
 def measure_streams(args, model, w, rank, local_rank, barrier, world):
-    """The multi-stream workload on this rank's GPU: slots begin staggered so
-    that every prompt ends on the same step, then `streams_steps` greedy steps
-    of all slots are timed on the device (qwc_streams_run_timed), then 32 steps
+    """The multi-stream workload on this rank's GPU: every slot's prompt is
+    prefilled at qwc_stream_begin, then `streams_steps` greedy steps of all
+    slots are timed on the device (qwc_streams_run_timed), then 32 steps
     through qwc_streams_step (host buffers each step) for the end-to-end figure."""
     import dataclasses
 
@@ -232,20 +232,15 @@ def measure_streams(args, model, w, rank, local_rank, barrier, world):
     prompts = [synthetic.make_prompt(w.config, lengths[s], w.text_ids, w.seed + 1000 * rank, stream=s)
                for s in range(w.streams)]
     plen = [len(p.tokens) for p in prompts]
-    pmax = max(plen)
     warm, e2e_steps = 4, 32
     steps = min(args.streams_steps, w.decode - 1 - warm - e2e_steps)
-    starts: dict[int, list[int]] = {}
-    for s in range(w.streams):
-        starts.setdefault(pmax - plen[s], []).append(s)
     t0 = time.perf_counter()
-    for step in range(pmax):
-        for s in starts.get(step, []):
-            gm.stream_begin(s, prompts[s].tokens, prompts[s].audio, w.decode)
-        gm.streams_step(w.streams)
+    for s in range(w.streams):  # each prompt prefilled on the tensor cores, 64 positions per step
+        gm.stream_begin(s, prompts[s].tokens, prompts[s].audio, w.decode)
+    torch.cuda.synchronize()
     prefill_s = time.perf_counter() - t0
     gm.streams_run_timed(warm)
-    positions = [pmax + warm] * w.streams  # every slot: prompt + first token + warm-up steps filled
+    positions = [plen[s] + warm for s in range(w.streams)]
     barrier()
     launches0 = gm.launches()
     with ClockSampler(local_rank) as clocks:
@@ -274,8 +269,9 @@ def measure_streams(args, model, w, rank, local_rank, barrier, world):
     return {
         "workload": w.name, "streams_per_gpu": w.streams, "value": tokens / (ms / 1000.0), "unit": "tokens/s",
         "ms_per_step": ms / steps, "steps": steps, "warmup": warm,
-        "prompt": f"{w.text_ids} text ids after U[{w.audio_rows[0]}, {w.audio_rows[1]}] audio rows per stream; "
-                  f"slots begin staggered so all prompts end together ({pmax} positions, {prefill_s:.1f} s)",
+        "prompt": f"{w.text_ids} text ids after U[{w.audio_rows[0]}, {w.audio_rows[1]}] audio rows per stream "
+                  f"({sum(plen)} prompt positions in all, prefilled in {prefill_s:.2f} s, 64 positions per "
+                  f"tensor-core step)",
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": peak_kind, "bytes_per_step": bytes_total / steps},
         "e2e": {"value": e2e_steps * w.streams * world / e2e_s, "unit": "tokens/s",
