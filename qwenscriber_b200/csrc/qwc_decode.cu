@@ -207,7 +207,7 @@ struct Producer {
   __device__ uint8_t* begin_tile(uint32_t bytes, uint64_t** bar) {
     const uint32_t slot = it % kSlots;
     const uint32_t parity = ((it / kSlots) & 1u) ^ 1u;
-    if (!mbar_wait_bounded(&s->empty[slot], parity, error, global_timer_ns() + timeout_ns, kErrEmpty)) {
+    if (!mbar_wait_bounded(&s->empty[slot], parity, error, timeout_ns, kErrEmpty)) {
       ok = false;
       return nullptr;
     }
@@ -348,7 +348,7 @@ __device__ const uint8_t* acquire_tile(Ctx& c) {
   const uint32_t slot = c.it % kSlots;
   const uint32_t parity = (c.it / kSlots) & 1u;
   const uint64_t w0 = (c.tracing && c.tid == 0) ? global_timer_ns() : 0;
-  if (c.ok && !mbar_wait_bounded(&c.s->full[slot], parity, c.P->error, global_timer_ns() + c.P->timeout_ns, kErrFull)) {
+  if (c.ok && !mbar_wait_bounded(&c.s->full[slot], parity, c.P->error, c.P->timeout_ns, kErrFull)) {
     c.ok = false;
   }
   if (c.tracing && c.tid == 0) c.full_wait_ns += global_timer_ns() - w0;
@@ -373,12 +373,15 @@ __device__ void grid_barrier(Ctx& c) {
     // The release is cumulative: it publishes every write the CTA's threads
     // made before the bar.sync above.
     red_release_add(c.P->barrier, 1);
-    const uint64_t deadline = global_timer_ns() + c.P->timeout_ns;
+    uint64_t deadline = 0;  // set on the first check, so a barrier that opens quickly never reads the clock
     uint32_t spins = 0;
     while (ld_acquire(c.P->barrier) < target) {
       if ((++spins & 63u) == 0) {
         if (error_set(c.P->error)) break;
-        if (global_timer_ns() > deadline) {
+        const uint64_t now = global_timer_ns();
+        if (deadline == 0) {
+          deadline = now + c.P->timeout_ns;
+        } else if (now > deadline) {
           atomicCAS(c.P->error, 0, kErrBarrier);
           break;
         }

@@ -250,10 +250,17 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* map, int32_t 
 // (bulk copy / TMA) accesses.
 __device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
-// Waits on an mbarrier phase with a wall-clock bound. Returns false (and sets
-// *error) if the bound is hit or another CTA already reported an error.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int32_t* error, uint64_t deadline,
+// Waits on an mbarrier phase for at most `timeout_ns` of wall-clock time.
+// Returns false (and sets *error) if the bound is hit or another CTA already
+// reported an error. The clock is read only once the phase has not completed
+// on the first attempts, so waits that are already satisfied stay cheap.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int32_t* error, uint64_t timeout_ns,
                                                   int32_t code) {
+#pragma unroll 1
+  for (int spin = 0; spin < 32; ++spin) {
+    if (mbar_try_wait(bar, parity)) return true;
+  }
+  const uint64_t deadline = global_timer_ns() + timeout_ns;
   uint32_t spins = 0;
   while (!mbar_try_wait(bar, parity)) {
     if ((++spins & 255u) == 0) {

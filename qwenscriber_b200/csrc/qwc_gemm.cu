@@ -8,21 +8,26 @@
 // range of K, in blocks of 64 (one quantization group):
 //
 //   warp 0   TMA producer: raw code and scale boxes of the tile, and the
-//            activation box, into a 4-stage ring (mbarrier complete_tx);
-//   warp 1   TMEM owner and MMA issuer: tcgen05.mma kind::f16, M=128, N=128,
-//            K=16, accumulating in TMEM; tcgen05.commit frees ring stages;
-//   warps 2-9 dequantize each raw block, half a row per thread, into a
-//            2-stage operand buffer in the canonical K-major no-swizzle
-//            layout; then read the accumulator back (tcgen05.ld) and store
-//            f32 results (two warps per TMEM lane quarter, 32 streams each).
+//            activation box, into a 6-stage shared-memory ring (mbarrier
+//            complete_tx);
+//   warp 1   TMEM owner and MMA issuer: tcgen05.mma kind::f16 with the
+//            weights from TMEM and the activations from shared memory,
+//            M=128, K=16, accumulating in TMEM; tcgen05.commit frees stages;
+//   warps 2-9 dequantize each raw block straight into TMEM (tcgen05.st, one
+//            tile row per TMEM lane, two warps per lane quarter, half of the
+//            block's K each), 4 stages deep; then read the accumulator back
+//            (tcgen05.ld) and store f32 results.
+//
+// Keeping the dequantized weights out of shared memory leaves its bandwidth
+// to the TMA boxes and the activation reads of the MMAs.
 //
 // Exactness: a dequantized weight (code - bias) * scale is split into
 // hi = f16(w) and lo = w - hi, which is exact in f16 (at most 8 significant
 // bits remain); each activation into hi = f16(x) and lo = f16(x - hi). The
-// activation box holds the 64 hi rows, then the 64 lo rows, as the MMA's 128
-// columns; two MMAs per K step (weights hi, then lo) accumulate w * (x_hi +
-// x_lo) in f32, and the epilogue adds the two column halves. Products are thus
-// those of the exact weights with 22-bit activations.
+// activation box holds the 64 hi rows, then the 64 lo rows. Per K step two
+// MMAs (weights hi, then lo) take all 128 columns; the epilogue adds the two
+// column halves. Products are thus those of the exact weights with 22-bit
+// activations.
 //
 // Activations arrive by TMA in 128-byte-swizzled rows; the dequantized weights
 // are written by the threads in the no-swizzle core-matrix layout.
@@ -47,20 +52,22 @@ namespace {
 
 constexpr int kGemmThreads = 320;
 constexpr int kDequantWarps = 8;
-constexpr int kRawStages = 4;
-constexpr int kAStages = 2;
+constexpr int kRawStages = 6;
+constexpr int kAStages = 4;  // dequantized operands (TMEM) in flight between the dequant warps and the MMAs
 constexpr uint32_t kTileM = 128;
 constexpr uint32_t kStreamCols = 64;                      // streams per launch
 constexpr uint32_t kTileN = 2 * kStreamCols;              // hi rows then lo rows
 constexpr uint32_t kKBlock = 64;
-constexpr uint32_t kAHalfBytes = kTileM * kKBlock * 2;    // 16 KB of f16 (hi or lo)
 constexpr uint32_t kBStageBytes = kTileN * kKBlock * 2;   // 16 KB of f16, one 128-byte swizzle atom column
 constexpr uint32_t kCodeStageBytes = kTileM * kKBlock;    // q8: 64 B per row; q4 uses half
 constexpr uint32_t kScaleStageBytes = kTileM * 16;        // one 16-byte box column of scales
-constexpr uint32_t kTmemCols = 128;
+// TMEM: the f32 accumulator in columns [0, 128); A stage i in columns
+// 128 + 64 i: weights hi (4 K steps x 8 columns of f16 pairs), then lo.
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemA = kTileN;
+constexpr uint32_t kTmemAStage = 64;
 
 struct __align__(1024) GemmSmem {
-  uint8_t a16[kAStages][2][kAHalfBytes];
   uint8_t b[kRawStages][kBStageBytes];
   uint8_t codes[kRawStages][kCodeStageBytes];
   uint8_t scales[kRawStages][kScaleStageBytes];
@@ -74,6 +81,7 @@ struct __align__(1024) GemmSmem {
 static_assert(offsetof(GemmSmem, b) % 1024 == 0 && offsetof(GemmSmem, codes) % 128 == 0 &&
                   offsetof(GemmSmem, scales) % 128 == 0,
               "TMA destinations need 128-byte alignment (swizzled boxes 1024)");
+static_assert(kTmemA + kAStages * kTmemAStage <= kTmemCols, "TMEM budget");
 
 // ---- tcgen05 wrappers ----
 
@@ -96,7 +104,7 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 // two 8-element K halves of an MMA, `sbo` = byte distance between 8-row
 // groups. 128-byte swizzle: rows of 128 bytes, `sbo` = 1024 (8 rows), the
 // atom 1024-byte aligned; K steps inside the atom advance the start address.
-constexpr uint32_t kLayoutNone = 0, kLayoutSw128 = 2;
+constexpr uint32_t kLayoutSw128 = 2;
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
   uint64_t d = static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
   d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
@@ -106,23 +114,31 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint
   return d;  // base offset 0, absolute leading-offset mode
 }
 
-// Instruction descriptor: f16 x f16 -> f32, both K-major, M = 128, N = 128.
-constexpr uint32_t kIdesc = (1u << 4) | ((kTileN >> 3) << 17) | ((kTileM >> 4) << 24);
+// Instruction descriptor: f16 x f16 -> f32, both K-major, M = 128, N = 128
+// (activation hi and lo columns).
+constexpr uint32_t kIdescN128 = (1u << 4) | ((kTileN >> 3) << 17) | ((kTileM >> 4) << 24);
 
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+// D[tmem_d] (+)= A[tmem_a] * B[smem desc]: A read from tensor memory.
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+
+// 32 lanes x 8 columns of this warp's lane quarter from registers.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint4& a, const uint4& b) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+               "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w)
+               : "memory");
 }
 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
                : "memory");
 }
-
-__device__ __forceinline__ void fence_proxy_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const void* map, int32_t x, int32_t y, uint64_t* bar) {
   asm volatile(
@@ -236,7 +252,7 @@ enum GemmError : int32_t { kGemmErrWait = 1 };
 // Bounded wait; on expiry the first failing thread also records where
 // (error[1..3] = code site, block x, block y).
 __device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity, const GemmParams& p, int32_t site = 0) {
-  if (mbar_wait_bounded(bar, parity, p.error, global_timer_ns() + p.timeout_ns, kGemmErrWait + site)) return true;
+  if (mbar_wait_bounded(bar, parity, p.error, p.timeout_ns, kGemmErrWait + site)) return true;
   if (*reinterpret_cast<volatile int32_t*>(p.error) == kGemmErrWait + site) {
     p.error[1] = site;
     p.error[2] = static_cast<int32_t>(blockIdx.x);
@@ -312,6 +328,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else if (warp == 1) {
     // ---- MMA issuer ----
+    const uint64_t b_desc0 = umma_desc(smem_addr(s->b[0]), 16, 1024, kLayoutSw128);
     if (lane == 0) {
       for (uint32_t i = 0; i < nkb && ok; ++i) {
         const uint32_t st = i % kRawStages;
@@ -322,16 +339,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t a_hi = smem_addr(s->a16[at][0]);
-        const uint32_t a_lo = smem_addr(s->a16[at][1]);
-        const uint32_t b_base = smem_addr(s->b[st]);
+        // A: 8 TMEM columns (16 f16 of K) per MMA. B: one swizzle atom of
+        // 128 rows x 128 B; 32 B per K step (the descriptor's start-address
+        // field advances in 16-byte units).
+        const uint32_t ahi = tmem + kTmemA + at * kTmemAStage;
+        const uint32_t alo = ahi + kTmemAStage / 2;
+        const uint64_t bd0 = b_desc0 + ((uint64_t(st) * kBStageBytes) >> 4);
 #pragma unroll
         for (uint32_t k = 0; k < kKBlock / 16; ++k) {
-          // A: two 8-element K chunks per MMA, 2048 B apart (128 rows x 16 B).
-          // B: one swizzle atom of 128 rows x 128 B; 32 B per K step.
-          const uint64_t bd = umma_desc(b_base + k * 32, 16, 1024, kLayoutSw128);
-          umma_f16(tmem, umma_desc(a_hi + k * 2 * 2048, 2048, 128, kLayoutNone), bd, (i > 0 || k > 0) ? 1u : 0u);
-          umma_f16(tmem, umma_desc(a_lo + k * 2 * 2048, 2048, 128, kLayoutNone), bd, 1u);
+          const uint64_t bd = bd0 + 2 * k;
+          // weights hi, then lo, against activations hi | lo
+          umma_f16_ts(tmem, ahi + 8 * k, bd, kIdescN128, (i > 0 || k > 0) ? 1u : 0u);
+          umma_f16_ts(tmem, alo + 8 * k, bd, kIdescN128, 1u);
         }
         umma_commit(&s->a_empty[at]);
         umma_commit(&s->raw_empty[st]);
@@ -341,51 +360,51 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!ok) wait_bounded(&s->acc_full, 0, p);
     }
   } else {
-    // ---- dequantize, then epilogue ----
-    const uint32_t t = (warp - 2) * 32 + lane;
-    const uint32_t r = t % kTileM;   // row of the tile
-    const uint32_t half = t / kTileM;  // which four of the block's eight 8-value chunks
+    // ---- dequantize into TMEM, then epilogue ----
+    const uint32_t quarter = static_cast<uint32_t>(warp % 4);
+    const uint32_t part = static_cast<uint32_t>((warp - 2) / 4);  // K steps 2 part, 2 part + 1 of each block
+    const uint32_t r = quarter * 32 + lane;                      // tile row = TMEM lane
+    const uint32_t lane_addr = (quarter * 32u) << 16;
     for (uint32_t i = 0; i < nkb && ok; ++i) {
       const uint32_t st = i % kRawStages;
       const uint32_t at = i % kAStages;
-      if (!wait_bounded(&s->raw_full[st], (i / kRawStages) & 1u, p, 40)) {
+      bool ready = wait_bounded(&s->raw_full[st], (i / kRawStages) & 1u, p, 40);
+      if (ready && i >= kAStages) ready = wait_bounded(&s->a_empty[at], ((i / kAStages) - 1) & 1u, p, 50);
+      if (!__all_sync(0xffffffffu, ready)) {  // tcgen05.st below is warp-collective
         ok = false;
         break;
       }
-      if (i >= kAStages && !wait_bounded(&s->a_empty[at], ((i / kAStages) - 1) & 1u, p, 50)) {
-        ok = false;
-        break;
-      }
+      tc_fence_after();
       const uint32_t kb = kb0 + i;
       const uint16_t sb = *reinterpret_cast<const uint16_t*>(s->scales[st] + r * 16 + ((kb * 2u) & 15u));
       const uint32_t sc = static_cast<uint32_t>(sb) * 0x10001u;
-      uint8_t* ahi = s->a16[at][0] + r * 16 + half * 4 * 2048;
-      uint8_t* alo = s->a16[at][1] + r * 16 + half * 4 * 2048;
-      uint4 hi, lo;
+      const uint32_t ahi = tmem + lane_addr + kTmemA + at * kTmemAStage;
+      const uint32_t alo = ahi + kTmemAStage / 2;
+      uint4 h0, l0, h1, l1;
       if (q4) {
-        const uint4 w = *reinterpret_cast<const uint4*>(s->codes[st] + r * (kKBlock / 2) + half * 16);
-        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          dequant_q4_word(words[c], sc, hi, lo);
-          *reinterpret_cast<uint4*>(ahi + c * 2048) = hi;
-          *reinterpret_cast<uint4*>(alo + c * 2048) = lo;
-        }
+        // This half-row's 32 K values: one 16-byte chunk of codes, 8 per word.
+        const uint4 w = *reinterpret_cast<const uint4*>(s->codes[st] + r * (kKBlock / 2) + part * 16);
+        dequant_q4_word(w.x, sc, h0, l0);
+        dequant_q4_word(w.y, sc, h1, l1);
+        tmem_st8(ahi + 8 * (2 * part), h0, h1);
+        tmem_st8(alo + 8 * (2 * part), l0, l1);
+        dequant_q4_word(w.z, sc, h0, l0);
+        dequant_q4_word(w.w, sc, h1, l1);
+        tmem_st8(ahi + 8 * (2 * part + 1), h0, h1);
+        tmem_st8(alo + 8 * (2 * part + 1), l0, l1);
       } else {
-        const uint4* src = reinterpret_cast<const uint4*>(s->codes[st] + r * kKBlock + half * 32);
+        const uint4* src = reinterpret_cast<const uint4*>(s->codes[st] + r * kKBlock + part * 32);
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
           const uint4 w = src[q];
-          dequant_q8_words(w.x, w.y, sc, hi, lo);
-          *reinterpret_cast<uint4*>(ahi + (2 * q + 0) * 2048) = hi;
-          *reinterpret_cast<uint4*>(alo + (2 * q + 0) * 2048) = lo;
-          dequant_q8_words(w.z, w.w, sc, hi, lo);
-          *reinterpret_cast<uint4*>(ahi + (2 * q + 1) * 2048) = hi;
-          *reinterpret_cast<uint4*>(alo + (2 * q + 1) * 2048) = lo;
+          dequant_q8_words(w.x, w.y, sc, h0, l0);
+          dequant_q8_words(w.z, w.w, sc, h1, l1);
+          tmem_st8(ahi + 8 * (2 * part + q), h0, h1);
+          tmem_st8(alo + 8 * (2 * part + q), l0, l1);
         }
       }
-      // Generic-proxy stores, read next by the tensor core (async proxy).
-      fence_proxy_async_shared();
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s->a_full[at]);
     }
@@ -396,8 +415,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     go = __all_sync(0xffffffffu, go);  // tcgen05.ld is warp-collective
     if (go) {
       tc_fence_after();
-      const uint32_t quarter = static_cast<uint32_t>(warp % 4);
-      const uint32_t n0 = ((warp - 2) / 4) * 32;
+      const uint32_t n0 = part * 32;
       float v[32], vlo[32];
       tmem_ld32(tmem + ((quarter * 32u) << 16) + n0, v);
       tmem_ld32(tmem + ((quarter * 32u) << 16) + kStreamCols + n0, vlo);

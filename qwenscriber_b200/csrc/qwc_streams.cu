@@ -332,8 +332,7 @@ __global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kern
       for (uint32_t u = u0; u < u1; ++u, ++it) {
         const uint32_t slot = it % kAttnSlots;
         if (it >= kAttnSlots &&
-            !mbar_wait_bounded(&a->empty[slot], ((it / kAttnSlots) - 1) & 1u, P.error,
-                               global_timer_ns() + P.timeout_ns, 102)) {
+            !mbar_wait_bounded(&a->empty[slot], ((it / kAttnSlots) - 1) & 1u, P.error, P.timeout_ns, 102)) {
           break;
         }
         const UnitPos up = unit_pos(a, P, kv_heads, u);
@@ -436,7 +435,7 @@ __global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kern
       a->q[j][dd / 32][dd % 32] = P.qrot[size_t(up.s) * qw + (2 * up.h + j) * kHeadDim + dd];
     }
     const uint32_t slot = it % kAttnSlots;
-    if (ok && !mbar_wait_bounded(&a->full[slot], (it / kAttnSlots) & 1u, P.error, global_timer_ns() + P.timeout_ns,
+    if (ok && !mbar_wait_bounded(&a->full[slot], (it / kAttnSlots) & 1u, P.error, P.timeout_ns,
                                  101)) {
       ok = false;
     }
