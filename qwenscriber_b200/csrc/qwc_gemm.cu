@@ -4,8 +4,9 @@
 // out[s][r] = sum_k W[r][k] * x[s][k] for up to 64 streams s at once: the
 // projections of kernels.linearQuantized (src/core/qwen3_asr/kernels.zig:118-158)
 // for a batch of streams. W stays in the reference's two-plane q4/q8 layout
-// (src/core/quant.zig:144-176). Per CTA: one tile of 128 weight rows and a
-// range of K, in blocks of 64 (one quantization group):
+// (src/core/quant.zig:144-176). Per CTA: two tiles of 128 weight rows (each
+// activation block feeds both) and a range of K, in blocks of 64 (one
+// quantization group):
 //
 //   warp 0   TMA producer: raw code and scale boxes of the tile, and the
 //            activation box, into a 6-stage shared-memory ring (mbarrier
@@ -14,8 +15,8 @@
 //            weights from TMEM and the activations from shared memory,
 //            M=128, K=16, accumulating in TMEM; tcgen05.commit frees stages;
 //   warps 2-9 dequantize each raw block straight into TMEM (tcgen05.st, one
-//            tile row per TMEM lane, two warps per lane quarter, half of the
-//            block's K each), 4 stages deep; then read the accumulator back
+//            tile row per TMEM lane; the four warps of tile t cover its lane
+//            quarters), 2 stages deep; then read tile t's accumulator back
 //            (tcgen05.ld) and store f32 results.
 //
 // Keeping the dequantized weights out of shared memory leaves its bandwidth
@@ -53,19 +54,22 @@ namespace {
 constexpr int kGemmThreads = 320;
 constexpr int kDequantWarps = 8;
 constexpr int kRawStages = 6;
-constexpr int kAStages = 4;  // dequantized operands (TMEM) in flight between the dequant warps and the MMAs
+constexpr int kAStages = 2;  // dequantized operands (TMEM) in flight between the dequant warps and the MMAs
 constexpr uint32_t kTileM = 128;
+constexpr uint32_t kTilesPerCta = 2;
+constexpr uint32_t kCtaRows = kTileM * kTilesPerCta;
 constexpr uint32_t kStreamCols = 64;                      // streams per launch
 constexpr uint32_t kTileN = 2 * kStreamCols;              // hi rows then lo rows
 constexpr uint32_t kKBlock = 64;
 constexpr uint32_t kBStageBytes = kTileN * kKBlock * 2;   // 16 KB of f16, one 128-byte swizzle atom column
-constexpr uint32_t kCodeStageBytes = kTileM * kKBlock;    // q8: 64 B per row; q4 uses half
-constexpr uint32_t kScaleStageBytes = kTileM * 16;        // one 16-byte box column of scales
-// TMEM: the f32 accumulator in columns [0, 128); A stage i in columns
-// 128 + 64 i: weights hi (4 K steps x 8 columns of f16 pairs), then lo.
+constexpr uint32_t kCodeStageBytes = kCtaRows * kKBlock;  // q8: 64 B per row; q4 uses half
+constexpr uint32_t kScaleStageBytes = kCtaRows * 16;      // one 16-byte box column of scales
+// TMEM: tile t's f32 accumulator in columns [128 t, 128 t + 128); A stage i
+// in columns 256 + 128 i: per tile (64 columns each) weights hi (4 K steps x
+// 8 columns of f16 pairs), then lo.
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemA = kTileN;
-constexpr uint32_t kTmemAStage = 64;
+constexpr uint32_t kTmemA = kTilesPerCta * kTileN;
+constexpr uint32_t kTmemAStage = 64 * kTilesPerCta;
 
 struct __align__(1024) GemmSmem {
   uint8_t b[kRawStages][kBStageBytes];
@@ -224,7 +228,7 @@ __device__ __forceinline__ void dequant_q8_words(uint32_t w0, uint32_t w1, uint3
 // that share K and the activations (Q, K and V; gate and up).
 struct GemmJob {
   uint32_t rows;        // M
-  uint32_t mtiles;      // ceil(rows / 128)
+  uint32_t mtiles;      // ceil(rows / 256): CTA tiles
   uint32_t format;      // q4 / q8
   uint32_t out_offset;  // first output column of this matrix in each output row
 };
@@ -268,14 +272,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t pad = (1024u - (smem_addr(gemm_smem_raw) & 1023u)) & 1023u;
   GemmSmem* s = reinterpret_cast<GemmSmem*>(gemm_smem_raw + pad);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  // Which matrix and which 128-row tile of it this CTA takes.
+  // Which matrix and which 256-row stretch of it this CTA takes.
   uint32_t tile = blockIdx.x, jb = 0;
   while (jb + 1 < p.njobs && tile >= p.job[jb].mtiles) tile -= p.job[jb++].mtiles;
   const GemmJob job = p.job[jb];
   const CUtensorMap* map_codes = &maps.codes[jb];
   const CUtensorMap* map_scales = &maps.scales[jb];
   const CUtensorMap* map_b = &maps.b;
-  const uint32_t m0 = tile * kTileM;
+  const uint32_t m0 = tile * kCtaRows;
   const uint32_t kblocks = p.cols / kKBlock;
   const uint32_t kb0 = blockIdx.y * p.kb_per_split;
   const uint32_t kb1 = min(kblocks, kb0 + p.kb_per_split);
@@ -312,7 +316,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           break;
         }
         const uint32_t kb = kb0 + i;
-        mbar_arrive_expect_tx(&s->raw_full[st], kTileM * code_box + kScaleStageBytes + kBStageBytes);
+        mbar_arrive_expect_tx(&s->raw_full[st], kCtaRows * code_box + kScaleStageBytes + kBStageBytes);
         tma_load_2d(s->codes[st], map_codes, static_cast<int32_t>(kb * code_box), static_cast<int32_t>(m0),
                     &s->raw_full[st]);
         // The 16-byte scale box holding this block's group.
@@ -342,15 +346,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // A: 8 TMEM columns (16 f16 of K) per MMA. B: one swizzle atom of
         // 128 rows x 128 B; 32 B per K step (the descriptor's start-address
         // field advances in 16-byte units).
-        const uint32_t ahi = tmem + kTmemA + at * kTmemAStage;
-        const uint32_t alo = ahi + kTmemAStage / 2;
+        const uint32_t a0 = tmem + kTmemA + at * kTmemAStage;
         const uint64_t bd0 = b_desc0 + ((uint64_t(st) * kBStageBytes) >> 4);
 #pragma unroll
         for (uint32_t k = 0; k < kKBlock / 16; ++k) {
           const uint64_t bd = bd0 + 2 * k;
-          // weights hi, then lo, against activations hi | lo
-          umma_f16_ts(tmem, ahi + 8 * k, bd, kIdescN128, (i > 0 || k > 0) ? 1u : 0u);
-          umma_f16_ts(tmem, alo + 8 * k, bd, kIdescN128, 1u);
+#pragma unroll
+          for (uint32_t t = 0; t < kTilesPerCta; ++t) {
+            // tile t: weights hi, then lo, against activations hi | lo
+            const uint32_t d = tmem + t * kTileN;
+            umma_f16_ts(d, a0 + 64 * t + 8 * k, bd, kIdescN128, (i > 0 || k > 0) ? 1u : 0u);
+            umma_f16_ts(d, a0 + 64 * t + 32 + 8 * k, bd, kIdescN128, 1u);
+          }
         }
         umma_commit(&s->a_empty[at]);
         umma_commit(&s->raw_empty[st]);
@@ -362,8 +369,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // ---- dequantize into TMEM, then epilogue ----
     const uint32_t quarter = static_cast<uint32_t>(warp % 4);
-    const uint32_t part = static_cast<uint32_t>((warp - 2) / 4);  // K steps 2 part, 2 part + 1 of each block
-    const uint32_t r = quarter * 32 + lane;                      // tile row = TMEM lane
+    const uint32_t t = static_cast<uint32_t>((warp - 2) / 4);  // tile of this warp
+    const uint32_t r = t * kTileM + quarter * 32 + lane;       // row of the CTA's stretch
     const uint32_t lane_addr = (quarter * 32u) << 16;
     for (uint32_t i = 0; i < nkb && ok; ++i) {
       const uint32_t st = i % kRawStages;
@@ -378,29 +385,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t kb = kb0 + i;
       const uint16_t sb = *reinterpret_cast<const uint16_t*>(s->scales[st] + r * 16 + ((kb * 2u) & 15u));
       const uint32_t sc = static_cast<uint32_t>(sb) * 0x10001u;
-      const uint32_t ahi = tmem + lane_addr + kTmemA + at * kTmemAStage;
-      const uint32_t alo = ahi + kTmemAStage / 2;
+      const uint32_t ahi = tmem + lane_addr + kTmemA + at * kTmemAStage + 64 * t;
+      const uint32_t alo = ahi + 32;
       uint4 h0, l0, h1, l1;
       if (q4) {
-        // This half-row's 32 K values: one 16-byte chunk of codes, 8 per word.
-        const uint4 w = *reinterpret_cast<const uint4*>(s->codes[st] + r * (kKBlock / 2) + part * 16);
-        dequant_q4_word(w.x, sc, h0, l0);
-        dequant_q4_word(w.y, sc, h1, l1);
-        tmem_st8(ahi + 8 * (2 * part), h0, h1);
-        tmem_st8(alo + 8 * (2 * part), l0, l1);
-        dequant_q4_word(w.z, sc, h0, l0);
-        dequant_q4_word(w.w, sc, h1, l1);
-        tmem_st8(ahi + 8 * (2 * part + 1), h0, h1);
-        tmem_st8(alo + 8 * (2 * part + 1), l0, l1);
-      } else {
-        const uint4* src = reinterpret_cast<const uint4*>(s->codes[st] + r * kKBlock + part * 32);
+        // The row's 64 K values: two 16-byte chunks of codes, 8 per word.
+        const uint4* src = reinterpret_cast<const uint4*>(s->codes[st] + r * (kKBlock / 2));
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
           const uint4 w = src[q];
+          dequant_q4_word(w.x, sc, h0, l0);
+          dequant_q4_word(w.y, sc, h1, l1);
+          tmem_st8(ahi + 8 * (2 * q), h0, h1);
+          tmem_st8(alo + 8 * (2 * q), l0, l1);
+          dequant_q4_word(w.z, sc, h0, l0);
+          dequant_q4_word(w.w, sc, h1, l1);
+          tmem_st8(ahi + 8 * (2 * q + 1), h0, h1);
+          tmem_st8(alo + 8 * (2 * q + 1), l0, l1);
+        }
+      } else {
+        const uint4* src = reinterpret_cast<const uint4*>(s->codes[st] + r * kKBlock);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 w = src[q];
           dequant_q8_words(w.x, w.y, sc, h0, l0);
           dequant_q8_words(w.z, w.w, sc, h1, l1);
-          tmem_st8(ahi + 8 * (2 * part + q), h0, h1);
-          tmem_st8(alo + 8 * (2 * part + q), l0, l1);
+          tmem_st8(ahi + 8 * q, h0, h1);
+          tmem_st8(alo + 8 * q, l0, l1);
         }
       }
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
@@ -408,23 +419,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&s->a_full[at]);
     }
-    // Epilogue: TMEM lane = tile row; a warp may read lanes 32 * (warp % 4) +
-    // [0, 32). The two warps of a quarter take streams [0, 32) and [32, 64):
-    // columns n (x hi) and 64 + n (x lo).
+    // Epilogue: TMEM lane = tile row; this warp reads tile t's accumulator in
+    // its lane quarter: columns n (x hi) and 64 + n (x lo).
     bool go = ok && nkb > 0 && wait_bounded(&s->acc_full, 0, p, 60);
     go = __all_sync(0xffffffffu, go);  // tcgen05.ld is warp-collective
     if (go) {
       tc_fence_after();
-      const uint32_t n0 = part * 32;
-      float v[32], vlo[32];
-      tmem_ld32(tmem + ((quarter * 32u) << 16) + n0, v);
-      tmem_ld32(tmem + ((quarter * 32u) << 16) + kStreamCols + n0, vlo);
-      const uint32_t row = m0 + quarter * 32 + lane;
-      if (row < job.rows) {
-        float* out = p.out + size_t(blockIdx.y) * p.streams * p.out_ld + job.out_offset + row;
+      const uint32_t row = m0 + r;
+      float* out = p.out + size_t(blockIdx.y) * p.streams * p.out_ld + job.out_offset + row;
 #pragma unroll
-        for (int n = 0; n < 32; ++n) {
-          if (n0 + n < p.streams) out[size_t(n0 + n) * p.out_ld] = v[n] + vlo[n];
+      for (uint32_t n0 = 0; n0 < kStreamCols; n0 += 32) {
+        float v[32], vlo[32];
+        tmem_ld32(tmem + lane_addr + t * kTileN + n0, v);
+        tmem_ld32(tmem + lane_addr + t * kTileN + kStreamCols + n0, vlo);
+        if (row < job.rows) {
+#pragma unroll
+          for (int n = 0; n < 32; ++n) {
+            if (n0 + n < p.streams) out[size_t(n0 + n) * p.out_ld] = v[n] + vlo[n];
+          }
         }
       }
     }
@@ -483,10 +495,10 @@ int32_t gemm_weight_maps(uint32_t format, const void* codes, const void* scales,
   const uint64_t code_row = uint64_t(groups) * data_bytes_per_group(format), scale_row = uint64_t(groups) * 2;
   const uint64_t dims_c[2] = {code_row, rows};
   const uint64_t str_c[1] = {code_row};
-  const uint32_t box_c[2] = {format == kFormatQ4 ? kKBlock / 2 : kKBlock, kTileM};
+  const uint32_t box_c[2] = {format == kFormatQ4 ? kKBlock / 2 : kKBlock, kCtaRows};
   const uint64_t dims_s[2] = {scale_row, rows};
   const uint64_t str_s[1] = {scale_row};
-  const uint32_t box_s[2] = {16, kTileM};
+  const uint32_t box_s[2] = {16, kCtaRows};
   const int32_t rc = encode_tensor_map(codes_map, kMapU8, 2, const_cast<void*>(codes), dims_c, str_c, box_c, false);
   if (rc != QWC_OK) return rc;
   return encode_tensor_map(scales_map, kMapU8, 2, const_cast<void*>(scales), dims_s, str_s, box_s, false);
@@ -504,7 +516,7 @@ int32_t gemm_act_map(void* base, uint32_t cols, uint8_t* out) {
 // pipeline fill, TMEM set-up and epilogue) and the partial sums the next
 // kernel reads.
 uint32_t gemm_splits(uint32_t rows, uint32_t cols, int sms) {
-  const uint32_t mtiles = (rows + kTileM - 1) / kTileM;
+  const uint32_t mtiles = (rows + kCtaRows - 1) / kCtaRows;
   const uint32_t kblocks = cols / kKBlock;
   uint32_t best = 1;
   double best_cost = 1e30;
@@ -533,7 +545,7 @@ int launch_gemm_jobs(const uint8_t (*codes_maps)[128], const uint8_t (*scale_map
   for (uint32_t j = 0; j < njobs; ++j) {
     std::memcpy(&maps.codes[j], codes_maps[j], 128);
     std::memcpy(&maps.scales[j], scale_maps[j], 128);
-    p.job[j] = GemmJob{rows[j], (rows[j] + kTileM - 1) / kTileM, formats[j], out_offsets[j]};
+    p.job[j] = GemmJob{rows[j], (rows[j] + kCtaRows - 1) / kCtaRows, formats[j], out_offsets[j]};
     tiles += p.job[j].mtiles;
   }
   for (uint32_t j = njobs; j < 3; ++j) {
