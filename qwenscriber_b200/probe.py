@@ -24,8 +24,13 @@ def main(argv=None) -> int:
     p.add_argument("--workload", default="cfg3_1p7b_q4_s64")
     p.add_argument("--steps", type=int, default=1)
     p.add_argument("--chunk", type=int, default=16, help="decode steps per launch (single stream)")
+    p.add_argument("--streams", type=int, default=0, help="override the workload's streams per GPU")
     a = p.parse_args(argv)
     w = synthetic.workloads()[a.workload]
+    if a.streams:
+        import dataclasses
+
+        w = dataclasses.replace(w, streams=a.streams)
     model = synthetic.make_model(w.config, w.fmt, w.seed)
     gm = rt.CudaModel(0)
     synthetic.load_into(model, gm, cache_format=rt.CACHE_Q8, streams=w.streams)
