@@ -76,6 +76,10 @@ struct Smem {
   float amax_v[kConsumerWarps];
   uint32_t amax_i[kConsumerWarps];
   uint32_t flag;
+  // The model description, copied from device memory at launch: every stage
+  // reads matrix shapes and pointers from it, and shared-memory loads keep
+  // those reads off the stage's critical path.
+  alignas(16) uint8_t model[sizeof(DevModel)];
 };
 
 // Attention scratch overlays the activation buffer (never live together).
@@ -97,6 +101,7 @@ static_assert(offsetof(AttnSmem, q) % 16 == 0 && offsetof(AttnSmem, vpart) % 16 
 static_assert(offsetof(Smem, x) % 16 == 0 && offsetof(Smem, ring) % 128 == 0 && kSlotBytes % 128 == 0,
               "activation buffer and TMA destinations alignment");
 static_assert(sizeof(AttnSmem) <= sizeof(float) * kXMax, "attention scratch must fit the activation buffer");
+static_assert(sizeof(Smem) <= 227 * 1024, "one CTA per SM: the shared memory fits the 227 KB opt-in limit");
 static_assert(kAttnTileBytes <= kSlotBytes, "an attention tile fills one ring slot");
 static_assert(kHiddenMax * 4 <= kSlotBytes, "a norm weight vector fills one ring slot");
 
@@ -297,7 +302,7 @@ struct Producer {
 // rows; then, for tokens with logits, the final norm and the lm_head rows.
 __device__ void run_producer(const DecodeLaunch& P, const KvMaps& maps, Smem* s) {
   if ((threadIdx.x & 31) != 0) return;
-  const DevModel& m = *P.model;
+  const DevModel& m = *reinterpret_cast<const DevModel*>(s->model);
   Producer pr{s, 0, P.error, P.timeout_ns, true};
   for (uint32_t t = 0; t < P.n_tokens && pr.ok; ++t) {
     const uint32_t position = P.first_position + t;
@@ -333,6 +338,8 @@ struct Ctx {
   bool tracing;           // this token's phase timeline is being recorded
   uint64_t full_wait_ns;  // thread 0: time spent waiting for streamed tiles
   uint64_t bar_wait_ns;   // thread 0: time between barrier arrival and release
+  uint64_t tile_ns;       // thread 0: time from a tile's arrival to its release
+  uint64_t tile_t0;
 };
 
 __device__ bool error_set(const int32_t* e) { return *reinterpret_cast<const volatile int32_t*>(e) != 0; }
@@ -351,13 +358,17 @@ __device__ const uint8_t* acquire_tile(Ctx& c) {
   if (c.ok && !mbar_wait_bounded(&c.s->full[slot], parity, c.P->error, c.P->timeout_ns, kErrFull)) {
     c.ok = false;
   }
-  if (c.tracing && c.tid == 0) c.full_wait_ns += global_timer_ns() - w0;
+  if (c.tracing && c.tid == 0) {
+    c.tile_t0 = global_timer_ns();
+    c.full_wait_ns += c.tile_t0 - w0;
+  }
   return c.s->ring[slot];
 }
 
 // Hands the current slot back to the producer once this warp is done with it.
 __device__ void release_tile(Ctx& c) {
   __syncwarp();
+  if (c.tracing && c.tid == 0) c.tile_ns += global_timer_ns() - c.tile_t0;
   if (c.lane == 0) mbar_arrive(&c.s->empty[c.it % kSlots]);
   ++c.it;
 }
@@ -877,9 +888,9 @@ __device__ void attention_stage(Ctx& c, uint32_t layer, uint32_t position) {
 // ---- the consumer program ----
 
 __device__ void run_consumers(const DecodeLaunch& P, Smem* s) {
-  const DevModel& m = *P.model;
+  const DevModel& m = *reinterpret_cast<const DevModel*>(s->model);
   Ctx c{&P, &m, s, 0, 0, true, static_cast<int>(threadIdx.x / 32), static_cast<int>(threadIdx.x % 32),
-        static_cast<int>(threadIdx.x), false, 0, 0};
+        static_cast<int>(threadIdx.x), false, 0, 0, 0, 0};
   const Span own = split_rows(m.hidden, blockIdx.x, gridDim.x);  // hidden rows of O and down
   const uint32_t qw = m.q_heads * kHeadDim;
   uint32_t input = P.first_input;
@@ -938,31 +949,34 @@ __device__ void run_consumers(const DecodeLaunch& P, Smem* s) {
       trace_mark(c, e0 + 7);
       // -- RMSNorm -> gate/up -> SwiGLU (decoder.zig:259-269)
       norm_global_into_x(c, P.hidden_g, m.hidden, stage_format(m, l, kStGate) == kFormatQ4);
+      trace_mark(c, e0 + 8);
       const Span fr = split_rows(m.ffn, blockIdx.x, gridDim.x);
       gemv_stage(c, kStGate, l, best, nullptr);
       for (uint32_t i = c.tid; i < fr.end - fr.begin; i += kConsumerThreads) s->gate[i] = s->part[i];
       consumer_sync(kConsumerThreads);
+      trace_mark(c, e0 + 9);
       gemv_stage(c, kStUp, l, best, nullptr);
       for (uint32_t i = c.tid; i < fr.end - fr.begin; i += kConsumerThreads) {
         const float g = s->gate[i];
         const float silu = g / (1.0f + expf(-g));
         P.act[fr.begin + i] = silu * s->part[i];
       }
-      trace_mark(c, e0 + 8);
+      trace_mark(c, e0 + 10);
       grid_barrier(c);
       if (!c.ok) break;
       // -- down + residual (decoder.zig:270-271)
       load_x_global(c, P.act, m.ffn, stage_format(m, l, kStDown) == kFormatQ4);
+      trace_mark(c, e0 + 11);
       gemv_stage(c, kStDown, l, best, nullptr);
       for (uint32_t r = own.begin + c.tid; r < own.end; r += kConsumerThreads) {
         const float h = s->resid[r - own.begin] + s->part[r - own.begin];
         s->resid[r - own.begin] = h;
         P.hidden_g[r] = h;
       }
-      trace_mark(c, e0 + 9);
+      trace_mark(c, e0 + 12);
       grid_barrier(c);
       if (!c.ok) break;
-      trace_mark(c, e0 + 10);
+      trace_mark(c, e0 + 13);
     }
     if (!c.ok) break;
     if (t >= P.logits_from) {
@@ -998,6 +1012,7 @@ __device__ void run_consumers(const DecodeLaunch& P, Smem* s) {
       if (!c.ok) break;
       trace_mark(c, el + 2);
       if (c.tracing && c.tid == 0) {
+        P.trace[blockIdx.x * kTraceEvents + kTraceEvents - 3] = c.tile_ns;
         P.trace[blockIdx.x * kTraceEvents + kTraceEvents - 2] = c.full_wait_ns;
         P.trace[blockIdx.x * kTraceEvents + kTraceEvents - 1] = c.bar_wait_ns;
       }
@@ -1046,6 +1061,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s->empty[i], kConsumerWarps);
     }
     fence_mbar_init();
+  }
+  static_assert(sizeof(DevModel) % 8 == 0, "the model description copies as 8-byte words");
+  for (uint32_t i = threadIdx.x; i < sizeof(DevModel) / 8; i += blockDim.x) {
+    reinterpret_cast<uint64_t*>(s->model)[i] = __ldg(reinterpret_cast<const uint64_t*>(P.model) + i);
   }
   __syncthreads();
   if (threadIdx.x >= kConsumerThreads) {

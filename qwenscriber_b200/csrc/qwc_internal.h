@@ -120,7 +120,7 @@ struct alignas(64) KvMaps {
 };
 
 constexpr uint32_t kTraceEvents = 512;
-constexpr uint32_t kTraceEventsPerLayer = 11;
+constexpr uint32_t kTraceEventsPerLayer = 14;
 
 }  // namespace qwc
 

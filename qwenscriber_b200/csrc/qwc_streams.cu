@@ -39,6 +39,29 @@ constexpr int kNormPer4 = kHiddenMax / 4 / kNormThreads;  // float4 groups per t
 // Position of element e (0..7) of a chunk in the activation layout.
 __device__ __forceinline__ uint32_t chunk_slot(uint32_t e) { return ((e & 3u) << 1) | (e >> 2); }
 
+__device__ __forceinline__ float4 add4(float4 a, float4 b) { return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w); }
+__device__ __forceinline__ float add4(float a, float b) { return a + b; }
+
+// Sum of a projection's split-K partials p[0], p[stride], ... in split
+// order. The loads of B partials are issued before their adds, so a sum
+// costs one L2 round trip per B splits rather than one per split.
+template <int B, typename T>
+__device__ __forceinline__ T sum_splits(const T* p, size_t stride, uint32_t splits) {
+  T y = p[0];
+  for (uint32_t s0 = 1; s0 < splits; s0 += B) {
+    T t[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      if (s0 + b < splits) t[b] = p[size_t(s0 + b) * stride];
+    }
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      if (s0 + b < splits) y = add4(y, t[b]);
+    }
+  }
+  return y;
+}
+
 // Writes 8 f32 values (K order k0..k0+7) as one 16-byte chunk of the
 // activation layout: f16 hi values at `dst`, the f16 remainders x - hi at
 // `dst + lo_offset` (the slot's lo row).
@@ -120,17 +143,8 @@ __global__ void __launch_bounds__(kNormThreads) streams_norm_kernel(const Stream
         // The projection is the sum of its split-K partials, then the
         // residual add (kernels.zig:221-230).
         const float4* pp = reinterpret_cast<const float4*>(parts) + size_t(s) * h4 + k4;
-        const size_t stride = size_t(kMaxStreams) * h4;
-        float4 y = pp[0];
-#pragma unroll 4
-        for (uint32_t sp = 1; sp < splits; ++sp) {
-          const float4 t = pp[sp * stride];
-          y.x += t.x;
-          y.y += t.y;
-          y.z += t.z;
-          y.w += t.w;
-        }
         const float4 r = h[k4];
+        const float4 y = sum_splits<8>(pp, size_t(kMaxStreams) * h4, splits);
         x = make_float4(r.x + y.x, r.y + y.y, r.z + y.z, r.w + y.w);
       }
       h[k4] = x;
@@ -181,12 +195,10 @@ __global__ void __launch_bounds__(256) streams_qkv_kernel(const StreamsStep P, u
   const uint32_t qw = m.q_heads * kHeadDim, kvw = m.kv_heads * kHeadDim;
   const uint32_t rows = qw + 2 * kvw;
   const int tid = threadIdx.x, j = tid / kHeadDim, dd = tid % kHeadDim, warp = tid / 32, lane = tid % 32;
-  float qraw = 0.0f, kvraw = 0.0f;
-  for (uint32_t sp = 0; sp < splits; ++sp) {
-    const float* row = P.part0 + (size_t(sp) * kMaxStreams + s) * rows;
-    qraw += row[(2 * h + j) * kHeadDim + dd];
-    kvraw += row[qw + j * kvw + h * kHeadDim + dd];
-  }
+  const float* row = P.part0 + size_t(s) * rows;
+  const size_t stride = size_t(kMaxStreams) * rows;
+  const float qraw = sum_splits<8>(row + (2 * h + j) * kHeadDim + dd, stride, splits);
+  const float kvraw = sum_splits<8>(row + qw + j * kvw + h * kHeadDim + dd, stride, splits);
   const DevLayer& L = m.layers[layer];
   const float ss = warp_sum(qraw * qraw), kss = warp_sum(kvraw * kvraw);
   if (lane == 0) {
@@ -258,19 +270,15 @@ static_assert(kTV % 128 == 0 && kTKS % 128 == 0 && kTVS % 128 == 0 && kTileBytes
 struct __align__(128) AttnSmem {
   uint8_t ring[kAttnSlots][kTileBytes];
   alignas(16) float q[2][4][36];   // rotated queries, 32-dim quarters padded against bank conflicts
-  alignas(16) float prob[2][kAttnChunk];
-  alignas(16) float vpart[8][2][kHeadDim];
-  alignas(16) float red[2][8];
-  alignas(16) float lsum[2][8];
-  float mnew[2];
+  alignas(16) float vpart[8][2][kHeadDim];  // per-warp outputs at a segment's end
+  alignas(16) float red[2][8];              // per-warp running maxima
+  alignas(16) float lsum[2][8];             // per-warp running sums
   uint32_t prefix[kMaxStreams + 1];
   uint32_t flag;
   alignas(8) uint64_t full[kAttnSlots];
   alignas(8) uint64_t empty[kAttnSlots];
 };
-static_assert(offsetof(AttnSmem, vpart) % 16 == 0 && offsetof(AttnSmem, q) % 16 == 0 &&
-                  offsetof(AttnSmem, prob) % 16 == 0,
-              "vector access alignment");
+static_assert(offsetof(AttnSmem, vpart) % 16 == 0 && offsetof(AttnSmem, q) % 16 == 0, "vector access alignment");
 
 __device__ __forceinline__ void tma_load_4d(void* dst, const void* map, int32_t x, int32_t y, int32_t z, int32_t w,
                                             uint64_t* bar) {
@@ -357,23 +365,59 @@ __global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kern
     return;
   }
 
-  // ---- consumers: 256 threads; thread (j, d) owns output dim d of query head 2h + j ----
+  // ---- consumers: 8 warps; warp w takes positions 8w..8w+7 of every tile ----
+  //
+  // Each warp carries its own online softmax (running max, sum and output
+  // per query head) across the units of a (slot, head) segment, so a unit
+  // needs no block-wide synchronisation: the warps meet only when a segment
+  // ends, where their states are merged (flash-decode rescale).
+  // Scores: lane (i, qd) = (lane / 4, lane % 4) holds position 8w + i, dims
+  // 32 qd .. 32 qd + 31; the two lanes of a 64-value group add their sums
+  // before the group scale (q8GroupDot, kernels.zig:636-661).
+  // Values: lane l holds output dims 4 l .. 4 l + 3 of both query heads.
   const int j = tid / kHeadDim, dd = tid % kHeadDim;
-  const uint32_t rr = static_cast<uint32_t>(tid) / 4, qd = static_cast<uint32_t>(tid) % 4;
+  const uint32_t pi = static_cast<uint32_t>(lane) / 4, qd = static_cast<uint32_t>(lane) % 4;
+  const uint32_t prow = static_cast<uint32_t>(warp) * 8 + pi;  // this lane's score row in the tile
   const uint32_t grp = static_cast<uint32_t>(lane) / 16;
   bool ok = true;
-  float o_run = 0.0f, l_run = 0.0f, m_run = -INFINITY;
+  float wm[2] = {-INFINITY, -INFINITY}, wl[2] = {0.0f, 0.0f};
+  float wo[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
   UnitPos cur{0xFFFFFFFFu, 0xFFFFFFFFu, 0, 0, 0};
   uint32_t seg_first = 0, seg_count = 0;
 
-  // Emits the running state of the current (slot, head) segment.
+  // Merges the warps' states of the current (slot, head) segment and emits
+  // it: the final output when the segment covers every chunk of the head,
+  // else a partial for the last-arriving CTA to combine.
   auto flush = [&]() {
+    if (lane == 0) {
+      a->red[0][warp] = wm[0];
+      a->red[1][warp] = wm[1];
+      a->lsum[0][warp] = wl[0];
+      a->lsum[1][warp] = wl[1];
+    }
+    *reinterpret_cast<float4*>(&a->vpart[warp][0][4 * lane]) = make_float4(wo[0][0], wo[0][1], wo[0][2], wo[0][3]);
+    *reinterpret_cast<float4*>(&a->vpart[warp][1][4 * lane]) = make_float4(wo[1][0], wo[1][1], wo[1][2], wo[1][3]);
+    consumer_sync(kAttnConsumers);
+    float m_run = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) m_run = fmaxf(m_run, a->red[j][w]);
+    float o_run = 0.0f, l_run = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const float mw = a->red[j][w];
+      if (mw != -INFINITY) {
+        const float f = expf(mw - m_run);
+        o_run = fmaf(a->vpart[w][j][dd], f, o_run);
+        l_run = fmaf(a->lsum[j][w], f, l_run);
+      }
+    }
     __half* xq = static_cast<__half*>(P.xb_q) + size_t(cur.s) * qw;
     const size_t xq_lo = size_t(kMaxStreams) * qw;
     const uint32_t col = (2 * cur.h + j) * kHeadDim + dd;
     const uint32_t out_index = (col & ~7u) | chunk_slot(col & 7u);
     if (seg_count == cur.chunks) {
       store_one(xq + out_index, xq_lo, o_run / l_run);
+      consumer_sync(kAttnConsumers);  // red / vpart reused by the next segment
       return;
     }
     float* part = P.attn_part + ((size_t(cur.s) * m.q_heads + 2 * cur.h + j) * P.max_chunks + seg_first) * (kHeadDim + 2);
@@ -421,38 +465,37 @@ __global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kern
     consumer_sync(kAttnConsumers);
   };
 
+  const float scaling = m.attn_scaling;
+  const uint64_t bias = pack2(kNegQ8, kNegQ8);
   uint32_t it = 0;
   for (uint32_t u = u0; u < u1; ++u, ++it) {
     const UnitPos up = unit_pos(a, P, kv_heads, u);
     if (up.s != cur.s || up.h != cur.h) {
-      if (cur.s != 0xFFFFFFFFu) flush();
+      if (cur.s != 0xFFFFFFFFu) flush();  // ends with every warp past the previous segment
       cur = up;
       seg_first = up.ch;
       seg_count = 0;
-      o_run = 0.0f;
-      l_run = 0.0f;
-      m_run = -INFINITY;
+      wm[0] = wm[1] = -INFINITY;
+      wl[0] = wl[1] = 0.0f;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) wo[0][t] = wo[1][t] = 0.0f;
       a->q[j][dd / 32][dd % 32] = P.qrot[size_t(up.s) * qw + (2 * up.h + j) * kHeadDim + dd];
+      consumer_sync(kAttnConsumers);
     }
     const uint32_t slot = it % kAttnSlots;
-    if (ok && !mbar_wait_bounded(&a->full[slot], (it / kAttnSlots) & 1u, P.error, P.timeout_ns,
-                                 101)) {
+    if (ok && !mbar_wait_bounded(&a->full[slot], (it / kAttnSlots) & 1u, P.error, P.timeout_ns, 101)) {
       ok = false;
     }
-    consumer_sync(kAttnConsumers);  // q written, tile landed
     const uint8_t* tile = a->ring[slot];
     const uint32_t newest = P.desc[up.s].position;
-    // Scores: four lanes per position; the two lanes of a 64-value group add
-    // their sums before the group scale (q8GroupDot, kernels.zig:636-661).
-    const uint32_t pos = up.ch * kAttnChunk + rr;
-    const bool valid = ok && pos <= newest;
-    float sc0, sc1;
+    const uint32_t base_pos = up.ch * kAttnChunk + static_cast<uint32_t>(warp) * 8;
+    const bool valid = ok && base_pos + pi <= newest;
+    float s0, s1;
     {
-      const uint4* src = reinterpret_cast<const uint4*>(tile + kTK + rr * kHeadDim + qd * 32);
+      const uint4* src = reinterpret_cast<const uint4*>(tile + kTK + prow * kHeadDim + qd * 32);
       const uint4 kw0 = src[0], kw1 = src[1];
-      const uint32_t kbits = *reinterpret_cast<const uint16_t*>(tile + kTKS + rr * 16 + (up.h % 4) * 4 + (qd / 2) * 2);
+      const uint32_t kbits = *reinterpret_cast<const uint16_t*>(tile + kTKS + prow * 16 + (up.h % 4) * 4 + (qd / 2) * 2);
       const uint32_t words[8] = {kw0.x, kw0.y, kw0.z, kw0.w, kw1.x, kw1.y, kw1.z, kw1.w};
-      const uint64_t bias = pack2(kNegQ8, kNegQ8);
       uint64_t acc0 = 0, acc1 = 0;
 #pragma unroll
       for (int w = 0; w < 8; ++w) {
@@ -476,77 +519,57 @@ __global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kern
       g1 *= scale;
       g0 += __shfl_xor_sync(0xffffffffu, g0, 2);
       g1 += __shfl_xor_sync(0xffffffffu, g1, 2);
-      sc0 = valid ? m.attn_scaling * g0 : -INFINITY;
-      sc1 = valid ? m.attn_scaling * g1 : -INFINITY;
-      const float w0 = warp_max(sc0), w1 = warp_max(sc1);
-      if (lane == 0) {
-        a->red[0][warp] = w0;
-        a->red[1][warp] = w1;
+      s0 = valid ? scaling * g0 : -INFINITY;
+      s1 = valid ? scaling * g1 : -INFINITY;
+    }
+    // Online softmax over this warp's 8 positions (math.zig:77-93 subtracts
+    // the row max before exp); the 4 lanes of a position hold equal scores.
+    float mx0 = s0, mx1 = s1;
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+    }
+    const float mn0 = fmaxf(wm[0], mx0), mn1 = fmaxf(wm[1], mx1);
+    const float p0 = valid ? expf(s0 - mn0) : 0.0f;
+    const float p1 = valid ? expf(s1 - mn1) : 0.0f;
+    const float r0 = (wm[0] == -INFINITY) ? 0.0f : expf(wm[0] - mn0);
+    const float r1 = (wm[1] == -INFINITY) ? 0.0f : expf(wm[1] - mn1);
+    float ls0 = p0, ls1 = p1;
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      ls0 += __shfl_xor_sync(0xffffffffu, ls0, o);
+      ls1 += __shfl_xor_sync(0xffffffffu, ls1, o);
+    }
+    wl[0] = fmaf(wl[0], r0, ls0);
+    wl[1] = fmaf(wl[1], r1, ls1);
+    wm[0] = mn0;
+    wm[1] = mn1;
+    // Values (q8GroupAccumulate, kernels.zig:665-688).
+    float acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t row = static_cast<uint32_t>(warp) * 8 + i;
+      const uint32_t word = *reinterpret_cast<const uint32_t*>(tile + kTV + row * kHeadDim + 4 * lane);
+      const uint32_t bits = *reinterpret_cast<const uint16_t*>(tile + kTVS + row * 16 + (up.h % 4) * 4 + grp * 2);
+      const float scale = f16_bits_to_f32_fast(bits);
+      const float q0 = __shfl_sync(0xffffffffu, p0, 4 * i), q1 = __shfl_sync(0xffffffffu, p1, 4 * i);
+      const float sw0 = scale * q0, sw1 = scale * q1;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float cv = bits_f32(__byte_perm(word, kMagic, 0x7440 + t)) + kNegQ8;
+        acc[0][t] = fmaf(cv, sw0, acc[0][t]);
+        acc[1][t] = fmaf(cv, sw1, acc[1][t]);
       }
     }
-    consumer_sync(kAttnConsumers);
-    float cm0 = -INFINITY, cm1 = -INFINITY;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&a->empty[slot]);  // this warp is done with the tile
 #pragma unroll
-    for (int w = 0; w < 8; ++w) {
-      cm0 = fmaxf(cm0, a->red[0][w]);
-      cm1 = fmaxf(cm1, a->red[1][w]);
+    for (int t = 0; t < 4; ++t) {
+      wo[0][t] = fmaf(wo[0][t], r0, acc[0][t]);
+      wo[1][t] = fmaf(wo[1][t], r1, acc[1][t]);
     }
-    // Online softmax (math.zig:77-93 subtracts the row max before exp). The
-    // threads of a head share its running max; the probabilities need both
-    // heads' new maxima, published through shared memory.
-    const float m_new = fmaxf(m_run, j == 0 ? cm0 : cm1);
-    if (dd == 0) a->mnew[j] = m_new;
-    consumer_sync(kAttnConsumers);
-    const float mh0 = a->mnew[0], mh1 = a->mnew[1];
-    const float p0 = valid ? expf(sc0 - mh0) : 0.0f;
-    const float p1 = valid ? expf(sc1 - mh1) : 0.0f;
-    if (qd == 0) {
-      a->prob[0][rr] = p0;
-      a->prob[1][rr] = p1;
-    }
-    const float l0 = warp_sum(qd == 0 ? p0 : 0.0f), l1 = warp_sum(qd == 0 ? p1 : 0.0f);
-    if (lane == 0) {
-      a->lsum[0][warp] = l0;
-      a->lsum[1][warp] = l1;
-    }
-    consumer_sync(kAttnConsumers);
-    // Values (q8GroupAccumulate, kernels.zig:665-688): lane = 4 dims, warp = 8 positions.
-    {
-      float acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const uint32_t q = warp * 8 + i;
-        const uint32_t word = *reinterpret_cast<const uint32_t*>(tile + kTV + q * kHeadDim + 4 * lane);
-        const uint32_t bits = *reinterpret_cast<const uint16_t*>(tile + kTVS + q * 16 + (up.h % 4) * 4 + grp * 2);
-        const float scale = f16_bits_to_f32_fast(bits);
-        const bool vq = ok && up.ch * kAttnChunk + q <= newest;
-        const float sw0 = vq ? scale * a->prob[0][q] : 0.0f;
-        const float sw1 = vq ? scale * a->prob[1][q] : 0.0f;
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const float cv = bits_f32(__byte_perm(word, kMagic, 0x7440 + t)) + kNegQ8;
-          acc[0][t] = fmaf(cv, sw0, acc[0][t]);
-          acc[1][t] = fmaf(cv, sw1, acc[1][t]);
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&a->empty[slot]);  // this warp is done with the tile
-      *reinterpret_cast<float4*>(&a->vpart[warp][0][4 * lane]) = make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
-      *reinterpret_cast<float4*>(&a->vpart[warp][1][4 * lane]) = make_float4(acc[1][0], acc[1][1], acc[1][2], acc[1][3]);
-    }
-    consumer_sync(kAttnConsumers);
-    float o = 0.0f, l = 0.0f;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) {
-      o += a->vpart[w][j][dd];
-      l += a->lsum[j][w];
-    }
-    const float rescale = (m_run == -INFINITY) ? 0.0f : expf(m_run - m_new);
-    o_run = o_run * rescale + o;
-    l_run = l_run * rescale + l;
-    m_run = m_new;
     ++seg_count;
-    consumer_sync(kAttnConsumers);  // vpart / prob / red reused by the next unit
   }
   if (cur.s != 0xFFFFFFFFu) flush();
 }
@@ -566,17 +589,16 @@ __global__ void streams_swiglu_kernel(const StreamsStep P, uint32_t splits) {
       continue;
     }
     // Gate rows at [0, ffn), up rows at [ffn, 2 ffn) of each partial row.
+    const float4* g4 = reinterpret_cast<const float4*>(P.part0 + size_t(s) * 2 * ffn + c * 8);
+    const float4* u4 = reinterpret_cast<const float4*>(P.part0 + size_t(s) * 2 * ffn + ffn + c * 8);
+    const size_t stride = size_t(kMaxStreams) * 2 * ffn / 4;
+    const float4 ga = sum_splits<4>(g4, stride, splits), gb = sum_splits<4>(g4 + 1, stride, splits);
+    const float4 ua = sum_splits<4>(u4, stride, splits), ub = sum_splits<4>(u4 + 1, stride, splits);
+    const float g[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+    const float u[8] = {ua.x, ua.y, ua.z, ua.w, ub.x, ub.y, ub.z, ub.w};
     float v[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const size_t idx = size_t(s) * 2 * ffn + c * 8 + e;
-      float g = P.part0[idx], u = P.part0[idx + ffn];
-      for (uint32_t sp = 1; sp < splits; ++sp) {
-        g += P.part0[size_t(sp) * kMaxStreams * 2 * ffn + idx];
-        u += P.part0[size_t(sp) * kMaxStreams * 2 * ffn + idx + ffn];
-      }
-      v[e] = g / (1.0f + expf(-g)) * u;
-    }
+    for (int e = 0; e < 8; ++e) v[e] = g[e] / (1.0f + expf(-g[e])) * u[e];
     store_chunk(dst, lo, v);
   }
 }
@@ -592,11 +614,23 @@ __global__ void __launch_bounds__(1024) streams_argmax_kernel(const StreamsStep 
   const float* row = P.logits + size_t(s) * vocab;
   float bv = -INFINITY;
   uint32_t bi = 0xFFFFFFFFu;
-  for (uint32_t i = threadIdx.x; i < vocab; i += blockDim.x) {
-    const float v = row[i];
-    if (v > bv || (v == bv && i < bi)) {
-      bv = v;
-      bi = i;
+  // Eight independent loads per thread per round; a thread's indices ascend
+  // within and across rounds, so strict > keeps its first maximum.
+  constexpr uint32_t kUnroll = 8;
+  for (uint32_t i0 = threadIdx.x; i0 < vocab; i0 += kUnroll * blockDim.x) {
+    float v[kUnroll];
+#pragma unroll
+    for (uint32_t r = 0; r < kUnroll; ++r) {
+      const uint32_t i = i0 + r * blockDim.x;
+      v[r] = i < vocab ? row[i] : -INFINITY;
+    }
+#pragma unroll
+    for (uint32_t r = 0; r < kUnroll; ++r) {
+      const uint32_t i = i0 + r * blockDim.x;
+      if (i < vocab && (v[r] > bv || (v[r] == bv && i < bi))) {
+        bv = v[r];
+        bi = i;
+      }
     }
   }
 #pragma unroll

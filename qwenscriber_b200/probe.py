@@ -1,6 +1,7 @@
 """Runs one workload for profiling: load, prefill, then a few device-timed steps.
 
     python -m qwenscriber_b200.probe [--workload NAME] [--steps K]
+    python -m qwenscriber_b200.probe --gemm ROWS COLS [--steps K]
 
 Single-stream workloads prefill with qwc_decode_begin and time K greedy
 steps of the persistent decode kernel (qwc_decode_run_timed); multi-stream
@@ -8,6 +9,11 @@ workloads begin every slot (tensor-core prefill) and time K batched steps
 (qwc_streams_run_timed). Prints the device time and the kernels launched
 before the timed steps, which is the skip count a profiler needs to land on
 them.
+
+--gemm times K calls of qwc_op_gemm_streams on a random q4 matrix of ROWS x
+COLS against 64 stream columns, after 3 untimed calls: each call launches the
+activation packing, the GEMM and the split-K sum; a profiler filtered on
+gemm_streams_kernel skips 3 launches to land on the first timed one.
 """
 
 from __future__ import annotations
@@ -15,6 +21,7 @@ from __future__ import annotations
 import argparse
 import sys
 
+from . import quant
 from . import runtime as rt
 from . import synthetic
 
@@ -25,7 +32,10 @@ def main(argv=None) -> int:
     p.add_argument("--steps", type=int, default=1)
     p.add_argument("--chunk", type=int, default=16, help="decode steps per launch (single stream)")
     p.add_argument("--streams", type=int, default=0, help="override the workload's streams per GPU")
+    p.add_argument("--gemm", type=int, nargs=2, metavar=("ROWS", "COLS"), help="time the stream GEMM op alone")
     a = p.parse_args(argv)
+    if a.gemm:
+        return gemm(*a.gemm, a.steps)
     w = synthetic.workloads()[a.workload]
     if a.streams:
         import dataclasses
@@ -53,6 +63,37 @@ def main(argv=None) -> int:
     print(f"{w.name}: {a.steps} steps, {ms / a.steps:.3f} ms/step, {tokens / (ms / 1000.0):.0f} tokens/s; "
           f"kernels before the timed steps: {before}")
     gm.close()
+    return 0
+
+
+def gemm(rows: int, cols: int, reps: int) -> int:
+    import numpy as np
+    import torch
+
+    L = rt.lib()
+    rng = np.random.default_rng(0)
+    groups = cols // 64
+    scales = torch.from_numpy((np.abs(rng.standard_normal((rows, groups))) * 0.003).astype(np.float16)
+                              .view(np.uint16)).cuda()
+    codes = torch.from_numpy(rng.integers(0, 256, size=(rows, groups * 32), dtype=np.uint8)).cuda()
+    x = torch.randn(64, cols, device="cuda")
+    out = torch.zeros(64, rows, device="cuda")
+
+    def call():
+        rt.check(L.qwc_op_gemm_streams(quant.Q4, scales.data_ptr(), codes.data_ptr(), rows, cols,
+                                       x.data_ptr(), 64, out.data_ptr(), None), "qwc_op_gemm_streams")
+
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / reps
+    print(f"stream gemm q4 {rows} x {cols}, 64 columns: {us:.1f} us per op call (packing + GEMM + split-K sum)")
     return 0
 
 
