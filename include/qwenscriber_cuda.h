@@ -209,12 +209,12 @@ int32_t qwc_debug_hold(uint32_t handle, uint32_t slot, int64_t force, uint32_t* 
  * (before QK-norm and RoPE), 2 = attention output, 3 = silu(gate) * up. */
 int32_t qwc_debug_scratch(uint32_t handle, uint32_t which, float* out, uint32_t count);
 /* Phase timeline of the last launch (QWC_OPTION_TRACE): grid x 512 nanosecond
- * stamps, 14 per layer (layer start, QKV input ready, QKV done, barrier,
- * attention done, barrier, O done, barrier, FFN input ready, gate done,
- * up done, barrier, down input ready, down done + barrier) then lm_head
- * start, done, barrier; the last three words of a CTA's row are its thread
- * 0's time with streamed tiles in hand, waiting for tiles, and waiting at
- * grid barriers. Returns the count. */
+ * stamps. A token walks six stages per layer (QKV, attention, O, gate, up,
+ * down) and then the lm_head stage; each stage records three stamps (input
+ * ready, output done, grid barrier passed; gate has no barrier of its own).
+ * The last three words of a CTA's row are its thread 0's time with streamed
+ * tiles in hand, waiting for tiles, and waiting at grid barriers. Returns
+ * the count. */
 int32_t qwc_debug_trace(uint32_t handle, uint64_t* out, uint32_t count);
 /* Raw key (which = 0) or value (which = 1) cache bytes of `slot`, in the
  * reference's layer-major two-plane layout (src/core/qwen3_asr/decoder.zig:45-65). */

@@ -60,7 +60,17 @@ static_assert(kTileVCodes % 128 == 0 && kTileKScales % 128 == 0 && kTileVScales 
                   kTileCos % 16 == 0 && kTileSin % 16 == 0,
               "TMA boxes land on 128-byte boundaries, bulk copies on 16-byte boundaries");
 
-enum Stage : int { kStQKV = 0, kStO = 1, kStGate = 2, kStUp = 3, kStDown = 4, kStLM = 5 };
+enum Stage : int { kStQKV = 0, kStO = 1, kStGate = 2, kStUp = 3, kStDown = 4, kStLM = 5, kStAttn = 6 };
+
+// A token is a walk over stages: six per layer in this order, then the
+// lm_head stage for tokens with logits. The producer and the consumers run
+// the same walk, each with one code path per kind of stage, so the code a
+// layer executes stays small enough to remain in the instruction cache.
+constexpr int kStagesPerLayer = 6;
+__device__ __forceinline__ int layer_stage(uint32_t i) {
+  // QKV, attention, O, gate, up, down (decoder.zig:165-271).
+  return i == 0 ? kStQKV : i == 1 ? kStAttn : i == 2 ? kStO : i == 3 ? kStGate : i == 4 ? kStUp : kStDown;
+}
 
 enum ErrorCode : int32_t { kErrBarrier = 1, kErrFull = 2, kErrEmpty = 3, kErrShape = 4 };
 
@@ -306,18 +316,20 @@ __device__ void run_producer(const DecodeLaunch& P, const KvMaps& maps, Smem* s)
   Producer pr{s, 0, P.error, P.timeout_ns, true};
   for (uint32_t t = 0; t < P.n_tokens && pr.ok; ++t) {
     const uint32_t position = P.first_position + t;
-    for (uint32_t l = 0; l < m.n_layers && pr.ok; ++l) {
-      const DevLayer& L = m.layers[l];
-      pr.vector_tile(L.attn_norm, m.hidden);
-      if (pr.ok) pr.stage(m, l, kStQKV);
-      if (pr.ok) pr.attention_tiles(m, maps, l, position);
-      if (pr.ok) pr.stage(m, l, kStO);
-      if (pr.ok) pr.vector_tile(L.ffn_norm, m.hidden);
-      for (int st = kStGate; st <= kStDown && pr.ok; ++st) pr.stage(m, l, st);
-    }
-    if (t >= P.logits_from && pr.ok) {
-      pr.vector_tile(m.final_norm, m.hidden);
-      if (pr.ok) pr.stage(m, 0, kStLM);
+    const uint32_t walk = m.n_layers * kStagesPerLayer + (t >= P.logits_from ? 1u : 0u);
+    for (uint32_t q = 0; q < walk && pr.ok; ++q) {
+      const uint32_t l = q / kStagesPerLayer;
+      const int st = l < m.n_layers ? layer_stage(q % kStagesPerLayer) : kStLM;
+      if (st == kStQKV || st == kStGate || st == kStLM) {
+        const float* norm = st == kStQKV ? m.layers[l].attn_norm : st == kStGate ? m.layers[l].ffn_norm : m.final_norm;
+        pr.vector_tile(norm, m.hidden);
+      }
+      if (!pr.ok) break;
+      if (st == kStAttn) {
+        pr.attention_tiles(m, maps, l, position);
+      } else {
+        pr.stage(m, st == kStLM ? 0 : l, st);
+      }
     }
   }
   if (!pr.ok) pr.drain();
@@ -346,7 +358,7 @@ __device__ bool error_set(const int32_t* e) { return *reinterpret_cast<const vol
 
 // Phase timeline (DecodeLaunch::trace): event e of the traced token.
 __device__ __forceinline__ void trace_mark(const Ctx& c, uint32_t e) {
-  if (c.tracing && c.tid == 0 && e < kTraceEvents) c.P->trace[blockIdx.x * kTraceEvents + e] = global_timer_ns();
+  if (c.tracing && c.tid == 0 && e < kTraceEvents - 3) c.P->trace[blockIdx.x * kTraceEvents + e] = global_timer_ns();
 }
 
 // Waits (bounded) for the next streamed tile and returns its slot. Every
@@ -417,28 +429,51 @@ __device__ float block_sum(Ctx& c, float v) {
   return total;
 }
 
-// Multiplies x[k] by 16^-(nibble position) for q4 stages (see qwc_device.cuh).
-__device__ __forceinline__ float prescale(float v, uint32_t k, bool q4) { return q4 ? v * q4_xscale(k & 7u) : v; }
+// x holds activations multiplied by 16^-(nibble position) for q4 stages
+// (see qwc_device.cuh), so the GEMV can OR nibbles into floats in place.
 
-constexpr int kMaxPerThread = (kHiddenMax + kConsumerThreads - 1) / kConsumerThreads;
+constexpr int kMaxPer4 = (kHiddenMax / 4 + kConsumerThreads - 1) / kConsumerThreads;  // float4 groups per thread
+
+// x[k .. k + 3] <- v, prescaled for q4 stages; k is a multiple of 4.
+__device__ __forceinline__ void store_x4(Ctx& c, uint32_t k, float4 v, bool q4) {
+  if (q4) {
+    // q4_xscale over k & 7 = 0..3 or 4..7.
+    const bool hi = (k & 4u) != 0;
+    v.x *= hi ? q4_xscale(4) : q4_xscale(0);
+    v.y *= hi ? q4_xscale(5) : q4_xscale(1);
+    v.z *= hi ? q4_xscale(6) : q4_xscale(2);
+    v.w *= hi ? q4_xscale(7) : q4_xscale(3);
+  }
+  *reinterpret_cast<float4*>(&c.s->x[x_index(k)]) = v;
+}
 
 // x <- rmsnorm(raw) * weight (math.zig:120-130: value * inverse_rms * weight),
-// stored prescaled for q4 stages. `raw` holds this thread's values
-// (k = tid + i * kConsumerThreads); the weight vector is the next streamed tile.
-__device__ void normalize_into_x(Ctx& c, const float (&raw)[kMaxPerThread], uint32_t width, bool q4) {
+// stored prescaled for q4 stages. `raw` holds this thread's float4 groups
+// (k = 4 * (tid + i * kConsumerThreads)); the weight vector is the next
+// streamed tile.
+__device__ void normalize_into_x(Ctx& c, const float4 (&raw)[kMaxPer4], uint32_t width, bool q4) {
   float ss = 0.0f;
 #pragma unroll
-  for (int i = 0; i < kMaxPerThread; ++i) {
-    const uint32_t k = c.tid + i * kConsumerThreads;
-    if (k < width) ss = fmaf(raw[i], raw[i], ss);
+  for (int i = 0; i < kMaxPer4; ++i) {
+    if (c.tid + i * kConsumerThreads < width / 4) {
+      ss = fmaf(raw[i].x, raw[i].x, ss);
+      ss = fmaf(raw[i].y, raw[i].y, ss);
+      ss = fmaf(raw[i].z, raw[i].z, ss);
+      ss = fmaf(raw[i].w, raw[i].w, ss);
+    }
   }
   const float total = block_sum(c, ss);
   const float inv = 1.0f / sqrtf(total / static_cast<float>(width) + c.m->eps);
-  const float* weight = reinterpret_cast<const float*>(acquire_tile(c));
+  const float4* weight = reinterpret_cast<const float4*>(acquire_tile(c));
 #pragma unroll
-  for (int i = 0; i < kMaxPerThread; ++i) {
-    const uint32_t k = c.tid + i * kConsumerThreads;
-    if (k < width) c.s->x[x_index(k)] = prescale(raw[i] * inv * weight[k], k, q4);
+  for (int i = 0; i < kMaxPer4; ++i) {
+    const uint32_t k4 = c.tid + i * kConsumerThreads;
+    if (k4 < width / 4) {
+      const float4 w = weight[k4];
+      store_x4(c, 4 * k4,
+               make_float4(raw[i].x * inv * w.x, raw[i].y * inv * w.y, raw[i].z * inv * w.z, raw[i].w * inv * w.w),
+               q4);
+    }
   }
   release_tile(c);
   consumer_sync(kConsumerThreads);
@@ -446,11 +481,11 @@ __device__ void normalize_into_x(Ctx& c, const float (&raw)[kMaxPerThread], uint
 
 // x <- rmsnorm(hidden) * weight for a hidden vector other CTAs wrote (L2 loads).
 __device__ void norm_global_into_x(Ctx& c, const float* src, uint32_t width, bool q4) {
-  float raw[kMaxPerThread];
+  float4 raw[kMaxPer4];
 #pragma unroll
-  for (int i = 0; i < kMaxPerThread; ++i) {
-    const uint32_t k = c.tid + i * kConsumerThreads;
-    raw[i] = k < width ? ld_cg(src + k) : 0.0f;
+  for (int i = 0; i < kMaxPer4; ++i) {
+    const uint32_t k4 = c.tid + i * kConsumerThreads;
+    raw[i] = k4 < width / 4 ? ld_cg4(reinterpret_cast<const float4*>(src) + k4) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   normalize_into_x(c, raw, width, q4);
 }
@@ -458,13 +493,7 @@ __device__ void norm_global_into_x(Ctx& c, const float* src, uint32_t width, boo
 // Copies a vector other CTAs wrote into x (L2-coherent loads), prescaled for q4.
 __device__ void load_x_global(Ctx& c, const float* src, uint32_t width, bool q4) {
   for (uint32_t k4 = c.tid; k4 < width / 4; k4 += kConsumerThreads) {
-    float4 v = ld_cg4(reinterpret_cast<const float4*>(src) + k4);
-    const uint32_t k = k4 * 4;
-    v.x = prescale(v.x, k, q4);
-    v.y = prescale(v.y, k + 1, q4);
-    v.z = prescale(v.z, k + 2, q4);
-    v.w = prescale(v.w, k + 3, q4);
-    *reinterpret_cast<float4*>(&c.s->x[x_index(k)]) = v;
+    store_x4(c, 4 * k4, ld_cg4(reinterpret_cast<const float4*>(src) + k4), q4);
   }
   consumer_sync(kConsumerThreads);
 }
@@ -474,33 +503,42 @@ __device__ void load_x_global(Ctx& c, const float* src, uint32_t width, bool q4)
 __device__ void input_into_x(Ctx& c, uint32_t token, int32_t audio_row, Span own, bool q4) {
   const DevModel& m = *c.m;
   const uint32_t hidden = m.hidden;
-  float raw[kMaxPerThread];
+  float4 raw[kMaxPer4];
   const DevMat& e = m.embed;
-  const uint32_t e_format = e.format;
   const uint8_t* srow = e.scales + size_t(token) * e.scale_row;
   const uint8_t* crow = e.codes + size_t(token) * e.code_row;
   const float* arow = c.P->audio + size_t(audio_row < 0 ? 0 : audio_row) * hidden;
 #pragma unroll
-  for (int i = 0; i < kMaxPerThread; ++i) {
-    const uint32_t k = c.tid + i * kConsumerThreads;
-    float v = 0.0f;
-    if (k < hidden) {
+  for (int i = 0; i < kMaxPer4; ++i) {
+    const uint32_t k4 = c.tid + i * kConsumerThreads;
+    float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (k4 < hidden / 4) {
+      const uint32_t k = 4 * k4;
       if (audio_row >= 0) {
-        v = __ldg(arow + k);
+        const float4 a = __ldg(reinterpret_cast<const float4*>(arow) + k4);
+        v[0] = a.x;
+        v[1] = a.y;
+        v[2] = a.z;
+        v[3] = a.w;
       } else {
+        // The four values share one group: code (u - bias) times the group's scale.
         const float scale = f16_bits_to_f32_fast(__ldg(reinterpret_cast<const uint16_t*>(srow) + k / kGroup));
-        int code;
-        if (e_format == kFormatQ4) {
-          const uint8_t b = __ldg(crow + k / 2);
-          code = static_cast<int>((k & 1u) ? (b >> 4) : (b & 0x0F)) - 8;
+        if (e.format == kFormatQ4) {
+          const uint32_t b = __ldg(reinterpret_cast<const uint16_t*>(crow + k / 2));
+#pragma unroll
+          for (int t = 0; t < 4; ++t) v[t] = static_cast<float>(static_cast<int>((b >> (4 * t)) & 0xFu) - 8) * scale;
         } else {
-          code = static_cast<int>(__ldg(crow + k)) - 128;
+          const uint32_t b = __ldg(reinterpret_cast<const uint32_t*>(crow + k));
+#pragma unroll
+          for (int t = 0; t < 4; ++t) v[t] = static_cast<float>(static_cast<int>((b >> (8 * t)) & 0xFFu) - 128) * scale;
         }
-        v = static_cast<float>(code) * scale;
       }
-      if (k >= own.begin && k < own.end) c.s->resid[k - own.begin] = v;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        if (k + t >= own.begin && k + t < own.end) c.s->resid[k + t - own.begin] = v[t];
+      }
     }
-    raw[i] = v;
+    raw[i] = make_float4(v[0], v[1], v[2], v[3]);
   }
   normalize_into_x(c, raw, hidden, q4);
 }
@@ -533,9 +571,7 @@ struct Best {
 // l * 16 + 512 * j of a row, and the matching activations from x.
 template <uint32_t FMT>
 __device__ void gemv_tiles(Ctx& c, const Piece* pieces, int np, bool lm, Best& best, float* logits_out) {
-#pragma unroll
-  for (int p = 0; p < 3; ++p) {
-    if (p >= np) break;
+  for (int p = 0; p < np; ++p) {
     const Piece pc = pieces[p];
     const uint32_t per = rows_per_tile(pc);
     const uint32_t chunks = pc.code_row / 512u;
@@ -550,6 +586,7 @@ __device__ void gemv_tiles(Ctx& c, const Piece* pieces, int np, bool lm, Best& b
         // together (warp_sum4). Rows past the tile are skipped (warp-uniform).
         for (uint32_t i0 = c.warp; i0 < nr; i0 += kRowsPerPass * kConsumerWarps) {
           float acc[kRowsPerPass] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 1
           for (uint32_t j = 0; j < chunks; ++j) {
             const uint32_t off = 16u * c.lane + 512u * j;
             const uint32_t kbase = off * Fmt<FMT>::kKPerByte;
@@ -598,13 +635,11 @@ __device__ void gemv_tiles(Ctx& c, const Piece* pieces, int np, bool lm, Best& b
 }
 
 // Runs one GEMV stage over the CTA's pieces.
-__device__ void gemv_stage(Ctx& c, int stage, uint32_t layer, Best& best, float* logits_out) {
-  Piece pieces[3];
-  const int np = stage_pieces(*c.m, layer, stage, blockIdx.x, gridDim.x, pieces);
-  if (stage_format(*c.m, layer, stage) == kFormatQ4) {
-    gemv_tiles<kFormatQ4>(c, pieces, np, stage == kStLM, best, logits_out);
+__device__ void gemv_stage(Ctx& c, const Piece* pieces, int np, bool q4, bool lm, Best& best, float* logits_out) {
+  if (q4) {
+    gemv_tiles<kFormatQ4>(c, pieces, np, lm, best, logits_out);
   } else {
-    gemv_tiles<kFormatQ8>(c, pieces, np, stage == kStLM, best, logits_out);
+    gemv_tiles<kFormatQ8>(c, pieces, np, lm, best, logits_out);
   }
   consumer_sync(kConsumerThreads);
 }
@@ -892,6 +927,7 @@ __device__ void run_consumers(const DecodeLaunch& P, Smem* s) {
   Ctx c{&P, &m, s, 0, 0, true, static_cast<int>(threadIdx.x / 32), static_cast<int>(threadIdx.x % 32),
         static_cast<int>(threadIdx.x), false, 0, 0, 0, 0};
   const Span own = split_rows(m.hidden, blockIdx.x, gridDim.x);  // hidden rows of O and down
+  const Span fr = split_rows(m.ffn, blockIdx.x, gridDim.x);      // ffn rows of gate and up
   const uint32_t qw = m.q_heads * kHeadDim;
   uint32_t input = P.first_input;
 
@@ -903,119 +939,97 @@ __device__ void run_consumers(const DecodeLaunch& P, Smem* s) {
       row = P.forced_row ? P.forced_row[t] : -1;
     }
     c.tracing = P.trace != nullptr && t == P.trace_token;
-    for (uint32_t l = 0; l < m.n_layers && c.ok; ++l) {
-      Best best{-INFINITY, 0};
-      const uint32_t e0 = l * kTraceEventsPerLayer;
-      trace_mark(c, e0 + 0);
-      // -- QKV: x = rmsnorm(hidden) (decoder.zig:165-176)
-      const bool qkv_q4 = stage_format(m, l, kStQKV) == kFormatQ4;
-      if (l == 0) {
-        input_into_x(c, input, row, own, qkv_q4);
+    const bool logits = t >= P.logits_from;
+    const uint32_t walk = m.n_layers * kStagesPerLayer + (logits ? 1u : 0u);
+    for (uint32_t q = 0; q < walk; ++q) {
+      const uint32_t l = q / kStagesPerLayer;
+      const int st = l < m.n_layers ? layer_stage(q % kStagesPerLayer) : kStLM;
+      const uint32_t e0 = q * kTraceEventsPerStage;
+      if (st == kStAttn) {
+        // -- attention over position + 1 cached rows (decoder.zig:216-253)
+        trace_mark(c, e0);
+        attention_stage(c, l, position);
       } else {
-        norm_global_into_x(c, P.hidden_g, m.hidden, qkv_q4);
-      }
-      trace_mark(c, e0 + 1);
-      gemv_stage(c, kStQKV, l, best, nullptr);
-      {
+        const uint32_t lq = st == kStLM ? 0 : l;
+        const bool q4 = stage_format(m, lq, st) == kFormatQ4;
+        // -- stage input into x: the layer-0 input row, an RMSNorm of the
+        // residual stream (decoder.zig:165-176, 259-262, 277-283), or the
+        // attention output / SwiGLU activations; up reuses gate's input.
+        if (st == kStQKV && l == 0) {
+          input_into_x(c, input, row, own, q4);
+        } else if (st == kStQKV || st == kStGate || st == kStLM) {
+          norm_global_into_x(c, P.hidden_g, m.hidden, q4);
+        } else if (st == kStO || st == kStDown) {
+          load_x_global(c, st == kStO ? P.attn_out : P.act, st == kStO ? qw : m.ffn, q4);
+        }
+        trace_mark(c, e0);
         Piece pieces[3];
-        const int np = stage_pieces(m, l, kStQKV, blockIdx.x, gridDim.x, pieces);
-        for (int p = 0; p < np; ++p) {
-          for (uint32_t i = c.tid; i < pieces[p].rows; i += kConsumerThreads) {
-            P.qkv[pieces[p].out0 + i] = s->part[pieces[p].local0 + i];
+        const int np = stage_pieces(m, lq, st, blockIdx.x, gridDim.x, pieces);
+        Best best{-INFINITY, 0xFFFFFFFFu};
+        float* logits_out = (st == kStLM && P.logits_out && t + 1 == P.n_tokens) ? P.logits_out : nullptr;
+        gemv_stage(c, pieces, np, q4, st == kStLM, best, logits_out);
+        // -- stage output
+        if (st == kStQKV) {
+          for (int p = 0; p < np; ++p) {
+            for (uint32_t i = c.tid; i < pieces[p].rows; i += kConsumerThreads) {
+              P.qkv[pieces[p].out0 + i] = s->part[pieces[p].local0 + i];
+            }
+          }
+        } else if (st == kStO || st == kStDown) {
+          // Residual adds (decoder.zig:256-257, 270-271) on this CTA's rows.
+          for (uint32_t r = own.begin + c.tid; r < own.end; r += kConsumerThreads) {
+            const float h = s->resid[r - own.begin] + s->part[r - own.begin];
+            s->resid[r - own.begin] = h;
+            P.hidden_g[r] = h;
+          }
+        } else if (st == kStGate) {
+          for (uint32_t i = c.tid; i < fr.end - fr.begin; i += kConsumerThreads) s->gate[i] = s->part[i];
+          consumer_sync(kConsumerThreads);
+        } else if (st == kStUp) {
+          // SwiGLU (kernels.zig:233-239).
+          for (uint32_t i = c.tid; i < fr.end - fr.begin; i += kConsumerThreads) {
+            const float g = s->gate[i];
+            const float silu = g / (1.0f + expf(-g));
+            P.act[fr.begin + i] = silu * s->part[i];
+          }
+        } else {
+          // lm_head: this CTA's first maximum (decoder.zig:290-301).
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best.v, o);
+            const uint32_t oi = __shfl_xor_sync(0xffffffffu, best.i, o);
+            if (ov > best.v || (ov == best.v && oi < best.i)) best = Best{ov, oi};
+          }
+          if (c.lane == 0) {
+            s->amax_v[c.warp] = best.v;
+            s->amax_i[c.warp] = best.i;
+          }
+          consumer_sync(kConsumerThreads);
+          if (c.tid == 0) {
+            Best b{s->amax_v[0], s->amax_i[0]};
+            for (int w = 1; w < kConsumerWarps; ++w) {
+              const Best o{s->amax_v[w], s->amax_i[w]};
+              if (o.v > b.v || (o.v == b.v && o.i < b.i)) b = o;
+            }
+            P.amax_val[blockIdx.x] = b.v;
+            P.amax_idx[blockIdx.x] = b.i;
           }
         }
       }
+      trace_mark(c, e0 + 1);
+      if (st != kStGate) {
+        grid_barrier(c);
+        if (!c.ok) break;
+      }
       trace_mark(c, e0 + 2);
-      grid_barrier(c);
-      if (!c.ok) break;
-      trace_mark(c, e0 + 3);
-      // -- attention over position + 1 cached rows (decoder.zig:216-253)
-      attention_stage(c, l, position);
-      trace_mark(c, e0 + 4);
-      grid_barrier(c);
-      if (!c.ok) break;
-      trace_mark(c, e0 + 5);
-      // -- O projection + residual (decoder.zig:256-257)
-      load_x_global(c, P.attn_out, qw, stage_format(m, l, kStO) == kFormatQ4);
-      gemv_stage(c, kStO, l, best, nullptr);
-      for (uint32_t r = own.begin + c.tid; r < own.end; r += kConsumerThreads) {
-        const float h = s->resid[r - own.begin] + s->part[r - own.begin];
-        s->resid[r - own.begin] = h;
-        P.hidden_g[r] = h;
-      }
-      trace_mark(c, e0 + 6);
-      grid_barrier(c);
-      if (!c.ok) break;
-      trace_mark(c, e0 + 7);
-      // -- RMSNorm -> gate/up -> SwiGLU (decoder.zig:259-269)
-      norm_global_into_x(c, P.hidden_g, m.hidden, stage_format(m, l, kStGate) == kFormatQ4);
-      trace_mark(c, e0 + 8);
-      const Span fr = split_rows(m.ffn, blockIdx.x, gridDim.x);
-      gemv_stage(c, kStGate, l, best, nullptr);
-      for (uint32_t i = c.tid; i < fr.end - fr.begin; i += kConsumerThreads) s->gate[i] = s->part[i];
-      consumer_sync(kConsumerThreads);
-      trace_mark(c, e0 + 9);
-      gemv_stage(c, kStUp, l, best, nullptr);
-      for (uint32_t i = c.tid; i < fr.end - fr.begin; i += kConsumerThreads) {
-        const float g = s->gate[i];
-        const float silu = g / (1.0f + expf(-g));
-        P.act[fr.begin + i] = silu * s->part[i];
-      }
-      trace_mark(c, e0 + 10);
-      grid_barrier(c);
-      if (!c.ok) break;
-      // -- down + residual (decoder.zig:270-271)
-      load_x_global(c, P.act, m.ffn, stage_format(m, l, kStDown) == kFormatQ4);
-      trace_mark(c, e0 + 11);
-      gemv_stage(c, kStDown, l, best, nullptr);
-      for (uint32_t r = own.begin + c.tid; r < own.end; r += kConsumerThreads) {
-        const float h = s->resid[r - own.begin] + s->part[r - own.begin];
-        s->resid[r - own.begin] = h;
-        P.hidden_g[r] = h;
-      }
-      trace_mark(c, e0 + 12);
-      grid_barrier(c);
-      if (!c.ok) break;
-      trace_mark(c, e0 + 13);
     }
     if (!c.ok) break;
-    if (t >= P.logits_from) {
-      // -- final RMSNorm -> lm_head -> argmax (decoder.zig:277-301)
-      norm_global_into_x(c, P.hidden_g, m.hidden, m.lm_head.format == kFormatQ4);
-      Best best{-INFINITY, 0xFFFFFFFFu};
-      float* logits = (P.logits_out && t + 1 == P.n_tokens) ? P.logits_out : nullptr;
-      const uint32_t el = m.n_layers * kTraceEventsPerLayer;
-      trace_mark(c, el + 0);
-      gemv_stage(c, kStLM, 0, best, logits);
-      trace_mark(c, el + 1);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best.v, o);
-        const uint32_t oi = __shfl_xor_sync(0xffffffffu, best.i, o);
-        if (ov > best.v || (ov == best.v && oi < best.i)) best = Best{ov, oi};
-      }
-      if (c.lane == 0) {
-        s->amax_v[c.warp] = best.v;
-        s->amax_i[c.warp] = best.i;
-      }
-      consumer_sync(kConsumerThreads);
-      if (c.tid == 0) {
-        Best b{s->amax_v[0], s->amax_i[0]};
-        for (int w = 1; w < kConsumerWarps; ++w) {
-          const Best o{s->amax_v[w], s->amax_i[w]};
-          if (o.v > b.v || (o.v == b.v && o.i < b.i)) b = o;
-        }
-        P.amax_val[blockIdx.x] = b.v;
-        P.amax_idx[blockIdx.x] = b.i;
-      }
-      grid_barrier(c);
-      if (!c.ok) break;
-      trace_mark(c, el + 2);
-      if (c.tracing && c.tid == 0) {
-        P.trace[blockIdx.x * kTraceEvents + kTraceEvents - 3] = c.tile_ns;
-        P.trace[blockIdx.x * kTraceEvents + kTraceEvents - 2] = c.full_wait_ns;
-        P.trace[blockIdx.x * kTraceEvents + kTraceEvents - 1] = c.bar_wait_ns;
-      }
+    if (c.tracing && c.tid == 0) {
+      P.trace[blockIdx.x * kTraceEvents + kTraceEvents - 3] = c.tile_ns;
+      P.trace[blockIdx.x * kTraceEvents + kTraceEvents - 2] = c.full_wait_ns;
+      P.trace[blockIdx.x * kTraceEvents + kTraceEvents - 1] = c.bar_wait_ns;
+    }
+    if (logits) {
       // Every CTA combines the per-CTA maxima (one L2 round trip, then a
       // block reduction). CTA row ranges ascend, so lowest-index-on-tie over
       // (value, index) pairs is the reference's first-maximum rule.

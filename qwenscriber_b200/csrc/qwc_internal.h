@@ -120,7 +120,7 @@ struct alignas(64) KvMaps {
 };
 
 constexpr uint32_t kTraceEvents = 512;
-constexpr uint32_t kTraceEventsPerLayer = 14;
+constexpr uint32_t kTraceEventsPerStage = 3;  // input ready, output done, barrier passed
 
 }  // namespace qwc
 
