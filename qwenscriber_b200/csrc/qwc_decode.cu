@@ -38,8 +38,8 @@ constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kThreads = kConsumerThreads + 32;
 constexpr int kRowsPerPass = 4;                // rows one warp works on at a time
-constexpr int kSlots = 6;
-constexpr uint32_t kSlotBytes = 28 * 1024;
+constexpr int kSlots = 5;
+constexpr uint32_t kSlotBytes = 34 * 1024;            // 32 rows of a q4 matrix with K = 2048
 constexpr uint32_t kXMax = 8192;               // floats in the activation buffer (max K)
 constexpr uint32_t kRowsMax = 256;             // rows of one stage per CTA (non-LM stages)
 constexpr uint32_t kResidMax = 256;            // hidden rows owned by one CTA
@@ -80,6 +80,7 @@ struct Smem {
   uint64_t empty[kSlots];
   float x[kXMax];                 // activation vector, swizzled (x_index), q4-prescaled when asked
   float part[kRowsMax];           // per-row dot products of the current stage
+  float chunk_part[kSlotBytes / 512];  // per (row, 512-byte chunk) dot products of the current tile
   float gate[kRowsMax];           // gate outputs waiting for the up rows
   float resid[kResidMax];         // this CTA's rows of the residual stream
   float red[kConsumerWarps * 2];  // block reductions
@@ -566,9 +567,13 @@ struct Best {
 };
 
 // Consumes the stage's tiles. Non-LM stages leave per-row dot products in
-// s->part[local]; the LM stage keeps a running argmax per lane and optionally
-// stores the logits. Lane l of a warp always takes the 16-byte code chunks at
-// l * 16 + 512 * j of a row, and the matching activations from x.
+// s->part[local]; the LM stage keeps a running argmax per thread and
+// optionally stores the logits. A warp pass covers four rows of one 512-byte
+// chunk of codes: lane l takes the 16 bytes at l * 16 of the chunk, the
+// matching activations from x are loaded once for the four rows, and the
+// four dot products reduce together (warp_sum4). Rows past the tile repeat
+// the last row so the pass has no branches; their sums are dropped. The
+// chunk sums of a row are added in chunk order after the tile.
 template <uint32_t FMT>
 __device__ void gemv_tiles(Ctx& c, const Piece* pieces, int np, bool lm, Best& best, float* logits_out) {
   for (int p = 0; p < np; ++p) {
@@ -577,59 +582,56 @@ __device__ void gemv_tiles(Ctx& c, const Piece* pieces, int np, bool lm, Best& b
     const uint32_t chunks = pc.code_row / 512u;
     for (uint32_t r = 0; r < pc.rows; r += per) {
       const uint32_t nr = min(per, pc.rows - r);
+      const uint32_t passes = (nr + kRowsPerPass - 1) / kRowsPerPass * chunks;
       const uint8_t* base = acquire_tile(c);
       if (c.ok) {
         const uint8_t* codes = base + nr * pc.scale_row;
         const uint32_t magic = magic_reg();
-        // Up to four rows per pass (rows i0, i0 + 8, ...): independent
-        // dot-product chains that share each activation load, reduced
-        // together (warp_sum4). Rows past the tile are skipped (warp-uniform).
-        for (uint32_t i0 = c.warp; i0 < nr; i0 += kRowsPerPass * kConsumerWarps) {
-          float acc[kRowsPerPass] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll 1
-          for (uint32_t j = 0; j < chunks; ++j) {
-            const uint32_t off = 16u * c.lane + 512u * j;
-            const uint32_t kbase = off * Fmt<FMT>::kKPerByte;
-            uint64_t x2[Fmt<FMT>::kPairs];
+        for (uint32_t ps = c.warp; ps < passes; ps += kConsumerWarps) {
+          const uint32_t r0 = (ps / chunks) * kRowsPerPass, j = ps % chunks;
+          const uint32_t off = 16u * c.lane + 512u * j;
+          const uint32_t kbase = off * Fmt<FMT>::kKPerByte;
+          uint64_t x2[Fmt<FMT>::kPairs];
 #pragma unroll
-            for (int q = 0; q < Fmt<FMT>::kPairs / 2; ++q) {
-              const float4 v = *reinterpret_cast<const float4*>(&c.s->x[x_index(kbase + 4 * q)]);
-              x2[2 * q] = pack2(v.x, v.y);
-              x2[2 * q + 1] = pack2(v.z, v.w);
-            }
+          for (int q = 0; q < Fmt<FMT>::kPairs / 2; ++q) {
+            const float4 v = *reinterpret_cast<const float4*>(&c.s->x[x_index(kbase + 4 * q)]);
+            x2[2 * q] = pack2(v.x, v.y);
+            x2[2 * q + 1] = pack2(v.z, v.w);
+          }
+          float acc[kRowsPerPass];
 #pragma unroll
-            for (int q = 0; q < kRowsPerPass; ++q) {
-              const uint32_t row = i0 + q * kConsumerWarps;
-              if (row < nr) {
-                const uint4 w = *reinterpret_cast<const uint4*>(codes + row * pc.code_row + off);
-                const float scale = f16_bits_to_f32_fast(
-                    *reinterpret_cast<const uint16_t*>(base + row * pc.scale_row + (off / Fmt<FMT>::kDB) * 2));
-                float d;
-                if constexpr (FMT == kFormatQ4) {
-                  d = q4_chunk_dot(w, x2, magic);
-                } else {
-                  d = q8_chunk_dot(w, x2);
-                }
-                acc[q] = fmaf(d, scale, acc[q]);
-              }
+          for (int q = 0; q < kRowsPerPass; ++q) {
+            const uint32_t row = min(r0 + q, nr - 1);
+            const uint4 w = *reinterpret_cast<const uint4*>(codes + row * pc.code_row + off);
+            const float scale = f16_bits_to_f32_fast(
+                *reinterpret_cast<const uint16_t*>(base + row * pc.scale_row + (off / Fmt<FMT>::kDB) * 2));
+            float d;
+            if constexpr (FMT == kFormatQ4) {
+              d = q4_chunk_dot(w, x2, magic);
+            } else {
+              d = q8_chunk_dot(w, x2);
             }
+            acc[q] = d * scale;
           }
           const float total = warp_sum4(acc[0], acc[1], acc[2], acc[3]);
-          const uint32_t q = static_cast<uint32_t>(c.lane) >> 3;
-          const uint32_t i = i0 + q * kConsumerWarps;
-          if ((c.lane & 7) == 0 && i < nr) {
-            const uint32_t local = pc.local0 + r + i;
-            if (!lm) {
-              c.s->part[local] = total;
-            } else {
-              const uint32_t row = pc.out0 + r + i;
-              if (logits_out) logits_out[row] = total;
-              if (total > best.v || (total == best.v && row < best.i)) best = Best{total, row};
-            }
-          }
+          const uint32_t row = r0 + (static_cast<uint32_t>(c.lane) >> 3);
+          if ((c.lane & 7) == 0 && row < nr) c.s->chunk_part[row * chunks + j] = total;
         }
       }
       release_tile(c);
+      consumer_sync(kConsumerThreads);
+      for (uint32_t i = c.tid; i < nr; i += kConsumerThreads) {
+        float total = c.s->chunk_part[i * chunks];
+        for (uint32_t j = 1; j < chunks; ++j) total += c.s->chunk_part[i * chunks + j];
+        if (!lm) {
+          c.s->part[pc.local0 + r + i] = total;
+        } else {
+          const uint32_t row = pc.out0 + r + i;
+          if (logits_out) logits_out[row] = total;
+          if (total > best.v || (total == best.v && row < best.i)) best = Best{total, row};
+        }
+      }
+      consumer_sync(kConsumerThreads);  // chunk_part is reused by the next tile
     }
   }
 }
