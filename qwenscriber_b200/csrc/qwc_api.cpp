@@ -532,7 +532,7 @@ int32_t finish_model(Handle* h, const Config& c) {
   QWC_CUDA(cudaMemset(h->attn_count.ptr, 0, h->attn_count.bytes));
   QWC_TRY(h->amax_val.alloc(size_t(h->grid) * 4));
   QWC_TRY(h->amax_idx.alloc(size_t(h->grid) * 4));
-  QWC_TRY(h->barrier.alloc(256));
+  QWC_TRY(h->barrier.alloc(kBarrierBytes));
   QWC_TRY(h->error.alloc(256));
   QWC_CUDA(cudaMemset(h->error.ptr, 0, h->error.bytes));
   QWC_TRY(h->tokens_out.alloc(size_t(std::max<uint32_t>(c.max_positions, 256)) * 4));
@@ -590,7 +590,7 @@ int32_t run_decode(Handle* h, uint32_t n_tokens, uint32_t first_position, uint32
   }
   L.max_chunks = h->max_chunks;
   (void)m;
-  QWC_CUDA(cudaMemsetAsync(h->barrier.ptr, 0, 4, h->stream));
+  QWC_CUDA(cudaMemsetAsync(h->barrier.ptr, 0, kBarrierBytes, h->stream));
   const int e = launch_decode(L, h->kv_maps, h->grid, h->stream);
   if (e != 0) {
     if (std::getenv("QWC_VERBOSE")) std::fprintf(stderr, "qwc: decode launch failed: %s\n", cudaGetErrorString(static_cast<cudaError_t>(e)));

@@ -399,19 +399,27 @@ __device__ void grid_barrier(Ctx& c) {
     red_release_add(c.P->barrier, 1);
     uint64_t deadline = 0;  // set on the first check, so a barrier that opens quickly never reads the clock
     uint32_t spins = 0;
+    bool failed = false;
+    // The error word is read only while waiting: a barrier that opens costs
+    // no extra L2 round trip. An error raised by a CTA that still arrives is
+    // seen by the host after the launch, and by the next barrier that waits.
     while (ld_acquire(c.P->barrier) < target) {
       if ((++spins & 63u) == 0) {
-        if (error_set(c.P->error)) break;
+        if (error_set(c.P->error)) {
+          failed = true;
+          break;
+        }
         const uint64_t now = global_timer_ns();
         if (deadline == 0) {
           deadline = now + c.P->timeout_ns;
         } else if (now > deadline) {
           atomicCAS(c.P->error, 0, kErrBarrier);
+          failed = true;
           break;
         }
       }
     }
-    c.s->flag = error_set(c.P->error) ? 1u : 0u;
+    c.s->flag = failed ? 1u : 0u;
     if (c.tracing) c.bar_wait_ns += global_timer_ns() - arrive;
   }
   consumer_sync(kConsumerThreads);
@@ -872,25 +880,26 @@ __device__ void attention_stage(Ctx& c, uint32_t layer, uint32_t position) {
         dst[kHeadDim + 1] = l;
       }
     }
-    __threadfence();
+    // The counter update is acquire-release at gpu scope: its release (after
+    // the bar.sync) publishes this CTA's partial, and the last arriver's
+    // acquire makes every other CTA's partial visible to the loads below.
     consumer_sync(kConsumerThreads);
     if (tid == 0) {
-      const uint32_t prev = atomicAdd(c.P->attn_count + h, 1u);
+      const uint32_t prev = atom_add_acq_rel(c.P->attn_count + h, 1u);
       c.s->flag = (prev == chunks - 1) ? 1u : 0u;
     }
     consumer_sync(kConsumerThreads);
     if (c.s->flag) {
-      __threadfence();
-      // Chunks are combined eight at a time with all loads of a batch issued
-      // together (online rescale).
+      // Chunks are combined sixteen at a time with all loads of a batch
+      // issued together (online rescale).
       float mx = -INFINITY;
       o = 0.0f;
       l = 0.0f;
       const float* base = c.P->attn_part + size_t(2 * h + j) * c.P->max_chunks * (kHeadDim + 2);
-      for (uint32_t q0 = 0; q0 < chunks; q0 += 8) {
-        float pm[8], po[8], pl[8];
+      for (uint32_t q0 = 0; q0 < chunks; q0 += 16) {
+        float pm[16], po[16], pl[16];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
+        for (int q = 0; q < 16; ++q) {
           pm[q] = -INFINITY;
           po[q] = 0.0f;
           pl[q] = 0.0f;
@@ -903,12 +912,12 @@ __device__ void attention_stage(Ctx& c, uint32_t layer, uint32_t position) {
         }
         float bm = mx;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) bm = fmaxf(bm, pm[q]);
+        for (int q = 0; q < 16; ++q) bm = fmaxf(bm, pm[q]);
         const float rescale = (mx == -INFINITY) ? 0.0f : expf(mx - bm);
         o *= rescale;
         l *= rescale;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
+        for (int q = 0; q < 16; ++q) {
           const float f = (pm[q] == -INFINITY) ? 0.0f : expf(pm[q] - bm);
           o = fmaf(po[q], f, o);
           l = fmaf(pl[q], f, l);

@@ -119,6 +119,7 @@ struct alignas(64) KvMaps {
   uint8_t v_scales[128];
 };
 
+constexpr uint32_t kBarrierBytes = 1024;   // grid-barrier counters of the decode kernel, zeroed per launch
 constexpr uint32_t kTraceEvents = 512;
 constexpr uint32_t kTraceEventsPerStage = 3;  // input ready, output done, barrier passed
 
