@@ -227,6 +227,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes or about `hint_ns` pass, instead of spinning on the issue slots
+// its warp shares with the scheduler's other warps.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return done != 0;
+}
+
 // Bulk copy global -> shared, completing on `bar` (cp.async.bulk, non-multicast).
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
@@ -261,14 +274,13 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     if (mbar_try_wait(bar, parity)) return true;
   }
   const uint64_t deadline = global_timer_ns() + timeout_ns;
-  uint32_t spins = 0;
-  while (!mbar_try_wait(bar, parity)) {
-    if ((++spins & 255u) == 0) {
-      if (*reinterpret_cast<volatile int32_t*>(error) != 0) return false;
-      if (global_timer_ns() > deadline) {
-        atomicCAS(error, 0, code);
-        return false;
-      }
+  // Each try sleeps up to 20 us unless the phase completes first, so the
+  // error word and the clock are checked on every pass of the loop.
+  while (!mbar_try_wait_sleep(bar, parity, 20000u)) {
+    if (*reinterpret_cast<volatile int32_t*>(error) != 0) return false;
+    if (global_timer_ns() > deadline) {
+      atomicCAS(error, 0, code);
+      return false;
     }
   }
   return true;
