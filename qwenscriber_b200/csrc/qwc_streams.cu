@@ -546,7 +546,8 @@ __global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kern
     wm[0] = mn0;
     wm[1] = mn1;
     // Values (q8GroupAccumulate, kernels.zig:665-688).
-    float acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+    // Packed pairs: (dims 4l, 4l+1) and (4l+2, 4l+3) of each head.
+    uint64_t acc01[2] = {0, 0}, acc23[2] = {0, 0};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const uint32_t row = static_cast<uint32_t>(warp) * 8 + i;
@@ -555,19 +556,25 @@ __global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kern
       const float scale = f16_bits_to_f32_fast(bits);
       const float q0 = __shfl_sync(0xffffffffu, p0, 4 * i), q1 = __shfl_sync(0xffffffffu, p1, 4 * i);
       const float sw0 = scale * q0, sw1 = scale * q1;
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const float cv = bits_f32(__byte_perm(word, kMagic, 0x7440 + t)) + kNegQ8;
-        acc[0][t] = fmaf(cv, sw0, acc[0][t]);
-        acc[1][t] = fmaf(cv, sw1, acc[1][t]);
-      }
+      const uint64_t c01 = add2(pack2(bits_f32(__byte_perm(word, kMagic, 0x7440)),
+                                      bits_f32(__byte_perm(word, kMagic, 0x7441))), bias);  // code - 128, exact
+      const uint64_t c23 = add2(pack2(bits_f32(__byte_perm(word, kMagic, 0x7442)),
+                                      bits_f32(__byte_perm(word, kMagic, 0x7443))), bias);
+      acc01[0] = fma2(c01, pack2(sw0, sw0), acc01[0]);
+      acc23[0] = fma2(c23, pack2(sw0, sw0), acc23[0]);
+      acc01[1] = fma2(c01, pack2(sw1, sw1), acc01[1]);
+      acc23[1] = fma2(c23, pack2(sw1, sw1), acc23[1]);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&a->empty[slot]);  // this warp is done with the tile
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      wo[0][t] = fmaf(wo[0][t], r0, acc[0][t]);
-      wo[1][t] = fmaf(wo[1][t], r1, acc[1][t]);
+    for (int hh = 0; hh < 2; ++hh) {
+      const float2 v01 = unpack2(acc01[hh]), v23 = unpack2(acc23[hh]);
+      const float rr = hh == 0 ? r0 : r1;
+      wo[hh][0] = fmaf(wo[hh][0], rr, v01.x);
+      wo[hh][1] = fmaf(wo[hh][1], rr, v01.y);
+      wo[hh][2] = fmaf(wo[hh][2], rr, v23.x);
+      wo[hh][3] = fmaf(wo[hh][3], rr, v23.y);
     }
     ++seg_count;
   }
