@@ -274,6 +274,8 @@ struct __align__(128) AttnSmem {
   alignas(16) float red[2][8];              // per-warp running maxima
   alignas(16) float lsum[2][8];             // per-warp running sums
   uint32_t prefix[kMaxStreams + 1];
+  uint32_t pos[kMaxStreams];    // each column's newest position
+  uint32_t cache[kMaxStreams];  // each column's cache slot
   uint32_t flag;
   alignas(8) uint64_t full[kAttnSlots];
   alignas(8) uint64_t empty[kAttnSlots];
@@ -300,9 +302,9 @@ __device__ __forceinline__ UnitPos unit_pos(const AttnSmem* a, const StreamsStep
     const uint32_t mid = (lo + hi) / 2;
     if (a->prefix[mid] <= u) lo = mid; else hi = mid;
   }
-  const uint32_t chunks = P.desc[lo].position / kAttnChunk + 1;
+  const uint32_t chunks = a->pos[lo] / kAttnChunk + 1;
   const uint32_t r = u - a->prefix[lo];
-  return UnitPos{lo, r / chunks, r % chunks, chunks, static_cast<uint32_t>(P.desc[lo].cache)};
+  return UnitPos{lo, r / chunks, r % chunks, chunks, a->cache[lo]};
 }
 
 __global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kernel(const StreamsStep P,
@@ -324,6 +326,8 @@ __global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kern
     for (uint32_t s = 0; s < kMaxStreams; ++s) {
       a->prefix[s] = acc;
       const SlotStep d = P.desc[s];
+      a->pos[s] = static_cast<uint32_t>(d.position);
+      a->cache[s] = static_cast<uint32_t>(d.cache);
       if (d.active) acc += kv_heads * (d.position / kAttnChunk + 1);
     }
     a->prefix[kMaxStreams] = acc;
@@ -422,36 +426,56 @@ __global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kern
     }
     float* part = P.attn_part + ((size_t(cur.s) * m.q_heads + 2 * cur.h + j) * P.max_chunks + seg_first) * (kHeadDim + 2);
     part[dd] = o_run;
-    if (dd == 0) part[kHeadDim + 1] = l_run;
-    __threadfence();
-    consumer_sync(kAttnConsumers);
     if (dd == 0) {
-      // The max goes last: a non-NaN max marks the partial as written.
-      reinterpret_cast<volatile float*>(part)[kHeadDim] = m_run;
+      part[kHeadDim] = m_run;  // a non-NaN max marks the chunk as a segment start
+      part[kHeadDim + 1] = l_run;
     }
-    __threadfence();
+    // The counter update is acquire-release at gpu scope: its release (after
+    // the bar.sync) publishes this CTA's partial, and the last arriver's
+    // acquire makes every other CTA's partial visible to its loads.
     consumer_sync(kAttnConsumers);
     uint32_t* counter = P.attn_count + size_t(cur.s) * kv_heads + cur.h;
     if (tid == 0) {
-      const uint32_t prev = atomicAdd(counter, seg_count);
+      const uint32_t prev = atom_add_acq_rel(counter, seg_count);
       a->flag = (prev + seg_count == cur.chunks) ? 1u : 0u;
     }
     consumer_sync(kAttnConsumers);
     if (a->flag) {
-      __threadfence();
+      // Segment starts are read sixteen chunks at a time with every load of a
+      // batch in flight together; NaN maxima mark chunks no segment starts at.
       float mx = -INFINITY, o = 0.0f, l = 0.0f;
-      float* base = P.attn_part + (size_t(cur.s) * m.q_heads + 2 * cur.h + j) * P.max_chunks * (kHeadDim + 2);
-      for (uint32_t c = 0; c < cur.chunks; ++c) {
-        float* src = base + size_t(c) * (kHeadDim + 2);
-        const float pm = ld_cg(src + kHeadDim);
-        if (pm != pm) continue;  // NaN: no segment starts at this chunk
-        const float po = ld_cg(src + dd), pl = ld_cg(src + kHeadDim + 1);
-        const float nm = fmaxf(mx, pm);
-        const float f_old = (mx == -INFINITY) ? 0.0f : expf(mx - nm);
-        const float f_new = expf(pm - nm);
-        o = o * f_old + po * f_new;
-        l = l * f_old + pl * f_new;
-        mx = nm;
+      const float* base = P.attn_part + (size_t(cur.s) * m.q_heads + 2 * cur.h + j) * P.max_chunks * (kHeadDim + 2);
+      for (uint32_t c0 = 0; c0 < cur.chunks; c0 += 16) {
+        float pm[16], po[16], pl[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          pm[q] = -INFINITY;
+          po[q] = 0.0f;
+          pl[q] = 0.0f;
+          if (c0 + q < cur.chunks) {
+            const float* src = base + size_t(c0 + q) * (kHeadDim + 2);
+            pm[q] = ld_cg(src + kHeadDim);
+            po[q] = ld_cg(src + dd);
+            pl[q] = ld_cg(src + kHeadDim + 1);
+          }
+        }
+        float bm = mx;
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          if (pm[q] == pm[q]) bm = fmaxf(bm, pm[q]);
+        }
+        const float rescale = (mx == -INFINITY) ? 0.0f : expf(mx - bm);
+        o *= rescale;
+        l *= rescale;
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          if (pm[q] == pm[q] && pm[q] != -INFINITY) {
+            const float f = expf(pm[q] - bm);
+            o = fmaf(po[q], f, o);
+            l = fmaf(pl[q], f, l);
+          }
+        }
+        mx = bm;
       }
       store_one(xq + out_index, xq_lo, o / l);
       consumer_sync(kAttnConsumers);
@@ -487,7 +511,7 @@ __global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kern
       ok = false;
     }
     const uint8_t* tile = a->ring[slot];
-    const uint32_t newest = P.desc[up.s].position;
+    const uint32_t newest = a->pos[up.s];
     const uint32_t base_pos = up.ch * kAttnChunk + static_cast<uint32_t>(warp) * 8;
     const bool valid = ok && base_pos + pi <= newest;
     float s0, s1;
