@@ -286,6 +286,17 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   return true;
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start while the previous kernel of the stream drains.
+// Every thread waits here for the previous kernels to complete (their memory
+// visible) before touching data they produced or still read, then lets the
+// next kernel's CTAs be scheduled. Without the launch attribute both are
+// no-ops.
+__device__ __forceinline__ void pdl_wait_and_trigger() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void red_release_add(uint32_t* p, uint32_t v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -326,6 +337,25 @@ __device__ __forceinline__ uint8_t q8_code(float value, float stored_scale) {
   else if (rounded >= 127.0f) code = 127;
   else code = static_cast<int>(rounded);
   return static_cast<uint8_t>(code + 128);
+}
+
+// Launches `kernel` with programmatic stream serialization (see
+// pdl_wait_and_trigger); inside stream capture this becomes a programmatic
+// edge of the graph.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
 }  // namespace qwc

@@ -305,6 +305,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   const uint32_t tmem = s->tmem_base;
   bool ok = true;
+  pdl_wait_and_trigger();  // the prologue above overlaps the previous kernel's tail
 
   if (warp == 0) {
     // ---- producer ----
@@ -452,6 +453,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // x[s][k] f32 -> the activation box rows: f16 hi values in rows [0, 64),
 // lo remainders in rows [64, 128), chunks in the permuted order.
 __global__ void pack_activations_kernel(const float* x, uint32_t streams, uint32_t cols, __half* out) {
+  pdl_wait_and_trigger();
   const uint32_t chunks = cols / 8;
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < streams * chunks; i += gridDim.x * blockDim.x) {
     const uint32_t sidx = i / chunks, c = i % chunks;
@@ -471,6 +473,7 @@ __global__ void pack_activations_kernel(const float* x, uint32_t streams, uint32
 }
 
 __global__ void sum_splits_kernel(const float* parts, uint32_t splits, uint32_t n, float* out) {
+  pdl_wait_and_trigger();
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     float acc = parts[i];
     for (uint32_t sp = 1; sp < splits; ++sp) acc += parts[size_t(sp) * n + i];
@@ -564,8 +567,8 @@ int launch_gemm_jobs(const uint8_t (*codes_maps)[128], const uint8_t (*scale_map
   p.timeout_ns = 2000000000ull;
   const uint32_t real_splits = (kblocks + p.kb_per_split - 1) / p.kb_per_split;
   const int smem = gemm_smem_bytes();
-  gemm_streams_kernel<<<dim3(tiles, real_splits), kGemmThreads, smem, static_cast<cudaStream_t>(stream)>>>(maps, p);
-  return static_cast<int>(cudaGetLastError());
+  return static_cast<int>(launch_pdl(gemm_streams_kernel, dim3(tiles, real_splits), dim3(kGemmThreads), smem,
+                                     static_cast<cudaStream_t>(stream), maps, p));
 }
 
 int launch_gemm_streams(const uint8_t* map_codes, const uint8_t* map_scales, const uint8_t* map_b, uint32_t rows,

@@ -92,6 +92,7 @@ __device__ __forceinline__ void store_one(__half* dst, size_t lo_offset, float v
 template <int kInput>
 __global__ void __launch_bounds__(kNormThreads) streams_norm_kernel(const StreamsStep P, const float* weight,
                                                                     const float* parts, uint32_t splits) {
+  pdl_wait_and_trigger();
   __shared__ float xs[kHiddenMax];
   __shared__ float red[kNormThreads / 32];
   const DevModel& m = *P.model;
@@ -185,6 +186,7 @@ __global__ void __launch_bounds__(kNormThreads) streams_norm_kernel(const Stream
 // ---- QK-norm, RoPE, q8 append (decoder.zig:177-216) ----
 
 __global__ void __launch_bounds__(256) streams_qkv_kernel(const StreamsStep P, uint32_t layer, uint32_t splits) {
+  pdl_wait_and_trigger();
   __shared__ float red[16];
   __shared__ float tq[2][kHeadDim];
   __shared__ float tk[kHeadDim];
@@ -310,6 +312,7 @@ __device__ __forceinline__ UnitPos unit_pos(const AttnSmem* a, const StreamsStep
 __global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kernel(const StreamsStep P,
                                                                                const __grid_constant__ KvMaps4 maps,
                                                                                uint32_t layer) {
+  pdl_wait_and_trigger();
   extern __shared__ __align__(128) uint8_t attn_smem_raw[];
   AttnSmem* a = reinterpret_cast<AttnSmem*>(attn_smem_raw);
   const DevModel& m = *P.model;
@@ -608,6 +611,7 @@ __global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kern
 // ---- SwiGLU (kernels.zig:233-239) into f16 activations ----
 
 __global__ void streams_swiglu_kernel(const StreamsStep P, uint32_t splits) {
+  pdl_wait_and_trigger();
   const DevModel& m = *P.model;
   const uint32_t ffn = m.ffn, chunks = ffn / 8;
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < kMaxStreams * chunks; i += gridDim.x * blockDim.x) {
@@ -637,6 +641,7 @@ __global__ void streams_swiglu_kernel(const StreamsStep P, uint32_t splits) {
 // ---- argmax per slot (decoder.zig:290-301: strict >, first index wins) ----
 
 __global__ void __launch_bounds__(1024) streams_argmax_kernel(const StreamsStep P) {
+  pdl_wait_and_trigger();
   __shared__ float sv[32];
   __shared__ uint32_t si[32];
   const uint32_t s = blockIdx.x;
@@ -692,6 +697,7 @@ __global__ void __launch_bounds__(1024) streams_argmax_kernel(const StreamsStep 
 // After a step: every active slot's next input is its argmax at the next
 // position; the tokens also go to row `*counter` of `history`.
 __global__ void streams_advance_kernel(const StreamsStep P, uint32_t* history, uint32_t* counter, uint32_t rows) {
+  pdl_wait_and_trigger();
   const uint32_t s = threadIdx.x;
   const uint32_t step = *counter;
   __syncthreads();
@@ -711,8 +717,9 @@ __global__ void streams_advance_kernel(const StreamsStep P, uint32_t* history, u
 }  // namespace
 
 int launch_streams_advance(const StreamsStep& P, uint32_t* history, uint32_t* counter, uint32_t rows, void* stream) {
-  streams_advance_kernel<<<1, kMaxStreams, 0, static_cast<cudaStream_t>(stream)>>>(P, history, counter, rows);
-  return static_cast<int>(cudaGetLastError());
+  return static_cast<int>(
+      launch_pdl(streams_advance_kernel, dim3(1), dim3(kMaxStreams), 0, static_cast<cudaStream_t>(stream), P, history,
+                 counter, rows));
 }
 
 int prepare_stream_kernels() {
@@ -723,33 +730,29 @@ int prepare_stream_kernels() {
 int launch_streams_norm(const StreamsStep& P, int input_mode, const float* weight, const float* parts, uint32_t splits,
                         void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (input_mode) {
-    streams_norm_kernel<1><<<kMaxStreams, kNormThreads, 0, st>>>(P, weight, parts, splits);
-  } else {
-    streams_norm_kernel<0><<<kMaxStreams, kNormThreads, 0, st>>>(P, weight, parts, splits);
-  }
-  return static_cast<int>(cudaGetLastError());
+  return static_cast<int>(launch_pdl(input_mode ? streams_norm_kernel<1> : streams_norm_kernel<0>, dim3(kMaxStreams),
+                                     dim3(kNormThreads), 0, st, P, weight, parts, splits));
 }
 
 int launch_streams_qkv(const StreamsStep& P, uint32_t layer, uint32_t splits, uint32_t kv_heads, void* stream) {
-  streams_qkv_kernel<<<dim3(kv_heads, kMaxStreams), 256, 0, static_cast<cudaStream_t>(stream)>>>(P, layer, splits);
-  return static_cast<int>(cudaGetLastError());
+  return static_cast<int>(launch_pdl(streams_qkv_kernel, dim3(kv_heads, kMaxStreams), dim3(256), 0,
+                                     static_cast<cudaStream_t>(stream), P, layer, splits));
 }
 
 int launch_streams_attention(const StreamsStep& P, const KvMaps4& maps, uint32_t layer, int grid, void* stream) {
   const int smem = static_cast<int>(sizeof(AttnSmem));
-  streams_attention_kernel<<<grid, kAttnConsumers + 32, smem, static_cast<cudaStream_t>(stream)>>>(P, maps, layer);
-  return static_cast<int>(cudaGetLastError());
+  return static_cast<int>(launch_pdl(streams_attention_kernel, dim3(grid), dim3(kAttnConsumers + 32), smem,
+                                     static_cast<cudaStream_t>(stream), P, maps, layer));
 }
 
 int launch_streams_swiglu(const StreamsStep& P, uint32_t splits, void* stream) {
-  streams_swiglu_kernel<<<592, 256, 0, static_cast<cudaStream_t>(stream)>>>(P, splits);
-  return static_cast<int>(cudaGetLastError());
+  return static_cast<int>(
+      launch_pdl(streams_swiglu_kernel, dim3(592), dim3(256), 0, static_cast<cudaStream_t>(stream), P, splits));
 }
 
 int launch_streams_argmax(const StreamsStep& P, void* stream) {
-  streams_argmax_kernel<<<kMaxStreams, 1024, 0, static_cast<cudaStream_t>(stream)>>>(P);
-  return static_cast<int>(cudaGetLastError());
+  return static_cast<int>(
+      launch_pdl(streams_argmax_kernel, dim3(kMaxStreams), dim3(1024), 0, static_cast<cudaStream_t>(stream), P));
 }
 
 }  // namespace qwc
