@@ -42,6 +42,10 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decode tokens/s, 1.7B q4, 1 & 64 streams/GPU at 1/2/4/8 GPU; % of HBM roofline"
 KV_BYTES_PER_POSITION = 28 * 2 * (1024 + 1024 // 64 * 2)  # all layers, K and V, q8 codes + f16 scales
+# DRAM bytes (read + write) per decoded token of decode_kernel at cfg2, from one
+# ncu capture of a 16-token launch (dram__bytes_read.sum 15.058 GB +
+# dram__bytes_write.sum 29.3 MB, divided by 16 tokens).
+DECODE_TRAFFIC_PER_TOKEN = (15.058409e9 + 29.326592e6) / 16
 
 
 def parse_args():
@@ -363,7 +367,9 @@ def run_ours(args, rank, world, local_rank):
             "vs_baseline": None, "dtype": "f32 (q4 codes dequantized exactly in registers)", "data": "synthetic",
             "config": config_block(w, args, world),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_kind": peak_kind, "traffic": None,
+                         "peak_kind": peak_kind,
+                         "traffic": DECODE_TRAFFIC_PER_TOKEN if args.workload == "cfg2_1p7b_q4_b1" else None,
+                         "traffic_unit": "bytes per step, from an ncu capture of decode_kernel at cfg2",
                          "bytes_per_step": bytes_total / args.steps,
                          "kernel": "decode_kernel (persistent, one launch per %d steps)" % args.chunk},
             "e2e": {"value": tokens / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,

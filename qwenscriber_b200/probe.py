@@ -2,6 +2,12 @@
 
     python -m qwenscriber_b200.probe [--workload NAME] [--steps K]
     python -m qwenscriber_b200.probe --gemm ROWS COLS [--steps K]
+    python -m qwenscriber_b200.probe --workload cfg2_1p7b_q4_b1 --trace
+
+--trace (single-stream workloads) runs one more launch with the phase
+timeline on (QWC_OPTION_TRACE) and prints, per stage of a layer, the mean
+time from the previous barrier to the stage's input being ready, the compute
+time, and the grid-barrier wait, over CTAs and the middle layers.
 
 Single-stream workloads prefill with qwc_decode_begin and time K greedy
 steps of the persistent decode kernel (qwc_decode_run_timed); multi-stream
@@ -33,6 +39,7 @@ def main(argv=None) -> int:
     p.add_argument("--chunk", type=int, default=16, help="decode steps per launch (single stream)")
     p.add_argument("--streams", type=int, default=0, help="override the workload's streams per GPU")
     p.add_argument("--gemm", type=int, nargs=2, metavar=("ROWS", "COLS"), help="time the stream GEMM op alone")
+    p.add_argument("--trace", action="store_true", help="print the per-stage timeline of one decode launch")
     a = p.parse_args(argv)
     if a.gemm:
         return gemm(*a.gemm, a.steps)
@@ -62,8 +69,46 @@ def main(argv=None) -> int:
         tokens = a.steps
     print(f"{w.name}: {a.steps} steps, {ms / a.steps:.3f} ms/step, {tokens / (ms / 1000.0):.0f} tokens/s; "
           f"kernels before the timed steps: {before}")
+    if a.trace and w.streams <= 1:
+        gm.set_option(rt.OPTION_TRACE, 1)
+        gm.run_timed(min(a.chunk, 8))
+        print_trace(gm.debug_trace(), w.config.text_layers)
     gm.close()
     return 0
+
+
+STAGES = ("qkv", "attention", "o", "gate", "up", "down")
+
+
+def print_trace(raw, layers: int) -> None:
+    """Per-stage means of the decode kernel's phase timeline (three stamps per
+    stage: input ready, output done, barrier passed), over CTAs and layers
+    1 .. layers - 2, in microseconds; brackets hold the mean over layers of
+    the slowest CTA."""
+    import numpy as np
+
+    tr = raw.reshape(-1, 512).astype(np.int64)
+    ev = (tr - tr[:, 0].min()) / 1000.0
+    per = len(STAGES)
+    print(f"{'stage':10s} {'input':>16s} {'compute':>16s} {'barrier':>16s}")
+    for si, name in enumerate(STAGES):
+        cols = []
+        for k in range(3):
+            means, maxes = [], []
+            for layer in range(1, layers - 1):
+                q = layer * per + si
+                stamps = [ev[:, q * 3 - 1], ev[:, q * 3], ev[:, q * 3 + 1], ev[:, q * 3 + 2]]
+                d = stamps[k + 1] - stamps[k]
+                means.append(d.mean())
+                maxes.append(d.max())
+            cols.append(f"{np.mean(means):6.2f} [{np.mean(maxes):6.2f}]")
+        print(f"{name:10s} " + " ".join(f"{c:>16s}" for c in cols))
+    span = [ev[:, (layer + 1) * per * 3 - 1].max() - ev[:, layer * per * 3 - 1].max() for layer in range(1, layers - 1)]
+    q = layers * per
+    lm = [(ev[:, q * 3 + k] - ev[:, q * 3 + k - 1]).mean() for k in range(3)]
+    print(f"layer {np.mean(span):.2f} us; lm_head input {lm[0]:.2f} compute {lm[1]:.2f} barrier {lm[2]:.2f} us; "
+          f"per token and CTA: tiles in hand {tr[:, 509].mean() / 1000:.1f} us, waiting for tiles "
+          f"{tr[:, 510].mean() / 1000:.1f} us, at grid barriers {tr[:, 511].mean() / 1000:.1f} us")
 
 
 def gemm(rows: int, cols: int, reps: int) -> int:
