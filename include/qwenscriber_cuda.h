@@ -134,12 +134,31 @@ int32_t qwc_set_option(uint32_t handle, uint32_t option, uint32_t value);
 
 /* qw_model_begin: starts a model attempt; legal in every state and also the unload path. */
 int32_t qwc_model_begin(uint32_t handle);
-/* Replaces qw_model_add_shard for one tensor: `payload` holds that tensor's
+/* One tensor without a container (the per-tensor form of qwc_model_add_shard): `payload` holds that tensor's
  * container payload -- for q4/q5/q8 the f16 scale plane, padding to 16 bytes,
  * then the code plane (src/core/quant.zig:144-176); for f32 vectors the
  * values. Copied to device memory before returning. */
 int32_t qwc_model_add_tensor(uint32_t handle, uint32_t kind, uint32_t layer, uint32_t format, uint32_t rows,
                              uint32_t cols, const void* payload, uint64_t len);
+/* qw_model_add_shard (src/wasm/exports.zig:333-340; src/wasm/model.zig:156-178):
+ * validates one `.qw` shard in place -- magic, version, index order and
+ * ranges, every tensor's shape and byte length, and the payload checksum
+ * (src/core/container.zig:98-291) -- and copies its decoder tensors to device
+ * memory, as qwc_model_add_tensor does. `bytes` must be 16-byte aligned and
+ * may be freed after the call. Tensors of other kinds (audio tower,
+ * projector) are validated and not kept. A shard whose payload checksum
+ * matches one already added, or a tensor already added, is invalid_argument; a decoder tensor in a
+ * format the kernels do not run (q5, f16, bf16) is unsupported_model; more
+ * than 64 shards is limit_exceeded. A shard refused by any of these checks
+ * leaves the handle unchanged. */
+int32_t qwc_model_add_shard(uint32_t handle, const void* bytes, uint64_t len);
+/* container.File.parse followed by verifyChecksum on its own: no handle and
+ * no device. Returns QWC_OK (and the tensor count) or the status the shard
+ * would be refused with. */
+int32_t qwc_shard_validate(const void* bytes, uint64_t len, uint32_t* tensor_count);
+/* The payload checksum a shard header stores: the low 32 bits of FNV-1a 64
+ * over `len` bytes (container.zig:283-286); for shard writers. */
+uint32_t qwc_shard_checksum(const void* bytes, uint64_t len);
 /* qw_model_set_cache_format (exports.zig:352-363): ready state only. */
 int32_t qwc_model_set_cache_format(uint32_t handle, uint32_t format);
 /* Number of independent decode streams the next finish allocates (default 1). */

@@ -23,6 +23,7 @@
 
 #include "../../include/qwenscriber_cuda.h"
 #include "qwc_internal.h"
+#include "qwc_shard.h"
 
 namespace qwc {
 namespace {
@@ -275,11 +276,16 @@ struct Handle {
   KvMaps kv_maps{};
   std::unique_ptr<Batched> batched;  // streams > 1
   std::vector<StreamSlot> slots;
+  // Payload checksums of the shards added since qwc_model_begin, for the
+  // reference's duplicate-shard check (src/wasm/model.zig:162-175).
+  std::vector<uint32_t> shards;
 
   ~Handle() {
     if (stream) cudaStreamDestroy(stream);
   }
 };
+
+constexpr size_t kShardCountMax = 64;  // src/wasm/model.zig:81
 
 std::mutex g_mutex;
 std::map<uint32_t, std::unique_ptr<Handle>> g_handles;
@@ -309,6 +315,7 @@ int32_t status_of(cudaError_t e) {
 
 void release_model(Handle* h) {
   h->tensors.clear();
+  h->shards.clear();
   for (DevBuf* b : {&h->model_buf, &h->rope_cos, &h->rope_sin, &h->k_cache, &h->v_cache, &h->qkv, &h->attn_out,
                     &h->hidden_g, &h->act, &h->attn_part, &h->attn_count, &h->amax_val, &h->amax_idx, &h->barrier,
                     &h->error, &h->tokens_out, &h->logits, &h->prompt_ids, &h->prompt_rows, &h->audio_rows, &h->trace_buf}) {
@@ -1199,11 +1206,53 @@ int32_t qwc_model_add_tensor(uint32_t handle, uint32_t kind, uint32_t layer, uin
   return QWC_OK;
 }
 
+int32_t qwc_model_add_shard(uint32_t handle, const void* bytes, uint64_t len) {
+  Handle* h = lookup(handle);
+  if (!h) return QWC_INVALID_ARGUMENT;
+  if (h->state != State::kReady) return QWC_INVALID_STATE;
+  if (h->shards.size() >= kShardCountMax) return QWC_LIMIT_EXCEEDED;
+  ShardView v;
+  QWC_TRY(parse_shard(bytes, len, &v));
+  // DuplicateShard: the reference also compares buffer addresses, which here
+  // can repeat legitimately (the caller may free a shard after the call and
+  // reuse the memory), so only the payload checksum identifies a repeat.
+  for (uint32_t c : h->shards) {
+    if (c == v.checksum) return QWC_INVALID_ARGUMENT;
+  }
+  // Every decoder tensor is checked before any is copied, so a rejected shard
+  // leaves the handle as it was. Tensors of other kinds (audio tower,
+  // projector) are validated by the parse and otherwise not kept: this
+  // library runs the decoder only.
+  auto decoder_kind = [](uint32_t kind) {
+    return kind >= QWC_KIND_DECODER_EMBED_TOKENS && kind <= QWC_KIND_DECODER_DOWN;
+  };
+  for (uint32_t i = 0; i < v.count; ++i) {
+    const ShardEntry e = shard_entry(v, i);
+    if (!decoder_kind(e.kind)) continue;
+    const bool vec = e.rank == 1 && e.format == QWC_FORMAT_F32;
+    const bool mat = e.rank == 2 && (e.format == QWC_FORMAT_Q4 || e.format == QWC_FORMAT_Q8 || e.format == QWC_FORMAT_F32);
+    if (!vec && !mat) return QWC_UNSUPPORTED_MODEL;
+    if (h->tensors.count({e.kind, e.layer})) return QWC_INVALID_ARGUMENT;  // DuplicateTensor
+  }
+  for (uint32_t i = 0; i < v.count; ++i) {
+    const ShardEntry e = shard_entry(v, i);
+    if (!decoder_kind(e.kind)) continue;
+    const uint32_t rows = e.rank == 1 ? 1u : e.dims[0];
+    const uint32_t cols = e.rank == 1 ? e.dims[0] : e.dims[1];
+    QWC_TRY(qwc_model_add_tensor(handle, e.kind, e.layer, e.format, rows, cols, v.payload + e.offset_bytes,
+                                 e.len_bytes));
+  }
+  h->shards.push_back(v.checksum);
+  return QWC_OK;
+}
+
 int32_t qwc_model_set_cache_format(uint32_t handle, uint32_t format) {
   Handle* h = lookup(handle);
   if (!h) return QWC_INVALID_ARGUMENT;
   if (format != QWC_CACHE_F32 && format != QWC_CACHE_Q8) return QWC_INVALID_ARGUMENT;
-  if (h->state != State::kReady || h->tensors.empty()) return QWC_INVALID_STATE;  // model.zig:184-188
+  if (h->state != State::kReady || (h->tensors.empty() && h->shards.empty())) {
+    return QWC_INVALID_STATE;  // model.zig:184-188
+  }
   h->cache_format = format;
   return QWC_OK;
 }

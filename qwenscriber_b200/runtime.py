@@ -42,6 +42,9 @@ SIGNATURES = {
     "qwc_status_message": (c_char_p, [c_int32]),
     "qwc_set_option": (c_int32, [c_uint32, c_uint32, c_uint32]),
     "qwc_model_begin": (c_int32, [c_uint32]),
+    "qwc_model_add_shard": (c_int32, [c_uint32, c_void_p, c_uint64]),
+    "qwc_shard_validate": (c_int32, [c_void_p, c_uint64, c_void_p]),
+    "qwc_shard_checksum": (c_uint32, [c_void_p, c_uint64]),
     "qwc_model_add_tensor": (c_int32, [c_uint32, c_uint32, c_uint32, c_uint32, c_uint32, c_uint32, c_void_p, c_uint64]),
     "qwc_model_set_cache_format": (c_int32, [c_uint32, c_uint32]),
     "qwc_model_set_streams": (c_int32, [c_uint32, c_uint32]),
@@ -107,6 +110,25 @@ def lib() -> ctypes.CDLL:
     return _lib
 
 
+def aligned_copy(data: bytes | np.ndarray, alignment: int = 16) -> np.ndarray:
+    """The bytes of `data` in a fresh uint8 array whose first byte is
+    `alignment`-aligned."""
+    raw = np.frombuffer(bytes(data), np.uint8) if not isinstance(data, np.ndarray) else data.view(np.uint8).ravel()
+    store = np.empty(raw.nbytes + alignment, np.uint8)
+    start = (-store.ctypes.data) % alignment
+    out = store[start:start + raw.nbytes]
+    out[:] = raw
+    return out
+
+
+def shard_validate(shard: bytes | np.ndarray) -> tuple[int, int]:
+    """qwc_shard_validate: (status, tensor count); needs no GPU."""
+    buf = aligned_copy(shard)
+    count = ctypes.c_uint32(0)
+    status = lib().qwc_shard_validate(buf.ctypes.data, buf.nbytes, ctypes.byref(count))
+    return status, count.value
+
+
 def check(status: int, call: str) -> int:
     if status < 0:
         raise QwcError(status, call)
@@ -163,6 +185,12 @@ class CudaModel:
         p = np.ascontiguousarray(payload)
         check(self._L.qwc_model_add_tensor(self.handle, kind, layer, fmt, rows, cols, p.ctypes.data, p.nbytes),
               f"qwc_model_add_tensor(kind={kind}, layer={layer})")
+
+    def add_shard(self, shard: bytes | np.ndarray) -> None:
+        """qwc_model_add_shard on a whole `.qw` shard (copied into a 16-byte
+        aligned buffer first, as the ABI requires)."""
+        buf = aligned_copy(shard)
+        check(self._L.qwc_model_add_shard(self.handle, buf.ctypes.data, buf.nbytes), "qwc_model_add_shard")
 
     def set_cache_format(self, fmt: int) -> None:
         check(self._L.qwc_model_set_cache_format(self.handle, fmt), "qwc_model_set_cache_format")
