@@ -309,6 +309,22 @@ __device__ __forceinline__ UnitPos unit_pos(const AttnSmem* a, const StreamsStep
   return UnitPos{lo, r / chunks, r % chunks, chunks, a->cache[lo]};
 }
 
+// The unit after `up` in (column, kv head, chunk) order, skipping columns
+// without units; the walk from one unit to the next costs a few compares
+// instead of unit_pos's search and division.
+__device__ __forceinline__ UnitPos next_unit(const AttnSmem* a, uint32_t kv_heads, UnitPos up) {
+  if (++up.ch < up.chunks) return up;
+  up.ch = 0;
+  if (++up.h < kv_heads) return up;
+  up.h = 0;
+  uint32_t s = up.s + 1;
+  while (s < kMaxStreams - 1 && a->prefix[s + 1] == a->prefix[s]) ++s;
+  up.s = s;
+  up.chunks = a->pos[s] / kAttnChunk + 1;
+  up.cache = a->cache[s];
+  return up;
+}
+
 __global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kernel(const StreamsStep P,
                                                                                const __grid_constant__ KvMaps4 maps,
                                                                                uint32_t layer) {
@@ -344,13 +360,13 @@ __global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kern
     // ---- producer: TMA boxes of units u0..u1 into the ring ----
     if (lane == 0) {
       uint32_t it = 0;
-      for (uint32_t u = u0; u < u1; ++u, ++it) {
+      UnitPos up = unit_pos(a, P, kv_heads, u0);
+      for (uint32_t u = u0; u < u1; ++u, ++it, up = next_unit(a, kv_heads, up)) {
         const uint32_t slot = it % kAttnSlots;
         if (it >= kAttnSlots &&
             !mbar_wait_bounded(&a->empty[slot], ((it / kAttnSlots) - 1) & 1u, P.error, P.timeout_ns, 102)) {
           break;
         }
-        const UnitPos up = unit_pos(a, P, kv_heads, u);
         uint8_t* dst = a->ring[slot];
         mbar_arrive_expect_tx(&a->full[slot], kTileBytes);
         const int32_t y = static_cast<int32_t>(up.ch * kAttnChunk), z = static_cast<int32_t>(layer),
@@ -495,8 +511,8 @@ __global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kern
   const float scaling = m.attn_scaling;
   const uint64_t bias = pack2(kNegQ8, kNegQ8);
   uint32_t it = 0;
-  for (uint32_t u = u0; u < u1; ++u, ++it) {
-    const UnitPos up = unit_pos(a, P, kv_heads, u);
+  UnitPos up = unit_pos(a, P, kv_heads, u0);
+  for (uint32_t u = u0; u < u1; ++u, ++it, up = next_unit(a, kv_heads, up)) {
     if (up.s != cur.s || up.h != cur.h) {
       if (cur.s != 0xFFFFFFFFu) flush();  // ends with every warp past the previous segment
       cur = up;
@@ -558,10 +574,15 @@ __global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kern
       mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
     }
     const float mn0 = fmaxf(wm[0], mx0), mn1 = fmaxf(wm[1], mx1);
-    const float p0 = valid ? expf(s0 - mn0) : 0.0f;
-    const float p1 = valid ? expf(s1 - mn1) : 0.0f;
-    const float r0 = (wm[0] == -INFINITY) ? 0.0f : expf(wm[0] - mn0);
-    const float r1 = (wm[1] == -INFINITY) ? 0.0f : expf(wm[1] - mn1);
+    const float p0 = valid ? __expf(s0 - mn0) : 0.0f;
+    const float p1 = valid ? __expf(s1 - mn1) : 0.0f;
+    const float r0 = (wm[0] == -INFINITY) ? 0.0f : __expf(wm[0] - mn0);
+    const float r1 = (wm[1] == -INFINITY) ? 0.0f : __expf(wm[1] - mn1);
+    // Lane (i, qd) also weighs position i's values: scale of value group
+    // qd & 1 times the probability of query head qd >> 1.
+    const float sw_lane = f16_bits_to_f32_fast(*reinterpret_cast<const uint16_t*>(
+                              tile + kTVS + prow * 16 + (up.h % 4) * 4 + (qd & 1u) * 2)) *
+                          ((qd >> 1) ? p1 : p0);
     float ls0 = p0, ls1 = p1;
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) {
@@ -579,10 +600,8 @@ __global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kern
     for (int i = 0; i < 8; ++i) {
       const uint32_t row = static_cast<uint32_t>(warp) * 8 + i;
       const uint32_t word = *reinterpret_cast<const uint32_t*>(tile + kTV + row * kHeadDim + 4 * lane);
-      const uint32_t bits = *reinterpret_cast<const uint16_t*>(tile + kTVS + row * 16 + (up.h % 4) * 4 + grp * 2);
-      const float scale = f16_bits_to_f32_fast(bits);
-      const float q0 = __shfl_sync(0xffffffffu, p0, 4 * i), q1 = __shfl_sync(0xffffffffu, p1, 4 * i);
-      const float sw0 = scale * q0, sw1 = scale * q1;
+      const float sw0 = __shfl_sync(0xffffffffu, sw_lane, 4 * i + grp);
+      const float sw1 = __shfl_sync(0xffffffffu, sw_lane, 4 * i + grp + 2);
       const uint64_t c01 = add2(pack2(bits_f32(__byte_perm(word, kMagic, 0x7440)),
                                       bits_f32(__byte_perm(word, kMagic, 0x7441))), bias);  // code - 128, exact
       const uint64_t c23 = add2(pack2(bits_f32(__byte_perm(word, kMagic, 0x7442)),
