@@ -132,11 +132,18 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, ui
       : "memory");
 }
 
-// 32 lanes x 8 columns of this warp's lane quarter from registers.
-__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint4& a, const uint4& b) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
-               "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w)
-               : "memory");
+
+// 32 lanes x 32 columns of this warp's lane quarter from registers: one
+// instruction for a row's whole K block of hi (or lo) values.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint4 (&v)[8]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(v[0].x), "r"(v[0].y), "r"(v[0].z), "r"(v[0].w), "r"(v[1].x), "r"(v[1].y), "r"(v[1].z), "r"(v[1].w),
+      "r"(v[2].x), "r"(v[2].y), "r"(v[2].z), "r"(v[2].w), "r"(v[3].x), "r"(v[3].y), "r"(v[3].z), "r"(v[3].w),
+      "r"(v[4].x), "r"(v[4].y), "r"(v[4].z), "r"(v[4].w), "r"(v[5].x), "r"(v[5].y), "r"(v[5].z), "r"(v[5].w),
+      "r"(v[6].x), "r"(v[6].y), "r"(v[6].z), "r"(v[6].w), "r"(v[7].x), "r"(v[7].y), "r"(v[7].z), "r"(v[7].w)
+      : "memory");
 }
 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -388,33 +395,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t sc = static_cast<uint32_t>(sb) * 0x10001u;
       const uint32_t ahi = tmem + lane_addr + kTmemA + at * kTmemAStage + 64 * t;
       const uint32_t alo = ahi + 32;
-      uint4 h0, l0, h1, l1;
+      // The row's 64 K values as 32 columns of f16 pairs, hi and lo; each
+      // goes to TMEM in one 32-column store.
+      uint4 hv[8], lv[8];
       if (q4) {
-        // The row's 64 K values: two 16-byte chunks of codes, 8 per word.
+        // Two 16-byte chunks of codes, 8 per word.
         const uint4* src = reinterpret_cast<const uint4*>(s->codes[st] + r * (kKBlock / 2));
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
           const uint4 w = src[q];
-          dequant_q4_word(w.x, sc, h0, l0);
-          dequant_q4_word(w.y, sc, h1, l1);
-          tmem_st8(ahi + 8 * (2 * q), h0, h1);
-          tmem_st8(alo + 8 * (2 * q), l0, l1);
-          dequant_q4_word(w.z, sc, h0, l0);
-          dequant_q4_word(w.w, sc, h1, l1);
-          tmem_st8(ahi + 8 * (2 * q + 1), h0, h1);
-          tmem_st8(alo + 8 * (2 * q + 1), l0, l1);
+          dequant_q4_word(w.x, sc, hv[4 * q], lv[4 * q]);
+          dequant_q4_word(w.y, sc, hv[4 * q + 1], lv[4 * q + 1]);
+          dequant_q4_word(w.z, sc, hv[4 * q + 2], lv[4 * q + 2]);
+          dequant_q4_word(w.w, sc, hv[4 * q + 3], lv[4 * q + 3]);
         }
       } else {
         const uint4* src = reinterpret_cast<const uint4*>(s->codes[st] + r * kKBlock);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const uint4 w = src[q];
-          dequant_q8_words(w.x, w.y, sc, h0, l0);
-          dequant_q8_words(w.z, w.w, sc, h1, l1);
-          tmem_st8(ahi + 8 * q, h0, h1);
-          tmem_st8(alo + 8 * q, l0, l1);
+          dequant_q8_words(w.x, w.y, sc, hv[2 * q], lv[2 * q]);
+          dequant_q8_words(w.z, w.w, sc, hv[2 * q + 1], lv[2 * q + 1]);
         }
       }
+      tmem_st32(ahi, hv);
+      tmem_st32(alo, lv);
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
       __syncwarp();
