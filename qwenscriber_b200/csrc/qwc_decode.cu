@@ -438,20 +438,21 @@ __device__ float block_sum(Ctx& c, float v) {
   return total;
 }
 
-// x holds activations multiplied by 16^-(nibble position) for q4 stages
-// (see qwc_device.cuh), so the GEMV can OR nibbles into floats in place.
+// x holds activations multiplied by 2^74 * 16^-(nibble position) for q4
+// stages (q4_chunk_dot_sub, qwc_device.cuh), so the GEMV can mask nibbles
+// straight into floats.
 
 constexpr int kMaxPer4 = (kHiddenMax / 4 + kConsumerThreads - 1) / kConsumerThreads;  // float4 groups per thread
 
 // x[k .. k + 3] <- v, prescaled for q4 stages; k is a multiple of 4.
 __device__ __forceinline__ void store_x4(Ctx& c, uint32_t k, float4 v, bool q4) {
   if (q4) {
-    // q4_xscale over k & 7 = 0..3 or 4..7.
+    // kQ4SubScale * q4_xscale over k & 7 = 0..3 or 4..7 (powers of two: exact).
     const bool hi = (k & 4u) != 0;
-    v.x *= hi ? q4_xscale(4) : q4_xscale(0);
-    v.y *= hi ? q4_xscale(5) : q4_xscale(1);
-    v.z *= hi ? q4_xscale(6) : q4_xscale(2);
-    v.w *= hi ? q4_xscale(7) : q4_xscale(3);
+    v.x *= hi ? kQ4SubScale * q4_xscale(4) : kQ4SubScale * q4_xscale(0);
+    v.y *= hi ? kQ4SubScale * q4_xscale(5) : kQ4SubScale * q4_xscale(1);
+    v.z *= hi ? kQ4SubScale * q4_xscale(6) : kQ4SubScale * q4_xscale(2);
+    v.w *= hi ? kQ4SubScale * q4_xscale(7) : kQ4SubScale * q4_xscale(3);
   }
   *reinterpret_cast<float4*>(&c.s->x[x_index(k)]) = v;
 }
@@ -594,7 +595,6 @@ __device__ void gemv_tiles(Ctx& c, const Piece* pieces, int np, bool lm, Best& b
       const uint8_t* base = acquire_tile(c);
       if (c.ok) {
         const uint8_t* codes = base + nr * pc.scale_row;
-        const uint32_t magic = magic_reg();
         for (uint32_t ps = c.warp; ps < passes; ps += kConsumerWarps) {
           const uint32_t r0 = (ps / chunks) * kRowsPerPass, j = ps % chunks;
           const uint32_t off = 16u * c.lane + 512u * j;
@@ -606,6 +606,9 @@ __device__ void gemv_tiles(Ctx& c, const Piece* pieces, int np, bool lm, Best& b
             x2[2 * q] = pack2(v.x, v.y);
             x2[2 * q + 1] = pack2(v.z, v.w);
           }
+          // q4: the pass's 8 * sum(x), shared by its four rows.
+          float xbias = 0.0f;
+          if constexpr (FMT == kFormatQ4) xbias = 8.0f * q4_chunk_xsum(x2);
           float acc[kRowsPerPass];
 #pragma unroll
           for (int q = 0; q < kRowsPerPass; ++q) {
@@ -615,7 +618,7 @@ __device__ void gemv_tiles(Ctx& c, const Piece* pieces, int np, bool lm, Best& b
                 *reinterpret_cast<const uint16_t*>(base + row * pc.scale_row + (off / Fmt<FMT>::kDB) * 2));
             float d;
             if constexpr (FMT == kFormatQ4) {
-              d = q4_chunk_dot(w, x2, magic);
+              d = fmaf(q4_chunk_dot_sub(w, x2), kQ4SubUnscale, -xbias);  // sum((u - 8) * x)
             } else {
               d = q8_chunk_dot(w, x2);
             }

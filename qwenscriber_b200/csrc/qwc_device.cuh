@@ -105,6 +105,51 @@ __device__ __forceinline__ float q4_chunk_dot(uint4 w, const uint64_t* x2, uint3
 
 __device__ __forceinline__ float q4_chunk_dot(uint4 w, const uint64_t* x2) { return q4_chunk_dot(w, x2, magic_reg()); }
 
+// The same eight nibbles as subnormal floats: (w & 0xF << p) read as f32 is
+// exactly u * 2^(p - 149), with no bias constant to remove. Against
+// activations prescaled by 2^(74 - p) the products are u * x * 2^-75, so
+// one power-of-two multiply of the sum restores sum(u * x); the bias comes
+// out separately as 8 * sum(x) (q4_chunk_xsum). Needs subnormals kept
+// (no flush-to-zero), which is the compiler's default.
+constexpr float kQ4SubScale = 0x1p74f;   // activation prescale on top of q4_xscale
+constexpr float kQ4SubUnscale = 0x1p75f;  // sum(u * x) = kQ4SubUnscale * sum of products
+__device__ __forceinline__ void q4_word_sub(uint32_t w, const uint64_t* x2, uint64_t& acc) {
+  const uint32_t h = w >> 12;
+  acc = fma2(pack2(bits_f32(w & 0xFu), bits_f32(w & 0xF0u)), x2[0], acc);
+  acc = fma2(pack2(bits_f32(w & 0xF00u), bits_f32(w & 0xF000u)), x2[1], acc);
+  acc = fma2(pack2(bits_f32(w & 0xF0000u), bits_f32(h & 0xF00u)), x2[2], acc);
+  acc = fma2(pack2(bits_f32(h & 0xF000u), bits_f32(h & 0xF0000u)), x2[3], acc);
+}
+
+// sum(u * x) * 2^-75 over 32 q4 weights (one 16-byte chunk).
+__device__ __forceinline__ float q4_chunk_dot_sub(uint4 w, const uint64_t* x2) {
+  uint64_t a = 0, b = 0;
+  q4_word_sub(w.x, x2 + 0, a);
+  q4_word_sub(w.y, x2 + 4, b);
+  q4_word_sub(w.z, x2 + 8, a);
+  q4_word_sub(w.w, x2 + 12, b);
+  const float2 fa = unpack2(a), fb = unpack2(b);
+  return (fa.x + fa.y) + (fb.x + fb.y);
+}
+
+// sum(x) over the chunk's 32 activations, from their prescaled pairs.
+__device__ __forceinline__ float q4_chunk_xsum(const uint64_t* x2) {
+  // Undo kQ4SubScale * q4_xscale per pair position: nibble positions
+  // (0, 4), (8, 12), (16, 8), (12, 16) bits.
+  const uint64_t d0 = pack2(0x1p-74f, 0x1p-70f), d1 = pack2(0x1p-66f, 0x1p-62f);
+  const uint64_t d2 = pack2(0x1p-58f, 0x1p-66f), d3 = pack2(0x1p-62f, 0x1p-58f);
+  uint64_t a = 0, b = 0;
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    a = fma2(x2[4 * t + 0], d0, a);
+    b = fma2(x2[4 * t + 1], d1, b);
+    a = fma2(x2[4 * t + 2], d2, a);
+    b = fma2(x2[4 * t + 3], d3, b);
+  }
+  const float2 fa = unpack2(a), fb = unpack2(b);
+  return (fa.x + fa.y) + (fb.x + fb.y);
+}
+
 __device__ __forceinline__ void q8_word(uint32_t w, const uint64_t* x2, uint64_t& acc) {
   const uint64_t v01 = pack2(bits_f32(__byte_perm(w, kMagic, 0x7440)), bits_f32(__byte_perm(w, kMagic, 0x7441)));
   const uint64_t v23 = pack2(bits_f32(__byte_perm(w, kMagic, 0x7442)), bits_f32(__byte_perm(w, kMagic, 0x7443)));
