@@ -576,60 +576,78 @@ struct Best {
 };
 
 // Consumes the stage's tiles. Non-LM stages leave per-row dot products in
-// s->part[local]; the LM stage keeps a running argmax per thread and
-// optionally stores the logits. A warp pass covers four rows of one 512-byte
-// chunk of codes: lane l takes the 16 bytes at l * 16 of the chunk, the
-// matching activations from x are loaded once for the four rows, and the
-// four dot products reduce together (warp_sum4). Rows past the tile repeat
-// the last row so the pass has no branches; their sums are dropped. The
-// chunk sums of a row are added in chunk order after the tile.
+// s->part[local]; the LM stage keeps a running argmax per lane and optionally
+// stores the logits. A warp pass covers four rows: lane l takes the 16 bytes
+// at l * 16 of each 512-byte chunk, the matching activations from x are
+// loaded once per chunk for the four rows, and the four dot products reduce
+// together (warp_sum4). Rows past the tile repeat the last row so the pass
+// has no branches; their sums are dropped.
 template <uint32_t FMT>
 __device__ void gemv_tiles(Ctx& c, const Piece* pieces, int np, bool lm, Best& best, float* logits_out) {
   for (int p = 0; p < np; ++p) {
     const Piece pc = pieces[p];
     const uint32_t per = rows_per_tile(pc);
     const uint32_t chunks = pc.code_row / 512u;
+    // Rows of at most two chunks are taken whole by one pass, and their sums
+    // go straight to their rows; longer rows are split into one-chunk passes
+    // whose sums are added after the tile.
+    const bool whole = chunks <= 2;
+    const uint32_t span = whole ? chunks : 1u;  // chunks per pass
     for (uint32_t r = 0; r < pc.rows; r += per) {
       const uint32_t nr = min(per, pc.rows - r);
-      const uint32_t passes = (nr + kRowsPerPass - 1) / kRowsPerPass * chunks;
+      const uint32_t quads = (nr + kRowsPerPass - 1) / kRowsPerPass;
+      const uint32_t passes = whole ? quads : quads * chunks;
       const uint8_t* base = acquire_tile(c);
       if (c.ok) {
         const uint8_t* codes = base + nr * pc.scale_row;
         for (uint32_t ps = c.warp; ps < passes; ps += kConsumerWarps) {
-          const uint32_t r0 = (ps / chunks) * kRowsPerPass, j = ps % chunks;
-          const uint32_t off = 16u * c.lane + 512u * j;
-          const uint32_t kbase = off * Fmt<FMT>::kKPerByte;
-          uint64_t x2[Fmt<FMT>::kPairs];
+          const uint32_t r0 = (whole ? ps : ps / chunks) * kRowsPerPass, j0 = whole ? 0u : ps % chunks;
+          float acc[kRowsPerPass] = {0.0f, 0.0f, 0.0f, 0.0f};
+          for (uint32_t j = j0; j < j0 + span; ++j) {
+            const uint32_t off = 16u * c.lane + 512u * j;
+            const uint32_t kbase = off * Fmt<FMT>::kKPerByte;
+            uint64_t x2[Fmt<FMT>::kPairs];
 #pragma unroll
-          for (int q = 0; q < Fmt<FMT>::kPairs / 2; ++q) {
-            const float4 v = *reinterpret_cast<const float4*>(&c.s->x[x_index(kbase + 4 * q)]);
-            x2[2 * q] = pack2(v.x, v.y);
-            x2[2 * q + 1] = pack2(v.z, v.w);
-          }
-          // q4: the pass's 8 * sum(x), shared by its four rows.
-          float xbias = 0.0f;
-          if constexpr (FMT == kFormatQ4) xbias = 8.0f * q4_chunk_xsum(x2);
-          float acc[kRowsPerPass];
-#pragma unroll
-          for (int q = 0; q < kRowsPerPass; ++q) {
-            const uint32_t row = min(r0 + q, nr - 1);
-            const uint4 w = *reinterpret_cast<const uint4*>(codes + row * pc.code_row + off);
-            const float scale = f16_bits_to_f32_fast(
-                *reinterpret_cast<const uint16_t*>(base + row * pc.scale_row + (off / Fmt<FMT>::kDB) * 2));
-            float d;
-            if constexpr (FMT == kFormatQ4) {
-              d = fmaf(q4_chunk_dot_sub(w, x2), kQ4SubUnscale, -xbias);  // sum((u - 8) * x)
-            } else {
-              d = q8_chunk_dot(w, x2);
+            for (int q = 0; q < Fmt<FMT>::kPairs / 2; ++q) {
+              const float4 v = *reinterpret_cast<const float4*>(&c.s->x[x_index(kbase + 4 * q)]);
+              x2[2 * q] = pack2(v.x, v.y);
+              x2[2 * q + 1] = pack2(v.z, v.w);
             }
-            acc[q] = d * scale;
+            // q4: the chunk's 8 * sum(x), shared by the pass's four rows.
+            float xbias = 0.0f;
+            if constexpr (FMT == kFormatQ4) xbias = 8.0f * q4_chunk_xsum(x2);
+#pragma unroll
+            for (int q = 0; q < kRowsPerPass; ++q) {
+              const uint32_t row = min(r0 + q, nr - 1);
+              const uint4 w = *reinterpret_cast<const uint4*>(codes + row * pc.code_row + off);
+              const float scale = f16_bits_to_f32_fast(
+                  *reinterpret_cast<const uint16_t*>(base + row * pc.scale_row + (off / Fmt<FMT>::kDB) * 2));
+              float d;
+              if constexpr (FMT == kFormatQ4) {
+                d = fmaf(q4_chunk_dot_sub(w, x2), kQ4SubUnscale, -xbias);  // sum((u - 8) * x)
+              } else {
+                d = q8_chunk_dot(w, x2);
+              }
+              acc[q] = fmaf(d, scale, acc[q]);
+            }
           }
           const float total = warp_sum4(acc[0], acc[1], acc[2], acc[3]);
-          const uint32_t row = r0 + (static_cast<uint32_t>(c.lane) >> 3);
-          if ((c.lane & 7) == 0 && row < nr) c.s->chunk_part[row * chunks + j] = total;
+          const uint32_t i = r0 + (static_cast<uint32_t>(c.lane) >> 3);
+          if ((c.lane & 7) == 0 && i < nr) {
+            if (!whole) {
+              c.s->chunk_part[i * chunks + j0] = total;
+            } else if (!lm) {
+              c.s->part[pc.local0 + r + i] = total;
+            } else {
+              const uint32_t row = pc.out0 + r + i;
+              if (logits_out) logits_out[row] = total;
+              if (total > best.v || (total == best.v && row < best.i)) best = Best{total, row};
+            }
+          }
         }
       }
       release_tile(c);
+      if (whole) continue;
       consumer_sync(kConsumerThreads);
       for (uint32_t i = c.tid; i < nr; i += kConsumerThreads) {
         float total = c.s->chunk_part[i * chunks];
