@@ -534,7 +534,7 @@ int32_t finish_model(Handle* h, const Config& c) {
   QWC_TRY(h->attn_out.alloc(size_t(qw) * 4));
   QWC_TRY(h->hidden_g.alloc(size_t(hidden) * 4));
   QWC_TRY(h->act.alloc(size_t(ffn) * 4));
-  QWC_TRY(h->attn_part.alloc(size_t(c.text_attention_heads) * h->max_chunks * (kHeadDim + 2) * 4));
+  QWC_TRY(h->attn_part.alloc(size_t(c.text_attention_heads) * h->max_chunks * kAttnPartStride * 4));
   QWC_TRY(h->attn_count.alloc(size_t(c.text_key_value_heads) * 4));
   QWC_CUDA(cudaMemset(h->attn_count.ptr, 0, h->attn_count.bytes));
   QWC_TRY(h->amax_val.alloc(size_t(h->grid) * 4));

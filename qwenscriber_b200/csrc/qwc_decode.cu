@@ -508,6 +508,83 @@ __device__ void load_x_global(Ctx& c, const float* src, uint32_t width, bool q4)
   consumer_sync(kConsumerThreads);
 }
 
+// The O projection's input: the attention output of every query head,
+// merged from its chunk partials (flash-decode rescale: each chunk's o and
+// sum scaled by exp(max_chunk - max_all), then o / sum). A thread owns
+// kMergeGroups float4 groups of the output and issues the loads of eight
+// chunks for all of them together, one L2 round trip per eight chunks.
+constexpr int kMergeGroups = 2;
+__device__ void attention_into_x(Ctx& c, const float* parts, uint32_t chunks, bool q4) {
+  const uint32_t qw4 = c.m->q_heads * kHeadDim / 4;
+  const uint32_t stride = c.P->max_chunks * kAttnPartStride;  // floats per query head
+  for (uint32_t g0 = c.tid; g0 < qw4; g0 += kMergeGroups * kConsumerThreads) {
+    const float* base[kMergeGroups];
+    uint32_t k4[kMergeGroups];
+    bool on[kMergeGroups];
+    float mx[kMergeGroups], l[kMergeGroups];
+    float4 o[kMergeGroups];
+#pragma unroll
+    for (int g = 0; g < kMergeGroups; ++g) {
+      k4[g] = g0 + g * kConsumerThreads;
+      on[g] = k4[g] < qw4;
+      const uint32_t k = on[g] ? k4[g] * 4 : 0u;
+      base[g] = parts + size_t(k / kHeadDim) * stride + k % kHeadDim;
+      mx[g] = -INFINITY;
+      l[g] = 0.0f;
+      o[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    for (uint32_t c0 = 0; c0 < chunks; c0 += 8) {
+      float pm[kMergeGroups][8], pl[kMergeGroups][8];
+      float4 po[kMergeGroups][8];
+#pragma unroll
+      for (int g = 0; g < kMergeGroups; ++g) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          pm[g][q] = -INFINITY;
+          pl[g][q] = 0.0f;
+          po[g][q] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (on[g] && c0 + q < chunks) {
+            const float* src = base[g] + size_t(c0 + q) * kAttnPartStride;
+            const uint32_t d = static_cast<uint32_t>(k4[g] * 4 % kHeadDim);
+            pm[g][q] = ld_cg(src - d + kHeadDim);
+            pl[g][q] = ld_cg(src - d + kHeadDim + 1);
+            po[g][q] = ld_cg4(reinterpret_cast<const float4*>(src));
+          }
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < kMergeGroups; ++g) {
+        float bm = mx[g];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) bm = fmaxf(bm, pm[g][q]);
+        const float rescale = (mx[g] == -INFINITY) ? 0.0f : expf(mx[g] - bm);
+        float4 acc = make_float4(o[g].x * rescale, o[g].y * rescale, o[g].z * rescale, o[g].w * rescale);
+        float ls = l[g] * rescale;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float f = (pm[g][q] == -INFINITY) ? 0.0f : expf(pm[g][q] - bm);
+          acc = make_float4(fmaf(po[g][q].x, f, acc.x), fmaf(po[g][q].y, f, acc.y), fmaf(po[g][q].z, f, acc.z),
+                            fmaf(po[g][q].w, f, acc.w));
+          ls = fmaf(pl[g][q], f, ls);
+        }
+        o[g] = acc;
+        l[g] = ls;
+        mx[g] = bm;
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < kMergeGroups; ++g) {
+      if (!on[g]) continue;
+      const float4 out = make_float4(o[g].x / l[g], o[g].y / l[g], o[g].z / l[g], o[g].w / l[g]);
+      // Every CTA merges the same partials in the same order; CTA 0 also
+      // keeps the attention output for qwc_debug_scratch.
+      if (blockIdx.x == 0) reinterpret_cast<float4*>(c.P->attn_out)[k4[g]] = out;
+      store_x4(c, 4 * k4[g], out, q4);
+    }
+  }
+  consumer_sync(kConsumerThreads);
+}
+
 // Layer-0 input: the token's embedding row (decoder.zig:346-376, quant.zig:348-364)
 // or an audio row; this CTA's residual rows keep the raw values, x the normed.
 __device__ void input_into_x(Ctx& c, uint32_t token, int32_t audio_row, Span own, bool q4) {
@@ -888,67 +965,18 @@ __device__ void attention_stage(Ctx& c, uint32_t layer, uint32_t position) {
       l += a->lsum[j][w];
     }
     const float mj = a->mx[j];
-    if (chunks == 1) {
-      c.P->attn_out[(2 * h + j) * kHeadDim + d] = o / l;
-      consumer_sync(kConsumerThreads);
-      continue;
-    }
+    // 7. The chunk's partial (o[d], max, sum) goes to global memory; the O
+    // stage merges the partials of every chunk of every head while it loads
+    // its input (attention_into_x), so no unit waits for another here.
     {
-      float* dst = c.P->attn_part + (size_t(2 * h + j) * c.P->max_chunks + ch) * (kHeadDim + 2);
+      float* dst = c.P->attn_part + (size_t(2 * h + j) * c.P->max_chunks + ch) * kAttnPartStride;
       dst[d] = o;
       if (d == 0) {
         dst[kHeadDim] = mj;
         dst[kHeadDim + 1] = l;
       }
     }
-    // The counter update is acquire-release at gpu scope: its release (after
-    // the bar.sync) publishes this CTA's partial, and the last arriver's
-    // acquire makes every other CTA's partial visible to the loads below.
-    consumer_sync(kConsumerThreads);
-    if (tid == 0) {
-      const uint32_t prev = atom_add_acq_rel(c.P->attn_count + h, 1u);
-      c.s->flag = (prev == chunks - 1) ? 1u : 0u;
-    }
-    consumer_sync(kConsumerThreads);
-    if (c.s->flag) {
-      // Chunks are combined sixteen at a time with all loads of a batch
-      // issued together (online rescale).
-      float mx = -INFINITY;
-      o = 0.0f;
-      l = 0.0f;
-      const float* base = c.P->attn_part + size_t(2 * h + j) * c.P->max_chunks * (kHeadDim + 2);
-      for (uint32_t q0 = 0; q0 < chunks; q0 += 16) {
-        float pm[16], po[16], pl[16];
-#pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          pm[q] = -INFINITY;
-          po[q] = 0.0f;
-          pl[q] = 0.0f;
-          if (q0 + q < chunks) {
-            const float* src = base + size_t(q0 + q) * (kHeadDim + 2);
-            pm[q] = ld_cg(src + kHeadDim);
-            po[q] = ld_cg(src + d);
-            pl[q] = ld_cg(src + kHeadDim + 1);
-          }
-        }
-        float bm = mx;
-#pragma unroll
-        for (int q = 0; q < 16; ++q) bm = fmaxf(bm, pm[q]);
-        const float rescale = (mx == -INFINITY) ? 0.0f : expf(mx - bm);
-        o *= rescale;
-        l *= rescale;
-#pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          const float f = (pm[q] == -INFINITY) ? 0.0f : expf(pm[q] - bm);
-          o = fmaf(po[q], f, o);
-          l = fmaf(pl[q], f, l);
-        }
-        mx = bm;
-      }
-      c.P->attn_out[(2 * h + j) * kHeadDim + d] = o / l;
-      if (tid == 0) c.P->attn_count[h] = 0;
-    }
-    consumer_sync(kConsumerThreads);
+    consumer_sync(kConsumerThreads);  // the scratch is reused by the next unit
   }
 }
 
@@ -960,7 +988,6 @@ __device__ void run_consumers(const DecodeLaunch& P, Smem* s) {
         static_cast<int>(threadIdx.x), false, 0, 0, 0, 0};
   const Span own = split_rows(m.hidden, blockIdx.x, gridDim.x);  // hidden rows of O and down
   const Span fr = split_rows(m.ffn, blockIdx.x, gridDim.x);      // ffn rows of gate and up
-  const uint32_t qw = m.q_heads * kHeadDim;
   uint32_t input = P.first_input;
 
   for (uint32_t t = 0; t < P.n_tokens && c.ok; ++t) {
@@ -991,8 +1018,10 @@ __device__ void run_consumers(const DecodeLaunch& P, Smem* s) {
           input_into_x(c, input, row, own, q4);
         } else if (st == kStQKV || st == kStGate || st == kStLM) {
           norm_global_into_x(c, P.hidden_g, m.hidden, q4);
-        } else if (st == kStO || st == kStDown) {
-          load_x_global(c, st == kStO ? P.attn_out : P.act, st == kStO ? qw : m.ffn, q4);
+        } else if (st == kStO) {
+          attention_into_x(c, P.attn_part, position / kAttnChunk + 1, q4);
+        } else if (st == kStDown) {
+          load_x_global(c, P.act, m.ffn, q4);
         }
         trace_mark(c, e0);
         Piece pieces[3];

@@ -17,6 +17,9 @@ constexpr uint32_t kPositionLimit = 8192;  // src/core/qwen3_asr/model.zig:62
 constexpr uint32_t kAttnChunk = 64;        // positions per split-K attention unit
 constexpr uint32_t kHiddenMax = 4096;      // widest hidden vector of the decode kernel
 constexpr uint32_t kHeadDim = 128;         // the kernels are written for head_dim 128
+// Floats per attention chunk partial of the decode kernel: o[head_dim], max,
+// sum, two pad words (16-byte aligned rows for float4 loads).
+constexpr uint32_t kAttnPartStride = kHeadDim + 4;
 
 inline uint32_t data_bytes_per_group(uint32_t format) {
   return format == kFormatQ4 ? 32u : (format == kFormatQ8 ? 64u : 0u);
@@ -93,7 +96,7 @@ struct DecodeLaunch {
   float* attn_out;           // q_width
   float* hidden_g;           // hidden
   float* act;                // ffn
-  float* attn_part;          // [q_heads][max_chunks][head_dim + 2]
+  float* attn_part;          // [q_heads][max_chunks][kAttnPartStride]
   uint32_t* attn_count;      // [kv_heads]
   float* amax_val;           // [grid]
   uint32_t* amax_idx;        // [grid]
