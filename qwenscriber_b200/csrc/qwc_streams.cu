@@ -109,6 +109,13 @@ __global__ void __launch_bounds__(kNormThreads) streams_norm_kernel(const Stream
     return;
   }
   float4* h = reinterpret_cast<float4*>(P.hidden + size_t(s) * hidden);
+  // The norm weights do not depend on the reduction: load them first.
+  float4 wv[kNormPer4];
+#pragma unroll
+  for (int i = 0; i < kNormPer4; ++i) {
+    const uint32_t k4 = threadIdx.x + i * kNormThreads;
+    wv[i] = k4 < h4 ? reinterpret_cast<const float4*>(weight)[k4] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   float4 v[kNormPer4];
   float ss = 0.0f;
 #pragma unroll
@@ -167,7 +174,7 @@ __global__ void __launch_bounds__(kNormThreads) streams_norm_kernel(const Stream
   for (int i = 0; i < kNormPer4; ++i) {
     const uint32_t k4 = threadIdx.x + i * kNormThreads;
     if (k4 < h4) {
-      const float4 w = reinterpret_cast<const float4*>(weight)[k4];
+      const float4 w = wv[i];
       xs[k4 * 4 + 0] = v[i].x * inv * w.x;
       xs[k4 * 4 + 1] = v[i].y * inv * w.y;
       xs[k4 * 4 + 2] = v[i].z * inv * w.z;

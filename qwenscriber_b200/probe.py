@@ -63,7 +63,7 @@ def main(argv=None) -> int:
         tokens = a.steps * w.streams
     else:
         pr = synthetic.make_prompt(w.config, w.audio_rows, w.text_ids, w.seed)
-        gm.decode_begin(pr.tokens, pr.audio, a.steps + 1)
+        gm.decode_begin(pr.tokens, pr.audio, a.steps + 1 + (min(a.chunk, 8) if a.trace else 0))
         before = gm.launches()
         ms = gm.run_timed(a.steps)
         tokens = a.steps
