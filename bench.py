@@ -223,17 +223,18 @@ def measure_streams(args, model, w, rank, local_rank, barrier, world):
     import dataclasses
 
     import torch
-    import torch.distributed as dist
 
     from qwenscriber_b200 import runtime as rt
-    from qwenscriber_b200 import synthetic
+    from qwenscriber_b200 import shards, synthetic
 
     m = dataclasses.replace(model, config=w.config)
     gm = rt.CudaModel(local_rank)
     synthetic.load_into(m, gm, cache_format=rt.CACHE_Q8, streams=w.streams)
     gm.set_option(rt.OPTION_IGNORE_EOS, 1)
-    lengths = synthetic.prefix_lengths(w)
-    prompts = [synthetic.make_prompt(w.config, lengths[s], w.text_ids, w.seed + 1000 * rank, stream=s)
+    # This rank's global streams (shards.shard): their own prefix lengths and prompts.
+    lengths = synthetic.prefix_lengths(w, world, rank)
+    ids = shards.shard(w.streams * world, world, rank)
+    prompts = [synthetic.make_prompt(w.config, lengths[s], w.text_ids, w.seed, stream=ids[s])
                for s in range(w.streams)]
     plen = [len(p.tokens) for p in prompts]
     warm, e2e_steps = 4, 32
@@ -251,34 +252,29 @@ def measure_streams(args, model, w, rank, local_rank, barrier, world):
         ms = gm.streams_run_timed(steps)
     launches = gm.launches() - launches0
     barrier()
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = shards.max_over_ranks(ms)
     barrier()
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
         gm.streams_step(w.streams)
     e2e_s = time.perf_counter() - t0
     barrier()
-    if world > 1:
-        t = torch.tensor([e2e_s], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
+    e2e_s = shards.max_over_ranks(e2e_s)
     gm.close()
     tokens = steps * w.streams * world
     bytes_total = streams_bytes(m, positions, steps)
     peak, peak_kind = measured_peak()
     achieved = bytes_total / (ms / 1000.0) / 1e9
     return {
-        "workload": w.name, "streams_per_gpu": w.streams, "value": tokens / (ms / 1000.0), "unit": "tokens/s",
+        "workload": w.name, "streams_per_gpu": w.streams,
+        "value": shards.aggregate_rate(steps * w.streams, world, ms / 1000.0), "unit": "tokens/s",
         "ms_per_step": ms / steps, "steps": steps, "warmup": warm,
         "prompt": f"{w.text_ids} text ids after U[{w.audio_rows[0]}, {w.audio_rows[1]}] audio rows per stream "
                   f"({sum(plen)} prompt positions in all, prefilled in {prefill_s:.2f} s, 64 positions per "
                   f"tensor-core step)",
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": peak_kind, "bytes_per_step": bytes_total / steps},
-        "e2e": {"value": e2e_steps * w.streams * world / e2e_s, "unit": "tokens/s",
+        "e2e": {"value": shards.aggregate_rate(e2e_steps * w.streams, world, e2e_s), "unit": "tokens/s",
                 "h2d_bytes_per_step": 64 * 16, "d2h_bytes_per_step": 64 * 4 + 16,
                 "includes": "qwc_streams_step: slot descriptors up, one graph replay, tokens down, per step"},
         "gpu_launches": launches, "clocks": clocks.summary(),
@@ -290,7 +286,7 @@ def run_ours(args, rank, world, local_rank):
     import torch.distributed as dist
 
     from qwenscriber_b200 import runtime as rt
-    from qwenscriber_b200 import synthetic
+    from qwenscriber_b200 import shards, synthetic
 
     torch.cuda.set_device(local_rank)
     if world > 1:
@@ -322,10 +318,7 @@ def run_ours(args, rank, world, local_rank):
         ms = gm.run_timed(args.steps)
     launches = gm.launches() - launches0
     barrier()
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = shards.max_over_ranks(ms)
     gm.decode_end()
 
     # ---- end to end through the public API: prompt upload + prefill + K steps, tokens read each step ----
@@ -337,10 +330,7 @@ def run_ours(args, rank, world, local_rank):
     e2e_s = time.perf_counter() - t0
     gm.decode_end()
     barrier()
-    if world > 1:
-        t = torch.tensor([e2e_s], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
+    e2e_s = shards.max_over_ranks(e2e_s)
 
     streams = None
     if args.streams_workload != "none":
@@ -356,7 +346,7 @@ def run_ours(args, rank, world, local_rank):
 
     if rank == 0:
         tokens = args.steps * world
-        value = tokens / (ms / 1000.0)
+        value = shards.aggregate_rate(args.steps, world, ms / 1000.0)
         bytes_total = algorithmic_bytes(model, first_position, args.steps)
         peak, peak_kind = measured_peak()
         achieved = bytes_total / (ms / 1000.0) / 1e9
@@ -372,7 +362,7 @@ def run_ours(args, rank, world, local_rank):
                          "traffic_unit": "bytes per step, from an ncu capture of decode_kernel at cfg2",
                          "bytes_per_step": bytes_total / args.steps,
                          "kernel": "decode_kernel (persistent, one launch per %d steps)" % args.chunk},
-            "e2e": {"value": tokens / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
+            "e2e": {"value": shards.aggregate_rate(args.steps, world, e2e_s), "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
                     "includes": "prompt upload + prefill of %d positions + %d decode steps via qwc_decode_step"
                                 % (len(prompt.tokens), args.steps)},
             "gpu_launches": launches,

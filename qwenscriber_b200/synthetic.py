@@ -131,13 +131,17 @@ def workloads() -> dict[str, Workload]:
     }
 
 
-def prefix_lengths(w: Workload) -> list[int]:
-    """Audio-prefix rows of every stream of a multi-stream workload (uniform in
-    the stated range, per-workload seed)."""
+def prefix_lengths(w: Workload, world: int = 1, rank: int = 0) -> list[int]:
+    """Audio-prefix rows of the streams one GPU decodes in a multi-stream
+    workload (uniform in the stated range, per-workload seed): rank `rank` of
+    `world` takes global streams [rank * streams, (rank + 1) * streams)."""
+    from . import shards
+
     if isinstance(w.audio_rows, int):
         return [w.audio_rows] * w.streams
     lo, hi = w.audio_rows
-    return [int(x) for x in np.random.default_rng([w.seed, 3]).integers(lo, hi + 1, size=w.streams)]
+    every = shards.prefix_lengths(lo, hi, w.seed, w.streams * world)
+    return [every[g] for g in shards.shard(w.streams * world, world, rank)]
 
 
 def load_into(model: Model, target, cache_format: int = 1, streams: int | None = None) -> None:
