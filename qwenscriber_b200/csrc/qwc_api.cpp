@@ -344,12 +344,12 @@ DevMat make_mat(const Tensor& t) {
   return m;
 }
 
-// The decode kernel's layout rules for one matrix: q4/q8, whole 512-byte
-// code spans per row (a warp reads 32 x 16 bytes per step), K within the
-// activation buffer, and one row per ring slot at least.
+// The decode kernel's layout rules for one matrix: q4/q5/q8, whole code spans
+// per row (a warp reads 32 x 16 bytes per step, or 16 q5 groups = 640 bytes),
+// K within the activation buffer, and one row per ring slot at least.
 int32_t kernel_fits(const DevMat& m) {
-  if (m.format != kFormatQ4 && m.format != kFormatQ8) return QWC_UNSUPPORTED_MODEL;
-  if (m.code_row % 512 != 0 || m.scale_row % 16 != 0) return QWC_UNSUPPORTED_MODEL;
+  if (m.format != kFormatQ4 && m.format != kFormatQ5 && m.format != kFormatQ8) return QWC_UNSUPPORTED_MODEL;
+  if (m.code_row % (m.format == kFormatQ5 ? 640u : 512u) != 0 || m.scale_row % 16 != 0) return QWC_UNSUPPORTED_MODEL;
   if (m.cols > 8192) return QWC_UNSUPPORTED_MODEL;
   if (m.scale_row + m.code_row > 28 * 1024) return QWC_UNSUPPORTED_MODEL;
   return QWC_OK;
@@ -425,6 +425,7 @@ int32_t finish_model(Handle* h, const Config& c) {
   if (c.text_key_value_heads % 4 != 0) return QWC_UNSUPPORTED_MODEL;
   const bool tied = (c.flags & 1u) != 0;
 
+  bool any_q5 = false;
   auto find = [&](uint32_t kind, uint32_t layer) -> const Tensor* {
     auto it = h->tensors.find({kind, layer});
     return it == h->tensors.end() ? nullptr : &it->second;
@@ -435,6 +436,7 @@ int32_t finish_model(Handle* h, const Config& c) {
     if (!t) return QWC_NOT_FOUND;
     if (is_vector_kind(kind) || t->rows != rows || t->cols != cols) return QWC_SHAPE_MISMATCH;
     *out = make_mat(*t);
+    if (out->format == kFormatQ5) any_q5 = true;
     return kernel_fits(*out);
   };
   auto need_vec = [&](uint32_t kind, uint32_t layer, uint32_t width, const float** out) -> int32_t {
@@ -553,8 +555,15 @@ int32_t finish_model(Handle* h, const Config& c) {
   h->slots.clear();
   h->slots.resize(h->streams);
   h->config = c;
-  // Every handle gets the batched engine: it runs the prompt prefills (64
-  // positions per step) and, with streams > 1, the batched decode steps.
+  // Every handle with q4/q8 weights gets the batched engine: it runs the
+  // prompt prefills (64 positions per step) and, with streams > 1, the batched
+  // decode steps. Its tensor-core GEMM reads q4 and q8 blocks only; a model
+  // with q5 matrices runs one stream through the persistent kernel, and its
+  // prompts prefill token by token there.
+  if (any_q5) {
+    if (h->streams > 1) return QWC_UNSUPPORTED_MODEL;
+    return QWC_OK;
+  }
   QWC_TRY(build_batched(h));
   return QWC_OK;
 }
@@ -1000,11 +1009,14 @@ int32_t stream_begin(Handle* h, uint32_t slot, const uint32_t* prompt, uint32_t 
     QWC_CUDA(cudaMemcpyAsync(s.audio->ptr, audio, s.audio->bytes, cudaMemcpyHostToDevice, h->stream));
     dev_audio = s.audio->as<float>();
   }
-  QWC_CUDA(cudaMemcpyAsync(h->batched->audio_ptrs.as<const float*>() + slot, &dev_audio, sizeof(dev_audio),
-                           cudaMemcpyHostToDevice, h->stream));
+  if (h->batched) {
+    QWC_CUDA(cudaMemcpyAsync(h->batched->audio_ptrs.as<const float*>() + slot, &dev_audio, sizeof(dev_audio),
+                             cudaMemcpyHostToDevice, h->stream));
+  }
   QWC_CUDA(cudaStreamSynchronize(h->stream));
   uint32_t next = 0, col = 0;
-  if (h->prefill_serial && h->streams == 1) {
+  const bool serial = (h->prefill_serial || !h->batched) && h->streams == 1;
+  if (serial) {
     // Token by token through the persistent kernel (decoder.zig:308-333 as written).
     QWC_CUDA(cudaMemcpyAsync(h->prompt_ids.ptr, prompt, size_t(prompt_len) * 4, cudaMemcpyHostToDevice, h->stream));
     QWC_CUDA(cudaMemcpyAsync(h->prompt_rows.ptr, rows.data(), size_t(prompt_len) * 4, cudaMemcpyHostToDevice,
@@ -1024,7 +1036,7 @@ int32_t stream_begin(Handle* h, uint32_t slot, const uint32_t* prompt, uint32_t 
   s.next_token = next;
   s.max_tokens = max_tokens;
   s.generated.reserve(max_tokens);
-  s.logits_batched = !(h->prefill_serial && h->streams == 1);
+  s.logits_batched = !serial;
   s.logits_col = col;
   return QWC_OK;
 }
@@ -1185,7 +1197,7 @@ int32_t qwc_model_add_tensor(uint32_t handle, uint32_t kind, uint32_t layer, uin
   uint64_t need = 0;
   if (format == QWC_FORMAT_F32) {
     need = uint64_t(rows) * cols * 4;
-  } else if (format == QWC_FORMAT_Q4 || format == QWC_FORMAT_Q8) {
+  } else if (format == QWC_FORMAT_Q4 || format == QWC_FORMAT_Q5 || format == QWC_FORMAT_Q8) {
     if (cols % kGroup != 0) return QWC_SHAPE_MISMATCH;  // RowNotGroupAligned (quant.zig:77-81)
     // quant.zig:144-176 with a 16-byte-aligned base.
     const uint64_t groups = uint64_t(rows) * (cols / kGroup);
@@ -1230,7 +1242,8 @@ int32_t qwc_model_add_shard(uint32_t handle, const void* bytes, uint64_t len) {
     const ShardEntry e = shard_entry(v, i);
     if (!decoder_kind(e.kind)) continue;
     const bool vec = e.rank == 1 && e.format == QWC_FORMAT_F32;
-    const bool mat = e.rank == 2 && (e.format == QWC_FORMAT_Q4 || e.format == QWC_FORMAT_Q8 || e.format == QWC_FORMAT_F32);
+    const bool mat = e.rank == 2 && (e.format == QWC_FORMAT_Q4 || e.format == QWC_FORMAT_Q5 ||
+                                     e.format == QWC_FORMAT_Q8 || e.format == QWC_FORMAT_F32);
     if (!vec && !mat) return QWC_UNSUPPORTED_MODEL;
     if (h->tensors.count({e.kind, e.layer})) return QWC_INVALID_ARGUMENT;  // DuplicateTensor
   }
@@ -1360,7 +1373,7 @@ int32_t qwc_stream_end(uint32_t handle, uint32_t slot) {
   const uint64_t stride = h->host_model.cache_stream_stride;
   QWC_CUDA(cudaMemsetAsync(h->k_cache.as<uint8_t>() + stride * slot, 0, stride, h->stream));
   QWC_CUDA(cudaMemsetAsync(h->v_cache.as<uint8_t>() + stride * slot, 0, stride, h->stream));
-  {
+  if (h->batched) {
     const float* none = nullptr;
     QWC_CUDA(cudaMemcpyAsync(h->batched->audio_ptrs.as<const float*>() + slot, &none, sizeof(none),
                              cudaMemcpyHostToDevice, h->stream));

@@ -614,6 +614,10 @@ __device__ void input_into_x(Ctx& c, uint32_t token, int32_t audio_row, Span own
           const uint32_t b = __ldg(reinterpret_cast<const uint16_t*>(crow + k / 2));
 #pragma unroll
           for (int t = 0; t < 4; ++t) v[t] = static_cast<float>(static_cast<int>((b >> (4 * t)) & 0xFu) - 8) * scale;
+        } else if (e.format == kFormatQ5) {
+          const uint8_t* grp = crow + (k / kGroup) * 40u;
+#pragma unroll
+          for (int t = 0; t < 4; ++t) v[t] = static_cast<float>(q5_code(grp, (k + t) % kGroup)) * scale;
         } else {
           const uint32_t b = __ldg(reinterpret_cast<const uint32_t*>(crow + k));
 #pragma unroll
@@ -646,6 +650,19 @@ struct Fmt<kFormatQ8> {
   static constexpr uint32_t kDB = 64;
   static constexpr uint32_t kKPerByte = 1;
 };
+template <>
+struct Fmt<kFormatQ5> {  // its chunks are 16 groups (640 bytes); a lane takes half a group
+  static constexpr int kPairs = 16;
+  static constexpr uint32_t kDB = 40;
+  static constexpr uint32_t kKPerByte = 0;
+};
+
+// Code bytes a warp covers per chunk step: 32 lanes x 16 bytes, or for q5
+// 16 whole groups (a lane's 32 weights: 16 bytes of nibbles + 4 of fifth bits).
+template <uint32_t FMT>
+__host__ __device__ constexpr uint32_t chunk_bytes() {
+  return FMT == kFormatQ5 ? 16u * 40u : 512u;
+}
 
 struct Best {
   float v;
@@ -664,7 +681,7 @@ __device__ void gemv_tiles(Ctx& c, const Piece* pieces, int np, bool lm, Best& b
   for (int p = 0; p < np; ++p) {
     const Piece pc = pieces[p];
     const uint32_t per = rows_per_tile(pc);
-    const uint32_t chunks = pc.code_row / 512u;
+    const uint32_t chunks = pc.code_row / chunk_bytes<FMT>();
     // Rows of at most two chunks are taken whole by one pass, and their sums
     // go straight to their rows; longer rows are split into one-chunk passes
     // whose sums are added after the tile.
@@ -681,6 +698,32 @@ __device__ void gemv_tiles(Ctx& c, const Piece* pieces, int np, bool lm, Best& b
           const uint32_t r0 = (whole ? ps : ps / chunks) * kRowsPerPass, j0 = whole ? 0u : ps % chunks;
           float acc[kRowsPerPass] = {0.0f, 0.0f, 0.0f, 0.0f};
           for (uint32_t j = j0; j < j0 + span; ++j) {
+            if constexpr (FMT == kFormatQ5) {
+              // Lane l: half (l & 1) of group 16 j + l / 2; activations unscaled.
+              const uint32_t g = 16u * j + (static_cast<uint32_t>(c.lane) >> 1);
+              const uint32_t h = static_cast<uint32_t>(c.lane) & 1u;
+              float xs[32];
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const float4 v = *reinterpret_cast<const float4*>(&c.s->x[x_index(64u * g + 32u * h + 4 * q)]);
+                xs[4 * q] = v.x;
+                xs[4 * q + 1] = v.y;
+                xs[4 * q + 2] = v.z;
+                xs[4 * q + 3] = v.w;
+              }
+#pragma unroll
+              for (int q = 0; q < kRowsPerPass; ++q) {
+                const uint32_t row = min(r0 + q, nr - 1);
+                const uint8_t* grp = codes + row * pc.code_row + 40u * g;
+                const uint2 l0 = *reinterpret_cast<const uint2*>(grp + 16u * h);
+                const uint2 l1 = *reinterpret_cast<const uint2*>(grp + 16u * h + 8u);
+                const uint32_t fifth = *reinterpret_cast<const uint32_t*>(grp + 32u + 4u * h);
+                const float scale =
+                    f16_bits_to_f32_fast(*reinterpret_cast<const uint16_t*>(base + row * pc.scale_row + g * 2));
+                acc[q] = fmaf(q5_half_dot(l0.x, l0.y, l1.x, l1.y, fifth, xs), scale, acc[q]);
+              }
+              continue;
+            }
             const uint32_t off = 16u * c.lane + 512u * j;
             const uint32_t kbase = off * Fmt<FMT>::kKPerByte;
             uint64_t x2[Fmt<FMT>::kPairs];
@@ -743,9 +786,12 @@ __device__ void gemv_tiles(Ctx& c, const Piece* pieces, int np, bool lm, Best& b
 }
 
 // Runs one GEMV stage over the CTA's pieces.
-__device__ void gemv_stage(Ctx& c, const Piece* pieces, int np, bool q4, bool lm, Best& best, float* logits_out) {
-  if (q4) {
+__device__ void gemv_stage(Ctx& c, const Piece* pieces, int np, uint32_t format, bool lm, Best& best,
+                           float* logits_out) {
+  if (format == kFormatQ4) {
     gemv_tiles<kFormatQ4>(c, pieces, np, lm, best, logits_out);
+  } else if (format == kFormatQ5) {
+    gemv_tiles<kFormatQ5>(c, pieces, np, lm, best, logits_out);
   } else {
     gemv_tiles<kFormatQ8>(c, pieces, np, lm, best, logits_out);
   }
@@ -1010,7 +1056,8 @@ __device__ void run_consumers(const DecodeLaunch& P, Smem* s) {
         attention_stage(c, l, position);
       } else {
         const uint32_t lq = st == kStLM ? 0 : l;
-        const bool q4 = stage_format(m, lq, st) == kFormatQ4;
+        const uint32_t format = stage_format(m, lq, st);
+        const bool q4 = format == kFormatQ4;  // q4 stages keep x prescaled (store_x4)
         // -- stage input into x: the layer-0 input row, an RMSNorm of the
         // residual stream (decoder.zig:165-176, 259-262, 277-283), or the
         // attention output / SwiGLU activations; up reuses gate's input.
@@ -1028,7 +1075,7 @@ __device__ void run_consumers(const DecodeLaunch& P, Smem* s) {
         const int np = stage_pieces(m, lq, st, blockIdx.x, gridDim.x, pieces);
         Best best{-INFINITY, 0xFFFFFFFFu};
         float* logits_out = (st == kStLM && P.logits_out && t + 1 == P.n_tokens) ? P.logits_out : nullptr;
-        gemv_stage(c, pieces, np, q4, st == kStLM, best, logits_out);
+        gemv_stage(c, pieces, np, format, st == kStLM, best, logits_out);
         // -- stage output
         if (st == kStQKV) {
           for (int p = 0; p < np; ++p) {

@@ -150,6 +150,41 @@ __device__ __forceinline__ float q4_chunk_xsum(const uint64_t* x2) {
   return (fa.x + fa.y) + (fb.x + fb.y);
 }
 
+// q5 (quant.zig:253-269, 327-335): a group's 32 bytes of low nibbles (the q4
+// layout: weight 2i in the low nibble of byte i, 2i + 1 in the high one), then
+// 8 bytes of fifth bits (bit i % 8 of byte i / 8 for weight i); the code is
+// low | fifth << 4, bias 16. One half group, 32 weights: the low nibbles in
+// four words (weight 8 w + p at nibble p of word w), the fifth bits in one word
+// (bit i for weight i). (2^23 + u) - (2^23 + 16) = u - 16 is exact in f32.
+constexpr float kNegQ5 = -8388624.0f;  // -(2^23 + 16)
+__device__ __forceinline__ float q5_half_dot(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3, uint32_t fifth,
+                                             const float* x) {
+  const uint32_t lo[4] = {w0, w1, w2, w3};
+  float a = 0.0f, b = 0.0f;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+#pragma unroll
+    for (int p = 0; p < 8; ++p) {
+      const int i = 8 * w + p;
+      const uint32_t u = ((lo[w] >> (4 * p)) & 0xFu) | (((fifth >> i) & 1u) << 4);
+      const float v = bits_f32(kMagic | u) + kNegQ5;
+      if (p & 1) {
+        b = fmaf(v, x[i], b);
+      } else {
+        a = fmaf(v, x[i], a);
+      }
+    }
+  }
+  return a + b;
+}
+
+// Code of weight i (0..63) of one q5 group starting at `g`.
+__device__ __forceinline__ int q5_code(const uint8_t* g, uint32_t i) {
+  const uint32_t lo = (i & 1u) ? (g[i / 2] >> 4) : (g[i / 2] & 0x0Fu);
+  const uint32_t hi = (g[32 + i / 8] >> (i % 8)) & 1u;
+  return static_cast<int>(lo | (hi << 4)) - 16;
+}
+
 __device__ __forceinline__ void q8_word(uint32_t w, const uint64_t* x2, uint64_t& acc) {
   const uint64_t v01 = pack2(bits_f32(__byte_perm(w, kMagic, 0x7440)), bits_f32(__byte_perm(w, kMagic, 0x7441)));
   const uint64_t v23 = pack2(bits_f32(__byte_perm(w, kMagic, 0x7442)), bits_f32(__byte_perm(w, kMagic, 0x7443)));

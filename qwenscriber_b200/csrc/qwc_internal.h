@@ -6,11 +6,18 @@
 #include <cstddef>
 #include <cstdint>
 
+#ifdef __CUDACC__
+#define QWC_HOST_DEVICE __host__ __device__
+#else
+#define QWC_HOST_DEVICE
+#endif
+
 namespace qwc {
 
 constexpr uint32_t kGroup = 64;           // src/core/quant.zig:49
 constexpr uint32_t kFormatF32 = 0;
 constexpr uint32_t kFormatQ4 = 16;
+constexpr uint32_t kFormatQ5 = 17;
 constexpr uint32_t kFormatQ8 = 18;
 constexpr uint32_t kMaxLayers = 64;
 constexpr uint32_t kPositionLimit = 8192;  // src/core/qwen3_asr/model.zig:62
@@ -21,8 +28,10 @@ constexpr uint32_t kHeadDim = 128;         // the kernels are written for head_d
 // sum, two pad words (16-byte aligned rows for float4 loads).
 constexpr uint32_t kAttnPartStride = kHeadDim + 4;
 
-inline uint32_t data_bytes_per_group(uint32_t format) {
-  return format == kFormatQ4 ? 32u : (format == kFormatQ8 ? 64u : 0u);
+// Code bytes per 64-value group (quant.zig:47-59): q4 32, q5 40 (32 bytes of
+// low nibbles, then an 8-byte plane of fifth bits), q8 64.
+QWC_HOST_DEVICE inline uint32_t data_bytes_per_group(uint32_t format) {
+  return format == kFormatQ4 ? 32u : format == kFormatQ5 ? 40u : (format == kFormatQ8 ? 64u : 0u);
 }
 
 // One quantized matrix in HBM, in the reference's two-plane layout

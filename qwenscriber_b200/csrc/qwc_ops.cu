@@ -31,6 +31,8 @@ __global__ void dequantize_kernel(uint32_t format, const uint8_t* scales, const 
     if (format == kFormatQ4) {
       const uint8_t b = codes[r * groups * 32 + k / 2];
       code = static_cast<int>((k & 1u) ? (b >> 4) : (b & 0x0F)) - 8;
+    } else if (format == kFormatQ5) {
+      code = q5_code(codes + (r * groups + g) * 40, k % kGroup);
     } else {
       code = static_cast<int>(codes[r * groups * 64 + k]) - 128;
     }
@@ -57,18 +59,33 @@ __global__ void quantize_q8_kernel(const float* values, uint32_t rows, uint32_t 
   }
 }
 
-// One warp per row; lane l takes the 16-byte chunks at l*16 + 512*j of the row.
+// One warp per row; lane l takes the 16-byte chunks at l*16 + 512*j of the row
+// (q5: half l & 1 of group l / 2 + 16 j).
 __global__ void gemv_kernel(uint32_t format, const uint8_t* scales, const uint8_t* codes, uint32_t rows, uint32_t cols,
                             const float* x, float* out) {
   const uint32_t lane = threadIdx.x & 31;
   const uint32_t warps = blockDim.x / 32;
   const uint32_t groups = cols / kGroup;
-  const uint32_t db = format == kFormatQ4 ? 32u : 64u;
+  const uint32_t db = data_bytes_per_group(format);
   const uint32_t code_row = groups * db;
   for (uint32_t r = blockIdx.x * warps + threadIdx.x / 32; r < rows; r += gridDim.x * warps) {
     const uint8_t* crow = codes + size_t(r) * code_row;
     const uint16_t* srow = reinterpret_cast<const uint16_t*>(scales) + size_t(r) * groups;
     float acc = 0.0f;
+    if (format == kFormatQ5) {
+      for (uint32_t g = lane / 2; g < groups; g += 16) {
+        const uint32_t h = lane & 1u;
+        const uint8_t* grp = crow + size_t(g) * 40;
+        const uint2 l0 = *reinterpret_cast<const uint2*>(grp + 16u * h);
+        const uint2 l1 = *reinterpret_cast<const uint2*>(grp + 16u * h + 8u);
+        const uint32_t fifth = *reinterpret_cast<const uint32_t*>(grp + 32u + 4u * h);
+        const float d = q5_half_dot(l0.x, l0.y, l1.x, l1.y, fifth, x + 64u * g + 32u * h);
+        acc = fmaf(d, f16_bits_to_f32(srow[g]), acc);
+      }
+      acc = warp_sum(acc);
+      if (lane == 0) out[r] = acc;
+      continue;
+    }
     for (uint32_t off = 16u * lane; off < code_row; off += 512u) {
       const uint4 w = ld_nc4(crow + off);
       const float scale = f16_bits_to_f32(srow[off / db]);
@@ -275,7 +292,7 @@ int32_t status_of(cudaError_t e) {
   return QWC_INVALID_STATE;
 }
 
-bool quant_format_ok(uint32_t format) { return format == kFormatQ4 || format == kFormatQ8; }
+bool quant_format_ok(uint32_t format) { return format == kFormatQ4 || format == kFormatQ5 || format == kFormatQ8; }
 
 // ---- argmax over a fixed, statically allocated device scratch ----
 //
@@ -343,9 +360,10 @@ int32_t qwc_op_gemv(uint32_t format, const void* scales, const void* codes, uint
                     const float* x, float* out, void* stream) {
   if (!quant_format_ok(format)) return QWC_UNSUPPORTED;
   if (!scales || !codes || !x || !out) return QWC_INVALID_ARGUMENT;
-  // The chunk walk needs whole 512-byte spans of codes per row.
+  // The chunk walk needs whole 512-byte spans of codes per row (q5: whole
+  // groups, 8-byte aligned rows).
   const uint32_t code_row = cols / kGroup * data_bytes_per_group(format);
-  if (cols % kGroup != 0 || code_row % 512 != 0) return QWC_SHAPE_MISMATCH;
+  if (cols % kGroup != 0 || code_row % (format == kFormatQ5 ? 8u : 512u) != 0) return QWC_SHAPE_MISMATCH;
   if (rows == 0) return QWC_OK;
   const uint32_t blocks = (rows + 7) / 8;
   gemv_kernel<<<blocks < 4096 ? blocks : 4096, 256, 0, static_cast<cudaStream_t>(stream)>>>(

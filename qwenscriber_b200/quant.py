@@ -36,8 +36,8 @@ def plane_layout(fmt: int, rows: int, cols: int) -> tuple[int, int, int, int]:
 
 def quantize(fmt: int, values: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
     """quantizeRow over every row: returns (scales u16[rows, groups], codes u8[rows, groups*bytes])."""
-    if fmt not in (Q4, Q8):
-        raise ValueError("q4 and q8 are the formats this backend runs")
+    if fmt not in (Q4, Q5, Q8):
+        raise ValueError("q4, q5 and q8 are the formats this backend runs")
     v = np.ascontiguousarray(values, dtype=np.float32)
     rows, cols = v.shape
     g = v.reshape(rows, cols // GROUP, GROUP)
@@ -54,7 +54,33 @@ def quantize(fmt: int, values: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
     codes = codes.astype(np.uint8).reshape(rows, cols)
     if fmt == Q4:
         codes = (codes[:, 0::2] | (codes[:, 1::2] << 4)).astype(np.uint8)
+    elif fmt == Q5:
+        codes = pack_q5(codes)
     return scale16.view(np.uint16), codes
+
+
+def pack_q5(u: np.ndarray) -> np.ndarray:
+    """q5 codes u8[rows, cols] (0..31) -> the group layout of quant.zig:253-269:
+    per 64-value group, 32 bytes of low nibbles (weight 2i low, 2i + 1 high in
+    byte i), then 8 bytes of fifth bits (weight i at bit i % 8 of byte i / 8)."""
+    rows, cols = u.shape
+    g = u.reshape(rows, cols // GROUP, GROUP)
+    nib = g & 0x0F
+    low = (nib[:, :, 0::2] | (nib[:, :, 1::2] << 4)).astype(np.uint8)
+    bits = ((g >> 4) & 1).astype(np.uint8).reshape(rows, cols // GROUP, 8, 8)
+    plane = np.packbits(bits, axis=-1, bitorder="little").reshape(rows, cols // GROUP, 8)
+    return np.concatenate([low, plane], axis=2).reshape(rows, cols // GROUP * 40)
+
+
+def unpack_q5(codes: np.ndarray, cols: int) -> np.ndarray:
+    """The inverse of pack_q5: unsigned codes int32[rows, cols]."""
+    rows = codes.shape[0]
+    g = np.asarray(codes, dtype=np.uint8).reshape(rows, cols // GROUP, 40)
+    u = np.empty((rows, cols // GROUP, GROUP), np.int32)
+    u[:, :, 0::2] = g[:, :, :32] & 0x0F
+    u[:, :, 1::2] = g[:, :, :32] >> 4
+    bits = np.unpackbits(g[:, :, 32:], axis=-1, bitorder="little").astype(np.int32)
+    return (u | (bits << 4)).reshape(rows, cols)
 
 
 def dequantize(fmt: int, scales: np.ndarray, codes: np.ndarray, cols: int) -> np.ndarray:
@@ -66,6 +92,8 @@ def dequantize(fmt: int, scales: np.ndarray, codes: np.ndarray, cols: int) -> np
         u = np.empty((rows, cols), np.int32)
         u[:, 0::2] = c & 0x0F
         u[:, 1::2] = c >> 4
+    elif fmt == Q5:
+        u = unpack_q5(c, cols)
     else:
         u = c.astype(np.int32)
     vals = (u - BIAS[fmt]).astype(np.float32).reshape(rows, cols // GROUP, GROUP)

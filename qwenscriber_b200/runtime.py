@@ -31,6 +31,7 @@ CACHE_F32, CACHE_Q8 = 0, 1
 OPTION_IGNORE_EOS, OPTION_KEEP_LOGITS, OPTION_STEP_CHUNK, OPTION_TRACE, OPTION_PREFILL_SERIAL = 1, 2, 3, 4, 5
 FEATURE_MODEL, FEATURE_DECODE, FEATURE_STREAMS = 1 << 3, 1 << 4, 1 << 8
 LIMIT_EXCEEDED = -9
+UNSUPPORTED_MODEL = -13
 ARGMAX_NOALLOC_MAX_COUNT = 4194304  # QWC_ARGMAX_NOALLOC_MAX_COUNT
 
 # Every symbol include/qwenscriber_cuda.h declares: (restype, argtypes).

@@ -4,8 +4,8 @@ No checkpoint or dataset is available, so every input is drawn with numpy's
 PCG64 (`default_rng`), in the shapes and value distributions the benchmark
 configurations state:
 
-  * q8 models: f32 weights N(0, 0.02), quantized with the reference's q8
-    blocks (quant.zig:197-288 via `quant.quantize`);
+  * q8 (and q5) models: f32 weights N(0, 0.02), quantized with the
+    reference's q8 (q5) blocks (quant.zig:197-288 via `quant.quantize`);
   * q4 "direct" models: int4 codes uniform in [-8, 7] (bytes uniform in
     [0, 255], i.e. two uniform nibbles) and f16 group scales |N(0, 0.003)|;
   * RMSNorm weights 1.0 f32; the lm_head tied to the embedding;
@@ -54,9 +54,9 @@ class Model:
 
 
 def _matrix(rng: np.random.Generator, fmt: int, rows: int, cols: int, std: float, q4_scale_std: float) -> np.ndarray:
-    if fmt == quant.Q8:
+    if fmt in (quant.Q8, quant.Q5):
         w = rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(std)
-        scales, codes = quant.quantize(quant.Q8, w)
+        scales, codes = quant.quantize(fmt, w)
     else:
         codes = rng.integers(0, 256, size=(rows, cols // 2), dtype=np.uint8)
         s = np.abs(rng.standard_normal((rows, cols // quant.GROUP), dtype=np.float32) * np.float32(q4_scale_std))

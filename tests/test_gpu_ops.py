@@ -35,7 +35,7 @@ def _random_planes(rng, fmt, rows, cols):
     return scales, codes
 
 
-@pytest.mark.parametrize("fmt", [quant.Q4, quant.Q8])
+@pytest.mark.parametrize("fmt", [quant.Q4, quant.Q5, quant.Q8])
 def test_dequantize_is_bit_exact(gpu, cuda_lib, oracle_lib, fmt):
     import torch
 
@@ -71,7 +71,8 @@ def test_quantize_q8_is_bit_exact(gpu, cuda_lib, oracle_lib):
 
 
 @pytest.mark.parametrize("fmt,cols", [(quant.Q4, 1024), (quant.Q4, 2048), (quant.Q4, 3072), (quant.Q4, 6144),
-                                      (quant.Q8, 1024), (quant.Q8, 3072)])
+                                      (quant.Q8, 1024), (quant.Q8, 3072),
+                                      (quant.Q5, 128), (quant.Q5, 1024), (quant.Q5, 2048), (quant.Q5, 6144)])
 def test_gemv_matches_linear_quantized(gpu, cuda_lib, oracle_lib, fmt, cols):
     import torch
 

@@ -32,7 +32,7 @@ def _decode(gm, prompt, steps):
     return tokens, logits
 
 
-@pytest.mark.parametrize("fmt", [quant.Q8, quant.Q4])
+@pytest.mark.parametrize("fmt", [quant.Q8, quant.Q4, quant.Q5])
 def test_shards_load_the_same_model_as_tensors(gpu, cuda_lib, fmt):
     config = small_config(fmt, layers=3)
     model = synthetic.make_model(config, fmt, seed=17)
@@ -78,10 +78,10 @@ def test_shard_refusals(gpu, cuda_lib):
         with pytest.raises(rt.QwcError) as e:
             gm.add_shard(shard.build([shard.tensor_entry(t)]))
         assert e.value.status == CODE["invalid_argument"]
-        # A decoder matrix in q5 (valid container, no kernel for it).
-        q5 = shard.build([(synthetic.Q, 9, quant.Q5, (64, 64), bytes(128 + 64 * 40))])
+        # A decoder matrix in f16 (valid container, no kernel for it).
+        f16 = shard.build([(synthetic.Q, 9, 1, (64, 64), bytes(64 * 64 * 2))])
         with pytest.raises(rt.QwcError) as e:
-            gm.add_shard(q5)
+            gm.add_shard(f16)
         assert e.value.status == CODE["unsupported_model"]
         gm.add_shard(parts[1])
         gm.set_cache_format(rt.CACHE_Q8)

@@ -25,7 +25,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 HEADER = os.path.join(ROOT, "include", "qwenscriber_cuda.h")
 
 
-@pytest.mark.parametrize("fmt", [quant.Q4, quant.Q8])
+@pytest.mark.parametrize("fmt", [quant.Q4, quant.Q5, quant.Q8])
 def test_numpy_quantizer_is_bit_exact(oracle_lib, fmt):
     rng = np.random.default_rng(11)
     v = (rng.standard_normal((64, 512)) * rng.choice([1e-3, 0.02, 1.0, 40.0], size=(64, 1))).astype(np.float32)
@@ -123,7 +123,9 @@ def test_header_constants_match_reference():
     # quant constants used by the kernels (quant.zig:49-59)
     internal = open(os.path.join(ROOT, "qwenscriber_b200", "csrc", "qwc_internal.h")).read()
     assert re.search(r"kGroup = 64;", internal)
-    assert "return format == kFormatQ4 ? 32u : (format == kFormatQ8 ? 64u : 0u);" in internal
+    assert ("return format == kFormatQ4 ? 32u : format == kFormatQ5 ? 40u : (format == kFormatQ8 ? 64u : 0u);"
+            in internal)
+    assert re.search(r"kFormatQ5 = 17;", internal)
 
 
 def test_qwc_create_without_device_returns_zero(cuda_lib):
