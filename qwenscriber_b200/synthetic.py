@@ -128,6 +128,10 @@ def workloads() -> dict[str, Workload]:
         "cfg4_1p7b_q4_s64_long": Workload("cfg4_1p7b_q4_s64_long",
                                           qwen3_asr_1p7b(max_positions=4096, max_decode_tokens=1024),
                                           quant.Q4, 1, (2048, 3584), 16, 512, 64),
+        # Not a benchmark configuration: configs[0]'s model and prompt with q5
+        # weights (the format the reference ships to browsers), for the q5 path.
+        "q5_0p6b_b1": Workload("q5_0p6b_b1", qwen3_asr_0p6b(max_positions=512, max_decode_tokens=512),
+                               quant.Q5, 0, 188, 8, 64, 1),
     }
 
 
