@@ -249,13 +249,16 @@ int32_t qwc_rope_tables(float theta, uint32_t head_dim, uint32_t max_positions, 
  * of the token loop on its own buffers and so parity tests can check each
  * against the reference arithmetic. All pointers are device pointers. */
 
-/* quant.dequantizeRow (src/core/quant.zig:348-364) over `rows` rows: bit exact. */
+/* quant.dequantizeRow (src/core/quant.zig:348-364) over `rows` rows: bit exact.
+ * Formats q4, q5, q8; `scales` 2-byte aligned (else QWC_INVALID_ARGUMENT). */
 int32_t qwc_op_dequantize(uint32_t format, const void* scales, const void* codes, uint32_t rows, uint32_t cols,
                           float* out, void* stream);
 /* quant.quantizeRow(.q8) (src/core/quant.zig:197-288) over `rows` rows: bit exact. */
 int32_t qwc_op_quantize_q8(const float* values, uint32_t rows, uint32_t cols, void* scales, void* codes,
                            void* stream);
-/* kernels.linearQuantized with one token (src/core/qwen3_asr/kernels.zig:118-158): out[rows]. */
+/* kernels.linearQuantized with one token (src/core/qwen3_asr/kernels.zig:118-158): out[rows].
+ * Formats q4, q5, q8. Alignment (else QWC_INVALID_ARGUMENT, before any launch): `codes` and `x`
+ * 16-byte aligned for q4/q8, `codes` 8-byte and `x` 4-byte aligned for q5, `scales` 2-byte. */
 int32_t qwc_op_gemv(uint32_t format, const void* scales, const void* codes, uint32_t rows, uint32_t cols,
                     const float* x, float* out, void* stream);
 /* kernels.decodeAttentionStepQ8 (src/core/qwen3_asr/kernels.zig:697-767) over

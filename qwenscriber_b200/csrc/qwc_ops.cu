@@ -292,6 +292,8 @@ int32_t status_of(cudaError_t e) {
   return QWC_INVALID_STATE;
 }
 
+bool aligned(const void* p, uintptr_t a) { return reinterpret_cast<uintptr_t>(p) % a == 0; }
+
 bool quant_format_ok(uint32_t format) { return format == kFormatQ4 || format == kFormatQ5 || format == kFormatQ8; }
 
 // ---- argmax over a fixed, statically allocated device scratch ----
@@ -341,6 +343,7 @@ int32_t qwc_op_dequantize(uint32_t format, const void* scales, const void* codes
                           float* out, void* stream) {
   if (!quant_format_ok(format)) return QWC_UNSUPPORTED;
   if (!scales || !codes || !out || cols % kGroup != 0) return QWC_INVALID_ARGUMENT;
+  if (!aligned(scales, 2) || !aligned(out, 4)) return QWC_INVALID_ARGUMENT;
   if (rows == 0) return QWC_OK;
   dequantize_kernel<<<592, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       format, static_cast<const uint8_t*>(scales), static_cast<const uint8_t*>(codes), rows, cols, out);
@@ -360,6 +363,13 @@ int32_t qwc_op_gemv(uint32_t format, const void* scales, const void* codes, uint
                     const float* x, float* out, void* stream) {
   if (!quant_format_ok(format)) return QWC_UNSUPPORTED;
   if (!scales || !codes || !x || !out) return QWC_INVALID_ARGUMENT;
+  // The kernel reads codes and activations with vector loads (16-byte for
+  // q4/q8; 8-byte codes and scalar activations for q5): refuse pointers they
+  // would fault on.
+  const bool q5 = format == kFormatQ5;
+  if (!aligned(codes, q5 ? 8 : 16) || !aligned(x, q5 ? 4 : 16) || !aligned(scales, 2) || !aligned(out, 4)) {
+    return QWC_INVALID_ARGUMENT;
+  }
   // The chunk walk needs whole 512-byte spans of codes per row (q5: whole
   // groups, 8-byte aligned rows).
   const uint32_t code_row = cols / kGroup * data_bytes_per_group(format);

@@ -27,6 +27,8 @@ STATUS = {
     -11: "truncated", -12: "invalid_encoding", -13: "unsupported_model", -14: "audio_too_long",
 }
 
+STATUS_CODE = {name: code for code, name in STATUS.items()}
+
 CACHE_F32, CACHE_Q8 = 0, 1
 OPTION_IGNORE_EOS, OPTION_KEEP_LOGITS, OPTION_STEP_CHUNK, OPTION_TRACE, OPTION_PREFILL_SERIAL = 1, 2, 3, 4, 5
 FEATURE_MODEL, FEATURE_DECODE, FEATURE_STREAMS = 1 << 3, 1 << 4, 1 << 8

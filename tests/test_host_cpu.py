@@ -95,6 +95,24 @@ def test_host_only_calls(cuda_lib):
     assert cuda_lib.qwc_status_message(-99) == b"unknown status"
 
 
+def test_operators_refuse_misaligned_pointers(cuda_lib):
+    # The checks run before any CUDA call, so fake device addresses are safe
+    # here: a pointer the GEMV's vector loads would fault on is refused.
+    A = 1 << 20  # an address aligned to everything the operators ask for
+    out = A + 4096
+    gemv = cuda_lib.qwc_op_gemv
+    bad = rt.STATUS_CODE["invalid_argument"]
+    for fmt in (quant.Q4, quant.Q8):
+        assert gemv(fmt, A, A + 8, 4, 1024, A, out, None) == bad      # codes 8-byte aligned only
+        assert gemv(fmt, A, A, 4, 1024, A + 4, out, None) == bad      # x 4-byte aligned only
+        assert gemv(fmt, A + 1, A, 4, 1024, A, out, None) == bad      # scales odd
+    assert gemv(quant.Q5, A, A + 4, 4, 1024, A, out, None) == bad     # q5 codes need 8 bytes
+    assert gemv(quant.Q5, A, A, 4, 1024, A + 2, out, None) == bad     # q5 x needs 4 bytes
+    assert cuda_lib.qwc_op_dequantize(quant.Q4, A + 1, A, 4, 1024, out, None) == bad
+    assert gemv(quant.Q4, A, A, 4, 100, A, out, None) == rt.STATUS_CODE["shape_mismatch"]  # cols not whole groups
+    assert gemv(7, A, A, 4, 1024, A, out, None) == rt.STATUS_CODE["unsupported"]
+
+
 def test_rope_tables_match_oracle_bit_for_bit(cuda_lib, oracle_lib):
     # kernels.zig:534-564: the tables the CUDA backend uploads equal the oracle's.
     cos_p, sin_p = rt.rope_tables(1000000.0, 128, 4096)
