@@ -699,18 +699,26 @@ __device__ void gemv_tiles(Ctx& c, const Piece* pieces, int np, bool lm, Best& b
           float acc[kRowsPerPass] = {0.0f, 0.0f, 0.0f, 0.0f};
           for (uint32_t j = j0; j < j0 + span; ++j) {
             if constexpr (FMT == kFormatQ5) {
-              // Lane l: half (l & 1) of group 16 j + l / 2; activations unscaled.
+              // Lane l: half (l & 1) of group 16 j + l / 2. The activations
+              // are stored as for q4 (prescaled), so the low nibbles go through
+              // q4_chunk_dot_sub; each set fifth bit adds its activation, and
+              // sum((u - 16) x) = sum(nib x) + 16 sum(bit x) - 16 sum(x).
               const uint32_t g = 16u * j + (static_cast<uint32_t>(c.lane) >> 1);
               const uint32_t h = static_cast<uint32_t>(c.lane) & 1u;
-              float xs[32];
+              uint64_t x2[16];
+              float xp[32];  // the activations themselves, for the fifth bits
 #pragma unroll
               for (int q = 0; q < 8; ++q) {
                 const float4 v = *reinterpret_cast<const float4*>(&c.s->x[x_index(64u * g + 32u * h + 4 * q)]);
-                xs[4 * q] = v.x;
-                xs[4 * q + 1] = v.y;
-                xs[4 * q + 2] = v.z;
-                xs[4 * q + 3] = v.w;
+                x2[2 * q] = pack2(v.x, v.y);
+                x2[2 * q + 1] = pack2(v.z, v.w);
+                const int p0 = (4 * q) % 8;  // nibble position of v.x
+                xp[4 * q] = v.x * q4_unscale(p0);
+                xp[4 * q + 1] = v.y * q4_unscale(p0 + 1);
+                xp[4 * q + 2] = v.z * q4_unscale(p0 + 2);
+                xp[4 * q + 3] = v.w * q4_unscale(p0 + 3);
               }
+              const float xbias = 16.0f * q4_chunk_xsum(x2);
 #pragma unroll
               for (int q = 0; q < kRowsPerPass; ++q) {
                 const uint32_t row = min(r0 + q, nr - 1);
@@ -720,7 +728,15 @@ __device__ void gemv_tiles(Ctx& c, const Piece* pieces, int np, bool lm, Best& b
                 const uint32_t fifth = *reinterpret_cast<const uint32_t*>(grp + 32u + 4u * h);
                 const float scale =
                     f16_bits_to_f32_fast(*reinterpret_cast<const uint16_t*>(base + row * pc.scale_row + g * 2));
-                acc[q] = fmaf(q5_half_dot(l0.x, l0.y, l1.x, l1.y, fifth, xs), scale, acc[q]);
+                float b0 = 0.0f, b1 = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 32; i += 2) {
+                  if (fifth & (1u << i)) b0 += xp[i];
+                  if (fifth & (2u << i)) b1 += xp[i + 1];
+                }
+                const float nib = q4_chunk_dot_sub(make_uint4(l0.x, l0.y, l1.x, l1.y), x2);
+                const float d = fmaf(nib, kQ4SubUnscale, fmaf(16.0f, b0 + b1, -xbias));
+                acc[q] = fmaf(d, scale, acc[q]);
               }
               continue;
             }
@@ -1057,7 +1073,7 @@ __device__ void run_consumers(const DecodeLaunch& P, Smem* s) {
       } else {
         const uint32_t lq = st == kStLM ? 0 : l;
         const uint32_t format = stage_format(m, lq, st);
-        const bool q4 = format == kFormatQ4;  // q4 stages keep x prescaled (store_x4)
+        const bool q4 = format == kFormatQ4 || format == kFormatQ5;  // x prescaled for masked nibbles (store_x4)
         // -- stage input into x: the layer-0 input row, an RMSNorm of the
         // residual stream (decoder.zig:165-176, 259-262, 277-283), or the
         // attention output / SwiGLU activations; up reuses gate's input.

@@ -63,6 +63,12 @@ __host__ __device__ constexpr float q4_xscale(int i) {
                 : 0.0000152587890625f;
 }
 
+// 1 / (kQ4SubScale * q4_xscale(i)): undoes the q4 activation prescale.
+__host__ __device__ constexpr float q4_unscale(int i) {
+  return i == 0 ? 0x1p-74f : i == 1 ? 0x1p-70f : (i == 2 || i == 5) ? 0x1p-66f : (i == 3 || i == 6) ? 0x1p-62f
+                                                                                                     : 0x1p-58f;
+}
+
 // (w & MASK) | magic in one lop3 (LUT 0xEA = (a & b) | c).
 template <uint32_t MASK>
 __device__ __forceinline__ uint32_t and_or(uint32_t w, uint32_t magic) {
