@@ -1,10 +1,11 @@
-"""Host-side q4/q8 group quantizer and tensor payload layout.
+"""Host-side q4/q5/q8 group quantizer and tensor payload layout.
 
 Numpy restatement of the reference converter's arithmetic
 (src/core/quant.zig:144-288): 64-value groups, an f16 scale of
 `max_abs / bias` rounded to nearest even, codes quantized against the
 *stored* scale with round-half-away-from-zero and clamping, q4 nibbles
-little-endian within a byte. All arithmetic stays in float32, as the Zig code
+little-endian within a byte, q5 as q4 nibbles followed by a plane of fifth
+bits (quant.zig:253-269). All arithmetic stays in float32, as the Zig code
 does, so the bytes match the reference bit for bit.
 """
 
