@@ -40,6 +40,19 @@ def test_numpy_quantizer_is_bit_exact(oracle_lib, fmt):
     assert np.array_equal(quant.dequantize(fmt, s_np, c_np, 512), O.dequantize_rows(fmt, s_or, c_or, 512))
 
 
+def test_q5_packing_round_trips_every_code():
+    # quant.zig:253-269: low nibbles in the q4 layout, then the fifth-bit plane.
+    rng = np.random.default_rng(5)
+    u = rng.integers(0, 32, size=(7, 256)).astype(np.uint8)
+    u[0, :64] = np.arange(64) % 32          # every code, every bit position of a group
+    packed = quant.pack_q5(u)
+    assert packed.shape == (7, 4 * 40)
+    assert np.array_equal(quant.unpack_q5(packed, 256), u.astype(np.int32))
+    g0 = packed[0, :40]
+    assert g0[0] == (0 | (1 << 4)) and g0[15] == ((30 & 15) | ((31 & 15) << 4))  # low nibbles of 0, 1 / 30, 31
+    assert g0[32 + 2] == 0xFF and g0[32] == 0x00                     # weights 16..23 have the fifth bit
+
+
 def test_plane_layout_matches_reference_cases():
     # quant.zig:423-435: 896 x 896 q4 at base 0, alignment 16.
     so, sl, do, dl = quant.plane_layout(quant.Q4, 896, 896)
