@@ -97,6 +97,19 @@ typedef struct qwc_requirements {
   uint32_t reserved;
 } qwc_requirements;
 
+/* qw_model_tensor_descriptor layout, 64 bytes (src/wasm/abi.zig:370-382). */
+typedef struct qwc_tensor_descriptor {
+  uint64_t offset_bytes; /* from the start of its shard's bytes; 0 for a tensor added alone */
+  uint64_t len_bytes;    /* its payload bytes */
+  uint32_t kind;
+  uint32_t layer;
+  uint32_t format;
+  uint32_t rank;
+  uint32_t dims[4];      /* unused dimensions are 1, as the container writes them */
+  uint32_t shard_index;  /* its shard, in the order shards were added; 0xFFFFFFFF if added alone */
+  uint32_t reserved[3];
+} qwc_tensor_descriptor;
+
 /* Handle options (qwc_set_option). */
 enum {
   /* Nonzero: decode does not stop at end-of-sequence tokens (fixed-length
@@ -170,6 +183,12 @@ int32_t qwc_model_finish(uint32_t handle, const void* config, uint32_t config_le
 int32_t qwc_model_requirements(uint32_t handle, qwc_requirements* out);
 /* qw_model_tensor_count (exports.zig:384-389): tensors held by the loaded model. */
 int32_t qwc_model_tensor_count(uint32_t handle, uint32_t* out);
+/* qw_model_tensor_descriptor (exports.zig:402-412, model.zig:281-319): where tensor `index` of
+ * the loaded model came from and its shape, in the order tensors were added (a shard's in its
+ * index order). It describes the tensors this library keeps, the decoder's: a shard's other
+ * tensors are validated and not kept, so they are neither counted nor described. QWC_NOT_FOUND
+ * past the last tensor, QWC_INVALID_STATE before qwc_model_finish. */
+int32_t qwc_model_tensor_descriptor(uint32_t handle, uint32_t index, qwc_tensor_descriptor* out);
 
 /* ---- decode family, stream slot 0 (src/wasm/exports.zig:440-497; model.zig:370-474) ---- */
 

@@ -202,6 +202,10 @@ struct Tensor {
   uint32_t kind, layer, format, rows, cols;
   std::unique_ptr<DevBuf> buf;
   uint64_t scales_offset = 0, codes_offset = 0;
+  // Its qwc_model_tensor_descriptor: source offset and length, shape as the
+  // container records it, and the shard it came from (kNoShard if added alone).
+  uint64_t src_offset = 0, src_len = 0;
+  uint32_t rank = 2, dims[4] = {1, 1, 1, 1}, shard_index = 0xFFFFFFFFu;
 };
 
 struct StreamSlot {
@@ -265,6 +269,7 @@ struct Handle {
   uint32_t step_chunk = 16;
   uint64_t launches = 0;
   std::map<std::pair<uint32_t, uint32_t>, Tensor> tensors;
+  std::vector<std::pair<uint32_t, uint32_t>> tensor_order;  // keys of `tensors` in the order they were added
   Config config{};
   int grid = 0;
   DevModel host_model{};
@@ -315,6 +320,7 @@ int32_t status_of(cudaError_t e) {
 
 void release_model(Handle* h) {
   h->tensors.clear();
+  h->tensor_order.clear();
   h->shards.clear();
   for (DevBuf* b : {&h->model_buf, &h->rope_cos, &h->rope_sin, &h->k_cache, &h->v_cache, &h->qkv, &h->attn_out,
                     &h->hidden_g, &h->act, &h->attn_part, &h->attn_count, &h->amax_val, &h->amax_idx, &h->barrier,
@@ -1214,7 +1220,12 @@ int32_t qwc_model_add_tensor(uint32_t handle, uint32_t kind, uint32_t layer, uin
   QWC_TRY(t.buf->alloc(need));
   QWC_CUDA(cudaMemcpy(t.buf->ptr, payload, need, cudaMemcpyHostToDevice));
   h->weight_bytes += need;
+  t.src_len = len;
+  t.rank = (rows == 1 && is_vector_kind(kind)) ? 1u : 2u;
+  t.dims[0] = t.rank == 1 ? cols : rows;
+  if (t.rank == 2) t.dims[1] = cols;
   h->tensors.emplace(std::make_pair(kind, layer), std::move(t));
+  h->tensor_order.emplace_back(kind, layer);
   return QWC_OK;
 }
 
@@ -1254,6 +1265,12 @@ int32_t qwc_model_add_shard(uint32_t handle, const void* bytes, uint64_t len) {
     const uint32_t cols = e.rank == 1 ? e.dims[0] : e.dims[1];
     QWC_TRY(qwc_model_add_tensor(handle, e.kind, e.layer, e.format, rows, cols, v.payload + e.offset_bytes,
                                  e.len_bytes));
+    // model.zig:298-310: the offset within the shard's bytes, the entry's shape.
+    Tensor& t = h->tensors.at({e.kind, e.layer});
+    t.src_offset = uint64_t(v.payload - v.bytes) + e.offset_bytes;
+    t.rank = e.rank;
+    for (int d = 0; d < 4; ++d) t.dims[d] = e.dims[d];
+    t.shard_index = static_cast<uint32_t>(h->shards.size());
   }
   h->shards.push_back(v.checksum);
   return QWC_OK;
@@ -1332,6 +1349,27 @@ int32_t qwc_model_tensor_count(uint32_t handle, uint32_t* out) {
   if (!h || !out) return QWC_INVALID_ARGUMENT;
   if (h->state != State::kLoaded) return QWC_INVALID_STATE;
   *out = static_cast<uint32_t>(h->tensors.size());
+  return QWC_OK;
+}
+
+static_assert(sizeof(qwc_tensor_descriptor) == 64, "abi.zig:391: the descriptor is 64 bytes");
+
+int32_t qwc_model_tensor_descriptor(uint32_t handle, uint32_t index, qwc_tensor_descriptor* out) {
+  Handle* h = lookup(handle);
+  if (!h || !out) return QWC_INVALID_ARGUMENT;
+  if (h->state != State::kLoaded) return QWC_INVALID_STATE;
+  if (index >= h->tensor_order.size()) return QWC_NOT_FOUND;  // model.zig:318
+  const Tensor& t = h->tensors.at(h->tensor_order[index]);
+  qwc_tensor_descriptor d{};
+  d.offset_bytes = t.src_offset;
+  d.len_bytes = t.src_len;
+  d.kind = t.kind;
+  d.layer = t.layer;
+  d.format = t.format;
+  d.rank = t.rank;
+  for (int i = 0; i < 4; ++i) d.dims[i] = t.dims[i];
+  d.shard_index = t.shard_index;
+  *out = d;
   return QWC_OK;
 }
 

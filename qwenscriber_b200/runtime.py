@@ -14,6 +14,7 @@ from __future__ import annotations
 
 import ctypes
 import os
+import struct
 from ctypes import POINTER, c_char_p, c_float, c_int32, c_int64, c_uint32, c_uint64, c_void_p
 
 import numpy as np
@@ -54,6 +55,7 @@ SIGNATURES = {
     "qwc_model_finish": (c_int32, [c_uint32, c_void_p, c_uint32]),
     "qwc_model_requirements": (c_int32, [c_uint32, c_void_p]),
     "qwc_model_tensor_count": (c_int32, [c_uint32, POINTER(c_uint32)]),
+    "qwc_model_tensor_descriptor": (c_int32, [c_uint32, c_uint32, c_void_p]),
     "qwc_decode_begin": (c_int32, [c_uint32, c_void_p, c_uint32, c_void_p, c_uint32, c_uint32]),
     "qwc_decode_step": (c_int32, [c_uint32, POINTER(c_uint32)]),
     "qwc_decode_tokens": (c_int32, [c_uint32, c_void_p, c_uint32]),
@@ -216,6 +218,17 @@ class CudaModel:
         n = c_uint32(0)
         check(self._L.qwc_model_tensor_count(self.handle, ctypes.byref(n)), "qwc_model_tensor_count")
         return n.value
+
+    def tensor_descriptor(self, index: int) -> dict:
+        """qwc_model_tensor_descriptor: the 64-byte descriptor as a dict."""
+        raw = (ctypes.c_uint8 * 64)()
+        check(self._L.qwc_model_tensor_descriptor(self.handle, index, ctypes.addressof(raw)),
+              "qwc_model_tensor_descriptor")
+        b = bytes(raw)
+        off, length = struct.unpack_from("<QQ", b, 0)
+        kind, layer, fmt, rank, d0, d1, d2, d3, shard_index = struct.unpack_from("<9I", b, 16)
+        return {"offset_bytes": off, "len_bytes": length, "kind": kind, "layer": layer, "format": fmt,
+                "rank": rank, "dims": (d0, d1, d2, d3), "shard_index": shard_index}
 
     def set_option(self, option: int, value: int) -> None:
         check(self._L.qwc_set_option(self.handle, option, value), "qwc_set_option")

@@ -126,6 +126,16 @@ def test_operators_refuse_misaligned_pointers(cuda_lib):
     assert gemv(7, A, A, 4, 1024, A, out, None) == rt.STATUS_CODE["unsupported"]
 
 
+def test_tensor_descriptor_refuses_bad_handles(cuda_lib):
+    # A handle needs a device; without one the lookup fails before anything else.
+    import ctypes
+
+    buf = (ctypes.c_uint8 * 64)()
+    bad = rt.STATUS_CODE["invalid_argument"]
+    assert cuda_lib.qwc_model_tensor_descriptor(0, 0, ctypes.addressof(buf)) == bad
+    assert cuda_lib.qwc_model_tensor_descriptor(12345, 0, None) == bad
+
+
 def test_rope_tables_match_oracle_bit_for_bit(cuda_lib, oracle_lib):
     # kernels.zig:534-564: the tables the CUDA backend uploads equal the oracle's.
     cos_p, sin_p = rt.rope_tables(1000000.0, 128, 4096)
