@@ -161,7 +161,7 @@ int32_t qwc_model_add_tensor(uint32_t handle, uint32_t kind, uint32_t layer, uin
  * may be freed after the call. Tensors of other kinds (audio tower,
  * projector) are validated and not kept. A shard whose payload checksum
  * matches one already added, or a tensor already added, is invalid_argument; a decoder tensor in a
- * format the kernels do not run (q5, f16, bf16) is unsupported_model; more
+ * format the kernels do not run (f16, bf16) is unsupported_model; more
  * than 64 shards is limit_exceeded. A shard refused by any of these checks
  * leaves the handle unchanged. */
 int32_t qwc_model_add_shard(uint32_t handle, const void* bytes, uint64_t len);
@@ -174,7 +174,8 @@ int32_t qwc_shard_validate(const void* bytes, uint64_t len, uint32_t* tensor_cou
 uint32_t qwc_shard_checksum(const void* bytes, uint64_t len);
 /* qw_model_set_cache_format (exports.zig:352-363): ready state only. */
 int32_t qwc_model_set_cache_format(uint32_t handle, uint32_t format);
-/* Number of independent decode streams the next finish allocates (default 1). */
+/* Number of independent decode streams the next finish allocates (default 1). A model with
+ * q5 matrices runs one stream: finish returns unsupported_model for more. */
 int32_t qwc_model_set_streams(uint32_t handle, uint32_t streams);
 /* qw_model_finish: validates the 160-byte Config (src/core/model_config.zig:110-177,
  * 260-328), resolves every tensor, allocates caches and scratch. */
