@@ -203,7 +203,7 @@ struct Tensor {
   std::unique_ptr<DevBuf> buf;
   uint64_t scales_offset = 0, codes_offset = 0;
   // Its qwc_model_tensor_descriptor: source offset and length, shape as the
-  // container records it, and the shard it came from (kNoShard if added alone).
+  // container records it, and the shard it came from (0xFFFFFFFF if added alone).
   uint64_t src_offset = 0, src_len = 0;
   uint32_t rank = 2, dims[4] = {1, 1, 1, 1}, shard_index = 0xFFFFFFFFu;
 };
