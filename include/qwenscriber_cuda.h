@@ -126,7 +126,21 @@ enum {
   /* Prompt prefill of single-stream handles: 0 (default) batched on the
    * tensor cores, 64 positions per step; 1 token by token through the
    * persistent decode kernel. */
-  QWC_OPTION_PREFILL_SERIAL = 5
+  QWC_OPTION_PREFILL_SERIAL = 5,
+  /* Single-stream handles. Nonzero: every f32 operation of the decode runs
+   * in the order the reference's CPU path writes it (Decoder.forwardToken,
+   * decoder.zig:133-287): each dot product's four lanes summed in index
+   * order, sums of squares and softmax sums in order, attention over the
+   * whole history per kv head, no contracted multiply-adds, and exp computed
+   * as the host C library's expf. Logits, cache rows and greedy tokens then
+   * equal the CPU oracle's bit for bit. The prompt is prefilled token by
+   * token through the same kernel. Slower than the default. */
+  QWC_OPTION_EXACT = 6,
+  /* Bound on every device-side wait of the decode kernels (mbarrier phases,
+   * grid barriers, split-K counters), in microseconds; 0 restores the default
+   * (4 s single-stream, 2 s batched). A wait that runs out makes the call
+   * return QWC_INVALID_STATE instead of hanging; the handle stays usable. */
+  QWC_OPTION_WAIT_LIMIT_US = 7
 };
 
 /* ---- version and lifecycle (src/wasm/exports.zig:49-120) ---- */
@@ -245,7 +259,10 @@ int32_t qwc_debug_logits(uint32_t handle, uint32_t slot, float* out, uint32_t co
 int32_t qwc_debug_hold(uint32_t handle, uint32_t slot, int64_t force, uint32_t* held_out);
 /* Device scratch of the last launch's last forward pass, last layer:
  * which 0 = hidden (after the final residual add), 1 = q|k|v projections
- * (before QK-norm and RoPE), 2 = attention output, 3 = silu(gate) * up. */
+ * (before QK-norm and RoPE), 2 = attention output, 3 = silu(gate) * up.
+ * which 4 (handles with the batched engine): the batched step's q|k|v
+ * projections of the last layer before QK-norm and RoPE, 64 rows (one per
+ * GEMM column) of q width + 2 kv width floats. */
 int32_t qwc_debug_scratch(uint32_t handle, uint32_t which, float* out, uint32_t count);
 /* Phase timeline of the last launch (QWC_OPTION_TRACE): grid x 512 nanosecond
  * stamps. A token walks six stages per layer (QKV, attention, O, gate, up,

@@ -230,6 +230,7 @@ struct MatMaps {
 // Device state of the batched multi-stream step (streams > 1).
 struct Batched {
   DevBuf hidden, xb_h, xb_q, xb_f, part0, qrot, attn_part, attn_count, logits, tokens, desc, audio_ptrs, err;
+  DevBuf qkv_rows;  // the last layer's pre-norm q/k/v rows of the last step (qwc_debug_scratch 4)
   DevBuf history, counter;
   std::vector<MatMaps> mq, mk, mv, mo, mg, mu, md;
   MatMaps mlm;
@@ -266,6 +267,8 @@ struct Handle {
   bool keep_logits = false;
   bool trace = false;
   bool prefill_serial = false;  // QWC_OPTION_PREFILL_SERIAL
+  bool exact = false;           // QWC_OPTION_EXACT
+  uint64_t wait_limit_ns = 0;   // QWC_OPTION_WAIT_LIMIT_US (0: the defaults)
   uint32_t step_chunk = 16;
   uint64_t launches = 0;
   std::map<std::pair<uint32_t, uint32_t>, Tensor> tensors;
@@ -275,7 +278,7 @@ struct Handle {
   DevModel host_model{};
   DevBuf model_buf, rope_cos, rope_sin, k_cache, v_cache;
   DevBuf qkv, attn_out, hidden_g, act, attn_part, attn_count, amax_val, amax_idx, barrier, error, tokens_out, logits;
-  DevBuf prompt_ids, prompt_rows, audio_rows, trace_buf;
+  DevBuf prompt_ids, prompt_rows, audio_rows, trace_buf, exact_scratch;
   uint32_t max_chunks = 0;
   uint64_t weight_bytes = 0;
   KvMaps kv_maps{};
@@ -291,6 +294,9 @@ struct Handle {
 };
 
 constexpr size_t kShardCountMax = 64;  // src/wasm/model.zig:81
+// Default bounds on the device-side waits (QWC_OPTION_WAIT_LIMIT_US overrides).
+constexpr uint64_t kDecodeWaitNs = 4000000000ull;
+constexpr uint64_t kBatchedWaitNs = 2000000000ull;
 
 std::mutex g_mutex;
 std::map<uint32_t, std::unique_ptr<Handle>> g_handles;
@@ -324,7 +330,8 @@ void release_model(Handle* h) {
   h->shards.clear();
   for (DevBuf* b : {&h->model_buf, &h->rope_cos, &h->rope_sin, &h->k_cache, &h->v_cache, &h->qkv, &h->attn_out,
                     &h->hidden_g, &h->act, &h->attn_part, &h->attn_count, &h->amax_val, &h->amax_idx, &h->barrier,
-                    &h->error, &h->tokens_out, &h->logits, &h->prompt_ids, &h->prompt_rows, &h->audio_rows, &h->trace_buf}) {
+                    &h->error, &h->tokens_out, &h->logits, &h->prompt_ids, &h->prompt_rows, &h->audio_rows, &h->trace_buf,
+                    &h->exact_scratch}) {
     b->alloc(0);
   }
   h->slots.clear();
@@ -555,6 +562,8 @@ int32_t finish_model(Handle* h, const Config& c) {
   QWC_TRY(h->prompt_ids.alloc(size_t(c.max_positions) * 4));
   QWC_TRY(h->prompt_rows.alloc(size_t(c.max_positions) * 4));
   QWC_TRY(h->audio_rows.alloc(size_t(c.max_positions) * hidden * 4));
+  // Exact mode's attention scores and value weights: [q_heads][3][max_positions].
+  QWC_TRY(h->exact_scratch.alloc(size_t(c.text_attention_heads) * 3 * c.max_positions * 4));
 
   QWC_TRY(h->model_buf.alloc(sizeof(DevModel)));
   QWC_CUDA(cudaMemcpy(h->model_buf.ptr, &m, sizeof(DevModel), cudaMemcpyHostToDevice));
@@ -603,7 +612,9 @@ int32_t run_decode(Handle* h, uint32_t n_tokens, uint32_t first_position, uint32
   L.amax_idx = h->amax_idx.as<uint32_t>();
   L.barrier = h->barrier.as<uint32_t>();
   L.error = h->error.as<int32_t>();
-  L.timeout_ns = 4000000000ull;
+  L.timeout_ns = h->wait_limit_ns ? h->wait_limit_ns : kDecodeWaitNs;
+  L.exact = h->exact ? 1u : 0u;
+  L.exact_scratch = h->exact_scratch.as<float>();
   if (h->trace) {
     if (h->trace_buf.bytes == 0) QWC_TRY(h->trace_buf.alloc(size_t(h->grid) * kTraceEvents * 8));
     QWC_CUDA(cudaMemsetAsync(h->trace_buf.ptr, 0, h->trace_buf.bytes, h->stream));
@@ -710,6 +721,30 @@ int32_t record_step(Handle* h) {
   return QWC_OK;
 }
 
+// Records the step once as a CUDA graph (replayed every step), replacing any
+// earlier recording; kernel parameters such as the wait bound are fixed at
+// capture.
+int32_t capture_step(Handle* h) {
+  Batched& b = *h->batched;
+  if (b.exec) cudaGraphExecDestroy(b.exec);
+  if (b.graph) cudaGraphDestroy(b.graph);
+  b.exec = nullptr;
+  b.graph = nullptr;
+  QWC_CUDA(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+  const int32_t rec = record_step(h);
+  cudaGraph_t graph = nullptr;
+  const cudaError_t ce = cudaStreamEndCapture(h->stream, &graph);
+  if (rec != QWC_OK || ce != cudaSuccess) {
+    if (graph) cudaGraphDestroy(graph);
+    cudaGetLastError();
+    return rec != QWC_OK ? rec : status_of(ce);
+  }
+  b.graph = graph;
+  const cudaError_t ie = cudaGraphInstantiate(&b.exec, graph, 0);
+  if (ie != cudaSuccess) return status_of(ie);
+  return QWC_OK;
+}
+
 int32_t build_batched(Handle* h) {
   const DevModel& m = h->host_model;
   const Config& c = h->config;
@@ -735,6 +770,7 @@ int32_t build_batched(Handle* h) {
   QWC_TRY(b.attn_part.alloc(S * m.q_heads * h->max_chunks * (kHeadDim + 2) * 4));
   QWC_TRY(b.attn_count.alloc(S * m.kv_heads * 4));
   QWC_TRY(b.logits.alloc(S * m.vocab * 4));
+  QWC_TRY(b.qkv_rows.alloc(S * (qw + 2 * kvw) * 4));
   QWC_TRY(b.tokens.alloc(S * 4));
   QWC_TRY(b.desc.alloc(S * sizeof(SlotStep)));
   QWC_TRY(b.audio_ptrs.alloc(S * sizeof(float*)));
@@ -790,33 +826,19 @@ int32_t build_batched(Handle* h) {
   P.k_cache = h->k_cache.as<uint8_t>();
   P.v_cache = h->v_cache.as<uint8_t>();
   P.logits = b.logits.as<float>();
+  P.qkv_rows = b.qkv_rows.as<float>();
   P.tokens = b.tokens.as<uint32_t>();
   P.error = b.err.as<int32_t>();
   P.max_chunks = h->max_chunks;
-  P.timeout_ns = 2000000000ull;
+  P.timeout_ns = h->wait_limit_ns ? h->wait_limit_ns : kBatchedWaitNs;
 
   int e = prepare_gemm_kernel();
   if (e == 0) e = prepare_stream_kernels();
   if (e != 0) return status_of(static_cast<cudaError_t>(e));
   h->batched = std::move(bp);
-  // The step is recorded once as a CUDA graph and replayed every step.
-  QWC_CUDA(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
-  const int32_t rec = record_step(h);
-  cudaGraph_t graph = nullptr;
-  const cudaError_t ce = cudaStreamEndCapture(h->stream, &graph);
-  if (rec != QWC_OK || ce != cudaSuccess) {
-    if (graph) cudaGraphDestroy(graph);
-    cudaGetLastError();
-    h->batched.reset();
-    return rec != QWC_OK ? rec : status_of(ce);
-  }
-  h->batched->graph = graph;
-  const cudaError_t ie = cudaGraphInstantiate(&h->batched->exec, graph, 0);
-  if (ie != cudaSuccess) {
-    h->batched.reset();
-    return status_of(ie);
-  }
-  return QWC_OK;
+  const int32_t st = capture_step(h);
+  if (st != QWC_OK) h->batched.reset();
+  return st;
 }
 
 // Runs the captured step once for the columns in b.host_desc and reads the
@@ -1021,7 +1043,7 @@ int32_t stream_begin(Handle* h, uint32_t slot, const uint32_t* prompt, uint32_t 
   }
   QWC_CUDA(cudaStreamSynchronize(h->stream));
   uint32_t next = 0, col = 0;
-  const bool serial = (h->prefill_serial || !h->batched) && h->streams == 1;
+  const bool serial = (h->prefill_serial || h->exact || !h->batched) && h->streams == 1;
   if (serial) {
     // Token by token through the persistent kernel (decoder.zig:308-333 as written).
     QWC_CUDA(cudaMemcpyAsync(h->prompt_ids.ptr, prompt, size_t(prompt_len) * 4, cudaMemcpyHostToDevice, h->stream));
@@ -1165,6 +1187,15 @@ int32_t qwc_set_option(uint32_t handle, uint32_t option, uint32_t value) {
     case QWC_OPTION_KEEP_LOGITS: h->keep_logits = value != 0; return QWC_OK;
     case QWC_OPTION_TRACE: h->trace = value != 0; return QWC_OK;
     case QWC_OPTION_PREFILL_SERIAL: h->prefill_serial = value != 0; return QWC_OK;
+    case QWC_OPTION_EXACT: h->exact = value != 0; return QWC_OK;
+    case QWC_OPTION_WAIT_LIMIT_US:
+      h->wait_limit_ns = uint64_t(value) * 1000ull;
+      if (h->batched) {
+        cudaSetDevice(h->device);
+        h->batched->P.timeout_ns = h->wait_limit_ns ? h->wait_limit_ns : kBatchedWaitNs;
+        return capture_step(h);
+      }
+      return QWC_OK;
     case QWC_OPTION_STEP_CHUNK:
       if (value == 0 || value > 256) return QWC_INVALID_ARGUMENT;
       h->step_chunk = value;
@@ -1312,7 +1343,8 @@ int32_t qwc_model_finish(uint32_t handle, const void* config, uint32_t config_le
     // model.zig:197-204: a failed load releases what it allocated; shards stay.
     for (DevBuf* b : {&h->model_buf, &h->rope_cos, &h->rope_sin, &h->k_cache, &h->v_cache, &h->qkv, &h->attn_out,
                       &h->hidden_g, &h->act, &h->attn_part, &h->attn_count, &h->amax_val, &h->amax_idx, &h->barrier,
-                      &h->error, &h->tokens_out, &h->logits, &h->prompt_ids, &h->prompt_rows, &h->audio_rows}) {
+                      &h->error, &h->tokens_out, &h->logits, &h->prompt_ids, &h->prompt_rows, &h->audio_rows,
+                      &h->exact_scratch}) {
       b->alloc(0);
     }
     return st;
@@ -1331,7 +1363,8 @@ int32_t qwc_model_requirements(uint32_t handle, qwc_requirements* out) {
   uint64_t scratch = 0;
   for (const DevBuf* b : {&h->model_buf, &h->rope_cos, &h->rope_sin, &h->qkv, &h->attn_out, &h->hidden_g, &h->act,
                           &h->attn_part, &h->attn_count, &h->amax_val, &h->amax_idx, &h->barrier, &h->error,
-                          &h->tokens_out, &h->logits, &h->prompt_ids, &h->prompt_rows, &h->audio_rows}) {
+                          &h->tokens_out, &h->logits, &h->prompt_ids, &h->prompt_rows, &h->audio_rows,
+                          &h->exact_scratch}) {
     scratch += b->bytes;
   }
   r.scratch_bytes = scratch;
@@ -1533,9 +1566,11 @@ int32_t qwc_debug_hold(uint32_t handle, uint32_t slot, int64_t force, uint32_t* 
 
 int32_t qwc_debug_scratch(uint32_t handle, uint32_t which, float* out, uint32_t count) {
   Handle* h = lookup(handle);
-  if (!h || !out || which > 3) return QWC_INVALID_ARGUMENT;
+  if (!h || !out || which > 4) return QWC_INVALID_ARGUMENT;
   if (h->state != State::kLoaded) return QWC_INVALID_STATE;
-  const DevBuf* b = which == 0 ? &h->hidden_g : which == 1 ? &h->qkv : which == 2 ? &h->attn_out : &h->act;
+  if (which == 4 && !h->batched) return QWC_INVALID_STATE;
+  const DevBuf* b = which == 0 ? &h->hidden_g : which == 1 ? &h->qkv : which == 2 ? &h->attn_out
+                  : which == 3 ? &h->act : &h->batched->qkv_rows;
   if (uint64_t(count) * 4 < b->bytes) return QWC_LIMIT_EXCEEDED;
   cudaSetDevice(h->device);
   QWC_CUDA(cudaMemcpyAsync(out, b->ptr, b->bytes, cudaMemcpyDeviceToHost, h->stream));

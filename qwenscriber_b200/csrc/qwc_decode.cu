@@ -87,6 +87,7 @@ struct Smem {
   float amax_v[kConsumerWarps];
   uint32_t amax_i[kConsumerWarps];
   uint32_t flag;
+  uint32_t abort;  // set by any consumer thread whose bounded wait gave up
   // The model description, copied from device memory at launch: every stage
   // reads matrix shapes and pointers from it, and shared-memory loads keep
   // those reads off the stage's critical path.
@@ -327,7 +328,7 @@ __device__ void run_producer(const DecodeLaunch& P, const KvMaps& maps, Smem* s)
       }
       if (!pr.ok) break;
       if (st == kStAttn) {
-        pr.attention_tiles(m, maps, l, position);
+        if (!P.exact) pr.attention_tiles(m, maps, l, position);  // exact mode reads the cache with plain loads
       } else {
         pr.stage(m, st == kStLM ? 0 : l, st);
       }
@@ -387,10 +388,18 @@ __device__ void release_tile(Ctx& c) {
 }
 
 // Grid-wide barrier among the consumer warps of every CTA. The counter is
-// monotonic within a launch (zeroed by the host before it).
+// monotonic within a launch (zeroed by the host before it). It is also where
+// a CTA decides, for all its consumer threads at once, to stop after a
+// bounded wait gave up: a thread whose own wait ran out must not leave the
+// stage walk while the others go on to the next block-wide barrier.
 __device__ void grid_barrier(Ctx& c) {
+  if (!c.ok) c.s->abort = 1u;
   consumer_sync(kConsumerThreads);
-  if (c.tid == 0) {
+  if (c.tid == 0 && c.s->abort) {
+    // This CTA stops without arriving; the others see the error word (set by
+    // the wait that gave up) or run out their own bounded waits.
+    c.s->flag = 1u;
+  } else if (c.tid == 0) {
     c.barriers += 1;
     const uint32_t target = c.barriers * gridDim.x;
     const uint64_t arrive = c.tracing ? global_timer_ns() : 0;
@@ -423,7 +432,7 @@ __device__ void grid_barrier(Ctx& c) {
     if (c.tracing) c.bar_wait_ns += global_timer_ns() - arrive;
   }
   consumer_sync(kConsumerThreads);
-  if (c.s->flag) c.ok = false;
+  c.ok = c.s->flag == 0u;
 }
 
 // Block-wide sum over the consumer threads.
@@ -444,8 +453,28 @@ __device__ float block_sum(Ctx& c, float v) {
 
 constexpr int kMaxPer4 = (kHiddenMax / 4 + kConsumerThreads - 1) / kConsumerThreads;  // float4 groups per thread
 
-// x[k .. k + 3] <- v, prescaled for q4 stages; k is a multiple of 4.
-__device__ __forceinline__ void store_x4(Ctx& c, uint32_t k, float4 v, bool q4) {
+// Exact mode keeps x as four lane arrays, the reference dotF32's lanes
+// (kernels.zig:39-51): lane array j holds x[j], x[4 + j], x[8 + j], ... at
+// s->x[j * xs + i], so the thread that runs lane j of a row reads its
+// activations as consecutive float4s. The 16-byte pad between the arrays
+// keeps the four lanes' reads in different banks.
+__device__ __forceinline__ uint32_t x_lane_stride(uint32_t width) {
+  return width / 4 + ((width + 16 <= kXMax) ? 4u : 0u);
+}
+
+// x[k .. k + 3] <- v, prescaled for q4 stages; k is a multiple of 4 and
+// `width` the length of the vector x holds.
+template <bool E>
+__device__ __forceinline__ void store_x4(Ctx& c, uint32_t k, float4 v, bool q4, uint32_t width) {
+  if constexpr (E) {
+    const uint32_t xs = x_lane_stride(width);
+    float* x = c.s->x + (k >> 2);
+    x[0] = v.x;
+    x[xs] = v.y;
+    x[2 * xs] = v.z;
+    x[3 * xs] = v.w;
+    return;
+  }
   if (q4) {
     // kQ4SubScale * q4_xscale over k & 7 = 0..3 or 4..7 (powers of two: exact).
     const bool hi = (k & 4u) != 0;
@@ -461,7 +490,37 @@ __device__ __forceinline__ void store_x4(Ctx& c, uint32_t k, float4 v, bool q4) 
 // stored prescaled for q4 stages. `raw` holds this thread's float4 groups
 // (k = 4 * (tid + i * kConsumerThreads)); the weight vector is the next
 // streamed tile.
+template <bool E>
 __device__ void normalize_into_x(Ctx& c, const float4 (&raw)[kMaxPer4], uint32_t width, bool q4) {
+  if constexpr (E) {
+    // The raw vector goes to shared memory in index order, and one thread
+    // sums its squares in that order (math.zig:123); every CTA does this
+    // itself, so no grid-wide exchange is added.
+#pragma unroll
+    for (int i = 0; i < kMaxPer4; ++i) {
+      const uint32_t k4 = c.tid + i * kConsumerThreads;
+      if (k4 < width / 4) reinterpret_cast<float4*>(c.s->x)[k4] = raw[i];
+    }
+    consumer_sync(kConsumerThreads);
+    if (c.tid == 0) c.s->red[0] = rms_inverse(sum_squares_seq(c.s->x, width), width, c.m->eps);
+    consumer_sync(kConsumerThreads);
+    const float inv = c.s->red[0];
+    const float4* weight = reinterpret_cast<const float4*>(acquire_tile(c));
+#pragma unroll
+    for (int i = 0; i < kMaxPer4; ++i) {
+      const uint32_t k4 = c.tid + i * kConsumerThreads;
+      if (k4 < width / 4) {
+        const float4 w = weight[k4];
+        store_x4<true>(c, 4 * k4,
+                 make_float4(__fmul_rn(__fmul_rn(raw[i].x, inv), w.x), __fmul_rn(__fmul_rn(raw[i].y, inv), w.y),
+                             __fmul_rn(__fmul_rn(raw[i].z, inv), w.z), __fmul_rn(__fmul_rn(raw[i].w, inv), w.w)),
+                 false, width);
+      }
+    }
+    release_tile(c);
+    consumer_sync(kConsumerThreads);
+    return;
+  }
   float ss = 0.0f;
 #pragma unroll
   for (int i = 0; i < kMaxPer4; ++i) {
@@ -480,9 +539,9 @@ __device__ void normalize_into_x(Ctx& c, const float4 (&raw)[kMaxPer4], uint32_t
     const uint32_t k4 = c.tid + i * kConsumerThreads;
     if (k4 < width / 4) {
       const float4 w = weight[k4];
-      store_x4(c, 4 * k4,
+      store_x4<false>(c, 4 * k4,
                make_float4(raw[i].x * inv * w.x, raw[i].y * inv * w.y, raw[i].z * inv * w.z, raw[i].w * inv * w.w),
-               q4);
+               q4, width);
     }
   }
   release_tile(c);
@@ -490,6 +549,7 @@ __device__ void normalize_into_x(Ctx& c, const float4 (&raw)[kMaxPer4], uint32_t
 }
 
 // x <- rmsnorm(hidden) * weight for a hidden vector other CTAs wrote (L2 loads).
+template <bool E>
 __device__ void norm_global_into_x(Ctx& c, const float* src, uint32_t width, bool q4) {
   float4 raw[kMaxPer4];
 #pragma unroll
@@ -497,13 +557,14 @@ __device__ void norm_global_into_x(Ctx& c, const float* src, uint32_t width, boo
     const uint32_t k4 = c.tid + i * kConsumerThreads;
     raw[i] = k4 < width / 4 ? ld_cg4(reinterpret_cast<const float4*>(src) + k4) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  normalize_into_x(c, raw, width, q4);
+  normalize_into_x<E>(c, raw, width, q4);
 }
 
 // Copies a vector other CTAs wrote into x (L2-coherent loads), prescaled for q4.
+template <bool E>
 __device__ void load_x_global(Ctx& c, const float* src, uint32_t width, bool q4) {
   for (uint32_t k4 = c.tid; k4 < width / 4; k4 += kConsumerThreads) {
-    store_x4(c, 4 * k4, ld_cg4(reinterpret_cast<const float4*>(src) + k4), q4);
+    store_x4<E>(c, 4 * k4, ld_cg4(reinterpret_cast<const float4*>(src) + k4), q4, width);
   }
   consumer_sync(kConsumerThreads);
 }
@@ -579,7 +640,7 @@ __device__ void attention_into_x(Ctx& c, const float* parts, uint32_t chunks, bo
       // Every CTA merges the same partials in the same order; CTA 0 also
       // keeps the attention output for qwc_debug_scratch.
       if (blockIdx.x == 0) reinterpret_cast<float4*>(c.P->attn_out)[k4[g]] = out;
-      store_x4(c, 4 * k4[g], out, q4);
+      store_x4<false>(c, 4 * k4[g], out, q4, 4 * qw4);
     }
   }
   consumer_sync(kConsumerThreads);
@@ -587,6 +648,7 @@ __device__ void attention_into_x(Ctx& c, const float* parts, uint32_t chunks, bo
 
 // Layer-0 input: the token's embedding row (decoder.zig:346-376, quant.zig:348-364)
 // or an audio row; this CTA's residual rows keep the raw values, x the normed.
+template <bool E>
 __device__ void input_into_x(Ctx& c, uint32_t token, int32_t audio_row, Span own, bool q4) {
   const DevModel& m = *c.m;
   const uint32_t hidden = m.hidden;
@@ -631,7 +693,7 @@ __device__ void input_into_x(Ctx& c, uint32_t token, int32_t audio_row, Span own
     }
     raw[i] = make_float4(v[0], v[1], v[2], v[3]);
   }
-  normalize_into_x(c, raw, hidden, q4);
+  normalize_into_x<E>(c, raw, hidden, q4);
 }
 
 // ---- GEMV over the streamed tiles ----
@@ -668,6 +730,16 @@ struct Best {
   float v;
   uint32_t i;
 };
+
+// The value a logit competes with in the argmax. decoder.zig:290-301 seeds
+// the running maximum with values[0] and replaces it only on a strict `>`:
+// a NaN at index 0 is never replaced (the answer is 0), and a NaN elsewhere
+// never wins. Ranking a NaN logit 0 as +inf (ties go to the lowest index) and
+// skipping every other NaN (all comparisons with NaN are false) gives the
+// same answer from any order of reduction.
+__device__ __forceinline__ float argmax_key(float v, uint32_t index) {
+  return (index == 0 && v != v) ? __int_as_float(0x7F800000) : v;
+}
 
 // Consumes the stage's tiles. Non-LM stages leave per-row dot products in
 // s->part[local]; the LM stage keeps a running argmax per lane and optionally
@@ -777,7 +849,8 @@ __device__ void gemv_tiles(Ctx& c, const Piece* pieces, int np, bool lm, Best& b
             } else {
               const uint32_t row = pc.out0 + r + i;
               if (logits_out) logits_out[row] = total;
-              if (total > best.v || (total == best.v && row < best.i)) best = Best{total, row};
+              const float key = argmax_key(total, row);
+              if (key > best.v || (key == best.v && row < best.i)) best = Best{key, row};
             }
           }
         }
@@ -793,7 +866,8 @@ __device__ void gemv_tiles(Ctx& c, const Piece* pieces, int np, bool lm, Best& b
         } else {
           const uint32_t row = pc.out0 + r + i;
           if (logits_out) logits_out[row] = total;
-          if (total > best.v || (total == best.v && row < best.i)) best = Best{total, row};
+          const float key = argmax_key(total, row);
+          if (key > best.v || (key == best.v && row < best.i)) best = Best{key, row};
         }
       }
       consumer_sync(kConsumerThreads);  // chunk_part is reused by the next tile
@@ -801,9 +875,125 @@ __device__ void gemv_tiles(Ctx& c, const Piece* pieces, int np, bool lm, Best& b
   }
 }
 
+// ---- exact mode: dot products in the reference's order ----
+//
+// One lane of dotF32 (kernels.zig:39-51) over a row that linearQuantized
+// dequantizes first (kernels.zig:118-158, quant.zig:315-345): lane j sums
+// w[4 i + j] * x[4 i + j] for i = 0, 1, 2, ... with every product and sum
+// rounded, where w = (code - bias) * scale exactly. `xl` is lane array j of x.
+template <uint32_t FMT>
+__device__ __forceinline__ float lane_dot(const uint8_t* scales, const uint8_t* codes, uint32_t groups, const float* xl,
+                                          uint32_t j) {
+  float l = 0.0f;
+  for (uint32_t g = 0; g < groups; ++g) {
+    const float s = f16_bits_to_f32(reinterpret_cast<const uint16_t*>(scales)[g]);
+    if constexpr (FMT == kFormatQ8) {
+      // Word q of the group's codes holds elements 4 q .. 4 q + 3; lane j takes byte j.
+      const uint4* cw = reinterpret_cast<const uint4*>(codes + 64u * g);
+      const float4* xg = reinterpret_cast<const float4*>(xl + 16u * g);
+      const uint32_t sel = 0x7440u | j;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 w = cw[q];
+        const float4 xv = xg[q];
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float cv = __fadd_rn(bits_f32(__byte_perm(ws[e], kMagic, sel)), kNegQ8);  // code - 128, exact
+          l = __fadd_rn(l, __fmul_rn(__fmul_rn(cv, s), xs[e]));
+        }
+      }
+    } else if constexpr (FMT == kFormatQ4) {
+      // Word q holds elements 8 q .. 8 q + 7 at nibble positions 0..7; lane j
+      // takes positions j and j + 4 (lane indices 2 q and 2 q + 1).
+      const uint4* cw = reinterpret_cast<const uint4*>(codes + 32u * g);
+      const float2* xg = reinterpret_cast<const float2*>(xl + 16u * g);
+      const uint32_t sh = 4u * j;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint4 w = cw[h];
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 xv = xg[4 * h + e];
+          const float c0 = __fadd_rn(bits_f32(((ws[e] >> sh) & 0xFu) | kMagic), kNegM0);  // u - 8, exact
+          const float c1 = __fadd_rn(bits_f32(((ws[e] >> (sh + 16u)) & 0xFu) | kMagic), kNegM0);
+          l = __fadd_rn(l, __fmul_rn(__fmul_rn(c0, s), xv.x));
+          l = __fadd_rn(l, __fmul_rn(__fmul_rn(c1, s), xv.y));
+        }
+      }
+    } else {
+      const uint8_t* grp = codes + 40u * g;
+      for (uint32_t i = 0; i < 16; ++i) {
+        const float cv = static_cast<float>(q5_code(grp, 4u * i + j));
+        l = __fadd_rn(l, __fmul_rn(__fmul_rn(cv, s), xl[16u * g + i]));
+      }
+    }
+  }
+  return l;
+}
+
+// Consumes the stage's tiles in exact mode. Warps 0-3 take the stage's even
+// tiles and warps 4-7 its odd ones; in a tile, thread 4 r + j of the group
+// runs lane j of rows r, r + 32, ..., and the row's sum is
+// ((l0 + l1) + l2) + l3 as @reduce(.Add) forms it.
+template <uint32_t FMT>
+__device__ void gemv_tiles_exact(Ctx& c, const Piece* pieces, int np, bool lm, Best& best, float* logits_out) {
+  const uint32_t grp = static_cast<uint32_t>(c.warp) >> 2;
+  const uint32_t t = static_cast<uint32_t>(c.tid) & 127u;
+  const uint32_t j = t & 3u;
+  const float* xl = c.s->x + j * x_lane_stride(pieces[0].scale_row / 2 * kGroup);
+  uint32_t n = 0;
+  for (int p = 0; p < np; ++p) {
+    const Piece pc = pieces[p];
+    const uint32_t per = rows_per_tile(pc);
+    const uint32_t groups = pc.scale_row / 2;
+    for (uint32_t r = 0; r < pc.rows; r += per, ++n) {
+      const uint32_t nr = min(per, pc.rows - r);
+      const uint8_t* base = acquire_tile(c);
+      if (c.ok && (n & 1u) == grp) {
+        const uint8_t* codes = base + nr * pc.scale_row;
+        for (uint32_t i0 = 0; i0 < nr; i0 += 32) {
+          const uint32_t i = i0 + (t >> 2);
+          const uint32_t row = min(i, nr - 1);
+          const float l = lane_dot<FMT>(base + row * pc.scale_row, codes + row * pc.code_row, groups, xl, j);
+          const float l1 = __shfl_down_sync(0xffffffffu, l, 1);
+          const float l2 = __shfl_down_sync(0xffffffffu, l, 2);
+          const float l3 = __shfl_down_sync(0xffffffffu, l, 3);
+          if (j == 0 && i < nr) {
+            const float total = __fadd_rn(__fadd_rn(__fadd_rn(l, l1), l2), l3);
+            if (!lm) {
+              c.s->part[pc.local0 + r + i] = total;
+            } else {
+              const uint32_t out = pc.out0 + r + i;
+              if (logits_out) logits_out[out] = total;
+              const float key = argmax_key(total, out);
+              if (key > best.v || (key == best.v && out < best.i)) best = Best{key, out};
+            }
+          }
+        }
+      }
+      release_tile(c);
+    }
+  }
+}
+
 // Runs one GEMV stage over the CTA's pieces.
+template <bool E>
 __device__ void gemv_stage(Ctx& c, const Piece* pieces, int np, uint32_t format, bool lm, Best& best,
                            float* logits_out) {
+  if constexpr (E) {
+    if (format == kFormatQ4) {
+      gemv_tiles_exact<kFormatQ4>(c, pieces, np, lm, best, logits_out);
+    } else if (format == kFormatQ5) {
+      gemv_tiles_exact<kFormatQ5>(c, pieces, np, lm, best, logits_out);
+    } else {
+      gemv_tiles_exact<kFormatQ8>(c, pieces, np, lm, best, logits_out);
+    }
+    consumer_sync(kConsumerThreads);
+    return;
+  }
   if (format == kFormatQ4) {
     gemv_tiles<kFormatQ4>(c, pieces, np, lm, best, logits_out);
   } else if (format == kFormatQ5) {
@@ -851,44 +1041,36 @@ __device__ void attention_stage(Ctx& c, uint32_t layer, uint32_t position) {
     const float* k_norm = reinterpret_cast<const float*>(tile + kTileKNorm);
     const float* cos_row = reinterpret_cast<const float*>(tile + kTileCos);
     const float* sin_row = reinterpret_cast<const float*>(tile + kTileSin);
-    // 2. Per-head RMSNorm of the queries and the new key (decoder.zig:180-195).
+    // 2. Per-head RMSNorm of the queries and the new key (decoder.zig:180-195,
+    // math.zig:120-130): the sums of squares run in dimension order on three
+    // threads of different warps, and value * inverse_rms * weight rounds each
+    // product, so the key row equals the reference's on the same inputs.
     {
-      const float ss = warp_sum(qraw * qraw);
-      const float kss = warp_sum(kvraw * kvraw);
-      if (c.lane == 0) {
-        c.s->red[c.warp] = ss;
-        c.s->red[kConsumerWarps + c.warp] = kss;
+      a->tmp[j][d] = qraw;
+      if (last && j == 0) a->ktmp[d] = kvraw;
+      consumer_sync(kConsumerThreads);
+      if (tid == 0 || tid == 32 || (last && tid == 64)) {
+        const float* v = tid == 64 ? a->ktmp : a->tmp[tid / 32];
+        c.s->red[tid / 32] = rms_inverse(sum_squares_seq(v, kHeadDim), kHeadDim, m.eps);
       }
       consumer_sync(kConsumerThreads);
-      const int w0 = j * 4;
-      const float total = ((c.s->red[w0] + c.s->red[w0 + 1]) + c.s->red[w0 + 2]) + c.s->red[w0 + 3];
-      const float inv = 1.0f / sqrtf(total / static_cast<float>(kHeadDim) + m.eps);
-      a->tmp[j][d] = qraw * inv * q_norm[d];
-      if (last && j == 0) {
-        const float kt = ((c.s->red[kConsumerWarps] + c.s->red[kConsumerWarps + 1]) + c.s->red[kConsumerWarps + 2]) +
-                         c.s->red[kConsumerWarps + 3];
-        const float kinv = 1.0f / sqrtf(kt / static_cast<float>(kHeadDim) + m.eps);
-        a->ktmp[d] = kvraw * kinv * k_norm[d];
-      }
+      const float qn = __fmul_rn(__fmul_rn(qraw, c.s->red[j]), q_norm[d]);
+      const float kn = (last && j == 0) ? __fmul_rn(__fmul_rn(kvraw, c.s->red[2]), k_norm[d]) : 0.0f;
+      consumer_sync(kConsumerThreads);
+      a->tmp[j][d] = qn;
+      if (last && j == 0) a->ktmp[d] = kn;
       consumer_sync(kConsumerThreads);
     }
-    // 3. RoPE (rotate_half, kernels.zig rope) of the queries and the new key.
+    // 3. RoPE (rotate_half, kernels.zig:495-527) of the queries and the new key.
     const int pair = d % (kHeadDim / 2);
     const float cs = cos_row[pair], sn = sin_row[pair];
-    {
-      const float lo = a->tmp[j][pair], hi = a->tmp[j][pair + kHeadDim / 2];
-      const float rot = d < kHeadDim / 2 ? lo * cs - hi * sn : hi * cs + lo * sn;
-      a->q[j][d / 32][d % 32] = rot;
-    }
+    a->q[j][d / 32][d % 32] = rope_rn(d < kHeadDim / 2, a->tmp[j][pair], a->tmp[j][pair + kHeadDim / 2], cs, sn);
     // 4. The last chunk appends the new key (normed, rotated) and value rows
     // as q8 (decoder.zig:187-216, quant.zig:197-227): one 64-value group per
     // two warps. The codes also stay in shared memory for this unit.
     if (last) {
       float val = kvraw;
-      if (j == 0) {
-        const float lo = a->ktmp[pair], hi = a->ktmp[pair + kHeadDim / 2];
-        val = d < kHeadDim / 2 ? lo * cs - hi * sn : hi * cs + lo * sn;
-      }
+      if (j == 0) val = rope_rn(d < kHeadDim / 2, a->ktmp[pair], a->ktmp[pair + kHeadDim / 2], cs, sn);
       const float amax = warp_max(fabsf(val));
       consumer_sync(kConsumerThreads);
       if (c.lane == 0) c.s->red[c.warp] = amax;
@@ -1042,8 +1224,194 @@ __device__ void attention_stage(Ctx& c, uint32_t layer, uint32_t position) {
   }
 }
 
+// ---- exact mode: attention in the reference's order ----
+//
+// decodeAttentionStepQ8 (kernels.zig:697-767) with its softmax
+// (math.zig:77-93) as written: per query head, the scores of every cached
+// position (q8GroupDot: four lanes per 64-value group, sums rounded in
+// order), the maximum, exp of each difference, their sum in position order,
+// one reciprocal, and the outputs summed over positions in order
+// (q8GroupAccumulate). CTA h < kv_heads takes kv head h (query heads 2h and
+// 2h + 1); the other CTAs have no attention work. Scores and value weights go
+// through exact_scratch; the cache rows, including the one this stage
+// appends, are read with ordinary loads.
+struct AttnExact {
+  alignas(16) float raw[4][kHeadDim];  // pre-norm query heads 2h, 2h + 1, then the new key and value rows
+  alignas(16) float rot[3][kHeadDim];  // normed, rotated query heads and key
+  float inv[4];
+  float red[2][kConsumerWarps];
+  float amax[kConsumerWarps];
+};
+static_assert(sizeof(AttnExact) <= sizeof(float) * kXMax, "exact attention scratch must fit the activation buffer");
+
+__device__ void attention_stage_exact(const DecodeLaunch* P, const DevModel* mp_, Smem* s, uint32_t layer,
+                                                   uint32_t position) {
+  const DevModel& m = *mp_;
+  const uint32_t h = blockIdx.x;
+  if (h >= m.kv_heads) return;
+  AttnExact* a = reinterpret_cast<AttnExact*>(s->x);
+  const int warp = static_cast<int>(threadIdx.x / 32), lane = static_cast<int>(threadIdx.x % 32);
+  const DevLayer& L = m.layers[layer];
+  const uint32_t qw = m.q_heads * kHeadDim, kvw = m.kv_heads * kHeadDim, kv_groups = kvw / kGroup;
+  const uint32_t mp = m.max_positions, n = position + 1;
+  uint8_t* kl = P->k_cache + size_t(layer) * m.cache_layer_stride;
+  uint8_t* vl = P->v_cache + size_t(layer) * m.cache_layer_stride;
+  const int tid = static_cast<int>(threadIdx.x), j = tid / kHeadDim, d = tid % kHeadDim;
+  // 1. The pre-norm rows: queries 2h + j, and the new key (j = 0) or value (j = 1).
+  a->raw[j][d] = ld_cg(P->qkv + (2 * h + j) * kHeadDim + d);
+  a->raw[2 + j][d] = ld_cg(P->qkv + qw + size_t(j) * kvw + h * kHeadDim + d);
+  consumer_sync(kConsumerThreads);
+  // 2. QK-RMSNorm (decoder.zig:180-195): sequential sums on three warps.
+  if (tid == 0 || tid == 32 || tid == 64) {
+    a->inv[tid / 32] = rms_inverse(sum_squares_seq(a->raw[tid / 32], kHeadDim), kHeadDim, m.eps);
+  }
+  consumer_sync(kConsumerThreads);
+  a->rot[j][d] = __fmul_rn(__fmul_rn(a->raw[j][d], a->inv[j]), L.q_norm[d]);
+  if (j == 0) a->rot[2][d] = __fmul_rn(__fmul_rn(a->raw[2][d], a->inv[2]), L.k_norm[d]);
+  consumer_sync(kConsumerThreads);
+  // 3. RoPE at this position (kernels.zig:495-527).
+  const int pair = d % (kHeadDim / 2);
+  const float cs = m.rope_cos[size_t(position) * (kHeadDim / 2) + pair];
+  const float sn = m.rope_sin[size_t(position) * (kHeadDim / 2) + pair];
+  const float qr = rope_rn(d < kHeadDim / 2, a->rot[j][pair], a->rot[j][pair + kHeadDim / 2], cs, sn);
+  const float kr = j == 0 ? rope_rn(d < kHeadDim / 2, a->rot[2][pair], a->rot[2][pair + kHeadDim / 2], cs, sn) : 0.0f;
+  consumer_sync(kConsumerThreads);
+  a->rot[j][d] = qr;
+  if (j == 0) a->rot[2][d] = kr;
+  // 4. appendCacheRow (decoder.zig:68-106): the key (j = 0) and value
+  // (j = 1) rows as q8, one 64-value group per two warps (quant.zig:197-227).
+  {
+    const float val = j == 0 ? kr : a->raw[3][d];
+    const float amax = warp_max(fabsf(val));
+    if (lane == 0) a->amax[warp] = amax;
+    consumer_sync(kConsumerThreads);
+    const int gw = (warp / 2) * 2;
+    const __half sh = __float2half_rn(__fdiv_rn(fmaxf(a->amax[gw], a->amax[gw + 1]), 128.0f));
+    uint8_t* plane = j == 0 ? kl : vl;
+    plane[m.cache_scales_bytes + size_t(position) * kvw + h * kHeadDim + d] = q8_code(val, __half2float(sh));
+    if ((d % kGroup) == 0) {
+      reinterpret_cast<uint16_t*>(plane + size_t(position) * kv_groups * 2)[h * 2 + d / kGroup] = __half_as_ushort(sh);
+    }
+    // Later fast-mode tokens read this row through TMA (the async proxy).
+    fence_proxy_async_global();
+  }
+  consumer_sync(kConsumerThreads);  // the appended row is visible to this CTA's loads below
+  // 5. Scores (q8GroupDot, kernels.zig:636-661), both query heads per position.
+  float* sc0 = P->exact_scratch + size_t(2 * h) * 3 * mp;  // [3][mp]: scores / exp, value weights of groups 0, 1
+  float* sc1 = sc0 + size_t(3) * mp;
+  for (uint32_t p = tid; p < n; p += kConsumerThreads) {
+    const uint4* krow = reinterpret_cast<const uint4*>(kl + m.cache_scales_bytes + size_t(p) * kvw + h * kHeadDim);
+    const uint16_t* ks = reinterpret_cast<const uint16_t*>(kl + size_t(p) * kv_groups * 2) + h * 2;
+    float tot[2] = {0.0f, 0.0f};
+#pragma unroll 1
+    for (uint32_t g = 0; g < 2; ++g) {
+      const float scale = f16_bits_to_f32(ks[g]);
+      float lanes[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+#pragma unroll 1
+      for (int q = 0; q < 4; ++q) {
+        const uint4 w = krow[4 * g + q];
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            const float cv = __fadd_rn(bits_f32(__byte_perm(ws[e], kMagic, 0x7440 + b)), kNegQ8);
+            const uint32_t dim = 64 * g + 16 * q + 4 * e + b;
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) lanes[hh][b] = __fadd_rn(lanes[hh][b], __fmul_rn(cv, a->rot[hh][dim]));
+          }
+        }
+      }
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const float group = __fadd_rn(__fadd_rn(__fadd_rn(lanes[hh][0], lanes[hh][1]), lanes[hh][2]), lanes[hh][3]);
+        tot[hh] = __fadd_rn(tot[hh], __fmul_rn(group, scale));
+      }
+    }
+    sc0[p] = __fmul_rn(m.attn_scaling, tot[0]);
+    sc1[p] = __fmul_rn(m.attn_scaling, tot[1]);
+  }
+  consumer_sync(kConsumerThreads);
+  // 6. Row maxima (the order does not change a maximum).
+  {
+    float m0 = -INFINITY, m1 = -INFINITY;
+    for (uint32_t p = tid; p < n; p += kConsumerThreads) {
+      m0 = fmaxf(m0, sc0[p]);
+      m1 = fmaxf(m1, sc1[p]);
+    }
+    m0 = warp_max(m0);
+    m1 = warp_max(m1);
+    if (lane == 0) {
+      a->red[0][warp] = m0;
+      a->red[1][warp] = m1;
+    }
+    consumer_sync(kConsumerThreads);
+    m0 = -INFINITY;
+    m1 = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) {
+      m0 = fmaxf(m0, a->red[0][w]);
+      m1 = fmaxf(m1, a->red[1][w]);
+    }
+    // 7. exp(score - max) in place.
+    for (uint32_t p = tid; p < n; p += kConsumerThreads) {
+      sc0[p] = exp_ref(__fsub_rn(sc0[p], m0));
+      sc1[p] = exp_ref(__fsub_rn(sc1[p], m1));
+    }
+  }
+  consumer_sync(kConsumerThreads);
+  // 8. The sums in position order, then one reciprocal each.
+  if (tid == 0 || tid == 32) {
+    const float* e = tid == 0 ? sc0 : sc1;
+    float total = 0.0f;
+    uint32_t p = 0;
+    for (; p + 8 <= n; p += 8) {
+      float t[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) t[i] = e[p + i];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) total = __fadd_rn(total, t[i]);
+    }
+    for (; p < n; ++p) total = __fadd_rn(total, e[p]);
+    a->inv[tid / 32] = __fdiv_rn(1.0f, total);
+  }
+  consumer_sync(kConsumerThreads);
+  // 9. Value weights: scale of the position's value group times its
+  // probability (q8GroupAccumulate's scaled_weight), for both groups.
+  for (uint32_t q = tid; q < 2 * n; q += kConsumerThreads) {
+    const uint32_t hh = q / n, p = q % n;
+    float* sc = hh == 0 ? sc0 : sc1;
+    const float prob = __fmul_rn(sc[p], a->inv[hh]);
+    const uint16_t* vs = reinterpret_cast<const uint16_t*>(vl + size_t(p) * kv_groups * 2) + h * 2;
+    sc[mp + p] = __fmul_rn(f16_bits_to_f32(vs[0]), prob);
+    sc[2 * mp + p] = __fmul_rn(f16_bits_to_f32(vs[1]), prob);
+  }
+  consumer_sync(kConsumerThreads);
+  // 10. Output dimension d of query head 2h + j: the sum over positions in order.
+  {
+    const float* sw = (j == 0 ? sc0 : sc1) + size_t(1 + d / kGroup) * mp;
+    const uint8_t* vcol = vl + m.cache_scales_bytes + h * kHeadDim + d;
+    float out = 0.0f;
+    uint32_t p = 0;
+    for (; p + 8 <= n; p += 8) {
+      float cv[8], w[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        cv[i] = __fadd_rn(static_cast<float>(vcol[size_t(p + i) * kvw]), -128.0f);
+        w[i] = sw[p + i];
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) out = __fadd_rn(out, __fmul_rn(cv[i], w[i]));
+    }
+    for (; p < n; ++p) out = __fadd_rn(out, __fmul_rn(__fadd_rn(static_cast<float>(vcol[size_t(p) * kvw]), -128.0f), sw[p]));
+    P->attn_out[(2 * h + j) * kHeadDim + d] = out;
+  }
+  consumer_sync(kConsumerThreads);  // the activation buffer is reused by the next stage
+}
+
 // ---- the consumer program ----
 
+template <bool E>
 __device__ void run_consumers(const DecodeLaunch& P, Smem* s) {
   const DevModel& m = *reinterpret_cast<const DevModel*>(s->model);
   Ctx c{&P, &m, s, 0, 0, true, static_cast<int>(threadIdx.x / 32), static_cast<int>(threadIdx.x % 32),
@@ -1069,7 +1437,11 @@ __device__ void run_consumers(const DecodeLaunch& P, Smem* s) {
       if (st == kStAttn) {
         // -- attention over position + 1 cached rows (decoder.zig:216-253)
         trace_mark(c, e0);
-        attention_stage(c, l, position);
+        if constexpr (E) {
+          attention_stage_exact(&P, &m, s, l, position);
+        } else {
+          attention_stage(c, l, position);
+        }
       } else {
         const uint32_t lq = st == kStLM ? 0 : l;
         const uint32_t format = stage_format(m, lq, st);
@@ -1078,20 +1450,24 @@ __device__ void run_consumers(const DecodeLaunch& P, Smem* s) {
         // residual stream (decoder.zig:165-176, 259-262, 277-283), or the
         // attention output / SwiGLU activations; up reuses gate's input.
         if (st == kStQKV && l == 0) {
-          input_into_x(c, input, row, own, q4);
+          input_into_x<E>(c, input, row, own, q4);
         } else if (st == kStQKV || st == kStGate || st == kStLM) {
-          norm_global_into_x(c, P.hidden_g, m.hidden, q4);
+          norm_global_into_x<E>(c, P.hidden_g, m.hidden, q4);
         } else if (st == kStO) {
-          attention_into_x(c, P.attn_part, position / kAttnChunk + 1, q4);
+          if constexpr (E) {
+            load_x_global<E>(c, P.attn_out, m.q_heads * kHeadDim, q4);
+          } else {
+            attention_into_x(c, P.attn_part, position / kAttnChunk + 1, q4);
+          }
         } else if (st == kStDown) {
-          load_x_global(c, P.act, m.ffn, q4);
+          load_x_global<E>(c, P.act, m.ffn, q4);
         }
         trace_mark(c, e0);
         Piece pieces[3];
         const int np = stage_pieces(m, lq, st, blockIdx.x, gridDim.x, pieces);
         Best best{-INFINITY, 0xFFFFFFFFu};
         float* logits_out = (st == kStLM && P.logits_out && t + 1 == P.n_tokens) ? P.logits_out : nullptr;
-        gemv_stage(c, pieces, np, format, st == kStLM, best, logits_out);
+        gemv_stage<E>(c, pieces, np, format, st == kStLM, best, logits_out);
         // -- stage output
         if (st == kStQKV) {
           for (int p = 0; p < np; ++p) {
@@ -1113,8 +1489,13 @@ __device__ void run_consumers(const DecodeLaunch& P, Smem* s) {
           // SwiGLU (kernels.zig:233-239).
           for (uint32_t i = c.tid; i < fr.end - fr.begin; i += kConsumerThreads) {
             const float g = s->gate[i];
-            const float silu = g / (1.0f + expf(-g));
-            P.act[fr.begin + i] = silu * s->part[i];
+            if constexpr (E) {
+              const float silu = __fdiv_rn(g, __fadd_rn(1.0f, exp_ref(-g)));  // math.zig:69-71
+              P.act[fr.begin + i] = __fmul_rn(silu, s->part[i]);
+            } else {
+              const float silu = g / (1.0f + expf(-g));
+              P.act[fr.begin + i] = silu * s->part[i];
+            }
           }
         } else {
           // lm_head: this CTA's first maximum (decoder.zig:290-301).
@@ -1189,6 +1570,9 @@ __device__ void run_consumers(const DecodeLaunch& P, Smem* s) {
   }
 }
 
+// E = exact mode (DecodeLaunch::exact): a separate instantiation, so the
+// default kernel carries none of its code or register demands.
+template <bool E>
 __global__ void __launch_bounds__(kThreads, 1)
     decode_kernel(const __grid_constant__ DecodeLaunch P, const __grid_constant__ KvMaps maps) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -1199,6 +1583,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s->empty[i], kConsumerWarps);
     }
     fence_mbar_init();
+    s->abort = 0u;
   }
   static_assert(sizeof(DevModel) % 8 == 0, "the model description copies as 8-byte words");
   for (uint32_t i = threadIdx.x; i < sizeof(DevModel) / 8; i += blockDim.x) {
@@ -1208,7 +1593,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x >= kConsumerThreads) {
     run_producer(P, maps, s);
   } else {
-    run_consumers(P, s);
+    run_consumers<E>(P, s);
   }
 }
 
@@ -1224,13 +1609,14 @@ int decode_grid_size(int device) {
 
 int launch_decode(const DecodeLaunch& launch, const KvMaps& maps, int grid, void* stream) {
   const int smem = decode_kernel_smem_bytes();
-  cudaError_t e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  const void* fn = launch.exact ? reinterpret_cast<const void*>(decode_kernel<true>)
+                                : reinterpret_cast<const void*>(decode_kernel<false>);
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return static_cast<int>(e);
   DecodeLaunch copy = launch;
   KvMaps maps_copy = maps;
   void* args[] = {&copy, &maps_copy};
-  return static_cast<int>(cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(decode_kernel), dim3(grid),
-                                                      dim3(kThreads), args, static_cast<size_t>(smem),
+  return static_cast<int>(cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(kThreads), args, static_cast<size_t>(smem),
                                                       static_cast<cudaStream_t>(stream)));
 }
 

@@ -412,6 +412,89 @@ __device__ __forceinline__ void consumer_sync(uint32_t threads) {
   asm volatile("bar.sync 1, %0;" ::"r"(threads) : "memory");
 }
 
+// ---- arithmetic in the reference's order ----
+//
+// The reference's CPU path rounds every f32 product and sum separately (no
+// contraction into FMAs) and sums its reductions sequentially. The helpers
+// below use the _rn intrinsics, which nvcc never contracts, so code built on
+// them gives the same bits as that path on the same inputs.
+
+// exp of an f32 as the host C library's expf computes it: the table-driven
+// method of ARM's optimized-routines (Szabolcs Nagy, 2017; glibc >= 2.27
+// ships it, built with FMA on x86-64): x * 32 / ln 2 = k + r rounded to the
+// nearest integer k, exp(x) = 2^(k/32) * p(r) with p a cubic in double, the
+// 2^(i/32) factors from a 32-entry table. The table entries are the doubles
+// nearest 2^(i/32), minus i << 47 so that adding k << 47 forms 2^(k/32).
+// The CPU oracle calls that expf, and this restatement was checked against it
+// on every non-NaN f32 input.
+__device__ __forceinline__ float exp_ref(float x) {
+  constexpr double kInvLn2N = 0x1.71547652b82fep+0 * 32;
+  constexpr double kShift = 0x1.8p+52;
+  constexpr double kC0 = 0x1.c6af84b912394p-5 / 32 / 32 / 32;
+  constexpr double kC1 = 0x1.ebfce50fac4f3p-3 / 32 / 32;
+  constexpr double kC2 = 0x1.62e42ff0c52d6p-1 / 32;
+  static constexpr uint64_t kTab[32] = {
+      0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
+      0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
+      0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
+      0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull,
+      0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull,
+      0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,
+      0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
+      0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull,
+  };
+  const uint32_t bits = __float_as_uint(x);
+  const uint32_t abstop = (bits >> 20) & 0x7FFu;
+  if (abstop >= 0x42Bu) {  // |x| >= 88, or not finite
+    if (bits == 0xFF800000u) return 0.0f;                 // exp(-inf)
+    if (abstop >= 0x7F8u) return x + x;                   // +inf, NaN
+    if (x > 0x1.62e42ep6f) return __int_as_float(0x7F800000);  // overflow: log(2^128) ~ 88.72
+    if (x < -0x1.9fe368p6f) return 0.0f;                  // underflow: log(2^-150) ~ -103.97
+  }
+  const double xd = static_cast<double>(x);
+  double kd = __fma_rn(kInvLn2N, xd, kShift);
+  const uint64_t ki = static_cast<uint64_t>(__double_as_longlong(kd));
+  kd = __dsub_rn(kd, kShift);
+  const double r = __fma_rn(kInvLn2N, xd, -kd);
+  const uint64_t t = kTab[ki % 32] + (ki << 47);
+  const double s = __longlong_as_double(static_cast<long long>(t));
+  const double z = __fma_rn(kC0, r, kC1);
+  const double r2 = __dmul_rn(r, r);
+  double y = __fma_rn(kC2, r, 1.0);
+  y = __fma_rn(z, r2, y);
+  y = __dmul_rn(y, s);
+  return __double2float_rn(y);
+}
+
+// 1 / sqrt(mean_square + eps) with mean_square = sum / width
+// (math.zig:120-130): every step correctly rounded.
+__device__ __forceinline__ float rms_inverse(float sum_squares, uint32_t width, float eps) {
+  const float mean = __fdiv_rn(sum_squares, static_cast<float>(width));
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+}
+
+// sum_squares over n values in order (math.zig:123): s = s + v * v, each
+// product and sum rounded. `v` is read from shared or global memory.
+__device__ __forceinline__ float sum_squares_seq(const float* v, uint32_t n) {
+  float s = 0.0f;
+  uint32_t i = 0;
+  for (; i + 8 <= n; i += 8) {
+    float t[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) t[e] = v[i + e];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s = __fadd_rn(s, __fmul_rn(t[e], t[e]));
+  }
+  for (; i < n; ++i) s = __fadd_rn(s, __fmul_rn(v[i], v[i]));
+  return s;
+}
+
+// rotate_half RoPE of one element (kernels.zig:519-520): dims below half take
+// lo * cos - hi * sin, the others hi * cos + lo * sin; products rounded first.
+__device__ __forceinline__ float rope_rn(bool low_half, float lo, float hi, float cs, float sn) {
+  return low_half ? __fsub_rn(__fmul_rn(lo, cs), __fmul_rn(hi, sn)) : __fadd_rn(__fmul_rn(hi, cs), __fmul_rn(lo, sn));
+}
+
 // quant.zig:280-288 for q8 (bias 128): round half away from zero against the
 // stored f16 scale, then clamp into [-128, 127].
 __device__ __forceinline__ uint8_t q8_code(float value, float stored_scale) {

@@ -113,6 +113,12 @@ struct DecodeLaunch {
   int32_t* error;            // nonzero after a bounded wait gave up
   uint64_t timeout_ns;
   uint32_t max_chunks;
+  // Nonzero: every f32 operation in the reference's order (QWC_OPTION_EXACT):
+  // sequential dot-product lanes and sums of squares, whole-history
+  // attention per kv head, the host C library's exp. exact_scratch holds the
+  // attention scores and value weights, [q_heads][3][max_positions] floats.
+  uint32_t exact;
+  float* exact_scratch;
   // Optional phase timeline: when non-null, thread 0 of every CTA stores
   // %globaltimer at each phase boundary of token `trace_token` into
   // trace[cta * kTraceEvents + event].
@@ -179,6 +185,7 @@ struct StreamsStep {
   uint8_t* k_cache;
   uint8_t* v_cache;
   float* logits;                 // [slot][vocab]
+  float* qkv_rows;               // [slot][q width + 2 kv width]: the last layer's pre-norm q/k/v rows of the step
   uint32_t* tokens;              // [slot]
   int32_t* error;
   uint32_t max_chunks;

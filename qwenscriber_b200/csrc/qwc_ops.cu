@@ -190,6 +190,15 @@ __device__ __forceinline__ bool better(float v, uint32_t i, float bv, uint32_t b
   return v > bv || (v == bv && i < bi);
 }
 
+// decoder.zig:290-301 seeds the maximum with values[0] and replaces it only on
+// a strict `>`: a NaN at index 0 is never replaced, a NaN elsewhere never
+// wins. Ranking a NaN at index 0 as +inf (ties go to the lowest index) and
+// letting every other NaN lose all comparisons gives that answer from any
+// reduction order.
+__device__ __forceinline__ float argmax_key(float v, uint32_t i) {
+  return (i == 0 && v != v) ? __int_as_float(0x7F800000) : v;
+}
+
 // Pass 1: each block reduces a contiguous range to (max, first index).
 __global__ void argmax_partial_kernel(const float* values, uint32_t count, ArgmaxPartial* partial) {
   __shared__ float sv[32];
@@ -200,7 +209,7 @@ __global__ void argmax_partial_kernel(const float* values, uint32_t count, Argma
   float bv = -INFINITY;
   uint32_t bi = 0xFFFFFFFFu;
   for (uint32_t i = begin + threadIdx.x; i < end; i += blockDim.x) {
-    const float v = values[i];
+    const float v = argmax_key(values[i], i);
     if (better(v, i, bv, bi)) {
       bv = v;
       bi = i;
@@ -251,18 +260,17 @@ __global__ void argmax_final_kernel(const ArgmaxPartial* partial, uint32_t n, ui
   if (threadIdx.x == 0) *out = bi == 0xFFFFFFFFu ? 0u : bi;
 }
 
+// math.zig:120-130 as written: the sum of squares in index order (one
+// thread), then value * inverse_rms * weight with each product rounded.
 __global__ void rmsnorm_kernel(const float* x, const float* w, uint32_t width, float eps, float* out) {
-  __shared__ float red[32];
+  __shared__ float inv_s;
   const float* row = x + size_t(blockIdx.x) * width;
-  float ss = 0.0f;
-  for (uint32_t i = threadIdx.x; i < width; i += blockDim.x) ss = fmaf(row[i], row[i], ss);
-  ss = warp_sum(ss);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = ss;
+  if (threadIdx.x == 0) inv_s = rms_inverse(sum_squares_seq(row, width), width, eps);
   __syncthreads();
-  float total = 0.0f;
-  for (uint32_t i = 0; i < blockDim.x / 32; ++i) total += red[i];
-  const float inv = 1.0f / sqrtf(total / static_cast<float>(width) + eps);
-  for (uint32_t i = threadIdx.x; i < width; i += blockDim.x) out[size_t(blockIdx.x) * width + i] = row[i] * inv * w[i];
+  const float inv = inv_s;
+  for (uint32_t i = threadIdx.x; i < width; i += blockDim.x) {
+    out[size_t(blockIdx.x) * width + i] = __fmul_rn(__fmul_rn(row[i], inv), w[i]);
+  }
 }
 
 __global__ void rope_kernel(float* x, uint32_t heads, uint32_t head_dim, const float* cos_t, const float* sin_t,
@@ -274,15 +282,15 @@ __global__ void rope_kernel(float* x, uint32_t heads, uint32_t head_dim, const f
     float* row = x + size_t(h) * head_dim;
     const float lo = row[i], hi = row[i + half];
     const float c = cos_t[size_t(position) * half + i], s = sin_t[size_t(position) * half + i];
-    row[i] = lo * c - hi * s;
-    row[i + half] = hi * c + lo * s;
+    row[i] = rope_rn(true, lo, hi, c, s);
+    row[i + half] = rope_rn(false, lo, hi, c, s);
   }
 }
 
 __global__ void silu_mul_kernel(const float* gate, const float* up, uint32_t n, float* out) {
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const float g = gate[i];
-    out[i] = g / (1.0f + expf(-g)) * up[i];
+    out[i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, exp_ref(-g))), up[i]);  // math.zig:69-71, kernels.zig:233-239
   }
 }
 

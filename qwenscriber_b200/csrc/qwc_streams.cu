@@ -208,36 +208,37 @@ __global__ void __launch_bounds__(256) streams_qkv_kernel(const StreamsStep P, u
   const size_t stride = size_t(kMaxStreams) * rows;
   const float qraw = sum_splits<8>(row + (2 * h + j) * kHeadDim + dd, stride, splits);
   const float kvraw = sum_splits<8>(row + qw + j * kvw + h * kHeadDim + dd, stride, splits);
+  if (layer + 1 == m.n_layers) {
+    // Kept for qwc_debug_scratch: the inputs of this step's last append.
+    P.qkv_rows[size_t(s) * rows + (2 * h + j) * kHeadDim + dd] = qraw;
+    P.qkv_rows[size_t(s) * rows + qw + j * kvw + h * kHeadDim + dd] = kvraw;
+  }
   const DevLayer& L = m.layers[layer];
-  const float ss = warp_sum(qraw * qraw), kss = warp_sum(kvraw * kvraw);
-  if (lane == 0) {
-    red[warp] = ss;
-    red[8 + warp] = kss;
+  // QK-RMSNorm (math.zig:120-130): sums of squares in dimension order on one
+  // thread per head (different warps), each product rounded, so the appended
+  // key row equals the reference's on the same pre-norm values.
+  tq[j][dd] = qraw;
+  if (j == 0) tk[dd] = kvraw;
+  __syncthreads();
+  if (tid == 0 || tid == 32 || tid == 64) {
+    const float* v = tid == 64 ? tk : tq[tid / 32];
+    red[tid / 32] = rms_inverse(sum_squares_seq(v, kHeadDim), kHeadDim, m.eps);
   }
   __syncthreads();
-  const int w0 = j * 4;
-  const float total = ((red[w0] + red[w0 + 1]) + red[w0 + 2]) + red[w0 + 3];
-  const float inv = 1.0f / sqrtf(total / static_cast<float>(kHeadDim) + m.eps);
-  tq[j][dd] = qraw * inv * L.q_norm[dd];
-  if (j == 0) {
-    const float kt = ((red[8] + red[9]) + red[10]) + red[11];
-    const float kinv = 1.0f / sqrtf(kt / static_cast<float>(kHeadDim) + m.eps);
-    tk[dd] = kvraw * kinv * L.k_norm[dd];
-  }
+  const float qn = __fmul_rn(__fmul_rn(qraw, red[j]), L.q_norm[dd]);
+  const float kn = j == 0 ? __fmul_rn(__fmul_rn(kvraw, red[2]), L.k_norm[dd]) : 0.0f;
+  __syncthreads();
+  tq[j][dd] = qn;
+  if (j == 0) tk[dd] = kn;
   __syncthreads();
   const int pair = dd % (kHeadDim / 2);
   const float* cos_row = m.rope_cos + size_t(d.position) * (kHeadDim / 2);
   const float* sin_row = m.rope_sin + size_t(d.position) * (kHeadDim / 2);
   const float cs = cos_row[pair], sn = sin_row[pair];
-  {
-    const float lo = tq[j][pair], hi = tq[j][pair + kHeadDim / 2];
-    P.qrot[size_t(s) * qw + (2 * h + j) * kHeadDim + dd] = dd < kHeadDim / 2 ? lo * cs - hi * sn : hi * cs + lo * sn;
-  }
+  P.qrot[size_t(s) * qw + (2 * h + j) * kHeadDim + dd] =
+      rope_rn(dd < kHeadDim / 2, tq[j][pair], tq[j][pair + kHeadDim / 2], cs, sn);
   float val = kvraw;
-  if (j == 0) {
-    const float lo = tk[pair], hi = tk[pair + kHeadDim / 2];
-    val = dd < kHeadDim / 2 ? lo * cs - hi * sn : hi * cs + lo * sn;
-  }
+  if (j == 0) val = rope_rn(dd < kHeadDim / 2, tk[pair], tk[pair + kHeadDim / 2], cs, sn);
   // q8 row (quant.zig:197-227): groups of 64 values, two warps each.
   const float amax = warp_max(fabsf(val));
   __syncthreads();
@@ -684,7 +685,9 @@ __global__ void __launch_bounds__(1024) streams_argmax_kernel(const StreamsStep 
 #pragma unroll
     for (uint32_t r = 0; r < kUnroll; ++r) {
       const uint32_t i = i0 + r * blockDim.x;
-      v[r] = i < vocab ? row[i] : -INFINITY;
+      // decoder.zig:290-301: a NaN logit 0 wins (ranked +inf), other NaNs lose every comparison.
+      const float x = i < vocab ? row[i] : -INFINITY;
+      v[r] = (i == 0 && x != x) ? __int_as_float(0x7F800000) : x;
     }
 #pragma unroll
     for (uint32_t r = 0; r < kUnroll; ++r) {

@@ -239,12 +239,16 @@ def test_state_machine_and_limits(gpu, cuda_lib):
     m.close()
 
 
-def test_cfg0_greedy_tokens_identical(gpu, cuda_lib, oracle_lib):
-    """0.6B, q8 weights N(0, 0.02) seed 0, 188 audio rows + 8 ids, q8 cache, 64 greedy tokens."""
+def test_cfg0_default_path_teacher_forced_logits(gpu, cuda_lib, oracle_lib):
+    """configs[0] through the default (fast) kernel: 0.6B, q8 weights N(0, 0.02)
+    seed 0, 188 audio rows + 8 ids, q8 cache, 64 greedy tokens. The default
+    path sums its dot products in a different order from the reference, so
+    this is a tolerance check (logits within 2e-2, cosine >= 0.9999 at every
+    step), run teacher-forced: where the top-two logits are closer than the
+    logit error, the oracle's token is forced and counted. The north star's
+    identical-greedy-ids bar is met by QWC_OPTION_EXACT, free-running
+    (tests/test_gpu_exact.py)."""
     w = synthetic.workloads()["cfg0_0p6b_q8_b1"]
     model = synthetic.make_model(w.config, w.fmt, w.seed)
     prompt = synthetic.make_prompt(w.config, w.audio_rows, w.text_ids, w.seed)
-    # Random weights leave top-2 logit margins far below the logit tolerance,
-    # so a handful of near-tie steps may pick the other candidate; each is
-    # reported with its margin and the run continues teacher-forced.
     _run_parity(model, prompt, steps=w.decode, check_kv=True, max_near_ties=3, deep=True)

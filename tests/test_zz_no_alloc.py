@@ -32,18 +32,38 @@ def test_noalloc_argmax_matches_allocating_argmax_on_consecutive_calls(gpu, cuda
     out_ref = torch.full((1,), -1, dtype=torch.int32, device=gpu)
     out_new = torch.full((1,), -1, dtype=torch.int32, device=gpu)
 
-    # First call: a vocabulary-sized row with a tie; the lowest index must win.
-    first = rng.standard_normal(151936).astype(np.float32)
-    first[120000] = first[4321] = 9.5
+    # First call: every one of the 512 partials in use, a tie (the lowest index
+    # must win) and the row's maximum in one of the last partials.
+    first = rng.standard_normal(512 * 8192 // 4).astype(np.float32)
+    first[1000000] = first[900000] = 100.0
     ref1, new1 = _argmax_both(torch, cuda_lib, first, out_ref, out_new)
-    assert ref1 == new1 == 4321
+    assert ref1 == new1 == 900000
 
-    # Second call in a row, smaller and with its maximum late in the row, so
-    # stale partials from the first call would show up as a wrong index.
+    # Second call in a row, with 12 partials and a smaller maximum: a pass
+    # that read the first call's partials left in the scratch would return
+    # 900000 instead.
     second = rng.standard_normal(3000).astype(np.float32)
     second[2999] = 50.0
     ref2, new2 = _argmax_both(torch, cuda_lib, second, out_ref, out_new)
     assert ref2 == new2 == 2999
+
+    # Third call, as many partials as the first again, maximum near the end.
+    third = rng.standard_normal(first.size).astype(np.float32)
+    third[first.size - 3] = 60.0
+    ref3, new3 = _argmax_both(torch, cuda_lib, third, out_ref, out_new)
+    assert ref3 == new3 == first.size - 3
+
+    # The call allocates nothing: device-wide free memory and torch's pool
+    # are unchanged across it (its set-up ran in the calls above).
+    dv = torch.from_numpy(third).cuda()
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    torch_bytes0 = torch.cuda.memory_allocated()
+    assert cuda_lib.qwc_op_argmax_noalloc(dv.data_ptr(), third.size, out_new.data_ptr(), None) == 0
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0 and torch.cuda.memory_allocated() == torch_bytes0
+    assert int(out_new.item()) == first.size - 3
 
     # The largest accepted count (every scratch partial in use), then one more value.
     top = rt.ARGMAX_NOALLOC_MAX_COUNT
