@@ -140,7 +140,13 @@ enum {
    * grid barriers, split-K counters), in microseconds; 0 restores the default
    * (4 s single-stream, 2 s batched). A wait that runs out makes the call
    * return QWC_INVALID_STATE instead of hanging; the handle stays usable. */
-  QWC_OPTION_WAIT_LIMIT_US = 7
+  QWC_OPTION_WAIT_LIMIT_US = 7,
+  /* Failure-path testing, single-stream handles. Nonzero: the next launch of
+   * the decode kernel (only that one) makes its grid barriers wait for one
+   * more CTA than the launch has, so they can only end when their bound
+   * (QWC_OPTION_WAIT_LIMIT_US) runs out, and the call returns
+   * QWC_INVALID_STATE. No device fault is involved. */
+  QWC_OPTION_TEST_STALL = 8
 };
 
 /* ---- version and lifecycle (src/wasm/exports.zig:49-120) ---- */
@@ -176,8 +182,8 @@ int32_t qwc_model_add_tensor(uint32_t handle, uint32_t kind, uint32_t layer, uin
  * projector) are validated and not kept. A shard whose payload checksum
  * matches one already added, or a tensor already added, is invalid_argument; a decoder tensor in a
  * format the kernels do not run (f16, bf16) is unsupported_model; more
- * than 64 shards is limit_exceeded. A shard refused by any of these checks
- * leaves the handle unchanged. */
+ * than 64 shards is limit_exceeded. A shard refused by any of these checks, or whose copy to
+ * the device fails part way (out_of_memory), leaves the handle unchanged. */
 int32_t qwc_model_add_shard(uint32_t handle, const void* bytes, uint64_t len);
 /* container.File.parse followed by verifyChecksum on its own: no handle and
  * no device. Returns QWC_OK (and the tensor count) or the status the shard
@@ -196,13 +202,14 @@ int32_t qwc_model_set_streams(uint32_t handle, uint32_t streams);
 int32_t qwc_model_finish(uint32_t handle, const void* config, uint32_t config_len);
 /* qw_model_requirements (exports.zig:371-378). */
 int32_t qwc_model_requirements(uint32_t handle, qwc_requirements* out);
-/* qw_model_tensor_count (exports.zig:384-389): tensors held by the loaded model. */
+/* qw_model_tensor_count (exports.zig:384-389, model.zig:265-279): every entry of every shard
+ * added, audio-tower and projector tensors included, plus each tensor added alone. */
 int32_t qwc_model_tensor_count(uint32_t handle, uint32_t* out);
-/* qw_model_tensor_descriptor (exports.zig:402-412, model.zig:281-319): where tensor `index` of
- * the loaded model came from and its shape, in the order tensors were added (a shard's in its
- * index order). It describes the tensors this library keeps, the decoder's: a shard's other
- * tensors are validated and not kept, so they are neither counted nor described. QWC_NOT_FOUND
- * past the last tensor, QWC_INVALID_STATE before qwc_model_finish. */
+/* qw_model_tensor_descriptor (exports.zig:402-412, model.zig:281-319): entry `index` of that
+ * enumeration -- shards in the order they were added, each shard's entries in its index order,
+ * then tensors added alone in call order -- with its offset within its shard's bytes, length,
+ * shape and shard. Entries the decoder does not use are described though not kept on the device.
+ * QWC_NOT_FOUND past the last entry, QWC_INVALID_STATE before qwc_model_finish. */
 int32_t qwc_model_tensor_descriptor(uint32_t handle, uint32_t index, qwc_tensor_descriptor* out);
 
 /* ---- decode family, stream slot 0 (src/wasm/exports.zig:440-497; model.zig:370-474) ---- */

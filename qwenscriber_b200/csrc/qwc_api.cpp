@@ -202,10 +202,9 @@ struct Tensor {
   uint32_t kind, layer, format, rows, cols;
   std::unique_ptr<DevBuf> buf;
   uint64_t scales_offset = 0, codes_offset = 0;
-  // Its qwc_model_tensor_descriptor: source offset and length, shape as the
-  // container records it, and the shard it came from (0xFFFFFFFF if added alone).
-  uint64_t src_offset = 0, src_len = 0;
-  uint32_t rank = 2, dims[4] = {1, 1, 1, 1}, shard_index = 0xFFFFFFFFu;
+  // Its payload length and shape as the caller described them.
+  uint64_t src_len = 0;
+  uint32_t rank = 2, dims[4] = {1, 1, 1, 1};
 };
 
 struct StreamSlot {
@@ -269,10 +268,15 @@ struct Handle {
   bool prefill_serial = false;  // QWC_OPTION_PREFILL_SERIAL
   bool exact = false;           // QWC_OPTION_EXACT
   uint64_t wait_limit_ns = 0;   // QWC_OPTION_WAIT_LIMIT_US (0: the defaults)
+  bool test_stall = false;      // QWC_OPTION_TEST_STALL (applies to the next launch only)
   uint32_t step_chunk = 16;
   uint64_t launches = 0;
   std::map<std::pair<uint32_t, uint32_t>, Tensor> tensors;
-  std::vector<std::pair<uint32_t, uint32_t>> tensor_order;  // keys of `tensors` in the order they were added
+  // qwc_model_tensor_descriptor's enumeration (src/wasm/model.zig:265-319):
+  // every entry of every shard, shards in the order they were added and each
+  // shard's entries in index order, audio-tower and projector tensors
+  // included; a tensor added alone follows in call order.
+  std::vector<qwc_tensor_descriptor> descriptors;
   Config config{};
   int grid = 0;
   DevModel host_model{};
@@ -326,7 +330,7 @@ int32_t status_of(cudaError_t e) {
 
 void release_model(Handle* h) {
   h->tensors.clear();
-  h->tensor_order.clear();
+  h->descriptors.clear();
   h->shards.clear();
   for (DevBuf* b : {&h->model_buf, &h->rope_cos, &h->rope_sin, &h->k_cache, &h->v_cache, &h->qkv, &h->attn_out,
                     &h->hidden_g, &h->act, &h->attn_part, &h->attn_count, &h->amax_val, &h->amax_idx, &h->barrier,
@@ -487,6 +491,9 @@ int32_t finish_model(Handle* h, const Config& c) {
       return QWC_UNSUPPORTED_MODEL;
     }
   }
+  // The batched engine's tensor-core GEMM reads q4 and q8 blocks only: a
+  // model with q5 matrices runs one stream (refused before any allocation).
+  if (any_q5 && h->streams > 1) return QWC_UNSUPPORTED_MODEL;
 
   cudaSetDevice(h->device);
   h->grid = decode_grid_size(h->device);
@@ -575,10 +582,7 @@ int32_t finish_model(Handle* h, const Config& c) {
   // decode steps. Its tensor-core GEMM reads q4 and q8 blocks only; a model
   // with q5 matrices runs one stream through the persistent kernel, and its
   // prompts prefill token by token there.
-  if (any_q5) {
-    if (h->streams > 1) return QWC_UNSUPPORTED_MODEL;
-    return QWC_OK;
-  }
+  if (any_q5) return QWC_OK;
   QWC_TRY(build_batched(h));
   return QWC_OK;
 }
@@ -614,6 +618,8 @@ int32_t run_decode(Handle* h, uint32_t n_tokens, uint32_t first_position, uint32
   L.error = h->error.as<int32_t>();
   L.timeout_ns = h->wait_limit_ns ? h->wait_limit_ns : kDecodeWaitNs;
   L.exact = h->exact ? 1u : 0u;
+  L.stall = h->test_stall ? 1u : 0u;
+  h->test_stall = false;
   L.exact_scratch = h->exact_scratch.as<float>();
   if (h->trace) {
     if (h->trace_buf.bytes == 0) QWC_TRY(h->trace_buf.alloc(size_t(h->grid) * kTraceEvents * 8));
@@ -1188,6 +1194,7 @@ int32_t qwc_set_option(uint32_t handle, uint32_t option, uint32_t value) {
     case QWC_OPTION_TRACE: h->trace = value != 0; return QWC_OK;
     case QWC_OPTION_PREFILL_SERIAL: h->prefill_serial = value != 0; return QWC_OK;
     case QWC_OPTION_EXACT: h->exact = value != 0; return QWC_OK;
+    case QWC_OPTION_TEST_STALL: h->test_stall = value != 0; return QWC_OK;
     case QWC_OPTION_WAIT_LIMIT_US:
       h->wait_limit_ns = uint64_t(value) * 1000ull;
       if (h->batched) {
@@ -1217,10 +1224,13 @@ int32_t qwc_model_begin(uint32_t handle) {
   return QWC_OK;
 }
 
-int32_t qwc_model_add_tensor(uint32_t handle, uint32_t kind, uint32_t layer, uint32_t format, uint32_t rows,
-                             uint32_t cols, const void* payload, uint64_t len) {
-  Handle* h = lookup(handle);
-  if (!h) return QWC_INVALID_ARGUMENT;
+}  // extern "C"
+
+namespace {
+
+// Copies one tensor's payload to the device and records it under (kind, layer).
+int32_t add_tensor(Handle* h, uint32_t kind, uint32_t layer, uint32_t format, uint32_t rows, uint32_t cols,
+                   const void* payload, uint64_t len) {
   if (h->state != State::kReady) return QWC_INVALID_STATE;
   if (!payload || rows == 0 || cols == 0) return QWC_INVALID_ARGUMENT;
   if (kind < QWC_KIND_DECODER_EMBED_TOKENS || kind > QWC_KIND_DECODER_DOWN) return QWC_UNSUPPORTED_MODEL;
@@ -1256,7 +1266,29 @@ int32_t qwc_model_add_tensor(uint32_t handle, uint32_t kind, uint32_t layer, uin
   t.dims[0] = t.rank == 1 ? cols : rows;
   if (t.rank == 2) t.dims[1] = cols;
   h->tensors.emplace(std::make_pair(kind, layer), std::move(t));
-  h->tensor_order.emplace_back(kind, layer);
+  return QWC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t qwc_model_add_tensor(uint32_t handle, uint32_t kind, uint32_t layer, uint32_t format, uint32_t rows,
+                             uint32_t cols, const void* payload, uint64_t len) {
+  Handle* h = lookup(handle);
+  if (!h) return QWC_INVALID_ARGUMENT;
+  QWC_TRY(add_tensor(h, kind, layer, format, rows, cols, payload, len));
+  const Tensor& t = h->tensors.at({kind, layer});
+  qwc_tensor_descriptor d{};
+  d.offset_bytes = 0;
+  d.len_bytes = t.src_len;
+  d.kind = kind;
+  d.layer = layer;
+  d.format = format;
+  d.rank = t.rank;
+  for (int i = 0; i < 4; ++i) d.dims[i] = t.dims[i];
+  d.shard_index = 0xFFFFFFFFu;
+  h->descriptors.push_back(d);
   return QWC_OK;
 }
 
@@ -1289,19 +1321,39 @@ int32_t qwc_model_add_shard(uint32_t handle, const void* bytes, uint64_t len) {
     if (!vec && !mat) return QWC_UNSUPPORTED_MODEL;
     if (h->tensors.count({e.kind, e.layer})) return QWC_INVALID_ARGUMENT;  // DuplicateTensor
   }
+  // A copy that fails part way (out of device memory) takes back the
+  // tensors this shard added, so the handle is as it was and the same shard
+  // may be added again.
+  std::vector<std::pair<uint32_t, uint32_t>> added;
+  const uint64_t weight_bytes0 = h->weight_bytes;
   for (uint32_t i = 0; i < v.count; ++i) {
     const ShardEntry e = shard_entry(v, i);
     if (!decoder_kind(e.kind)) continue;
     const uint32_t rows = e.rank == 1 ? 1u : e.dims[0];
     const uint32_t cols = e.rank == 1 ? e.dims[0] : e.dims[1];
-    QWC_TRY(qwc_model_add_tensor(handle, e.kind, e.layer, e.format, rows, cols, v.payload + e.offset_bytes,
-                                 e.len_bytes));
-    // model.zig:298-310: the offset within the shard's bytes, the entry's shape.
-    Tensor& t = h->tensors.at({e.kind, e.layer});
-    t.src_offset = uint64_t(v.payload - v.bytes) + e.offset_bytes;
-    t.rank = e.rank;
-    for (int d = 0; d < 4; ++d) t.dims[d] = e.dims[d];
-    t.shard_index = static_cast<uint32_t>(h->shards.size());
+    const int32_t st = add_tensor(h, e.kind, e.layer, e.format, rows, cols, v.payload + e.offset_bytes, e.len_bytes);
+    if (st != QWC_OK) {
+      for (const auto& key : added) h->tensors.erase(key);
+      h->weight_bytes = weight_bytes0;
+      return st;
+    }
+    added.emplace_back(e.kind, e.layer);
+  }
+  // model.zig:298-310: one descriptor per entry, the offset absolute within
+  // the shard's bytes.
+  const uint32_t shard_index = static_cast<uint32_t>(h->shards.size());
+  for (uint32_t i = 0; i < v.count; ++i) {
+    const ShardEntry e = shard_entry(v, i);
+    qwc_tensor_descriptor d{};
+    d.offset_bytes = uint64_t(v.payload - v.bytes) + e.offset_bytes;
+    d.len_bytes = e.len_bytes;
+    d.kind = e.kind;
+    d.layer = e.layer;
+    d.format = e.format;
+    d.rank = e.rank;
+    for (int k = 0; k < 4; ++k) d.dims[k] = e.dims[k];
+    d.shard_index = shard_index;
+    h->descriptors.push_back(d);
   }
   h->shards.push_back(v.checksum);
   return QWC_OK;
@@ -1381,7 +1433,7 @@ int32_t qwc_model_tensor_count(uint32_t handle, uint32_t* out) {
   Handle* h = lookup(handle);
   if (!h || !out) return QWC_INVALID_ARGUMENT;
   if (h->state != State::kLoaded) return QWC_INVALID_STATE;
-  *out = static_cast<uint32_t>(h->tensors.size());
+  *out = static_cast<uint32_t>(h->descriptors.size());
   return QWC_OK;
 }
 
@@ -1391,18 +1443,8 @@ int32_t qwc_model_tensor_descriptor(uint32_t handle, uint32_t index, qwc_tensor_
   Handle* h = lookup(handle);
   if (!h || !out) return QWC_INVALID_ARGUMENT;
   if (h->state != State::kLoaded) return QWC_INVALID_STATE;
-  if (index >= h->tensor_order.size()) return QWC_NOT_FOUND;  // model.zig:318
-  const Tensor& t = h->tensors.at(h->tensor_order[index]);
-  qwc_tensor_descriptor d{};
-  d.offset_bytes = t.src_offset;
-  d.len_bytes = t.src_len;
-  d.kind = t.kind;
-  d.layer = t.layer;
-  d.format = t.format;
-  d.rank = t.rank;
-  for (int i = 0; i < 4; ++i) d.dims[i] = t.dims[i];
-  d.shard_index = t.shard_index;
-  *out = d;
+  if (index >= h->descriptors.size()) return QWC_NOT_FOUND;  // model.zig:318
+  *out = h->descriptors[index];
   return QWC_OK;
 }
 

@@ -401,7 +401,7 @@ __device__ void grid_barrier(Ctx& c) {
     c.s->flag = 1u;
   } else if (c.tid == 0) {
     c.barriers += 1;
-    const uint32_t target = c.barriers * gridDim.x;
+    const uint32_t target = c.barriers * gridDim.x + c.P->stall;
     const uint64_t arrive = c.tracing ? global_timer_ns() : 0;
     // The release is cumulative: it publishes every write the CTA's threads
     // made before the bar.sync above.

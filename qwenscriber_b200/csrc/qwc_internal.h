@@ -119,6 +119,10 @@ struct DecodeLaunch {
   // attention scores and value weights, [q_heads][3][max_positions] floats.
   uint32_t exact;
   float* exact_scratch;
+  // Failure-path testing (QWC_OPTION_TEST_STALL): added to every grid
+  // barrier's target, so with 1 the barriers wait for a CTA that does not
+  // exist and end only when their bound runs out.
+  uint32_t stall;
   // Optional phase timeline: when non-null, thread 0 of every CTA stores
   // %globaltimer at each phase boundary of token `trace_token` into
   // trace[cta * kTraceEvents + event].

@@ -32,7 +32,7 @@ STATUS_CODE = {name: code for code, name in STATUS.items()}
 
 CACHE_F32, CACHE_Q8 = 0, 1
 OPTION_IGNORE_EOS, OPTION_KEEP_LOGITS, OPTION_STEP_CHUNK, OPTION_TRACE, OPTION_PREFILL_SERIAL = 1, 2, 3, 4, 5
-OPTION_EXACT, OPTION_WAIT_LIMIT_US = 6, 7
+OPTION_EXACT, OPTION_WAIT_LIMIT_US, OPTION_TEST_STALL = 6, 7, 8
 FEATURE_MODEL, FEATURE_DECODE, FEATURE_STREAMS = 1 << 3, 1 << 4, 1 << 8
 LIMIT_EXCEEDED = -9
 UNSUPPORTED_MODEL = -13

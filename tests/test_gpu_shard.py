@@ -89,3 +89,66 @@ def test_shard_refusals(gpu, cuda_lib):
         assert gm.tensor_count() == len(model.tensors)
     finally:
         gm.close()
+
+
+def _index(shard_bytes: bytes, shard_index: int) -> list[dict]:
+    """The descriptors src/wasm/model.zig:281-319 reports for one shard: its
+    entries in index order, offsets absolute within the shard's bytes."""
+    import struct
+
+    _, _, index_len, payload_offset, _, count, _ = struct.unpack_from("<8sIIIIII", shard_bytes, 0)
+    out = []
+    for i in range(count):
+        kind, layer, fmt, rank, _, d0, d1, d2, d3, off, length = struct.unpack_from("<HHBBH4IQQ", shard_bytes,
+                                                                                    32 + 40 * i)
+        out.append({"offset_bytes": payload_offset + off, "len_bytes": length, "kind": kind, "layer": layer,
+                    "format": fmt, "rank": rank, "dims": (d0, d1, d2, d3), "shard_index": shard_index})
+    return out
+
+
+def test_tensor_descriptors_enumerate_every_shard_entry(gpu, cuda_lib):
+    """qw_model_tensor_count/descriptor over shards that also hold audio-tower
+    and projector tensors (kinds 1, 8, 26: not kept on the device, still
+    enumerated), and over a model added tensor by tensor."""
+    config = small_config(quant.Q4, layers=2)
+    model = synthetic.make_model(config, quant.Q4, seed=29)
+    extra = [(1, 0, quant.F32, (8, 4), bytes(range(128))),      # audio_conv1_weight
+             (8, 0, quant.F32, (16,), bytes(64)),               # audio_final_norm_weight
+             (26, 0, quant.F32, (4, 16), bytes(256))]           # projector_in_weight
+    first = [shard.tensor_entry(t) for t in model.tensors if t.layer <= 1] + extra
+    second = [shard.tensor_entry(t) for t in model.tensors if t.layer == 2]
+    parts = [shard.build(first), shard.build(second)]
+    expected = _index(parts[0], 0) + _index(parts[1], 1)
+    assert len(expected) == len(model.tensors) + len(extra)
+    a = rt.CudaModel(0)
+    b = rt.CudaModel(0)
+    try:
+        a.begin()
+        for p in parts:
+            a.add_shard(p)
+        a.set_cache_format(rt.CACHE_Q8)
+        a.finish(config.pack())
+        assert a.tensor_count() == len(expected)
+        for i, want in enumerate(expected):
+            assert a.tensor_descriptor(i) == want, i
+        with pytest.raises(rt.QwcError) as e:
+            a.tensor_descriptor(len(expected))
+        assert e.value.status == CODE["not_found"]
+
+        synthetic.load_into(model, b, cache_format=rt.CACHE_Q8)
+        assert b.tensor_count() == len(model.tensors)
+        for i, t in enumerate(model.tensors):
+            d = b.tensor_descriptor(i)
+            vec = t.fmt == quant.F32 and t.rows == 1
+            assert d == {"offset_bytes": 0, "len_bytes": t.payload.nbytes, "kind": t.kind, "layer": t.layer,
+                         "format": t.fmt, "rank": 1 if vec else 2,
+                         "dims": (t.cols, 1, 1, 1) if vec else (t.rows, t.cols, 1, 1), "shard_index": 0xFFFFFFFF}, i
+
+        # The shard-loaded handle (audio entries ignored) decodes like the tensor-loaded one.
+        prompt = synthetic.make_prompt(config, 10, 3, seed=29)
+        ta, la = _decode(a, prompt, 4)
+        tb, lb = _decode(b, prompt, 4)
+        assert ta == tb and all(np.array_equal(x, y) for x, y in zip(la, lb))
+    finally:
+        a.close()
+        b.close()
