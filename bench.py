@@ -1,32 +1,45 @@
 """Benchmark of the decoder token loop: greedy decode tokens/s on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py --profile WORKLOAD [--steps K] [--chunk C] [--streams S] [--trace] [--exact]
+    python bench.py --gemm ROWS COLS [--steps K]
 
-A step is one greedy decode step of the workload's stream (one token through
-28 layers, the tied lm_head and the argmax). The default workload is
+A step is one greedy decode step of the workload's streams (one position
+through 28 layers, the tied lm_head and the argmax). The headline workload is
 configs[2] of the benchmark definition: Qwen3-ASR-1.7B decoder, q4 weights
 (seed 1), 375 N(0,1) audio rows + 16 text ids, q8 KV cache, 448 greedy tokens
 (W + K = 448 by default). Weights (0.91 GB) exceed the 126 MB L2, so no flush
 is needed between steps.
 
-The same line carries a `streams64` object: configs[3] of the benchmark
-definition, 64 independent streams per GPU of the same model (prefixes
-uniform in [100, 1500] audio rows + 16 text ids, each prefilled on the tensor
-cores when its slot begins), timed over greedy steps of all 64 slots with the
-batched tensor-core step, with its own roofline and end-to-end figures.
+The same JSON line carries one object per other benchmark configuration
+(`configs`), each with its own device-timed value, roofline, end-to-end
+figure, launches and clocks:
+  cfg0  0.6B q8, batch 1, 188 + 8 prompt, 64 tokens; also timed in
+        QWC_OPTION_EXACT mode (the reference's arithmetic bit for bit);
+  cfg1  0.6B q4, batch 1, 500 + 12 prompt, 256 tokens;
+  cfg3  1.7B q4, 64 streams per GPU, prefixes U[100, 1500];
+  cfg4  1.7B q4, 64 streams per GPU of the box's 64 x N streams, prefixes
+        U[2048, 3584] in a 4096-position cache.
 
 Under torchrun (N > 1) every rank holds a full weight replica and decodes its
-own independent streams (streams shard across GPUs with no exchange): value =
-tokens of all ranks / the slowest rank's device time.
+own independent streams (streams shard across GPUs with no exchange): every
+value = tokens of all ranks / the slowest rank's device time.
 
 `--impl reference` times the CPU restatement of the reference's Zig decode
-path (oracle/, the reference itself cannot be built here: no Zig toolchain)
-on the host cores, on a bounded sample of the same workload.
+path (oracle/; the reference itself cannot be built here: no Zig toolchain)
+on one host core -- the reference's CPU core is single-threaded -- at the
+workload's decode positions, on a bounded sample of steps.
+
+`--profile` runs one workload for a profiler: load, prefill, K device-timed
+steps; it prints the kernels launched before the timed steps (the skip count
+a profiler needs). `--trace` adds the decode kernel's per-stage timeline.
+`--gemm` times the stream GEMM operator alone on a random q4 matrix.
 """
 
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import os
 import statistics
@@ -41,11 +54,11 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "decode tokens/s, 1.7B q4, 1 & 64 streams/GPU at 1/2/4/8 GPU; % of HBM roofline"
-KV_BYTES_PER_POSITION = 28 * 2 * (1024 + 1024 // 64 * 2)  # all layers, K and V, q8 codes + f16 scales
 # DRAM bytes (read + write) per decoded token of decode_kernel at cfg2, from one
 # ncu capture of a 16-token launch (dram__bytes_read.sum 15.058 GB +
 # dram__bytes_write.sum 29.3 MB, divided by 16 tokens).
 DECODE_TRAFFIC_PER_TOKEN = (15.058409e9 + 29.326592e6) / 16
+DEFAULT_CONFIGS = "cfg0_0p6b_q8_b1,cfg1_0p6b_q4_b1,cfg3_1p7b_q4_s64,cfg4_1p7b_q4_s64_long"
 
 
 def parse_args():
@@ -55,28 +68,39 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=8)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", default="cfg2_1p7b_q4_b1")
-    p.add_argument("--chunk", type=int, default=64, help="decode steps per device launch")
+    p.add_argument("--chunk", type=int, default=64, help="decode steps per device launch (single stream)")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--streams-workload", default="cfg3_1p7b_q4_s64",
-                   help="multi-stream workload measured beside the main one ('none' to skip)")
-    p.add_argument("--streams-steps", type=int, default=200)
+    p.add_argument("--configs", default=DEFAULT_CONFIGS,
+                   help="comma-separated workloads measured beside the headline one ('none' to skip)")
+    p.add_argument("--streams-steps", type=int, default=128, help="timed steps of the multi-stream workloads")
+    p.add_argument("--profile", metavar="WORKLOAD", help="profiling run of one workload (see the module doc)")
+    p.add_argument("--streams", type=int, default=0, help="--profile: override the workload's streams per GPU")
+    p.add_argument("--trace", action="store_true", help="--profile: per-stage timeline of one decode launch")
+    p.add_argument("--exact", action="store_true", help="--profile: QWC_OPTION_EXACT")
+    p.add_argument("--gemm", type=int, nargs=2, metavar=("ROWS", "COLS"), help="time the stream GEMM op alone")
     return p.parse_args()
 
 
-def algorithmic_bytes(model, first_position: int, steps: int) -> float:
-    """Bytes one greedy step must move, summed over `steps` steps starting at
-    `first_position`: every weight payload once (the tied embedding once, as
-    the lm_head), one embedding row, the norm vectors, the q8 KV rows read
-    (position + 1 rows) and the row written."""
+def kv_bytes_per_position(c) -> int:
+    """q8 K and V rows of one position, all layers: codes + f16 group scales."""
+    return c.text_layers * 2 * (c.kv_width + c.kv_width // 64 * 2)
+
+
+def step_bytes(model, positions: list[int], steps: int) -> float:
+    """Algorithmic bytes of `steps` greedy steps of streams at `positions`:
+    every weight payload once per step (shared by all streams; the tied
+    embedding once, as the lm_head), the norm vectors, and per stream its
+    embedding row, its (position + 1) q8 KV rows read and the row written."""
     c = model.config
     weights = sum(t.payload.nbytes for t in model.tensors if t.fmt != 0)
     norms = sum(t.payload.nbytes for t in model.tensors if t.fmt == 0)
-    embed_row = c.text_hidden_size // 64 * (2 + (32 if model.fmt == 16 else 64))
-    per_pos = c.text_layers * 2 * (c.kv_width + c.kv_width // 64 * 2)
+    embed_row = c.text_hidden_size // 64 * (2 + {16: 32, 17: 40, 18: 64}[model.fmt])
+    per_pos = kv_bytes_per_position(c)
     total = 0.0
     for i in range(steps):
-        p = first_position + i
-        total += weights + norms + embed_row + (p + 1) * per_pos + per_pos
+        total += weights + norms
+        for p0 in positions:
+            total += embed_row + (p0 + i + 1) * per_pos + per_pos
     return total
 
 
@@ -144,24 +168,56 @@ def measured_peak() -> tuple[float, str]:
         return 6650.0, "fallback"
 
 
-def config_block(w, args, world):
-    return {"workload": w.name, "model": "Qwen3-ASR-1.7B decoder" if w.config.text_hidden_size == 2048
-            else "Qwen3-ASR-0.6B decoder", "weights": "q4" if w.fmt == 16 else "q8", "kv_cache": "q8",
-            "streams_per_gpu": w.streams, "prompt": f"{w.audio_rows} audio rows + {w.text_ids} text ids",
-            "decode_tokens": args.warmup + args.steps, "l2": "weights 0.91 GB > 126 MB L2 (no flush needed)",
-            "parallelism": f"stream-replicas x{world}"}
+def roofline(bytes_total: float, ms: float, **extra) -> dict:
+    peak, peak_kind = measured_peak()
+    achieved = bytes_total / (ms / 1000.0) / 1e9
+    return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "peak_kind": peak_kind, **extra}
 
 
-def oracle_decode_rate(model, prompt, threads: int, budget_s: float = 20.0, max_steps: int = 64):
-    """Times the CPU port's greedy steps on a bounded sample: prefill of the
-    prompt's text ids only, then decode steps until `budget_s` has passed."""
-    import oracle as O
+def describe(w) -> dict:
+    big = w.config.text_hidden_size == 2048
+    rows = (f"{w.audio_rows} audio rows" if isinstance(w.audio_rows, int)
+            else f"U[{w.audio_rows[0]}, {w.audio_rows[1]}] audio rows per stream")
+    return {"workload": w.name, "model": "Qwen3-ASR-1.7B decoder" if big else "Qwen3-ASR-0.6B decoder",
+            "weights": {16: "q4", 17: "q5", 18: "q8"}[w.fmt], "kv_cache": "q8", "streams_per_gpu": w.streams,
+            "prompt": f"{rows} + {w.text_ids} text ids", "max_positions": w.config.max_positions}
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (oracle/, the reference's arithmetic restated; one core)
+# ---------------------------------------------------------------------------
+
+def cost_equivalent_cache(c, position: int, seed: int) -> tuple[np.ndarray, np.ndarray]:
+    """q8 K/V cache planes whose first `position` rows hold random codes and
+    positive f16 scales: a decode step at `position` reads and multiplies
+    exactly what it would after a real prefill of that many positions."""
+    rng = np.random.default_rng(seed)
+    kvw, groups, mp = c.kv_width, c.kv_width // 64, c.max_positions
+    planes = []
+    for _ in range(2):
+        layer = []
+        for _ in range(c.text_layers):
+            scales = np.zeros((mp, groups), np.uint16)
+            scales[:position] = (np.abs(rng.standard_normal((position, groups))) * 0.02 + 1e-3).astype(
+                np.float16).view(np.uint16)
+            codes = np.full((mp, kvw), 128, np.uint8)
+            codes[:position] = rng.integers(0, 256, size=(position, kvw), dtype=np.uint8)
+            layer.append(np.concatenate([scales.view(np.uint8).ravel(), codes.ravel()]))
+        planes.append(np.concatenate(layer))
+    return planes[0], planes[1]
+
+
+def oracle_decode_rate(model, position: int, first_token: int, budget_s: float, max_steps: int, threads: int = 1):
+    """Greedy steps of the CPU port at the workload's decode positions: the
+    decoder state is a cost-equivalent cache of `position` rows, then steps
+    run until `budget_s` has passed (at least two). Returns (rate, steps, s)."""
     from tests.parity import oracle_model
 
     om = oracle_model(model, threads=threads)
-    c = model.config
-    text = prompt.tokens[prompt.tokens != c.token_audio_pad][:8]
-    nxt = om.prefill(text, np.zeros((0, c.text_hidden_size), np.float32), 0)
+    keys, values = cost_equivalent_cache(model.config, position, seed=position)
+    om.set_state(keys, values, position)
+    nxt = first_token
     t0 = time.perf_counter()
     steps = 0
     while steps < max_steps and (steps < 2 or time.perf_counter() - t0 < budget_s):
@@ -169,8 +225,18 @@ def oracle_decode_rate(model, prompt, threads: int, budget_s: float = 20.0, max_
         steps += 1
     dt = time.perf_counter() - t0
     om.close()
-    del O
-    return steps / dt, steps, dt, len(text)
+    return steps / dt, steps, dt
+
+
+def cpu_model_name() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 def run_reference(args, rank):
@@ -180,48 +246,86 @@ def run_reference(args, rank):
         return
     w = synthetic.workloads()[args.workload]
     model = synthetic.make_model(w.config, w.fmt, w.seed)
-    prompt = synthetic.make_prompt(w.config, w.audio_rows if isinstance(w.audio_rows, int) else w.audio_rows[0],
-                                   w.text_ids, w.seed)
-    threads = os.cpu_count() or 1
-    rate, steps, dt, pre = oracle_decode_rate(model, prompt, threads, budget_s=60.0, max_steps=max(2, args.steps))
-    sample = (f"{steps} greedy steps after a {pre}-token text prefill (positions {pre}..{pre + steps - 1}; the "
-              f"workload decodes at positions ~{w.audio_rows}+: attention is <3% of a step's bytes), {dt:.1f} s")
+    prompt = synthetic.make_prompt(w.config, w.audio_rows, w.text_ids, w.seed)
+    position = len(prompt.tokens) + args.warmup
+    rate, steps, dt = oracle_decode_rate(model, position, int(prompt.tokens[-1]), budget_s=60.0,
+                                         max_steps=max(2, args.steps))
+    sample = (f"{steps} greedy steps at decode positions {position}..{position + steps - 1} of the workload "
+              f"(cache state: {position} cost-equivalent q8 rows), {dt:.1f} s on 1 core of {cpu_model_name()}")
     line = {"metric": METRIC, "value": rate, "unit": "tokens/s", "n_gpus": args.gpus, "steps": steps,
             "warmup": 0, "ms_per_step": 1000.0 / rate, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": config_block(w, args, 1),
-            "cpu_baseline": {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+            "config": {**describe(w), "decode_tokens": args.warmup + args.steps, "parallelism": "1 core"},
+            "cpu_baseline": {"value": rate, "unit": "tokens/s", "cores": 1, "kind": "port", "sample": sample},
             "e2e": {"value": rate, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "note": "CPU restatement of the reference's Zig decode path (oracle/); the Zig reference cannot be "
-                    "built here (no zig toolchain)"}
+            "note": "CPU restatement of the reference's Zig decode path (oracle/) on one core, as the reference's "
+                    "single-threaded CPU core runs; the Zig reference cannot be built here (no zig toolchain)"}
     print(json.dumps(line), flush=True)
 
 
-def streams_bytes(model, positions: list[int], steps: int) -> float:
-    """Algorithmic bytes of `steps` batched steps: every weight payload once
-    per step (shared by all slots), the norm vectors, and per slot its
-    embedding row, its (position + 1) q8 KV rows read and the row written."""
-    c = model.config
-    weights = sum(t.payload.nbytes for t in model.tensors if t.fmt != 0)
-    norms = sum(t.payload.nbytes for t in model.tensors if t.fmt == 0)
-    embed_row = c.text_hidden_size // 64 * (2 + (32 if model.fmt == 16 else 64))
-    per_pos = c.text_layers * 2 * (c.kv_width + c.kv_width // 64 * 2)
-    total = 0.0
-    for i in range(steps):
-        total += weights + norms
-        for p0 in positions:
-            p = p0 + i
-            total += embed_row + (p + 1) * per_pos + per_pos
-    return total
+# ---------------------------------------------------------------------------
+# GPU legs
+# ---------------------------------------------------------------------------
+
+def measure_single(w, model, prompt, local_rank, world, barrier, steps, warmup, chunk, exact=False, e2e=True):
+    """One stream through the persistent decode kernel: `warmup` untimed and
+    `steps` device-timed greedy steps with the inputs resident in HBM, then
+    (e2e) the same decode through the public API with host buffers: prompt
+    upload, prefill, and `steps` qwc_decode_step calls each returning its
+    token to the host."""
+    from qwenscriber_b200 import runtime as rt
+    from qwenscriber_b200 import shards, synthetic
+
+    gm = rt.CudaModel(local_rank)
+    synthetic.load_into(model, gm, cache_format=rt.CACHE_Q8)
+    gm.set_option(rt.OPTION_IGNORE_EOS, 1)
+    gm.set_option(rt.OPTION_STEP_CHUNK, chunk)
+    if exact:
+        gm.set_option(rt.OPTION_EXACT, 1)
+    gm.decode_begin(prompt.tokens, prompt.audio, warmup + steps + 1)
+    gm.run_timed(warmup)
+    first_position = len(prompt.tokens) + warmup
+    barrier()
+    launches0 = gm.launches()
+    with ClockSampler(local_rank) as clocks:
+        ms = gm.run_timed(steps)
+    launches = gm.launches() - launches0
+    barrier()
+    ms = shards.max_over_ranks(ms)
+    gm.decode_end()
+    out = {"workload": w.name, "mode": "exact" if exact else "default",
+           "value": shards.aggregate_rate(steps, world, ms / 1000.0), "unit": "tokens/s",
+           "ms_per_step": ms / steps, "steps": steps, "warmup": warmup,
+           "roofline": roofline(step_bytes(model, [first_position], steps), ms,
+                                bytes_per_step=step_bytes(model, [first_position], steps) / steps,
+                                kernel=f"decode_kernel ({'exact' if exact else 'default'} instantiation, "
+                                       f"one launch per {chunk} steps)"),
+           "gpu_launches": launches, "clocks": clocks.summary(), "decode_positions":
+               f"{first_position}..{first_position + steps - 1}"}
+    if e2e:
+        barrier()
+        t0 = time.perf_counter()
+        gm.decode_begin(prompt.tokens, prompt.audio, steps + 1)
+        for _ in range(steps):
+            gm.decode_step()
+        e2e_s = time.perf_counter() - t0
+        gm.decode_end()
+        barrier()
+        e2e_s = shards.max_over_ranks(e2e_s)
+        out["e2e"] = {"value": shards.aggregate_rate(steps, world, e2e_s), "unit": "tokens/s",
+                      "h2d_bytes_per_step": (prompt.tokens.nbytes + prompt.audio.nbytes) / steps,
+                      "d2h_bytes_per_step": 4,
+                      "includes": f"prompt upload + prefill of {len(prompt.tokens)} positions + {steps} decode "
+                                  f"steps via qwc_decode_step"}
+    gm.close()
+    return out
 
 
-def measure_streams(args, model, w, rank, local_rank, barrier, world):
-    """The multi-stream workload on this rank's GPU: every slot's prompt is
-    prefilled at qwc_stream_begin, then `streams_steps` greedy steps of all
-    slots are timed on the device (qwc_streams_run_timed), then 32 steps
-    through qwc_streams_step (host buffers each step) for the end-to-end figure."""
-    import dataclasses
-
+def measure_streams(args, w, model, rank, local_rank, barrier, world):
+    """The multi-stream workload on this rank's GPU: its 64 global streams'
+    prompts prefilled at qwc_stream_begin, `streams_steps` greedy steps of all
+    slots timed on the device (qwc_streams_run_timed), then 32 steps through
+    qwc_streams_step (host buffers each step) for the end-to-end figure."""
     import torch
 
     from qwenscriber_b200 import runtime as rt
@@ -231,14 +335,14 @@ def measure_streams(args, model, w, rank, local_rank, barrier, world):
     gm = rt.CudaModel(local_rank)
     synthetic.load_into(m, gm, cache_format=rt.CACHE_Q8, streams=w.streams)
     gm.set_option(rt.OPTION_IGNORE_EOS, 1)
-    # This rank's global streams (shards.shard): their own prefix lengths and prompts.
     lengths = synthetic.prefix_lengths(w, world, rank)
     ids = shards.shard(w.streams * world, world, rank)
     prompts = [synthetic.make_prompt(w.config, lengths[s], w.text_ids, w.seed, stream=ids[s])
                for s in range(w.streams)]
     plen = [len(p.tokens) for p in prompts]
     warm, e2e_steps = 4, 32
-    steps = min(args.streams_steps, w.decode - 1 - warm - e2e_steps)
+    room = min(w.decode, w.config.max_positions - max(plen)) - 1
+    steps = min(args.streams_steps, room - warm - e2e_steps)
     t0 = time.perf_counter()
     for s in range(w.streams):  # each prompt prefilled on the tensor cores, 64 positions per step
         gm.stream_begin(s, prompts[s].tokens, prompts[s].audio, w.decode)
@@ -261,21 +365,17 @@ def measure_streams(args, model, w, rank, local_rank, barrier, world):
     barrier()
     e2e_s = shards.max_over_ranks(e2e_s)
     gm.close()
-    tokens = steps * w.streams * world
-    bytes_total = streams_bytes(m, positions, steps)
-    peak, peak_kind = measured_peak()
-    achieved = bytes_total / (ms / 1000.0) / 1e9
+    bytes_total = step_bytes(m, positions, steps)
     return {
-        "workload": w.name, "streams_per_gpu": w.streams,
+        "workload": w.name, "streams_per_gpu": w.streams, "streams_total": w.streams * world,
         "value": shards.aggregate_rate(steps * w.streams, world, ms / 1000.0), "unit": "tokens/s",
         "ms_per_step": ms / steps, "steps": steps, "warmup": warm,
         "prompt": f"{w.text_ids} text ids after U[{w.audio_rows[0]}, {w.audio_rows[1]}] audio rows per stream "
-                  f"({sum(plen)} prompt positions in all, prefilled in {prefill_s:.2f} s, 64 positions per "
-                  f"tensor-core step)",
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_kind": peak_kind, "bytes_per_step": bytes_total / steps},
+                  f"({sum(plen)} prompt positions on this GPU, prefilled in {prefill_s:.2f} s, 64 positions per "
+                  f"tensor-core step); mean decode position {np.mean(positions):.0f}",
+        "roofline": roofline(bytes_total, ms, bytes_per_step=bytes_total / steps),
         "e2e": {"value": shards.aggregate_rate(e2e_steps * w.streams, world, e2e_s), "unit": "tokens/s",
-                "h2d_bytes_per_step": 64 * 16, "d2h_bytes_per_step": 64 * 4 + 16,
+                "h2d_bytes_per_step": 64 * 32, "d2h_bytes_per_step": 64 * 4 + 16,
                 "includes": "qwc_streams_step: slot descriptors up, one graph replay, tokens down, per step"},
         "gpu_launches": launches, "clocks": clocks.summary(),
     }
@@ -285,99 +385,200 @@ def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
 
-    from qwenscriber_b200 import runtime as rt
     from qwenscriber_b200 import shards, synthetic
 
     torch.cuda.set_device(local_rank)
     if world > 1:
         import datetime
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=torch.device(
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device(
             "cuda", local_rank))
-    w = synthetic.workloads()[args.workload]
-    model = synthetic.make_model(w.config, w.fmt, w.seed)
-    rows = w.audio_rows if isinstance(w.audio_rows, int) else w.audio_rows[0]
-    prompt = synthetic.make_prompt(w.config, rows, w.text_ids, w.seed, stream=rank)
-    gm = rt.CudaModel(local_rank)
-    synthetic.load_into(model, gm, cache_format=rt.CACHE_Q8)
-    gm.set_option(rt.OPTION_IGNORE_EOS, 1)
-    gm.set_option(rt.OPTION_STEP_CHUNK, args.chunk)
 
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
 
-    # ---- device-timed decode (inputs resident in HBM) ----
-    gm.decode_begin(prompt.tokens, prompt.audio, args.warmup + args.steps + 1)
-    gm.run_timed(args.warmup)
-    first_position = len(prompt.tokens) + args.warmup
-    barrier()
-    launches0 = gm.launches()
-    with ClockSampler(local_rank) as clocks:
-        ms = gm.run_timed(args.steps)
-    launches = gm.launches() - launches0
-    barrier()
-    ms = shards.max_over_ranks(ms)
-    gm.decode_end()
+    workloads = synthetic.workloads()
+    w = workloads[args.workload]
+    model = synthetic.make_model(w.config, w.fmt, w.seed)
+    prompt = synthetic.make_prompt(w.config, w.audio_rows, w.text_ids, w.seed, stream=rank)
+    head = measure_single(w, model, prompt, local_rank, world, barrier, args.steps, args.warmup, args.chunk)
 
-    # ---- end to end through the public API: prompt upload + prefill + K steps, tokens read each step ----
-    barrier()
-    t0 = time.perf_counter()
-    gm.decode_begin(prompt.tokens, prompt.audio, args.steps + 1)
-    for _ in range(args.steps):
-        gm.decode_step()
-    e2e_s = time.perf_counter() - t0
-    gm.decode_end()
-    barrier()
-    e2e_s = shards.max_over_ranks(e2e_s)
-
-    streams = None
-    if args.streams_workload != "none":
-        streams = measure_streams(args, model, synthetic.workloads()[args.streams_workload], rank, local_rank,
-                                  barrier, world)
+    others = {}
+    names = [] if args.configs == "none" else [n for n in args.configs.split(",") if n]
+    head_key = (w.config.text_hidden_size, w.fmt, w.seed)
+    other_model = {}
+    for name in names:
+        cw = workloads[name]
+        key = (cw.config.text_hidden_size, cw.fmt, cw.seed)
+        if key == head_key:
+            cm = model
+        else:
+            if key not in other_model:
+                other_model = {key: synthetic.make_model(cw.config, cw.fmt, cw.seed)}  # keep one at a time
+            cm = other_model[key]
+        cm = dataclasses.replace(cm, config=cw.config)
+        if cw.streams > 1:
+            others[name] = measure_streams(args, cw, cm, rank, local_rank, barrier, world)
+        else:
+            cp = synthetic.make_prompt(cw.config, cw.audio_rows, cw.text_ids, cw.seed, stream=rank)
+            warm = 4
+            others[name] = measure_single(cw, cm, cp, local_rank, world, barrier, cw.decode - 1 - warm, warm,
+                                          args.chunk)
+            if name == "cfg0_0p6b_q8_b1":
+                others[name + "_exact"] = measure_single(cw, cm, cp, local_rank, world, barrier,
+                                                         cw.decode - 1 - warm, warm, args.chunk, exact=True)
+                others[name + "_exact"]["config"] = describe(cw)
+        others[name]["config"] = describe(cw)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
-        rate, steps, dt, pre = oracle_decode_rate(model, prompt, threads, budget_s=20.0, max_steps=64)
-        cpu = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
-               "sample": f"{steps} greedy steps of the same model after a {pre}-token text prefill, {dt:.1f} s"}
+        position = len(prompt.tokens) + args.warmup
+        rate, steps, dt = oracle_decode_rate(model, position, int(prompt.tokens[-1]), budget_s=20.0, max_steps=64)
+        cpu = {"value": rate, "unit": "tokens/s", "cores": 1, "kind": "port",
+               "sample": f"{steps} greedy steps of the same model at decode positions {position}.."
+                         f"{position + steps - 1} (cache state: {position} cost-equivalent q8 rows), {dt:.1f} s "
+                         f"on 1 core of {cpu_model_name()} (the reference's CPU core is single-threaded)"}
 
     if rank == 0:
-        tokens = args.steps * world
-        value = shards.aggregate_rate(args.steps, world, ms / 1000.0)
-        bytes_total = algorithmic_bytes(model, first_position, args.steps)
-        peak, peak_kind = measured_peak()
-        achieved = bytes_total / (ms / 1000.0) / 1e9
-        h2d = (prompt.tokens.nbytes + prompt.audio.nbytes) / args.steps
+        r = head["roofline"]
+        if args.workload == "cfg2_1p7b_q4_b1":
+            r["traffic"] = DECODE_TRAFFIC_PER_TOKEN
+            r["traffic_unit"] = "bytes per step, from an ncu capture of decode_kernel at cfg2"
         line = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32 (q4 codes dequantized exactly in registers)", "data": "synthetic",
-            "config": config_block(w, args, world),
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_kind": peak_kind,
-                         "traffic": DECODE_TRAFFIC_PER_TOKEN if args.workload == "cfg2_1p7b_q4_b1" else None,
-                         "traffic_unit": "bytes per step, from an ncu capture of decode_kernel at cfg2",
-                         "bytes_per_step": bytes_total / args.steps,
-                         "kernel": "decode_kernel (persistent, one launch per %d steps)" % args.chunk},
-            "e2e": {"value": shards.aggregate_rate(args.steps, world, e2e_s), "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
-                    "includes": "prompt upload + prefill of %d positions + %d decode steps via qwc_decode_step"
-                                % (len(prompt.tokens), args.steps)},
-            "gpu_launches": launches,
-            "clocks": clocks.summary(),
-            "cpu_baseline": cpu,
-            "streams64": streams,
+            "metric": METRIC, "value": head["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32 (q4 codes dequantized exactly in registers)",
+            "data": "synthetic",
+            "config": {**describe(w), "decode_tokens": args.warmup + args.steps, "decode_positions":
+                       head["decode_positions"], "l2": "weights 0.91 GB > 126 MB L2 (no flush needed)",
+                       "parallelism": f"stream-replicas x{world}"},
+            "roofline": r, "e2e": head["e2e"], "gpu_launches": head["gpu_launches"], "clocks": head["clocks"],
+            "cpu_baseline": cpu, "configs": others,
         }
         print(json.dumps(line), flush=True)
-    gm.close()
     if world > 1:
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# profiling modes
+# ---------------------------------------------------------------------------
+
+STAGES = ("qkv", "attention", "o", "gate", "up", "down")
+
+
+def print_trace(raw, layers: int) -> None:
+    """Per-stage means of the decode kernel's phase timeline (three stamps per
+    stage: input ready, output done, barrier passed), over CTAs and layers
+    1 .. layers - 2, in microseconds; brackets hold the mean over layers of
+    the slowest CTA."""
+    tr = raw.reshape(-1, 512).astype(np.int64)
+    ev = (tr - tr[:, 0].min()) / 1000.0
+    per = len(STAGES)
+    print(f"{'stage':10s} {'input':>16s} {'compute':>16s} {'barrier':>16s}")
+    for si, name in enumerate(STAGES):
+        cols = []
+        for k in range(3):
+            means, maxes = [], []
+            for layer in range(1, layers - 1):
+                q = layer * per + si
+                stamps = [ev[:, q * 3 - 1], ev[:, q * 3], ev[:, q * 3 + 1], ev[:, q * 3 + 2]]
+                d = stamps[k + 1] - stamps[k]
+                means.append(d.mean())
+                maxes.append(d.max())
+            cols.append(f"{np.mean(means):6.2f} [{np.mean(maxes):6.2f}]")
+        print(f"{name:10s} " + " ".join(f"{c:>16s}" for c in cols))
+    span = [ev[:, (layer + 1) * per * 3 - 1].max() - ev[:, layer * per * 3 - 1].max() for layer in range(1, layers - 1)]
+    q = layers * per
+    lm = [(ev[:, q * 3 + k] - ev[:, q * 3 + k - 1]).mean() for k in range(3)]
+    print(f"layer {np.mean(span):.2f} us; lm_head input {lm[0]:.2f} compute {lm[1]:.2f} barrier {lm[2]:.2f} us; "
+          f"per token and CTA: tiles in hand {tr[:, 509].mean() / 1000:.1f} us, waiting for tiles "
+          f"{tr[:, 510].mean() / 1000:.1f} us, at grid barriers {tr[:, 511].mean() / 1000:.1f} us")
+
+
+def run_profile(args) -> None:
+    from qwenscriber_b200 import runtime as rt
+    from qwenscriber_b200 import synthetic
+
+    w = synthetic.workloads()[args.profile]
+    if args.streams:
+        w = dataclasses.replace(w, streams=args.streams)
+    model = synthetic.make_model(w.config, w.fmt, w.seed)
+    gm = rt.CudaModel(0)
+    synthetic.load_into(model, gm, cache_format=rt.CACHE_Q8, streams=w.streams)
+    gm.set_option(rt.OPTION_IGNORE_EOS, 1)
+    gm.set_option(rt.OPTION_STEP_CHUNK, args.chunk)
+    if args.exact:
+        gm.set_option(rt.OPTION_EXACT, 1)
+    if w.streams > 1:
+        lengths = synthetic.prefix_lengths(w)
+        for s in range(w.streams):
+            pr = synthetic.make_prompt(w.config, lengths[s], w.text_ids, w.seed, stream=s)
+            gm.stream_begin(s, pr.tokens, pr.audio, w.decode)
+        before = gm.launches()
+        ms = gm.streams_run_timed(args.steps)
+        tokens = args.steps * w.streams
+    else:
+        pr = synthetic.make_prompt(w.config, w.audio_rows, w.text_ids, w.seed)
+        gm.decode_begin(pr.tokens, pr.audio, args.steps + 1 + (min(args.chunk, 8) if args.trace else 0))
+        before = gm.launches()
+        ms = gm.run_timed(args.steps)
+        tokens = args.steps
+    print(f"{w.name}: {args.steps} steps, {ms / args.steps:.3f} ms/step, {tokens / (ms / 1000.0):.0f} tokens/s; "
+          f"kernels before the timed steps: {before}")
+    if args.trace and w.streams <= 1:
+        gm.set_option(rt.OPTION_TRACE, 1)
+        gm.run_timed(min(args.chunk, 8))
+        print_trace(gm.debug_trace(), w.config.text_layers)
+    gm.close()
+
+
+def run_gemm(rows: int, cols: int, reps: int) -> None:
+    """K calls of qwc_op_gemm_streams (activation packing, GEMM, split-K sum)
+    on a random q4 matrix against 64 stream columns, after 3 untimed calls: a
+    profiler filtered on gemm_streams_kernel skips 3 launches to land on the
+    first timed one."""
+    import torch
+
+    from qwenscriber_b200 import quant
+    from qwenscriber_b200 import runtime as rt
+
+    L = rt.lib()
+    rng = np.random.default_rng(0)
+    groups = cols // 64
+    scales = torch.from_numpy((np.abs(rng.standard_normal((rows, groups))) * 0.003).astype(np.float16)
+                              .view(np.uint16)).cuda()
+    codes = torch.from_numpy(rng.integers(0, 256, size=(rows, groups * 32), dtype=np.uint8)).cuda()
+    x = torch.randn(64, cols, device="cuda")
+    out = torch.zeros(64, rows, device="cuda")
+
+    def call():
+        rt.check(L.qwc_op_gemm_streams(quant.Q4, scales.data_ptr(), codes.data_ptr(), rows, cols,
+                                       x.data_ptr(), 64, out.data_ptr(), None), "qwc_op_gemm_streams")
+
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / reps
+    print(f"stream gemm q4 {rows} x {cols}, 64 columns: {us:.1f} us per op call (packing + GEMM + split-K sum)")
+
+
 def main():
     args = parse_args()
+    if args.gemm:
+        run_gemm(*args.gemm, args.steps if args.steps != 440 else 5)
+        return
+    if args.profile:
+        run_profile(args)
+        return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

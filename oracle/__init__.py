@@ -81,6 +81,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "orc_model_finish": (c_int32, [c_void_p]),
         "orc_decoder_reset": (None, [c_void_p]),
         "orc_decoder_position": (c_uint32, [c_void_p]),
+        "orc_decoder_set_state": (c_int32, [c_void_p, c_void_p, c_void_p, c_uint64, c_uint32]),
         "orc_forward_token": (c_int32, [c_void_p, c_uint32, fp, c_int]),
         "orc_argmax_logits": (c_uint32, [c_void_p]),
         "orc_prefill": (c_int32, [c_void_p, u32p, c_uint32, fp, c_uint32, u32p]),
@@ -268,6 +269,13 @@ class OracleModel:
     @property
     def position(self) -> int:
         return int(self._L.orc_decoder_position(self._h))
+
+    def set_state(self, keys: np.ndarray, values: np.ndarray, position: int) -> None:
+        """Loads whole q8 cache planes (the reference layout) and moves the decoder to `position`."""
+        k = np.ascontiguousarray(keys, np.uint8)
+        v = np.ascontiguousarray(values, np.uint8)
+        st = self._L.orc_decoder_set_state(self._h, k.ctypes.data, v.ctypes.data, k.size, position)
+        assert st == 0, st
 
     def forward_token(self, token: int, audio_row: np.ndarray | None = None, want_logits: bool = True) -> None:
         row = None

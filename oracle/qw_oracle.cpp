@@ -824,6 +824,16 @@ void orc_decoder_reset(OrcModel* m) {
 
 uint32_t orc_decoder_position(const OrcModel* m) { return m->position; }
 
+int32_t orc_decoder_set_state(OrcModel* m, const uint8_t* keys, const uint8_t* values, uint64_t len,
+                              uint32_t position) {
+  if (!m->finished || m->cache_format != 1) return kInvalidState;
+  if (len != m->cache_keys_q8.size() || position > m->config.max_positions) return kShapeMismatch;
+  std::memcpy(m->cache_keys_q8.data(), keys, len);
+  std::memcpy(m->cache_values_q8.data(), values, len);
+  m->position = position;
+  return kOk;
+}
+
 // decoder.zig:133-287
 int32_t orc_forward_token(OrcModel* m, uint32_t token, const float* audio_row, int want_logits) {
   if (!m->finished) return kInvalidState;

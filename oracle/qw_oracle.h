@@ -80,6 +80,11 @@ int32_t orc_model_set_tensor(OrcModel* model, uint32_t kind, uint32_t layer, uin
 int32_t orc_model_finish(OrcModel* model);
 void orc_decoder_reset(OrcModel* model);
 uint32_t orc_decoder_position(const OrcModel* model);
+/* Test and timing support (no reference counterpart): replaces the q8 cache
+ * contents (keys, values: the whole cache, len bytes each) and moves the
+ * decoder to `position`, as if that many positions had been prefilled. */
+int32_t orc_decoder_set_state(OrcModel* model, const uint8_t* keys, const uint8_t* values, uint64_t len,
+                              uint32_t position);
 int32_t orc_forward_token(OrcModel* model, uint32_t token, const float* audio_row, int want_logits);
 uint32_t orc_argmax_logits(const OrcModel* model);
 int32_t orc_prefill(OrcModel* model, const uint32_t* tokens, uint32_t n_tokens, const float* audio, uint32_t audio_steps,

@@ -238,18 +238,24 @@ struct Batched {
   alignas(64) uint8_t b_f[128];
   KvMaps4 kv;
   uint32_t splits_qkv = 1, splits_o = 1, splits_gu = 1, splits_down = 1;
-  uint32_t kernels_per_step = 0;
+  uint32_t kernels_per_step = 0, kernels_per_step_nologits = 0;
   uint32_t history_rows = 0;
   int attn_grid = 0;
   StreamsStep P{};
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
+  // The step without the final norm, lm_head and argmax: prompt-prefill
+  // steps whose logits nothing reads (every one but a prompt's last).
+  cudaGraph_t graph_nologits = nullptr;
+  cudaGraphExec_t exec_nologits = nullptr;
   SlotStep* host_desc = nullptr;    // pinned
   uint32_t* host_tokens = nullptr;  // pinned
   int32_t* host_err = nullptr;      // pinned
   ~Batched() {
     if (exec) cudaGraphExecDestroy(exec);
     if (graph) cudaGraphDestroy(graph);
+    if (exec_nologits) cudaGraphExecDestroy(exec_nologits);
+    if (graph_nologits) cudaGraphDestroy(graph_nologits);
     if (host_desc) cudaFreeHost(host_desc);
     if (host_tokens) cudaFreeHost(host_tokens);
     if (host_err) cudaFreeHost(host_err);
@@ -673,8 +679,9 @@ int32_t kv_map4(uint8_t* out, uint8_t* base, uint64_t row, const DevModel& m, ui
   return encode_tensor_map(out, kMapU8, 4, base, dims, str, box, false);
 }
 
-// Enqueues one whole step on the handle's stream (recorded into the graph).
-int32_t record_step(Handle* h) {
+// Enqueues one whole step on the handle's stream (recorded into the graph);
+// without `logits` it ends after the last layer's down projection.
+int32_t record_step(Handle* h, bool logits) {
   Batched& b = *h->batched;
   const DevModel& m = h->host_model;
   const StreamsStep& P = b.P;
@@ -719,6 +726,10 @@ int32_t record_step(Handle* h) {
     QWC_TRY(ok(launch_streams_swiglu(P, b.splits_gu, st)));
     QWC_TRY(gemm({&b.md[l]}, {&L.down}, b.b_f, m.ffn, b.splits_down, part, m.hidden));
   }
+  if (!logits) {
+    b.kernels_per_step_nologits = kernels;
+    return QWC_OK;
+  }
   QWC_TRY(ok(launch_streams_norm(P, 0, m.final_norm, part, b.splits_down, st)));
   QWC_TRY(gemm({&b.mlm}, {&m.lm_head}, b.b_h, m.hidden, 1, b.logits.as<float>(), m.vocab));
   QWC_TRY(ok(launch_streams_argmax(P, st)));
@@ -730,14 +741,13 @@ int32_t record_step(Handle* h) {
 // Records the step once as a CUDA graph (replayed every step), replacing any
 // earlier recording; kernel parameters such as the wait bound are fixed at
 // capture.
-int32_t capture_step(Handle* h) {
-  Batched& b = *h->batched;
-  if (b.exec) cudaGraphExecDestroy(b.exec);
-  if (b.graph) cudaGraphDestroy(b.graph);
-  b.exec = nullptr;
-  b.graph = nullptr;
+int32_t capture_one(Handle* h, bool logits, cudaGraph_t* graph_out, cudaGraphExec_t* exec_out) {
+  if (*exec_out) cudaGraphExecDestroy(*exec_out);
+  if (*graph_out) cudaGraphDestroy(*graph_out);
+  *exec_out = nullptr;
+  *graph_out = nullptr;
   QWC_CUDA(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
-  const int32_t rec = record_step(h);
+  const int32_t rec = record_step(h, logits);
   cudaGraph_t graph = nullptr;
   const cudaError_t ce = cudaStreamEndCapture(h->stream, &graph);
   if (rec != QWC_OK || ce != cudaSuccess) {
@@ -745,10 +755,16 @@ int32_t capture_step(Handle* h) {
     cudaGetLastError();
     return rec != QWC_OK ? rec : status_of(ce);
   }
-  b.graph = graph;
-  const cudaError_t ie = cudaGraphInstantiate(&b.exec, graph, 0);
+  *graph_out = graph;
+  const cudaError_t ie = cudaGraphInstantiate(exec_out, graph, 0);
   if (ie != cudaSuccess) return status_of(ie);
   return QWC_OK;
+}
+
+int32_t capture_step(Handle* h) {
+  Batched& b = *h->batched;
+  QWC_TRY(capture_one(h, true, &b.graph, &b.exec));
+  return capture_one(h, false, &b.graph_nologits, &b.exec_nologits);
 }
 
 int32_t build_batched(Handle* h) {
@@ -847,17 +863,17 @@ int32_t build_batched(Handle* h) {
   return st;
 }
 
-// Runs the captured step once for the columns in b.host_desc and reads the
-// argmax of every column back.
-int32_t run_batched(Handle* h) {
+// Runs the captured step once for the columns in b.host_desc and, with
+// `logits`, reads the argmax of every column back.
+int32_t run_batched(Handle* h, bool logits = true) {
   Batched& b = *h->batched;
   cudaStream_t st = h->stream;
   QWC_CUDA(cudaMemcpyAsync(b.desc.ptr, b.host_desc, kMaxStreams * sizeof(SlotStep), cudaMemcpyHostToDevice, st));
-  QWC_CUDA(cudaGraphLaunch(b.exec, st));
-  QWC_CUDA(cudaMemcpyAsync(b.host_tokens, b.tokens.ptr, kMaxStreams * 4, cudaMemcpyDeviceToHost, st));
+  QWC_CUDA(cudaGraphLaunch(logits ? b.exec : b.exec_nologits, st));
+  if (logits) QWC_CUDA(cudaMemcpyAsync(b.host_tokens, b.tokens.ptr, kMaxStreams * 4, cudaMemcpyDeviceToHost, st));
   QWC_CUDA(cudaMemcpyAsync(b.host_err, b.err.ptr, 16, cudaMemcpyDeviceToHost, st));
   QWC_CUDA(cudaStreamSynchronize(st));
-  h->launches += b.kernels_per_step;
+  h->launches += logits ? b.kernels_per_step : b.kernels_per_step_nologits;
   if (*b.host_err != 0) {
     if (std::getenv("QWC_VERBOSE")) {
       std::fprintf(stderr, "qwc: batched step gave up waiting (code %d, detail %d %d %d)\n", b.host_err[0],
@@ -884,7 +900,8 @@ int32_t batched_prefill(Handle* h, uint32_t slot, const uint32_t* prompt, const 
                                         static_cast<int32_t>(slot), {0, 0, 0}}
                              : SlotStep{0, 0, 0, -1, 0, {0, 0, 0}};
     }
-    QWC_TRY(run_batched(h));
+    // Decoder.prefill computes logits at the prompt's last position only (decoder.zig:308-333).
+    QWC_TRY(run_batched(h, c0 + n == prompt_len));
     last_col = n - 1;
   }
   *next_out = b.host_tokens[last_col];

@@ -35,11 +35,20 @@ def plane_layout(fmt: int, rows: int, cols: int) -> tuple[int, int, int, int]:
     return 0, scales_len, data_off, groups * DATA_BYTES[fmt]
 
 
-def quantize(fmt: int, values: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
-    """quantizeRow over every row: returns (scales u16[rows, groups], codes u8[rows, groups*bytes])."""
+def quantize(fmt: int, values: np.ndarray, block_rows: int = 2048) -> tuple[np.ndarray, np.ndarray]:
+    """quantizeRow over every row: returns (scales u16[rows, groups], codes u8[rows, groups*bytes]).
+    Rows are independent, so they are taken `block_rows` at a time (bounded temporaries)."""
     if fmt not in (Q4, Q5, Q8):
         raise ValueError("q4, q5 and q8 are the formats this backend runs")
     v = np.ascontiguousarray(values, dtype=np.float32)
+    rows, cols = v.shape
+    if rows > block_rows:
+        parts = [_quantize_block(fmt, v[r:r + block_rows]) for r in range(0, rows, block_rows)]
+        return np.concatenate([p[0] for p in parts]), np.concatenate([p[1] for p in parts])
+    return _quantize_block(fmt, v)
+
+
+def _quantize_block(fmt: int, v: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
     rows, cols = v.shape
     g = v.reshape(rows, cols // GROUP, GROUP)
     max_abs = np.abs(g).max(axis=2)
