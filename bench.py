@@ -512,11 +512,13 @@ def run_profile(args) -> None:
     gm.set_option(rt.OPTION_STEP_CHUNK, args.chunk)
     if args.exact:
         gm.set_option(rt.OPTION_EXACT, 1)
+    batched_before = 0
     if w.streams > 1:
         lengths = synthetic.prefix_lengths(w)
         for s in range(w.streams):
             pr = synthetic.make_prompt(w.config, lengths[s], w.text_ids, w.seed, stream=s)
             gm.stream_begin(s, pr.tokens, pr.audio, w.decode)
+            batched_before += (len(pr.tokens) + 63) // 64  # prefill steps, 64 positions each
         before = gm.launches()
         ms = gm.streams_run_timed(args.steps)
         tokens = args.steps * w.streams
@@ -527,7 +529,8 @@ def run_profile(args) -> None:
         ms = gm.run_timed(args.steps)
         tokens = args.steps
     print(f"{w.name}: {args.steps} steps, {ms / args.steps:.3f} ms/step, {tokens / (ms / 1000.0):.0f} tokens/s; "
-          f"kernels before the timed steps: {before}")
+          f"kernels before the timed steps: {before}; batched steps before them: {batched_before} "
+          f"(each launches every per-layer kernel once per layer)")
     if args.trace and w.streams <= 1:
         gm.set_option(rt.OPTION_TRACE, 1)
         gm.run_timed(min(args.chunk, 8))

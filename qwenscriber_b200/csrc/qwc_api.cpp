@@ -672,11 +672,15 @@ int32_t mat_maps(const DevMat& m, MatMaps* out) {
 
 int32_t act_map(uint8_t* out, void* base, uint32_t cols) { return gemm_act_map(base, cols, out); }
 
-int32_t kv_map4(uint8_t* out, uint8_t* base, uint64_t row, const DevModel& m, uint32_t streams, uint32_t box_x) {
+// `swizzle`: 128-byte rows land with the 128-byte swizzle (16-byte chunk c of
+// row r at chunk c ^ (r % 8)), so tensor-core fragment loads of a tile are
+// free of bank conflicts.
+int32_t kv_map4(uint8_t* out, uint8_t* base, uint64_t row, const DevModel& m, uint32_t streams, uint32_t box_x,
+                bool swizzle) {
   const uint64_t dims[4] = {row, m.max_positions, m.n_layers, streams};
   const uint64_t str[3] = {row, m.cache_layer_stride, m.cache_stream_stride};
   const uint32_t box[4] = {box_x, kAttnChunk, 1, 1};
-  return encode_tensor_map(out, kMapU8, 4, base, dims, str, box, false);
+  return encode_tensor_map(out, kMapU8, 4, base, dims, str, box, swizzle);
 }
 
 // Enqueues one whole step on the handle's stream (recorded into the graph);
@@ -779,7 +783,7 @@ int32_t build_batched(Handle* h) {
   b.splits_o = gemm_splits(m.hidden, qw, sms);
   b.splits_gu = gemm_splits(2 * m.ffn, m.hidden, sms);
   b.splits_down = gemm_splits(m.hidden, m.ffn, sms);
-  b.attn_grid = 2 * sms;
+  b.attn_grid = sms;  // one attention CTA per SM (its ring fills most of the shared memory)
   const size_t part_cols = std::max({size_t(b.splits_qkv) * (qw + 2 * kvw), size_t(b.splits_o) * m.hidden,
                                      size_t(b.splits_gu) * 2 * m.ffn, size_t(b.splits_down) * m.hidden});
   const size_t S = kMaxStreams;
@@ -789,7 +793,7 @@ int32_t build_batched(Handle* h) {
   QWC_TRY(b.xb_f.alloc(2 * S * m.ffn * 2));
   QWC_TRY(b.part0.alloc(S * part_cols * 4));
   QWC_TRY(b.qrot.alloc(S * qw * 4));
-  QWC_TRY(b.attn_part.alloc(S * m.q_heads * h->max_chunks * (kHeadDim + 2) * 4));
+  QWC_TRY(b.attn_part.alloc(S * m.q_heads * h->max_chunks * (kHeadDim + 4) * 4));
   QWC_TRY(b.attn_count.alloc(S * m.kv_heads * 4));
   QWC_TRY(b.logits.alloc(S * m.vocab * 4));
   QWC_TRY(b.qkv_rows.alloc(S * (qw + 2 * kvw) * 4));
@@ -828,10 +832,10 @@ int32_t build_batched(Handle* h) {
   QWC_TRY(act_map(b.b_q, b.xb_q.ptr, qw));
   QWC_TRY(act_map(b.b_f, b.xb_f.ptr, m.ffn));
   const uint64_t scale_row = uint64_t(kvw / kGroup) * 2;
-  QWC_TRY(kv_map4(b.kv.k_codes, h->k_cache.as<uint8_t>() + m.cache_scales_bytes, kvw, m, h->streams, kHeadDim));
-  QWC_TRY(kv_map4(b.kv.v_codes, h->v_cache.as<uint8_t>() + m.cache_scales_bytes, kvw, m, h->streams, kHeadDim));
-  QWC_TRY(kv_map4(b.kv.k_scales, h->k_cache.as<uint8_t>(), scale_row, m, h->streams, 16));
-  QWC_TRY(kv_map4(b.kv.v_scales, h->v_cache.as<uint8_t>(), scale_row, m, h->streams, 16));
+  QWC_TRY(kv_map4(b.kv.k_codes, h->k_cache.as<uint8_t>() + m.cache_scales_bytes, kvw, m, h->streams, kHeadDim, true));
+  QWC_TRY(kv_map4(b.kv.v_codes, h->v_cache.as<uint8_t>() + m.cache_scales_bytes, kvw, m, h->streams, kHeadDim, true));
+  QWC_TRY(kv_map4(b.kv.k_scales, h->k_cache.as<uint8_t>(), scale_row, m, h->streams, 16, false));
+  QWC_TRY(kv_map4(b.kv.v_scales, h->v_cache.as<uint8_t>(), scale_row, m, h->streams, 16, false));
 
   StreamsStep& P = b.P;
   P.model = h->model_buf.as<DevModel>();

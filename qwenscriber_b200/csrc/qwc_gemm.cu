@@ -75,7 +75,8 @@ struct __align__(1024) GemmSmem {
   uint8_t b[kRawStages][kBStageBytes];
   uint8_t codes[kRawStages][kCodeStageBytes];
   uint8_t scales[kRawStages][kScaleStageBytes];
-  uint64_t raw_full[kRawStages];
+  uint64_t w_full[kRawStages];  // the stage's weight codes and scales landed
+  uint64_t b_full[kRawStages];  // the stage's activation box landed
   uint64_t raw_empty[kRawStages];
   uint64_t a_full[kAStages];
   uint64_t a_empty[kAStages];
@@ -296,7 +297,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kRawStages; ++i) {
-      mbar_init(&s->raw_full[i], 1);
+      mbar_init(&s->w_full[i], 1);
+      mbar_init(&s->b_full[i], 1);
       mbar_init(&s->raw_empty[i], 1);
     }
     for (int i = 0; i < kAStages; ++i) {
@@ -312,30 +314,52 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   const uint32_t tmem = s->tmem_base;
   bool ok = true;
-  pdl_wait_and_trigger();  // the prologue above overlaps the previous kernel's tail
+  // Programmatic dependent launch, split by data: the weights never depend on
+  // the previous kernel, so the first stages' weight boxes and their
+  // dequantization start at once; only the producer's activation loads wait
+  // for the previous kernel (which writes the activations and reads the
+  // partial sums this launch overwrites). The MMAs and the epilogue follow
+  // those loads, so they run after it too.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
     // ---- producer ----
     if (lane == 0) {
-      for (uint32_t i = 0; i < nkb && ok; ++i) {
+      auto load_weights = [&](uint32_t i) {
+        const uint32_t st = i % kRawStages, kb = kb0 + i;
+        mbar_arrive_expect_tx(&s->w_full[st], kCtaRows * code_box + kScaleStageBytes);
+        tma_load_2d(s->codes[st], map_codes, static_cast<int32_t>(kb * code_box), static_cast<int32_t>(m0),
+                    &s->w_full[st]);
+        // The 16-byte scale box holding this block's group.
+        tma_load_2d(s->scales[st], map_scales, static_cast<int32_t>((kb * 2u) & ~15u), static_cast<int32_t>(m0),
+                    &s->w_full[st]);
+      };
+      auto load_acts = [&](uint32_t i) {
         const uint32_t st = i % kRawStages;
-        if (i >= kRawStages && !wait_bounded(&s->raw_empty[st], ((i / kRawStages) - 1) & 1u, p, 10)) {
+        mbar_arrive_expect_tx(&s->b_full[st], kBStageBytes);
+        tma_load_2d(s->b[st], map_b, static_cast<int32_t>((kb0 + i) * kKBlock), 0, &s->b_full[st]);
+      };
+      const uint32_t first = nkb < uint32_t(kRawStages) ? nkb : uint32_t(kRawStages);
+      for (uint32_t i = 0; i < first; ++i) load_weights(i);
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      for (uint32_t i = 0; i < first; ++i) load_acts(i);
+      uint32_t issued = first;
+      for (uint32_t i = first; i < nkb && ok; ++i) {
+        const uint32_t st = i % kRawStages;
+        if (!wait_bounded(&s->raw_empty[st], ((i / kRawStages) - 1) & 1u, p, 10)) {
           ok = false;
           break;
         }
-        const uint32_t kb = kb0 + i;
-        mbar_arrive_expect_tx(&s->raw_full[st], kCtaRows * code_box + kScaleStageBytes + kBStageBytes);
-        tma_load_2d(s->codes[st], map_codes, static_cast<int32_t>(kb * code_box), static_cast<int32_t>(m0),
-                    &s->raw_full[st]);
-        // The 16-byte scale box holding this block's group.
-        tma_load_2d(s->scales[st], map_scales, static_cast<int32_t>((kb * 2u) & ~15u), static_cast<int32_t>(m0),
-                    &s->raw_full[st]);
-        tma_load_2d(s->b[st], map_b, static_cast<int32_t>(kb * kKBlock), 0, &s->raw_full[st]);
+        load_weights(i);
+        load_acts(i);
+        issued = i + 1;
       }
-      // Drain: every armed stage must have landed before the CTA exits.
-      for (uint32_t i = (nkb > kRawStages ? nkb - kRawStages : 0); i < nkb; ++i) {
+      // Drain: the last stages issued must have landed before the CTA exits
+      // (an earlier stage was consumed before its slot was loaded again).
+      for (uint32_t i = issued > uint32_t(kRawStages) ? issued - kRawStages : 0u; i < issued; ++i) {
         const uint32_t st = i % kRawStages;
-        wait_bounded(&s->raw_full[st], (i / kRawStages) & 1u, p);
+        wait_bounded(&s->w_full[st], (i / kRawStages) & 1u, p);
+        wait_bounded(&s->b_full[st], (i / kRawStages) & 1u, p);
       }
     }
   } else if (warp == 1) {
@@ -345,7 +369,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (uint32_t i = 0; i < nkb && ok; ++i) {
         const uint32_t st = i % kRawStages;
         const uint32_t at = i % kAStages;
-        if (!wait_bounded(&s->raw_full[st], (i / kRawStages) & 1u, p, 20) ||
+        if (!wait_bounded(&s->b_full[st], (i / kRawStages) & 1u, p, 20) ||
             !wait_bounded(&s->a_full[at], (i / kAStages) & 1u, p, 30)) {
           ok = false;
           break;
@@ -383,7 +407,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (uint32_t i = 0; i < nkb && ok; ++i) {
       const uint32_t st = i % kRawStages;
       const uint32_t at = i % kAStages;
-      bool ready = wait_bounded(&s->raw_full[st], (i / kRawStages) & 1u, p, 40);
+      bool ready = wait_bounded(&s->w_full[st], (i / kRawStages) & 1u, p, 40);
       if (ready && i >= kAStages) ready = wait_bounded(&s->a_empty[at], ((i / kAStages) - 1) & 1u, p, 50);
       if (!__all_sync(0xffffffffu, ready)) {  // tcgen05.st below is warp-collective
         ok = false;

@@ -157,6 +157,9 @@ int decode_grid_size(int device);
 // ---- batched multi-stream step (qwc_streams.cu) ----
 
 constexpr uint32_t kMaxStreams = 64;  // stream columns of the tensor-core GEMM
+// One consumer warp's state at the end of a batched-attention segment:
+// max[2], sum[2], o[2][head_dim] of the two query heads of a kv head.
+constexpr uint32_t kStreamsPartFloats = 4 + 2 * kHeadDim;
 
 // What one GEMM column does in the next batched step: consume `token`
 // (embedding row) or, when `audio_row` >= 0, that row of the stream's audio,
@@ -184,7 +187,7 @@ struct StreamsStep {
   void* xb_f;                    // f16 [2 x slot][ffn]
   float* part0;                  // [split][slot][rows] projection partials
   float* qrot;                   // [slot][q width]: normed, rotated queries
-  float* attn_part;              // [slot][q head][chunk][head_dim + 2]
+  float* attn_part;              // [slot][q head][chunk][head_dim + 4]: o, max, sum of a CTA's segment
   uint32_t* attn_count;          // [slot][kv head]
   uint8_t* k_cache;
   uint8_t* v_cache;

@@ -263,26 +263,47 @@ __global__ void __launch_bounds__(256) streams_qkv_kernel(const StreamsStep P, u
 // contiguous ranges, so a CTA walks consecutive chunks of the same (slot,
 // head) and carries an online softmax across them (running max, sum and
 // output). A producer warp keeps a ring of TMA boxes of upcoming chunks in
-// flight. Each (slot, head) segment a CTA finishes becomes one partial
-// (o[128], max, sum) per query head; the CTA whose segment completes the
-// head's chunk count combines the partials (flash-decode rescale).
+// flight. At the end of a (slot, head) segment each consumer warp leaves its
+// state (o[2][128], max and sum of both query heads) in one of two
+// shared-memory buffers and goes on with the next segment; a merge warp
+// combines the eight states (flash-decode rescale) and writes either the
+// attention output (the segment is the whole head) or one partial per query
+// head, and the CTA whose partial completes the head's chunk count combines
+// the partials. Consumer warps never wait for one another.
+//
+// The products run on the tensor cores (mma.sync m16n8k16, f16 operands, f32
+// accumulation). Codes enter as exact f16 values code - 128 (a byte permute
+// against 0x64 and one f16 subtraction). Queries and the value weights
+// (probability times the value group's scale) enter as f16 pairs hi + lo,
+// which carry 22 bits of each f32. Warps 0-3 take the even chunks of the CTA's
+// range and warps 4-7 the odd ones; within a chunk warp w takes positions
+// 16 (w % 4) .. 16 (w % 4) + 15. Code boxes land with the 128-byte swizzle.
 
-constexpr uint32_t kTK = 0;                                    // [64][128] key codes
-constexpr uint32_t kTV = kTK + kAttnChunk * kHeadDim;          // [64][128] value codes
+constexpr uint32_t kTK = 0;                                    // [64][128] key codes (128-byte swizzle)
+constexpr uint32_t kTV = kTK + kAttnChunk * kHeadDim;          // [64][128] value codes (128-byte swizzle)
 constexpr uint32_t kTKS = kTV + kAttnChunk * kHeadDim;         // [64][16 B] key scales (4 kv heads)
 constexpr uint32_t kTVS = kTKS + kAttnChunk * 16;              // [64][16 B] value scales
 constexpr uint32_t kTileBytes = kTVS + kAttnChunk * 16;
-constexpr int kAttnSlots = 4;
+constexpr int kAttnSlots = 8;
 constexpr int kAttnConsumers = 256;
-static_assert(kTV % 128 == 0 && kTKS % 128 == 0 && kTVS % 128 == 0 && kTileBytes % 128 == 0,
-              "TMA boxes land on 128-byte boundaries");
+constexpr float kWeightScale = 4096.0f;
+constexpr uint32_t kPartFloats = kStreamsPartFloats;  // a warp's state: max[2], sum[2], o[2][128]
+constexpr uint32_t kPartStride = kHeadDim + 4;          // a CTA partial row: o[128], max, sum, pad
+constexpr int kAttnThreads = kAttnConsumers + 64;       // + the producer warp (8) and the merge warp (9)
+constexpr uint32_t kSegBufs = 4;                        // segment-state buffers between consumers and the merge warp  // value weights are f16 pairs of 2^12 p s (kept off the f16 subnormals)
+static_assert(kTV % 1024 == 0 && kTKS % 128 == 0 && kTVS % 128 == 0 && kTileBytes % 1024 == 0,
+              "swizzled code boxes start on 1024-byte boundaries");
 
-struct __align__(128) AttnSmem {
+struct SegState {
+  uint32_t s, h, first, count, chunks;
+};
+
+struct __align__(1024) AttnSmem {
   uint8_t ring[kAttnSlots][kTileBytes];
-  alignas(16) float q[2][4][36];   // rotated queries, 32-dim quarters padded against bank conflicts
-  alignas(16) float vpart[8][2][kHeadDim];  // per-warp outputs at a segment's end
-  alignas(16) float red[2][8];              // per-warp running maxima
-  alignas(16) float lsum[2][8];             // per-warp running sums
+  alignas(16) float wstate[kSegBufs][8][kPartFloats];  // consumer warps' segment states, a ring of buffers
+  SegState seg[kSegBufs];
+  alignas(8) uint64_t wfull[kSegBufs];   // eight consumer warps left their states
+  alignas(8) uint64_t wempty[kSegBufs];  // the merge warp is done with the buffer
   uint32_t prefix[kMaxStreams + 1];
   uint32_t pos[kMaxStreams];    // each column's newest position
   uint32_t cache[kMaxStreams];  // each column's cache slot
@@ -290,7 +311,7 @@ struct __align__(128) AttnSmem {
   alignas(8) uint64_t full[kAttnSlots];
   alignas(8) uint64_t empty[kAttnSlots];
 };
-static_assert(offsetof(AttnSmem, vpart) % 16 == 0 && offsetof(AttnSmem, q) % 16 == 0, "vector access alignment");
+constexpr size_t kAttnSmemBytes = sizeof(AttnSmem) + 1024;  // + alignment of the dynamic window
 
 __device__ __forceinline__ void tma_load_4d(void* dst, const void* map, int32_t x, int32_t y, int32_t z, int32_t w,
                                             uint64_t* bar) {
@@ -299,6 +320,34 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* map, int32_t 
       "[%6];" ::"r"(smem_addr(dst)),
       "l"(map), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_addr(bar))
       : "memory");
+}
+
+// Byte offset of 16-byte chunk `chunk` of row `row` in a 128-byte-swizzled box.
+__device__ __forceinline__ uint32_t swz(uint32_t row, uint32_t chunk) { return row * 128u + ((chunk ^ (row & 7u)) << 4); }
+
+// Bytes b0, b1 of `w` as the f16 pair (b0 - 128, b1 - 128) (sel 0x4140), or
+// bytes b2, b3 (sel 0x4342): 0x64 above a byte is the f16 1024 + byte.
+template <uint32_t SEL>
+__device__ __forceinline__ uint32_t codes_f16x2(uint32_t w) {
+  const uint32_t h = __byte_perm(w, 0x64646464u, SEL);
+  uint32_t r;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(0x64806480u));  // - (1024 + 128)
+  return r;
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// d += a * b, m16n8k16, A row-major f16, B column-major f16, f32 accumulators.
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 // Unit of column s (its stream's cache slot `cache`), kv head h, chunk ch.
@@ -333,12 +382,18 @@ __device__ __forceinline__ UnitPos next_unit(const AttnSmem* a, uint32_t kv_head
   return up;
 }
 
-__global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kernel(const StreamsStep P,
+__global__ void __launch_bounds__(kAttnThreads, 1) streams_attention_kernel(const StreamsStep P,
                                                                                const __grid_constant__ KvMaps4 maps,
                                                                                uint32_t layer) {
-  pdl_wait_and_trigger();
-  extern __shared__ __align__(128) uint8_t attn_smem_raw[];
-  AttnSmem* a = reinterpret_cast<AttnSmem*>(attn_smem_raw);
+  // Programmatic dependent launch, split: the next kernel may start its
+  // prologue at once, but this one waits for its predecessor (streams_qkv,
+  // which appends this step's rows and rotates the queries) only where it
+  // reads what that kernel writes. The slot descriptors and every cache row
+  // before a column's last chunk are older than the predecessor.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  extern __shared__ __align__(1024) uint8_t attn_smem_raw[];
+  const uint32_t pad = (1024u - (smem_addr(attn_smem_raw) & 1023u)) & 1023u;
+  AttnSmem* a = reinterpret_cast<AttnSmem*>(attn_smem_raw + pad);
   const DevModel& m = *P.model;
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   const uint32_t qw = m.q_heads * kHeadDim;
@@ -346,19 +401,33 @@ __global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kern
   if (tid == 0) {
     for (int i = 0; i < kAttnSlots; ++i) {
       mbar_init(&a->full[i], 1);
-      mbar_init(&a->empty[i], 8);
+      mbar_init(&a->empty[i], 4);  // the four warps that take the chunk
+    }
+    for (uint32_t i = 0; i < kSegBufs; ++i) {
+      mbar_init(&a->wfull[i], 8);
+      mbar_init(&a->wempty[i], 1);
     }
     fence_mbar_init();
-    uint32_t acc = 0;
-    for (uint32_t s = 0; s < kMaxStreams; ++s) {
-      a->prefix[s] = acc;
-      const SlotStep d = P.desc[s];
-      a->pos[s] = static_cast<uint32_t>(d.position);
-      a->cache[s] = static_cast<uint32_t>(d.cache);
-      if (d.active) acc += kv_heads * (d.position / kAttnChunk + 1);
-    }
-    a->prefix[kMaxStreams] = acc;
   }
+  // Unit prefix over the 64 columns: one column per thread of warps 0-1,
+  // an inclusive scan within each warp, then warp 1 adds warp 0's total.
+  static_assert(kMaxStreams == 64, "the prologue scans 64 columns with two warps");
+  if (tid < 64) {
+    const SlotStep d = P.desc[tid];
+    const uint32_t units = d.active ? kv_heads * (static_cast<uint32_t>(d.position) / kAttnChunk + 1) : 0u;
+    a->pos[tid] = static_cast<uint32_t>(d.position);
+    a->cache[tid] = static_cast<uint32_t>(d.cache);
+    uint32_t inc = units;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t v = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += v;
+    }
+    a->prefix[tid + 1] = inc;  // warp 1's values get warp 0's total below
+    if (tid == 0) a->prefix[0] = 0;
+  }
+  __syncthreads();
+  if (tid >= 32 && tid < 64) a->prefix[tid + 1] += a->prefix[32];
   __syncthreads();
   const uint32_t total = a->prefix[kMaxStreams];
   const uint32_t u0 = static_cast<uint32_t>((uint64_t(total) * blockIdx.x) / gridDim.x);
@@ -368,8 +437,13 @@ __global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kern
     // ---- producer: TMA boxes of units u0..u1 into the ring ----
     if (lane == 0) {
       uint32_t it = 0;
+      bool waited = false;
       UnitPos up = unit_pos(a, P, kv_heads, u0);
       for (uint32_t u = u0; u < u1; ++u, ++it, up = next_unit(a, kv_heads, up)) {
+        if (!waited && up.ch + 1 == up.chunks) {  // a last chunk holds rows the predecessor wrote
+          asm volatile("griddepcontrol.wait;" ::: "memory");
+          waited = true;
+        }
         const uint32_t slot = it % kAttnSlots;
         if (it >= kAttnSlots &&
             !mbar_wait_bounded(&a->empty[slot], ((it / kAttnSlots) - 1) & 1u, P.error, P.timeout_ns, 102)) {
@@ -396,128 +470,201 @@ __global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kern
     return;
   }
 
-  // ---- consumers: 8 warps; warp w takes positions 8w..8w+7 of every tile ----
-  //
-  // Each warp carries its own online softmax (running max, sum and output
-  // per query head) across the units of a (slot, head) segment, so a unit
-  // needs no block-wide synchronisation: the warps meet only when a segment
-  // ends, where their states are merged (flash-decode rescale).
-  // Scores: lane (i, qd) = (lane / 4, lane % 4) holds position 8w + i, dims
-  // 32 qd .. 32 qd + 31; the two lanes of a 64-value group add their sums
-  // before the group scale (q8GroupDot, kernels.zig:636-661).
-  // Values: lane l holds output dims 4 l .. 4 l + 3 of both query heads.
-  const int j = tid / kHeadDim, dd = tid % kHeadDim;
-  const uint32_t pi = static_cast<uint32_t>(lane) / 4, qd = static_cast<uint32_t>(lane) % 4;
-  const uint32_t prow = static_cast<uint32_t>(warp) * 8 + pi;  // this lane's score row in the tile
-  const uint32_t grp = static_cast<uint32_t>(lane) / 16;
-  bool ok = true;
-  float wm[2] = {-INFINITY, -INFINITY}, wl[2] = {0.0f, 0.0f};
-  float wo[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
-  UnitPos cur{0xFFFFFFFFu, 0xFFFFFFFFu, 0, 0, 0};
-  uint32_t seg_first = 0, seg_count = 0;
+  if (warp == 9) {
+    // ---- merge warp: the segments of u0..u1 in order ----
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const uint32_t qw4 = qw;
+    uint32_t nseg = 0;
+    auto merge = [&]() {
+      const uint32_t b = nseg % kSegBufs;
+      const bool ready = mbar_wait_bounded(&a->wfull[b], (nseg / kSegBufs) & 1u, P.error, P.timeout_ns, 103);
+      SegState sg = a->seg[b];
+      if (!ready || sg.s >= kMaxStreams || sg.h >= kv_heads || sg.first >= P.max_chunks || sg.chunks > P.max_chunks ||
+          sg.count > sg.chunks) {
+        // Only a wait that gave up leaves a descriptor this kernel did not
+        // write: record it and emit nothing for the segment.
+        atomicCAS(P.error, 0, 105);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a->wempty[b]);
+        ++nseg;
+        return;
+      }
+      // Lane l: dims 4 l .. 4 l + 3 of query heads 2 h and 2 h + 1.
+      float mh[2], lh[2];
+      float4 oh[2];
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        float mall = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) mall = fmaxf(mall, a->wstate[b][w][hh]);
+        float l = 0.0f;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          const float mw = a->wstate[b][w][hh];
+          if (mw == -INFINITY) continue;
+          const float f = __expf(mw - mall);
+          const float4 v = *reinterpret_cast<const float4*>(&a->wstate[b][w][4 + hh * kHeadDim + 4 * lane]);
+          o = make_float4(fmaf(v.x, f, o.x), fmaf(v.y, f, o.y), fmaf(v.z, f, o.z), fmaf(v.w, f, o.w));
+          l = fmaf(a->wstate[b][w][2 + hh], f, l);
+        }
+        mh[hh] = mall;
+        lh[hh] = l;
+        oh[hh] = o;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a->wempty[b]);  // the states are read
+      __half* xq = static_cast<__half*>(P.xb_q) + size_t(sg.s) * qw4;
+      const size_t xq_lo = size_t(kMaxStreams) * qw4;
+      auto emit = [&](int hh, float4 o, float l) {
+        const float inv = 1.0f / l;
+        const float ov[4] = {o.x * inv, o.y * inv, o.z * inv, o.w * inv};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t col = (2 * sg.h + hh) * kHeadDim + 4u * lane + e;
+          store_one(xq + ((col & ~7u) | chunk_slot(col & 7u)), xq_lo, ov[e]);
+        }
+      };
+      if (sg.count == sg.chunks) {
+        emit(0, oh[0], lh[0]);
+        emit(1, oh[1], lh[1]);
+      } else {
+        // One partial row per query head at the segment's first chunk; a
+        // non-NaN max marks the chunk as a segment start.
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          float* row = P.attn_part + ((size_t(sg.s) * m.q_heads + 2 * sg.h + hh) * P.max_chunks + sg.first) * kPartStride;
+          *reinterpret_cast<float4*>(row + 4 * lane) = oh[hh];
+          if (lane == 0) {
+            row[kHeadDim] = mh[hh];
+            row[kHeadDim + 1] = lh[hh];
+          }
+        }
+        // Acquire-release counter: __syncwarp orders the lanes' partial
+        // stores before lane 0's release; the last arriver's acquire comes
+        // before its lanes' loads of the other CTAs' partials.
+        __syncwarp();
+        uint32_t* counter = P.attn_count + size_t(sg.s) * kv_heads + sg.h;
+        uint32_t last = 0;
+        if (lane == 0) last = (atom_add_acq_rel(counter, sg.count) + sg.count == sg.chunks) ? 1u : 0u;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        __syncwarp();
+        if (last) {
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            float* base = P.attn_part + (size_t(sg.s) * m.q_heads + 2 * sg.h + hh) * P.max_chunks * kPartStride;
+            float mx = -INFINITY, l = 0.0f;
+            float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (uint32_t c0 = 0; c0 < sg.chunks; c0 += 8) {
+              float pm[8], pl[8];
+              float4 po[8];
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                pm[q] = __int_as_float(-1);
+                pl[q] = 0.0f;
+                po[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (c0 + q < sg.chunks) {
+                  const float* src = base + size_t(c0 + q) * kPartStride;
+                  pm[q] = ld_cg(src + kHeadDim);
+                  pl[q] = ld_cg(src + kHeadDim + 1);
+                  po[q] = __ldcg(reinterpret_cast<const float4*>(src) + lane);
+                }
+              }
+              float bm = mx;
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                if (pm[q] == pm[q]) bm = fmaxf(bm, pm[q]);
+              }
+              const float rs = (mx == -INFINITY) ? 0.0f : __expf(mx - bm);
+              o = make_float4(o.x * rs, o.y * rs, o.z * rs, o.w * rs);
+              l *= rs;
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                if (pm[q] == pm[q] && pm[q] != -INFINITY) {
+                  const float f = __expf(pm[q] - bm);
+                  o = make_float4(fmaf(po[q].x, f, o.x), fmaf(po[q].y, f, o.y), fmaf(po[q].z, f, o.z),
+                                  fmaf(po[q].w, f, o.w));
+                  l = fmaf(pl[q], f, l);
+                }
+              }
+              mx = bm;
+            }
+            emit(hh, o, l);
+            // Reset for the next step: partial maxima back to NaN.
+            for (uint32_t c = lane; c < sg.chunks; c += 32) base[size_t(c) * kPartStride + kHeadDim] = __int_as_float(-1);
+          }
+          if (lane == 0) *counter = 0;
+        }
+      }
+      ++nseg;
+    };
+    UnitPos cur{0xFFFFFFFFu, 0xFFFFFFFFu, 0, 0, 0};
+    UnitPos up = unit_pos(a, P, kv_heads, u0);
+    for (uint32_t u = u0; u < u1; ++u, up = next_unit(a, kv_heads, up)) {
+      if (up.s != cur.s || up.h != cur.h) {
+        if (cur.s != 0xFFFFFFFFu) merge();
+        cur = up;
+      }
+    }
+    if (cur.s != 0xFFFFFFFFu) merge();
+    return;
+  }
 
-  // Merges the warps' states of the current (slot, head) segment and emits
-  // it: the final output when the segment covers every chunk of the head,
-  // else a partial for the last-arriving CTA to combine.
+  // ---- consumers ----
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // queries, and the partial buffers other kernels use
+  //
+  // Lane L = 4 r + i. Scores: the m16n8k16 tile of warp w's 16 positions by
+  // 16 dims; B columns are (head 0 hi, head 0 lo, head 1 hi, head 1 lo)
+  // twice, so lane L ends up with head i & 1's scores of positions r and
+  // r + 8. Within a 64-dim group g, lane i's 16 contiguous code bytes of a row
+  // feed the four k-steps t (dims 64 g + 16 i + 4 t + 0..3); the query's B
+  // fragments follow the same dim order. Values: A rows rho = 4 hl + 2 g + h
+  // are the f16 hi (hl 0) / lo (hl 1) parts of head h's weights for value
+  // group g at the warp's 16 positions; n-tile (c, j) has column n <-> dim
+  // 32 c + 4 n + j, so the B fragment of lane L comes from one 4-byte word of
+  // each of four rows.
+  const uint32_t grp = static_cast<uint32_t>(warp) >> 2, wq = static_cast<uint32_t>(warp) & 3u;
+  const uint32_t r = static_cast<uint32_t>(lane) >> 2, i = static_cast<uint32_t>(lane) & 3u;
+  const uint32_t hrow = r & 1u, grow = (r >> 1) & 1u, hl = r >> 2;  // value-row head, group, hi/lo
+  const uint32_t prow0 = 16u * wq + r, prow1 = prow0 + 8u;           // tile rows of this lane's scores
+  const uint32_t va = 16u * wq + 2u * i;                              // tile rows va, va+1, va+8, va+9 (values)
+  bool ok = true;
+  float m_run = -INFINITY, l_run = 0.0f;  // head hq
+  float acc[16][4];
+  uint32_t qb[8][2];
+  UnitPos cur{0xFFFFFFFFu, 0xFFFFFFFFu, 0, 0, 0};
+
+  // At a segment's end: this warp's state into buffer (segment index mod
+  // kSegBufs) for the merge warp; that buffer's previous segment must have
+  // been merged.
+  uint32_t nseg = 0, seg_first = 0, seg_count = 0;
   auto flush = [&]() {
-    if (lane == 0) {
-      a->red[0][warp] = wm[0];
-      a->red[1][warp] = wm[1];
-      a->lsum[0][warp] = wl[0];
-      a->lsum[1][warp] = wl[1];
-    }
-    *reinterpret_cast<float4*>(&a->vpart[warp][0][4 * lane]) = make_float4(wo[0][0], wo[0][1], wo[0][2], wo[0][3]);
-    *reinterpret_cast<float4*>(&a->vpart[warp][1][4 * lane]) = make_float4(wo[1][0], wo[1][1], wo[1][2], wo[1][3]);
-    consumer_sync(kAttnConsumers);
-    float m_run = -INFINITY;
+    const uint32_t b = nseg % kSegBufs;
+    if (nseg >= kSegBufs) mbar_wait_bounded(&a->wempty[b], ((nseg / kSegBufs) - 1) & 1u, P.error, P.timeout_ns, 104);
+    float* st = a->wstate[b][warp];
+    // hi + lo value rows (lanes r and r + 4 hold the same head and group),
+    // the 2^12 weight scale removed.
 #pragma unroll
-    for (int w = 0; w < 8; ++w) m_run = fmaxf(m_run, a->red[j][w]);
-    float o_run = 0.0f, l_run = 0.0f;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) {
-      const float mw = a->red[j][w];
-      if (mw != -INFINITY) {
-        const float f = expf(mw - m_run);
-        o_run = fmaf(a->vpart[w][j][dd], f, o_run);
-        l_run = fmaf(a->lsum[j][w], f, l_run);
+    for (int nt = 0; nt < 16; ++nt) {
+      const float o0 = acc[nt][0] + __shfl_xor_sync(0xffffffffu, acc[nt][0], 16);
+      const float o1 = acc[nt][1] + __shfl_xor_sync(0xffffffffu, acc[nt][1], 16);
+      const uint32_t c = static_cast<uint32_t>(nt) >> 2, j = static_cast<uint32_t>(nt) & 3u;
+      if (hl == 0 && (c >> 1) == grow) {
+        st[4 + hrow * kHeadDim + 32u * c + 8u * i + j] = o0 * (1.0f / kWeightScale);
+        st[4 + hrow * kHeadDim + 32u * c + 8u * i + 4u + j] = o1 * (1.0f / kWeightScale);
       }
     }
-    __half* xq = static_cast<__half*>(P.xb_q) + size_t(cur.s) * qw;
-    const size_t xq_lo = size_t(kMaxStreams) * qw;
-    const uint32_t col = (2 * cur.h + j) * kHeadDim + dd;
-    const uint32_t out_index = (col & ~7u) | chunk_slot(col & 7u);
-    if (seg_count == cur.chunks) {
-      store_one(xq + out_index, xq_lo, o_run / l_run);
-      consumer_sync(kAttnConsumers);  // red / vpart reused by the next segment
-      return;
+    if (lane < 2) {
+      st[lane] = m_run;
+      st[2 + lane] = l_run;
     }
-    float* part = P.attn_part + ((size_t(cur.s) * m.q_heads + 2 * cur.h + j) * P.max_chunks + seg_first) * (kHeadDim + 2);
-    part[dd] = o_run;
-    if (dd == 0) {
-      part[kHeadDim] = m_run;  // a non-NaN max marks the chunk as a segment start
-      part[kHeadDim + 1] = l_run;
-    }
-    // The counter update is acquire-release at gpu scope: its release (after
-    // the bar.sync) publishes this CTA's partial, and the last arriver's
-    // acquire makes every other CTA's partial visible to its loads.
-    consumer_sync(kAttnConsumers);
-    uint32_t* counter = P.attn_count + size_t(cur.s) * kv_heads + cur.h;
-    if (tid == 0) {
-      const uint32_t prev = atom_add_acq_rel(counter, seg_count);
-      a->flag = (prev + seg_count == cur.chunks) ? 1u : 0u;
-    }
-    consumer_sync(kAttnConsumers);
-    if (a->flag) {
-      // Segment starts are read sixteen chunks at a time with every load of a
-      // batch in flight together; NaN maxima mark chunks no segment starts at.
-      float mx = -INFINITY, o = 0.0f, l = 0.0f;
-      const float* base = P.attn_part + (size_t(cur.s) * m.q_heads + 2 * cur.h + j) * P.max_chunks * (kHeadDim + 2);
-      for (uint32_t c0 = 0; c0 < cur.chunks; c0 += 16) {
-        float pm[16], po[16], pl[16];
-#pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          pm[q] = -INFINITY;
-          po[q] = 0.0f;
-          pl[q] = 0.0f;
-          if (c0 + q < cur.chunks) {
-            const float* src = base + size_t(c0 + q) * (kHeadDim + 2);
-            pm[q] = ld_cg(src + kHeadDim);
-            po[q] = ld_cg(src + dd);
-            pl[q] = ld_cg(src + kHeadDim + 1);
-          }
-        }
-        float bm = mx;
-#pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          if (pm[q] == pm[q]) bm = fmaxf(bm, pm[q]);
-        }
-        const float rescale = (mx == -INFINITY) ? 0.0f : expf(mx - bm);
-        o *= rescale;
-        l *= rescale;
-#pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          if (pm[q] == pm[q] && pm[q] != -INFINITY) {
-            const float f = expf(pm[q] - bm);
-            o = fmaf(po[q], f, o);
-            l = fmaf(pl[q], f, l);
-          }
-        }
-        mx = bm;
-      }
-      store_one(xq + out_index, xq_lo, o / l);
-      consumer_sync(kAttnConsumers);
-      // Reset for the next step: partial maxima back to NaN, counter to 0.
-      for (uint32_t c = tid; c < cur.chunks * 2; c += kAttnConsumers) {
-        float* base2 = P.attn_part + (size_t(cur.s) * m.q_heads + 2 * cur.h + (c & 1u)) * P.max_chunks * (kHeadDim + 2);
-        base2[size_t(c >> 1) * (kHeadDim + 2) + kHeadDim] = __int_as_float(-1);
-      }
-      if (tid == 0) *counter = 0;
-    }
-    consumer_sync(kAttnConsumers);
+    if (warp == 0 && lane == 0) a->seg[b] = SegState{cur.s, cur.h, seg_first, seg_count, cur.chunks};
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&a->wfull[b]);
+    ++nseg;
   };
 
   const float scaling = m.attn_scaling;
-  const uint64_t bias = pack2(kNegQ8, kNegQ8);
   uint32_t it = 0;
   UnitPos up = unit_pos(a, P, kv_heads, u0);
   for (uint32_t u = u0; u < u1; ++u, ++it, up = next_unit(a, kv_heads, up)) {
@@ -526,111 +673,124 @@ __global__ void __launch_bounds__(kAttnConsumers + 32, 2) streams_attention_kern
       cur = up;
       seg_first = up.ch;
       seg_count = 0;
-      wm[0] = wm[1] = -INFINITY;
-      wl[0] = wl[1] = 0.0f;
+      m_run = -INFINITY;
+      l_run = 0.0f;
 #pragma unroll
-      for (int t = 0; t < 4; ++t) wo[0][t] = wo[1][t] = 0.0f;
-      a->q[j][dd / 32][dd % 32] = P.qrot[size_t(up.s) * qw + (2 * up.h + j) * kHeadDim + dd];
-      consumer_sync(kAttnConsumers);
-    }
-    const uint32_t slot = it % kAttnSlots;
-    if (ok && !mbar_wait_bounded(&a->full[slot], (it / kAttnSlots) & 1u, P.error, P.timeout_ns, 101)) {
-      ok = false;
-    }
-    const uint8_t* tile = a->ring[slot];
-    const uint32_t newest = a->pos[up.s];
-    const uint32_t base_pos = up.ch * kAttnChunk + static_cast<uint32_t>(warp) * 8;
-    const bool valid = ok && base_pos + pi <= newest;
-    float s0, s1;
-    {
-      const uint4* src = reinterpret_cast<const uint4*>(tile + kTK + prow * kHeadDim + qd * 32);
-      const uint4 kw0 = src[0], kw1 = src[1];
-      const uint32_t kbits = *reinterpret_cast<const uint16_t*>(tile + kTKS + prow * 16 + (up.h % 4) * 4 + (qd / 2) * 2);
-      const uint32_t words[8] = {kw0.x, kw0.y, kw0.z, kw0.w, kw1.x, kw1.y, kw1.z, kw1.w};
-      uint64_t acc0 = 0, acc1 = 0;
+      for (int nt = 0; nt < 16; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
+      // The query B fragments: column n = r is head (r >> 1) & 1, hi (r even) or lo part.
+      const float* qsrc = P.qrot + size_t(up.s) * qw + (2 * up.h + ((r >> 1) & 1u)) * kHeadDim;
 #pragma unroll
-      for (int w = 0; w < 8; ++w) {
-        const float4 q0 = *reinterpret_cast<const float4*>(&a->q[0][qd][4 * w]);
-        const float4 q1 = *reinterpret_cast<const float4*>(&a->q[1][qd][4 * w]);
-        const uint64_t c01 = add2(pack2(bits_f32(__byte_perm(words[w], kMagic, 0x7440)),
-                                        bits_f32(__byte_perm(words[w], kMagic, 0x7441))), bias);
-        const uint64_t c23 = add2(pack2(bits_f32(__byte_perm(words[w], kMagic, 0x7442)),
-                                        bits_f32(__byte_perm(words[w], kMagic, 0x7443))), bias);
-        acc0 = fma2(c01, pack2(q0.x, q0.y), acc0);
-        acc0 = fma2(c23, pack2(q0.z, q0.w), acc0);
-        acc1 = fma2(c01, pack2(q1.x, q1.y), acc1);
-        acc1 = fma2(c23, pack2(q1.z, q1.w), acc1);
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t g = static_cast<uint32_t>(kk) >> 2, t = static_cast<uint32_t>(kk) & 3u;
+        const float4 qv = __ldcg(reinterpret_cast<const float4*>(qsrc + 64u * g + 16u * i + 4u * t));
+        const float q4[4] = {qv.x, qv.y, qv.z, qv.w};
+        float part[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float hi = __half2float(__float2half_rn(q4[e]));
+          part[e] = (r & 1u) ? q4[e] - hi : hi;
+        }
+        qb[kk][0] = pack_f16x2(part[0], part[1]);
+        qb[kk][1] = pack_f16x2(part[2], part[3]);
       }
-      const float2 f0 = unpack2(acc0), f1 = unpack2(acc1);
-      float g0 = f0.x + f0.y, g1 = f1.x + f1.y;
-      g0 += __shfl_xor_sync(0xffffffffu, g0, 1);
-      g1 += __shfl_xor_sync(0xffffffffu, g1, 1);
-      const float scale = f16_bits_to_f32_fast(kbits);
-      g0 *= scale;
-      g1 *= scale;
-      g0 += __shfl_xor_sync(0xffffffffu, g0, 2);
-      g1 += __shfl_xor_sync(0xffffffffu, g1, 2);
-      s0 = valid ? scaling * g0 : -INFINITY;
-      s1 = valid ? scaling * g1 : -INFINITY;
-    }
-    // Online softmax over this warp's 8 positions (math.zig:77-93 subtracts
-    // the row max before exp); the 4 lanes of a position hold equal scores.
-    float mx0 = s0, mx1 = s1;
-#pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-    }
-    const float mn0 = fmaxf(wm[0], mx0), mn1 = fmaxf(wm[1], mx1);
-    const float p0 = valid ? __expf(s0 - mn0) : 0.0f;
-    const float p1 = valid ? __expf(s1 - mn1) : 0.0f;
-    const float r0 = (wm[0] == -INFINITY) ? 0.0f : __expf(wm[0] - mn0);
-    const float r1 = (wm[1] == -INFINITY) ? 0.0f : __expf(wm[1] - mn1);
-    // Lane (i, qd) also weighs position i's values: scale of value group
-    // qd & 1 times the probability of query head qd >> 1.
-    const float sw_lane = f16_bits_to_f32_fast(*reinterpret_cast<const uint16_t*>(
-                              tile + kTVS + prow * 16 + (up.h % 4) * 4 + (qd & 1u) * 2)) *
-                          ((qd >> 1) ? p1 : p0);
-    float ls0 = p0, ls1 = p1;
-#pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-      ls0 += __shfl_xor_sync(0xffffffffu, ls0, o);
-      ls1 += __shfl_xor_sync(0xffffffffu, ls1, o);
-    }
-    wl[0] = fmaf(wl[0], r0, ls0);
-    wl[1] = fmaf(wl[1], r1, ls1);
-    wm[0] = mn0;
-    wm[1] = mn1;
-    // Values (q8GroupAccumulate, kernels.zig:665-688).
-    // Packed pairs: (dims 4l, 4l+1) and (4l+2, 4l+3) of each head.
-    uint64_t acc01[2] = {0, 0}, acc23[2] = {0, 0};
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t row = static_cast<uint32_t>(warp) * 8 + i;
-      const uint32_t word = *reinterpret_cast<const uint32_t*>(tile + kTV + row * kHeadDim + 4 * lane);
-      const float sw0 = __shfl_sync(0xffffffffu, sw_lane, 4 * i + grp);
-      const float sw1 = __shfl_sync(0xffffffffu, sw_lane, 4 * i + grp + 2);
-      const uint64_t c01 = add2(pack2(bits_f32(__byte_perm(word, kMagic, 0x7440)),
-                                      bits_f32(__byte_perm(word, kMagic, 0x7441))), bias);  // code - 128, exact
-      const uint64_t c23 = add2(pack2(bits_f32(__byte_perm(word, kMagic, 0x7442)),
-                                      bits_f32(__byte_perm(word, kMagic, 0x7443))), bias);
-      acc01[0] = fma2(c01, pack2(sw0, sw0), acc01[0]);
-      acc23[0] = fma2(c23, pack2(sw0, sw0), acc23[0]);
-      acc01[1] = fma2(c01, pack2(sw1, sw1), acc01[1]);
-      acc23[1] = fma2(c23, pack2(sw1, sw1), acc23[1]);
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&a->empty[slot]);  // this warp is done with the tile
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const float2 v01 = unpack2(acc01[hh]), v23 = unpack2(acc23[hh]);
-      const float rr = hh == 0 ? r0 : r1;
-      wo[hh][0] = fmaf(wo[hh][0], rr, v01.x);
-      wo[hh][1] = fmaf(wo[hh][1], rr, v01.y);
-      wo[hh][2] = fmaf(wo[hh][2], rr, v23.x);
-      wo[hh][3] = fmaf(wo[hh][3], rr, v23.y);
     }
     ++seg_count;
+    if ((it & 1u) != grp) continue;  // the other four warps take this chunk
+    const uint32_t slot = it % kAttnSlots;
+    if (ok && !mbar_wait_bounded(&a->full[slot], (it / kAttnSlots) & 1u, P.error, P.timeout_ns, 101)) ok = false;
+    const uint8_t* tile = a->ring[slot];
+    const uint32_t newest = a->pos[up.s];
+    const uint32_t base_pos = up.ch * kAttnChunk;
+    // ---- scores: q . k for positions prow0, prow1 (head hq) ----
+    float sc[2];
+    {
+      float d[2][4];
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        d[g][0] = d[g][1] = d[g][2] = d[g][3] = 0.0f;
+        const uint4 k0 = *reinterpret_cast<const uint4*>(tile + kTK + swz(prow0, 4u * g + i));
+        const uint4 k1 = *reinterpret_cast<const uint4*>(tile + kTK + swz(prow1, 4u * g + i));
+        const uint32_t w0[4] = {k0.x, k0.y, k0.z, k0.w};
+        const uint32_t w1[4] = {k1.x, k1.y, k1.z, k1.w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          mma16816(d[g], codes_f16x2<0x4140>(w0[t]), codes_f16x2<0x4140>(w1[t]), codes_f16x2<0x4342>(w0[t]),
+                   codes_f16x2<0x4342>(w1[t]), qb[4 * g + t][0], qb[4 * g + t][1]);
+        }
+      }
+      const uint32_t so = (up.h % 4u) * 4u;
+      const uint32_t ks0 = *reinterpret_cast<const uint32_t*>(tile + kTKS + prow0 * 16u + so);
+      const uint32_t ks1 = *reinterpret_cast<const uint32_t*>(tile + kTKS + prow1 * 16u + so);
+      const float s00 = f16_bits_to_f32_fast(ks0 & 0xFFFFu), s01 = f16_bits_to_f32_fast(ks0 >> 16);
+      const float s10 = f16_bits_to_f32_fast(ks1 & 0xFFFFu), s11 = f16_bits_to_f32_fast(ks1 >> 16);
+      const float t0 = fmaf(s00, d[0][0] + d[0][1], s01 * (d[1][0] + d[1][1]));
+      const float t1 = fmaf(s10, d[0][2] + d[0][3], s11 * (d[1][2] + d[1][3]));
+      sc[0] = (ok && base_pos + prow0 <= newest) ? scaling * t0 : -INFINITY;
+      sc[1] = (ok && base_pos + prow1 <= newest) ? scaling * t1 : -INFINITY;
+    }
+    // ---- online softmax over the warp's 16 positions (math.zig:77-93) ----
+    float mx = fmaxf(sc[0], sc[1]);
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+    const float m_new = fmaxf(m_run, mx);
+    const float resc = (m_run == -INFINITY) ? 0.0f : __expf(m_run - m_new);
+    const float p0 = sc[0] == -INFINITY ? 0.0f : __expf(sc[0] - m_new);
+    const float p1 = sc[1] == -INFINITY ? 0.0f : __expf(sc[1] - m_new);
+    float ps = p0 + p1;
+    ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+    l_run = fmaf(l_run, resc, ps);
+    m_run = m_new;
+    // Accumulators of value rows of head hrow: rescale when its maximum moved.
+    const float f_h0 = __shfl_sync(0xffffffffu, resc, 0), f_h1 = __shfl_sync(0xffffffffu, resc, 1);
+    const float f_row = hrow ? f_h1 : f_h0;
+    if (__any_sync(0xffffffffu, f_row != 1.0f)) {
+#pragma unroll
+      for (int nt = 0; nt < 16; ++nt) {
+        acc[nt][0] *= f_row;
+        acc[nt][1] *= f_row;
+      }
+    }
+    // ---- value weights: A rows (head hrow, group grow, hi/lo hl) at warp positions 2i, 2i+1, 2i+8, 2i+9 ----
+    uint32_t pa0, pa2;
+    {
+      const float a00 = __shfl_sync(0xffffffffu, p0, 8 * i + hrow);      // position 2i
+      const float a10 = __shfl_sync(0xffffffffu, p1, 8 * i + hrow);      // position 2i + 8
+      const float a01 = __shfl_sync(0xffffffffu, p0, 8 * i + 4 + hrow);  // position 2i + 1
+      const float a11 = __shfl_sync(0xffffffffu, p1, 8 * i + 4 + hrow);  // position 2i + 9
+      const uint32_t so = (up.h % 4u) * 4u + grow * 2u;
+      const float pw[4] = {a00, a01, a10, a11};
+      const uint32_t rows[4] = {va, va + 1u, va + 8u, va + 9u};
+      float wv[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float sv = f16_bits_to_f32_fast(*reinterpret_cast<const uint16_t*>(tile + kTVS + rows[e] * 16u + so));
+        const float x = pw[e] > 0.0f ? pw[e] * sv * kWeightScale : 0.0f;
+        const float xh = __half2float(__float2half_rn(x));
+        wv[e] = hl ? x - xh : xh;
+      }
+      pa0 = pack_f16x2(wv[0], wv[1]);
+      pa2 = pack_f16x2(wv[2], wv[3]);
+    }
+    // ---- values: acc[(c, j)] += weights x (code - 128) ----
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint32_t chunk = 2u * c + (r >> 2), off = 4u * (r & 3u);
+      const uint32_t wa = *reinterpret_cast<const uint32_t*>(tile + kTV + swz(va, chunk) + off);
+      const uint32_t wb = *reinterpret_cast<const uint32_t*>(tile + kTV + swz(va + 1u, chunk) + off);
+      const uint32_t wc = *reinterpret_cast<const uint32_t*>(tile + kTV + swz(va + 8u, chunk) + off);
+      const uint32_t wd = *reinterpret_cast<const uint32_t*>(tile + kTV + swz(va + 9u, chunk) + off);
+      const uint32_t ab01 = __byte_perm(wa, wb, 0x5140), ab23 = __byte_perm(wa, wb, 0x7362);
+      const uint32_t cd01 = __byte_perm(wc, wd, 0x5140), cd23 = __byte_perm(wc, wd, 0x7362);
+      mma16816(acc[4 * c + 0], pa0, 0u, pa2, 0u, codes_f16x2<0x4140>(ab01), codes_f16x2<0x4140>(cd01));
+      mma16816(acc[4 * c + 1], pa0, 0u, pa2, 0u, codes_f16x2<0x4342>(ab01), codes_f16x2<0x4342>(cd01));
+      mma16816(acc[4 * c + 2], pa0, 0u, pa2, 0u, codes_f16x2<0x4140>(ab23), codes_f16x2<0x4140>(cd23));
+      mma16816(acc[4 * c + 3], pa0, 0u, pa2, 0u, codes_f16x2<0x4342>(ab23), codes_f16x2<0x4342>(cd23));
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&a->empty[slot]);  // this warp is done with the chunk
   }
   if (cur.s != 0xFFFFFFFFu) flush();
 }
@@ -753,7 +913,7 @@ int launch_streams_advance(const StreamsStep& P, uint32_t* history, uint32_t* co
 
 int prepare_stream_kernels() {
   return static_cast<int>(cudaFuncSetAttribute(streams_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(sizeof(AttnSmem))));
+                                               static_cast<int>(kAttnSmemBytes)));
 }
 
 int launch_streams_norm(const StreamsStep& P, int input_mode, const float* weight, const float* parts, uint32_t splits,
@@ -769,8 +929,8 @@ int launch_streams_qkv(const StreamsStep& P, uint32_t layer, uint32_t splits, ui
 }
 
 int launch_streams_attention(const StreamsStep& P, const KvMaps4& maps, uint32_t layer, int grid, void* stream) {
-  const int smem = static_cast<int>(sizeof(AttnSmem));
-  return static_cast<int>(launch_pdl(streams_attention_kernel, dim3(grid), dim3(kAttnConsumers + 32), smem,
+  const int smem = static_cast<int>(kAttnSmemBytes);
+  return static_cast<int>(launch_pdl(streams_attention_kernel, dim3(grid), dim3(kAttnThreads), smem,
                                      static_cast<cudaStream_t>(stream), P, maps, layer));
 }
 

@@ -252,3 +252,17 @@ def test_cfg0_default_path_teacher_forced_logits(gpu, cuda_lib, oracle_lib):
     model = synthetic.make_model(w.config, w.fmt, w.seed)
     prompt = synthetic.make_prompt(w.config, w.audio_rows, w.text_ids, w.seed)
     _run_parity(model, prompt, steps=w.decode, check_kv=True, max_near_ties=3, deep=True)
+
+
+def test_cfg2_full_model_parity(gpu, cuda_lib, oracle_lib):
+    """configs[2]'s full model (1.7B: 28 layers, hidden 2048, ffn 6144, the
+    151,936-token tied lm_head, q4 weights seed 1) on a short prompt (20 audio
+    rows + 4 text ids): the default path within the logit bounds, teacher
+    forced at near ties, and the exact mode free-running and bit-exact."""
+    from .test_gpu_exact import _exact_run
+
+    w = synthetic.workloads()["cfg2_1p7b_q4_b1"]
+    model = synthetic.make_model(w.config, w.fmt, w.seed)
+    prompt = synthetic.make_prompt(w.config, 20, 4, w.seed)
+    _run_parity(model, prompt, steps=8, check_kv=True, max_near_ties=2, deep=True)
+    _exact_run(model, prompt, steps=8)

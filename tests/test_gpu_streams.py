@@ -16,6 +16,8 @@ tensor cores (documented in the header), so the q8 cache rows are held to the
 single-stream path's bound: codes within one, scales within one f16 ulp.
 """
 
+import dataclasses
+
 import numpy as np
 import pytest
 
@@ -57,7 +59,7 @@ def _run(model, slots, lengths, steps, max_near_ties, seed=5):
 
         errs = []
         for s, p in enumerate(prompts):
-            om = oracle_model(model, threads=4)
+            om = oracle_model(model)
             oms.append(om)
             expect.append(om.prefill(p.tokens, p.audio, p.audio.shape[0]))
             gm.stream_begin(s, p.tokens, p.audio, steps + 1)
@@ -131,3 +133,15 @@ def test_device_chained_steps_match_host_steps(gpu, cuda_lib, oracle_lib):
         runs.append([gm.stream_tokens(s) for s in range(5)])
         gm.close()
     assert runs[0] == runs[1] and all(len(r) == 9 for r in runs[0])
+
+
+def test_long_context_streams_match_oracle(gpu, cuda_lib, oracle_lib):
+    """configs[4]'s attention shapes: a 4096-position cache and prompts of
+    2,048-3,000 positions, so each slot's attention walks 33-48 chunks split
+    across CTAs and their partials are combined. One layer with a narrow FFN
+    keeps the CPU oracle's prefill short; the attention path is the
+    full-size one."""
+    base = small_config(quant.Q4, layers=1, vocab=8192, max_positions=4096)
+    config = dataclasses.replace(base, text_ffn_dim=1024)
+    model = synthetic.make_model(config, quant.Q4, seed=24)
+    _run(model, slots=3, lengths=[(2040, 8), (3000, 4), (2500, 6)], steps=6, max_near_ties=2)
