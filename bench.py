@@ -30,9 +30,15 @@ path (oracle/; the reference itself cannot be built here: no Zig toolchain)
 on one host core -- the reference's CPU core is single-threaded -- at the
 workload's decode positions, on a bounded sample of steps.
 
+The line's `audio` object times the audio tower and projector of the 1.7B
+model (Model.projectAudio) on a 30-second clip per GPU (3000 mel frames, 390
+packed steps): clips/s with the log-mel resident, a tensor-core roofline over
+the clip's algorithmic FLOPs, an end-to-end figure through qwc_audio_project,
+and a 1-core CPU baseline of the restated tower on one 1-second chunk.
+
 `--profile` runs one workload for a profiler: load, prefill, K device-timed
 steps; it prints the kernels launched before the timed steps (the skip count
-a profiler needs). `--trace` adds the decode kernel's per-stage timeline.
+a profiler needs). `--profile audio_1p7b_q4_30s` times K clips of the tower. `--trace` adds the decode kernel's per-stage timeline.
 `--gemm` times the stream GEMM operator alone on a random q4 matrix.
 """
 
@@ -70,6 +76,7 @@ def parse_args():
     p.add_argument("--workload", default="cfg2_1p7b_q4_b1")
     p.add_argument("--chunk", type=int, default=64, help="decode steps per device launch (single stream)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-audio", action="store_true", help="skip the audio tower's line")
     p.add_argument("--configs", default=DEFAULT_CONFIGS,
                    help="comma-separated workloads measured beside the headline one ('none' to skip)")
     p.add_argument("--streams-steps", type=int, default=128, help="timed steps of the multi-stream workloads")
@@ -159,13 +166,13 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def measured_peak() -> tuple[float, str]:
+def measured_peak(key: str = "hbm_gbs") -> tuple[float, str]:
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
         with open(path) as f:
-            return float(json.load(f)["hbm_gbs"]), "measured"
+            return float(json.load(f)[key]), "measured"
     except (OSError, KeyError, ValueError):
-        return 6650.0, "fallback"
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}[key], "fallback"
 
 
 def roofline(bytes_total: float, ms: float, **extra) -> dict:
@@ -321,6 +328,93 @@ def measure_single(w, model, prompt, local_rank, world, barrier, steps, warmup, 
     return out
 
 
+AUDIO_FRAMES = 3000  # a 30-second clip, the mel frontend's capacity (mel.zig:55-58)
+
+
+def audio_flops(c, frames: int) -> float:
+    """Algorithmic FLOPs (2 per multiply-add) of one clip through the tower and
+    projector: the three convolutions over every chunk, conv_out, per layer the
+    four attention projections, the windowed attention (scores and values) and
+    the feed-forward, then the projector."""
+    ch, d, ffn = c.audio_downsample_hidden_size, c.audio_d_model, c.audio_ffn_dim
+    cf, cs = c.audio_chunk_frames, c.audio_chunk_steps
+    chunks = -(-frames // cf)
+    h1, w1 = (c.mel_bins - 1) // 2 + 1, (cf - 1) // 2 + 1
+    h2, w2 = (h1 - 1) // 2 + 1, (w1 - 1) // 2 + 1
+    conv = 2 * 9 * ch * chunks * h1 * w1 + 2 * 9 * ch * ch * chunks * (h2 * w2 + c.audio_frequency_bins * cs)
+    steps = c.packed_steps(frames)
+    window = (c.audio_n_window_infer // cf) * cs
+    attn = sum(4 * min(window, steps - w0) ** 2 * d for w0 in range(0, steps, window))
+    gemm = 2 * steps * (d * c.audio_conv_out_features + d * d + c.audio_output_dim * d)
+    tower = c.audio_layers * (2 * steps * (4 * d * d + 2 * d * ffn) + attn)
+    return float(conv + gemm + tower)
+
+
+def measure_audio(args, local_rank, world, rank, barrier):
+    """The audio tower and projector (Model.projectAudio) of the 1.7B model on
+    a 30-second clip per GPU: warm-up clips, then `reps` clips device-timed
+    with the log-mel resident (qwc_audio_run_timed), then clips end to end
+    through qwc_audio_project (log-mel up, projected rows down)."""
+    from qwenscriber_b200 import runtime as rt
+    from qwenscriber_b200 import shards, synthetic
+
+    w = synthetic.workloads()["cfg2_1p7b_q4_b1"]
+    c = dataclasses.replace(w.config, text_layers=1)  # the decoder is not run here
+    model = synthetic.make_model(c, w.fmt, w.seed, audio=True)
+    mel = synthetic.make_log_mel(c, AUDIO_FRAMES, w.seed, stream=rank)
+    gm = rt.CudaModel(local_rank)
+    synthetic.load_into(model, gm, cache_format=rt.CACHE_Q8)
+    reps, warm = 20, 3
+    gm.audio_run_timed(mel, warm)
+    barrier()
+    with ClockSampler(local_rank) as clocks:
+        ms, launches = gm.audio_run_timed(mel, reps)
+    barrier()
+    ms = shards.max_over_ranks(ms)
+    per_clip = ms / reps
+    flops = audio_flops(c, AUDIO_FRAMES)
+    peak, kind = measured_peak("bf16_tflops")
+    achieved = flops / (per_clip / 1000.0) / 1e12
+    steps = c.packed_steps(AUDIO_FRAMES)
+    out = {"workload": "audio_1p7b_q4_30s", "value": shards.aggregate_rate(reps, world, ms / 1000.0),
+           "unit": "clips/s", "ms_per_clip": per_clip, "clips": reps, "warmup": warm,
+           "audio_seconds_per_second": shards.aggregate_rate(reps, world, ms / 1000.0) * AUDIO_FRAMES / 100.0,
+           "config": {"model": "Qwen3-ASR-1.7B audio tower (24 layers, width 1024, 480 conv channels) + projector",
+                      "weights": "q4 matrices, f16 convolutions", "clip": f"{AUDIO_FRAMES} mel frames (30 s), "
+                      f"{steps} packed steps", "data": "synthetic N(0, 0.5) log-mel"},
+           "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                        "frac": achieved / peak, "peak_kind": f"{kind} bf16 burst",
+                        "flops_per_clip": flops, "traffic": None,
+                        "kernel": "whole clip: gemm_dense_kernel (convolutions), gemm_streams_kernel (projections) "
+                                  "and the tower's other kernels"},
+           "gpu_launches": launches * reps, "clocks": clocks.summary()}
+    barrier()
+    e2e_reps = 5
+    t0 = time.perf_counter()
+    for _ in range(e2e_reps):
+        rows = gm.audio_project(mel, c.audio_output_dim)
+    e2e_s = shards.max_over_ranks(time.perf_counter() - t0)
+    barrier()
+    out["e2e"] = {"value": shards.aggregate_rate(e2e_reps, world, e2e_s), "unit": "clips/s",
+                  "h2d_bytes_per_step": mel.nbytes, "d2h_bytes_per_step": rows.nbytes,
+                  "includes": "log-mel upload, tower and projector, projected rows read back (qwc_audio_project)"}
+    gm.close()
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from tests.parity import oracle_audio
+
+        oa = oracle_audio(model, threads=1)
+        sample = mel[:, :100]
+        t0 = time.perf_counter()
+        oa.project(sample, c.audio_output_dim)
+        dt = time.perf_counter() - t0
+        oa.close()
+        out["cpu_baseline"] = {"value": 1.0 / (dt * AUDIO_FRAMES / 100.0), "unit": "clips/s", "cores": 1,
+                               "kind": "port", "sample": f"one 100-frame chunk (1 s of audio, 13 steps) of the same "
+                               f"tower in {dt:.1f} s on 1 core of {cpu_model_name()}, scaled by the clip's 30 "
+                               f"chunks"}
+    return out
+
+
 def measure_streams(args, w, model, rank, local_rank, barrier, world):
     """The multi-stream workload on this rank's GPU: its 64 global streams'
     prompts prefilled at qwc_stream_begin, `streams_steps` greedy steps of all
@@ -432,6 +526,8 @@ def run_ours(args, rank, world, local_rank):
                 others[name + "_exact"]["config"] = describe(cw)
         others[name]["config"] = describe(cw)
 
+    audio = measure_audio(args, local_rank, world, rank, barrier) if not args.no_audio else None
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         position = len(prompt.tokens) + args.warmup
@@ -455,7 +551,7 @@ def run_ours(args, rank, world, local_rank):
                        head["decode_positions"], "l2": "weights 0.91 GB > 126 MB L2 (no flush needed)",
                        "parallelism": f"stream-replicas x{world}"},
             "roofline": r, "e2e": head["e2e"], "gpu_launches": head["gpu_launches"], "clocks": head["clocks"],
-            "cpu_baseline": cpu, "configs": others,
+            "cpu_baseline": cpu, "configs": others, "audio": audio,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -502,6 +598,21 @@ def run_profile(args) -> None:
     from qwenscriber_b200 import runtime as rt
     from qwenscriber_b200 import synthetic
 
+    if args.profile == "audio_1p7b_q4_30s":
+        w = synthetic.workloads()["cfg2_1p7b_q4_b1"]
+        c = dataclasses.replace(w.config, text_layers=1)
+        model = synthetic.make_model(c, w.fmt, w.seed, audio=True)
+        mel = synthetic.make_log_mel(c, AUDIO_FRAMES, w.seed)
+        gm = rt.CudaModel(0)
+        synthetic.load_into(model, gm, cache_format=rt.CACHE_Q8)
+        gm.audio_run_timed(mel, 2)
+        before = gm.launches()
+        ms, per_clip = gm.audio_run_timed(mel, args.steps)
+        print(f"{args.profile}: {args.steps} clips, {ms / args.steps:.3f} ms/clip, "
+              f"{audio_flops(c, AUDIO_FRAMES) / (ms / args.steps / 1000) / 1e12:.1f} TFLOP/s algorithmic; "
+              f"kernels before the timed clips: {before}; kernels per clip: {per_clip}")
+        gm.close()
+        return
     w = synthetic.workloads()[args.profile]
     if args.streams:
         w = dataclasses.replace(w, streams=args.streams)

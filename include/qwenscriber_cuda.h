@@ -79,6 +79,45 @@ enum {
   QWC_KIND_DECODER_DOWN = 43
 };
 
+/* Audio tower and projector kinds (container.zig:334-362). Audio layer i is
+ * numbered 1024 + i (container.zig:307); the convolutions, conv_out, the
+ * final norm and the projector use layer 0. The three convolution weights are
+ * f16 [out][in][3][3] (layout.zig:150-175; through qwc_model_add_tensor as
+ * `out` rows of in * 9 values); biases and norm vectors f32; the matrices
+ * q4/q5/q8 like the decoder's. */
+enum {
+  QWC_KIND_AUDIO_CONV1_WEIGHT = 1,
+  QWC_KIND_AUDIO_CONV1_BIAS = 2,
+  QWC_KIND_AUDIO_CONV2_WEIGHT = 3,
+  QWC_KIND_AUDIO_CONV2_BIAS = 4,
+  QWC_KIND_AUDIO_CONV3_WEIGHT = 5,
+  QWC_KIND_AUDIO_CONV3_BIAS = 6,
+  QWC_KIND_AUDIO_CONV_OUT_WEIGHT = 7,
+  QWC_KIND_AUDIO_FINAL_NORM_WEIGHT = 8,
+  QWC_KIND_AUDIO_FINAL_NORM_BIAS = 9,
+  QWC_KIND_AUDIO_Q_WEIGHT = 10,
+  QWC_KIND_AUDIO_Q_BIAS = 11,
+  QWC_KIND_AUDIO_K_WEIGHT = 12,
+  QWC_KIND_AUDIO_K_BIAS = 13,
+  QWC_KIND_AUDIO_V_WEIGHT = 14,
+  QWC_KIND_AUDIO_V_BIAS = 15,
+  QWC_KIND_AUDIO_OUT_WEIGHT = 16,
+  QWC_KIND_AUDIO_OUT_BIAS = 17,
+  QWC_KIND_AUDIO_ATTENTION_NORM_WEIGHT = 18,
+  QWC_KIND_AUDIO_ATTENTION_NORM_BIAS = 19,
+  QWC_KIND_AUDIO_FFN_IN_WEIGHT = 20,
+  QWC_KIND_AUDIO_FFN_IN_BIAS = 21,
+  QWC_KIND_AUDIO_FFN_OUT_WEIGHT = 22,
+  QWC_KIND_AUDIO_FFN_OUT_BIAS = 23,
+  QWC_KIND_AUDIO_FINAL_LAYER_NORM_WEIGHT = 24,
+  QWC_KIND_AUDIO_FINAL_LAYER_NORM_BIAS = 25,
+  QWC_KIND_PROJECTOR_IN_WEIGHT = 26,
+  QWC_KIND_PROJECTOR_IN_BIAS = 27,
+  QWC_KIND_PROJECTOR_OUT_WEIGHT = 28,
+  QWC_KIND_PROJECTOR_OUT_BIAS = 29
+};
+#define QWC_AUDIO_LAYER_BASE 1024u
+
 /* Feature bits (src/wasm/abi.zig:179-207): model and decode families, plus
  * the batched multi-stream family this backend adds. */
 #define QWC_FEATURE_MODEL (1u << 3)
@@ -109,6 +148,30 @@ typedef struct qwc_tensor_descriptor {
   uint32_t shard_index;  /* its shard, in the order shards were added; 0xFFFFFFFF if added alone */
   uint32_t reserved[3];
 } qwc_tensor_descriptor;
+
+/* qw_model_audio_config layout, 72 bytes (src/wasm/abi.zig:292-340): the
+ * audio tower's geometry, every derived value resolved by the configuration
+ * helpers the forward pass uses. */
+typedef struct qwc_audio_config {
+  uint32_t d_model;                 /* tower width, in and out of every block */
+  uint32_t layers;                  /* encoder blocks */
+  uint32_t attention_heads;
+  uint32_t head_dim;                /* d_model / attention_heads */
+  uint32_t ffn_dim;
+  uint32_t downsample_hidden_size;  /* the convolution stack's output channels */
+  uint32_t n_window;                /* mel frames per half-chunk */
+  uint32_t n_window_infer;          /* mel frames one attention window spans */
+  uint32_t chunk_frames;            /* mel frames one convolution chunk consumes */
+  uint32_t frequency_bins;          /* mel bins left after the convolution stack */
+  uint32_t conv_out_input_features; /* downsample_hidden_size * frequency_bins */
+  uint32_t chunk_steps;             /* time steps the stack emits per chunk */
+  uint32_t max_position_steps;
+  uint32_t output_dim;              /* projector output width, the decoder's hidden size */
+  uint32_t mel_bins;
+  float layer_norm_eps;
+  uint32_t reserved_0;
+  uint32_t reserved_1;
+} qwc_audio_config;
 
 /* Handle options (qwc_set_option). */
 enum {
@@ -194,8 +257,7 @@ int32_t qwc_shard_validate(const void* bytes, uint64_t len, uint32_t* tensor_cou
 uint32_t qwc_shard_checksum(const void* bytes, uint64_t len);
 /* qw_model_set_cache_format (exports.zig:352-363): ready state only. */
 int32_t qwc_model_set_cache_format(uint32_t handle, uint32_t format);
-/* Number of independent decode streams the next finish allocates (default 1). A model with
- * q5 matrices runs one stream: finish returns unsupported_model for more. */
+/* Number of independent decode streams the next finish allocates (default 1), 1..64. */
 int32_t qwc_model_set_streams(uint32_t handle, uint32_t streams);
 /* qw_model_finish: validates the 160-byte Config (src/core/model_config.zig:110-177,
  * 260-328), resolves every tensor, allocates caches and scratch. */
@@ -212,6 +274,25 @@ int32_t qwc_model_tensor_count(uint32_t handle, uint32_t* out);
  * QWC_NOT_FOUND past the last entry, QWC_INVALID_STATE before qwc_model_finish. */
 int32_t qwc_model_tensor_descriptor(uint32_t handle, uint32_t index, qwc_tensor_descriptor* out);
 
+/* qw_model_audio_config (exports.zig:415-426, model.zig:327-360): in the loaded and decoding
+ * states, QWC_INVALID_STATE otherwise. */
+int32_t qwc_model_audio_config(uint32_t handle, qwc_audio_config* out);
+
+/* ---- audio family: the tower and projector (src/core/qwen3_asr/model.zig:445-744) ----
+ * A model that carries the audio-tower and projector tensors (all of them:
+ * qwc_model_finish returns QWC_NOT_FOUND when some are missing) runs them on
+ * the device. `log_mel` / `features` is the log-mel spectrogram of one clip,
+ * mel_bins x frames f32 row major (what qw_mel_compute writes), at most 3000
+ * frames (QWC_AUDIO_TOO_LONG beyond). A handle without a tower returns
+ * QWC_NOT_FOUND. */
+
+/* Model.projectAudio (model.zig:451-460): the convolution stack, the tower and
+ * the projector over one clip; writes steps x output_dim f32 rows to `out`
+ * (host memory, capacity in floats; QWC_LIMIT_EXCEEDED when too small) and
+ * the step count (Config.packedStepCount of the frames) to *steps_out. */
+int32_t qwc_audio_project(uint32_t handle, const float* log_mel, uint32_t frames, float* out,
+                          uint64_t out_capacity_floats, uint32_t* steps_out);
+
 /* ---- decode family, stream slot 0 (src/wasm/exports.zig:440-497; model.zig:370-474) ---- */
 
 /* qw_decode_begin after the audio tower: resets stream 0's cache, prefills
@@ -220,6 +301,15 @@ int32_t qwc_model_tensor_descriptor(uint32_t handle, uint32_t index, qwc_tensor_
  * the first predicted token. */
 int32_t qwc_decode_begin(uint32_t handle, const uint32_t* prompt, uint32_t prompt_len, const float* audio,
                          uint32_t audio_steps, uint32_t max_tokens);
+/* qw_decode_begin from the clip's log-mel features (exports.zig:440-458,
+ * model.zig:370-410): runs the tower and projector on the device, then
+ * prefills `prompt` with the projected rows, which stay on the device. The
+ * prompt's token ids come from the caller (the reference builds them from its
+ * vocabulary, prompt.zig): it must hold one Config.token_audio_pad per packed
+ * step (QWC_SHAPE_MISMATCH otherwise). features_len is in bytes, a whole
+ * number of mel_bins f32 columns. */
+int32_t qwc_decode_begin_features(uint32_t handle, const uint32_t* prompt, uint32_t prompt_len, const float* features,
+                                  uint64_t features_len, uint32_t max_tokens);
 /* qw_decode_step: 1 and *token_out written, 0 when finished, <0 status. */
 int32_t qwc_decode_step(uint32_t handle, uint32_t* token_out);
 /* qw_decode_tokens: copies the ids produced so far, returns their count. */
@@ -239,6 +329,9 @@ int32_t qwc_decode_end(uint32_t handle);
 
 int32_t qwc_stream_begin(uint32_t handle, uint32_t slot, const uint32_t* prompt, uint32_t prompt_len,
                          const float* audio, uint32_t audio_steps, uint32_t max_tokens);
+/* qwc_decode_begin_features for stream slot `slot`. */
+int32_t qwc_stream_begin_features(uint32_t handle, uint32_t slot, const uint32_t* prompt, uint32_t prompt_len,
+                                  const float* features, uint64_t features_len, uint32_t max_tokens);
 /* Advances every decoding slot by one token. results[slot]: 1 token written
  * to tokens_out[slot], 0 finished or idle, <0 status of that slot
  * (QWC_LIMIT_EXCEEDED at max_positions). Returns the number of tokens
@@ -282,6 +375,18 @@ int32_t qwc_debug_trace(uint32_t handle, uint64_t* out, uint32_t count);
 /* Raw key (which = 0) or value (which = 1) cache bytes of `slot`, in the
  * reference's layer-major two-plane layout (src/core/qwen3_asr/decoder.zig:45-65). */
 int32_t qwc_debug_cache(uint32_t handle, uint32_t slot, uint32_t which, void* out, uint64_t len);
+/* The audio tower's packed sequence of the last clip, steps x d_model f32:
+ * which 0 = after the convolution stack, conv_out and the position rows
+ * (Model.encodeConvStage, model.zig:476-485); which 1 = after the tower's
+ * blocks and its final LayerNorm (encodeTowerStage + encodedSteps,
+ * model.zig:491-499). `count` floats at most; returns the count written. */
+int32_t qwc_debug_audio(uint32_t handle, uint32_t which, float* out, uint64_t count);
+/* Measurement: uploads `log_mel` once, then runs the tower and projector
+ * `reps` times on the device (inputs resident, outputs left on the device),
+ * reporting the device time of all reps in milliseconds (CUDA events on the
+ * handle's stream) and the kernels one clip launches in *launches_out. */
+int32_t qwc_audio_run_timed(uint32_t handle, const float* log_mel, uint32_t frames, uint32_t reps, float* device_ms,
+                            uint32_t* launches_out);
 /* Device kernels launched by this handle since creation. */
 uint64_t qwc_kernel_launches(uint32_t handle);
 /* Rotary tables as the model builds them (src/core/qwen3_asr/kernels.zig:534-564):
@@ -330,8 +435,9 @@ int32_t qwc_op_argmax_noalloc(const float* values, uint32_t count, uint32_t* out
  * W[r][k] * x[s][k], x as [streams][cols] f32, out as [streams][rows] f32.
  * Each dequantized weight enters as an exact pair of f16 values (hi + lo)
  * and each activation as f16 hi + lo (22 significant bits); products
- * accumulate in f32. cols must be a multiple of 512. Uses a device workspace
- * the library allocates per call. */
+ * accumulate in f32. Formats q4, q5 and q8; cols must be a multiple of 512;
+ * `scales` and `codes` 16-byte aligned. Uses a device workspace the library
+ * allocates per call. */
 int32_t qwc_op_gemm_streams(uint32_t format, const void* scales, const void* codes, uint32_t rows, uint32_t cols,
                             const float* x, uint32_t streams, float* out, void* stream);
 /* math.rmsNormInPlace per row (src/core/math.zig:120-130), out of place. */

@@ -93,6 +93,32 @@ def _declare(L: ctypes.CDLL) -> None:
         "orc_cache_values_q8": (u8p, [c_void_p, POINTER(c_uint64)]),
         "orc_rope_cos": (fp, [c_void_p]),
         "orc_rope_sin": (fp, [c_void_p]),
+        "orc_erf": (c_float, [c_float]),
+        "orc_gelu": (c_float, [c_float]),
+        "orc_layer_norm": (None, [fp, fp, fp, c_uint32, c_uint32, c_float]),
+        "orc_conv3x3_stride2_gelu": (
+            c_int32,
+            [fp, fp, POINTER(c_uint16), fp, c_uint32, c_uint32, c_uint32, c_uint32, c_int],
+        ),
+        "orc_audio_attention_window": (
+            c_int32,
+            [fp, c_uint32, fp, c_uint32, fp, c_uint32, fp, c_uint32, c_uint32, c_uint32, c_uint32, c_uint32],
+        ),
+        "orc_add_sinusoidal_position": (None, [fp, c_uint32, c_uint32]),
+        "orc_audio_new": (c_void_p, [c_void_p, c_uint32]),
+        "orc_audio_free": (None, [c_void_p]),
+        "orc_audio_set_threads": (None, [c_void_p, c_int]),
+        "orc_audio_set_tensor": (
+            c_int32,
+            [c_void_p, c_uint32, c_uint32, c_uint32, c_uint32, c_uint32, c_void_p, c_size_t],
+        ),
+        "orc_audio_finish": (c_int32, [c_void_p]),
+        "orc_audio_packed_steps": (c_uint32, [c_void_p, c_uint32]),
+        "orc_audio_encode_conv": (c_int32, [c_void_p, fp, c_uint32, u32p]),
+        "orc_audio_encode_tower": (c_int32, [c_void_p, c_uint32]),
+        "orc_audio_project_steps": (c_int32, [c_void_p, c_uint32, fp]),
+        "orc_audio_project": (c_int32, [c_void_p, fp, c_uint32, fp, c_uint64, u32p]),
+        "orc_audio_encoded": (fp, [c_void_p, POINTER(c_uint32)]),
     }
     for name, (restype, argtypes) in sig.items():
         fn = getattr(L, name)
@@ -326,3 +352,124 @@ class OracleModel:
         c = np.ctypeslib.as_array(self._L.orc_rope_cos(self._h), shape=(max_positions * half,)).copy()
         s = np.ctypeslib.as_array(self._L.orc_rope_sin(self._h), shape=(max_positions * half,)).copy()
         return c, s
+
+
+# ---- the audio tower and projector (qw_oracle_audio.cpp) ----
+
+
+def erf(x: float) -> float:
+    return float(lib().orc_erf(x))
+
+
+def gelu(x: float) -> float:
+    return float(lib().orc_gelu(x))
+
+
+def layer_norm(x: np.ndarray, weight: np.ndarray, bias: np.ndarray, eps: float) -> np.ndarray:
+    """math.zig:99-116 over every row of x [tokens][width]."""
+    out = np.ascontiguousarray(x, np.float32).copy()
+    tokens, width = out.reshape(-1, x.shape[-1]).shape
+    lib().orc_layer_norm(_fp(out), _fp(np.ascontiguousarray(weight, np.float32)),
+                         _fp(np.ascontiguousarray(bias, np.float32)), width, tokens, eps)
+    return out
+
+
+def conv3x3_stride2_gelu(x: np.ndarray, weights_f16: np.ndarray, bias: np.ndarray, threads: int = 8) -> np.ndarray:
+    """kernels.zig:332-362: x [in_ch][h][w] f32, weights [out][in][3][3] as f16 bits (uint16)."""
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(weights_f16, np.uint16)
+    in_ch, h, wd = x.shape
+    out_ch = w.shape[0]
+    out = np.zeros((out_ch, (h - 1) // 2 + 1, (wd - 1) // 2 + 1), np.float32)
+    st = lib().orc_conv3x3_stride2_gelu(_fp(out), _fp(x), w.ctypes.data_as(POINTER(c_uint16)),
+                                        _fp(np.ascontiguousarray(bias, np.float32)), out_ch, in_ch, h, wd, threads)
+    assert st == 0, st
+    return out
+
+
+def audio_attention_window(q: np.ndarray, k: np.ndarray, v: np.ndarray, start: int, length: int, heads: int,
+                           head_dim: int, out: np.ndarray | None = None) -> np.ndarray:
+    """kernels.zig:435-487 on [steps][heads * head_dim] rows (stride = the row width)."""
+    q, k, v = (np.ascontiguousarray(a, np.float32) for a in (q, k, v))
+    width = heads * head_dim
+    if out is None:
+        out = np.zeros_like(q)
+    st = lib().orc_audio_attention_window(_fp(out), width, _fp(q), width, _fp(k), width, _fp(v), width, start, length,
+                                          heads, head_dim)
+    assert st == 0, st
+    return out
+
+
+def add_sinusoidal_position(row: np.ndarray, step: int) -> np.ndarray:
+    out = np.ascontiguousarray(row, np.float32).copy()
+    lib().orc_add_sinusoidal_position(_fp(out), step, out.size)
+    return out
+
+
+class OracleAudio:
+    """model.zig's audio tower and projector over borrowed payloads."""
+
+    def __init__(self, config_bytes: bytes, threads: int = 8):
+        self._L = lib()
+        self._cfg = ctypes.create_string_buffer(bytes(config_bytes), len(config_bytes))
+        self._h = self._L.orc_audio_new(self._cfg, len(config_bytes))
+        if not self._h:
+            raise ValueError("orc_audio_new refused the configuration")
+        self._keep = []
+        self._L.orc_audio_set_threads(self._h, threads)
+        self.steps = 0
+
+    def close(self):
+        if self._h:
+            self._L.orc_audio_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_tensor(self, kind: int, layer: int, fmt: int, rows: int, cols: int, payload: np.ndarray) -> int:
+        payload = np.ascontiguousarray(payload)
+        self._keep.append(payload)
+        return int(self._L.orc_audio_set_tensor(self._h, kind, layer, fmt, rows, cols, payload.ctypes.data,
+                                                payload.nbytes))
+
+    def finish(self) -> int:
+        return int(self._L.orc_audio_finish(self._h))
+
+    def packed_steps(self, frames: int) -> int:
+        return int(self._L.orc_audio_packed_steps(self._h, frames))
+
+    def encode_conv(self, log_mel: np.ndarray) -> int:
+        mel = np.ascontiguousarray(log_mel, np.float32)
+        steps = np.zeros(1, np.uint32)
+        st = self._L.orc_audio_encode_conv(self._h, _fp(mel), mel.shape[1], _u32p(steps))
+        if st != 0:
+            raise RuntimeError(f"orc_audio_encode_conv -> {st}")
+        self.steps = int(steps[0])
+        return self.steps
+
+    def encode_tower(self) -> None:
+        st = self._L.orc_audio_encode_tower(self._h, self.steps)
+        if st != 0:
+            raise RuntimeError(f"orc_audio_encode_tower -> {st}")
+
+    def encoded(self, width: int) -> np.ndarray:
+        n = c_uint32(0)
+        p = self._L.orc_audio_encoded(self._h, ctypes.byref(n))
+        return np.ctypeslib.as_array(p, shape=(n.value,)).copy().reshape(-1, width)
+
+    def project_steps(self, out_dim: int) -> np.ndarray:
+        out = np.zeros((self.steps, out_dim), np.float32)
+        st = self._L.orc_audio_project_steps(self._h, self.steps, _fp(out))
+        if st != 0:
+            raise RuntimeError(f"orc_audio_project_steps -> {st}")
+        return out
+
+    def project(self, log_mel: np.ndarray, out_dim: int) -> np.ndarray:
+        """model.zig:451-460: conv stage, tower, projector."""
+        self.encode_conv(log_mel)
+        self.encode_tower()
+        return self.project_steps(out_dim)

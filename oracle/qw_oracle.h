@@ -100,6 +100,37 @@ const uint8_t* orc_cache_values_q8(const OrcModel* model, uint64_t* len_out);
 const float* orc_rope_cos(const OrcModel* model);
 const float* orc_rope_sin(const OrcModel* model);
 
+/* ---- the audio tower and projector (qw_oracle_audio.cpp; model.zig:445-870,
+ * kernels.zig:210-487, math.zig:46-116) ---- */
+float orc_erf(float x);
+float orc_gelu(float x);
+void orc_layer_norm(float* x, const float* weight, const float* bias, uint32_t width, uint32_t tokens, float eps);
+/* out [out_ch][h'][w'], input [in_ch][in_h][in_w], weights [out_ch][in_ch][3][3] (f16 bits). */
+int32_t orc_conv3x3_stride2_gelu(float* out, const float* input, const uint16_t* weights, const float* bias,
+                                 uint32_t out_ch, uint32_t in_ch, uint32_t in_h, uint32_t in_w, int threads);
+int32_t orc_audio_attention_window(float* out, uint32_t out_stride, const float* q, uint32_t q_stride, const float* k,
+                                   uint32_t k_stride, const float* v, uint32_t v_stride, uint32_t window_start,
+                                   uint32_t window_length, uint32_t heads, uint32_t head_dim);
+void orc_add_sinusoidal_position(float* row, uint32_t step, uint32_t channels);
+
+typedef struct OrcAudio OrcAudio;
+OrcAudio* orc_audio_new(const void* config, uint32_t config_len);
+void orc_audio_free(OrcAudio* audio);
+void orc_audio_set_threads(OrcAudio* audio, int threads);
+/* Borrows payload until orc_audio_free: f32 vectors (rows 1), f16 convolution
+ * weights [out][in * 9], q4/q5/q8 matrix container payloads. */
+int32_t orc_audio_set_tensor(OrcAudio* audio, uint32_t kind, uint32_t layer, uint32_t format, uint32_t rows,
+                             uint32_t cols, const void* payload, size_t len);
+int32_t orc_audio_finish(OrcAudio* audio);
+uint32_t orc_audio_packed_steps(const OrcAudio* audio, uint32_t frames);
+/* log_mel: [mel_bins][frames] row major. */
+int32_t orc_audio_encode_conv(OrcAudio* audio, const float* log_mel, uint32_t frames, uint32_t* steps_out);
+int32_t orc_audio_encode_tower(OrcAudio* audio, uint32_t steps);
+int32_t orc_audio_project_steps(OrcAudio* audio, uint32_t steps, float* out);
+int32_t orc_audio_project(OrcAudio* audio, const float* log_mel, uint32_t frames, float* out, uint64_t capacity_floats,
+                          uint32_t* steps_out);
+const float* orc_audio_encoded(const OrcAudio* audio, uint32_t* count_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -101,6 +101,41 @@ class Config:
     def tied(self) -> bool:
         return bool(self.flags & FLAG_OUTPUT_PROJECTION_TIED)
 
+    # The audio tower's derived geometry (model_config.zig:190-240).
+    @staticmethod
+    def conv_steps(n: int) -> int:
+        """postConvolutionSteps: three kernel-3, stride-2, padding-1 halvings (0 stays 0)."""
+        if n == 0:
+            return 0
+        for _ in range(3):
+            n = (n - 1) // 2 + 1
+        return n
+
+    @property
+    def audio_head_dim(self) -> int:
+        return self.audio_d_model // self.audio_attention_heads
+
+    @property
+    def audio_chunk_frames(self) -> int:
+        return self.audio_n_window * 2
+
+    @property
+    def audio_chunk_steps(self) -> int:
+        return self.conv_steps(self.audio_chunk_frames)
+
+    @property
+    def audio_frequency_bins(self) -> int:
+        return self.conv_steps(self.mel_bins)
+
+    @property
+    def audio_conv_out_features(self) -> int:
+        return self.audio_downsample_hidden_size * self.audio_frequency_bins
+
+    def packed_steps(self, frames: int) -> int:
+        """packedStepCount: whole chunks convolved separately, then the partial one."""
+        chunk = self.audio_chunk_frames
+        return (frames // chunk) * self.conv_steps(chunk) + self.conv_steps(frames % chunk)
+
 
 def qwen3_asr_0p6b(**overrides) -> Config:
     """Decoder geometry of the released 0.6B checkpoint (model_config.zig:377-415)."""

@@ -22,6 +22,7 @@
 #include <vector>
 
 #include "../../include/qwenscriber_cuda.h"
+#include "qwc_audio_model.h"
 #include "qwc_internal.h"
 #include "qwc_shard.h"
 
@@ -293,6 +294,8 @@ struct Handle {
   uint64_t weight_bytes = 0;
   KvMaps kv_maps{};
   std::unique_ptr<Batched> batched;  // streams > 1
+  std::unique_ptr<AudioModel> audio;  // the audio tower and projector, when the model carries them
+  DevBuf audio_out;                   // projected rows of the last clip [steps][text_hidden_size]
   std::vector<StreamSlot> slots;
   // Payload checksums of the shards added since qwc_model_begin, for the
   // reference's duplicate-shard check (src/wasm/model.zig:162-175).
@@ -346,12 +349,61 @@ void release_model(Handle* h) {
   }
   h->slots.clear();
   h->batched.reset();
+  h->audio.reset();
+  h->audio_out.alloc(0);
   h->weight_bytes = 0;
 }
 
 bool is_vector_kind(uint32_t kind) {
   return kind == QWC_KIND_DECODER_FINAL_NORM || kind == QWC_KIND_DECODER_Q_NORM || kind == QWC_KIND_DECODER_K_NORM ||
          kind == QWC_KIND_DECODER_ATTENTION_NORM || kind == QWC_KIND_DECODER_FFN_NORM;
+}
+
+// container.zig:334-362: the audio tower and projector kinds (1-29); their
+// biases and norm vectors; the f16 convolution weights.
+bool is_audio_kind(uint32_t kind) { return kind >= QWC_KIND_AUDIO_CONV1_WEIGHT && kind <= QWC_KIND_PROJECTOR_OUT_BIAS; }
+bool is_audio_vector_kind(uint32_t kind) {
+  switch (kind) {
+    case QWC_KIND_AUDIO_CONV1_BIAS: case QWC_KIND_AUDIO_CONV2_BIAS: case QWC_KIND_AUDIO_CONV3_BIAS:
+    case QWC_KIND_AUDIO_FINAL_NORM_WEIGHT: case QWC_KIND_AUDIO_FINAL_NORM_BIAS: case QWC_KIND_AUDIO_Q_BIAS:
+    case QWC_KIND_AUDIO_K_BIAS: case QWC_KIND_AUDIO_V_BIAS: case QWC_KIND_AUDIO_OUT_BIAS:
+    case QWC_KIND_AUDIO_ATTENTION_NORM_WEIGHT: case QWC_KIND_AUDIO_ATTENTION_NORM_BIAS:
+    case QWC_KIND_AUDIO_FFN_IN_BIAS: case QWC_KIND_AUDIO_FFN_OUT_BIAS: case QWC_KIND_AUDIO_FINAL_LAYER_NORM_WEIGHT:
+    case QWC_KIND_AUDIO_FINAL_LAYER_NORM_BIAS: case QWC_KIND_PROJECTOR_IN_BIAS: case QWC_KIND_PROJECTOR_OUT_BIAS:
+      return true;
+    default:
+      return false;
+  }
+}
+bool is_conv_kind(uint32_t kind) {
+  return kind == QWC_KIND_AUDIO_CONV1_WEIGHT || kind == QWC_KIND_AUDIO_CONV2_WEIGHT ||
+         kind == QWC_KIND_AUDIO_CONV3_WEIGHT;
+}
+
+// The tower's geometry from the configuration (model_config.zig:190-240).
+AudioGeometry audio_geometry(const Config& c) {
+  AudioGeometry g{};
+  g.d_model = c.audio_d_model;
+  g.layers = c.audio_layers;
+  g.heads = c.audio_attention_heads;
+  g.head_dim = c.audio_d_model / c.audio_attention_heads;
+  g.ffn = c.audio_ffn_dim;
+  g.channels = c.audio_downsample_hidden_size;
+  g.n_window = c.audio_n_window;
+  g.n_window_infer = c.audio_n_window_infer;
+  g.chunk_frames = c.audio_n_window * 2;
+  g.bins = conv_steps(c.mel_bins);
+  g.conv_features = g.channels * g.bins;
+  g.chunk_steps = conv_steps(g.chunk_frames);
+  g.max_position_steps = c.audio_max_position_steps;
+  g.output_dim = c.audio_output_dim;
+  g.mel_bins = c.mel_bins;
+  g.eps = c.audio_layer_norm_eps;
+  g.window = (c.audio_n_window_infer / g.chunk_frames) * g.chunk_steps;  // model.zig:243-246
+  g.max_frames = kCapacityFrames;
+  g.max_chunks = (kCapacityFrames + g.chunk_frames - 1) / g.chunk_frames;
+  g.max_steps = audio_packed_steps(g, kCapacityFrames);
+  return g;
 }
 
 DevMat make_mat(const Tensor& t) {
@@ -448,7 +500,6 @@ int32_t finish_model(Handle* h, const Config& c) {
   if (c.text_key_value_heads % 4 != 0) return QWC_UNSUPPORTED_MODEL;
   const bool tied = (c.flags & 1u) != 0;
 
-  bool any_q5 = false;
   auto find = [&](uint32_t kind, uint32_t layer) -> const Tensor* {
     auto it = h->tensors.find({kind, layer});
     return it == h->tensors.end() ? nullptr : &it->second;
@@ -459,7 +510,6 @@ int32_t finish_model(Handle* h, const Config& c) {
     if (!t) return QWC_NOT_FOUND;
     if (is_vector_kind(kind) || t->rows != rows || t->cols != cols) return QWC_SHAPE_MISMATCH;
     *out = make_mat(*t);
-    if (out->format == kFormatQ5) any_q5 = true;
     return kernel_fits(*out);
   };
   auto need_vec = [&](uint32_t kind, uint32_t layer, uint32_t width, const float** out) -> int32_t {
@@ -497,9 +547,6 @@ int32_t finish_model(Handle* h, const Config& c) {
       return QWC_UNSUPPORTED_MODEL;
     }
   }
-  // The batched engine's tensor-core GEMM reads q4 and q8 blocks only: a
-  // model with q5 matrices runs one stream (refused before any allocation).
-  if (any_q5 && h->streams > 1) return QWC_UNSUPPORTED_MODEL;
 
   cudaSetDevice(h->device);
   h->grid = decode_grid_size(h->device);
@@ -583,13 +630,33 @@ int32_t finish_model(Handle* h, const Config& c) {
   h->slots.clear();
   h->slots.resize(h->streams);
   h->config = c;
-  // Every handle with q4/q8 weights gets the batched engine: it runs the
-  // prompt prefills (64 positions per step) and, with streams > 1, the batched
-  // decode steps. Its tensor-core GEMM reads q4 and q8 blocks only; a model
-  // with q5 matrices runs one stream through the persistent kernel, and its
-  // prompts prefill token by token there.
-  if (any_q5) return QWC_OK;
+  // Every handle gets the batched engine: it runs the prompt prefills (64
+  // positions per step) and, with streams > 1, the batched decode steps.
   QWC_TRY(build_batched(h));
+  // The audio tower and projector, when the model carries any of their
+  // tensors (then all of them, as model.zig:965-990 requires).
+  bool any_audio = false;
+  for (const auto& kv : h->tensors) any_audio = any_audio || is_audio_kind(kv.first.first);
+  if (any_audio) {
+    auto audio = std::make_unique<AudioModel>();
+    auto find_audio = [h](uint32_t kind, uint32_t layer, AudioTensorView* out) {
+      auto it = h->tensors.find({kind, layer});
+      if (it == h->tensors.end()) return false;
+      const Tensor& t = it->second;
+      out->format = t.format;
+      out->rows = t.rows;
+      out->cols = t.cols;
+      out->dev = static_cast<const uint8_t*>(t.buf->ptr);
+      out->scales_offset = t.scales_offset;
+      out->codes_offset = t.codes_offset;
+      return true;
+    };
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, h->device);
+    QWC_TRY(audio->build(audio_geometry(c), find_audio, sms));
+    QWC_TRY(h->audio_out.alloc(size_t(audio->g.max_steps) * c.audio_output_dim * 4));
+    h->audio = std::move(audio);
+  }
   return QWC_OK;
 }
 
@@ -1028,8 +1095,10 @@ int32_t batched_run_timed(Handle* h, uint32_t steps, float* device_ms) {
   return QWC_OK;
 }
 
+// `audio_on_device`: the audio rows are device memory (the tower's output)
+// rather than host memory.
 int32_t stream_begin(Handle* h, uint32_t slot, const uint32_t* prompt, uint32_t prompt_len, const float* audio,
-                     uint32_t audio_steps, uint32_t max_tokens) {
+                     uint32_t audio_steps, uint32_t max_tokens, bool audio_on_device = false) {
   if (h->state != State::kLoaded) return QWC_INVALID_STATE;
   if (slot >= h->slots.size()) return QWC_INVALID_ARGUMENT;
   StreamSlot& s = h->slots[slot];
@@ -1061,7 +1130,8 @@ int32_t stream_begin(Handle* h, uint32_t slot, const uint32_t* prompt, uint32_t 
   if (audio_steps) {
     s.audio = std::make_unique<DevBuf>();
     QWC_TRY(s.audio->alloc(size_t(audio_steps) * c.text_hidden_size * 4));
-    QWC_CUDA(cudaMemcpyAsync(s.audio->ptr, audio, s.audio->bytes, cudaMemcpyHostToDevice, h->stream));
+    QWC_CUDA(cudaMemcpyAsync(s.audio->ptr, audio, s.audio->bytes,
+                             audio_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, h->stream));
     dev_audio = s.audio->as<float>();
   }
   if (h->batched) {
@@ -1078,7 +1148,7 @@ int32_t stream_begin(Handle* h, uint32_t slot, const uint32_t* prompt, uint32_t 
                              h->stream));
     if (audio_steps) {
       QWC_CUDA(cudaMemcpyAsync(h->audio_rows.ptr, audio, size_t(audio_steps) * c.text_hidden_size * 4,
-                               cudaMemcpyHostToDevice, h->stream));
+                               audio_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, h->stream));
     }
     std::vector<uint32_t> tokens;
     QWC_TRY(run_decode(h, prompt_len, 0, prompt_len, 0, prompt_len - 1, &tokens));
@@ -1146,6 +1216,31 @@ int32_t stream_step(Handle* h, uint32_t slot, uint32_t* token_out) {
 }  // namespace qwc
 
 using namespace qwc;
+
+namespace {
+
+uint64_t audio_wait_ns(const Handle* h) { return h->wait_limit_ns ? h->wait_limit_ns : kBatchedWaitNs; }
+
+// Uploads one clip's log-mel features and runs the tower and projector into
+// h->audio_out. model.zig:380-386's checks: a whole number of mel columns,
+// at least one frame, at most the mel capacity.
+int32_t run_audio(Handle* h, const float* features, uint64_t floats, uint32_t* steps_out) {
+  if (!h->audio) return QWC_NOT_FOUND;
+  if (!features) return QWC_INVALID_ARGUMENT;
+  const AudioGeometry& g = h->audio->g;
+  if (floats == 0 || floats % g.mel_bins != 0) return QWC_SHAPE_MISMATCH;
+  const uint64_t frames = floats / g.mel_bins;
+  if (frames > g.max_frames) return QWC_AUDIO_TOO_LONG;
+  cudaSetDevice(h->device);
+  float* mel = h->audio->mel_buffer();
+  QWC_CUDA(cudaMemcpyAsync(mel, features, floats * 4, cudaMemcpyHostToDevice, h->stream));
+  const int32_t st = h->audio->run(mel, static_cast<uint32_t>(frames), h->audio_out.as<float>(), h->stream,
+                                   audio_wait_ns(h), steps_out);
+  h->launches += h->audio->launches();
+  return st;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -1254,7 +1349,9 @@ int32_t add_tensor(Handle* h, uint32_t kind, uint32_t layer, uint32_t format, ui
                    const void* payload, uint64_t len) {
   if (h->state != State::kReady) return QWC_INVALID_STATE;
   if (!payload || rows == 0 || cols == 0) return QWC_INVALID_ARGUMENT;
-  if (kind < QWC_KIND_DECODER_EMBED_TOKENS || kind > QWC_KIND_DECODER_DOWN) return QWC_UNSUPPORTED_MODEL;
+  if (!is_audio_kind(kind) && (kind < QWC_KIND_DECODER_EMBED_TOKENS || kind > QWC_KIND_DECODER_DOWN)) {
+    return QWC_UNSUPPORTED_MODEL;
+  }
   if (h->tensors.count({kind, layer})) return QWC_INVALID_ARGUMENT;  // DuplicateTensor
   Tensor t;
   t.kind = kind;
@@ -1265,6 +1362,8 @@ int32_t add_tensor(Handle* h, uint32_t kind, uint32_t layer, uint32_t format, ui
   uint64_t need = 0;
   if (format == QWC_FORMAT_F32) {
     need = uint64_t(rows) * cols * 4;
+  } else if (format == QWC_FORMAT_F16 && is_conv_kind(kind)) {
+    need = uint64_t(rows) * cols * 2;  // layout.zig:150-175: the convolutions stay f16 (element_f16)
   } else if (format == QWC_FORMAT_Q4 || format == QWC_FORMAT_Q5 || format == QWC_FORMAT_Q8) {
     if (cols % kGroup != 0) return QWC_SHAPE_MISMATCH;  // RowNotGroupAligned (quant.zig:77-81)
     // quant.zig:144-176 with a 16-byte-aligned base.
@@ -1283,7 +1382,7 @@ int32_t add_tensor(Handle* h, uint32_t kind, uint32_t layer, uint32_t format, ui
   QWC_CUDA(cudaMemcpy(t.buf->ptr, payload, need, cudaMemcpyHostToDevice));
   h->weight_bytes += need;
   t.src_len = len;
-  t.rank = (rows == 1 && is_vector_kind(kind)) ? 1u : 2u;
+  t.rank = (rows == 1 && (is_vector_kind(kind) || is_audio_vector_kind(kind))) ? 1u : 2u;
   t.dims[0] = t.rank == 1 ? cols : rows;
   if (t.rank == 2) t.dims[1] = cols;
   h->tensors.emplace(std::make_pair(kind, layer), std::move(t));
@@ -1326,20 +1425,20 @@ int32_t qwc_model_add_shard(uint32_t handle, const void* bytes, uint64_t len) {
   for (uint32_t c : h->shards) {
     if (c == v.checksum) return QWC_INVALID_ARGUMENT;
   }
-  // Every decoder tensor is checked before any is copied, so a rejected shard
-  // leaves the handle as it was. Tensors of other kinds (audio tower,
-  // projector) are validated by the parse and otherwise not kept: this
-  // library runs the decoder only.
-  auto decoder_kind = [](uint32_t kind) {
-    return kind >= QWC_KIND_DECODER_EMBED_TOKENS && kind <= QWC_KIND_DECODER_DOWN;
+  // Every tensor is checked before any is copied, so a rejected shard leaves
+  // the handle as it was. Decoder, audio-tower and projector tensors are kept
+  // on the device.
+  auto kept_kind = [](uint32_t kind) {
+    return is_audio_kind(kind) || (kind >= QWC_KIND_DECODER_EMBED_TOKENS && kind <= QWC_KIND_DECODER_DOWN);
   };
   for (uint32_t i = 0; i < v.count; ++i) {
     const ShardEntry e = shard_entry(v, i);
-    if (!decoder_kind(e.kind)) continue;
+    if (!kept_kind(e.kind)) continue;
     const bool vec = e.rank == 1 && e.format == QWC_FORMAT_F32;
     const bool mat = e.rank == 2 && (e.format == QWC_FORMAT_Q4 || e.format == QWC_FORMAT_Q5 ||
                                      e.format == QWC_FORMAT_Q8 || e.format == QWC_FORMAT_F32);
-    if (!vec && !mat) return QWC_UNSUPPORTED_MODEL;
+    const bool conv = e.rank == 4 && e.format == QWC_FORMAT_F16 && is_conv_kind(e.kind);
+    if (!vec && !mat && !conv) return QWC_UNSUPPORTED_MODEL;
     if (h->tensors.count({e.kind, e.layer})) return QWC_INVALID_ARGUMENT;  // DuplicateTensor
   }
   // A copy that fails part way (out of device memory) takes back the
@@ -1349,9 +1448,10 @@ int32_t qwc_model_add_shard(uint32_t handle, const void* bytes, uint64_t len) {
   const uint64_t weight_bytes0 = h->weight_bytes;
   for (uint32_t i = 0; i < v.count; ++i) {
     const ShardEntry e = shard_entry(v, i);
-    if (!decoder_kind(e.kind)) continue;
+    if (!kept_kind(e.kind)) continue;
+    // A convolution [out][in][3][3] is kept as out rows of in * 9 values.
     const uint32_t rows = e.rank == 1 ? 1u : e.dims[0];
-    const uint32_t cols = e.rank == 1 ? e.dims[0] : e.dims[1];
+    const uint32_t cols = e.rank == 1 ? e.dims[0] : e.rank == 4 ? e.dims[1] * e.dims[2] * e.dims[3] : e.dims[1];
     const int32_t st = add_tensor(h, e.kind, e.layer, e.format, rows, cols, v.payload + e.offset_bytes, e.len_bytes);
     if (st != QWC_OK) {
       for (const auto& key : added) h->tensors.erase(key);
@@ -1417,9 +1517,11 @@ int32_t qwc_model_finish(uint32_t handle, const void* config, uint32_t config_le
     for (DevBuf* b : {&h->model_buf, &h->rope_cos, &h->rope_sin, &h->k_cache, &h->v_cache, &h->qkv, &h->attn_out,
                       &h->hidden_g, &h->act, &h->attn_part, &h->attn_count, &h->amax_val, &h->amax_idx, &h->barrier,
                       &h->error, &h->tokens_out, &h->logits, &h->prompt_ids, &h->prompt_rows, &h->audio_rows,
-                      &h->exact_scratch}) {
+                      &h->exact_scratch, &h->audio_out}) {
       b->alloc(0);
     }
+    h->audio.reset();
+    h->batched.reset();
     return st;
   }
   h->state = State::kLoaded;
@@ -1664,6 +1766,117 @@ int32_t qwc_debug_cache(uint32_t handle, uint32_t slot, uint32_t which, void* ou
   QWC_CUDA(cudaMemcpyAsync(out, src, stride, cudaMemcpyDeviceToHost, h->stream));
   QWC_CUDA(cudaStreamSynchronize(h->stream));
   return QWC_OK;
+}
+
+int32_t qwc_model_audio_config(uint32_t handle, qwc_audio_config* out) {
+  Handle* h = lookup(handle);
+  if (!h || !out) return QWC_INVALID_ARGUMENT;
+  if (h->state != State::kLoaded) return QWC_INVALID_STATE;
+  const AudioGeometry g = audio_geometry(h->config);
+  qwc_audio_config a{};
+  a.d_model = g.d_model;
+  a.layers = g.layers;
+  a.attention_heads = g.heads;
+  a.head_dim = g.head_dim;
+  a.ffn_dim = g.ffn;
+  a.downsample_hidden_size = g.channels;
+  a.n_window = g.n_window;
+  a.n_window_infer = g.n_window_infer;
+  a.chunk_frames = g.chunk_frames;
+  a.frequency_bins = g.bins;
+  a.conv_out_input_features = g.conv_features;
+  a.chunk_steps = g.chunk_steps;
+  a.max_position_steps = g.max_position_steps;
+  a.output_dim = g.output_dim;
+  a.mel_bins = g.mel_bins;
+  a.layer_norm_eps = g.eps;
+  *out = a;
+  return QWC_OK;
+}
+
+int32_t qwc_audio_project(uint32_t handle, const float* log_mel, uint32_t frames, float* out,
+                          uint64_t out_capacity_floats, uint32_t* steps_out) {
+  Handle* h = lookup(handle);
+  if (!h || !out) return QWC_INVALID_ARGUMENT;
+  if (h->state != State::kLoaded) return QWC_INVALID_STATE;
+  if (!h->audio) return QWC_NOT_FOUND;
+  if (frames == 0) return QWC_SHAPE_MISMATCH;
+  if (frames > h->audio->g.max_frames) return QWC_AUDIO_TOO_LONG;
+  const uint32_t steps = audio_packed_steps(h->audio->g, frames);
+  if (out_capacity_floats < uint64_t(steps) * h->audio->g.output_dim) return QWC_LIMIT_EXCEEDED;
+  uint32_t got = 0;
+  QWC_TRY(run_audio(h, log_mel, uint64_t(frames) * h->audio->g.mel_bins, &got));
+  QWC_CUDA(cudaMemcpyAsync(out, h->audio_out.ptr, uint64_t(got) * h->audio->g.output_dim * 4, cudaMemcpyDeviceToHost,
+                           h->stream));
+  QWC_CUDA(cudaStreamSynchronize(h->stream));
+  if (steps_out) *steps_out = got;
+  return QWC_OK;
+}
+
+int32_t qwc_stream_begin_features(uint32_t handle, uint32_t slot, const uint32_t* prompt, uint32_t prompt_len,
+                                  const float* features, uint64_t features_len, uint32_t max_tokens) {
+  Handle* h = lookup(handle);
+  if (!h) return QWC_INVALID_ARGUMENT;
+  if (h->state != State::kLoaded) return QWC_INVALID_STATE;
+  if (slot >= h->slots.size()) return QWC_INVALID_ARGUMENT;
+  if (h->slots[slot].decoding) return QWC_INVALID_STATE;
+  if (max_tokens == 0 || max_tokens > h->config.max_decode_tokens) return QWC_LIMIT_EXCEEDED;  // model.zig:380-381
+  if (features_len == 0 || features_len % 4 != 0) return QWC_INVALID_ARGUMENT;                 // exports.zig:450-451
+  uint32_t steps = 0;
+  QWC_TRY(run_audio(h, features, features_len / 4, &steps));
+  return stream_begin(h, slot, prompt, prompt_len, h->audio_out.as<float>(), steps, max_tokens, true);
+}
+
+int32_t qwc_decode_begin_features(uint32_t handle, const uint32_t* prompt, uint32_t prompt_len, const float* features,
+                                  uint64_t features_len, uint32_t max_tokens) {
+  Handle* h = lookup(handle);
+  if (!h) return QWC_INVALID_ARGUMENT;
+  if (h->streams > 1) return QWC_UNSUPPORTED;
+  return qwc_stream_begin_features(handle, 0, prompt, prompt_len, features, features_len, max_tokens);
+}
+
+int32_t qwc_debug_audio(uint32_t handle, uint32_t which, float* out, uint64_t count) {
+  Handle* h = lookup(handle);
+  if (!h || !out || which > 1) return QWC_INVALID_ARGUMENT;
+  if (!h->audio) return QWC_NOT_FOUND;
+  const uint64_t n = std::min<uint64_t>(count, uint64_t(h->audio->g.max_steps) * h->audio->g.d_model);
+  const float* src = which == 0 ? h->audio->conv_stage() : h->audio->tower();
+  QWC_CUDA(cudaMemcpy(out, src, n * 4, cudaMemcpyDeviceToHost));
+  return static_cast<int32_t>(n);
+}
+
+int32_t qwc_audio_run_timed(uint32_t handle, const float* log_mel, uint32_t frames, uint32_t reps, float* device_ms,
+                            uint32_t* launches_out) {
+  Handle* h = lookup(handle);
+  if (!h || !log_mel || !device_ms || reps == 0) return QWC_INVALID_ARGUMENT;
+  if (h->state != State::kLoaded) return QWC_INVALID_STATE;
+  if (!h->audio) return QWC_NOT_FOUND;
+  if (frames == 0) return QWC_SHAPE_MISMATCH;
+  if (frames > h->audio->g.max_frames) return QWC_AUDIO_TOO_LONG;
+  cudaSetDevice(h->device);
+  float* mel = h->audio->mel_buffer();
+  QWC_CUDA(cudaMemcpyAsync(mel, log_mel, uint64_t(frames) * h->audio->g.mel_bins * 4, cudaMemcpyHostToDevice,
+                           h->stream));
+  cudaEvent_t e0, e1;
+  QWC_CUDA(cudaEventCreate(&e0));
+  QWC_CUDA(cudaEventCreate(&e1));
+  int32_t st = QWC_OK;
+  uint32_t steps = 0;
+  cudaEventRecord(e0, h->stream);
+  for (uint32_t r = 0; r < reps && st == QWC_OK; ++r) {
+    st = h->audio->run(mel, frames, h->audio_out.as<float>(), h->stream, audio_wait_ns(h), &steps, false);
+    h->launches += h->audio->launches();
+  }
+  cudaEventRecord(e1, h->stream);
+  if (st == QWC_OK) st = h->audio->check_error(h->stream);
+  cudaEventSynchronize(e1);
+  float ms = 0.0f;
+  cudaEventElapsedTime(&ms, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  *device_ms = ms;
+  if (launches_out) *launches_out = static_cast<uint32_t>(h->audio->launches());
+  return st;
 }
 
 uint64_t qwc_kernel_launches(uint32_t handle) {

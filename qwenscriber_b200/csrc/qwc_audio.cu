@@ -1,0 +1,465 @@
+// qwc_audio.cu -- the audio tower and projector (Model.projectAudio,
+// src/core/qwen3_asr/model.zig:445-744) on the device: every kernel of the
+// tower except its GEMMs, which are the tensor-core GEMMs of qwc_gemm.cu
+// (dense f16 weights for the convolutions, quantized weights for the rest).
+//
+// Data layout (one clip, `chunks` convolution chunks of chunk_frames mel
+// frames, `steps` packed encoder steps):
+//   conv planes   channel-last f32 [chunk][height][width][channel], so a
+//                 convolution tap reads 8 consecutive input channels with
+//                 two 16-byte loads;
+//   GEMM inputs   f16 hi and lo rows per 64-column block (the layout of the
+//                 GEMMs' activation boxes); the convolutions' K index is
+//                 (tap, input channel) in natural order, the quantized GEMMs'
+//                 K chunks of 8 are permuted [0 4 1 5 2 6 3 7];
+//   tower rows    f32 [step][width] (the reference's encoder scratch).
+//
+// Parity: the first convolution, GELU (math.zig:46-66) and the sinusoidal
+// position rows are the reference's arithmetic in its order. The GEMM-shaped
+// steps (convolutions 2 and 3, every projection) sum in another order with
+// 22-bit activations, and the LayerNorm and attention reductions are trees,
+// so the tower agrees with the reference to f32 rounding, not bit for bit.
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#include "../../include/qwenscriber_cuda.h"
+#include "qwc_device.cuh"
+#include "qwc_internal.h"
+
+namespace qwc {
+namespace {
+
+constexpr uint32_t kCols = 64;  // GEMM columns per column block
+// K order inside an 8-value chunk of the quantized GEMMs' activation rows:
+// position e holds value perm8(e) = [0 4 1 5 2 6 3 7][e].
+__host__ __device__ constexpr int perm8(int e) { return (e & 1) ? 4 + (e >> 1) : (e >> 1); }
+
+// math.zig:46-60, rounded as written (no contraction).
+__device__ __forceinline__ float erf_ref(float x) {
+  const float sign = x < 0.0f ? -1.0f : 1.0f;
+  const float m = fabsf(x);
+  const float t = __fdiv_rn(1.0f, __fadd_rn(1.0f, __fmul_rn(0.5f, m)));
+  float poly = __fadd_rn(-0.82215223f, __fmul_rn(t, 0.17087277f));
+  poly = __fadd_rn(1.48851587f, __fmul_rn(t, poly));
+  poly = __fadd_rn(-1.13520398f, __fmul_rn(t, poly));
+  poly = __fadd_rn(0.27886807f, __fmul_rn(t, poly));
+  poly = __fadd_rn(-0.18628806f, __fmul_rn(t, poly));
+  poly = __fadd_rn(0.09678418f, __fmul_rn(t, poly));
+  poly = __fadd_rn(0.37409196f, __fmul_rn(t, poly));
+  poly = __fadd_rn(1.00002368f, __fmul_rn(t, poly));
+  const float arg = __fadd_rn(__fsub_rn(__fmul_rn(-m, m), 1.26551223f), __fmul_rn(t, poly));
+  const float tau = __fmul_rn(t, exp_ref(arg));
+  return __fmul_rn(sign, __fsub_rn(1.0f, tau));
+}
+
+// math.zig:63-66
+__device__ __forceinline__ float gelu_ref(float x) {
+  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, erf_ref(__fmul_rn(x, 0.70710678f))));
+}
+
+__device__ __forceinline__ void split_store(__half* hi_row, __half* lo_row, const float (&v)[8]) {
+  __align__(16) __half hi[8];
+  __align__(16) __half lo[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    hi[j] = __float2half_rn(v[j]);
+    lo[j] = __float2half_rn(v[j] - __half2float(hi[j]));
+  }
+  *reinterpret_cast<uint4*>(hi_row) = *reinterpret_cast<const uint4*>(hi);
+  *reinterpret_cast<uint4*>(lo_row) = *reinterpret_cast<const uint4*>(lo);
+}
+
+// The f16 hi row of GEMM column `col` in a packed buffer of `k` columns per
+// row; its lo row is kCols rows further.
+__device__ __forceinline__ __half* packed_row(__half* base, uint32_t col, uint32_t k) {
+  return base + (size_t(col / kCols) * (2 * kCols) + col % kCols) * k;
+}
+
+// ---- convolution 1 (one input channel): kernels.zig:332-432 ----
+// mel [mel_bins][frames] -> out [chunk][h1][w1][channels], zero frames past
+// the clip (the reference pads each chunk in the mel domain, model.zig:535-545).
+__global__ void audio_conv1_kernel(const float* mel, uint32_t frames, uint32_t mel_bins, uint32_t chunk_frames,
+                                   uint32_t chunks, const __half* w, const float* bias, uint32_t channels,
+                                   float* out) {
+  pdl_wait_and_trigger();
+  const uint32_t h1 = (mel_bins - 1) / 2 + 1, w1 = (chunk_frames - 1) / 2 + 1;
+  const size_t total = size_t(chunks) * h1 * w1 * channels;
+  for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
+    const uint32_t oc = static_cast<uint32_t>(i % channels);
+    size_t rest = i / channels;
+    const uint32_t ox = static_cast<uint32_t>(rest % w1);
+    rest /= w1;
+    const uint32_t oy = static_cast<uint32_t>(rest % h1);
+    const uint32_t chunk = static_cast<uint32_t>(rest / h1);
+    float acc = 0.0f;
+#pragma unroll
+    for (int ky = 0; ky < 3; ++ky) {
+      const int iy = int(2 * oy) + ky - 1;
+      if (iy < 0 || iy >= int(mel_bins)) continue;
+#pragma unroll
+      for (int kx = 0; kx < 3; ++kx) {
+        const int ix = int(2 * ox) + kx - 1;
+        if (ix < 0 || ix >= int(chunk_frames)) continue;
+        const uint32_t frame = chunk * chunk_frames + uint32_t(ix);
+        const float sample = frame < frames ? mel[size_t(iy) * frames + frame] : 0.0f;
+        acc = __fadd_rn(acc, __fmul_rn(__half2float(w[oc * 9 + ky * 3 + kx]), sample));
+      }
+    }
+    out[i] = gelu_ref(__fadd_rn(bias[oc], acc));
+  }
+}
+
+// ---- im2col for convolutions 2 and 3 ----
+// in [chunk][ih][iw][channels] -> GEMM activation rows, column n =
+// (chunk, oy, ox), K index (ky * 3 + kx) * channels + ic, zero past 9 channels
+// and outside the input (padding 1). channels % 8 == 0.
+__global__ void audio_im2col_kernel(const float* in, uint32_t chunks, uint32_t ih, uint32_t iw, uint32_t channels,
+                                    uint32_t kpad, __half* out) {
+  pdl_wait_and_trigger();
+  const uint32_t oh = (ih - 1) / 2 + 1, ow = (iw - 1) / 2 + 1;
+  const uint32_t columns = chunks * oh * ow, groups = kpad / 8, taps_k = 9 * channels;
+  const size_t total = size_t(columns) * groups;
+  for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
+    const uint32_t g = static_cast<uint32_t>(i % groups), col = static_cast<uint32_t>(i / groups);
+    const uint32_t k0 = g * 8;
+    float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (k0 < taps_k) {
+      const uint32_t tap = k0 / channels, ic = k0 % channels;
+      const uint32_t ox = col % ow, oy = (col / ow) % oh, chunk = col / (ow * oh);
+      const int iy = int(2 * oy) + int(tap / 3) - 1, ix = int(2 * ox) + int(tap % 3) - 1;
+      if (iy >= 0 && iy < int(ih) && ix >= 0 && ix < int(iw)) {
+        const float4* src =
+            reinterpret_cast<const float4*>(in + ((size_t(chunk) * ih + iy) * iw + ix) * channels + ic);
+        const float4 a = src[0], b = src[1];
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      }
+    }
+    __half* hi = packed_row(out, col, kpad) + k0;
+    split_store(hi, hi + size_t(kCols) * kpad, v);
+  }
+}
+
+// Convolution epilogue: out[n][c] = gelu(bias[c] + sum of the split partials).
+__global__ void audio_conv_epilogue_kernel(const float* parts, uint32_t splits, uint32_t columns, uint32_t channels,
+                                           const float* bias, float* out) {
+  pdl_wait_and_trigger();
+  const size_t n = size_t(columns) * channels;
+  for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
+    float acc = parts[i];
+    for (uint32_t sp = 1; sp < splits; ++sp) acc += parts[size_t(sp) * n + i];
+    out[i] = gelu_ref(__fadd_rn(bias[i % channels], acc));
+  }
+}
+
+// model.zig:580-597: the conv_out input of packed step p (chunk p / steps,
+// time step p % steps) is flat[c * bins + f] = conv3[chunk][f][t][c]; packed
+// for the quantized GEMM (K chunks permuted).
+__global__ void audio_flatten_kernel(const float* conv3, uint32_t steps, uint32_t chunk_steps, uint32_t bins,
+                                     uint32_t channels, __half* out) {
+  pdl_wait_and_trigger();
+  const uint32_t k = channels * bins, groups = k / 8;
+  const size_t total = size_t(steps) * groups;
+  for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
+    const uint32_t g = static_cast<uint32_t>(i % groups), p = static_cast<uint32_t>(i / groups);
+    const uint32_t chunk = p / chunk_steps, t = p % chunk_steps;
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const uint32_t j = g * 8 + perm8(e), c = j / bins, f = j % bins;
+      v[e] = conv3[((size_t(chunk) * bins + f) * chunk_steps + t) * channels + c];
+    }
+    __half* hi = packed_row(out, p, k) + g * 8;
+    split_store(hi, hi + size_t(kCols) * k, v);
+  }
+}
+
+// Epilogues of the tower's quantized GEMMs over parts[split][steps][ld]
+// (columns [col0, col0 + width) of each row):
+//   kPosition  x[p][i] = sum + position[p % chunk_steps][i]   (conv_out, model.zig:600-601)
+//   kBias      x[p][i] = sum + bias[i]                        (q|k|v, projector out)
+//   kResidual  x[p][i] = x[p][i] + (sum + bias[i])           (kernels.zig:221-230)
+//   kGeluPack  gelu(sum + bias[i]) into GEMM activation rows (model.zig:863-866, 719)
+enum EpilogueMode : int { kPosition = 0, kBias = 1, kResidual = 2, kGeluPack = 3 };
+
+template <int Mode>
+__global__ void audio_epilogue_kernel(const float* parts, uint32_t splits, uint32_t steps, uint32_t ld,
+                                      uint32_t width, const float* add, uint32_t chunk_steps, float* x,
+                                      uint32_t x_ld, __half* packed) {
+  pdl_wait_and_trigger();
+  const uint32_t groups = width / 8;
+  const size_t total = size_t(steps) * groups, plane = size_t(steps) * ld;
+  for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
+    const uint32_t g = static_cast<uint32_t>(i % groups), p = static_cast<uint32_t>(i / groups);
+    const float* src = parts + size_t(p) * ld + g * 8;
+    float v[8];
+    {
+      const float4 a = reinterpret_cast<const float4*>(src)[0], b = reinterpret_cast<const float4*>(src)[1];
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+      v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    }
+    for (uint32_t sp = 1; sp < splits; ++sp) {
+      const float4 a = reinterpret_cast<const float4*>(src + sp * plane)[0];
+      const float4 b = reinterpret_cast<const float4*>(src + sp * plane)[1];
+      v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
+      v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+    }
+    const float* addp = Mode == kPosition ? add + size_t(p % chunk_steps) * width + g * 8 : add + g * 8;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], addp[e]);
+    if (Mode == kGeluPack) {
+      float w[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) w[e] = gelu_ref(v[perm8(e)]);
+      __half* hi = packed_row(packed, p, width) + g * 8;
+      split_store(hi, hi + size_t(kCols) * width, w);
+    } else {
+      float* dst = x + size_t(p) * x_ld + g * 8;
+      if (Mode == kResidual) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(dst[e], v[e]);
+      }
+      reinterpret_cast<float4*>(dst)[0] = make_float4(v[0], v[1], v[2], v[3]);
+      reinterpret_cast<float4*>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
+  }
+}
+
+// LayerNorm of each step row (math.zig:99-116: mean, then the mean of the
+// centred squares, 1 / sqrt(var + eps), (x - mean) * inv * w + b), one
+// 128-thread block per row; writes the f32 row (`out`, may alias `x`) and/or
+// the GEMM activation rows (`packed`). width % 8 == 0, width <= 128 * 8 * 4.
+constexpr int kNormThreads = 128;
+constexpr int kNormMaxChunks = 4;  // 8-value chunks per thread
+
+__global__ void __launch_bounds__(kNormThreads) audio_layernorm_kernel(const float* x, const float* weight,
+                                                                       const float* bias, uint32_t width, float eps,
+                                                                       float* out, __half* packed) {
+  pdl_wait_and_trigger();
+  __shared__ float red[kNormThreads / 32];
+  __shared__ float stat;
+  const uint32_t p = blockIdx.x, tid = threadIdx.x, chunks = width / 8;
+  const float* row = x + size_t(p) * width;
+  float v[kNormMaxChunks][8];
+  float sum = 0.0f;
+#pragma unroll
+  for (int c = 0; c < kNormMaxChunks; ++c) {
+    const uint32_t ch = tid + c * kNormThreads;
+    if (ch < chunks) {
+      const float4 a = reinterpret_cast<const float4*>(row + ch * 8)[0];
+      const float4 b = reinterpret_cast<const float4*>(row + ch * 8)[1];
+      v[c][0] = a.x; v[c][1] = a.y; v[c][2] = a.z; v[c][3] = a.w;
+      v[c][4] = b.x; v[c][5] = b.y; v[c][6] = b.z; v[c][7] = b.w;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sum += v[c][e];
+    }
+  }
+  auto block_sum = [&](float s) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((tid & 31) == 0) red[tid / 32] = s;
+    __syncthreads();
+    if (tid == 0) {
+      float t = 0.0f;
+      for (int w = 0; w < kNormThreads / 32; ++w) t += red[w];
+      stat = t;
+    }
+    __syncthreads();
+    const float r = stat;
+    __syncthreads();
+    return r;
+  };
+  const float mean = __fdiv_rn(block_sum(sum), static_cast<float>(width));
+  float sq = 0.0f;
+#pragma unroll
+  for (int c = 0; c < kNormMaxChunks; ++c) {
+    if (tid + c * kNormThreads < chunks) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float d = __fsub_rn(v[c][e], mean);
+        sq = __fadd_rn(sq, __fmul_rn(d, d));
+      }
+    }
+  }
+  const float variance = __fdiv_rn(block_sum(sq), static_cast<float>(width));
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(variance, eps)));
+#pragma unroll
+  for (int c = 0; c < kNormMaxChunks; ++c) {
+    const uint32_t ch = tid + c * kNormThreads;
+    if (ch < chunks) {
+      float y[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const uint32_t i = ch * 8 + e;
+        y[e] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[c][e], mean), inv), weight[i]), bias[i]);
+      }
+      if (out) {
+        float* dst = out + size_t(p) * width + ch * 8;
+        reinterpret_cast<float4*>(dst)[0] = make_float4(y[0], y[1], y[2], y[3]);
+        reinterpret_cast<float4*>(dst)[1] = make_float4(y[4], y[5], y[6], y[7]);
+      }
+      if (packed) {
+        float z[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) z[e] = y[perm8(e)];
+        __half* hi = packed_row(packed, p, width) + ch * 8;
+        split_store(hi, hi + size_t(kCols) * width, z);
+      }
+    }
+  }
+}
+
+// kernels.zig:435-487 for one (window, head): scores = q.k / sqrt(head_dim)
+// over the window's keys, softmax (math.zig:77-93), weighted sum of values.
+// qkv rows [step][3 width] (q | k | v); out [step][width]. One CTA per
+// (window, head), 8 warps over the window's queries; keys and values of the
+// window in shared memory (key rows padded by one float against bank
+// conflicts). head_dim <= 128.
+constexpr int kAttnWarps = 8;
+
+__global__ void __launch_bounds__(kAttnWarps * 32) audio_window_attention_kernel(const float* qkv, uint32_t steps,
+                                                                                 uint32_t width, uint32_t head_dim,
+                                                                                 uint32_t window, float* out) {
+  pdl_wait_and_trigger();
+  extern __shared__ float attn_smem[];
+  const uint32_t w0 = blockIdx.x * window, h = blockIdx.y;
+  const uint32_t len = min(window, steps - w0);
+  const uint32_t kstride = head_dim + 1;
+  float* ks = attn_smem;                                   // [window][head_dim + 1]
+  float* vs = ks + size_t(window) * kstride;               // [window][head_dim]
+  float* qs = vs + size_t(window) * head_dim;              // [warps][head_dim]
+  float* ps = qs + size_t(kAttnWarps) * head_dim;          // [warps][window]
+  const uint32_t ld = 3 * width;
+  for (uint32_t i = threadIdx.x; i < len * head_dim; i += blockDim.x) {
+    const uint32_t j = i / head_dim, d = i % head_dim;
+    const float* r = qkv + size_t(w0 + j) * ld + h * head_dim + d;
+    ks[j * kstride + d] = r[width];
+    vs[j * head_dim + d] = r[2 * width];
+  }
+  __syncthreads();
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const float scaling = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(head_dim)));
+  float* q = qs + warp * head_dim;
+  float* pw = ps + warp * window;
+  for (uint32_t qi = warp; qi < len; qi += kAttnWarps) {
+    for (uint32_t d = lane; d < head_dim; d += 32) q[d] = qkv[size_t(w0 + qi) * ld + h * head_dim + d];
+    __syncwarp();
+    float mx = -INFINITY;
+    for (uint32_t j = lane; j < len; j += 32) {
+      const float* kr = ks + j * kstride;
+      float acc = 0.0f;
+      for (uint32_t d = 0; d < head_dim; ++d) acc = fmaf(q[d], kr[d], acc);
+      const float s = __fmul_rn(acc, scaling);
+      pw[j] = s;
+      mx = fmaxf(mx, s);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float total = 0.0f;
+    for (uint32_t j = lane; j < len; j += 32) {
+      const float e = exp_ref(__fsub_rn(pw[j], mx));
+      pw[j] = e;
+      total += e;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+    const float inv = __fdiv_rn(1.0f, total);
+    __syncwarp();
+    for (uint32_t d = lane; d < head_dim; d += 32) {
+      float acc = 0.0f;
+      for (uint32_t j = 0; j < len; ++j) acc = fmaf(vs[j * head_dim + d], __fmul_rn(pw[j], inv), acc);
+      out[size_t(w0 + qi) * width + h * head_dim + d] = acc;
+    }
+    __syncwarp();
+  }
+}
+
+uint32_t grid_for(size_t work, uint32_t threads) {
+  const size_t blocks = (work + threads - 1) / threads;
+  return static_cast<uint32_t>(blocks < 148 * 16 ? (blocks ? blocks : 1) : 148 * 16);
+}
+
+}  // namespace
+
+int launch_audio_conv1(const float* mel, uint32_t frames, uint32_t mel_bins, uint32_t chunk_frames, uint32_t chunks,
+                       const void* w, const float* bias, uint32_t channels, float* out, void* stream) {
+  const size_t work = size_t(chunks) * ((mel_bins - 1) / 2 + 1) * ((chunk_frames - 1) / 2 + 1) * channels;
+  return static_cast<int>(launch_pdl(audio_conv1_kernel, dim3(grid_for(work, 256)), dim3(256), 0,
+                                     static_cast<cudaStream_t>(stream), mel, frames, mel_bins, chunk_frames, chunks,
+                                     static_cast<const __half*>(w), bias, channels, out));
+}
+
+int launch_audio_im2col(const float* in, uint32_t chunks, uint32_t ih, uint32_t iw, uint32_t channels, uint32_t kpad,
+                        void* out, void* stream) {
+  const size_t work = size_t(chunks) * ((ih - 1) / 2 + 1) * ((iw - 1) / 2 + 1) * (kpad / 8);
+  return static_cast<int>(launch_pdl(audio_im2col_kernel, dim3(grid_for(work, 256)), dim3(256), 0,
+                                     static_cast<cudaStream_t>(stream), in, chunks, ih, iw, channels, kpad,
+                                     static_cast<__half*>(out)));
+}
+
+int launch_audio_conv_epilogue(const float* parts, uint32_t splits, uint32_t columns, uint32_t channels,
+                               const float* bias, float* out, void* stream) {
+  return static_cast<int>(launch_pdl(audio_conv_epilogue_kernel, dim3(grid_for(size_t(columns) * channels, 256)),
+                                     dim3(256), 0, static_cast<cudaStream_t>(stream), parts, splits, columns,
+                                     channels, bias, out));
+}
+
+int launch_audio_flatten(const float* conv3, uint32_t steps, uint32_t chunk_steps, uint32_t bins, uint32_t channels,
+                         void* out, void* stream) {
+  return static_cast<int>(launch_pdl(audio_flatten_kernel, dim3(grid_for(size_t(steps) * channels * bins / 8, 256)),
+                                     dim3(256), 0, static_cast<cudaStream_t>(stream), conv3, steps, chunk_steps, bins,
+                                     channels, static_cast<__half*>(out)));
+}
+
+int launch_audio_epilogue(int mode, const float* parts, uint32_t splits, uint32_t steps, uint32_t ld, uint32_t width,
+                          const float* add, uint32_t chunk_steps, float* x, uint32_t x_ld, void* packed,
+                          void* stream) {
+  const dim3 grid(grid_for(size_t(steps) * width / 8, 256)), block(256);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  __half* pk = static_cast<__half*>(packed);
+  switch (mode) {
+    case kPosition:
+      return static_cast<int>(launch_pdl(audio_epilogue_kernel<kPosition>, grid, block, 0, st, parts, splits, steps,
+                                         ld, width, add, chunk_steps, x, x_ld, pk));
+    case kBias:
+      return static_cast<int>(launch_pdl(audio_epilogue_kernel<kBias>, grid, block, 0, st, parts, splits, steps, ld,
+                                         width, add, chunk_steps, x, x_ld, pk));
+    case kResidual:
+      return static_cast<int>(launch_pdl(audio_epilogue_kernel<kResidual>, grid, block, 0, st, parts, splits, steps,
+                                         ld, width, add, chunk_steps, x, x_ld, pk));
+    default:
+      return static_cast<int>(launch_pdl(audio_epilogue_kernel<kGeluPack>, grid, block, 0, st, parts, splits, steps,
+                                         ld, width, add, chunk_steps, x, x_ld, pk));
+  }
+}
+
+int launch_audio_layernorm(const float* x, const float* weight, const float* bias, uint32_t width, float eps,
+                           uint32_t steps, float* out, void* packed, void* stream) {
+  return static_cast<int>(launch_pdl(audio_layernorm_kernel, dim3(steps), dim3(kNormThreads), 0,
+                                     static_cast<cudaStream_t>(stream), x, weight, bias, width, eps, out,
+                                     static_cast<__half*>(packed)));
+}
+
+size_t audio_attention_smem(uint32_t window, uint32_t head_dim) {
+  return (size_t(window) * (2 * head_dim + 1) + size_t(kAttnWarps) * (head_dim + window)) * 4;
+}
+
+int launch_audio_attention(const float* qkv, uint32_t steps, uint32_t width, uint32_t heads, uint32_t head_dim,
+                           uint32_t window, float* out, void* stream) {
+  const size_t smem = audio_attention_smem(window, head_dim);
+  const dim3 grid((steps + window - 1) / window, heads);
+  return static_cast<int>(launch_pdl(audio_window_attention_kernel, grid, dim3(kAttnWarps * 32), smem,
+                                     static_cast<cudaStream_t>(stream), qkv, steps, width, head_dim, window, out));
+}
+
+int prepare_audio_kernels(uint32_t window, uint32_t head_dim) {
+  return static_cast<int>(cudaFuncSetAttribute(audio_window_attention_kernel,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(audio_attention_smem(window, head_dim))));
+}
+
+}  // namespace qwc

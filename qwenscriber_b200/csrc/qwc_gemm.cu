@@ -41,6 +41,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstddef>
 #include <cstring>
 
@@ -232,6 +233,39 @@ __device__ __forceinline__ void dequant_q8_words(uint32_t w0, uint32_t w1, uint3
   split_pair(hsub2_bits(lop_and_or(__byte_perm(w0, w1, 0x0703), mask, magic), bias), scale2, hi.w, lo.w);
 }
 
+// Code bytes a TMA box brings per row per K block, and the box's x
+// coordinate. q4 and q8 groups (32, 64 bytes) start on 16-byte boundaries;
+// a q5 group (40 bytes) starts 8 bytes past one when its index is odd, so
+// its box is 48 bytes from the boundary at or below it (the group at byte
+// offset (40 kb) & 15 within the box; the last box's overhang past the row
+// reads the fill value and is never used).
+__host__ __device__ constexpr uint32_t gemm_code_box(uint32_t format) {
+  return format == kFormatQ4 ? 32u : format == kFormatQ5 ? 48u : 64u;
+}
+__device__ __forceinline__ uint32_t gemm_code_x(uint32_t format, uint32_t kb) {
+  return format == kFormatQ5 ? (40u * kb) & ~15u : kb * gemm_code_box(format);
+}
+
+// Eight q5 weights of a group (K order 0..7): their low nibbles as one q4
+// code word `w`, their fifth bits as byte `f` (bit k for weight k). The code
+// is nibble | fifth << 4 with bias 16 (quant.zig:253-269, 327-335).
+__device__ __forceinline__ void dequant_q5_word(uint32_t w, uint32_t f, uint32_t scale2, uint4& hi, uint4& lo) {
+  const uint32_t magic = 0x64006400u;  // f16 1024 in both halves
+  const uint32_t bias = 0x64106410u;   // f16 1040 = 1024 + 16
+  const uint32_t mask = 0x000F000Fu;
+  uint32_t pr[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    // Pair (j, j + 4): fifth bits to bit 4 of each f16 half's mantissa.
+    const uint32_t fifth = (((f >> j) & 1u) << 4) | (((f >> (j + 4)) & 1u) << 20);
+    pr[j] = lop_and_or(w >> (4 * j), mask, magic) | fifth;  // f16 pair (1024 + code)
+  }
+  split_pair(hsub2_bits(pr[0], bias), scale2, hi.x, lo.x);
+  split_pair(hsub2_bits(pr[1], bias), scale2, hi.y, lo.y);
+  split_pair(hsub2_bits(pr[2], bias), scale2, hi.z, lo.z);
+  split_pair(hsub2_bits(pr[3], bias), scale2, hi.w, lo.w);
+}
+
 // One weight matrix of a launch. A launch multiplies up to three matrices
 // that share K and the activations (Q, K and V; gate and up).
 struct GemmJob {
@@ -245,7 +279,7 @@ struct GemmParams {
   GemmJob job[3];
   uint32_t njobs;
   uint32_t cols;        // K (multiple of kKBlock)
-  uint32_t streams;     // stream columns written (<= kStreamCols); output rows per split
+  uint32_t streams;     // columns written, over all column blocks (blockIdx.z: 64 each); output rows per split
   uint32_t kb_per_split;
   float* out;           // [split][streams][out_ld]
   uint32_t out_ld;
@@ -292,8 +326,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t kb0 = blockIdx.y * p.kb_per_split;
   const uint32_t kb1 = min(kblocks, kb0 + p.kb_per_split);
   const uint32_t nkb = kb1 > kb0 ? kb1 - kb0 : 0;
-  const bool q4 = job.format == kFormatQ4;
-  const uint32_t code_box = q4 ? kKBlock / 2 : kKBlock;  // bytes of codes per row per block
+  const bool q4 = job.format == kFormatQ4, q5 = job.format == kFormatQ5;
+  const uint32_t code_box = gemm_code_box(job.format);  // bytes of codes per row per block
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kRawStages; ++i) {
@@ -328,7 +362,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       auto load_weights = [&](uint32_t i) {
         const uint32_t st = i % kRawStages, kb = kb0 + i;
         mbar_arrive_expect_tx(&s->w_full[st], kCtaRows * code_box + kScaleStageBytes);
-        tma_load_2d(s->codes[st], map_codes, static_cast<int32_t>(kb * code_box), static_cast<int32_t>(m0),
+        tma_load_2d(s->codes[st], map_codes, static_cast<int32_t>(gemm_code_x(job.format, kb)), static_cast<int32_t>(m0),
                     &s->w_full[st]);
         // The 16-byte scale box holding this block's group.
         tma_load_2d(s->scales[st], map_scales, static_cast<int32_t>((kb * 2u) & ~15u), static_cast<int32_t>(m0),
@@ -337,7 +371,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       auto load_acts = [&](uint32_t i) {
         const uint32_t st = i % kRawStages;
         mbar_arrive_expect_tx(&s->b_full[st], kBStageBytes);
-        tma_load_2d(s->b[st], map_b, static_cast<int32_t>((kb0 + i) * kKBlock), 0, &s->b_full[st]);
+        tma_load_2d(s->b[st], map_b, static_cast<int32_t>((kb0 + i) * kKBlock), static_cast<int32_t>(blockIdx.z * kTileN),
+                    &s->b_full[st]);
       };
       const uint32_t first = nkb < uint32_t(kRawStages) ? nkb : uint32_t(kRawStages);
       for (uint32_t i = 0; i < first; ++i) load_weights(i);
@@ -422,7 +457,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // The row's 64 K values as 32 columns of f16 pairs, hi and lo; each
       // goes to TMEM in one 32-column store.
       uint4 hv[8], lv[8];
-      if (q4) {
+      if (q5) {
+        // The group's 32 bytes of nibbles (8 words of 8 weights) and 8 bytes of
+        // fifth bits, at byte 0 or 8 of the row's 48-byte box: 8-byte loads.
+        const uint2* g = reinterpret_cast<const uint2*>(s->codes[st] + r * 48u + ((40u * kb) & 15u));
+        const uint2 n0 = g[0], n1 = g[1], n2 = g[2], n3 = g[3], fifth = g[4];
+        const uint32_t nw[8] = {n0.x, n0.y, n1.x, n1.y, n2.x, n2.y, n3.x, n3.y};
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const uint32_t fb = ((q < 4 ? fifth.x : fifth.y) >> (8 * (q & 3))) & 0xFFu;
+          dequant_q5_word(nw[q], fb, sc, hv[q], lv[q]);
+        }
+      } else if (q4) {
         // Two 16-byte chunks of codes, 8 per word.
         const uint4* src = reinterpret_cast<const uint4*>(s->codes[st] + r * (kKBlock / 2));
 #pragma unroll
@@ -456,7 +502,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (go) {
       tc_fence_after();
       const uint32_t row = m0 + r;
-      float* out = p.out + size_t(blockIdx.y) * p.streams * p.out_ld + job.out_offset + row;
+      const uint32_t n_base = blockIdx.z * kStreamCols;  // this column block's first column
+      float* out = p.out + (size_t(blockIdx.y) * p.streams + n_base) * p.out_ld + job.out_offset + row;
 #pragma unroll
       for (uint32_t n0 = 0; n0 < kStreamCols; n0 += 32) {
         float v[32], vlo[32];
@@ -465,7 +512,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (row < job.rows) {
 #pragma unroll
           for (int n = 0; n < 32; ++n) {
-            if (n0 + n < p.streams) out[size_t(n0 + n) * p.out_ld] = v[n] + vlo[n];
+            if (n_base + n0 + n < p.streams) out[size_t(n0 + n) * p.out_ld] = v[n] + vlo[n];
           }
         }
       }
@@ -479,14 +526,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
-// x[s][k] f32 -> the activation box rows: f16 hi values in rows [0, 64),
-// lo remainders in rows [64, 128), chunks in the permuted order.
+// x[s][k] f32 -> the activation box rows: column s of block b = s / 64 has
+// its f16 hi values in row 128 b + s % 64 and its lo remainders in row
+// 128 b + 64 + s % 64, chunks in the permuted order.
 __global__ void pack_activations_kernel(const float* x, uint32_t streams, uint32_t cols, __half* out) {
   pdl_wait_and_trigger();
   const uint32_t chunks = cols / 8;
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < streams * chunks; i += gridDim.x * blockDim.x) {
-    const uint32_t sidx = i / chunks, c = i % chunks;
-    const float* src = x + size_t(sidx) * cols + c * 8;
+    const uint32_t col = i / chunks, c = i % chunks;
+    const uint32_t sidx = (col / kStreamCols) * kTileN + col % kStreamCols;
+    const float* src = x + size_t(col) * cols + c * 8;
     const int perm[8] = {0, 4, 1, 5, 2, 6, 3, 7};
     __align__(16) __half hi[8];
     __align__(16) __half lo[8];
@@ -510,9 +559,198 @@ __global__ void sum_splits_kernel(const float* parts, uint32_t splits, uint32_t 
   }
 }
 
+// ---- dense f16 weights: the audio tower's convolutions as GEMMs ----
+//
+// out[split][n][m] = sum over the split's K blocks of W[m][k] * X[n][k]: W is
+// f16 [rows][kpad] (exact: the convolution weights are stored in f16), X the
+// activation rows of pack_activations_kernel's layout in natural K order (f16
+// hi rows, then lo rows, per 64-column block). Both operands reach shared
+// memory by TMA in 128-byte-swizzled boxes and feed tcgen05.mma directly (A
+// from a shared-memory descriptor): per K step one MMA per 128-row tile over
+// 128 columns (x hi | x lo); the epilogue adds the two halves.
+// Warp 0: TMA producer; warp 1: MMA issuer; warps 2-9: epilogue (tile
+// (warp - 2) / 4, TMEM lane quarter warp % 4).
+constexpr int kDenseStages = 4;
+constexpr uint32_t kDenseAStage = kTileM * kKBlock * 2;  // one 128-row tile: 16 KB
+
+struct __align__(1024) DenseSmem {
+  uint8_t a[kDenseStages][kTilesPerCta][kDenseAStage];
+  uint8_t b[kDenseStages][kBStageBytes];
+  uint64_t full[kDenseStages];
+  uint64_t empty[kDenseStages];
+  uint64_t acc_full;
+  uint32_t tmem_base;
+};
+static_assert(offsetof(DenseSmem, b) % 1024 == 0 && kDenseAStage % 1024 == 0, "swizzled boxes need 1024 B alignment");
+
+struct DenseParams {
+  uint32_t rows;          // M
+  uint32_t kb_per_split;  // K blocks per split (grid y)
+  uint32_t kblocks;       // kpad / 64
+  uint32_t columns;       // N over all column blocks (grid z)
+  float* out;             // [split][columns][rows]
+  int32_t* error;
+  uint64_t timeout_ns;
+};
+
+struct alignas(64) DenseMaps {
+  CUtensorMap a;
+  CUtensorMap b;
+};
+
+// D[tmem_d] (+)= A[smem desc] * B[smem desc].
+__device__ __forceinline__ void umma_f16_ss(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ bool dense_wait(uint64_t* bar, uint32_t parity, const DenseParams& p, int32_t site) {
+  if (mbar_wait_bounded(bar, parity, p.error, p.timeout_ns, kGemmErrWait + site)) return true;
+  if (*reinterpret_cast<volatile int32_t*>(p.error) == kGemmErrWait + site) {
+    p.error[1] = site;
+    p.error[2] = static_cast<int32_t>(blockIdx.x);
+    p.error[3] = static_cast<int32_t>(blockIdx.y);
+  }
+  return false;
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_dense_kernel(const __grid_constant__ DenseMaps maps, const DenseParams p) {
+  extern __shared__ __align__(1024) uint8_t dense_smem_raw[];
+  const uint32_t pad = (1024u - (smem_addr(dense_smem_raw) & 1023u)) & 1023u;
+  DenseSmem* s = reinterpret_cast<DenseSmem*>(dense_smem_raw + pad);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t m0 = blockIdx.x * kCtaRows;
+  const uint32_t kb0 = blockIdx.y * p.kb_per_split;
+  const uint32_t kb1 = min(p.kblocks, kb0 + p.kb_per_split);
+  const uint32_t nkb = kb1 > kb0 ? kb1 - kb0 : 0;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kDenseStages; ++i) {
+      mbar_init(&s->full[i], 1);
+      mbar_init(&s->empty[i], 1);
+    }
+    mbar_init(&s->acc_full, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(&s->tmem_base, 256);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s->tmem_base;
+  bool ok = true;
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // The weights never depend on the previous kernel: the first stages'
+      // weight boxes go out before the dependency wait, the activations after.
+      auto load_a = [&](uint32_t i) {
+        const uint32_t st = i % kDenseStages, kb = kb0 + i;
+        mbar_arrive_expect_tx(&s->full[st], kTilesPerCta * kDenseAStage + kBStageBytes);
+        for (uint32_t t = 0; t < kTilesPerCta; ++t) {
+          tma_load_2d(s->a[st][t], &maps.a, static_cast<int32_t>(kb * kKBlock), static_cast<int32_t>(m0 + t * kTileM),
+                      &s->full[st]);
+        }
+      };
+      auto load_b = [&](uint32_t i) {
+        const uint32_t st = i % kDenseStages;
+        tma_load_2d(s->b[st], &maps.b, static_cast<int32_t>((kb0 + i) * kKBlock),
+                    static_cast<int32_t>(blockIdx.z * kTileN), &s->full[st]);
+      };
+      const uint32_t first = nkb < uint32_t(kDenseStages) ? nkb : uint32_t(kDenseStages);
+      for (uint32_t i = 0; i < first; ++i) load_a(i);
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      for (uint32_t i = 0; i < first; ++i) load_b(i);
+      uint32_t issued = first;
+      for (uint32_t i = first; i < nkb && ok; ++i) {
+        const uint32_t st = i % kDenseStages;
+        if (!dense_wait(&s->empty[st], ((i / kDenseStages) - 1) & 1u, p, 10)) {
+          ok = false;
+          break;
+        }
+        load_a(i);
+        load_b(i);
+        issued = i + 1;
+      }
+      for (uint32_t i = issued > uint32_t(kDenseStages) ? issued - kDenseStages : 0u; i < issued; ++i) {
+        dense_wait(&s->full[i % kDenseStages], (i / kDenseStages) & 1u, p, 11);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint64_t a_desc0 = umma_desc(smem_addr(s->a[0][0]), 16, 1024, kLayoutSw128);
+      const uint64_t b_desc0 = umma_desc(smem_addr(s->b[0]), 16, 1024, kLayoutSw128);
+      constexpr uint64_t kAStageUnits = (uint64_t(kTilesPerCta) * kDenseAStage) >> 4;
+      for (uint32_t i = 0; i < nkb && ok; ++i) {
+        const uint32_t st = i % kDenseStages;
+        if (!dense_wait(&s->full[st], (i / kDenseStages) & 1u, p, 20)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t ad = a_desc0 + st * kAStageUnits;
+        const uint64_t bd = b_desc0 + ((uint64_t(st) * kBStageBytes) >> 4);
+#pragma unroll
+        for (uint32_t k = 0; k < kKBlock / 16; ++k) {
+#pragma unroll
+          for (uint32_t t = 0; t < kTilesPerCta; ++t) {
+            umma_f16_ss(tmem + t * kTileN, ad + ((uint64_t(t) * kDenseAStage) >> 4) + 2 * k, bd + 2 * k, kIdescN128,
+                        (i > 0 || k > 0) ? 1u : 0u);
+          }
+        }
+        umma_commit(&s->empty[st]);
+      }
+      umma_commit(&s->acc_full);
+      if (!ok) dense_wait(&s->acc_full, 0, p, 21);
+    }
+  } else {
+    const uint32_t quarter = static_cast<uint32_t>(warp % 4);
+    const uint32_t t = static_cast<uint32_t>((warp - 2) / 4);
+    const uint32_t row = m0 + t * kTileM + quarter * 32 + lane;
+    bool go = nkb > 0 && dense_wait(&s->acc_full, 0, p, 60);
+    go = __all_sync(0xffffffffu, go);
+    if (go) {
+      tc_fence_after();
+      const uint32_t n_base = blockIdx.z * kStreamCols;
+      float* out = p.out + (size_t(blockIdx.y) * p.columns + n_base) * p.rows + row;
+      const uint32_t taddr = tmem + ((quarter * 32u) << 16) + t * kTileN;
+#pragma unroll
+      for (uint32_t n0 = 0; n0 < kStreamCols; n0 += 32) {
+        float v[32], vlo[32];
+        tmem_ld32(taddr + n0, v);
+        tmem_ld32(taddr + kStreamCols + n0, vlo);
+        if (row < p.rows) {
+#pragma unroll
+          for (int n = 0; n < 32; ++n) {
+            if (n_base + n0 + n < p.columns) out[size_t(n0 + n) * p.rows] = v[n] + vlo[n];
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
 }  // namespace
 
 int gemm_smem_bytes() { return static_cast<int>(sizeof(GemmSmem)) + 1024; }
+
+int launch_pack_activations(const float* x, uint32_t columns, uint32_t cols, void* out, void* stream) {
+  const uint32_t work = columns * (cols / 8);
+  const uint32_t grid = std::min<uint32_t>(1184u, (work + 255) / 256);
+  return static_cast<int>(launch_pdl(pack_activations_kernel, dim3(grid), dim3(256), 0,
+                                     static_cast<cudaStream_t>(stream), x, columns, cols,
+                                     static_cast<__half*>(out)));
+}
 
 int prepare_gemm_kernel() {
   return static_cast<int>(
@@ -522,12 +760,13 @@ int prepare_gemm_kernel() {
 // TMA descriptors of one weight matrix and of an activation buffer, with the
 // box sizes the kernel's transaction counts assume.
 int32_t gemm_weight_maps(uint32_t format, const void* codes, const void* scales, uint32_t rows, uint32_t cols,
-                         uint8_t* codes_map, uint8_t* scales_map) {
+                         uint8_t* codes_map, uint8_t* scales_map, uint32_t scale_stride) {
   const uint32_t groups = cols / kGroup;
-  const uint64_t code_row = uint64_t(groups) * data_bytes_per_group(format), scale_row = uint64_t(groups) * 2;
+  const uint64_t code_row = uint64_t(groups) * data_bytes_per_group(format);
+  const uint64_t scale_row = scale_stride ? scale_stride : uint64_t(groups) * 2;
   const uint64_t dims_c[2] = {code_row, rows};
   const uint64_t str_c[1] = {code_row};
-  const uint32_t box_c[2] = {format == kFormatQ4 ? kKBlock / 2 : kKBlock, kCtaRows};
+  const uint32_t box_c[2] = {gemm_code_box(format), kCtaRows};
   const uint64_t dims_s[2] = {scale_row, rows};
   const uint64_t str_s[1] = {scale_row};
   const uint32_t box_s[2] = {16, kCtaRows};
@@ -536,8 +775,8 @@ int32_t gemm_weight_maps(uint32_t format, const void* codes, const void* scales,
   return encode_tensor_map(scales_map, kMapU8, 2, const_cast<void*>(scales), dims_s, str_s, box_s, false);
 }
 
-int32_t gemm_act_map(void* base, uint32_t cols, uint8_t* out) {
-  const uint64_t dims[2] = {cols, kTileN};
+int32_t gemm_act_map(void* base, uint32_t cols, uint8_t* out, uint32_t col_blocks) {
+  const uint64_t dims[2] = {cols, uint64_t(kTileN) * col_blocks};
   const uint64_t str[1] = {uint64_t(cols) * 2};
   const uint32_t box[2] = {kKBlock, kTileN};
   return encode_tensor_map(out, kMapF16, 2, base, dims, str, box, true);
@@ -547,8 +786,8 @@ int32_t gemm_act_map(void* base, uint32_t cols, uint8_t* out) {
 // per SM) weighed against per-CTA fixed cost (about four K blocks of
 // pipeline fill, TMEM set-up and epilogue) and the partial sums the next
 // kernel reads.
-uint32_t gemm_splits(uint32_t rows, uint32_t cols, int sms) {
-  const uint32_t mtiles = (rows + kCtaRows - 1) / kCtaRows;
+uint32_t gemm_splits(uint32_t rows, uint32_t cols, int sms, uint32_t col_blocks) {
+  const uint32_t mtiles = (rows + kCtaRows - 1) / kCtaRows * col_blocks;
   const uint32_t kblocks = cols / kKBlock;
   uint32_t best = 1;
   double best_cost = 1e30;
@@ -570,7 +809,7 @@ uint32_t gemm_splits(uint32_t rows, uint32_t cols, int sms) {
 int launch_gemm_jobs(const uint8_t (*codes_maps)[128], const uint8_t (*scale_maps)[128], const uint32_t* rows,
                      const uint32_t* formats, const uint32_t* out_offsets, uint32_t njobs, const uint8_t* map_b,
                      uint32_t cols, uint32_t streams, uint32_t splits, float* out, uint32_t out_ld, int32_t* error,
-                     void* stream) {
+                     void* stream, uint32_t col_blocks) {
   GemmMaps maps;
   GemmParams p{};
   uint32_t tiles = 0;
@@ -596,8 +835,40 @@ int launch_gemm_jobs(const uint8_t (*codes_maps)[128], const uint8_t (*scale_map
   p.timeout_ns = 2000000000ull;
   const uint32_t real_splits = (kblocks + p.kb_per_split - 1) / p.kb_per_split;
   const int smem = gemm_smem_bytes();
-  return static_cast<int>(launch_pdl(gemm_streams_kernel, dim3(tiles, real_splits), dim3(kGemmThreads), smem,
+  return static_cast<int>(launch_pdl(gemm_streams_kernel, dim3(tiles, real_splits, col_blocks), dim3(kGemmThreads), smem,
                                      static_cast<cudaStream_t>(stream), maps, p));
+}
+
+int prepare_gemm_dense_kernel() {
+  return static_cast<int>(cudaFuncSetAttribute(gemm_dense_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(sizeof(DenseSmem)) + 1024));
+}
+
+int32_t gemm_dense_weight_map(const void* weights, uint32_t rows, uint32_t kpad, uint8_t* out) {
+  const uint64_t dims[2] = {kpad, rows};
+  const uint64_t str[1] = {uint64_t(kpad) * 2};
+  const uint32_t box[2] = {kKBlock, kTileM};
+  return encode_tensor_map(out, kMapF16, 2, const_cast<void*>(weights), dims, str, box, true);
+}
+
+int launch_gemm_dense(const uint8_t* map_a, const uint8_t* map_b, uint32_t rows, uint32_t kpad, uint32_t columns,
+                      uint32_t splits, float* out, int32_t* error, uint64_t timeout_ns, void* stream) {
+  DenseMaps maps;
+  std::memcpy(&maps.a, map_a, 128);
+  std::memcpy(&maps.b, map_b, 128);
+  DenseParams p{};
+  p.rows = rows;
+  p.kblocks = kpad / kKBlock;
+  p.kb_per_split = (p.kblocks + splits - 1) / splits;
+  p.columns = columns;
+  p.out = out;
+  p.error = error;
+  p.timeout_ns = timeout_ns;
+  const uint32_t real_splits = (p.kblocks + p.kb_per_split - 1) / p.kb_per_split;
+  const dim3 grid((rows + kCtaRows - 1) / kCtaRows, real_splits, (columns + kStreamCols - 1) / kStreamCols);
+  return static_cast<int>(launch_pdl(gemm_dense_kernel, grid, dim3(kGemmThreads),
+                                     static_cast<int>(sizeof(DenseSmem)) + 1024, static_cast<cudaStream_t>(stream),
+                                     maps, p));
 }
 
 int launch_gemm_streams(const uint8_t* map_codes, const uint8_t* map_scales, const uint8_t* map_b, uint32_t rows,
@@ -625,7 +896,7 @@ int32_t gemm_status(cudaError_t e) {
 extern "C" int32_t qwc_op_gemm_streams(uint32_t format, const void* scales, const void* codes, uint32_t rows,
                                        uint32_t cols, const float* x, uint32_t streams, float* out, void* stream) {
   if (!scales || !codes || !x || !out || rows == 0) return QWC_INVALID_ARGUMENT;
-  if (format != kFormatQ4 && format != kFormatQ8) return QWC_UNSUPPORTED;
+  if (format != kFormatQ4 && format != kFormatQ5 && format != kFormatQ8) return QWC_UNSUPPORTED;
   if (cols == 0 || cols % 512 != 0 || streams == 0 || streams > kStreamCols) return QWC_INVALID_ARGUMENT;
   if (reinterpret_cast<uintptr_t>(scales) % 16 != 0 || reinterpret_cast<uintptr_t>(codes) % 16 != 0) {
     return QWC_INVALID_ARGUMENT;

@@ -209,20 +209,55 @@ struct alignas(64) KvMaps4 {
 
 // One tensor-core GEMM launch over up to three matrices sharing K and the
 // activations: out[split][streams][out_ld], matrix j's rows at column
-// out_offsets[j]. Maps are 128-byte CUtensorMaps.
+// out_offsets[j]. Maps are 128-byte CUtensorMaps. `streams` columns are
+// taken 64 per column block (grid z), block b reading activation rows
+// [128 b, 128 b + 128).
 int launch_gemm_jobs(const uint8_t (*codes_maps)[128], const uint8_t (*scale_maps)[128], const uint32_t* rows,
                      const uint32_t* formats, const uint32_t* out_offsets, uint32_t njobs, const uint8_t* map_b,
                      uint32_t cols, uint32_t streams, uint32_t splits, float* out, uint32_t out_ld, int32_t* error,
-                     void* stream);
+                     void* stream, uint32_t col_blocks = 1);
 int launch_gemm_streams(const uint8_t* map_codes, const uint8_t* map_scales, const uint8_t* map_b, uint32_t rows,
                         uint32_t cols, uint32_t format, uint32_t splits, float* out, int32_t* error, void* stream);
 // TMA descriptors for the stream GEMM: a weight matrix (codes and scales
 // planes) and an activation buffer of 128 f16 rows (hi, then lo) x cols.
+// `scale_stride`: bytes between scale rows when the plane is padded (a
+// multiple of 16); 0 for the container's packed plane (cols / 32 bytes,
+// which must then be a multiple of 16).
 int32_t gemm_weight_maps(uint32_t format, const void* codes, const void* scales, uint32_t rows, uint32_t cols,
-                         uint8_t* codes_map, uint8_t* scales_map);
-int32_t gemm_act_map(void* base, uint32_t cols, uint8_t* out);
-// Split count for a GEMM of `rows` x `cols` on `sms` SMs.
-uint32_t gemm_splits(uint32_t rows, uint32_t cols, int sms);
+                         uint8_t* codes_map, uint8_t* scales_map, uint32_t scale_stride = 0);
+int32_t gemm_act_map(void* base, uint32_t cols, uint8_t* out, uint32_t col_blocks = 1);
+// Split count for a GEMM of `rows` x `cols` (times `col_blocks` blocks of 64
+// columns) on `sms` SMs.
+uint32_t gemm_splits(uint32_t rows, uint32_t cols, int sms, uint32_t col_blocks = 1);
+// Dense f16-weight GEMM (the audio convolutions): out[split][columns][rows]
+// = W[rows][kpad] X^T over the split's K blocks, X packed like the stream
+// GEMM's activations but in natural K order; map_a from
+// gemm_dense_weight_map, map_b from gemm_act_map(…, kpad, …, column blocks).
+int32_t gemm_dense_weight_map(const void* weights, uint32_t rows, uint32_t kpad, uint8_t* out);
+int launch_gemm_dense(const uint8_t* map_a, const uint8_t* map_b, uint32_t rows, uint32_t kpad, uint32_t columns,
+                      uint32_t splits, float* out, int32_t* error, uint64_t timeout_ns, void* stream);
+int prepare_gemm_dense_kernel();
+// Audio tower kernels (qwc_audio.cu); each returns cudaError_t as int.
+int launch_audio_conv1(const float* mel, uint32_t frames, uint32_t mel_bins, uint32_t chunk_frames, uint32_t chunks,
+                       const void* w, const float* bias, uint32_t channels, float* out, void* stream);
+int launch_audio_im2col(const float* in, uint32_t chunks, uint32_t ih, uint32_t iw, uint32_t channels, uint32_t kpad,
+                        void* out, void* stream);
+int launch_audio_conv_epilogue(const float* parts, uint32_t splits, uint32_t columns, uint32_t channels,
+                               const float* bias, float* out, void* stream);
+int launch_audio_flatten(const float* conv3, uint32_t steps, uint32_t chunk_steps, uint32_t bins, uint32_t channels,
+                         void* out, void* stream);
+// mode: 0 position, 1 bias, 2 residual, 3 GELU into GEMM activation rows.
+int launch_audio_epilogue(int mode, const float* parts, uint32_t splits, uint32_t steps, uint32_t ld, uint32_t width,
+                          const float* add, uint32_t chunk_steps, float* x, uint32_t x_ld, void* packed, void* stream);
+int launch_audio_layernorm(const float* x, const float* weight, const float* bias, uint32_t width, float eps,
+                           uint32_t steps, float* out, void* packed, void* stream);
+int launch_audio_attention(const float* qkv, uint32_t steps, uint32_t width, uint32_t heads, uint32_t head_dim,
+                           uint32_t window, float* out, void* stream);
+size_t audio_attention_smem(uint32_t window, uint32_t head_dim);
+int prepare_audio_kernels(uint32_t window, uint32_t head_dim);
+// x[columns][cols] f32 -> the GEMM's activation rows (f16 hi and lo, 128 rows
+// per 64-column block, K chunks in the weight order) at `out`.
+int launch_pack_activations(const float* x, uint32_t columns, uint32_t cols, void* out, void* stream);
 // Step kernels; each returns cudaError_t as int.
 int launch_streams_norm(const StreamsStep& P, int input_mode, const float* weight, const float* parts,
                         uint32_t splits, void* stream);

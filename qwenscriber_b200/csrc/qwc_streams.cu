@@ -140,6 +140,10 @@ __global__ void __launch_bounds__(kNormThreads) streams_norm_kernel(const Stream
             c[1] = static_cast<float>(static_cast<int>((b >> 4) & 0xF) - 8);
             c[2] = static_cast<float>(static_cast<int>((b >> 8) & 0xF) - 8);
             c[3] = static_cast<float>(static_cast<int>((b >> 12) & 0xF) - 8);
+          } else if (e.format == kFormatQ5) {
+            const uint8_t* grp = crow + (k / kGroup) * 40u;
+#pragma unroll
+            for (int t = 0; t < 4; ++t) c[t] = static_cast<float>(q5_code(grp, (k + t) % kGroup));
           } else {
             const uint32_t b = *reinterpret_cast<const uint32_t*>(crow + k);
 #pragma unroll

@@ -16,6 +16,7 @@ import numpy as np
 GROUP = 64
 Q4, Q5, Q8 = 16, 17, 18
 F32 = 0
+F16 = 1
 DATA_BYTES = {Q4: 32, Q5: 40, Q8: 64}
 BIAS = {Q4: 8, Q5: 16, Q8: 128}
 ALIGN = 16

@@ -73,6 +73,12 @@ SIGNATURES = {
     "qwc_debug_trace": (c_int32, [c_uint32, c_void_p, c_uint32]),
     "qwc_debug_cache": (c_int32, [c_uint32, c_uint32, c_uint32, c_void_p, c_uint64]),
     "qwc_kernel_launches": (c_uint64, [c_uint32]),
+    "qwc_model_audio_config": (c_int32, [c_uint32, c_void_p]),
+    "qwc_audio_project": (c_int32, [c_uint32, c_void_p, c_uint32, c_void_p, c_uint64, POINTER(c_uint32)]),
+    "qwc_decode_begin_features": (c_int32, [c_uint32, c_void_p, c_uint32, c_void_p, c_uint64, c_uint32]),
+    "qwc_stream_begin_features": (c_int32, [c_uint32, c_uint32, c_void_p, c_uint32, c_void_p, c_uint64, c_uint32]),
+    "qwc_debug_audio": (c_int32, [c_uint32, c_uint32, c_void_p, c_uint64]),
+    "qwc_audio_run_timed": (c_int32, [c_uint32, c_void_p, c_uint32, c_uint32, POINTER(c_float), POINTER(c_uint32)]),
     "qwc_rope_tables": (c_int32, [c_float, c_uint32, c_uint32, c_void_p, c_void_p]),
     "qwc_op_dequantize": (c_int32, [c_uint32, c_void_p, c_void_p, c_uint32, c_uint32, c_void_p, c_void_p]),
     "qwc_op_quantize_q8": (c_int32, [c_void_p, c_uint32, c_uint32, c_void_p, c_void_p, c_void_p]),
@@ -318,6 +324,54 @@ class CudaModel:
 
     def launches(self) -> int:
         return int(self._L.qwc_kernel_launches(self.handle))
+
+    # ---- audio family: the tower and projector ----
+    AUDIO_CONFIG_FIELDS = ("d_model", "layers", "attention_heads", "head_dim", "ffn_dim", "downsample_hidden_size",
+                           "n_window", "n_window_infer", "chunk_frames", "frequency_bins", "conv_out_input_features",
+                           "chunk_steps", "max_position_steps", "output_dim", "mel_bins", "layer_norm_eps",
+                           "reserved_0", "reserved_1")
+
+    def audio_config(self) -> dict:
+        """qwc_model_audio_config: the 72-byte qwc_audio_config as a dict."""
+        buf = ctypes.create_string_buffer(72)
+        check(self._L.qwc_model_audio_config(self.handle, buf), "qwc_model_audio_config")
+        return dict(zip(self.AUDIO_CONFIG_FIELDS, struct.unpack("<15If2I", buf.raw)))
+
+    def audio_project(self, log_mel: np.ndarray, out_dim: int, capacity: int | None = None) -> np.ndarray:
+        """qwc_audio_project on a [mel_bins][frames] log-mel: [steps][out_dim] projected rows."""
+        mel = np.ascontiguousarray(log_mel, dtype=np.float32)
+        frames = mel.shape[1] if mel.ndim == 2 else 0
+        cap = capacity if capacity is not None else max(1, 4 * frames) * out_dim
+        out = np.zeros(cap, np.float32)
+        steps = c_uint32(0)
+        check(self._L.qwc_audio_project(self.handle, mel.ctypes.data, frames, out.ctypes.data, cap,
+                                        ctypes.byref(steps)), "qwc_audio_project")
+        return out[:steps.value * out_dim].reshape(steps.value, out_dim)
+
+    def decode_begin_features(self, prompt, log_mel: np.ndarray, max_tokens: int) -> None:
+        ids = np.ascontiguousarray(np.asarray(prompt, dtype=np.uint32))
+        mel = np.ascontiguousarray(log_mel, dtype=np.float32)
+        check(self._L.qwc_decode_begin_features(self.handle, ids.ctypes.data, ids.size, mel.ctypes.data, mel.nbytes,
+                                                max_tokens), "qwc_decode_begin_features")
+
+    def stream_begin_features(self, slot: int, prompt, log_mel: np.ndarray, max_tokens: int) -> None:
+        ids = np.ascontiguousarray(np.asarray(prompt, dtype=np.uint32))
+        mel = np.ascontiguousarray(log_mel, dtype=np.float32)
+        check(self._L.qwc_stream_begin_features(self.handle, slot, ids.ctypes.data, ids.size, mel.ctypes.data,
+                                                mel.nbytes, max_tokens), "qwc_stream_begin_features")
+
+    def debug_audio(self, which: int, steps: int, width: int) -> np.ndarray:
+        out = np.zeros(steps * width, np.float32)
+        n = check(self._L.qwc_debug_audio(self.handle, which, out.ctypes.data, out.size), "qwc_debug_audio")
+        return out[:n].reshape(steps, width)
+
+    def audio_run_timed(self, log_mel: np.ndarray, reps: int) -> tuple[float, int]:
+        """(device ms of `reps` clips, kernels one clip launches)."""
+        mel = np.ascontiguousarray(log_mel, dtype=np.float32)
+        ms, launches = c_float(0.0), c_uint32(0)
+        check(self._L.qwc_audio_run_timed(self.handle, mel.ctypes.data, mel.shape[1], reps, ctypes.byref(ms),
+                                          ctypes.byref(launches)), "qwc_audio_run_timed")
+        return ms.value, launches.value
 
 
 def rope_tables(theta: float, head_dim: int, max_positions: int) -> tuple[np.ndarray, np.ndarray]:

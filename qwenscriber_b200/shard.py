@@ -81,19 +81,24 @@ def build(tensors: Iterable[tuple[int, int, int, tuple[int, ...], bytes]]) -> by
 
 def tensor_entry(t) -> tuple[int, int, int, tuple[int, ...], bytes]:
     """A synthetic-model tensor (kind, layer, fmt, rows, cols, payload) as a
-    shard item: f32 vectors are rank 1, matrices rank 2."""
-    dims = (t.cols,) if t.fmt == quant.F32 and t.rows == 1 else (t.rows, t.cols)
+    shard item: f32 vectors are rank 1, matrices rank 2, the audio tower's f16
+    convolution weights rank 4 [out][in][3][3] (layout.zig:150-175)."""
+    if t.fmt == quant.F16 and t.kind in (1, 3, 5):
+        dims = (t.rows, t.cols // 9, 3, 3)
+    else:
+        dims = (t.cols,) if t.fmt == quant.F32 and t.rows == 1 else (t.rows, t.cols)
     return (t.kind, t.layer, t.fmt, dims, np.ascontiguousarray(t.payload).tobytes())
 
 
 def write_model_shards(model, shards: int = 2) -> list[bytes]:
-    """The model's tensors as `shards` shards of contiguous layer ranges."""
+    """The model's tensors as `shards` shards of contiguous decoder layer
+    ranges; the layer-0 tensors and any audio-tower layers go to the first."""
     layers = model.config.text_layers
     bounds = [round(i * layers / shards) for i in range(shards + 1)]
     out = []
     for s in range(shards):
         lo, hi = bounds[s], bounds[s + 1]
         items = [tensor_entry(t) for t in model.tensors
-                 if (t.layer == 0 and s == 0) or (lo < t.layer <= hi)]
+                 if ((t.layer == 0 or t.layer >= 1024) and s == 0) or (lo < t.layer <= hi < 1024)]
         out.append(build(items))
     return out

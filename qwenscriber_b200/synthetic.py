@@ -30,6 +30,11 @@ from .config import Config, qwen3_asr_0p6b, qwen3_asr_1p7b
 # container.zig:333-376 (decoder kinds)
 EMBED, FINAL_NORM, OUTPUT = 30, 31, 32
 Q, K, V, O, Q_NORM, K_NORM, ATTN_NORM, FFN_NORM, GATE, UP, DOWN = range(33, 44)
+# container.zig:334-362 (audio tower and projector kinds); audio layer i is 1024 + i
+(A_CONV1_W, A_CONV1_B, A_CONV2_W, A_CONV2_B, A_CONV3_W, A_CONV3_B, A_CONV_OUT_W, A_FINAL_NORM_W, A_FINAL_NORM_B,
+ A_Q_W, A_Q_B, A_K_W, A_K_B, A_V_W, A_V_B, A_OUT_W, A_OUT_B, A_ATTN_NORM_W, A_ATTN_NORM_B, A_FFN_IN_W, A_FFN_IN_B,
+ A_FFN_OUT_W, A_FFN_OUT_B, A_LAYER_NORM_W, A_LAYER_NORM_B, P_IN_W, P_IN_B, P_OUT_W, P_OUT_B) = range(1, 30)
+AUDIO_LAYER_BASE = 1024
 
 
 @dataclasses.dataclass
@@ -64,7 +69,57 @@ def _matrix(rng: np.random.Generator, fmt: int, rows: int, cols: int, std: float
     return quant.payload(fmt, scales, codes)
 
 
-def make_model(config: Config, fmt: int, seed: int, std: float = 0.02, q4_scale_std: float = 0.003) -> Model:
+def make_audio(config: Config, fmt: int, seed: int, std: float = 0.02, q4_scale_std: float = 0.003) -> list[Tensor]:
+    """The audio tower and projector in the reference's layout (layout.zig:150-262), drawn from
+    default_rng([seed, 2]): convolution weights f16 N(0, 1/fan_in), biases N(0, 0.02), LayerNorm
+    weights 1 + N(0, 0.05) and biases N(0, 0.02), matrices like the decoder's (`_matrix`)."""
+    rng = np.random.default_rng([seed, 2])
+    c = config
+    d, ch, ffn = c.audio_d_model, c.audio_downsample_hidden_size, c.audio_ffn_dim
+
+    def vec(n, scale=0.02, base=0.0):
+        return (base + rng.standard_normal(n, dtype=np.float32) * np.float32(scale)).astype(np.float32)
+
+    def conv(cin):
+        w = rng.standard_normal((ch, cin * 9), dtype=np.float32) / np.float32(np.sqrt(cin * 9))
+        return w.astype(np.float16).view(np.uint16)
+
+    def mat(rows, cols):
+        return _matrix(rng, fmt, rows, cols, std, q4_scale_std)
+
+    t = [Tensor(A_CONV1_W, 0, quant.F16, ch, 9, conv(1)), Tensor(A_CONV1_B, 0, quant.F32, 1, ch, vec(ch)),
+         Tensor(A_CONV2_W, 0, quant.F16, ch, ch * 9, conv(ch)), Tensor(A_CONV2_B, 0, quant.F32, 1, ch, vec(ch)),
+         Tensor(A_CONV3_W, 0, quant.F16, ch, ch * 9, conv(ch)), Tensor(A_CONV3_B, 0, quant.F32, 1, ch, vec(ch)),
+         Tensor(A_CONV_OUT_W, 0, fmt, d, c.audio_conv_out_features, mat(d, c.audio_conv_out_features)),
+         Tensor(A_FINAL_NORM_W, 0, quant.F32, 1, d, vec(d, 0.05, 1.0)),
+         Tensor(A_FINAL_NORM_B, 0, quant.F32, 1, d, vec(d))]
+    for i in range(c.audio_layers):
+        L = AUDIO_LAYER_BASE + i
+        for kind in (A_Q_W, A_K_W, A_V_W, A_OUT_W):
+            t.append(Tensor(kind, L, fmt, d, d, mat(d, d)))
+            t.append(Tensor(kind + 1, L, quant.F32, 1, d, vec(d)))
+        t.append(Tensor(A_ATTN_NORM_W, L, quant.F32, 1, d, vec(d, 0.05, 1.0)))
+        t.append(Tensor(A_ATTN_NORM_B, L, quant.F32, 1, d, vec(d)))
+        t.append(Tensor(A_FFN_IN_W, L, fmt, ffn, d, mat(ffn, d)))
+        t.append(Tensor(A_FFN_IN_B, L, quant.F32, 1, ffn, vec(ffn)))
+        t.append(Tensor(A_FFN_OUT_W, L, fmt, d, ffn, mat(d, ffn)))
+        t.append(Tensor(A_FFN_OUT_B, L, quant.F32, 1, d, vec(d)))
+        t.append(Tensor(A_LAYER_NORM_W, L, quant.F32, 1, d, vec(d, 0.05, 1.0)))
+        t.append(Tensor(A_LAYER_NORM_B, L, quant.F32, 1, d, vec(d)))
+    t += [Tensor(P_IN_W, 0, fmt, d, d, mat(d, d)), Tensor(P_IN_B, 0, quant.F32, 1, d, vec(d)),
+          Tensor(P_OUT_W, 0, fmt, c.audio_output_dim, d, mat(c.audio_output_dim, d)),
+          Tensor(P_OUT_B, 0, quant.F32, 1, c.audio_output_dim, vec(c.audio_output_dim))]
+    return t
+
+
+def make_log_mel(config: Config, frames: int, seed: int, stream: int = 0) -> np.ndarray:
+    """A clip's log-mel stand-in: [mel_bins][frames] f32, N(0, 0.5) (default_rng([seed, 3, stream]))."""
+    rng = np.random.default_rng([seed, 3, stream])
+    return (rng.standard_normal((config.mel_bins, frames), dtype=np.float32) * np.float32(0.5)).astype(np.float32)
+
+
+def make_model(config: Config, fmt: int, seed: int, std: float = 0.02, q4_scale_std: float = 0.003,
+               audio: bool = False) -> Model:
     rng = np.random.default_rng(seed)
     c = config
     h, qw, kvw, ffn = c.text_hidden_size, c.q_width, c.kv_width, c.text_ffn_dim
@@ -82,6 +137,8 @@ def make_model(config: Config, fmt: int, seed: int, std: float = 0.02, q4_scale_
         tensors.append(Tensor(FFN_NORM, layer, quant.F32, 1, h, ones(h)))
         for kind, rows, cols in ((GATE, ffn, h), (UP, ffn, h), (DOWN, h, ffn)):
             tensors.append(Tensor(kind, layer, fmt, rows, cols, _matrix(rng, fmt, rows, cols, std, q4_scale_std)))
+    if audio:
+        tensors += make_audio(c, fmt, seed, std, q4_scale_std)
     return Model(c, fmt, tensors)
 
 

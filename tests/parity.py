@@ -28,9 +28,31 @@ def small_config(fmt: int, layers: int = 2, vocab: int = 8192, max_positions: in
 def oracle_model(model: synthetic.Model, threads: int | None = None) -> O.OracleModel:
     om = O.OracleModel(model.config.pack(), cache_format=1, threads=threads or os.cpu_count() or 8)
     for t in model.tensors:
-        om.set_tensor(t.kind, t.layer, t.fmt, t.rows, t.cols, t.payload)
+        if t.kind >= synthetic.EMBED:  # the decoder's tensors; the tower has its own oracle
+            om.set_tensor(t.kind, t.layer, t.fmt, t.rows, t.cols, t.payload)
     om.finish()
     return om
+
+
+def audio_config(fmt: int, layers: int = 2, d_model: int = 128, heads: int = 2, ffn: int = 256, channels: int = 32,
+                 n_window_infer: int = 200, text_layers: int = 2):
+    """A small tower (2 layers of width 128 by default, 32 convolution channels, attention windows
+    of two chunks = 26 packed steps) in front of small_config's decoder."""
+    base = small_config(fmt, layers=text_layers)
+    return dataclasses.replace(base, audio_d_model=d_model, audio_layers=layers, audio_attention_heads=heads,
+                               audio_ffn_dim=ffn, audio_downsample_hidden_size=channels,
+                               audio_n_window_infer=n_window_infer)
+
+
+def oracle_audio(model: synthetic.Model, threads: int | None = None) -> O.OracleAudio:
+    oa = O.OracleAudio(model.config.pack(), threads=threads or os.cpu_count() or 8)
+    for t in model.tensors:
+        if t.kind < synthetic.EMBED:
+            st = oa.set_tensor(t.kind, t.layer, t.fmt, t.rows, t.cols, t.payload)
+            assert st == 0, (t.kind, t.layer, st)
+    st = oa.finish()
+    assert st == 0, st
+    return oa
 
 
 def cosine(a: np.ndarray, b: np.ndarray) -> float:

@@ -34,6 +34,8 @@ def _weights(fmt, scales, codes):
         q = np.empty((rows, codes.shape[1] * 2), np.int32)
         q[:, 0::2], q[:, 1::2] = lo, hi
         q -= 8
+    elif fmt == quant.Q5:
+        q = quant.unpack_q5(codes, codes.shape[1] // 40 * 64) - 16
     else:
         q = codes.astype(np.int32) - 128
     s = np.repeat(scales.astype(np.float32), 64, axis=1)
@@ -42,7 +44,7 @@ def _weights(fmt, scales, codes):
 
 @pytest.mark.parametrize("fmt,rows,cols,streams", [
     (quant.Q4, 256, 1024, 64), (quant.Q4, 300, 2048, 7), (quant.Q8, 384, 2048, 64),
-    (quant.Q4, 128, 6144, 64), (quant.Q8, 200, 1024, 33)])
+    (quant.Q4, 128, 6144, 64), (quant.Q8, 200, 1024, 33), (quant.Q5, 256, 1024, 64), (quant.Q5, 300, 2048, 19)])
 def test_gemm_streams(gpu, cuda_lib, oracle_lib, fmt, rows, cols, streams):
     import torch
 
