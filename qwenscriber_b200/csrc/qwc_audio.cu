@@ -82,34 +82,40 @@ __device__ __forceinline__ __half* packed_row(__half* base, uint32_t col, uint32
 // ---- convolution 1 (one input channel): kernels.zig:332-432 ----
 // mel [mel_bins][frames] -> out [chunk][h1][w1][channels], zero frames past
 // the clip (the reference pads each chunk in the mel domain, model.zig:535-545).
+// A thread takes one output position and 8 channels: the 9 taps are read
+// once, and each channel sums its valid taps in the reference's order.
 __global__ void audio_conv1_kernel(const float* mel, uint32_t frames, uint32_t mel_bins, uint32_t chunk_frames,
                                    uint32_t chunks, const __half* w, const float* bias, uint32_t channels,
                                    float* out) {
   pdl_wait_and_trigger();
-  const uint32_t h1 = (mel_bins - 1) / 2 + 1, w1 = (chunk_frames - 1) / 2 + 1;
-  const size_t total = size_t(chunks) * h1 * w1 * channels;
-  for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
-    const uint32_t oc = static_cast<uint32_t>(i % channels);
-    size_t rest = i / channels;
-    const uint32_t ox = static_cast<uint32_t>(rest % w1);
-    rest /= w1;
-    const uint32_t oy = static_cast<uint32_t>(rest % h1);
-    const uint32_t chunk = static_cast<uint32_t>(rest / h1);
-    float acc = 0.0f;
+  const uint32_t h1 = (mel_bins - 1) / 2 + 1, w1 = (chunk_frames - 1) / 2 + 1, groups = channels / 8;
+  const uint32_t total = chunks * h1 * w1 * groups;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const uint32_t cg = i % groups, pos = i / groups;
+    const uint32_t ox = pos % w1, oy = (pos / w1) % h1, chunk = pos / (w1 * h1);
+    float x[9];
+    bool in[9];
 #pragma unroll
-    for (int ky = 0; ky < 3; ++ky) {
-      const int iy = int(2 * oy) + ky - 1;
-      if (iy < 0 || iy >= int(mel_bins)) continue;
-#pragma unroll
-      for (int kx = 0; kx < 3; ++kx) {
-        const int ix = int(2 * ox) + kx - 1;
-        if (ix < 0 || ix >= int(chunk_frames)) continue;
-        const uint32_t frame = chunk * chunk_frames + uint32_t(ix);
-        const float sample = frame < frames ? mel[size_t(iy) * frames + frame] : 0.0f;
-        acc = __fadd_rn(acc, __fmul_rn(__half2float(w[oc * 9 + ky * 3 + kx]), sample));
-      }
+    for (int t = 0; t < 9; ++t) {
+      const int iy = int(2 * oy) + t / 3 - 1, ix = int(2 * ox) + t % 3 - 1;
+      in[t] = iy >= 0 && iy < int(mel_bins) && ix >= 0 && ix < int(chunk_frames);
+      const uint32_t frame = chunk * chunk_frames + uint32_t(ix);
+      x[t] = in[t] && frame < frames ? mel[size_t(iy) * frames + frame] : 0.0f;
     }
-    out[i] = gelu_ref(__fadd_rn(bias[oc], acc));
+    float y[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const uint32_t oc = cg * 8 + c;
+      float acc = 0.0f;
+#pragma unroll
+      for (int t = 0; t < 9; ++t) {
+        if (in[t]) acc = __fadd_rn(acc, __fmul_rn(__half2float(w[oc * 9 + t]), x[t]));
+      }
+      y[c] = gelu_ref(__fadd_rn(bias[oc], acc));
+    }
+    float4* dst = reinterpret_cast<float4*>(out + size_t(pos) * channels + cg * 8);
+    dst[0] = make_float4(y[0], y[1], y[2], y[3]);
+    dst[1] = make_float4(y[4], y[5], y[6], y[7]);
   }
 }
 
@@ -122,9 +128,9 @@ __global__ void audio_im2col_kernel(const float* in, uint32_t chunks, uint32_t i
   pdl_wait_and_trigger();
   const uint32_t oh = (ih - 1) / 2 + 1, ow = (iw - 1) / 2 + 1;
   const uint32_t columns = chunks * oh * ow, groups = kpad / 8, taps_k = 9 * channels;
-  const size_t total = size_t(columns) * groups;
-  for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
-    const uint32_t g = static_cast<uint32_t>(i % groups), col = static_cast<uint32_t>(i / groups);
+  const uint32_t total = columns * groups;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const uint32_t g = i % groups, col = i / groups;
     const uint32_t k0 = g * 8;
     float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     if (k0 < taps_k) {
@@ -148,8 +154,8 @@ __global__ void audio_im2col_kernel(const float* in, uint32_t chunks, uint32_t i
 __global__ void audio_conv_epilogue_kernel(const float* parts, uint32_t splits, uint32_t columns, uint32_t channels,
                                            const float* bias, float* out) {
   pdl_wait_and_trigger();
-  const size_t n = size_t(columns) * channels;
-  for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
+  const uint32_t n = columns * channels;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     float acc = parts[i];
     for (uint32_t sp = 1; sp < splits; ++sp) acc += parts[size_t(sp) * n + i];
     out[i] = gelu_ref(__fadd_rn(bias[i % channels], acc));
@@ -163,9 +169,9 @@ __global__ void audio_flatten_kernel(const float* conv3, uint32_t steps, uint32_
                                      uint32_t channels, __half* out) {
   pdl_wait_and_trigger();
   const uint32_t k = channels * bins, groups = k / 8;
-  const size_t total = size_t(steps) * groups;
-  for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
-    const uint32_t g = static_cast<uint32_t>(i % groups), p = static_cast<uint32_t>(i / groups);
+  const uint32_t total = steps * groups;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const uint32_t g = i % groups, p = i / groups;
     const uint32_t chunk = p / chunk_steps, t = p % chunk_steps;
     float v[8];
 #pragma unroll
@@ -192,9 +198,10 @@ __global__ void audio_epilogue_kernel(const float* parts, uint32_t splits, uint3
                                       uint32_t x_ld, __half* packed) {
   pdl_wait_and_trigger();
   const uint32_t groups = width / 8;
-  const size_t total = size_t(steps) * groups, plane = size_t(steps) * ld;
-  for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
-    const uint32_t g = static_cast<uint32_t>(i % groups), p = static_cast<uint32_t>(i / groups);
+  const uint32_t total = steps * groups;
+  const size_t plane = size_t(steps) * ld;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const uint32_t g = i % groups, p = i / groups;
     const float* src = parts + size_t(p) * ld + g * 8;
     float v[8];
     {
@@ -315,66 +322,128 @@ __global__ void __launch_bounds__(kNormThreads) audio_layernorm_kernel(const flo
 
 // kernels.zig:435-487 for one (window, head): scores = q.k / sqrt(head_dim)
 // over the window's keys, softmax (math.zig:77-93), weighted sum of values.
-// qkv rows [step][3 width] (q | k | v); out [step][width]. One CTA per
-// (window, head), 8 warps over the window's queries; keys and values of the
-// window in shared memory (key rows padded by one float against bank
-// conflicts). head_dim <= 128.
-constexpr int kAttnWarps = 8;
+// qkv rows [step][3 width] (q | k | v); out [step][width]. head_dim 64,
+// windows of at most 128 steps. One CTA per (window, head, 16 queries): the
+// window's keys and values in shared memory (key rows padded by one float
+// against bank conflicts), each of 4 warps takes 4 queries at once, so a lane
+// carries 16 independent score sums (4 queries x its 4 keys) and 8 value sums
+// (4 queries x its 2 dimensions) instead of one long chain.
+constexpr int kAttnWarps = 4;
+constexpr int kAttnQueries = 4;                        // per warp
+constexpr int kAttnCtaQueries = kAttnWarps * kAttnQueries;
+constexpr uint32_t kAttnHead = 64;
+constexpr uint32_t kAttnMaxWindow = 128;
 
 __global__ void __launch_bounds__(kAttnWarps * 32) audio_window_attention_kernel(const float* qkv, uint32_t steps,
-                                                                                 uint32_t width, uint32_t head_dim,
-                                                                                 uint32_t window, float* out) {
+                                                                                 uint32_t width, uint32_t window,
+                                                                                 float* out) {
   pdl_wait_and_trigger();
   extern __shared__ float attn_smem[];
+  constexpr uint32_t hd = kAttnHead, kstride = hd + 1;
   const uint32_t w0 = blockIdx.x * window, h = blockIdx.y;
   const uint32_t len = min(window, steps - w0);
-  const uint32_t kstride = head_dim + 1;
-  float* ks = attn_smem;                                   // [window][head_dim + 1]
-  float* vs = ks + size_t(window) * kstride;               // [window][head_dim]
-  float* qs = vs + size_t(window) * head_dim;              // [warps][head_dim]
-  float* ps = qs + size_t(kAttnWarps) * head_dim;          // [warps][window]
+  const uint32_t q0 = blockIdx.z * kAttnCtaQueries;
+  if (q0 >= len) return;
+  float* ks = attn_smem;                                       // [window][hd + 1]
+  float* vs = ks + (size_t(window) * kstride + 3) / 4 * 4;     // [window][hd], 16-byte aligned
+  float* qs = vs + size_t(window) * hd;                        // [warps][queries][hd]
+  float* ps = qs + size_t(kAttnWarps) * kAttnQueries * hd;     // [warps][queries][window]
   const uint32_t ld = 3 * width;
-  for (uint32_t i = threadIdx.x; i < len * head_dim; i += blockDim.x) {
-    const uint32_t j = i / head_dim, d = i % head_dim;
-    const float* r = qkv + size_t(w0 + j) * ld + h * head_dim + d;
-    ks[j * kstride + d] = r[width];
-    vs[j * head_dim + d] = r[2 * width];
+  // The window's key and value rows, 16 bytes a load, all loads of a thread
+  // issued before their stores.
+  constexpr uint32_t kVec = hd / 4;
+#pragma unroll 4
+  for (uint32_t i = threadIdx.x; i < len * kVec; i += blockDim.x) {
+    const uint32_t j = i / kVec, d = (i % kVec) * 4;
+    const float* r = qkv + size_t(w0 + j) * ld + h * hd + d;
+    const float4 kv = *reinterpret_cast<const float4*>(r + width);
+    const float4 vv = *reinterpret_cast<const float4*>(r + 2 * width);
+    float* kd = ks + j * kstride + d;
+    kd[0] = kv.x;
+    kd[1] = kv.y;
+    kd[2] = kv.z;
+    kd[3] = kv.w;
+    *reinterpret_cast<float4*>(vs + j * hd + d) = vv;
+  }
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t qw = q0 + warp * kAttnQueries;  // this warp's first query
+  float* q = qs + size_t(warp) * kAttnQueries * hd;
+  float* pw = ps + size_t(warp) * kAttnQueries * window;
+  for (uint32_t i = lane; i < kAttnQueries * hd; i += 32) {
+    const uint32_t qq = i / hd, d = i % hd;
+    q[i] = qw + qq < len ? qkv[size_t(w0 + qw + qq) * ld + h * hd + d] : 0.0f;
   }
   __syncthreads();
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const float scaling = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(head_dim)));
-  float* q = qs + warp * head_dim;
-  float* pw = ps + warp * window;
-  for (uint32_t qi = warp; qi < len; qi += kAttnWarps) {
-    for (uint32_t d = lane; d < head_dim; d += 32) q[d] = qkv[size_t(w0 + qi) * ld + h * head_dim + d];
-    __syncwarp();
+  if (qw >= len) return;
+  const float scaling = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(hd)));
+  float acc[kAttnQueries][4];
+#pragma unroll
+  for (int a = 0; a < kAttnQueries; ++a) {
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) acc[a][kk] = 0.0f;
+  }
+  uint32_t kidx[4];
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) kidx[kk] = min(lane + 32u * kk, len - 1) * kstride;
+#pragma unroll 4
+  for (uint32_t d = 0; d < hd; ++d) {
+    float kv[4], qv[kAttnQueries];
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) kv[kk] = ks[kidx[kk] + d];
+#pragma unroll
+    for (int a = 0; a < kAttnQueries; ++a) qv[a] = q[a * hd + d];
+#pragma unroll
+    for (int a = 0; a < kAttnQueries; ++a) {
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) acc[a][kk] = fmaf(qv[a], kv[kk], acc[a][kk]);
+    }
+  }
+#pragma unroll
+  for (int a = 0; a < kAttnQueries; ++a) {
     float mx = -INFINITY;
-    for (uint32_t j = lane; j < len; j += 32) {
-      const float* kr = ks + j * kstride;
-      float acc = 0.0f;
-      for (uint32_t d = 0; d < head_dim; ++d) acc = fmaf(q[d], kr[d], acc);
-      const float s = __fmul_rn(acc, scaling);
-      pw[j] = s;
-      mx = fmaxf(mx, s);
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      acc[a][kk] = __fmul_rn(acc[a][kk], scaling);
+      if (lane + 32u * kk < len) mx = fmaxf(mx, acc[a][kk]);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     float total = 0.0f;
-    for (uint32_t j = lane; j < len; j += 32) {
-      const float e = exp_ref(__fsub_rn(pw[j], mx));
-      pw[j] = e;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const float e = lane + 32u * kk < len ? exp_ref(__fsub_rn(acc[a][kk], mx)) : 0.0f;
+      acc[a][kk] = e;
       total += e;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
     const float inv = __fdiv_rn(1.0f, total);
-    __syncwarp();
-    for (uint32_t d = lane; d < head_dim; d += 32) {
-      float acc = 0.0f;
-      for (uint32_t j = 0; j < len; ++j) acc = fmaf(vs[j * head_dim + d], __fmul_rn(pw[j], inv), acc);
-      out[size_t(w0 + qi) * width + h * head_dim + d] = acc;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      if (lane + 32u * kk < len) pw[a * window + lane + 32u * kk] = __fmul_rn(acc[a][kk], inv);
     }
-    __syncwarp();
+  }
+  __syncwarp();
+  float o[kAttnQueries][2];
+#pragma unroll
+  for (int a = 0; a < kAttnQueries; ++a) o[a][0] = o[a][1] = 0.0f;
+#pragma unroll 4
+  for (uint32_t j = 0; j < len; ++j) {
+    const float v0 = vs[j * hd + lane], v1 = vs[j * hd + lane + 32];
+#pragma unroll
+    for (int a = 0; a < kAttnQueries; ++a) {
+      const float p = pw[a * window + j];
+      o[a][0] = fmaf(v0, p, o[a][0]);
+      o[a][1] = fmaf(v1, p, o[a][1]);
+    }
+  }
+#pragma unroll
+  for (int a = 0; a < kAttnQueries; ++a) {
+    if (qw + a < len) {
+      float* dst = out + size_t(w0 + qw + a) * width + h * hd;
+      dst[lane] = o[a][0];
+      dst[lane + 32] = o[a][1];
+    }
   }
 }
 
@@ -387,7 +456,7 @@ uint32_t grid_for(size_t work, uint32_t threads) {
 
 int launch_audio_conv1(const float* mel, uint32_t frames, uint32_t mel_bins, uint32_t chunk_frames, uint32_t chunks,
                        const void* w, const float* bias, uint32_t channels, float* out, void* stream) {
-  const size_t work = size_t(chunks) * ((mel_bins - 1) / 2 + 1) * ((chunk_frames - 1) / 2 + 1) * channels;
+  const size_t work = size_t(chunks) * ((mel_bins - 1) / 2 + 1) * ((chunk_frames - 1) / 2 + 1) * (channels / 8);
   return static_cast<int>(launch_pdl(audio_conv1_kernel, dim3(grid_for(work, 256)), dim3(256), 0,
                                      static_cast<cudaStream_t>(stream), mel, frames, mel_bins, chunk_frames, chunks,
                                      static_cast<const __half*>(w), bias, channels, out));
@@ -445,15 +514,17 @@ int launch_audio_layernorm(const float* x, const float* weight, const float* bia
 }
 
 size_t audio_attention_smem(uint32_t window, uint32_t head_dim) {
-  return (size_t(window) * (2 * head_dim + 1) + size_t(kAttnWarps) * (head_dim + window)) * 4;
+  if (head_dim != kAttnHead || window > kAttnMaxWindow) return ~size_t(0);  // the kernel's limits
+  return ((size_t(window) * (head_dim + 1) + 3) / 4 * 4 + size_t(window) * head_dim +
+          size_t(kAttnWarps) * kAttnQueries * (head_dim + window)) * 4;
 }
 
 int launch_audio_attention(const float* qkv, uint32_t steps, uint32_t width, uint32_t heads, uint32_t head_dim,
                            uint32_t window, float* out, void* stream) {
   const size_t smem = audio_attention_smem(window, head_dim);
-  const dim3 grid((steps + window - 1) / window, heads);
+  const dim3 grid((steps + window - 1) / window, heads, (window + kAttnCtaQueries - 1) / kAttnCtaQueries);
   return static_cast<int>(launch_pdl(audio_window_attention_kernel, grid, dim3(kAttnWarps * 32), smem,
-                                     static_cast<cudaStream_t>(stream), qkv, steps, width, head_dim, window, out));
+                                     static_cast<cudaStream_t>(stream), qkv, steps, width, window, out));
 }
 
 int prepare_audio_kernels(uint32_t window, uint32_t head_dim) {

@@ -71,6 +71,7 @@ uint32_t audio_packed_steps(const AudioGeometry& g, uint32_t frames) {
 }
 
 AudioModel::~AudioModel() {
+  for (Graph& gr : graphs_) cudaGraphExecDestroy(gr.exec);
   for (void* p : owned_) cudaFree(p);
 }
 
@@ -288,6 +289,42 @@ int32_t AudioModel::run(const float* mel_dev, uint32_t frames, float* out_dev, c
                         uint64_t timeout_ns, uint32_t* steps_out, bool sync) {
   if (frames == 0) return QWC_SHAPE_MISMATCH;         // UnexpectedShape (model.zig:383)
   if (frames > g.max_frames) return QWC_AUDIO_TOO_LONG;  // model.zig:386
+  // One CUDA graph per clip length (and buffers and wait bound): about 300
+  // launches replayed with one call. Kept for the last kMaxGraphs lengths.
+  Graph* hit = nullptr;
+  for (Graph& gr : graphs_) {
+    if (gr.frames == frames && gr.mel == mel_dev && gr.out == out_dev && gr.timeout_ns == timeout_ns) hit = &gr;
+  }
+  if (!hit) {
+    if (graphs_.size() >= kMaxGraphs) {
+      cudaGraphExecDestroy(graphs_.front().exec);
+      graphs_.erase(graphs_.begin());
+    }
+    cudaGraph_t graph = nullptr;
+    AUDIO_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+    const int32_t st = enqueue(mel_dev, frames, out_dev, stream, timeout_ns);
+    const cudaError_t end = cudaStreamEndCapture(stream, &graph);
+    if (st != QWC_OK || end != cudaSuccess) {
+      if (graph) cudaGraphDestroy(graph);
+      cudaGetLastError();
+      return st != QWC_OK ? st : cuda_status(end);
+    }
+    Graph gr{frames, mel_dev, out_dev, timeout_ns, nullptr, launches_};
+    const cudaError_t inst = cudaGraphInstantiate(&gr.exec, graph, 0);
+    cudaGraphDestroy(graph);
+    AUDIO_CUDA(inst);
+    graphs_.push_back(gr);
+    hit = &graphs_.back();
+  }
+  AUDIO_CUDA(cudaGraphLaunch(hit->exec, stream));
+  launches_ = hit->launches;
+  if (steps_out) *steps_out = audio_packed_steps(g, frames);
+  if (!sync) return QWC_OK;
+  return check_error(stream);
+}
+
+int32_t AudioModel::enqueue(const float* mel_dev, uint32_t frames, float* out_dev, cudaStream_t stream,
+                            uint64_t timeout_ns) {
   launches_ = 0;
   const uint32_t d = g.d_model, C = g.channels, cf = g.chunk_frames;
   const uint32_t chunks = ceil_div(frames, cf), steps = audio_packed_steps(g, frames);
@@ -393,9 +430,7 @@ int32_t AudioModel::run(const float* mel_dev, uint32_t frames, float* out_dev, c
                                        g.output_dim, nullptr, st));
   }
   (void)blocks;
-  if (steps_out) *steps_out = steps;
-  if (!sync) return QWC_OK;
-  return check_error(stream);
+  return QWC_OK;
 }
 
 }  // namespace qwc

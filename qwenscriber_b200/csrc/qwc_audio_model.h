@@ -80,6 +80,20 @@ class AudioModel {
     const float *attn_norm_w, *attn_norm_b, *o_b, *ffn_in_b, *ffn_out_b, *norm_w, *norm_b;
   };
   void* alloc(size_t bytes);
+  // Enqueues one clip's launches on `stream` (the body of run(), captured
+  // into a graph there).
+  int32_t enqueue(const float* mel_dev, uint32_t frames, float* out_dev, cudaStream_t stream, uint64_t timeout_ns);
+
+  struct Graph {
+    uint32_t frames;
+    const float* mel;
+    float* out;
+    uint64_t timeout_ns;
+    cudaGraphExec_t exec;
+    uint64_t launches;
+  };
+  static constexpr size_t kMaxGraphs = 8;
+  std::vector<Graph> graphs_;
 
   std::vector<void*> owned_;
   uint64_t scratch_bytes_ = 0;

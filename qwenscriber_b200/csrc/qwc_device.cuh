@@ -427,13 +427,10 @@ __device__ __forceinline__ void consumer_sync(uint32_t threads) {
 // nearest 2^(i/32), minus i << 47 so that adding k << 47 forms 2^(k/32).
 // The CPU oracle calls that expf, and this restatement was checked against it
 // on every non-NaN f32 input.
-__device__ __forceinline__ float exp_ref(float x) {
-  constexpr double kInvLn2N = 0x1.71547652b82fep+0 * 32;
-  constexpr double kShift = 0x1.8p+52;
-  constexpr double kC0 = 0x1.c6af84b912394p-5 / 32 / 32 / 32;
-  constexpr double kC1 = 0x1.ebfce50fac4f3p-3 / 32 / 32;
-  constexpr double kC2 = 0x1.62e42ff0c52d6p-1 / 32;
-  static constexpr uint64_t kTab[32] = {
+// 2^(i/32) of the table below, as global memory: a warp's lanes index it
+// with different i, which the constant cache would serialize; global loads of
+// its two 128-byte lines do not.
+static __device__ const uint64_t kExpRefTab[32] = {
       0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
       0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
       0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
@@ -443,6 +440,13 @@ __device__ __forceinline__ float exp_ref(float x) {
       0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
       0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull,
   };
+
+__device__ __forceinline__ float exp_ref(float x) {
+  constexpr double kInvLn2N = 0x1.71547652b82fep+0 * 32;
+  constexpr double kShift = 0x1.8p+52;
+  constexpr double kC0 = 0x1.c6af84b912394p-5 / 32 / 32 / 32;
+  constexpr double kC1 = 0x1.ebfce50fac4f3p-3 / 32 / 32;
+  constexpr double kC2 = 0x1.62e42ff0c52d6p-1 / 32;
   const uint32_t bits = __float_as_uint(x);
   const uint32_t abstop = (bits >> 20) & 0x7FFu;
   if (abstop >= 0x42Bu) {  // |x| >= 88, or not finite
@@ -456,7 +460,7 @@ __device__ __forceinline__ float exp_ref(float x) {
   const uint64_t ki = static_cast<uint64_t>(__double_as_longlong(kd));
   kd = __dsub_rn(kd, kShift);
   const double r = __fma_rn(kInvLn2N, xd, -kd);
-  const uint64_t t = kTab[ki % 32] + (ki << 47);
+  const uint64_t t = __ldg(&kExpRefTab[ki % 32]) + (ki << 47);
   const double s = __longlong_as_double(static_cast<long long>(t));
   const double z = __fma_rn(kC0, r, kC1);
   const double r2 = __dmul_rn(r, r);
