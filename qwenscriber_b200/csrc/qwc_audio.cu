@@ -14,8 +14,8 @@
 //                 K chunks of 8 are permuted [0 4 1 5 2 6 3 7];
 //   tower rows    f32 [step][width] (the reference's encoder scratch).
 //
-// Parity: the first convolution, GELU (math.zig:46-66) and the sinusoidal
-// position rows are the reference's arithmetic in its order. The GEMM-shaped
+// Parity: the first convolution, GELU (math.zig:46-66, with CUDA's expf) and
+// the sinusoidal position rows follow the reference's order. The GEMM-shaped
 // steps (convolutions 2 and 3, every projection) sum in another order with
 // 22-bit activations, and the LayerNorm and attention reductions are trees,
 // so the tower agrees with the reference to f32 rounding, not bit for bit.
@@ -38,7 +38,11 @@ constexpr uint32_t kCols = 64;  // GEMM columns per column block
 // position e holds value perm8(e) = [0 4 1 5 2 6 3 7][e].
 __host__ __device__ constexpr int perm8(int e) { return (e & 1) ? 4 + (e >> 1) : (e >> 1); }
 
-// math.zig:46-60, rounded as written (no contraction).
+// math.zig:46-60, rounded as written (no contraction), with the exponential
+// from CUDA's expf (within 2 ulp of exp). The reference's own exp (the host
+// libm expf, restated bit for bit as exp_ref) computes in double, and double
+// arithmetic is slow enough on this part that it made the first convolution's
+// 46 M GELUs of a 30-second clip its most expensive kernel.
 __device__ __forceinline__ float erf_ref(float x) {
   const float sign = x < 0.0f ? -1.0f : 1.0f;
   const float m = fabsf(x);
@@ -52,7 +56,7 @@ __device__ __forceinline__ float erf_ref(float x) {
   poly = __fadd_rn(0.37409196f, __fmul_rn(t, poly));
   poly = __fadd_rn(1.00002368f, __fmul_rn(t, poly));
   const float arg = __fadd_rn(__fsub_rn(__fmul_rn(-m, m), 1.26551223f), __fmul_rn(t, poly));
-  const float tau = __fmul_rn(t, exp_ref(arg));
+  const float tau = __fmul_rn(t, expf(arg));
   return __fmul_rn(sign, __fsub_rn(1.0f, tau));
 }
 
@@ -82,40 +86,39 @@ __device__ __forceinline__ __half* packed_row(__half* base, uint32_t col, uint32
 // ---- convolution 1 (one input channel): kernels.zig:332-432 ----
 // mel [mel_bins][frames] -> out [chunk][h1][w1][channels], zero frames past
 // the clip (the reference pads each chunk in the mel domain, model.zig:535-545).
-// A thread takes one output position and 8 channels: the 9 taps are read
-// once, and each channel sums its valid taps in the reference's order.
-__global__ void audio_conv1_kernel(const float* mel, uint32_t frames, uint32_t mel_bins, uint32_t chunk_frames,
-                                   uint32_t chunks, const __half* w, const float* bias, uint32_t channels,
-                                   float* out) {
+// A thread takes one (position, channel), channels fastest, so a warp's taps
+// are one broadcast load each and its stores are contiguous. The weights sit
+// in shared memory as [tap][channel] floats (lanes read consecutive banks).
+// Each channel sums its valid taps in the reference's order.
+constexpr uint32_t kConv1MaxChannels = 1024;
+
+__global__ void __launch_bounds__(256) audio_conv1_kernel(const float* mel, uint32_t frames, uint32_t mel_bins,
+                                                          uint32_t chunk_frames, uint32_t chunks, const __half* w,
+                                                          const float* bias, uint32_t channels, float* out) {
+  __shared__ float ws[9 * kConv1MaxChannels];
+  __shared__ float bs[kConv1MaxChannels];
+  for (uint32_t i = threadIdx.x; i < 9 * channels; i += blockDim.x) {
+    const uint32_t oc = i / 9, t = i % 9;
+    ws[t * channels + oc] = __half2float(w[i]);
+  }
+  for (uint32_t i = threadIdx.x; i < channels; i += blockDim.x) bs[i] = bias[i];
+  __syncthreads();
   pdl_wait_and_trigger();
-  const uint32_t h1 = (mel_bins - 1) / 2 + 1, w1 = (chunk_frames - 1) / 2 + 1, groups = channels / 8;
-  const uint32_t total = chunks * h1 * w1 * groups;
+  const uint32_t h1 = (mel_bins - 1) / 2 + 1, w1 = (chunk_frames - 1) / 2 + 1;
+  const uint32_t total = chunks * h1 * w1 * channels;
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
-    const uint32_t cg = i % groups, pos = i / groups;
+    const uint32_t oc = i % channels, pos = i / channels;
     const uint32_t ox = pos % w1, oy = (pos / w1) % h1, chunk = pos / (w1 * h1);
-    float x[9];
-    bool in[9];
+    float acc = 0.0f;
 #pragma unroll
     for (int t = 0; t < 9; ++t) {
       const int iy = int(2 * oy) + t / 3 - 1, ix = int(2 * ox) + t % 3 - 1;
-      in[t] = iy >= 0 && iy < int(mel_bins) && ix >= 0 && ix < int(chunk_frames);
+      if (iy < 0 || iy >= int(mel_bins) || ix < 0 || ix >= int(chunk_frames)) continue;
       const uint32_t frame = chunk * chunk_frames + uint32_t(ix);
-      x[t] = in[t] && frame < frames ? mel[size_t(iy) * frames + frame] : 0.0f;
+      const float sample = frame < frames ? mel[size_t(iy) * frames + frame] : 0.0f;
+      acc = __fadd_rn(acc, __fmul_rn(ws[t * channels + oc], sample));
     }
-    float y[8];
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const uint32_t oc = cg * 8 + c;
-      float acc = 0.0f;
-#pragma unroll
-      for (int t = 0; t < 9; ++t) {
-        if (in[t]) acc = __fadd_rn(acc, __fmul_rn(__half2float(w[oc * 9 + t]), x[t]));
-      }
-      y[c] = gelu_ref(__fadd_rn(bias[oc], acc));
-    }
-    float4* dst = reinterpret_cast<float4*>(out + size_t(pos) * channels + cg * 8);
-    dst[0] = make_float4(y[0], y[1], y[2], y[3]);
-    dst[1] = make_float4(y[4], y[5], y[6], y[7]);
+    out[i] = gelu_ref(__fadd_rn(bs[oc], acc));
   }
 }
 
@@ -238,19 +241,25 @@ __global__ void audio_epilogue_kernel(const float* parts, uint32_t splits, uint3
 
 // LayerNorm of each step row (math.zig:99-116: mean, then the mean of the
 // centred squares, 1 / sqrt(var + eps), (x - mean) * inv * w + b), one
-// 128-thread block per row; writes the f32 row (`out`, may alias `x`) and/or
-// the GEMM activation rows (`packed`). width % 8 == 0, width <= 128 * 8 * 4.
+// 128-thread block per row, optionally after the residual add that precedes
+// it in the block (kernels.zig:221-230): with `parts`, the row first becomes
+// x + (sum of the split partials + rbias) and is written back to x. The
+// normalized row goes to the GEMM activation rows (`packed`) and/or to `out`
+// (f32; may be x itself, which then holds the normalized row).
+// width % 8 == 0, width <= 128 * 8 * 4.
 constexpr int kNormThreads = 128;
 constexpr int kNormMaxChunks = 4;  // 8-value chunks per thread
 
-__global__ void __launch_bounds__(kNormThreads) audio_layernorm_kernel(const float* x, const float* weight,
-                                                                       const float* bias, uint32_t width, float eps,
-                                                                       float* out, __half* packed) {
+__global__ void __launch_bounds__(kNormThreads) audio_layernorm_kernel(float* x, const float* parts, uint32_t splits,
+                                                                       size_t plane, const float* rbias,
+                                                                       const float* weight, const float* bias,
+                                                                       uint32_t width, float eps, float* out,
+                                                                       __half* packed) {
   pdl_wait_and_trigger();
   __shared__ float red[kNormThreads / 32];
   __shared__ float stat;
   const uint32_t p = blockIdx.x, tid = threadIdx.x, chunks = width / 8;
-  const float* row = x + size_t(p) * width;
+  float* row = x + size_t(p) * width;
   float v[kNormMaxChunks][8];
   float sum = 0.0f;
 #pragma unroll
@@ -261,6 +270,27 @@ __global__ void __launch_bounds__(kNormThreads) audio_layernorm_kernel(const flo
       const float4 b = reinterpret_cast<const float4*>(row + ch * 8)[1];
       v[c][0] = a.x; v[c][1] = a.y; v[c][2] = a.z; v[c][3] = a.w;
       v[c][4] = b.x; v[c][5] = b.y; v[c][6] = b.z; v[c][7] = b.w;
+      if (parts) {
+        const float* src = parts + size_t(p) * width + ch * 8;
+        float r[8];
+        {
+          const float4 u = reinterpret_cast<const float4*>(src)[0], w = reinterpret_cast<const float4*>(src)[1];
+          r[0] = u.x; r[1] = u.y; r[2] = u.z; r[3] = u.w;
+          r[4] = w.x; r[5] = w.y; r[6] = w.z; r[7] = w.w;
+        }
+        for (uint32_t sp = 1; sp < splits; ++sp) {
+          const float4 u = reinterpret_cast<const float4*>(src + sp * plane)[0];
+          const float4 w = reinterpret_cast<const float4*>(src + sp * plane)[1];
+          r[0] += u.x; r[1] += u.y; r[2] += u.z; r[3] += u.w;
+          r[4] += w.x; r[5] += w.y; r[6] += w.z; r[7] += w.w;
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[c][e] = __fadd_rn(v[c][e], __fadd_rn(r[e], rbias[ch * 8 + e]));
+        if (out != x) {
+          reinterpret_cast<float4*>(row + ch * 8)[0] = make_float4(v[c][0], v[c][1], v[c][2], v[c][3]);
+          reinterpret_cast<float4*>(row + ch * 8)[1] = make_float4(v[c][4], v[c][5], v[c][6], v[c][7]);
+        }
+      }
 #pragma unroll
       for (int e = 0; e < 8; ++e) sum += v[c][e];
     }
@@ -322,7 +352,10 @@ __global__ void __launch_bounds__(kNormThreads) audio_layernorm_kernel(const flo
 
 // kernels.zig:435-487 for one (window, head): scores = q.k / sqrt(head_dim)
 // over the window's keys, softmax (math.zig:77-93), weighted sum of values.
-// qkv rows [step][3 width] (q | k | v); out [step][width]. head_dim 64,
+// The q|k|v rows are the Q|K|V GEMM's split partials [split][step][3 width]
+// summed here, plus the biases (projectQkv, model.zig:764-782); the output
+// goes straight into the O GEMM's activation rows (f16 hi and lo, K chunks
+// permuted). head_dim 64,
 // windows of at most 128 steps. One CTA per (window, head, 16 queries): the
 // window's keys and values in shared memory (key rows padded by one float
 // against bank conflicts), each of 4 warps takes 4 queries at once, so a lane
@@ -334,9 +367,13 @@ constexpr int kAttnCtaQueries = kAttnWarps * kAttnQueries;
 constexpr uint32_t kAttnHead = 64;
 constexpr uint32_t kAttnMaxWindow = 128;
 
-__global__ void __launch_bounds__(kAttnWarps * 32) audio_window_attention_kernel(const float* qkv, uint32_t steps,
+// Position of value v inside an 8-value chunk of the activation rows.
+__device__ __forceinline__ uint32_t perm8_inverse(uint32_t v) { return v < 4 ? 2 * v : 2 * (v - 4) + 1; }
+
+__global__ void __launch_bounds__(kAttnWarps * 32) audio_window_attention_kernel(const float* parts, uint32_t splits,
+                                                                                 const float* qkv_bias, uint32_t steps,
                                                                                  uint32_t width, uint32_t window,
-                                                                                 float* out) {
+                                                                                 __half* packed) {
   pdl_wait_and_trigger();
   extern __shared__ float attn_smem[];
   constexpr uint32_t hd = kAttnHead, kstride = hd + 1;
@@ -349,15 +386,26 @@ __global__ void __launch_bounds__(kAttnWarps * 32) audio_window_attention_kernel
   float* qs = vs + size_t(window) * hd;                        // [warps][queries][hd]
   float* ps = qs + size_t(kAttnWarps) * kAttnQueries * hd;     // [warps][queries][window]
   const uint32_t ld = 3 * width;
-  // The window's key and value rows, 16 bytes a load, all loads of a thread
-  // issued before their stores.
+  const size_t plane = size_t(steps) * ld;
+  // Element e of q|k|v row `step`: the sum of its split partials plus its bias.
+  auto qkv4 = [&](uint32_t step, uint32_t e) {
+    const float* src = parts + size_t(step) * ld + e;
+    float4 a = *reinterpret_cast<const float4*>(src);
+    for (uint32_t sp = 1; sp < splits; ++sp) {
+      const float4 b = *reinterpret_cast<const float4*>(src + sp * plane);
+      a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+    }
+    const float4 bias = *reinterpret_cast<const float4*>(qkv_bias + e);
+    return make_float4(__fadd_rn(a.x, bias.x), __fadd_rn(a.y, bias.y), __fadd_rn(a.z, bias.z),
+                       __fadd_rn(a.w, bias.w));
+  };
+  // The window's key and value rows, 16 bytes a load.
   constexpr uint32_t kVec = hd / 4;
 #pragma unroll 4
   for (uint32_t i = threadIdx.x; i < len * kVec; i += blockDim.x) {
     const uint32_t j = i / kVec, d = (i % kVec) * 4;
-    const float* r = qkv + size_t(w0 + j) * ld + h * hd + d;
-    const float4 kv = *reinterpret_cast<const float4*>(r + width);
-    const float4 vv = *reinterpret_cast<const float4*>(r + 2 * width);
+    const float4 kv = qkv4(w0 + j, width + h * hd + d);
+    const float4 vv = qkv4(w0 + j, 2 * width + h * hd + d);
     float* kd = ks + j * kstride + d;
     kd[0] = kv.x;
     kd[1] = kv.y;
@@ -369,9 +417,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32) audio_window_attention_kernel
   const uint32_t qw = q0 + warp * kAttnQueries;  // this warp's first query
   float* q = qs + size_t(warp) * kAttnQueries * hd;
   float* pw = ps + size_t(warp) * kAttnQueries * window;
-  for (uint32_t i = lane; i < kAttnQueries * hd; i += 32) {
-    const uint32_t qq = i / hd, d = i % hd;
-    q[i] = qw + qq < len ? qkv[size_t(w0 + qw + qq) * ld + h * hd + d] : 0.0f;
+  for (uint32_t i = lane; i < kAttnQueries * hd / 4; i += 32) {
+    const uint32_t qq = i / (hd / 4), d = (i % (hd / 4)) * 4;
+    const float4 v = qw + qq < len ? qkv4(w0 + qw + qq, h * hd + d) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    q[qq * hd + d] = v.x;
+    q[qq * hd + d + 1] = v.y;
+    q[qq * hd + d + 2] = v.z;
+    q[qq * hd + d + 3] = v.w;
   }
   __syncthreads();
   if (qw >= len) return;
@@ -411,7 +463,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) audio_window_attention_kernel
     float total = 0.0f;
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
-      const float e = lane + 32u * kk < len ? exp_ref(__fsub_rn(acc[a][kk], mx)) : 0.0f;
+      const float e = lane + 32u * kk < len ? expf(__fsub_rn(acc[a][kk], mx)) : 0.0f;
       acc[a][kk] = e;
       total += e;
     }
@@ -440,9 +492,15 @@ __global__ void __launch_bounds__(kAttnWarps * 32) audio_window_attention_kernel
 #pragma unroll
   for (int a = 0; a < kAttnQueries; ++a) {
     if (qw + a < len) {
-      float* dst = out + size_t(w0 + qw + a) * width + h * hd;
-      dst[lane] = o[a][0];
-      dst[lane + 32] = o[a][1];
+      __half* hi = packed_row(packed, w0 + qw + a, width);
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const uint32_t k = h * hd + lane + 32 * u;
+        const uint32_t at = (k & ~7u) + perm8_inverse(k & 7u);
+        const __half vh = __float2half_rn(o[a][u]);
+        hi[at] = vh;
+        hi[size_t(kCols) * width + at] = __float2half_rn(o[a][u] - __half2float(vh));
+      }
     }
   }
 }
@@ -456,7 +514,7 @@ uint32_t grid_for(size_t work, uint32_t threads) {
 
 int launch_audio_conv1(const float* mel, uint32_t frames, uint32_t mel_bins, uint32_t chunk_frames, uint32_t chunks,
                        const void* w, const float* bias, uint32_t channels, float* out, void* stream) {
-  const size_t work = size_t(chunks) * ((mel_bins - 1) / 2 + 1) * ((chunk_frames - 1) / 2 + 1) * (channels / 8);
+  const size_t work = size_t(chunks) * ((mel_bins - 1) / 2 + 1) * ((chunk_frames - 1) / 2 + 1) * channels;
   return static_cast<int>(launch_pdl(audio_conv1_kernel, dim3(grid_for(work, 256)), dim3(256), 0,
                                      static_cast<cudaStream_t>(stream), mel, frames, mel_bins, chunk_frames, chunks,
                                      static_cast<const __half*>(w), bias, channels, out));
@@ -506,10 +564,12 @@ int launch_audio_epilogue(int mode, const float* parts, uint32_t splits, uint32_
   }
 }
 
-int launch_audio_layernorm(const float* x, const float* weight, const float* bias, uint32_t width, float eps,
-                           uint32_t steps, float* out, void* packed, void* stream) {
+int launch_audio_layernorm(float* x, const float* parts, uint32_t splits, const float* rbias, const float* weight,
+                           const float* bias, uint32_t width, float eps, uint32_t steps, float* out, void* packed,
+                           void* stream) {
   return static_cast<int>(launch_pdl(audio_layernorm_kernel, dim3(steps), dim3(kNormThreads), 0,
-                                     static_cast<cudaStream_t>(stream), x, weight, bias, width, eps, out,
+                                     static_cast<cudaStream_t>(stream), x, parts, splits,
+                                     size_t(steps) * width, rbias, weight, bias, width, eps, out,
                                      static_cast<__half*>(packed)));
 }
 
@@ -519,12 +579,14 @@ size_t audio_attention_smem(uint32_t window, uint32_t head_dim) {
           size_t(kAttnWarps) * kAttnQueries * (head_dim + window)) * 4;
 }
 
-int launch_audio_attention(const float* qkv, uint32_t steps, uint32_t width, uint32_t heads, uint32_t head_dim,
-                           uint32_t window, float* out, void* stream) {
+int launch_audio_attention(const float* parts, uint32_t splits, const float* qkv_bias, uint32_t steps,
+                           uint32_t width, uint32_t heads, uint32_t head_dim, uint32_t window, void* packed,
+                           void* stream) {
   const size_t smem = audio_attention_smem(window, head_dim);
   const dim3 grid((steps + window - 1) / window, heads, (window + kAttnCtaQueries - 1) / kAttnCtaQueries);
   return static_cast<int>(launch_pdl(audio_window_attention_kernel, grid, dim3(kAttnWarps * 32), smem,
-                                     static_cast<cudaStream_t>(stream), qkv, steps, width, window, out));
+                                     static_cast<cudaStream_t>(stream), parts, splits, qkv_bias, steps, width,
+                                     window, static_cast<__half*>(packed)));
 }
 
 int prepare_audio_kernels(uint32_t window, uint32_t head_dim) {

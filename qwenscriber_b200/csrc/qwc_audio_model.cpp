@@ -93,7 +93,7 @@ int32_t AudioModel::build(const AudioGeometry& geometry, const Find& find, int s
   // What these kernels take: 8-channel taps for the im2col loads, 8-value
   // chunks of every row, LayerNorm rows of at most 4096, head_dim <= 128, and
   // an attention window whose keys and values fit in shared memory.
-  if (C % 8 != 0 || d % 8 != 0 || g.ffn % 8 != 0 || g.output_dim % 8 != 0 || d > 4096 || g.head_dim > 128 ||
+  if (C % 8 != 0 || C > 1024 || d % 8 != 0 || g.ffn % 8 != 0 || g.output_dim % 8 != 0 || d > 4096 || g.head_dim > 128 ||
       g.window == 0 || audio_attention_smem(g.window, g.head_dim) > 200 * 1024) {
     return QWC_UNSUPPORTED_MODEL;
   }
@@ -257,11 +257,8 @@ int32_t AudioModel::build(const AudioGeometry& geometry, const Find& find, int s
   xb_ = alloc(steps_blocks * 2 * kColsPerBlock * maxk * 2);
   x_ = alloc(size_t(g.max_steps) * d * 4);
   conv_stage_ = alloc(size_t(g.max_steps) * d * 4);
-  qkv_ = alloc(size_t(g.max_steps) * 3 * d * 4);
-  attn_ = alloc(size_t(g.max_steps) * d * 4);
   err_ = static_cast<int32_t*>(alloc(256));
-  for (void* p : {mel_, conv1_, im2col_, conv2_, conv3_, parts_, xb_, x_, conv_stage_, qkv_, attn_,
-                  static_cast<void*>(err_)}) {
+  for (void* p : {mel_, conv1_, im2col_, conv2_, conv3_, parts_, xb_, x_, conv_stage_, static_cast<void*>(err_)}) {
     if (!p) return QWC_OUT_OF_MEMORY;
   }
   AUDIO_CUDA(cudaMemset(im2col_, 0, size_t(ceil_div(cols2, kColsPerBlock)) * 2 * kColsPerBlock * kpad_ * 2));
@@ -388,24 +385,27 @@ int32_t AudioModel::enqueue(const float* mel_dev, uint32_t frames, float* out_de
   }
   AUDIO_CUDA(cudaMemcpyAsync(conv_stage_, x, size_t(steps) * d * 4, cudaMemcpyDeviceToDevice, stream));
 
-  // The tower's blocks (model.zig:622-704).
-  float* qkv = static_cast<float*>(qkv_);
-  float* attn = static_cast<float*>(attn_);
+  // The tower's blocks (model.zig:622-704). Each block's residual add of
+  // O (and of the feed-forward) runs in the LayerNorm kernel that follows it:
+  // the block's ffn norm, the next block's attention norm, or the final norm
+  // (in place, as the reference's last layerNorm).
+  if (!layers_.empty()) {
+    AUDIO_LAUNCH(launch_audio_layernorm(x, nullptr, 0, nullptr, layers_[0].attn_norm_w, layers_[0].attn_norm_b, d,
+                                        g.eps, steps, nullptr, xb_, st));
+  } else {
+    AUDIO_LAUNCH(launch_audio_layernorm(x, nullptr, 0, nullptr, final_w_, final_b_, d, g.eps, steps, x, xb_, st));
+  }
   for (uint32_t li = 0; li < g.layers; ++li) {
     const Layer& l = layers_[li];
-    AUDIO_LAUNCH(launch_audio_layernorm(x, l.attn_norm_w, l.attn_norm_b, d, g.eps, steps, nullptr, xb_, st));
     const Mat* m3[3] = {&l.q, &l.k, &l.v};
     int32_t s = gemm(m3, 3, d, steps, 3 * d);
     if (s < 0) return s;
-    AUDIO_LAUNCH(launch_audio_epilogue(1, parts, s, steps, 3 * d, 3 * d, qkv_bias_ + size_t(li) * 3 * d, 0, qkv,
-                                       3 * d, nullptr, st));
-    AUDIO_LAUNCH(launch_audio_attention(qkv, steps, d, g.heads, g.head_dim, g.window, attn, st));
-    AUDIO_LAUNCH(launch_pack_activations(attn, steps, d, xb_, st));
+    AUDIO_LAUNCH(launch_audio_attention(parts, s, qkv_bias_ + size_t(li) * 3 * d, steps, d, g.heads, g.head_dim,
+                                        g.window, xb_, st));
     const Mat* mo[1] = {&l.o};
     s = gemm(mo, 1, d, steps, d);
     if (s < 0) return s;
-    AUDIO_LAUNCH(launch_audio_epilogue(2, parts, s, steps, d, d, l.o_b, 0, x, d, nullptr, st));
-    AUDIO_LAUNCH(launch_audio_layernorm(x, l.norm_w, l.norm_b, d, g.eps, steps, nullptr, xb_, st));
+    AUDIO_LAUNCH(launch_audio_layernorm(x, parts, s, l.o_b, l.norm_w, l.norm_b, d, g.eps, steps, nullptr, xb_, st));
     const Mat* mi[1] = {&l.ffn_in};
     s = gemm(mi, 1, d, steps, g.ffn);
     if (s < 0) return s;
@@ -413,9 +413,15 @@ int32_t AudioModel::enqueue(const float* mel_dev, uint32_t frames, float* out_de
     const Mat* mf[1] = {&l.ffn_out};
     s = gemm(mf, 1, g.ffn, steps, d);
     if (s < 0) return s;
-    AUDIO_LAUNCH(launch_audio_epilogue(2, parts, s, steps, d, d, l.ffn_out_b, 0, x, d, nullptr, st));
+    if (li + 1 < g.layers) {
+      const Layer& next = layers_[li + 1];
+      AUDIO_LAUNCH(launch_audio_layernorm(x, parts, s, l.ffn_out_b, next.attn_norm_w, next.attn_norm_b, d, g.eps,
+                                          steps, nullptr, xb_, st));
+    } else {
+      AUDIO_LAUNCH(launch_audio_layernorm(x, parts, s, l.ffn_out_b, final_w_, final_b_, d, g.eps, steps, x, xb_,
+                                          st));
+    }
   }
-  AUDIO_LAUNCH(launch_audio_layernorm(x, final_w_, final_b_, d, g.eps, steps, x, xb_, st));
 
   // Projector (model.zig:707-733).
   {

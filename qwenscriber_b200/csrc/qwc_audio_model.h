@@ -110,7 +110,7 @@ class AudioModel {
   float* qkv_bias_ = nullptr;  // [layer][3 d_model]
   float* position_ = nullptr;  // [chunk_steps][d_model]
   void *mel_ = nullptr, *conv1_ = nullptr, *im2col_ = nullptr, *conv2_ = nullptr, *conv3_ = nullptr, *parts_ = nullptr,
-       *xb_ = nullptr, *x_ = nullptr, *conv_stage_ = nullptr, *qkv_ = nullptr, *attn_ = nullptr;
+       *xb_ = nullptr, *x_ = nullptr, *conv_stage_ = nullptr;
   int32_t* err_ = nullptr;
   size_t parts_floats_ = 0;
 };

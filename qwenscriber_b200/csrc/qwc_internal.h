@@ -249,10 +249,16 @@ int launch_audio_flatten(const float* conv3, uint32_t steps, uint32_t chunk_step
 // mode: 0 position, 1 bias, 2 residual, 3 GELU into GEMM activation rows.
 int launch_audio_epilogue(int mode, const float* parts, uint32_t splits, uint32_t steps, uint32_t ld, uint32_t width,
                           const float* add, uint32_t chunk_steps, float* x, uint32_t x_ld, void* packed, void* stream);
-int launch_audio_layernorm(const float* x, const float* weight, const float* bias, uint32_t width, float eps,
-                           uint32_t steps, float* out, void* packed, void* stream);
-int launch_audio_attention(const float* qkv, uint32_t steps, uint32_t width, uint32_t heads, uint32_t head_dim,
-                           uint32_t window, float* out, void* stream);
+// LayerNorm of each of `steps` rows of x, after x += sum of `splits`
+// partials [split][steps][width] + rbias when `parts` is given.
+int launch_audio_layernorm(float* x, const float* parts, uint32_t splits, const float* rbias, const float* weight,
+                           const float* bias, uint32_t width, float eps, uint32_t steps, float* out, void* packed,
+                           void* stream);
+// Windowed attention over the Q|K|V GEMM's partials [split][steps][3 width]
+// plus the q|k|v biases, into the O GEMM's activation rows.
+int launch_audio_attention(const float* parts, uint32_t splits, const float* qkv_bias, uint32_t steps,
+                           uint32_t width, uint32_t heads, uint32_t head_dim, uint32_t window, void* packed,
+                           void* stream);
 size_t audio_attention_smem(uint32_t window, uint32_t head_dim);
 int prepare_audio_kernels(uint32_t window, uint32_t head_dim);
 // x[columns][cols] f32 -> the GEMM's activation rows (f16 hi and lo, 128 rows
