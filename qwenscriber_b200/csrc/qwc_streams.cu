@@ -669,9 +669,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) streams_attention_kernel(cons
   };
 
   const float scaling = m.attn_scaling;
-  uint32_t it = 0;
+  // Work items: two consecutive chunks of one segment (or a segment's last
+  // odd chunk alone); the two warp groups take alternate items. A warp's
+  // latency chain (score MMAs, the softmax shuffles, value MMAs) then covers
+  // 32 positions instead of 16.
+  uint32_t it = 0, item = 0;
   UnitPos up = unit_pos(a, P, kv_heads, u0);
-  for (uint32_t u = u0; u < u1; ++u, ++it, up = next_unit(a, kv_heads, up)) {
+  for (uint32_t u = u0; u < u1;) {
     if (up.s != cur.s || up.h != cur.h) {
       if (cur.s != 0xFFFFFFFFu) flush();  // ends with every warp past the previous segment
       cur = up;
@@ -698,103 +702,141 @@ __global__ void __launch_bounds__(kAttnThreads, 1) streams_attention_kernel(cons
         qb[kk][1] = pack_f16x2(part[2], part[3]);
       }
     }
-    ++seg_count;
-    if ((it & 1u) != grp) continue;  // the other four warps take this chunk
-    const uint32_t slot = it % kAttnSlots;
-    if (ok && !mbar_wait_bounded(&a->full[slot], (it / kAttnSlots) & 1u, P.error, P.timeout_ns, 101)) ok = false;
-    const uint8_t* tile = a->ring[slot];
-    const uint32_t newest = a->pos[up.s];
-    const uint32_t base_pos = up.ch * kAttnChunk;
-    // ---- scores: q . k for positions prow0, prow1 (head hq) ----
-    float sc[2];
-    {
-      float d[2][4];
+    UnitPos nx = up;
+    bool two = false;
+    if (u + 1 < u1) {
+      nx = next_unit(a, kv_heads, up);
+      two = nx.s == up.s && nx.h == up.h;
+    }
+    const uint32_t nt_units = two ? 2u : 1u;
+    seg_count += nt_units;
+    if ((item & 1u) == grp) {
+      const uint8_t* tiles[2];
+      uint32_t slots[2];
 #pragma unroll
-      for (int g = 0; g < 2; ++g) {
-        d[g][0] = d[g][1] = d[g][2] = d[g][3] = 0.0f;
-        const uint4 k0 = *reinterpret_cast<const uint4*>(tile + kTK + swz(prow0, 4u * g + i));
-        const uint4 k1 = *reinterpret_cast<const uint4*>(tile + kTK + swz(prow1, 4u * g + i));
-        const uint32_t w0[4] = {k0.x, k0.y, k0.z, k0.w};
-        const uint32_t w1[4] = {k1.x, k1.y, k1.z, k1.w};
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          mma16816(d[g], codes_f16x2<0x4140>(w0[t]), codes_f16x2<0x4140>(w1[t]), codes_f16x2<0x4342>(w0[t]),
-                   codes_f16x2<0x4342>(w1[t]), qb[4 * g + t][0], qb[4 * g + t][1]);
+      for (int tt = 0; tt < 2; ++tt) {
+        const uint32_t itt = it + (tt == 1 && two ? 1u : 0u);
+        slots[tt] = itt % kAttnSlots;
+        tiles[tt] = a->ring[slots[tt]];
+        if ((tt == 0 || two) && ok &&
+            !mbar_wait_bounded(&a->full[slots[tt]], (itt / kAttnSlots) & 1u, P.error, P.timeout_ns, 101)) {
+          ok = false;
         }
       }
-      const uint32_t so = (up.h % 4u) * 4u;
-      const uint32_t ks0 = *reinterpret_cast<const uint32_t*>(tile + kTKS + prow0 * 16u + so);
-      const uint32_t ks1 = *reinterpret_cast<const uint32_t*>(tile + kTKS + prow1 * 16u + so);
-      const float s00 = f16_bits_to_f32_fast(ks0 & 0xFFFFu), s01 = f16_bits_to_f32_fast(ks0 >> 16);
-      const float s10 = f16_bits_to_f32_fast(ks1 & 0xFFFFu), s11 = f16_bits_to_f32_fast(ks1 >> 16);
-      const float t0 = fmaf(s00, d[0][0] + d[0][1], s01 * (d[1][0] + d[1][1]));
-      const float t1 = fmaf(s10, d[0][2] + d[0][3], s11 * (d[1][2] + d[1][3]));
-      sc[0] = (ok && base_pos + prow0 <= newest) ? scaling * t0 : -INFINITY;
-      sc[1] = (ok && base_pos + prow1 <= newest) ? scaling * t1 : -INFINITY;
-    }
-    // ---- online softmax over the warp's 16 positions (math.zig:77-93) ----
-    float mx = fmaxf(sc[0], sc[1]);
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-    const float m_new = fmaxf(m_run, mx);
-    const float resc = (m_run == -INFINITY) ? 0.0f : __expf(m_run - m_new);
-    const float p0 = sc[0] == -INFINITY ? 0.0f : __expf(sc[0] - m_new);
-    const float p1 = sc[1] == -INFINITY ? 0.0f : __expf(sc[1] - m_new);
-    float ps = p0 + p1;
-    ps += __shfl_xor_sync(0xffffffffu, ps, 4);
-    ps += __shfl_xor_sync(0xffffffffu, ps, 8);
-    ps += __shfl_xor_sync(0xffffffffu, ps, 16);
-    l_run = fmaf(l_run, resc, ps);
-    m_run = m_new;
-    // Accumulators of value rows of head hrow: rescale when its maximum moved.
-    const float f_h0 = __shfl_sync(0xffffffffu, resc, 0), f_h1 = __shfl_sync(0xffffffffu, resc, 1);
-    const float f_row = hrow ? f_h1 : f_h0;
-    if (__any_sync(0xffffffffu, f_row != 1.0f)) {
+      const uint32_t newest = a->pos[up.s];
+      // ---- scores: q . k for positions prow0, prow1 of each tile (head hq) ----
+      float sc[2][2];
 #pragma unroll
-      for (int nt = 0; nt < 16; ++nt) {
-        acc[nt][0] *= f_row;
-        acc[nt][1] *= f_row;
+      for (int tt = 0; tt < 2; ++tt) {
+        sc[tt][0] = sc[tt][1] = -INFINITY;
+        if (tt == 1 && !two) continue;
+        const uint8_t* tile = tiles[tt];
+        const uint32_t base_pos = (up.ch + tt) * kAttnChunk;
+        float d[2][4];
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          d[g][0] = d[g][1] = d[g][2] = d[g][3] = 0.0f;
+          const uint4 k0 = *reinterpret_cast<const uint4*>(tile + kTK + swz(prow0, 4u * g + i));
+          const uint4 k1 = *reinterpret_cast<const uint4*>(tile + kTK + swz(prow1, 4u * g + i));
+          const uint32_t w0[4] = {k0.x, k0.y, k0.z, k0.w};
+          const uint32_t w1[4] = {k1.x, k1.y, k1.z, k1.w};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            mma16816(d[g], codes_f16x2<0x4140>(w0[t]), codes_f16x2<0x4140>(w1[t]), codes_f16x2<0x4342>(w0[t]),
+                     codes_f16x2<0x4342>(w1[t]), qb[4 * g + t][0], qb[4 * g + t][1]);
+          }
+        }
+        const uint32_t so = (up.h % 4u) * 4u;
+        const uint32_t ks0 = *reinterpret_cast<const uint32_t*>(tile + kTKS + prow0 * 16u + so);
+        const uint32_t ks1 = *reinterpret_cast<const uint32_t*>(tile + kTKS + prow1 * 16u + so);
+        const float s00 = f16_bits_to_f32_fast(ks0 & 0xFFFFu), s01 = f16_bits_to_f32_fast(ks0 >> 16);
+        const float s10 = f16_bits_to_f32_fast(ks1 & 0xFFFFu), s11 = f16_bits_to_f32_fast(ks1 >> 16);
+        const float t0 = fmaf(s00, d[0][0] + d[0][1], s01 * (d[1][0] + d[1][1]));
+        const float t1 = fmaf(s10, d[0][2] + d[0][3], s11 * (d[1][2] + d[1][3]));
+        sc[tt][0] = (ok && base_pos + prow0 <= newest) ? scaling * t0 : -INFINITY;
+        sc[tt][1] = (ok && base_pos + prow1 <= newest) ? scaling * t1 : -INFINITY;
+      }
+      // ---- online softmax over the warp's positions of the item (math.zig:77-93) ----
+      float mx = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      const float m_new = fmaxf(m_run, mx);
+      const float resc = (m_run == -INFINITY) ? 0.0f : __expf(m_run - m_new);
+      float pp[2][2];
+#pragma unroll
+      for (int tt = 0; tt < 2; ++tt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) pp[tt][e] = sc[tt][e] == -INFINITY ? 0.0f : __expf(sc[tt][e] - m_new);
+      }
+      float ps = (pp[0][0] + pp[0][1]) + (pp[1][0] + pp[1][1]);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+      l_run = fmaf(l_run, resc, ps);
+      m_run = m_new;
+      // Accumulators of value rows of head hrow: rescale when its maximum moved.
+      const float f_h0 = __shfl_sync(0xffffffffu, resc, 0), f_h1 = __shfl_sync(0xffffffffu, resc, 1);
+      const float f_row = hrow ? f_h1 : f_h0;
+      if (__any_sync(0xffffffffu, f_row != 1.0f)) {
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+          acc[n][0] *= f_row;
+          acc[n][1] *= f_row;
+        }
+      }
+#pragma unroll
+      for (int tt = 0; tt < 2; ++tt) {
+        if (tt == 1 && !two) continue;
+        const uint8_t* tile = tiles[tt];
+        // ---- value weights: A rows (head hrow, group grow, hi/lo hl) at warp positions 2i, 2i+1, 2i+8, 2i+9 ----
+        uint32_t pa0, pa2;
+        {
+          const float a00 = __shfl_sync(0xffffffffu, pp[tt][0], 8 * i + hrow);      // position 2i
+          const float a10 = __shfl_sync(0xffffffffu, pp[tt][1], 8 * i + hrow);      // position 2i + 8
+          const float a01 = __shfl_sync(0xffffffffu, pp[tt][0], 8 * i + 4 + hrow);  // position 2i + 1
+          const float a11 = __shfl_sync(0xffffffffu, pp[tt][1], 8 * i + 4 + hrow);  // position 2i + 9
+          const uint32_t so = (up.h % 4u) * 4u + grow * 2u;
+          const float pw[4] = {a00, a01, a10, a11};
+          const uint32_t rows[4] = {va, va + 1u, va + 8u, va + 9u};
+          float wv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float sv =
+                f16_bits_to_f32_fast(*reinterpret_cast<const uint16_t*>(tile + kTVS + rows[e] * 16u + so));
+            const float x = pw[e] > 0.0f ? pw[e] * sv * kWeightScale : 0.0f;
+            const float xh = __half2float(__float2half_rn(x));
+            wv[e] = hl ? x - xh : xh;
+          }
+          pa0 = pack_f16x2(wv[0], wv[1]);
+          pa2 = pack_f16x2(wv[2], wv[3]);
+        }
+        // ---- values: acc[(c, j)] += weights x (code - 128) ----
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t chunk = 2u * c + (r >> 2), off = 4u * (r & 3u);
+          const uint32_t wa = *reinterpret_cast<const uint32_t*>(tile + kTV + swz(va, chunk) + off);
+          const uint32_t wb = *reinterpret_cast<const uint32_t*>(tile + kTV + swz(va + 1u, chunk) + off);
+          const uint32_t wc = *reinterpret_cast<const uint32_t*>(tile + kTV + swz(va + 8u, chunk) + off);
+          const uint32_t wd = *reinterpret_cast<const uint32_t*>(tile + kTV + swz(va + 9u, chunk) + off);
+          const uint32_t ab01 = __byte_perm(wa, wb, 0x5140), ab23 = __byte_perm(wa, wb, 0x7362);
+          const uint32_t cd01 = __byte_perm(wc, wd, 0x5140), cd23 = __byte_perm(wc, wd, 0x7362);
+          mma16816(acc[4 * c + 0], pa0, 0u, pa2, 0u, codes_f16x2<0x4140>(ab01), codes_f16x2<0x4140>(cd01));
+          mma16816(acc[4 * c + 1], pa0, 0u, pa2, 0u, codes_f16x2<0x4342>(ab01), codes_f16x2<0x4342>(cd01));
+          mma16816(acc[4 * c + 2], pa0, 0u, pa2, 0u, codes_f16x2<0x4140>(ab23), codes_f16x2<0x4140>(cd23));
+          mma16816(acc[4 * c + 3], pa0, 0u, pa2, 0u, codes_f16x2<0x4342>(ab23), codes_f16x2<0x4342>(cd23));
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&a->empty[slots[0]]);  // this warp is done with the item's chunks
+        if (two) mbar_arrive(&a->empty[slots[1]]);
       }
     }
-    // ---- value weights: A rows (head hrow, group grow, hi/lo hl) at warp positions 2i, 2i+1, 2i+8, 2i+9 ----
-    uint32_t pa0, pa2;
-    {
-      const float a00 = __shfl_sync(0xffffffffu, p0, 8 * i + hrow);      // position 2i
-      const float a10 = __shfl_sync(0xffffffffu, p1, 8 * i + hrow);      // position 2i + 8
-      const float a01 = __shfl_sync(0xffffffffu, p0, 8 * i + 4 + hrow);  // position 2i + 1
-      const float a11 = __shfl_sync(0xffffffffu, p1, 8 * i + 4 + hrow);  // position 2i + 9
-      const uint32_t so = (up.h % 4u) * 4u + grow * 2u;
-      const float pw[4] = {a00, a01, a10, a11};
-      const uint32_t rows[4] = {va, va + 1u, va + 8u, va + 9u};
-      float wv[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float sv = f16_bits_to_f32_fast(*reinterpret_cast<const uint16_t*>(tile + kTVS + rows[e] * 16u + so));
-        const float x = pw[e] > 0.0f ? pw[e] * sv * kWeightScale : 0.0f;
-        const float xh = __half2float(__float2half_rn(x));
-        wv[e] = hl ? x - xh : xh;
-      }
-      pa0 = pack_f16x2(wv[0], wv[1]);
-      pa2 = pack_f16x2(wv[2], wv[3]);
-    }
-    // ---- values: acc[(c, j)] += weights x (code - 128) ----
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const uint32_t chunk = 2u * c + (r >> 2), off = 4u * (r & 3u);
-      const uint32_t wa = *reinterpret_cast<const uint32_t*>(tile + kTV + swz(va, chunk) + off);
-      const uint32_t wb = *reinterpret_cast<const uint32_t*>(tile + kTV + swz(va + 1u, chunk) + off);
-      const uint32_t wc = *reinterpret_cast<const uint32_t*>(tile + kTV + swz(va + 8u, chunk) + off);
-      const uint32_t wd = *reinterpret_cast<const uint32_t*>(tile + kTV + swz(va + 9u, chunk) + off);
-      const uint32_t ab01 = __byte_perm(wa, wb, 0x5140), ab23 = __byte_perm(wa, wb, 0x7362);
-      const uint32_t cd01 = __byte_perm(wc, wd, 0x5140), cd23 = __byte_perm(wc, wd, 0x7362);
-      mma16816(acc[4 * c + 0], pa0, 0u, pa2, 0u, codes_f16x2<0x4140>(ab01), codes_f16x2<0x4140>(cd01));
-      mma16816(acc[4 * c + 1], pa0, 0u, pa2, 0u, codes_f16x2<0x4342>(ab01), codes_f16x2<0x4342>(cd01));
-      mma16816(acc[4 * c + 2], pa0, 0u, pa2, 0u, codes_f16x2<0x4140>(ab23), codes_f16x2<0x4140>(cd23));
-      mma16816(acc[4 * c + 3], pa0, 0u, pa2, 0u, codes_f16x2<0x4342>(ab23), codes_f16x2<0x4342>(cd23));
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&a->empty[slot]);  // this warp is done with the chunk
+    ++item;
+    u += nt_units;
+    it += nt_units;
+    up = two ? next_unit(a, kv_heads, nx) : nx;
   }
   if (cur.s != 0xFFFFFFFFu) flush();
 }
