@@ -780,7 +780,8 @@ int32_t record_step(Handle* h, bool logits) {
       ++n;
       ++mi;
     }
-    return ok(launch_gemm_jobs(cm, sm, rows, fmts, offs, n, bmap, cols, kMaxStreams, splits, out, ld, P.error, st));
+    return ok(launch_gemm_jobs(cm, sm, rows, fmts, offs, n, bmap, cols, kMaxStreams, splits, out, ld, P.error, st, 1,
+                               P.timeout_ns));
   };
   float* part = b.part0.as<float>();
   QWC_TRY(ok(launch_streams_norm(P, 1, m.layers[0].attn_norm, nullptr, 0, st)));

@@ -356,7 +356,7 @@ int32_t AudioModel::enqueue(const float* mel_dev, uint32_t frames, float* out_de
     const uint32_t cb = ceil_div(columns, kColsPerBlock);
     AUDIO_TRY(gemm_act_map(xb_, k, bm, cb));
     const uint32_t s = splits_for(total, k, columns);
-    AUDIO_LAUNCH(launch_gemm_jobs(cm, sm, rows, fmts, offs, n, bm, k, columns, s, parts, ld, err_, st, cb));
+    AUDIO_LAUNCH(launch_gemm_jobs(cm, sm, rows, fmts, offs, n, bm, k, columns, s, parts, ld, err_, st, cb, timeout_ns));
     return static_cast<int32_t>(s);
   };
   auto conv_gemm = [&](int j, const float* in, uint32_t ih, uint32_t iw, float* out) -> int32_t {

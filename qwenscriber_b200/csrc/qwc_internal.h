@@ -215,7 +215,7 @@ struct alignas(64) KvMaps4 {
 int launch_gemm_jobs(const uint8_t (*codes_maps)[128], const uint8_t (*scale_maps)[128], const uint32_t* rows,
                      const uint32_t* formats, const uint32_t* out_offsets, uint32_t njobs, const uint8_t* map_b,
                      uint32_t cols, uint32_t streams, uint32_t splits, float* out, uint32_t out_ld, int32_t* error,
-                     void* stream, uint32_t col_blocks = 1);
+                     void* stream, uint32_t col_blocks = 1, uint64_t timeout_ns = 2000000000ull);
 int launch_gemm_streams(const uint8_t* map_codes, const uint8_t* map_scales, const uint8_t* map_b, uint32_t rows,
                         uint32_t cols, uint32_t format, uint32_t splits, float* out, int32_t* error, void* stream);
 // TMA descriptors for the stream GEMM: a weight matrix (codes and scales
