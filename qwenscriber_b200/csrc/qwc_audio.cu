@@ -46,7 +46,7 @@ __host__ __device__ constexpr int perm8(int e) { return (e & 1) ? 4 + (e >> 1) :
 __device__ __forceinline__ float erf_ref(float x) {
   const float sign = x < 0.0f ? -1.0f : 1.0f;
   const float m = fabsf(x);
-  const float t = __fdiv_rn(1.0f, __fadd_rn(1.0f, __fmul_rn(0.5f, m)));
+  const float t = __frcp_rn(__fadd_rn(1.0f, __fmul_rn(0.5f, m)));  // 1 / (1 + m / 2), correctly rounded
   float poly = __fadd_rn(-0.82215223f, __fmul_rn(t, 0.17087277f));
   poly = __fadd_rn(1.48851587f, __fmul_rn(t, poly));
   poly = __fadd_rn(-1.13520398f, __fmul_rn(t, poly));
@@ -86,11 +86,13 @@ __device__ __forceinline__ __half* packed_row(__half* base, uint32_t col, uint32
 // ---- convolution 1 (one input channel): kernels.zig:332-432 ----
 // mel [mel_bins][frames] -> out [chunk][h1][w1][channels], zero frames past
 // the clip (the reference pads each chunk in the mel domain, model.zig:535-545).
-// A thread takes one (position, channel), channels fastest, so a warp's taps
-// are one broadcast load each and its stores are contiguous. The weights sit
-// in shared memory as [tap][channel] floats (lanes read consecutive banks).
+// A thread takes one position and kConv1Group channels c0 + k * (C / group),
+// channels fastest across threads, so a warp's taps are broadcast loads, read
+// once for the group, and its stores are contiguous. The weights sit in
+// shared memory as [tap][channel] floats (lanes read consecutive banks).
 // Each channel sums its valid taps in the reference's order.
 constexpr uint32_t kConv1MaxChannels = 1024;
+constexpr uint32_t kConv1Group = 4;
 
 __global__ void __launch_bounds__(256) audio_conv1_kernel(const float* mel, uint32_t frames, uint32_t mel_bins,
                                                           uint32_t chunk_frames, uint32_t chunks, const __half* w,
@@ -105,20 +107,30 @@ __global__ void __launch_bounds__(256) audio_conv1_kernel(const float* mel, uint
   __syncthreads();
   pdl_wait_and_trigger();
   const uint32_t h1 = (mel_bins - 1) / 2 + 1, w1 = (chunk_frames - 1) / 2 + 1;
-  const uint32_t total = chunks * h1 * w1 * channels;
+  const uint32_t per = channels / kConv1Group;
+  const uint32_t total = chunks * h1 * w1 * per;
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
-    const uint32_t oc = i % channels, pos = i / channels;
+    const uint32_t c0 = i % per, pos = i / per;
     const uint32_t ox = pos % w1, oy = (pos / w1) % h1, chunk = pos / (w1 * h1);
-    float acc = 0.0f;
+    float x[9];
+    bool in[9];
 #pragma unroll
     for (int t = 0; t < 9; ++t) {
       const int iy = int(2 * oy) + t / 3 - 1, ix = int(2 * ox) + t % 3 - 1;
-      if (iy < 0 || iy >= int(mel_bins) || ix < 0 || ix >= int(chunk_frames)) continue;
+      in[t] = iy >= 0 && iy < int(mel_bins) && ix >= 0 && ix < int(chunk_frames);
       const uint32_t frame = chunk * chunk_frames + uint32_t(ix);
-      const float sample = frame < frames ? mel[size_t(iy) * frames + frame] : 0.0f;
-      acc = __fadd_rn(acc, __fmul_rn(ws[t * channels + oc], sample));
+      x[t] = in[t] && frame < frames ? mel[size_t(iy) * frames + frame] : 0.0f;
     }
-    out[i] = gelu_ref(__fadd_rn(bs[oc], acc));
+#pragma unroll
+    for (uint32_t k = 0; k < kConv1Group; ++k) {
+      const uint32_t oc = c0 + k * per;
+      float acc = 0.0f;
+#pragma unroll
+      for (int t = 0; t < 9; ++t) {
+        if (in[t]) acc = __fadd_rn(acc, __fmul_rn(ws[t * channels + oc], x[t]));
+      }
+      out[size_t(pos) * channels + oc] = gelu_ref(__fadd_rn(bs[oc], acc));
+    }
   }
 }
 
@@ -514,7 +526,7 @@ uint32_t grid_for(size_t work, uint32_t threads) {
 
 int launch_audio_conv1(const float* mel, uint32_t frames, uint32_t mel_bins, uint32_t chunk_frames, uint32_t chunks,
                        const void* w, const float* bias, uint32_t channels, float* out, void* stream) {
-  const size_t work = size_t(chunks) * ((mel_bins - 1) / 2 + 1) * ((chunk_frames - 1) / 2 + 1) * channels;
+  const size_t work = size_t(chunks) * ((mel_bins - 1) / 2 + 1) * ((chunk_frames - 1) / 2 + 1) * channels / 4;
   return static_cast<int>(launch_pdl(audio_conv1_kernel, dim3(grid_for(work, 256)), dim3(256), 0,
                                      static_cast<cudaStream_t>(stream), mel, frames, mel_bins, chunk_frames, chunks,
                                      static_cast<const __half*>(w), bias, channels, out));
