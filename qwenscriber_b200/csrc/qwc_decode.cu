@@ -13,7 +13,10 @@
 //   * eight consumer warps dequantize in registers and reduce with warp
 //     shuffles (the dot products of kernels.zig:118-158); the activation
 //     vector sits in shared memory, read once per 16-byte code chunk and
-//     shared by the four rows a warp works on at a time. Fused epilogues:
+//     shared by the four rows a warp works on at a time. The lm_head (the
+//     one stage with many tiles per CTA) runs on the integer tensor cores
+//     instead: exact integer group sums of the codes against byte limbs of
+//     the activations (gemv_tiles_mma). Fused epilogues:
 //     QK-RMSNorm + RoPE + q8 KV append inside the attention phase, residual
 //     adds, SwiGLU, and the argmax.
 //
@@ -196,7 +199,11 @@ __device__ int stage_pieces(const DevModel& m, uint32_t layer, int stage, uint32
   return count;
 }
 
-__device__ __forceinline__ uint32_t rows_per_tile(const Piece& p) { return kSlotBytes / (p.scale_row + p.code_row); }
+// Rows per ring slot; an integer-GEMV tile (`regions`) leaves 64 bytes for
+// the gap between its two code regions (Producer::issue).
+__device__ __forceinline__ uint32_t rows_per_tile(const Piece& p, bool regions = false) {
+  return (kSlotBytes - (regions ? 64u : 0u)) / (p.scale_row + p.code_row);
+}
 
 __device__ __forceinline__ uint32_t stage_format(const DevModel& m, uint32_t layer, int stage) {
   const DevLayer& L = m.layers[layer];
@@ -206,6 +213,22 @@ __device__ __forceinline__ uint32_t stage_format(const DevModel& m, uint32_t lay
        : stage == kStGate ? L.gate.format
        : stage == kStUp ? L.up.format
                         : L.down.format;
+}
+
+// Length of the stage's input vector (the GEMV's K).
+__device__ __forceinline__ uint32_t stage_width(const DevModel& m, int stage) {
+  return stage == kStO ? m.q_heads * kHeadDim : stage == kStDown ? m.ffn : m.hidden;
+}
+
+// Stages the integer tensor-core GEMV takes (gemv_tiles_mma): the lm_head,
+// for q4 and q8 matrices whose K is a multiple of 256 and fits its side
+// arrays. (The layer stages have one to three tiles per CTA, too few to give
+// whole 16-row blocks to every warp; split over the warps, with a block
+// barrier and a reduction per stage plus the conversion of their inputs,
+// they measured slower than the CUDA-core GEMV.)
+constexpr uint32_t kMmaKMax = 6144;
+__device__ __forceinline__ bool mma_gemv(int stage, uint32_t format, uint32_t width) {
+  return stage == kStLM && (format == kFormatQ4 || format == kFormatQ8) && width % 256 == 0 && width <= kMmaKMax;
 }
 
 // ---------------------------------------------------------------------------
@@ -234,15 +257,25 @@ struct Producer {
     return s->ring[slot];
   }
 
-  // `nr` whole rows of one matrix: their scales, then their codes.
-  __device__ void issue(const Piece& pc, uint32_t r0, uint32_t nr) {
+  // `nr` whole rows of one matrix: their scales, then their codes. For the
+  // integer GEMV (`regions`) the codes go in two regions, the first
+  // (nr + 1) / 2 rows and the rest, the second starting 64 bytes further on
+  // (mod 128) so that rows of the two regions fall in different banks.
+  __device__ void issue(const Piece& pc, uint32_t r0, uint32_t nr, bool regions) {
     const uint32_t bytes_s = nr * pc.scale_row;
     const uint32_t bytes_c = nr * pc.code_row;
     uint64_t* bar;
     uint8_t* dst = begin_tile(bytes_s + bytes_c, &bar);
     if (!dst) return;
     bulk_g2s(dst, pc.scales + size_t(r0) * pc.scale_row, bytes_s, bar);
-    bulk_g2s(dst + bytes_s, pc.codes + size_t(r0) * pc.code_row, bytes_c, bar);
+    const uint8_t* src = pc.codes + size_t(r0) * pc.code_row;
+    if (!regions || nr < 2) {
+      bulk_g2s(dst + bytes_s, src, bytes_c, bar);
+      return;
+    }
+    const uint32_t ha = (nr + 1) / 2;
+    bulk_g2s(dst + bytes_s, src, ha * pc.code_row, bar);
+    bulk_g2s(dst + bytes_s + ha * pc.code_row + 64, src + size_t(ha) * pc.code_row, (nr - ha) * pc.code_row, bar);
   }
 
   // A norm weight vector of n floats.
@@ -283,13 +316,13 @@ struct Producer {
     }
   }
 
-  __device__ void stage(const DevModel& m, uint32_t layer, int st) {
+  __device__ void stage(const DevModel& m, uint32_t layer, int st, bool regions) {
     Piece pieces[3];
     const int np = stage_pieces(m, layer, st, blockIdx.x, gridDim.x, pieces);
     for (int p = 0; p < np && ok; ++p) {
-      const uint32_t per = rows_per_tile(pieces[p]);
+      const uint32_t per = rows_per_tile(pieces[p], regions);
       for (uint32_t r = 0; r < pieces[p].rows && ok; r += per) {
-        issue(pieces[p], r, min(per, pieces[p].rows - r));
+        issue(pieces[p], r, min(per, pieces[p].rows - r), regions);
       }
     }
   }
@@ -330,7 +363,8 @@ __device__ void run_producer(const DecodeLaunch& P, const KvMaps& maps, Smem* s)
       if (st == kStAttn) {
         if (!P.exact) pr.attention_tiles(m, maps, l, position);  // exact mode reads the cache with plain loads
       } else {
-        pr.stage(m, st == kStLM ? 0 : l, st);
+        const uint32_t lq = st == kStLM ? 0 : l;
+        pr.stage(m, lq, st, st == kStLM && !P.exact && mma_gemv(st, stage_format(m, lq, st), stage_width(m, st)));
       }
     }
   }
@@ -875,6 +909,319 @@ __device__ void gemv_tiles(Ctx& c, const Piece* pieces, int np, bool lm, Best& b
   }
 }
 
+// ---- GEMV on the integer tensor cores (default mode, the q4/q8 lm_head) ----
+//
+// The activation vector becomes integers: per quad of 256 activations,
+// x_int = rint(x * 2^e') with |x_int| < 2^30 (e' = e - 4 for q4, below),
+// written as four signed byte limbs (x_int = sum_j limb_j * 256^j). A warp
+// multiplies 16 weight rows by the limb columns with mma.sync m16n8k32
+// (s8 x s8, s32 accumulators), so a group's 64 products and their sum are
+// exact integers. The weights enter already centred, in one or two logic
+// operations per four codes: a q8 code u as u ^ 0x80 = u - 128; a q4 nibble
+// as 16 (u - 8) = (16 u) ^ 0x80, the high nibble masked in place and the low
+// one shifted up first (the factor 16 is why q4 activations are taken at
+// 2^(e - 4)). The per-group integers are combined two limbs at a time,
+// converted to f32 once and scaled by the group's f16 scale; per quad by
+// 2^-e.
+//
+// q4: an MMA covers a pair of groups, the first group's limbs in B columns
+// 0-3 and the second's in columns 4-7 (lanes t < 2 load the first group's
+// codes, t >= 2 the second's, 16 bytes each, and B is zero where a column and
+// a k belong to different groups). q8: an MMA pair covers one group; columns
+// 4-7 repeat 0-3.
+//
+// Shared-memory banks: a tile's codes sit in two regions (Producer::issue)
+// 64 bytes apart mod 128, and MMA row m reads region m & 1, so the eight lanes
+// of a 16-byte load phase read two rows in different banks.
+//
+// Limb layout (written over the quad's own 256 floats of x, 256 bytes per
+// group): q4 [limb j][half t'][32 bytes: the B registers of the four MMAs of
+// that half-group], q8 [limb j][t][16 bytes: k 0-3, 16-19 of the first MMA,
+// then the second's]. The side arrays follow the limb planes in x.
+constexpr uint32_t kMmaScaleOff = kMmaKMax;  // f32 [kMmaKMax / 256]: 2^-e per quad, floats of x
+constexpr uint32_t kMmaZeroOff = 6180;       // 32 zero bytes, 16 mod 128 bytes from x
+static_assert(kMmaScaleOff + kMmaKMax / 256 <= kMmaZeroOff && kMmaZeroOff + 8 <= kXMax,
+              "the integer GEMV's side arrays fit in x");
+static_assert(kMmaScaleOff % 4 == 0 && (kMmaZeroOff * 4) % 128 == 16,
+              "16-byte aligned side arrays; the zero block in banks the limb loads leave free");
+
+__device__ __forceinline__ void mma_s8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1, int c0, int c1, int c2, int c3) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1), "r"(c2), "r"(c3));
+}
+
+// out[j] byte i = in[i] byte j.
+__device__ __forceinline__ void transpose_bytes(const uint32_t (&in)[4], uint32_t (&out)[4]) {
+  const uint32_t a = __byte_perm(in[0], in[1], 0x5140), b = __byte_perm(in[0], in[1], 0x7362);
+  const uint32_t c = __byte_perm(in[2], in[3], 0x5140), d = __byte_perm(in[2], in[3], 0x7362);
+  out[0] = __byte_perm(a, c, 0x5410);
+  out[1] = __byte_perm(a, c, 0x7632);
+  out[2] = __byte_perm(b, d, 0x5410);
+  out[3] = __byte_perm(b, d, 0x7632);
+}
+
+// Four q4 codes of a word as 16 (u - 8) in s8: the high nibbles in place, the
+// low ones shifted up (lop3 LUT 0x6A = (a & b) ^ c).
+__device__ __forceinline__ uint32_t q4_high16(uint32_t w) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, 0xF0F0F0F0, 0x80808080, 0x6A;" : "=r"(r) : "r"(w));
+  return r;
+}
+__device__ __forceinline__ uint32_t q4_low16(uint32_t w) { return q4_high16(w << 4); }
+
+// Writes quad qd's limb planes and scale from this lane's eight activations:
+// lane (gi, t, h) holds activations 64 gi + 16 t + 8 h .. + 7 of the quad.
+// Warp-collective; the caller orders any reads of the quad's bytes before it.
+template <uint32_t FMT>
+__device__ __forceinline__ void limbs_store(Ctx& c, uint32_t qd, const float (&xs)[8]) {
+  const uint32_t lane = static_cast<uint32_t>(c.lane);
+  const uint32_t gi = lane >> 3, t = (lane >> 1) & 3u, h = lane & 1u;
+  uint32_t mb = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) mb = max(mb, __float_as_uint(xs[i]) & 0x7FFFFFFFu);
+  mb = __reduce_max_sync(0xffffffffu, mb);
+  // e = 156 - biased exponent of the quad's largest |x|, so |x| * 2^e < 2^30;
+  // capped so 2^-e stays a normal float. A non-finite quad yields NaN sums.
+  const uint32_t eb = mb >> 23;
+  const int e = eb == 255u ? 0 : min(156 - static_cast<int>(eb), 126);
+  const float up = __uint_as_float(static_cast<uint32_t>(127 + e) << 23);
+  const float sc = FMT == kFormatQ4 ? up * 0.0625f : up;  // q4 codes enter as 16 (u - 8): 2^(e - 4)
+  uint32_t lw[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int xi = __float2int_rn(xs[i] * sc);
+    // Signed base-256 digits: bytes of xi + 0x808080, the low three re-centred.
+    lw[i] = (static_cast<uint32_t>(xi) + 0x00808080u) ^ 0x00808080u;
+  }
+  uint32_t first[4], second[4];
+  if constexpr (FMT == kFormatQ4) {
+    const uint32_t lo[4] = {lw[0], lw[2], lw[4], lw[6]}, hi[4] = {lw[1], lw[3], lw[5], lw[7]};
+    transpose_bytes(lo, first);
+    transpose_bytes(hi, second);
+  } else {
+    const uint32_t a[4] = {lw[0], lw[1], lw[2], lw[3]}, b[4] = {lw[4], lw[5], lw[6], lw[7]};
+    transpose_bytes(a, first);
+    transpose_bytes(b, second);
+  }
+  uint8_t* grp = reinterpret_cast<uint8_t*>(c.s->x) + qd * 1024 + gi * 256;
+  if constexpr (FMT == kFormatQ4) {
+    // This lane's eight activations are block m = 2 (t & 1) + h of the 32 in
+    // half t >> 1: low nibbles in register (m & 1) + 4 (m >> 1) of the half's
+    // eight, high nibbles two registers later.
+    const uint32_t m = 2 * (t & 1u) + h;
+    uint8_t* dst = grp + (t >> 1) * 32 + 4 * ((m & 1u) + 4 * (m >> 1));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      *reinterpret_cast<uint32_t*>(dst + 64 * j) = first[j];
+      *reinterpret_cast<uint32_t*>(dst + 64 * j + 8) = second[j];
+    }
+  } else {
+    uint8_t* dst = grp + t * 16 + h * 8;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) *reinterpret_cast<uint2*>(dst + 64 * j) = make_uint2(first[j], second[j]);
+  }
+  if (lane == 0) {
+    c.s->x[kMmaScaleOff + qd] =
+        eb == 255u ? __uint_as_float(0x7FC00000u) : __uint_as_float(static_cast<uint32_t>(127 - e) << 23);
+  }
+}
+
+// The first of the eight activations a lane converts in quad qd.
+__device__ __forceinline__ uint32_t limb_k0(const Ctx& c, uint32_t qd) {
+  const uint32_t lane = static_cast<uint32_t>(c.lane);
+  return qd * 256 + (lane >> 3) * 64 + 16 * ((lane >> 1) & 3u) + 8 * (lane & 1u);
+}
+
+// Rewrites x (plain f32, x_index order, `width` values) as limb planes in
+// place: a warp takes whole quads and writes a quad once it has read all of it.
+// Also writes the zero block q4 lanes read for B columns of the other group
+// (f32 inputs of other stages overwrite it).
+template <uint32_t FMT>
+__device__ void limbs_from_x(Ctx& c, uint32_t width) {
+  for (uint32_t qd = static_cast<uint32_t>(c.warp); qd < width / 256; qd += kConsumerWarps) {
+    const uint32_t k0 = limb_k0(c, qd);
+    const float4 v0 = *reinterpret_cast<const float4*>(&c.s->x[x_index(k0)]);
+    const float4 v1 = *reinterpret_cast<const float4*>(&c.s->x[x_index(k0 + 4)]);
+    const float xs[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    __syncwarp();  // every lane has read its activations before the quad is overwritten
+    limbs_store<FMT>(c, qd, xs);
+  }
+  if (c.warp == 0 && c.lane < 8) c.s->x[kMmaZeroOff + c.lane] = 0.0f;
+  consumer_sync(kConsumerThreads);
+}
+
+// Per-lane constants of the integer GEMV.
+struct MmaLane {
+  const uint8_t* lb;  // B fragments of pair / group 0
+  uint32_t lstride;   // bytes per pair (q4) / group (q8)
+  uint32_t sh;        // q4: this lane's group within a pair's scale halfwords
+};
+
+template <uint32_t FMT>
+__device__ __forceinline__ MmaLane mma_lane(const Ctx& c) {
+  const uint32_t lane = static_cast<uint32_t>(c.lane);
+  const uint32_t g = lane >> 2, t = lane & 3u;
+  const uint8_t* xb = reinterpret_cast<const uint8_t*>(c.s->x);
+  // q4: lane (g, t) holds B column g; its k belong to group t >> 1 of the
+  // pair, so it loads limb g & 3 of that half-group where (t < 2) == (g < 4),
+  // else zeros (stride 0 keeps it on the zero block).
+  const bool active = FMT == kFormatQ8 || ((t < 2) == (g < 4));
+  MmaLane L;
+  L.lb = FMT == kFormatQ4 ? (active ? xb + (t >> 1) * 256 + (g & 3u) * 64 + (t & 1u) * 32 : xb + kMmaZeroOff * 4)
+                          : xb + (g & 3u) * 64 + t * 16;
+  L.lstride = FMT == kFormatQ4 ? (active ? 512u : 0u) : 256u;
+  L.sh = 16 * (t >> 1);
+  return L;
+}
+
+// Dot products of the 16 rows of block b of a tile (MMA row m: row
+// 8 b + (m >> 1) of code region m & 1, clamped) over every quad; lane (g, 0)
+// returns MMA rows g and g + 8 in out_g, out_8.
+template <uint32_t FMT>
+__device__ __forceinline__ void block_dot(const Ctx& c, const MmaLane& L, const uint8_t* base, const Piece& pc,
+                                          uint32_t nr, uint32_t b, float& out_g, float& out_8) {
+  const uint32_t lane = static_cast<uint32_t>(c.lane);
+  const uint32_t g = lane >> 2, t = lane & 3u;
+  const uint32_t ha = (nr + 1) / 2, hb = nr - ha;
+  const uint32_t quads = pc.code_row / (FMT == kFormatQ4 ? 128u : 256u);
+  const bool second = (g & 1u) && hb > 0;  // a tile of one row has no second region
+  const uint32_t rsize = second ? hb : ha, row0 = second ? ha : 0;
+  const uint32_t lg = min(8 * b + (g >> 1), rsize - 1), l8 = min(8 * b + 4 + (g >> 1), rsize - 1);
+  const uint8_t* codes = base + nr * pc.scale_row + (second ? ha * pc.code_row + 64 : 0) + 16 * t;
+  const uint8_t* cg = codes + lg * pc.code_row;
+  const uint8_t* c8 = codes + l8 * pc.code_row;
+  const uint8_t* sg = base + (row0 + lg) * pc.scale_row;
+  const uint8_t* s8 = base + (row0 + l8) * pc.scale_row;
+  const float* qscale = c.s->x + kMmaScaleOff;
+  float acc_g = 0.0f, acc_8 = 0.0f;
+  for (uint32_t qd = 0; qd < quads; ++qd) {
+    const uint2 sgw = *reinterpret_cast<const uint2*>(sg + qd * 8);
+    const uint2 s8w = *reinterpret_cast<const uint2*>(s8 + qd * 8);
+    float fg = 0.0f, f8 = 0.0f;
+    if constexpr (FMT == kFormatQ4) {
+#pragma unroll
+      for (uint32_t pp = 0; pp < 2; ++pp) {
+        const uint32_t pr = 2 * qd + pp;
+        const uint4 wg = *reinterpret_cast<const uint4*>(cg + pr * 64);
+        const uint4 w8 = *reinterpret_cast<const uint4*>(c8 + pr * 64);
+        const uint4 b0 = *reinterpret_cast<const uint4*>(L.lb + pr * L.lstride);
+        const uint4 b1 = *reinterpret_cast<const uint4*>(L.lb + pr * L.lstride + 16);
+        int d[4];
+        mma_s8s8(d, q4_low16(wg.x), q4_low16(w8.x), q4_low16(wg.y), q4_low16(w8.y), b0.x, b0.y, 0, 0, 0, 0);
+        mma_s8s8(d, q4_high16(wg.x), q4_high16(w8.x), q4_high16(wg.y), q4_high16(w8.y), b0.z, b0.w, d[0], d[1], d[2],
+                 d[3]);
+        mma_s8s8(d, q4_low16(wg.z), q4_low16(w8.z), q4_low16(wg.w), q4_low16(w8.w), b1.x, b1.y, d[0], d[1], d[2], d[3]);
+        mma_s8s8(d, q4_high16(wg.z), q4_high16(w8.z), q4_high16(wg.w), q4_high16(w8.w), b1.z, b1.w, d[0], d[1], d[2],
+                 d[3]);
+        // Lane t: group t >> 1 of the pair, limbs 2 (t & 1) and 2 (t & 1) + 1.
+        const int eg = d[0] + 256 * d[1], e8 = d[2] + 256 * d[3];
+        const uint32_t hg = ((pp ? sgw.y : sgw.x) >> L.sh) & 0xFFFFu;
+        const uint32_t h8 = ((pp ? s8w.y : s8w.x) >> L.sh) & 0xFFFFu;
+        fg = fmaf(static_cast<float>(eg), __half2float(__ushort_as_half(static_cast<unsigned short>(hg))), fg);
+        f8 = fmaf(static_cast<float>(e8), __half2float(__ushort_as_half(static_cast<unsigned short>(h8))), f8);
+      }
+    } else {
+      const uint32_t sgv[4] = {sgw.x & 0xFFFFu, sgw.x >> 16, sgw.y & 0xFFFFu, sgw.y >> 16};
+      const uint32_t s8v[4] = {s8w.x & 0xFFFFu, s8w.x >> 16, s8w.y & 0xFFFFu, s8w.y >> 16};
+#pragma unroll
+      for (uint32_t q = 0; q < 4; ++q) {
+        const uint32_t grp = 4 * qd + q;
+        const uint4 wg = *reinterpret_cast<const uint4*>(cg + grp * 64);
+        const uint4 w8 = *reinterpret_cast<const uint4*>(c8 + grp * 64);
+        const uint4 bl = *reinterpret_cast<const uint4*>(L.lb + grp * L.lstride);
+        constexpr uint32_t kC = 0x80808080u;  // u - 128 as s8
+        int d[4];
+        mma_s8s8(d, wg.x ^ kC, w8.x ^ kC, wg.y ^ kC, w8.y ^ kC, bl.x, bl.y, 0, 0, 0, 0);
+        mma_s8s8(d, wg.z ^ kC, w8.z ^ kC, wg.w ^ kC, w8.w ^ kC, bl.z, bl.w, d[0], d[1], d[2], d[3]);
+        // Lane t holds limbs 2t and 2t + 1 (t < 2; lanes t >= 2 repeat them).
+        const int eg = d[0] + 256 * d[1], e8 = d[2] + 256 * d[3];
+        fg = fmaf(static_cast<float>(eg), __half2float(__ushort_as_half(static_cast<unsigned short>(sgv[q]))), fg);
+        f8 = fmaf(static_cast<float>(e8), __half2float(__ushort_as_half(static_cast<unsigned short>(s8v[q]))), f8);
+      }
+    }
+    const float qs = qscale[qd];
+    acc_g = fmaf(fg, qs, acc_g);
+    acc_8 = fmaf(f8, qs, acc_8);
+  }
+  if constexpr (FMT == kFormatQ4) {
+    // The pair's two groups (lanes t and t ^ 2) add up.
+    acc_g += __shfl_xor_sync(0xffffffffu, acc_g, 2);
+    acc_8 += __shfl_xor_sync(0xffffffffu, acc_8, 2);
+  }
+  // Limbs 2 and 3 (lane t = 1) weigh 65536 against limbs 0 and 1.
+  out_g = fmaf(__shfl_xor_sync(0xffffffffu, acc_g, 1), 65536.0f, acc_g);
+  out_8 = fmaf(__shfl_xor_sync(0xffffffffu, acc_8, 1), 65536.0f, acc_8);
+}
+
+// Consumes the lm_head's tiles with the limb planes in x. A tile's rows
+// form blocks of 16 (8 from each code region); warps take the stage's blocks
+// in turn, each covering every quad of its block, so no block barrier or
+// reduction is needed per tile. Each lane keeps its running argmax (and
+// stores the logits where asked), as the CUDA-core GEMV does.
+template <uint32_t FMT>
+__device__ void gemv_tiles_mma(Ctx& c, const Piece* pieces, int np, Best& best, float* logits_out) {
+  const uint32_t lane = static_cast<uint32_t>(c.lane), warp = static_cast<uint32_t>(c.warp);
+  const uint32_t g = lane >> 2, t = lane & 3u;
+  const MmaLane L = mma_lane<FMT>(c);
+  uint32_t unit = 0;
+  for (int p = 0; p < np; ++p) {
+    const Piece pc = pieces[p];
+    const uint32_t per = rows_per_tile(pc, true);
+    for (uint32_t r = 0; r < pc.rows; r += per) {
+      const uint32_t nr = min(per, pc.rows - r);
+      const uint32_t ha = (nr + 1) / 2, hb = nr - ha;
+      const uint32_t blocks = (ha + 7) / 8;
+      const uint8_t* base = acquire_tile(c);
+      for (uint32_t b = 0; b < blocks; ++b, ++unit) {
+        if (unit % kConsumerWarps != warp || !c.ok) continue;
+        float tg, t8;
+        block_dot<FMT>(c, L, base, pc, nr, b, tg, t8);
+        // MMA rows g and g + 8: local rows 8 b + (g >> 1) and + 4 of region g & 1.
+        const uint32_t region = g & 1u, size = region ? hb : ha;
+        const uint32_t l0 = 8 * b + (g >> 1);
+        const float tot[2] = {tg, t8};
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          if (t != 0 || l0 + 4 * k >= size) continue;
+          const uint32_t row = pc.out0 + r + region * ha + l0 + 4 * k;
+          if (logits_out) logits_out[row] = tot[k];
+          const float key = argmax_key(tot[k], row);
+          if (key > best.v || (key == best.v && row < best.i)) best = Best{key, row};
+        }
+      }
+      release_tile(c);
+    }
+  }
+}
+
+// The lm_head on the integer tensor cores and the conversion of its input,
+// out of line and with plain-value arguments: inlined, they changed the
+// register allocation of the layer stages' walk and slowed those stages more
+// than the lm_head gained.
+struct LmResult {
+  uint32_t it;
+  uint32_t ok;
+  float v;
+  uint32_t i;
+};
+template <uint32_t FMT>
+__device__ __noinline__ LmResult lm_head_mma(const DecodeLaunch* P, const DevModel* m, Smem* s, uint32_t it, Piece pc,
+                                             float* logits_out, float best_v, uint32_t best_i) {
+  Ctx c{P, m, s, it, 0, true, static_cast<int>(threadIdx.x / 32), static_cast<int>(threadIdx.x % 32),
+        static_cast<int>(threadIdx.x), false, 0, 0, 0, 0};
+  Best best{best_v, best_i};
+  gemv_tiles_mma<FMT>(c, &pc, 1, best, logits_out);
+  return LmResult{c.it, c.ok ? 1u : 0u, best.v, best.i};
+}
+template <uint32_t FMT>
+__device__ __noinline__ void lm_input_limbs(const DecodeLaunch* P, const DevModel* m, Smem* s, uint32_t width) {
+  Ctx c{P, m, s, 0, 0, true, static_cast<int>(threadIdx.x / 32), static_cast<int>(threadIdx.x % 32),
+        static_cast<int>(threadIdx.x), false, 0, 0, 0, 0};
+  limbs_from_x<FMT>(c, width);
+}
+
 // ---- exact mode: dot products in the reference's order ----
 //
 // One lane of dotF32 (kernels.zig:39-51) over a row that linearQuantized
@@ -981,7 +1328,7 @@ __device__ void gemv_tiles_exact(Ctx& c, const Piece* pieces, int np, bool lm, B
 
 // Runs one GEMV stage over the CTA's pieces.
 template <bool E>
-__device__ void gemv_stage(Ctx& c, const Piece* pieces, int np, uint32_t format, bool lm, Best& best,
+__device__ void gemv_stage(Ctx& c, const Piece* pieces, int np, uint32_t format, bool mma, bool lm, Best& best,
                            float* logits_out) {
   if constexpr (E) {
     if (format == kFormatQ4) {
@@ -994,7 +1341,17 @@ __device__ void gemv_stage(Ctx& c, const Piece* pieces, int np, uint32_t format,
     consumer_sync(kConsumerThreads);
     return;
   }
-  if (format == kFormatQ4) {
+  if (mma) {
+    // The lm_head stage is one piece (or none: a CTA without rows).
+    if (np > 0 && c.ok) {
+      const LmResult o = format == kFormatQ4
+                             ? lm_head_mma<kFormatQ4>(c.P, c.m, c.s, c.it, pieces[0], logits_out, best.v, best.i)
+                             : lm_head_mma<kFormatQ8>(c.P, c.m, c.s, c.it, pieces[0], logits_out, best.v, best.i);
+      c.it = o.it;
+      c.ok = o.ok != 0;
+      best = Best{o.v, o.i};
+    }
+  } else if (format == kFormatQ4) {
     gemv_tiles<kFormatQ4>(c, pieces, np, lm, best, logits_out);
   } else if (format == kFormatQ5) {
     gemv_tiles<kFormatQ5>(c, pieces, np, lm, best, logits_out);
@@ -1445,7 +1802,11 @@ __device__ void run_consumers(const DecodeLaunch& P, Smem* s) {
       } else {
         const uint32_t lq = st == kStLM ? 0 : l;
         const uint32_t format = stage_format(m, lq, st);
-        const bool q4 = format == kFormatQ4 || format == kFormatQ5;  // x prescaled for masked nibbles (store_x4)
+        // The default-mode q4/q8 lm_head multiplies on the integer tensor
+        // cores (gemv_tiles_mma) and takes x unscaled; the other stages mask
+        // nibbles against a prescaled x (store_x4).
+        const bool mma = !E && st == kStLM && mma_gemv(st, format, m.hidden);
+        const bool q4 = !mma && (format == kFormatQ4 || format == kFormatQ5);
         // -- stage input into x: the layer-0 input row, an RMSNorm of the
         // residual stream (decoder.zig:165-176, 259-262, 277-283), or the
         // attention output / SwiGLU activations; up reuses gate's input.
@@ -1462,12 +1823,20 @@ __device__ void run_consumers(const DecodeLaunch& P, Smem* s) {
         } else if (st == kStDown) {
           load_x_global<E>(c, P.act, m.ffn, q4);
         }
+        // The integer lm_head takes its input as limb planes.
+        if (mma) {
+          if (format == kFormatQ4) {
+            lm_input_limbs<kFormatQ4>(c.P, c.m, c.s, m.hidden);
+          } else {
+            lm_input_limbs<kFormatQ8>(c.P, c.m, c.s, m.hidden);
+          }
+        }
         trace_mark(c, e0);
         Piece pieces[3];
         const int np = stage_pieces(m, lq, st, blockIdx.x, gridDim.x, pieces);
         Best best{-INFINITY, 0xFFFFFFFFu};
         float* logits_out = (st == kStLM && P.logits_out && t + 1 == P.n_tokens) ? P.logits_out : nullptr;
-        gemv_stage<E>(c, pieces, np, format, st == kStLM, best, logits_out);
+        gemv_stage<E>(c, pieces, np, format, mma, st == kStLM, best, logits_out);
         // -- stage output
         if (st == kStQKV) {
           for (int p = 0; p < np; ++p) {
