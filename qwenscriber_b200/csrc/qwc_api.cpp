@@ -609,7 +609,9 @@ int32_t finish_model(Handle* h, const Config& c) {
   QWC_TRY(h->attn_out.alloc(size_t(qw) * 4));
   QWC_TRY(h->hidden_g.alloc(size_t(hidden) * 4));
   QWC_TRY(h->act.alloc(size_t(ffn) * 4));
-  QWC_TRY(h->attn_part.alloc(size_t(c.text_attention_heads) * h->max_chunks * kAttnPartStride * 4));
+  // The decode kernel's attention partials: one per chunk of cached positions
+  // and one for the new row (max_chunks + 1 per query head).
+  QWC_TRY(h->attn_part.alloc(size_t(c.text_attention_heads) * (h->max_chunks + 1) * kAttnPartStride * 4));
   QWC_TRY(h->attn_count.alloc(size_t(c.text_key_value_heads) * 4));
   QWC_CUDA(cudaMemset(h->attn_count.ptr, 0, h->attn_count.bytes));
   QWC_TRY(h->amax_val.alloc(size_t(h->grid) * 4));
@@ -700,7 +702,7 @@ int32_t run_decode(Handle* h, uint32_t n_tokens, uint32_t first_position, uint32
     L.trace = h->trace_buf.as<uint64_t>();
     L.trace_token = 0;
   }
-  L.max_chunks = h->max_chunks;
+  L.max_chunks = h->max_chunks + 1;  // partial slots per query head (attn_part)
   (void)m;
   QWC_CUDA(cudaMemsetAsync(h->barrier.ptr, 0, kBarrierBytes, h->stream));
   const int e = launch_decode(L, h->kv_maps, h->grid, h->stream);

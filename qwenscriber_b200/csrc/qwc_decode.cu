@@ -288,15 +288,26 @@ struct Producer {
 
   // This CTA's attention units at `position` (the same walk as attention_stage).
   __device__ void attention_tiles(const DevModel& m, const KvMaps& maps, uint32_t layer, uint32_t position) {
-    const uint32_t chunks = position / kAttnChunk + 1;
-    const uint32_t units = m.kv_heads * chunks;
+    const uint32_t cached = (position + kAttnChunk - 1) / kAttnChunk;  // chunks of cached positions
+    const uint32_t slots = cached + 1;                                 // + the new row's unit
+    const uint32_t units = m.kv_heads * slots;
     const DevLayer& L = m.layers[layer];
     const float* cos_row = m.rope_cos + size_t(position) * (kHeadDim / 2);
     const float* sin_row = m.rope_sin + size_t(position) * (kHeadDim / 2);
     for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
-      const uint32_t h = u / chunks;
-      const uint32_t ch = u % chunks;
+      const uint32_t h = u / slots;
+      const uint32_t ch = u % slots;
       uint64_t* bar;
+      if (ch == cached) {
+        // The new row's unit: the norm weights and the RoPE row only.
+        uint8_t* dst = begin_tile(kHeadDim * 4 * 2 + kHeadDim * 2 * 2, &bar);
+        if (!dst) return;
+        bulk_g2s(dst + kTileQNorm, L.q_norm, kHeadDim * 4, bar);
+        bulk_g2s(dst + kTileKNorm, L.k_norm, kHeadDim * 4, bar);
+        bulk_g2s(dst + kTileCos, cos_row, kHeadDim * 2, bar);
+        bulk_g2s(dst + kTileSin, sin_row, kHeadDim * 2, bar);
+        continue;
+      }
       uint8_t* dst = begin_tile(kAttnTileBytes, &bar);
       if (!dst) return;
       // The cache rows were written with ordinary stores by earlier tokens;
@@ -1363,18 +1374,22 @@ __device__ void gemv_stage(Ctx& c, const Piece* pieces, int np, uint32_t format,
 
 // ---- attention (decodeAttentionStepQ8, kernels.zig:697-767, split-K) ----
 //
-// Unit u = (kv head h, chunk ch of kAttnChunk positions); CTA b takes units
-// b, b + grid, ... The producer streams each unit's tile: the chunk's cached
-// key/value rows (codes and scales, TMA boxes of the q8 cache), the layer's
-// q/k RMSNorm weights and this position's RoPE row. The newest position's
-// key/value row is computed here by the unit that holds it and never read
-// back from the cache.
+// Units per kv head h: one per chunk of kAttnChunk cached positions
+// (0 .. position - 1), then the new row's unit; CTA b takes units b,
+// b + grid, ... The producer streams each unit's tile: for a chunk, its cached
+// key/value rows (codes and scales, TMA boxes of the q8 cache); for every
+// unit the layer's q/k RMSNorm weights and this position's RoPE row. The new
+// row's unit computes and appends the new key/value row and its one-position
+// partial; the chunk units, which no longer wait for that work, run beside it.
 
 __device__ void attention_stage(Ctx& c, uint32_t layer, uint32_t position) {
   const DevModel& m = *c.m;
   AttnSmem* a = reinterpret_cast<AttnSmem*>(c.s->x);
-  const uint32_t chunks = position / kAttnChunk + 1;
-  const uint32_t units = m.kv_heads * chunks;
+  // Units per kv head: one per chunk of cached positions (0 .. position - 1),
+  // then the new row's unit.
+  const uint32_t cached = (position + kAttnChunk - 1) / kAttnChunk;
+  const uint32_t slots = cached + 1;
+  const uint32_t units = m.kv_heads * slots;
   const uint32_t kvw = m.kv_heads * kHeadDim;
   const uint32_t qw = m.q_heads * kHeadDim;
   const uint32_t kv_groups = kvw / kGroup;
@@ -1386,11 +1401,11 @@ __device__ void attention_stage(Ctx& c, uint32_t layer, uint32_t position) {
   const uint32_t newest = position;
 
   for (uint32_t u = blockIdx.x; u < units; u += gridDim.x) {
-    const uint32_t h = u / chunks;
-    const uint32_t ch = u % chunks;
-    const bool last = ch == chunks - 1;
-    // 1. Query rows 2h, 2h+1 (and in the last chunk the new key/value rows)
-    // from L2, issued before waiting for the tile.
+    const uint32_t h = u / slots;
+    const uint32_t ch = u % slots;
+    const bool last = ch == cached;  // the new row's unit
+    // 1. Query rows 2h, 2h+1 (and for the new row's unit the new key/value
+    // rows) from L2, issued before waiting for the tile.
     const float qraw = ld_cg(c.P->qkv + (2 * h + j) * kHeadDim + d);
     const float kvraw = last ? ld_cg(c.P->qkv + qw + size_t(j) * kvw + h * kHeadDim + d) : 0.0f;
     const uint8_t* tile = acquire_tile(c);
@@ -1399,21 +1414,22 @@ __device__ void attention_stage(Ctx& c, uint32_t layer, uint32_t position) {
     const float* cos_row = reinterpret_cast<const float*>(tile + kTileCos);
     const float* sin_row = reinterpret_cast<const float*>(tile + kTileSin);
     // 2. Per-head RMSNorm of the queries and the new key (decoder.zig:180-195,
-    // math.zig:120-130): the sums of squares run in dimension order on three
-    // threads of different warps, and value * inverse_rms * weight rounds each
-    // product, so the key row equals the reference's on the same inputs.
+    // math.zig:120-130). The key's sum of squares runs in dimension order on
+    // one thread and value * inverse_rms * weight rounds each product, so the
+    // appended row equals the reference's on the same inputs. The queries are
+    // never stored: their sums are warp reductions (head j on warps 4j..4j+3).
     {
-      a->tmp[j][d] = qraw;
       if (last && j == 0) a->ktmp[d] = kvraw;
+      const float qss = warp_sum(qraw * qraw);
+      if (c.lane == 0) c.s->red[c.warp] = qss;
       consumer_sync(kConsumerThreads);
-      if (tid == 0 || tid == 32 || (last && tid == 64)) {
-        const float* v = tid == 64 ? a->ktmp : a->tmp[tid / 32];
-        c.s->red[tid / 32] = rms_inverse(sum_squares_seq(v, kHeadDim), kHeadDim, m.eps);
-      }
+      if (last && tid == 64) c.s->red[kConsumerWarps] = rms_inverse(sum_squares_seq(a->ktmp, kHeadDim), kHeadDim, m.eps);
       consumer_sync(kConsumerThreads);
-      const float qn = __fmul_rn(__fmul_rn(qraw, c.s->red[j]), q_norm[d]);
-      const float kn = (last && j == 0) ? __fmul_rn(__fmul_rn(kvraw, c.s->red[2]), k_norm[d]) : 0.0f;
-      consumer_sync(kConsumerThreads);
+      const float* r4 = c.s->red + 4 * j;
+      const float inv = 1.0f / sqrtf(((r4[0] + r4[1]) + (r4[2] + r4[3])) / static_cast<float>(kHeadDim) + m.eps);
+      const float qn = qraw * inv * q_norm[d];
+      const float kn =
+          (last && j == 0) ? __fmul_rn(__fmul_rn(kvraw, c.s->red[kConsumerWarps]), k_norm[d]) : 0.0f;
       a->tmp[j][d] = qn;
       if (last && j == 0) a->ktmp[d] = kn;
       consumer_sync(kConsumerThreads);
@@ -1422,9 +1438,9 @@ __device__ void attention_stage(Ctx& c, uint32_t layer, uint32_t position) {
     const int pair = d % (kHeadDim / 2);
     const float cs = cos_row[pair], sn = sin_row[pair];
     a->q[j][d / 32][d % 32] = rope_rn(d < kHeadDim / 2, a->tmp[j][pair], a->tmp[j][pair + kHeadDim / 2], cs, sn);
-    // 4. The last chunk appends the new key (normed, rotated) and value rows
-    // as q8 (decoder.zig:187-216, quant.zig:197-227): one 64-value group per
-    // two warps. The codes also stay in shared memory for this unit.
+    // 4. The new row's unit appends the new key (normed, rotated) and value
+    // rows as q8 (decoder.zig:187-216, quant.zig:197-227): one 64-value group
+    // per two warps. The codes also stay in shared memory for this unit.
     if (last) {
       float val = kvraw;
       if (j == 0) val = rope_rn(d < kHeadDim / 2, a->ktmp[pair], a->ktmp[pair + kHeadDim / 2], cs, sn);
@@ -1447,6 +1463,29 @@ __device__ void attention_stage(Ctx& c, uint32_t layer, uint32_t position) {
       fence_proxy_async_global();
     }
     consumer_sync(kConsumerThreads);
+    if (last) {
+      // The new row's attention: one position, so its softmax weight is 1
+      // and the partial is (value row, score, 1). Query head j's score is
+      // q . k over the two 64-value groups, each group's sum times its scale
+      // (q8GroupDot, kernels.zig:636-661); warps 4j .. 4j + 3 hold head j.
+      const float kc = static_cast<float>(reinterpret_cast<const uint8_t*>(a->new_codes[0])[d]) - 128.0f;
+      const float part = warp_sum(a->q[j][d / 32][d % 32] * kc);
+      if (c.lane == 0) c.s->red[c.warp] = part;
+      consumer_sync(kConsumerThreads);
+      const float* r4 = c.s->red + 4 * j;
+      const float score = m.attn_scaling * ((r4[0] + r4[1]) * f16_bits_to_f32_fast(a->new_scales[0][0]) +
+                                            (r4[2] + r4[3]) * f16_bits_to_f32_fast(a->new_scales[0][1]));
+      const float vc = static_cast<float>(reinterpret_cast<const uint8_t*>(a->new_codes[1])[d]) - 128.0f;
+      float* dst = c.P->attn_part + (size_t(2 * h + j) * c.P->max_chunks + ch) * kAttnPartStride;
+      dst[d] = vc * f16_bits_to_f32_fast(a->new_scales[1][d / kGroup]);
+      if (d == 0) {
+        dst[kHeadDim] = score;
+        dst[kHeadDim + 1] = 1.0f;
+      }
+      release_tile(c);
+      consumer_sync(kConsumerThreads);  // the scratch is reused by the next unit
+      continue;
+    }
     // 5. Scores (q8GroupDot, kernels.zig:636-661): four lanes per position,
     // 32 dimensions each; the two lanes of a 64-value group add their sums
     // before the group scale.
@@ -1455,20 +1494,11 @@ __device__ void attention_stage(Ctx& c, uint32_t layer, uint32_t position) {
     float p0, p1;
     {
       const uint32_t pos = ch * kAttnChunk + r;
-      const bool valid = pos <= newest;
-      uint4 kw0, kw1;
-      uint32_t kbits;
-      if (pos == newest) {
-        const uint4* src = reinterpret_cast<const uint4*>(a->new_codes[0]) + qd * 2;
-        kw0 = src[0];
-        kw1 = src[1];
-        kbits = a->new_scales[0][qd / 2];
-      } else {
-        const uint4* src = reinterpret_cast<const uint4*>(tile + kTileKCodes + r * kHeadDim + qd * 32);
-        kw0 = src[0];
-        kw1 = src[1];
-        kbits = *reinterpret_cast<const uint16_t*>(tile + kTileKScales + r * 16 + (h % 4) * 4 + (qd / 2) * 2);
-      }
+      const bool valid = pos < newest;  // the cached positions; the new row has its own unit
+      const uint4* src = reinterpret_cast<const uint4*>(tile + kTileKCodes + r * kHeadDim + qd * 32);
+      const uint4 kw0 = src[0], kw1 = src[1];
+      const uint32_t kbits =
+          *reinterpret_cast<const uint16_t*>(tile + kTileKScales + r * 16 + (h % 4) * 4 + (qd / 2) * 2);
       const uint32_t words[8] = {kw0.x, kw0.y, kw0.z, kw0.w, kw1.x, kw1.y, kw1.z, kw1.w};
       const uint64_t bias = pack2(kNegQ8, kNegQ8);
       uint64_t acc0 = 0, acc1 = 0;
@@ -1532,16 +1562,10 @@ __device__ void attention_stage(Ctx& c, uint32_t layer, uint32_t position) {
       for (int i = 0; i < kAttnChunk / kConsumerWarps; ++i) {
         const uint32_t rr = c.warp * (kAttnChunk / kConsumerWarps) + i;
         const uint32_t pos = ch * kAttnChunk + rr;
-        uint32_t word, bits;
-        if (pos == newest) {
-          word = a->new_codes[1][c.lane];
-          bits = a->new_scales[1][grp];
-        } else {
-          word = *reinterpret_cast<const uint32_t*>(tile + kTileVCodes + rr * kHeadDim + 4 * c.lane);
-          bits = *reinterpret_cast<const uint16_t*>(tile + kTileVScales + rr * 16 + (h % 4) * 4 + grp * 2);
-        }
+        const uint32_t word = *reinterpret_cast<const uint32_t*>(tile + kTileVCodes + rr * kHeadDim + 4 * c.lane);
+        const uint32_t bits = *reinterpret_cast<const uint16_t*>(tile + kTileVScales + rr * 16 + (h % 4) * 4 + grp * 2);
         const float scale = f16_bits_to_f32_fast(bits);
-        const bool valid = pos <= newest;
+        const bool valid = pos < newest;
         const float sw0 = valid ? scale * a->prob[0][rr] : 0.0f;
         const float sw1 = valid ? scale * a->prob[1][rr] : 0.0f;
 #pragma unroll
@@ -1818,7 +1842,8 @@ __device__ void run_consumers(const DecodeLaunch& P, Smem* s) {
           if constexpr (E) {
             load_x_global<E>(c, P.attn_out, m.q_heads * kHeadDim, q4);
           } else {
-            attention_into_x(c, P.attn_part, position / kAttnChunk + 1, q4);
+            // Partials: one per chunk of cached positions, then the new row's.
+            attention_into_x(c, P.attn_part, (position + kAttnChunk - 1) / kAttnChunk + 1, q4);
           }
         } else if (st == kStDown) {
           load_x_global<E>(c, P.act, m.ffn, q4);
