@@ -562,7 +562,7 @@ def run_ours(args, rank, world, local_rank):
 # profiling modes
 # ---------------------------------------------------------------------------
 
-STAGES = ("qkv", "attention", "o", "gate", "up", "down")
+STAGES = ("qkv", "attention", "o", "gate+up", "down")
 
 
 def print_trace(raw, layers: int) -> None:

@@ -551,9 +551,12 @@ int32_t finish_model(Handle* h, const Config& c) {
   cudaSetDevice(h->device);
   h->grid = decode_grid_size(h->device);
   if (h->grid <= 0) return QWC_INVALID_STATE;
-  // Rows of a non-LM stage held by one CTA must fit the kernel's row buffers.
-  const uint32_t widest = std::max({qw + 2 * kvw, ffn, hidden});
-  if ((widest + h->grid - 1) / h->grid > 256) return QWC_UNSUPPORTED_MODEL;
+  // Rows of a non-LM stage held by one CTA must fit the kernel's row buffers
+  // (the gate-and-up stage holds a CTA's gate rows and as many up rows).
+  if ((qw + 2 * kvw + h->grid - 1) / h->grid > 256 || 2 * ((ffn + h->grid - 1) / h->grid) > 256 ||
+      (hidden + h->grid - 1) / h->grid > 256) {
+    return QWC_UNSUPPORTED_MODEL;
+  }
   // Every CTA streams at least one tile of each stage, which keeps a layer's
   // attention tiles (TMA reads of cache rows earlier tokens wrote) more than
   // a ring's depth of tiles behind those writes.

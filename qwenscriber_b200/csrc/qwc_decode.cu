@@ -63,16 +63,16 @@ static_assert(kTileVCodes % 128 == 0 && kTileKScales % 128 == 0 && kTileVScales 
                   kTileCos % 16 == 0 && kTileSin % 16 == 0,
               "TMA boxes land on 128-byte boundaries, bulk copies on 16-byte boundaries");
 
-enum Stage : int { kStQKV = 0, kStO = 1, kStGate = 2, kStUp = 3, kStDown = 4, kStLM = 5, kStAttn = 6 };
+enum Stage : int { kStQKV = 0, kStO = 1, kStGateUp = 2, kStDown = 4, kStLM = 5, kStAttn = 6 };
 
-// A token is a walk over stages: six per layer in this order, then the
+// A token is a walk over stages: five per layer in this order, then the
 // lm_head stage for tokens with logits. The producer and the consumers run
 // the same walk, each with one code path per kind of stage, so the code a
 // layer executes stays small enough to remain in the instruction cache.
-constexpr int kStagesPerLayer = 6;
+constexpr int kStagesPerLayer = 5;
 __device__ __forceinline__ int layer_stage(uint32_t i) {
-  // QKV, attention, O, gate, up, down (decoder.zig:165-271).
-  return i == 0 ? kStQKV : i == 1 ? kStAttn : i == 2 ? kStO : i == 3 ? kStGate : i == 4 ? kStUp : kStDown;
+  // QKV, attention, O, gate and up, down (decoder.zig:165-271).
+  return i == 0 ? kStQKV : i == 1 ? kStAttn : i == 2 ? kStO : i == 3 ? kStGateUp : kStDown;
 }
 
 enum ErrorCode : int32_t { kErrBarrier = 1, kErrFull = 2, kErrEmpty = 3, kErrShape = 4 };
@@ -84,7 +84,6 @@ struct Smem {
   float x[kXMax];                 // activation vector, swizzled (x_index), q4-prescaled when asked
   float part[kRowsMax];           // per-row dot products of the current stage
   float chunk_part[kSlotBytes / 512];  // per (row, 512-byte chunk) dot products of the current tile
-  float gate[kRowsMax];           // gate outputs waiting for the up rows
   float resid[kResidMax];         // this CTA's rows of the residual stream
   float red[kConsumerWarps * 2];  // block reductions
   float amax_v[kConsumerWarps];
@@ -175,14 +174,12 @@ __device__ int stage_pieces(const DevModel& m, uint32_t layer, int stage, uint32
       add(&L.o, s.begin, s.end, 0, s.begin);
       break;
     }
-    case kStGate: {
+    case kStGateUp: {
+      // This CTA's gate rows, then the same rows of up: one stage, so its
+      // tiles run across the two matrices.
       const Span s = split_rows(L.gate.rows, c, n);
       add(&L.gate, s.begin, s.end, 0, s.begin);
-      break;
-    }
-    case kStUp: {
-      const Span s = split_rows(L.up.rows, c, n);
-      add(&L.up, s.begin, s.end, 0, s.begin);
+      add(&L.up, s.begin, s.end, s.end - s.begin, s.begin);
       break;
     }
     case kStDown: {
@@ -210,8 +207,7 @@ __device__ __forceinline__ uint32_t stage_format(const DevModel& m, uint32_t lay
   return stage == kStLM ? m.lm_head.format
        : stage == kStQKV ? L.q.format
        : stage == kStO ? L.o.format
-       : stage == kStGate ? L.gate.format
-       : stage == kStUp ? L.up.format
+       : stage == kStGateUp ? L.gate.format
                         : L.down.format;
 }
 
@@ -327,15 +323,39 @@ struct Producer {
     }
   }
 
+  // Rows t0 .. t0 + nr of the stage's pieces taken end to end (one K and one
+  // format per stage), as one tile: each piece's segment in two bulk copies,
+  // its scales and its codes, at the segment's place in the tile.
+  __device__ void issue_span(const Piece* pieces, int np, uint32_t t0, uint32_t nr) {
+    const uint32_t sr = pieces[0].scale_row, cr = pieces[0].code_row;
+    uint64_t* bar;
+    uint8_t* dst = begin_tile(nr * (sr + cr), &bar);
+    if (!dst) return;
+    uint32_t first = 0;  // stage row of the piece's first row
+    for (int p = 0; p < np; ++p) {
+      const uint32_t b = max(t0, first), e = min(t0 + nr, first + pieces[p].rows);
+      if (b < e) {
+        const uint32_t r = b - first, k = b - t0, n = e - b;
+        bulk_g2s(dst + k * sr, pieces[p].scales + size_t(r) * sr, n * sr, bar);
+        bulk_g2s(dst + nr * sr + k * cr, pieces[p].codes + size_t(r) * cr, n * cr, bar);
+      }
+      first += pieces[p].rows;
+    }
+  }
+
   __device__ void stage(const DevModel& m, uint32_t layer, int st, bool regions) {
     Piece pieces[3];
     const int np = stage_pieces(m, layer, st, blockIdx.x, gridDim.x, pieces);
-    for (int p = 0; p < np && ok; ++p) {
-      const uint32_t per = rows_per_tile(pieces[p], regions);
-      for (uint32_t r = 0; r < pieces[p].rows && ok; r += per) {
-        issue(pieces[p], r, min(per, pieces[p].rows - r), regions);
-      }
+    if (np == 0) return;
+    if (regions) {  // the integer lm_head: one piece
+      const uint32_t per = rows_per_tile(pieces[0], true);
+      for (uint32_t r = 0; r < pieces[0].rows && ok; r += per) issue(pieces[0], r, min(per, pieces[0].rows - r), true);
+      return;
     }
+    uint32_t total = 0;
+    for (int p = 0; p < np; ++p) total += pieces[p].rows;
+    const uint32_t per = rows_per_tile(pieces[0]);
+    for (uint32_t t0 = 0; t0 < total && ok; t0 += per) issue_span(pieces, np, t0, min(per, total - t0));
   }
 
   // After an error: wait (bounded) for every copy still in flight so no bulk
@@ -366,8 +386,8 @@ __device__ void run_producer(const DecodeLaunch& P, const KvMaps& maps, Smem* s)
     for (uint32_t q = 0; q < walk && pr.ok; ++q) {
       const uint32_t l = q / kStagesPerLayer;
       const int st = l < m.n_layers ? layer_stage(q % kStagesPerLayer) : kStLM;
-      if (st == kStQKV || st == kStGate || st == kStLM) {
-        const float* norm = st == kStQKV ? m.layers[l].attn_norm : st == kStGate ? m.layers[l].ffn_norm : m.final_norm;
+      if (st == kStQKV || st == kStGateUp || st == kStLM) {
+        const float* norm = st == kStQKV ? m.layers[l].attn_norm : st == kStGateUp ? m.layers[l].ffn_norm : m.final_norm;
         pr.vector_tile(norm, m.hidden);
       }
       if (!pr.ok) break;
@@ -1339,8 +1359,17 @@ __device__ void gemv_tiles_exact(Ctx& c, const Piece* pieces, int np, bool lm, B
 
 // Runs one GEMV stage over the CTA's pieces.
 template <bool E>
-__device__ void gemv_stage(Ctx& c, const Piece* pieces, int np, uint32_t format, bool mma, bool lm, Best& best,
+__device__ void gemv_stage(Ctx& c, const Piece* pieces_in, int np, uint32_t format, bool mma, bool lm, Best& best,
                            float* logits_out) {
+  // The CUDA-core GEMVs see a stage's pieces end to end as one: the pieces
+  // share K and format, their stage-local rows (local0) run on from one to
+  // the next, and the producer cuts the tiles across them (issue_span). Only
+  // the lm_head, a single piece, reads out0.
+  Piece whole = pieces_in[0];
+  for (int p = 1; p < np; ++p) whole.rows += pieces_in[p].rows;
+  whole.local0 = 0;
+  const Piece* pieces = mma ? pieces_in : &whole;
+  if (!mma) np = np > 0 ? 1 : 0;
   if constexpr (E) {
     if (format == kFormatQ4) {
       gemv_tiles_exact<kFormatQ4>(c, pieces, np, lm, best, logits_out);
@@ -1833,10 +1862,10 @@ __device__ void run_consumers(const DecodeLaunch& P, Smem* s) {
         const bool q4 = !mma && (format == kFormatQ4 || format == kFormatQ5);
         // -- stage input into x: the layer-0 input row, an RMSNorm of the
         // residual stream (decoder.zig:165-176, 259-262, 277-283), or the
-        // attention output / SwiGLU activations; up reuses gate's input.
+        // attention output / SwiGLU activations; gate and up share one input.
         if (st == kStQKV && l == 0) {
           input_into_x<E>(c, input, row, own, q4);
-        } else if (st == kStQKV || st == kStGate || st == kStLM) {
+        } else if (st == kStQKV || st == kStGateUp || st == kStLM) {
           norm_global_into_x<E>(c, P.hidden_g, m.hidden, q4);
         } else if (st == kStO) {
           if constexpr (E) {
@@ -1876,19 +1905,17 @@ __device__ void run_consumers(const DecodeLaunch& P, Smem* s) {
             s->resid[r - own.begin] = h;
             P.hidden_g[r] = h;
           }
-        } else if (st == kStGate) {
-          for (uint32_t i = c.tid; i < fr.end - fr.begin; i += kConsumerThreads) s->gate[i] = s->part[i];
-          consumer_sync(kConsumerThreads);
-        } else if (st == kStUp) {
-          // SwiGLU (kernels.zig:233-239).
-          for (uint32_t i = c.tid; i < fr.end - fr.begin; i += kConsumerThreads) {
-            const float g = s->gate[i];
+        } else if (st == kStGateUp) {
+          // SwiGLU (kernels.zig:233-239): gate rows, then up rows, in part.
+          const uint32_t nf = fr.end - fr.begin;
+          for (uint32_t i = c.tid; i < nf; i += kConsumerThreads) {
+            const float g = s->part[i];
             if constexpr (E) {
               const float silu = __fdiv_rn(g, __fadd_rn(1.0f, exp_ref(-g)));  // math.zig:69-71
-              P.act[fr.begin + i] = __fmul_rn(silu, s->part[i]);
+              P.act[fr.begin + i] = __fmul_rn(silu, s->part[nf + i]);
             } else {
               const float silu = g / (1.0f + expf(-g));
-              P.act[fr.begin + i] = silu * s->part[i];
+              P.act[fr.begin + i] = silu * s->part[nf + i];
             }
           }
         } else {
@@ -1916,10 +1943,8 @@ __device__ void run_consumers(const DecodeLaunch& P, Smem* s) {
         }
       }
       trace_mark(c, e0 + 1);
-      if (st != kStGate) {
-        grid_barrier(c);
-        if (!c.ok) break;
-      }
+      grid_barrier(c);
+      if (!c.ok) break;
       trace_mark(c, e0 + 2);
     }
     if (!c.ok) break;
