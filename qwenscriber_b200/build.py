@@ -47,7 +47,10 @@ def build(verbose: bool = False, ptxas_verbose: bool = False) -> str:
         path = os.path.join(CSRC, src)
         obj = os.path.join(BUILD, src + ".o")
         objects.append(obj)
-        if not _stale(obj, [path, *headers, __file__]) and not ptxas_verbose:
+        # A source may include another (qwc_decode_wide.cu compiles qwc_decode.cu
+        # with a wider weight ring), so every source counts as a dependency.
+        deps = [path, *headers, *(os.path.join(CSRC, f) for f in sources if f.endswith(".cu")), __file__]
+        if not _stale(obj, deps) and not ptxas_verbose:
             continue
         cmd = [NVCC, *ARCH, *COMMON, "-c", path, "-o", obj]
         if src.endswith(".cpp"):

@@ -291,6 +291,7 @@ struct Handle {
   DevBuf qkv, attn_out, hidden_g, act, attn_part, attn_count, amax_val, amax_idx, barrier, error, tokens_out, logits;
   DevBuf prompt_ids, prompt_rows, audio_rows, trace_buf, exact_scratch;
   uint32_t max_chunks = 0;
+  bool wide_slots = false;  // decode with the three-slot kernel (launch_decode_wide)
   uint64_t weight_bytes = 0;
   KvMaps kv_maps{};
   std::unique_ptr<Batched> batched;  // streams > 1
@@ -561,6 +562,14 @@ int32_t finish_model(Handle* h, const Config& c) {
   // attention tiles (TMA reads of cache rows earlier tokens wrote) more than
   // a ring's depth of tiles behind those writes.
   if (std::min(hidden, ffn) < static_cast<uint32_t>(h->grid)) return QWC_UNSUPPORTED_MODEL;
+  // The decode kernel's wide-slot copy pays off when a CTA's down-projection
+  // rows fit one wide slot but not one narrow one (two tiles become one);
+  // otherwise the five narrow slots keep the deeper prefetch.
+  {
+    const uint64_t down_bytes = uint64_t((hidden + h->grid - 1) / h->grid) *
+                                (m.layers[0].down.scale_row + m.layers[0].down.code_row);
+    h->wide_slots = down_bytes > kDecodeSlotBytes && down_bytes <= kDecodeWideSlotBytes;
+  }
 
   m.n_layers = L;
   m.hidden = hidden;
@@ -708,7 +717,8 @@ int32_t run_decode(Handle* h, uint32_t n_tokens, uint32_t first_position, uint32
   L.max_chunks = h->max_chunks + 1;  // partial slots per query head (attn_part)
   (void)m;
   QWC_CUDA(cudaMemsetAsync(h->barrier.ptr, 0, kBarrierBytes, h->stream));
-  const int e = launch_decode(L, h->kv_maps, h->grid, h->stream);
+  const int e = h->wide_slots ? launch_decode_wide(L, h->kv_maps, h->grid, h->stream)
+                              : launch_decode(L, h->kv_maps, h->grid, h->stream);
   if (e != 0) {
     if (std::getenv("QWC_VERBOSE")) std::fprintf(stderr, "qwc: decode launch failed: %s\n", cudaGetErrorString(static_cast<cudaError_t>(e)));
     return status_of(static_cast<cudaError_t>(e));

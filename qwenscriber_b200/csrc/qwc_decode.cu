@@ -41,8 +41,16 @@ constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kThreads = kConsumerThreads + 32;
 constexpr int kRowsPerPass = 4;                // rows one warp works on at a time
-constexpr int kSlots = 5;
-constexpr uint32_t kSlotBytes = 34 * 1024;            // 32 rows of a q4 matrix with K = 2048
+// The weight ring: five slots of 34 KB (32 rows of a q4 matrix with K = 2048),
+// or, in the copy of this kernel that qwc_decode_wide.cu compiles, three of
+// 57 KB, for models whose down-projection share fits one wide slot but not one
+// narrow slot (one tile instead of two per CTA). The host picks the copy per
+// model (launch_decode / launch_decode_wide).
+#ifndef QWC_DECODE_WIDE_SLOTS
+#define QWC_DECODE_WIDE_SLOTS 0
+#endif
+constexpr int kSlots = QWC_DECODE_WIDE_SLOTS ? 3 : 5;
+constexpr uint32_t kSlotBytes = QWC_DECODE_WIDE_SLOTS ? kDecodeWideSlotBytes : kDecodeSlotBytes;
 constexpr uint32_t kXMax = 8192;               // floats in the activation buffer (max K)
 constexpr uint32_t kRowsMax = 256;             // rows of one stage per CTA (non-LM stages)
 constexpr uint32_t kResidMax = 256;            // hidden rows owned by one CTA
@@ -2018,8 +2026,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace
 
-int decode_kernel_smem_bytes() { return static_cast<int>(sizeof(Smem)); }
-
+#if QWC_DECODE_WIDE_SLOTS
+int launch_decode_wide(const DecodeLaunch& launch, const KvMaps& maps, int grid, void* stream) {
+#else
 int decode_grid_size(int device) {
   int sms = 0;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
@@ -2027,7 +2036,8 @@ int decode_grid_size(int device) {
 }
 
 int launch_decode(const DecodeLaunch& launch, const KvMaps& maps, int grid, void* stream) {
-  const int smem = decode_kernel_smem_bytes();
+#endif
+  const int smem = static_cast<int>(sizeof(Smem));
   const void* fn = launch.exact ? reinterpret_cast<const void*>(decode_kernel<true>)
                                 : reinterpret_cast<const void*>(decode_kernel<false>);
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

@@ -149,9 +149,14 @@ constexpr uint32_t kTraceEventsPerStage = 3;  // input ready, output done, barri
 
 // Launchers implemented in the .cu files (host-callable).
 namespace qwc {
-int decode_kernel_smem_bytes();
 // Returns cudaError_t as int.
 int launch_decode(const DecodeLaunch& launch, const KvMaps& maps, int grid, void* stream);
+// The same kernel with three 57 KB ring slots instead of five of 34 KB
+// (qwc_decode_wide.cu), for models whose down-projection share per CTA fits
+// one wide slot but not one narrow slot.
+int launch_decode_wide(const DecodeLaunch& launch, const KvMaps& maps, int grid, void* stream);
+constexpr uint32_t kDecodeSlotBytes = 34 * 1024;
+constexpr uint32_t kDecodeWideSlotBytes = 453 * 128;
 int decode_grid_size(int device);
 
 // ---- batched multi-stream step (qwc_streams.cu) ----
